@@ -1,0 +1,377 @@
+"""Benchmark of the B200-native llama2c op trio.
+
+One step = one pass of the hot path over one batch:
+  rows launch  rmsnorm of x [1024][16384] (fp32 out + bf16 GEMM operand) and
+               softmax of an independent logits buffer [1024][16384];
+  GEMM         out[b][r] = sum_k W[r][k] * xnorm[b][k], 1024 x 8192 x 16384,
+               tcgen05 bf16 with fp32 accumulation (W converted once at setup).
+Metric: TFLOP/s of the step (2*B*N*K per step) and ms per step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun, one rank per GPU): every rank runs the same step on its own
+batch (batch rows are independent; no data-path collective): weak scaling,
+value = all ranks' FLOPs / max-over-ranks time.
+--impl reference: the CPU arm (rank 0 only): the oracle's multithreaded fp32
+restatement of the same step on a bounded sample of batch rows.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BATCH, SIZE, ROWS = 1024, 16384, 8192
+METRIC = "llama2c step TFLOP/s & ms/iter (1024x16384x8192); decode tokens/s at 1-8 GPU"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "tf32", "fp32"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="target CPU time of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def flops_per_step(batch=BATCH):
+    return 2.0 * batch * ROWS * SIZE
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return p, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def ncu_traffic(name):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary under
+    profiles/ (a line 'dram_bytes_per_launch: N'), or None."""
+    path = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        for line in f:
+            if line.strip().startswith("dram_bytes_per_launch:"):
+                try:
+                    return float(line.split(":", 1)[1].split()[0])
+                except ValueError:
+                    return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the
+    timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in self.rows:
+            for name, val in zip(names, r[5:9]):
+                if val.strip().lower() in ("active", "1"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU arm / baseline
+
+def cpu_step_sample(seconds, x, w, logits, W):
+    """Times the oracle's multithreaded fp32 trio on the first S batch rows
+    (S grows until one run takes about `seconds`). Returns (TFLOP/s, S,
+    threads, elapsed)."""
+    from oracle import oracle as O
+    s = 4
+    while True:
+        t0 = time.perf_counter()
+        _, _, _, threads = O.trio_fp32(x[:s], w, logits[:s], W)
+        dt = time.perf_counter() - t0
+        if dt >= seconds * 0.5 or s >= BATCH:
+            return flops_per_step(s) / dt / 1e12, s, threads, dt
+        s = min(BATCH, max(s * 2, int(s * seconds / max(dt, 1e-3))))
+
+
+def run_reference(args, rank):
+    """--impl reference: the CPU arm. Rank 0 only; other ranks exit 0."""
+    if rank != 0:
+        return
+    import __graft_entry__
+    ce = __graft_entry__.load_package()
+    x, w, logits, W = ce.trio_inputs_host(0, BATCH, SIZE, ROWS)
+    # sample size chosen so one step is about 2 s, the whole run a few minutes
+    per_step = max(0.5, min(4.0, 120.0 / max(1, args.steps + args.warmup)))
+    _, s, threads, _ = cpu_step_sample(per_step, x, w, logits, W)
+    from oracle import oracle as O
+    for _ in range(args.warmup):
+        O.trio_fp32(x[:s], w, logits[:s], W)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        O.trio_fp32(x[:s], w, logits[:s], W)
+    dt = (time.perf_counter() - t0) / args.steps
+    value = flops_per_step(s) / dt / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": dt * 1e3 * BATCH / s, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "llama2c op trio 1024x16384x8192 (rmsnorm, softmax, GEMM on the "
+                               "normalized batch), CPU sample of the batch rows",
+                   "batch": BATCH, "size": SIZE, "rows": ROWS, "sample_rows": s},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{s} of {BATCH} batch rows, full 8192x16384 matrix, per step; "
+                                   "ms_per_step scaled to the full batch"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+    import __graft_entry__
+    ce = __graft_entry__.load_package()
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+
+    prec = {"bf16": ce.PREC_BF16, "tf32": ce.PREC_TF32, "fp32": ce.PREC_FP32}[args.precision]
+    # every rank: its own batch (seed = rank), the same matrix
+    x, w, logits, W = ce.trio_inputs_host(rank, BATCH, SIZE, ROWS)
+    plan = ce.Plan(BATCH, SIZE, ROWS, prec)
+    dW = torch.from_numpy(W).to(dev)
+    plan.set_weights(dW)
+    del dW
+    dx, dw, dl = (torch.from_numpy(a).to(dev) for a in (x, w, logits))
+    norm = torch.empty((BATCH, SIZE), device=dev)
+    soft = torch.empty((BATCH, SIZE), device=dev)
+    out = torch.empty((BATCH, ROWS), device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    s = stream.cuda_stream
+
+    def step(ev_mid=None):
+        plan.rows(norm, soft, dx, dw, dl, stream=s)
+        if ev_mid is not None:
+            ev_mid.record(stream)
+        plan.gemm(out, stream=s)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step()
+    ce.device_status()
+    barrier()
+
+    # ---- timed region: K steps, events around each GEMM launch ----
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    time.sleep(0.3)
+    barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            step(mids[i])
+            ends[i].record(stream)
+        t1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    ce.device_status()
+    total_ms = t0.elapsed_time(t1)
+    gemm_ms = float(np.mean([mids[i].elapsed_time(ends[i]) for i in range(args.steps)]))
+    rows_ms = float(np.mean([starts[i].elapsed_time(mids[i]) for i in range(args.steps)]))
+    t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_per_step = total_ms / args.steps
+    value = world * flops_per_step() / (ms_per_step * 1e-3) / 1e12
+
+    # ---- end to end through the C ABI with pinned host buffers ----
+    hx = torch.from_numpy(x).pin_memory()
+    hl = torch.from_numpy(logits).pin_memory()
+    hn = torch.empty((BATCH, SIZE), pin_memory=True)
+    hs = torch.empty((BATCH, SIZE), pin_memory=True)
+    ho = torch.empty((BATCH, ROWS), pin_memory=True)
+    e2e_steps = max(3, min(args.steps, 10))
+
+    def e2e_step():
+        dx.copy_(hx, non_blocking=True)
+        dl.copy_(hl, non_blocking=True)
+        plan.trio(norm, soft, out, dx, dw, dl, stream=s)
+        hn.copy_(norm, non_blocking=True)
+        hs.copy_(soft, non_blocking=True)
+        ho.copy_(out, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    e2e_value = world * flops_per_step() / (e2e_ms * 1e-3) / 1e12
+    h2d = hx.numel() * 4 + hl.numel() * 4
+    d2h = hn.numel() * 4 + hs.numel() * 4 + ho.numel() * 4
+
+    # ---- legacy llama2c iteration (reference semantics: GEMV on input row 0) ----
+    mat = torch.empty((ROWS, SIZE), device=dev)
+    mat.copy_(torch.from_numpy(W))
+    prod = torch.empty(ROWS, device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            ce.llama2c_iteration(norm, soft, prod, dx, dw, dl, mat, stream=s)
+        l0 = torch.cuda.Event(enable_timing=True)
+        l1 = torch.cuda.Event(enable_timing=True)
+        l0.record(stream)
+        legacy_iters = 20
+        for _ in range(legacy_iters):
+            ce.llama2c_iteration(norm, soft, prod, dx, dw, dl, mat, stream=s)
+        l1.record(stream)
+    torch.cuda.synchronize(dev)
+    legacy_ms = l0.elapsed_time(l1) / legacy_iters
+    min_bytes = 805470208.0  # llama2c_cuda_graph.cu:340-345 at this shape
+    del mat
+
+    pk, pk_kind = peaks()
+    long_region = total_ms > 1000.0
+    peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
+    achieved = flops_per_step() / (gemm_ms * 1e-3) / 1e12
+    traffic = ncu_traffic("gemm_bf16_1024x8192x16384.txt")
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tflops, srows, threads, dt = cpu_step_sample(args.cpu_seconds, x, w, logits, W)
+        cpu = {"value": tflops, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{srows} of {BATCH} batch rows through rmsnorm, softmax and the "
+                         f"8192x16384 GEMM (fp32, {dt:.1f} s)"}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": args.precision if args.precision != "fp32" else "f32",
+            "data": "synthetic",
+            "config": {"workload": "llama2c op trio 1024x16384x8192: fused rmsnorm+softmax rows "
+                                   "launch (fp32) then the tcgen05 GEMM on the normalized batch",
+                       "batch": BATCH, "size": SIZE, "rows": ROWS, "precision": args.precision,
+                       "parallelism": f"dp{world} (independent batches, no collective)",
+                       "l2": "inputs larger than L2 (x and logits 64 MiB each, W 256 MiB bf16); "
+                             "no flush between steps"},
+            "gpu_launches": 2 * args.steps,
+            "kernels_ms": {"rows": rows_ms, "gemm": gemm_ms},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_source": f"{pk_kind} {'sustained' if long_region else 'burst'} bf16"},
+            "rows_roofline": {"bound": "hbm", "achieved": (4.0 * BATCH * SIZE * 4 + BATCH * SIZE * 2 + SIZE * 4)
+                              / (rows_ms * 1e-3) / 1e9, "peak": pk.get("hbm_gbs", 6650.0),
+                              "unit": "GB/s"},
+            "legacy_iteration": {"ms_per_iter": legacy_ms, "min_bytes_per_iter": min_bytes,
+                                 "achieved_gbps": min_bytes / (legacy_ms * 1e-3) / 1e9},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "clocks": clocks,
+        }
+        line["rows_roofline"]["frac"] = line["rows_roofline"]["achieved"] / line["rows_roofline"]["peak"]
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    plan.close()
+    if dist is not None:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,306 @@
+"""cuda-elastic_b200: the B200-native llama2c hot path, host-side mirror.
+
+The compute lives in libce_b200.so (hand-written sm_100a CUDA behind the C
+ABI of include/ce_b200.h). This module binds that ABI with ctypes and
+mirrors the reference's operator surface for the path:
+
+  * the llama2c iteration (llama2c/llama2c_cuda_graph.cu): rmsnorm, softmax
+    and the GEMV, with the same seeded inputs (llama2c_common.h:105-132);
+  * the BASELINE op trio: rmsnorm -> tensor-core GEMM on the normalized
+    batch, plus softmax, through a Plan (weights prepared once at setup).
+
+PyTorch is used only for device memory and streams; tensors are passed to
+the library as raw device pointers. There is no CPU fallback: if the
+library is missing, importing or calling this module fails loudly.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libce_b200.so")
+
+OK = 0
+ERR_USAGE = 2
+ERR_CUDA = 70
+ERR_TIMEOUT = 71
+ERR_NOMEM = 72
+
+PREC_FP32 = 0
+PREC_TF32 = 1
+PREC_BF16 = 2
+PREC_FP8_E4M3 = 3
+
+RMS_EPS = 1.0e-5  # kRmsEpsilon, llama2c/llama2c_common.h:44
+
+_lib = None
+
+
+class CeError(RuntimeError):
+    """A non-zero status from libce_b200 (status in .status)."""
+
+    def __init__(self, status, message):
+        super().__init__(f"libce_b200 status {status}: {message}")
+        self.status = status
+
+
+def build(verbose=False):
+    """Compiles libce_b200.so in place (nvcc, sm_100a)."""
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("_ce_b200_build", os.path.join(_HERE, "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.build(verbose=verbose)
+
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+_u64 = ctypes.c_uint64
+_i64 = ctypes.c_int64
+
+# name -> argtypes (restype int unless listed in _RESTYPES)
+_SIGNATURES = {
+    "ce_version": [],
+    "ce_last_error": [ctypes.c_char_p, ctypes.c_size_t],
+    "ce_device_info": [ctypes.POINTER(_i), ctypes.POINTER(_i)],
+    "ce_device_status": [],
+    "ce_fill_llama2c_host": [_i, _u64, _i, _i, _i, _vp, _vp, _vp, _vp],
+    "ce_fill_normal_host": [_u64, _u64, _i64, _i64, _f, _vp],
+    "ce_fill_uniform_host": [_u64, _u64, _i64, _i64, _f, _f, _vp],
+    "ce_rmsnorm": [_vp, _vp, _vp, _i, _i, _f, _vp],
+    "ce_softmax": [_vp, _vp, _i, _i, _vp],
+    "ce_gemv": [_vp, _vp, _vp, _i, _i, _vp],
+    "ce_llama2c_iteration": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp],
+    "ce_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "ce_gemm_bf16_tile": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
+    "ce_gemm_tf32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "ce_gemm_fp32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "ce_convert_bf16": [_vp, _vp, _i, _i, _i, _vp],
+    "ce_rmsnorm_bf16": [_vp, _vp, _i, _vp, _vp, _i, _i, _f, _vp],
+    "ce_plan_create": [ctypes.POINTER(_vp), _i, _i, _i, _i],
+    "ce_plan_destroy": [_vp],
+    "ce_plan_set_weights": [_vp, _vp, _vp],
+    "ce_plan_rmsnorm_gemm": [_vp, _vp, _vp, _vp, _vp, _f, _vp],
+    "ce_plan_trio": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
+    "ce_plan_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
+    "ce_plan_gemm": [_vp, _vp, _vp],
+}
+_RESTYPES = {"ce_version": ctypes.c_char_p}
+
+
+def lib():
+    """The loaded libce_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run __graft_entry__.build() "
+                              "(the CUDA library is required; there is no CPU fallback)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, args in _SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = _RESTYPES.get(name, ctypes.c_int)
+        _lib = L
+    return _lib
+
+
+def last_error():
+    buf = ctypes.create_string_buffer(1024)
+    code = lib().ce_last_error(buf, len(buf))
+    return code, buf.value.decode(errors="replace")
+
+
+def check(status):
+    if status != OK:
+        raise CeError(status, last_error()[1])
+    return status
+
+
+def _ptr(t):
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+def _stream(stream):
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, int):
+        return stream
+    return stream.cuda_stream
+
+
+def device_status():
+    """Synchronizes and raises CeError(ERR_TIMEOUT) if a device wait gave up."""
+    return check(lib().ce_device_status())
+
+
+def device_info():
+    sms, sm100 = _i(), _i()
+    check(lib().ce_device_info(ctypes.byref(sms), ctypes.byref(sm100)))
+    return sms.value, bool(sm100.value)
+
+
+# ---------------------------------------------------------------------------
+# Host generators (the reference harness's fill_inputs and fixture normals)
+
+def fill_llama2c_host(random, seed, batch, size, rows):
+    """llama2c inputs (llama2c_common.h:105-132) as numpy float32 arrays:
+    input [batch][size], probabilities [batch][size], weight [size],
+    matrix [rows][size]."""
+    x = np.empty((batch, size), np.float32)
+    p = np.empty((batch, size), np.float32)
+    w = np.empty(size, np.float32)
+    m = np.empty((rows, size), np.float32)
+    check(lib().ce_fill_llama2c_host(int(bool(random)), seed, batch, size, rows,
+                                     _ptr(x), _ptr(p), _ptr(w), _ptr(m)))
+    return x, p, w, m
+
+
+def fill_normal_host(seed, stream, count, scale=1.0, first=0, out=None):
+    out = np.empty(count, np.float32) if out is None else out
+    check(lib().ce_fill_normal_host(seed, stream, first, count, scale, _ptr(out)))
+    return out
+
+
+def fill_uniform_host(seed, stream, count, lo, hi, first=0, out=None):
+    out = np.empty(count, np.float32) if out is None else out
+    check(lib().ce_fill_uniform_host(seed, stream, first, count, lo, hi, _ptr(out)))
+    return out
+
+
+def trio_inputs_host(seed, batch, size, rows):
+    """BASELINE op-trio inputs: x ~ N(0,1) (stream 1), weight matrix
+    W ~ N(0,1) * float(1/sqrt(size)) (stream 2), softmax logits ~ N(0,1)
+    (stream 3), rmsnorm weight ~ U(0.5, 1.5) (stream 4), from the fixture
+    generator of experiments/blackwell/lowprec/reference.cpp:172-209."""
+    x = fill_normal_host(seed, 1, batch * size).reshape(batch, size)
+    W = fill_normal_host(seed, 2, rows * size,
+                         float(np.float32(1.0 / np.sqrt(size)))).reshape(rows, size)
+    logits = fill_normal_host(seed, 3, batch * size).reshape(batch, size)
+    w = fill_uniform_host(seed, 4, size, 0.5, 1.5)
+    return x, w, logits, W
+
+
+# ---------------------------------------------------------------------------
+# Row operations (device tensors)
+
+def rmsnorm(out, x, w, eps=RMS_EPS, stream=None):
+    rows, cols = x.shape
+    check(lib().ce_rmsnorm(_ptr(out), _ptr(x), _ptr(w), rows, cols, eps, _stream(stream)))
+    return out
+
+
+def rmsnorm_bf16(out, out_bf16, x, w, eps=RMS_EPS, stream=None):
+    rows, cols = x.shape
+    check(lib().ce_rmsnorm_bf16(_ptr(out), _ptr(out_bf16), out_bf16.shape[1], _ptr(x), _ptr(w),
+                                rows, cols, eps, _stream(stream)))
+    return out_bf16
+
+
+def softmax(out, logits, stream=None):
+    rows, cols = logits.shape
+    check(lib().ce_softmax(_ptr(out), _ptr(logits), rows, cols, _stream(stream)))
+    return out
+
+
+def gemv(product, matrix, x, stream=None):
+    rows, cols = matrix.shape
+    check(lib().ce_gemv(_ptr(product), _ptr(matrix), _ptr(x), rows, cols, _stream(stream)))
+    return product
+
+
+def llama2c_iteration(normalized, softmax_out, product, inp, weight, probabilities, matrix,
+                      eps=RMS_EPS, stream=None):
+    """One llama2c iteration in one launch (rmsnorm + softmax + GEMV on the
+    first `size` floats of the input)."""
+    batch, size = inp.shape
+    rows = matrix.shape[0]
+    check(lib().ce_llama2c_iteration(_ptr(normalized), _ptr(softmax_out), _ptr(product), _ptr(inp),
+                                     _ptr(weight), _ptr(probabilities), _ptr(matrix), batch, size,
+                                     rows, eps, _stream(stream)))
+
+
+# ---------------------------------------------------------------------------
+# GEMMs: d[m][n] = sum_k a[m][k] * b[n][k]
+
+def gemm_bf16(d, a, b, k=None, tile_n=0, stream=None):
+    """a, b: int16/uint16/bfloat16 tensors holding bf16 bits, K-contiguous."""
+    M, lda = a.shape
+    N, ldb = b.shape
+    K = lda if k is None else k
+    check(lib().ce_gemm_bf16_tile(_ptr(d), _ptr(a), _ptr(b), M, N, K, lda, ldb, d.shape[1], tile_n,
+                                  _stream(stream)))
+    return d
+
+
+def gemm_tf32(d, a, b, k=None, stream=None):
+    M, lda = a.shape
+    N, ldb = b.shape
+    K = lda if k is None else k
+    check(lib().ce_gemm_tf32(_ptr(d), _ptr(a), _ptr(b), M, N, K, lda, ldb, d.shape[1],
+                             _stream(stream)))
+    return d
+
+
+def gemm_fp32(d, a, b, k=None, stream=None):
+    M, lda = a.shape
+    N, ldb = b.shape
+    K = lda if k is None else k
+    check(lib().ce_gemm_fp32(_ptr(d), _ptr(a), _ptr(b), M, N, K, lda, ldb, d.shape[1],
+                             _stream(stream)))
+    return d
+
+
+def convert_bf16(out, inp, stream=None):
+    rows, cols = inp.shape
+    check(lib().ce_convert_bf16(_ptr(out), _ptr(inp), rows, cols, out.shape[1], _stream(stream)))
+    return out
+
+
+class Plan:
+    """Op-trio plan (rmsnorm -> GEMM on the normalized batch, + softmax) for
+    one shape and precision. Weights are converted once by set_weights."""
+
+    def __init__(self, batch, size, rows, precision=PREC_BF16):
+        self.batch, self.size, self.rows, self.precision = batch, size, rows, precision
+        h = ctypes.c_void_p()
+        check(lib().ce_plan_create(ctypes.byref(h), batch, size, rows, precision))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().ce_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_weights(self, W, stream=None):
+        check(lib().ce_plan_set_weights(self._h, _ptr(W), _stream(stream)))
+
+    def rmsnorm_gemm(self, out, x, norm_w, normalized=None, eps=RMS_EPS, stream=None):
+        check(lib().ce_plan_rmsnorm_gemm(self._h, _ptr(out), _ptr(normalized), _ptr(x),
+                                         _ptr(norm_w), eps, _stream(stream)))
+        return out
+
+    def rows(self, normalized, softmax_out, x, norm_w, logits, eps=RMS_EPS, stream=None):
+        check(lib().ce_plan_rows(self._h, _ptr(normalized), _ptr(softmax_out), _ptr(x),
+                                 _ptr(norm_w), _ptr(logits), eps, _stream(stream)))
+
+    def gemm(self, out, stream=None):
+        check(lib().ce_plan_gemm(self._h, _ptr(out), _stream(stream)))
+        return out
+
+    def trio(self, normalized, softmax_out, out, x, norm_w, logits, eps=RMS_EPS, stream=None):
+        check(lib().ce_plan_trio(self._h, _ptr(normalized), _ptr(softmax_out), _ptr(out), _ptr(x),
+                                 _ptr(norm_w), _ptr(logits), eps, _stream(stream)))
+        return out

@@ -1,0 +1,445 @@
+// extern "C" entry points of libce_b200.so (declared in include/ce_b200.h),
+// the host-side seeded input generators, and the op-trio plan.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "common.cuh"
+
+namespace ce {
+
+// ---- kernels defined in the other translation units ----
+int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, const float *input,
+                   const float *weight, float *softmax, const float *logits, float *product,
+                   const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
+                   int cols, int gemv_rows, float eps, cudaStream_t s);
+int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
+int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+              int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
+              cudaStream_t s);
+int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,
+              int ldd, const float *row_scale, const float *col_scale, int force_bn,
+              cudaStream_t s);
+int gemm_simt_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda,
+                   int ldb, int ldd, cudaStream_t s);
+int gemm_status();
+
+// ---------------------------------------------------------------------------
+// Status
+
+namespace {
+thread_local int t_last_code = CE_OK;
+thread_local std::string t_last_msg;
+}  // namespace
+
+int set_error(int code, const std::string &msg) {
+  t_last_code = code;
+  t_last_msg = msg;
+  return code;
+}
+
+int cuda_error(cudaError_t err, const char *what) {
+  return set_error(err == cudaErrorMemoryAllocation ? CE_ERR_NOMEM : CE_ERR_CUDA,
+                   format("%s failed: %s", what, cudaGetErrorString(err)));
+}
+
+std::string format(const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  return std::string(buf);
+}
+
+namespace {
+struct DeviceProps {
+  int sms = 0;
+  int major = 0;
+};
+DeviceProps props_of_current() {
+  static std::mutex mu;
+  static DeviceProps cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev].sms == 0) {
+    cudaDeviceGetAttribute(&cache[dev].sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&cache[dev].major, cudaDevAttrComputeCapabilityMajor, dev);
+  }
+  return cache[dev];
+}
+}  // namespace
+
+int sm_count() {
+  const int n = props_of_current().sms;
+  return n > 0 ? n : 148;
+}
+bool is_sm100() { return props_of_current().major == 10; }
+
+// ---------------------------------------------------------------------------
+// Seeded generators (host)
+
+namespace {
+
+inline uint64_t splitmix_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+// llama2c counter generator: mix(x) = splitmix64 finaliser of x + golden.
+inline uint64_t llama2c_mix(uint64_t x) { return splitmix_mix(x + 0x9e3779b97f4a7c15ull); }
+inline float llama2c_uniform(uint64_t seed, uint64_t stream, uint64_t index) {
+  const uint64_t bits = llama2c_mix(llama2c_mix(seed * 4 + stream) ^ index);
+  return (float)(int64_t)(bits >> 40) * (1.0f / 8388608.0f) - 1.0f;
+}
+// Output number k (1-based) of the sequential splitmix64 generator seeded
+// with `state`: the state advances by the golden increment per call, so any
+// output can be computed directly.
+inline uint64_t splitmix_nth(uint64_t state, uint64_t k) {
+  return splitmix_mix(state + k * 0x9e3779b97f4a7c15ull);
+}
+inline double unit_of(uint64_t x) { return (double)(x >> 11) * 0x1.0p-53; }
+
+template <class F>
+void parallel_for(int64_t n, F &&body) {
+  unsigned hw = std::thread::hardware_concurrency();
+  int64_t threads = hw == 0 ? 1 : (int64_t)hw;
+  if (n < (1 << 16)) threads = 1;
+  if (threads > n) threads = n > 0 ? n : 1;
+  if (threads <= 1) {
+    body(0, n);
+    return;
+  }
+  std::vector<std::thread> pool;
+  const int64_t chunk = (n + threads - 1) / threads;
+  for (int64_t t = 0; t < threads; ++t) {
+    const int64_t lo = t * chunk, hi = std::min<int64_t>(n, lo + chunk);
+    if (lo >= hi) break;
+    pool.emplace_back([&body, lo, hi] { body(lo, hi); });
+  }
+  for (auto &th : pool) th.join();
+}
+
+}  // namespace
+}  // namespace ce
+
+using namespace ce;
+
+// ---------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+const char *ce_version(void) { return "ce_b200 0.1"; }
+
+int ce_last_error(char *buf, size_t len) {
+  if (buf != nullptr && len > 0) {
+    std::strncpy(buf, t_last_msg.c_str(), len - 1);
+    buf[len - 1] = '\0';
+  }
+  return t_last_code;
+}
+
+int ce_device_info(int *sms, int *sm100) {
+  int dev = 0;
+  CE_CUDA_TRY(cudaGetDevice(&dev));
+  if (sms) *sms = sm_count();
+  if (sm100) *sm100 = is_sm100() ? 1 : 0;
+  return CE_OK;
+}
+
+// Synchronizes the device and returns CE_ERR_TIMEOUT if a bounded device
+// wait of a tensor-core kernel gave up since the last call (clearing it).
+int ce_device_status(void) { return gemm_status(); }
+
+int ce_fill_llama2c_host(int random, uint64_t seed, int batch, int size, int rows, float *input,
+                         float *probabilities, float *weight, float *matrix) {
+  CE_REQUIRE(batch >= 1 && size >= 1 && rows >= 1, "batch, size and rows must be >= 1");
+  const int64_t vec = (int64_t)batch * size, mat = (int64_t)rows * size;
+  if (!random) {
+    parallel_for(vec, [&](int64_t lo, int64_t hi) {
+      for (int64_t i = lo; i < hi; ++i) {
+        const float v = 1.0f + (float)(i % 4);
+        if (input) input[i] = v;
+        if (probabilities) probabilities[i] = v;
+      }
+    });
+    if (weight)
+      for (int i = 0; i < size; ++i) weight[i] = 1.0f;
+    if (matrix)
+      parallel_for(mat, [&](int64_t lo, int64_t hi) {
+        for (int64_t i = lo; i < hi; ++i) {
+          const int64_t r = i / size, c = i % size;
+          matrix[i] = c == (r % size) ? 1.0f : 0.0f;
+        }
+      });
+    return CE_OK;
+  }
+  parallel_for(vec, [&](int64_t lo, int64_t hi) {
+    for (int64_t i = lo; i < hi; ++i) {
+      if (input) input[i] = llama2c_uniform(seed, 0, (uint64_t)i);
+      if (probabilities) probabilities[i] = llama2c_uniform(seed, 1, (uint64_t)i);
+    }
+  });
+  if (weight)
+    for (int i = 0; i < size; ++i) weight[i] = llama2c_uniform(seed, 2, (uint64_t)i);
+  if (matrix)
+    parallel_for(mat, [&](int64_t lo, int64_t hi) {
+      for (int64_t i = lo; i < hi; ++i) matrix[i] = llama2c_uniform(seed, 3, (uint64_t)i);
+    });
+  return CE_OK;
+}
+
+int ce_fill_normal_host(uint64_t seed, uint64_t stream, int64_t first, int64_t count, float scale,
+                        float *out) {
+  CE_REQUIRE(first >= 0 && count >= 0 && out != nullptr, "bad normal fill range");
+  const uint64_t state = seed * 0x100000001b3ull + stream;
+  const double two_pi = 6.283185307179586476925286766559;
+  parallel_for(count, [&](int64_t lo, int64_t hi) {
+    for (int64_t j = lo; j < hi; ++j) {
+      const int64_t i = first + j, pair = i / 2;
+      const double u1 = unit_of(splitmix_nth(state, (uint64_t)(2 * pair + 1)));
+      const double u2 = unit_of(splitmix_nth(state, (uint64_t)(2 * pair + 2)));
+      const double radius = std::sqrt(-2.0 * std::log(1.0 - u1));
+      const double v = (i & 1) ? radius * std::sin(two_pi * u2) : radius * std::cos(two_pi * u2);
+      out[j] = (float)v * scale;
+    }
+  });
+  return CE_OK;
+}
+
+int ce_fill_uniform_host(uint64_t seed, uint64_t stream, int64_t first, int64_t count, float lo_v,
+                         float hi_v, float *out) {
+  CE_REQUIRE(first >= 0 && count >= 0 && out != nullptr, "bad uniform fill range");
+  const uint64_t state = seed * 0x100000001b3ull + stream;
+  parallel_for(count, [&](int64_t lo, int64_t hi) {
+    for (int64_t j = lo; j < hi; ++j) {
+      const double u = unit_of(splitmix_nth(state, (uint64_t)(first + j + 1)));
+      out[j] = (float)((double)lo_v + ((double)hi_v - (double)lo_v) * u);
+    }
+  });
+  return CE_OK;
+}
+
+int ce_rmsnorm(float *out, const float *x, const float *w, int rows, int cols, float eps,
+               ce_stream_t stream) {
+  CE_REQUIRE(rows >= 1 && cols >= 1, "rows and cols must be >= 1 (got %d, %d)", rows, cols);
+  return rows_iteration(out, nullptr, 0, x, w, nullptr, nullptr, nullptr, nullptr, nullptr, rows,
+                        0, cols, 0, eps, (cudaStream_t)stream);
+}
+
+int ce_rmsnorm_bf16(float *out, uint16_t *out_bf16, int ld_bf16, const float *x, const float *w,
+                    int rows, int cols, float eps, ce_stream_t stream) {
+  CE_REQUIRE(rows >= 1 && cols >= 1, "rows and cols must be >= 1 (got %d, %d)", rows, cols);
+  CE_REQUIRE(out_bf16 != nullptr, "null bf16 output");
+  return rows_iteration(out, out_bf16, ld_bf16, x, w, nullptr, nullptr, nullptr, nullptr, nullptr,
+                        rows, 0, cols, 0, eps, (cudaStream_t)stream);
+}
+
+int ce_softmax(float *out, const float *logits, int rows, int cols, ce_stream_t stream) {
+  CE_REQUIRE(rows >= 1 && cols >= 1, "rows and cols must be >= 1 (got %d, %d)", rows, cols);
+  return rows_iteration(nullptr, nullptr, 0, nullptr, nullptr, out, logits, nullptr, nullptr,
+                        nullptr, 0, rows, cols, 0, 0.f, (cudaStream_t)stream);
+}
+
+int ce_gemv(float *product, const float *matrix, const float *x, int rows, int cols,
+            ce_stream_t stream) {
+  CE_REQUIRE(rows >= 1 && cols >= 1, "rows and cols must be >= 1 (got %d, %d)", rows, cols);
+  return rows_iteration(nullptr, nullptr, 0, nullptr, nullptr, nullptr, nullptr, product, matrix,
+                        x, 0, 0, cols, rows, 0.f, (cudaStream_t)stream);
+}
+
+int ce_llama2c_iteration(float *normalized, float *softmax, float *product, const float *input,
+                         const float *weight, const float *probabilities, const float *matrix,
+                         int batch, int size, int rows, float eps, ce_stream_t stream) {
+  CE_REQUIRE(batch >= 1 && size >= 1 && rows >= 1, "batch, size and rows must be >= 1");
+  return rows_iteration(normalized, nullptr, 0, input, weight, softmax, probabilities, product,
+                        matrix, input, batch, batch, size, rows, eps, (cudaStream_t)stream);
+}
+
+int ce_gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+                 int ldb, int ldd, ce_stream_t stream) {
+  return gemm_bf16(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, (cudaStream_t)stream);
+}
+
+// Same as ce_gemm_bf16 with a forced tile width (test hook: 128, 160, 192,
+// 224 or 256 output columns per tile; 0 = automatic).
+int ce_gemm_bf16_tile(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+                      int ldb, int ldd, int tile_n, ce_stream_t stream) {
+  return gemm_bf16(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, tile_n,
+                   (cudaStream_t)stream);
+}
+
+int ce_gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,
+                 int ldd, ce_stream_t stream) {
+  return gemm_tf32(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, (cudaStream_t)stream);
+}
+
+int ce_gemm_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,
+                 int ldd, ce_stream_t stream) {
+  return gemm_simt_fp32(d, a, b, M, N, K, lda, ldb, ldd, (cudaStream_t)stream);
+}
+
+int ce_convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld_out,
+                    ce_stream_t stream) {
+  CE_REQUIRE(out && in, "null pointer");
+  return convert_bf16(out, in, rows, cols, ld_out, (cudaStream_t)stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Op-trio plan
+
+struct ce_plan {
+  int batch = 0, size = 0, rows = 0, precision = 0, device = 0;
+  int ld = 0;                    // padded K of the prepared operands
+  void *weights = nullptr;       // bf16 / fp32 [rows][ld], or fp32 [rows][size] (FP32)
+  void *activations = nullptr;   // bf16 / fp32 [batch][ld]
+  bool has_weights = false;
+};
+
+extern "C" {
+
+int ce_plan_create(ce_plan **out, int batch, int size, int rows, int precision) {
+  CE_REQUIRE(out != nullptr, "null plan pointer");
+  *out = nullptr;
+  CE_REQUIRE(batch >= 1 && size >= 1 && rows >= 1, "batch, size and rows must be >= 1");
+  CE_REQUIRE(precision == CE_PREC_FP32 || precision == CE_PREC_TF32 || precision == CE_PREC_BF16,
+             "precision %d is not available in this build", precision);
+  ce_plan *p = new ce_plan();
+  p->batch = batch;
+  p->size = size;
+  p->rows = rows;
+  p->precision = precision;
+  CE_CUDA_TRY(cudaGetDevice(&p->device));
+  p->ld = precision == CE_PREC_FP32 ? size : ((size + 63) / 64) * 64;
+  const size_t elem = precision == CE_PREC_BF16 ? 2 : 4;
+  cudaError_t e = cudaMalloc(&p->activations, (size_t)batch * p->ld * elem);
+  if (e != cudaSuccess) {
+    delete p;
+    return cuda_error(e, "cudaMalloc(activations)");
+  }
+  *out = p;
+  return CE_OK;
+}
+
+int ce_plan_destroy(ce_plan *p) {
+  if (p == nullptr) return CE_OK;
+  if (p->weights) cudaFree(p->weights);
+  if (p->activations) cudaFree(p->activations);
+  delete p;
+  return CE_OK;
+}
+
+int ce_plan_set_weights(ce_plan *p, const float *w, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && w != nullptr, "null plan or weights");
+  cudaStream_t s = (cudaStream_t)stream;
+  const size_t elem = p->precision == CE_PREC_BF16 ? 2 : 4;
+  if (p->weights == nullptr) CE_CUDA_TRY(cudaMalloc(&p->weights, (size_t)p->rows * p->ld * elem));
+  if (p->precision == CE_PREC_BF16) {
+    int rc = convert_bf16(static_cast<uint16_t *>(p->weights), w, p->rows, p->size, p->ld, s);
+    if (rc) return rc;
+  } else {
+    CE_CUDA_TRY(cudaMemset2DAsync(p->weights, (size_t)p->ld * 4, 0, (size_t)p->ld * 4, p->rows, s));
+    CE_CUDA_TRY(cudaMemcpy2DAsync(p->weights, (size_t)p->ld * 4, w, (size_t)p->size * 4,
+                                  (size_t)p->size * 4, p->rows, cudaMemcpyDeviceToDevice, s));
+  }
+  CE_CUDA_TRY(cudaStreamSynchronize(s));
+  p->has_weights = true;
+  return CE_OK;
+}
+
+static int plan_gemm(ce_plan *p, float *out, cudaStream_t s) {
+  switch (p->precision) {
+    case CE_PREC_BF16:
+      return gemm_bf16(out, static_cast<const uint16_t *>(p->activations),
+                       static_cast<const uint16_t *>(p->weights), p->batch, p->rows, p->size,
+                       p->ld, p->ld, p->rows, nullptr, nullptr, 0, s);
+    case CE_PREC_TF32:
+      return gemm_tf32(out, static_cast<const float *>(p->activations),
+                       static_cast<const float *>(p->weights), p->batch, p->rows, p->size, p->ld,
+                       p->ld, p->rows, nullptr, nullptr, 0, s);
+    default:
+      return gemm_simt_fp32(out, static_cast<const float *>(p->activations),
+                            static_cast<const float *>(p->weights), p->batch, p->rows, p->size,
+                            p->ld, p->ld, p->rows, s);
+  }
+}
+
+// Rows stage of the trio: rmsnorm (fp32 output plus the GEMM operand in the
+// plan's layout) and, if logits != NULL, the softmax rows in the same launch.
+static int plan_rows(ce_plan *p, float *normalized, float *softmax, const float *x,
+                     const float *norm_w, const float *logits, float eps, cudaStream_t s) {
+  const int nsoft = logits ? p->batch : 0;
+  if (p->precision == CE_PREC_BF16)
+    return rows_iteration(normalized, static_cast<uint16_t *>(p->activations), p->ld, x, norm_w,
+                          softmax, logits, nullptr, nullptr, nullptr, p->batch, nsoft, p->size, 0,
+                          eps, s);
+  // fp32 operand: the normalized rows themselves, written into the padded
+  // workspace (ld == size for FP32; for TF32 the padding columns stay 0 from
+  // the memset at the first call of this plan's stream work).
+  float *work = static_cast<float *>(p->activations);
+  int rc;
+  if (p->ld == p->size) {
+    rc = rows_iteration(work, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr, nullptr,
+                        p->batch, nsoft, p->size, 0, eps, s);
+    if (rc) return rc;
+    if (normalized)
+      CE_CUDA_TRY(cudaMemcpyAsync(normalized, work, (size_t)p->batch * p->size * 4,
+                                  cudaMemcpyDeviceToDevice, s));
+    return CE_OK;
+  }
+  float *dst = normalized ? normalized : work;
+  rc = rows_iteration(dst, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr, nullptr,
+                      p->batch, nsoft, p->size, 0, eps, s);
+  if (rc) return rc;
+  CE_CUDA_TRY(cudaMemset2DAsync(work, (size_t)p->ld * 4, 0, (size_t)p->ld * 4, p->batch, s));
+  CE_CUDA_TRY(cudaMemcpy2DAsync(work, (size_t)p->ld * 4, dst, (size_t)p->size * 4,
+                                (size_t)p->size * 4, p->batch, cudaMemcpyDeviceToDevice, s));
+  return CE_OK;
+}
+
+int ce_plan_rows(ce_plan *p, float *normalized, float *softmax, const float *x,
+                 const float *norm_w, const float *logits, float eps, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && x && norm_w, "null argument");
+  CE_REQUIRE((logits == nullptr) == (softmax == nullptr), "logits and softmax go together");
+  return plan_rows(p, normalized, softmax, x, norm_w, logits, eps, (cudaStream_t)stream);
+}
+
+int ce_plan_gemm(ce_plan *p, float *out, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && out != nullptr, "null argument");
+  CE_REQUIRE(p->has_weights, "ce_plan_set_weights has not been called");
+  return plan_gemm(p, out, (cudaStream_t)stream);
+}
+
+int ce_plan_rmsnorm_gemm(ce_plan *p, float *out, float *normalized, const float *x,
+                         const float *norm_w, float eps, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && out && x && norm_w, "null argument");
+  CE_REQUIRE(p->has_weights, "ce_plan_set_weights has not been called");
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = plan_rows(p, normalized, nullptr, x, norm_w, nullptr, eps, s);
+  if (rc) return rc;
+  return plan_gemm(p, out, s);
+}
+
+int ce_plan_trio(ce_plan *p, float *normalized, float *softmax, float *out, const float *x,
+                 const float *norm_w, const float *logits, float eps, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && out && x && norm_w && logits && softmax, "null argument");
+  CE_REQUIRE(p->has_weights, "ce_plan_set_weights has not been called");
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = plan_rows(p, normalized, softmax, x, norm_w, logits, eps, s);
+  if (rc) return rc;
+  return plan_gemm(p, out, s);
+}
+
+}  // extern "C"

@@ -1,0 +1,233 @@
+// Shared helpers of libce_b200: status reporting, launch checks and the
+// sm_100a PTX wrappers (mbarrier, TMA, tcgen05) used by the tensor-core
+// kernels. Every device-side wait here is bounded: it gives up after
+// kWaitLimitNs of wall time (read from %globaltimer), records where it gave
+// up in a device status word, and returns false so the caller can unwind.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/ce_b200.h"
+
+namespace ce {
+
+// ---------------------------------------------------------------------------
+// Host-side status
+
+// Records msg as the calling thread's last error and returns code.
+int set_error(int code, const std::string &msg);
+int cuda_error(cudaError_t err, const char *what);
+inline int ok() { return CE_OK; }
+
+#define CE_CUDA_TRY(call)                                             \
+  do {                                                                \
+    cudaError_t ce_err__ = (call);                                    \
+    if (ce_err__ != cudaSuccess) return ::ce::cuda_error(ce_err__, #call); \
+  } while (0)
+
+#define CE_LAUNCH_CHECK(what) CE_CUDA_TRY(cudaPeekAtLastError())
+
+#define CE_REQUIRE(cond, ...)                                          \
+  do {                                                                 \
+    if (!(cond)) return ::ce::set_error(CE_ERR_USAGE, ::ce::format(__VA_ARGS__)); \
+  } while (0)
+
+std::string format(const char *fmt, ...);
+
+int sm_count();          // SMs of the current device (cached per device)
+bool is_sm100();         // compute capability 10.x
+
+// Device status word of the kernels that wait on barriers. Each such .cu
+// file owns one as a file-scope __device__ variable; the host reads and
+// clears it after synchronizing (ce_device_status in capi.cu).
+struct DeviceStatus {
+  unsigned int code;    // 0 = fine, else CE_ERR_TIMEOUT
+  unsigned int where;   // which wait gave up (site id)
+  unsigned int block;   // blockIdx.x of the first failure
+  unsigned int pad;
+};
+
+// ---------------------------------------------------------------------------
+// Device-side helpers
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void report_timeout(DeviceStatus *st, unsigned where) {
+  if (st != nullptr && atomicCAS(&st->code, 0u, (unsigned)CE_ERR_TIMEOUT) == 0u) {
+    st->where = where;
+    st->block = blockIdx.x;
+  }
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// --- mbarrier --------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}"
+               ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Waits until the phase with the given parity has completed. Returns false
+// (and records the site) when kWaitLimitNs passes first, or when another
+// thread of the grid already reported a failure.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, DeviceStatus *st,
+                                          unsigned where) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long start = globaltimer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((spin & 255u) == 0u) {
+      if (globaltimer() - start > kWaitLimitNs) {
+        report_timeout(st, where);
+        return false;
+      }
+      if (st != nullptr && *(volatile unsigned *)&st->code != 0u) return false;
+    }
+  }
+}
+
+// Warp-collective bounded wait: every lane polls, the result is the AND over
+// the warp, so control flow after it stays warp-uniform (the .aligned
+// tcgen05 instructions and barriers that follow need that).
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, DeviceStatus *st,
+                                          unsigned where) {
+  const bool r = mbar_wait(bar, parity, st, where);
+  return __all_sync(0xffffffffu, r) != 0;
+}
+
+// --- TMA -------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const void *desc) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");
+}
+
+// 2-D tiled bulk tensor load into this CTA's shared memory, completion
+// signalled on bar (no multicast).
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *desc, uint64_t *bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(desc), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// --- tcgen05 ---------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;"
+               ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Arrives on bar once every tcgen05.mma issued so far by this thread has
+// completed (their shared-memory reads included).
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+
+// D(tmem) (+)= A(smem desc) x B(smem desc)^T, one instruction.
+template <int kKind>  // 0: kind::f16, 1: kind::tf32, 2: kind::f8f6f4
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  if constexpr (kKind == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else if constexpr (kKind == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  }
+}
+
+// 32 lanes x 32 consecutive fp32 columns per warp: thread t of the warp gets
+// lane (base lane + t), columns [col, col + 32).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor of a K-major operand tile stored with the
+// 128-byte swizzle (rows of 128 bytes, 8-row / 1024-byte swizzle atoms):
+// start address >> 4 in bits 0-13, leading byte offset (unused by swizzled
+// K-major layouts, encoded as 1) in bits 16-29, stride byte offset (1024 B
+// between 8-row groups) >> 4 in bits 32-45, descriptor version 1 in bits
+// 46-47, base offset 0 (atoms are 1024-byte aligned), layout type 2
+// (SWIZZLE_128B) in bits 61-63.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+}  // namespace ce

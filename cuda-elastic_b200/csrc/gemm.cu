@@ -1,0 +1,414 @@
+// Tensor-core GEMM for sm_100a: D[m][n] = sum_k A[m][k] * B[n][k].
+//
+// This is the B200 engine behind the reference's classifier / matmul GEMMs
+// (applications/loom_private/decoder/decoder_optimized.cu:343-439, SIMT
+// SGEMM with stream-K; experiments/blackwell/lowprec/decoder_lowprec.cu:85-127,
+// CUTLASS mma.sync / SM120 GEMMs). Design:
+//   * persistent kernel, one CTA per SM, static round-robin tile schedule
+//     (tile t -> m block t % tiles_m, n block t / tiles_m, so the CTAs that
+//     run together share B tiles through L2);
+//   * warp specialisation, 192 threads: warp 0 = TMA producer, warp 1 = TMEM
+//     allocator + tcgen05.mma issuer, warps 2-5 = epilogue (tcgen05.ld ->
+//     registers -> global);
+//   * operands staged by TMA (cp.async.bulk.tensor, no multicast) into a
+//     kStages ring of 128-byte-swizzled K-major tiles, 128 bytes of K per
+//     stage whatever the element type;
+//   * accumulators in TMEM, two buffers of BN fp32 columns, so the epilogue
+//     of tile i overlaps the main loop of tile i + 1;
+//   * every mbarrier wait is bounded (common.cuh); a wait that gives up
+//     records CE_ERR_TIMEOUT in g_gemm_status, the CTA drains its own TMA
+//     copies and MMAs (bounded), frees its TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace ce {
+
+static __device__ DeviceStatus g_gemm_status;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 512;
+constexpr int kRowBytes = 128;  // K bytes per stage (one swizzle row)
+
+// Operand kinds: 0 = bf16 (kind::f16), 1 = fp32 as tf32 (kind::tf32),
+// 2 = fp8 e4m3 (kind::f8f6f4).
+template <int kKind>
+struct Kind;
+template <>
+struct Kind<0> {
+  static constexpr int elem = 2;
+  static constexpr uint32_t fmt = 1;  // BF16
+};
+template <>
+struct Kind<1> {
+  static constexpr int elem = 4;
+  static constexpr uint32_t fmt = 2;  // TF32
+};
+template <>
+struct Kind<2> {
+  static constexpr int elem = 1;
+  static constexpr uint32_t fmt = 0;  // E4M3
+};
+
+template <int BN>
+struct Smem {
+  static constexpr int a_bytes = BM * kRowBytes;
+  static constexpr int b_bytes = BN * kRowBytes;
+  static constexpr int stage_bytes = a_bytes + b_bytes;
+  static constexpr int bar_offset = kStages * stage_bytes;
+  // full[kStages], empty[kStages], tmem_full[2], tmem_empty[2], drain, tmem holder
+  static constexpr int total = bar_offset + 256 + 1024;  // + alignment slack
+};
+
+// Instruction descriptor (kind::f16 / tf32 / f8f6f4): D fp32 (bits 4-5 = 1),
+// A and B format (bits 7-9, 10-12), both K-major (bits 15, 16 = 0),
+// N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+template <int kKind, int BN>
+__host__ __device__ constexpr uint32_t instr_desc() {
+  return (1u << 4) | (Kind<kKind>::fmt << 7) | (Kind<kKind>::fmt << 10) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+struct GemmArgs {
+  float *d;
+  const float *row_scale;  // optional per-m scale (nullptr = 1)
+  const float *col_scale;  // optional per-n scale (nullptr = 1)
+  int M, N, K, ldd;
+  int tiles_m, tiles_n, k_blocks;
+};
+
+template <int kKind, int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+            GemmArgs args) {
+  using S = Smem<BN>;
+  constexpr int kElemsPerRow = kRowBytes / Kind<kKind>::elem;  // K elements per stage
+  constexpr int kUmmaK = 32 / Kind<kKind>::elem;               // K elements per MMA
+  constexpr int kMmasPerStage = kElemsPerRow / kUmmaK;         // = 4
+  constexpr uint32_t kIdesc = instr_desc<kKind, BN>();
+  constexpr uint32_t kAccStride = 256;                         // TMEM columns per buffer
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_offset);
+  uint64_t *empty = full + kStages;
+  uint64_t *tmem_full = empty + kStages;
+  uint64_t *tmem_empty = tmem_full + 2;
+  uint64_t *drain = tmem_empty + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+
+  DeviceStatus *st = &g_gemm_status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_tiles = args.tiles_m * args.tiles_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 0) {
+    // ---------------- TMA producer (lane 0 issues; the warp stays converged)
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool okay = true;
+    for (int t = blockIdx.x; t < num_tiles && okay; t += gridDim.x) {
+      const int m0 = (t % args.tiles_m) * BM;
+      const int n0 = (t / args.tiles_m) * BN;
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (!warp_wait(&empty[stage], phase ^ 1u, st, 1)) {
+          okay = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t *a_dst = smem + stage * S::stage_bytes;
+          uint8_t *b_dst = a_dst + S::a_bytes;
+          mbar_arrive_expect_tx(&full[stage], S::stage_bytes);
+          tma_load_2d(a_dst, &tmA, &full[stage], kb * kElemsPerRow, m0);
+          tma_load_2d(b_dst, &tmB, &full[stage], kb * kElemsPerRow, n0);
+        }
+        __syncwarp();
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // Every copy this warp issued must land before the CTA can exit.
+    for (int s = 0; s < kStages; ++s)
+      if (issued_mask & (1u << s)) warp_wait(&full[s], (issued_parity >> s) & 1u, st, 2);
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (lane 0 issues)
+    int stage = 0;
+    uint32_t phase = 0;
+    bool okay = true;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles && okay; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!warp_wait(&tmem_empty[acc], acc_phase ^ 1u, st, 3)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)acc * kAccStride;
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (!warp_wait(&full[stage], phase, st, 4)) {
+          okay = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(smem + stage * S::stage_bytes);
+          const uint32_t b_addr = a_addr + S::a_bytes;
+#pragma unroll
+          for (int k = 0; k < kMmasPerStage; ++k) {
+            const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32);
+            const uint64_t b_desc = smem_desc_sw128(b_addr + k * 32);
+            tc_mma<kKind>(d_tmem, a_desc, b_desc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == kStages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (okay && lane == 0) tc_commit(&tmem_full[acc]);
+      __syncwarp();
+    }
+    // All MMAs issued by this warp complete before TMEM is released.
+    if (lane == 0) tc_commit(drain);
+    __syncwarp();
+    warp_wait(drain, 0, st, 5);
+  } else {
+    // ---------------- Epilogue (warps 2-5)
+    const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!warp_wait(&tmem_full[acc], acc_phase, st, 6)) break;
+      tc_fence_after();
+      const int m0 = (t % args.tiles_m) * BM;
+      const int n0 = (t / args.tiles_m) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const float rs = (args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f;
+      float *drow = args.d + (size_t)row * args.ldd;
+      const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.d) & 15u) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kAccStride + c, r);
+        tmem_ld_wait();
+        if (row < args.M) {
+          const int col0 = n0 + c;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(r[j]) * rs;
+            if (args.col_scale != nullptr && col0 + j < args.N) x *= args.col_scale[col0 + j];
+            v[j] = x;
+          }
+          if (vec_ok && col0 + 32 <= args.N) {
+            float4 *dst = reinterpret_cast<float4 *>(drow + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.N) drow[col0 + j] = v[j];
+          }
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// K-major operand [outer][ld] with `inner` valid K elements; box = 128 bytes
+// of K by box_outer rows, 128-byte swizzle, zero fill out of bounds.
+int make_operand_map(CUtensorMap *map, const void *base, CUtensorMapDataType dtype, int elem,
+                     int inner, int outer, int ld, int box_outer) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return set_error(CE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * (cuuint64_t)elem};
+  cuuint32_t box[2] = {(cuuint32_t)(kRowBytes / elem), (cuuint32_t)box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(CE_ERR_CUDA, format("cuTensorMapEncodeTiled failed (%d) for %dx%d ld %d", (int)r, outer, inner, ld));
+  return CE_OK;
+}
+
+template <int kKind, int BN>
+int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int grid,
+                cudaStream_t s) {
+  using S = Smem<BN>;
+  static bool configured[64] = {};  // the attribute is per function and device
+  int dev = 0;
+  CE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    CE_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<kKind, BN>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, S::total));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  gemm_kernel<kKind, BN><<<grid, kThreads, S::total, s>>>(ta, tb, args);
+  CE_LAUNCH_CHECK("gemm_kernel");
+  return CE_OK;
+}
+
+// Tile width choice: the candidate that minimises (waves x BN), i.e. the
+// busiest SM's column count; ties go to the wider tile.
+int choose_bn(int M, int N, int sms) {
+  static const int kCandidates[] = {256, 224, 192, 160, 128};
+  int best = 256;
+  long long best_cost = -1;
+  const int tiles_m = (M + BM - 1) / BM;
+  for (int bn : kCandidates) {
+    const long long tiles = (long long)tiles_m * ((N + bn - 1) / bn);
+    const long long waves = (tiles + sms - 1) / sms;
+    const long long cost = waves * bn;
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+template <int kKind>
+int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
+                  int ldd, const float *row_scale, const float *col_scale, int force_bn,
+                  cudaStream_t s) {
+  constexpr int elem = Kind<kKind>::elem;
+  const CUtensorMapDataType dt = kKind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : kKind == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                              : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CE_REQUIRE(M >= 1 && N >= 1 && K >= 1, "GEMM dims must be >= 1 (M=%d N=%d K=%d)", M, N, K);
+  CE_REQUIRE(lda >= K && ldb >= K && ldd >= N, "leading dimensions too small");
+  CE_REQUIRE((lda * elem) % 16 == 0 && (ldb * elem) % 16 == 0,
+             "operand row strides must be multiples of 16 bytes (lda=%d ldb=%d)", lda, ldb);
+  CE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0,
+             "operand base pointers must be 16-byte aligned");
+  CE_REQUIRE(d != nullptr, "null output");
+  if (!is_sm100()) return set_error(CE_ERR_USAGE, "tcgen05 GEMM needs an sm_100 device");
+  const int sms = sm_count();
+  const int bn = force_bn > 0 ? force_bn : choose_bn(M, N, sms);
+  CUtensorMap ta, tb;
+  int rc = make_operand_map(&ta, a, dt, elem, K, M, lda, BM);
+  if (rc) return rc;
+  rc = make_operand_map(&tb, b, dt, elem, K, N, ldb, bn);
+  if (rc) return rc;
+  GemmArgs args;
+  args.d = d;
+  args.row_scale = row_scale;
+  args.col_scale = col_scale;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.ldd = ldd;
+  args.tiles_m = (M + BM - 1) / BM;
+  args.tiles_n = (N + bn - 1) / bn;
+  args.k_blocks = (K + (kRowBytes / elem) - 1) / (kRowBytes / elem);
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int grid = tiles < sms ? tiles : sms;
+  switch (bn) {
+    case 256: return launch_gemm<kKind, 256>(ta, tb, args, grid, s);
+    case 224: return launch_gemm<kKind, 224>(ta, tb, args, grid, s);
+    case 192: return launch_gemm<kKind, 192>(ta, tb, args, grid, s);
+    case 160: return launch_gemm<kKind, 160>(ta, tb, args, grid, s);
+    case 128: return launch_gemm<kKind, 128>(ta, tb, args, grid, s);
+    default: return set_error(CE_ERR_USAGE, format("unsupported tile width %d", bn));
+  }
+}
+
+}  // namespace
+
+int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+              int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
+              cudaStream_t s) {
+  return gemm_dispatch<0>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn, s);
+}
+
+int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,
+              int ldd, const float *row_scale, const float *col_scale, int force_bn,
+              cudaStream_t s) {
+  return gemm_dispatch<1>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn, s);
+}
+
+int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K, int lda,
+              int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
+              cudaStream_t s) {
+  return gemm_dispatch<2>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn, s);
+}
+
+// Synchronizes the device, reads and clears the GEMM status word.
+int gemm_status() {
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  DeviceStatus h{};
+  CE_CUDA_TRY(cudaMemcpyFromSymbol(&h, g_gemm_status, sizeof(h)));
+  if (h.code != 0) {
+    DeviceStatus zero{};
+    CE_CUDA_TRY(cudaMemcpyToSymbol(g_gemm_status, &zero, sizeof(zero)));
+    return set_error(CE_ERR_TIMEOUT, format("tensor-core GEMM wait %u gave up in block %u", h.where, h.block));
+  }
+  return CE_OK;
+}
+
+}  // namespace ce

@@ -1,0 +1,473 @@
+// Row kernels of the llama2c iteration: RMSNorm, softmax, GEMV and their
+// one-launch fusion. All four are HBM streams (each input read once, each
+// output written once), so they are written for bandwidth:
+//   * one CTA per 64 KiB row, the row held in registers as float4s loaded
+//     with 16-byte streaming loads (ld.global.cs), reduced with warp
+//     shuffles plus one shared-memory step, written back from the same
+//     registers with streaming stores -- one read and one write per element;
+//   * GEMV: one warp per matrix row, 16-byte streaming loads unrolled so each
+//     warp keeps 4 KiB in flight, the x vector served from L1/L2;
+//   * shapes whose rows do not fit the register budget, or whose rows are
+//     not 16-byte aligned, take a generic two-pass path in the same files.
+// Reference kernels replaced: llama2c/llama2c_cuda_graph.cu:58-162 and the
+// fused llama2c/llama2c_sota.cu:263-298.
+#include <cuda_bf16.h>
+#include <float.h>
+
+#include "common.cuh"
+
+namespace ce {
+namespace {
+
+constexpr int kRowThreads = 512;      // register path: threads per row
+constexpr int kGenericThreads = 512;  // generic path
+constexpr int kGemvWarps = 16;        // GEMV rows per 512-thread block
+constexpr int kGemvUnroll = 8;        // float4 loads in flight per lane
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum / max, result broadcast to every thread. `scratch` holds 32
+// floats; the trailing barrier lets the caller reuse it immediately.
+__device__ __forceinline__ float block_sum(float v, float *scratch) {
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  v = lane < (int)(blockDim.x >> 5) ? scratch[lane] : 0.0f;
+  v = warp_sum(v);
+  __syncthreads();
+  return v;
+}
+__device__ __forceinline__ float block_max(float v, float *scratch) {
+  v = warp_max(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  v = lane < (int)(blockDim.x >> 5) ? scratch[lane] : -FLT_MAX;
+  v = warp_max(v);
+  __syncthreads();
+  return v;
+}
+
+// ---------------------------------------------------------------------------
+// Register-resident row bodies. Each thread owns float4 slots
+// threadIdx.x + j * blockDim.x, j < NV, of a row of cols4 float4s.
+
+template <int NV>
+__device__ __forceinline__ void load_row(float4 (&v)[NV], const float4 *row, int cols4) {
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    v[j] = i < cols4 ? __ldcs(row + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+}
+
+// RMSNorm of one row: out = x * scale * w, scale = 1 / sqrtf(ss / cols + eps)
+// (IEEE division and square root, the llama2.c order of run.c's rmsnorm as
+// restated in applications/loom_private/decoder/decoder.cu:71-76).
+template <int NV>
+__device__ __forceinline__ void rmsnorm_row(const float4 *x, const float4 *w, float4 *out,
+                                            uint2 *out_bf16, int cols4, int cols,
+                                            float eps, float *scratch) {
+  float4 v[NV];
+  load_row<NV>(v, x, cols4);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  ss = block_sum(ss, scratch);
+  const float scale = 1.0f / sqrtf(ss / (float)cols + eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4) {
+      const float4 g = __ldg(w + i);
+      float4 o;
+      o.x = g.x * (scale * v[j].x);
+      o.y = g.y * (scale * v[j].y);
+      o.z = g.z * (scale * v[j].z);
+      o.w = g.w * (scale * v[j].w);
+      if (out != nullptr) __stcs(out + i, o);
+      if (out_bf16 != nullptr) {
+        __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y);
+        __nv_bfloat162 hi = __floats2bfloat162_rn(o.z, o.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t *>(&lo);
+        packed.y = *reinterpret_cast<uint32_t *>(&hi);
+        out_bf16[i] = packed;
+      }
+    }
+  }
+}
+
+// Softmax of one row held in registers: max, then e = expf(l - max) kept in
+// registers, their sum, then e / sum. One read, one write.
+template <int NV>
+__device__ __forceinline__ void softmax_row(const float4 *logits, float4 *out, int cols4,
+                                            float *scratch) {
+  float4 v[NV];
+  load_row<NV>(v, logits, cols4);
+  float m = -FLT_MAX;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4) m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+  }
+  m = block_max(m, scratch);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4) {
+      v[j].x = expf(v[j].x - m);
+      v[j].y = expf(v[j].y - m);
+      v[j].z = expf(v[j].z - m);
+      v[j].w = expf(v[j].w - m);
+      s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+    }
+  }
+  s = block_sum(s, scratch);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4) {
+      float4 o;
+      o.x = v[j].x / s;
+      o.y = v[j].y / s;
+      o.z = v[j].z / s;
+      o.w = v[j].w / s;
+      __stcs(out + i, o);
+    }
+  }
+}
+
+// GEMV rows: warp w of the block computes product[row0 + w].
+__device__ __forceinline__ void gemv_rows_vec(const float4 *matrix, const float4 *x, float *product,
+                                              int row0, int rows, int cols4) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  for (int row = row0 + warp; row < rows && row < row0 + nwarps; row += nwarps) {
+    const float4 *m = matrix + (size_t)row * cols4;
+    float acc[kGemvUnroll];
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) acc[u] = 0.f;
+    int i = lane;
+    for (; i + 32 * (kGemvUnroll - 1) < cols4; i += 32 * kGemvUnroll) {
+      float4 a[kGemvUnroll];
+#pragma unroll
+      for (int u = 0; u < kGemvUnroll; ++u) a[u] = __ldcs(m + i + 32 * u);
+#pragma unroll
+      for (int u = 0; u < kGemvUnroll; ++u) {
+        const float4 b = __ldg(x + i + 32 * u);
+        acc[u] += a[u].x * b.x + a[u].y * b.y + a[u].z * b.z + a[u].w * b.w;
+      }
+    }
+    for (; i < cols4; i += 32) {
+      const float4 a = __ldcs(m + i);
+      const float4 b = __ldg(x + i);
+      acc[0] += a.x * b.x + a.y * b.y + a.z * b.z + a.w * b.w;
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int u = 0; u < kGemvUnroll; ++u) sum += acc[u];
+    sum = warp_sum(sum);
+    if (lane == 0) product[row] = sum;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernels
+
+// Work of one fused launch. Blocks [0, 2*min(nr,ns)) alternate rmsnorm and
+// softmax rows, then the leftover rows of the longer list, then GEMV blocks
+// of kGemvWarps rows each.
+struct IterationWork {
+  float *normalized;
+  uint2 *normalized_bf16;
+  int ld_bf16_4;  // bf16 row stride in units of 4 elements
+  const float *input;
+  const float *weight;
+  float *softmax;
+  const float *logits;
+  float *product;
+  const float *matrix;
+  const float *gemv_x;
+  int cols;
+  int rms_rows;
+  int softmax_rows;
+  int gemv_rows;
+  float eps;
+};
+
+template <int NV>
+__global__ void __launch_bounds__(kRowThreads, (NV <= 8 ? 2 : 1))
+iteration_kernel(IterationWork w) {
+  __shared__ float scratch[32];
+  const int cols4 = w.cols >> 2;
+  int b = blockIdx.x;
+  const int both = min(w.rms_rows, w.softmax_rows);
+  int rms_row = -1, soft_row = -1;
+  if (b < 2 * both) {
+    if (b & 1) soft_row = b >> 1; else rms_row = b >> 1;
+  } else {
+    b -= 2 * both;
+    const int extra_rms = w.rms_rows - both, extra_soft = w.softmax_rows - both;
+    if (b < extra_rms) {
+      rms_row = both + b;
+    } else if (b < extra_rms + extra_soft) {
+      soft_row = both + (b - extra_rms);
+    } else {
+      b -= extra_rms + extra_soft;
+      gemv_rows_vec(reinterpret_cast<const float4 *>(w.matrix),
+                    reinterpret_cast<const float4 *>(w.gemv_x), w.product,
+                    b * (int)(blockDim.x >> 5), w.gemv_rows, cols4);
+      return;
+    }
+  }
+  if (rms_row >= 0) {
+    const size_t off = (size_t)rms_row * cols4;
+    rmsnorm_row<NV>(reinterpret_cast<const float4 *>(w.input) + off,
+                    reinterpret_cast<const float4 *>(w.weight),
+                    w.normalized ? reinterpret_cast<float4 *>(w.normalized) + off : nullptr,
+                    w.normalized_bf16 ? w.normalized_bf16 + (size_t)rms_row * w.ld_bf16_4 : nullptr,
+                    cols4, w.cols, w.eps, scratch);
+  } else {
+    const size_t off = (size_t)soft_row * cols4;
+    softmax_row<NV>(reinterpret_cast<const float4 *>(w.logits) + off,
+                    reinterpret_cast<float4 *>(w.softmax) + off, cols4, scratch);
+  }
+}
+
+// Generic path: any cols, any alignment, rows longer than the register
+// budget. One 512-thread block per row; RMSNorm reads its row twice
+// (sum of squares, then scale), softmax runs an online max/sum pass then a
+// write pass. GEMV: warp per row, scalar loads.
+__global__ void __launch_bounds__(kGenericThreads)
+generic_rmsnorm_kernel(float *out, __nv_bfloat16 *out_bf16, int ld_bf16, const float *x,
+                       const float *w, int rows, int cols, float eps) {
+  __shared__ float scratch[32];
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const float *xr = x + (size_t)row * cols;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float v = xr[i];
+    ss += v * v;
+  }
+  ss = block_sum(ss, scratch);
+  const float scale = 1.0f / sqrtf(ss / (float)cols + eps);
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float o = w[i] * (scale * xr[i]);
+    if (out) out[(size_t)row * cols + i] = o;
+    if (out_bf16) out_bf16[(size_t)row * ld_bf16 + i] = __float2bfloat16_rn(o);
+  }
+}
+
+__global__ void __launch_bounds__(kGenericThreads)
+generic_softmax_kernel(float *out, const float *logits, int rows, int cols) {
+  __shared__ float sm[32], ss[32];
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const float *l = logits + (size_t)row * cols;
+  // Online pass: running maximum m and sum s of exp(l - m).
+  float m = -FLT_MAX, s = 0.f;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) {
+    const float v = l[i];
+    if (v > m) {
+      s = s * expf(m - v) + 1.0f;
+      m = v;
+    } else {
+      s += expf(v - m);
+    }
+  }
+  // Combine (m, s) pairs across the block.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+    const float mm = fmaxf(m, m2);
+    s = s * expf(m - mm) + s2 * expf(m2 - mm);
+    m = mm;
+  }
+  if (lane == 0) { sm[warp] = m; ss[warp] = s; }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    m = lane < nw ? sm[lane] : -FLT_MAX;
+    s = lane < nw ? ss[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float mm = fmaxf(m, m2);
+      s = s * expf(m - mm) + s2 * expf(m2 - mm);
+      m = mm;
+    }
+    if (lane == 0) { sm[0] = m; ss[0] = s; }
+  }
+  __syncthreads();
+  m = sm[0];
+  s = ss[0];
+  float *o = out + (size_t)row * cols;
+  for (int i = threadIdx.x; i < cols; i += blockDim.x) o[i] = expf(l[i] - m) / s;
+}
+
+__global__ void __launch_bounds__(kGenericThreads)
+generic_gemv_kernel(float *product, const float *matrix, const float *x, int rows, int cols) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (row >= rows) return;
+  const float *m = matrix + (size_t)row * cols;
+  float acc = 0.f;
+  for (int i = lane; i < cols; i += 32) acc += __ldcs(m + i) * __ldg(x + i);
+  acc = warp_sum(acc);
+  if (lane == 0) product[row] = acc;
+}
+
+// Pads columns [cols, ld) of a bf16 matrix with zeros.
+__global__ void pad_bf16_kernel(__nv_bfloat16 *out, int rows, int cols, int ld) {
+  const int pad = ld - cols;
+  const size_t total = (size_t)rows * pad;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / pad, c = cols + i % pad;
+    out[r * ld + c] = __float2bfloat16_rn(0.f);
+  }
+}
+
+__global__ void convert_bf16_kernel(__nv_bfloat16 *out, const float *in, int rows, int cols,
+                                    int ld) {
+  const size_t total = (size_t)rows * ld;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / ld, c = i % ld;
+    out[i] = __float2bfloat16_rn(c < (size_t)cols ? in[r * cols + c] : 0.f);
+  }
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Picks float4 slots per thread (NV) and threads per row for the register
+// path; returns 0 if the row is too long (generic path).
+int pick_nv(int cols4, int *threads) {
+  static const int kNv[] = {1, 2, 4, 8, 16};
+  for (int nv : kNv) {
+    const int need = (cols4 + nv - 1) / nv;
+    if (need <= kRowThreads) {
+      *threads = ((need + 31) / 32) * 32;
+      if (*threads < 32) *threads = 32;
+      return nv;
+    }
+  }
+  return 0;
+}
+
+int launch_iteration(const IterationWork &w, int nv, int threads, cudaStream_t s) {
+  const int both = w.rms_rows < w.softmax_rows ? w.rms_rows : w.softmax_rows;
+  const int row_blocks = 2 * both + (w.rms_rows - both) + (w.softmax_rows - both);
+  const int warps = threads / 32;
+  const int gemv_blocks = w.gemv_rows > 0 ? (w.gemv_rows + warps - 1) / warps : 0;
+  const int grid = row_blocks + gemv_blocks;
+  if (grid == 0) return CE_OK;
+  switch (nv) {
+    case 1: iteration_kernel<1><<<grid, threads, 0, s>>>(w); break;
+    case 2: iteration_kernel<2><<<grid, threads, 0, s>>>(w); break;
+    case 4: iteration_kernel<4><<<grid, threads, 0, s>>>(w); break;
+    case 8: iteration_kernel<8><<<grid, threads, 0, s>>>(w); break;
+    case 16: iteration_kernel<16><<<grid, threads, 0, s>>>(w); break;
+    default: return set_error(CE_ERR_USAGE, std::string("internal: bad vector count"));
+  }
+  CE_LAUNCH_CHECK("iteration_kernel");
+  return CE_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Entry points used by capi.cu
+
+int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, const float *input,
+                   const float *weight, float *softmax, const float *logits, float *product,
+                   const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
+                   int cols, int gemv_rows, float eps, cudaStream_t s) {
+  CE_REQUIRE(cols >= 1, "cols must be >= 1 (got %d)", cols);
+  CE_REQUIRE(batch_rms >= 0 && batch_softmax >= 0 && gemv_rows >= 0, "negative row count");
+  if (batch_rms > 0) CE_REQUIRE(input && weight && (normalized || normalized_bf16), "rmsnorm needs input, weight and an output");
+  if (batch_softmax > 0) CE_REQUIRE(logits && softmax, "softmax needs logits and an output");
+  if (gemv_rows > 0) CE_REQUIRE(matrix && gemv_x && product, "gemv needs matrix, x and product");
+  if (normalized_bf16) CE_REQUIRE(ld_bf16 >= cols && ld_bf16 % 8 == 0, "bf16 leading dimension must be >= cols and a multiple of 8 (got %d)", ld_bf16);
+  int threads = 0;
+  const int nv = (cols % 4 == 0) ? pick_nv(cols / 4, &threads) : 0;
+  const bool vec = nv > 0 && aligned16(normalized) && aligned16(input) && aligned16(weight) &&
+                   aligned16(softmax) && aligned16(logits) && aligned16(matrix) &&
+                   aligned16(gemv_x) && aligned16(normalized_bf16);
+  if (vec) {
+    IterationWork w;
+    w.normalized = normalized;
+    w.normalized_bf16 = reinterpret_cast<uint2 *>(normalized_bf16);
+    w.ld_bf16_4 = ld_bf16 / 4;
+    w.input = input;
+    w.weight = weight;
+    w.softmax = softmax;
+    w.logits = logits;
+    w.product = product;
+    w.matrix = matrix;
+    w.gemv_x = gemv_x;
+    w.cols = cols;
+    w.rms_rows = batch_rms;
+    w.softmax_rows = batch_softmax;
+    w.gemv_rows = gemv_rows;
+    w.eps = eps;
+    // The GEMV blocks use the same block size; at least 256 threads keeps
+    // enough warps per GEMV block.
+    if (gemv_rows > 0 && threads < 256) threads = 256;
+    int rc = launch_iteration(w, nv, threads, s);
+    if (rc != CE_OK) return rc;
+  } else {
+    if (batch_rms > 0) {
+      generic_rmsnorm_kernel<<<batch_rms, kGenericThreads, 0, s>>>(
+          normalized, reinterpret_cast<__nv_bfloat16 *>(normalized_bf16), ld_bf16, input, weight,
+          batch_rms, cols, eps);
+      CE_LAUNCH_CHECK("generic_rmsnorm_kernel");
+    }
+    if (batch_softmax > 0) {
+      generic_softmax_kernel<<<batch_softmax, kGenericThreads, 0, s>>>(softmax, logits,
+                                                                      batch_softmax, cols);
+      CE_LAUNCH_CHECK("generic_softmax_kernel");
+    }
+    if (gemv_rows > 0) {
+      const int warps = kGenericThreads / 32;
+      generic_gemv_kernel<<<(gemv_rows + warps - 1) / warps, kGenericThreads, 0, s>>>(
+          product, matrix, gemv_x, gemv_rows, cols);
+      CE_LAUNCH_CHECK("generic_gemv_kernel");
+    }
+  }
+  if (normalized_bf16 && ld_bf16 > cols && batch_rms > 0) {
+    pad_bf16_kernel<<<256, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16 *>(normalized_bf16),
+                                        batch_rms, cols, ld_bf16);
+    CE_LAUNCH_CHECK("pad_bf16_kernel");
+  }
+  return CE_OK;
+}
+
+int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s) {
+  CE_REQUIRE(rows >= 1 && cols >= 1 && ld >= cols, "bad conversion shape %dx%d ld %d", rows, cols, ld);
+  const size_t total = (size_t)rows * ld;
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  convert_bf16_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16 *>(out), in, rows,
+                                             cols, ld);
+  CE_LAUNCH_CHECK("convert_bf16_kernel");
+  return CE_OK;
+}
+
+}  // namespace ce

@@ -1,0 +1,213 @@
+/*
+ * ce_b200.h -- C ABI of the B200-native llama2c hot path (libce_b200.so).
+ *
+ * The reference (ankaijin/cuda-elastic) exposes this path only as CUDA
+ * kernels with raw-pointer signatures, launched on a caller's stream by a
+ * per-workload harness. Every entry point below replaces one of those
+ * kernels or harness steps; the comment above each names the reference
+ * symbol (file:line, paths relative to the reference project root).
+ *
+ * Conventions
+ *   - Every function returns an int status: CE_OK (0) or one of CE_ERR_*.
+ *     The status values follow the loom_private harness exit codes
+ *     (applications/loom_private/common/lp_harness.cuh:88-92): usage errors
+ *     are 2, CUDA errors 70. ce_last_error() returns the message of the last
+ *     failure on the calling host thread.
+ *   - Pointers named *_dev are device pointers allocated by the caller; host
+ *     pointers are named *_host. Matrices are row-major, rows contiguous.
+ *   - Enqueue functions (everything that takes a ce_stream_t except the
+ *     *_create / *_set_* setup calls) allocate nothing, never synchronize the
+ *     host and read no environment variable, so they can be captured in a
+ *     CUDA graph (the reference's lp::Workload::enqueue_compute contract,
+ *     lp_harness.cuh:236-239).
+ *   - ce_stream_t is binary-identical to cudaStream_t / CUstream; NULL is the
+ *     legacy default stream.
+ */
+#ifndef CE_B200_H
+#define CE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *ce_stream_t;
+
+/* Status codes. */
+#define CE_OK 0
+#define CE_ERR_USAGE 2        /* invalid argument or unsupported shape */
+#define CE_ERR_CUDA 70        /* a CUDA runtime / driver call failed */
+#define CE_ERR_TIMEOUT 71     /* a bounded device-side wait ran out */
+#define CE_ERR_NOMEM 72       /* device or pinned allocation failed */
+
+/* Arithmetic of the matmul (the classifier / GEMM operand precision). */
+#define CE_PREC_FP32 0        /* SIMT fp32, sequential k, separate mul+add */
+#define CE_PREC_TF32 1        /* tcgen05 kind::tf32 on fp32 operands */
+#define CE_PREC_BF16 2        /* tcgen05 kind::f16, bf16 operands */
+#define CE_PREC_FP8_E4M3 3    /* tcgen05 kind::f8f6f4, per-row fp32 scales */
+#define CE_PREC_MXFP6_E3M2 4  /* reserved: block-scaled E3M2, UE8M0 / 32 */
+#define CE_PREC_NVFP4_E2M1 5  /* reserved: block-scaled E2M1, UE4M3 / 16 */
+
+/* ------------------------------------------------------------------ */
+/* Library                                                             */
+
+/* Version string of the library ("ce_b200 <major>.<minor>"). */
+const char *ce_version(void);
+
+/* Copies the last error message of the calling thread into buf (always
+ * NUL-terminated when len > 0) and returns the last status. */
+int ce_last_error(char *buf, size_t len);
+
+/* Number of SMs of the current device and whether it is an sm_100 part
+ * (tcgen05 paths need it). */
+int ce_device_info(int *sm_count, int *is_sm100);
+
+/* Synchronizes the current device and reports whether a bounded device-side
+ * wait of a tensor-core kernel gave up since the last call (CE_ERR_TIMEOUT,
+ * then cleared). The reference's stream-K consumer waits without a limit
+ * (applications/loom_private/decoder/decoder_optimized.cu:391-394); every
+ * wait of this library is bounded and reported here instead. */
+int ce_device_status(void);
+
+/* ------------------------------------------------------------------ */
+/* Seeded inputs (host side, multithreaded).                           */
+
+/* llama2c input generator: llama2c/llama2c_common.h:105-132 (fill_inputs).
+ * random == 0: deterministic inputs (1,2,3,4 repeating; weight 1; shifted
+ * identity matrix). random != 0: uniform in [-1,1) from the counter-based
+ * splitmix64 stream (seed, stream 0 input, 1 probabilities, 2 weight,
+ * 3 matrix). Any output pointer may be NULL to skip it. */
+int ce_fill_llama2c_host(int random, uint64_t seed, int batch, int size, int rows,
+                         float *input_host, float *probabilities_host,
+                         float *weight_host, float *matrix_host);
+
+/* Standard normals of the reference's fixture generator
+ * (experiments/blackwell/lowprec/reference.cpp:172-194): splitmix64 seeded
+ * with seed * 0x100000001b3 + stream, Box-Muller pairs in double, each
+ * value times `scale` (float product, reference.cpp:203-209), rounded to
+ * float. Writes elements [first, first + count) of the stream. */
+int ce_fill_normal_host(uint64_t seed, uint64_t stream, int64_t first, int64_t count,
+                        float scale, float *out_host);
+
+/* Uniform values lo + (hi - lo) * u, u = (splitmix64 >> 11) * 2^-53, of the
+ * same seeded stream layout as ce_fill_normal_host (one value per call of
+ * the generator). */
+int ce_fill_uniform_host(uint64_t seed, uint64_t stream, int64_t first, int64_t count,
+                         float lo, float hi, float *out_host);
+
+/* ------------------------------------------------------------------ */
+/* Row operations (HBM-bound).                                         */
+
+/* RMSNorm: out[b,i] = x[b,i] * rsqrt(sum_i x[b,i]^2 / cols + eps) * w[i].
+ * Replaces rmsnorm_kernel, llama2c/llama2c_cuda_graph.cu:58-78. */
+int ce_rmsnorm(float *out_dev, const float *x_dev, const float *w_dev, int rows, int cols,
+               float eps, ce_stream_t stream);
+
+/* Row softmax: out[b,i] = exp(l[b,i] - max_b) / sum_i exp(l[b,i] - max_b).
+ * Replaces softmax_kernel, llama2c/llama2c_cuda_graph.cu:82-115. */
+int ce_softmax(float *out_dev, const float *logits_dev, int rows, int cols,
+               ce_stream_t stream);
+
+/* GEMV: product[r] = sum_c matrix[r,c] * x[c] (x = the first `cols` floats
+ * of the raw input). Replaces matmul_kernel / matmul_coalesced_kernel,
+ * llama2c/llama2c_cuda_graph.cu:119-162. */
+int ce_gemv(float *product_dev, const float *matrix_dev, const float *x_dev, int rows,
+            int cols, ce_stream_t stream);
+
+/* The llama2c iteration in one launch: rmsnorm of input [batch][size],
+ * softmax of probabilities [batch][size], GEMV of matrix [rows][size] with
+ * input row 0. Replaces llama2c_sota_kernel, llama2c/llama2c_sota.cu:263-298
+ * (and the three-stream enqueue_iteration, llama2c_cuda_graph.cu:347-381). */
+int ce_llama2c_iteration(float *normalized_dev, float *softmax_dev, float *product_dev,
+                         const float *input_dev, const float *weight_dev,
+                         const float *probabilities_dev, const float *matrix_dev,
+                         int batch, int size, int rows, float eps, ce_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* Tensor-core GEMM (tcgen05 + TMEM, operands by TMA).                 */
+
+/* D[m][n] = sum_k A[m][k] * B[n][k] (both operands K-contiguous, D fp32
+ * row-major with leading dimension ldd). A and B are bf16 bit patterns
+ * (uint16). Requirements: lda, ldb multiples of 8 elements, 16-byte aligned
+ * base pointers; M, N, K >= 1. Ragged M, N, K are handled (zero fill).
+ * This is the engine behind the classifier GEMM of
+ * applications/loom_private/decoder/decoder_optimized.cu:343-439 and the
+ * BF16 CUTLASS GEMM of experiments/blackwell/lowprec/decoder_lowprec.cu:85-92. */
+int ce_gemm_bf16(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev, int M, int N,
+                 int K, int lda, int ldb, int ldd, ce_stream_t stream);
+
+/* ce_gemm_bf16 with a forced output-tile width (128, 160, 192, 224 or 256
+ * columns; 0 = automatic). Test hook in the spirit of the reference's forced
+ * tiles (decoder_optimized.cu:543-557, DECODER_OPT_TILE). */
+int ce_gemm_bf16_tile(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev, int M, int N,
+                      int K, int lda, int ldb, int ldd, int tile_n, ce_stream_t stream);
+
+/* Same contraction on fp32 operands with tcgen05 kind::tf32 (the tensor
+ * core reads the upper 19 bits of each fp32 value). lda, ldb multiples of 4
+ * elements, 16-byte aligned base pointers. */
+int ce_gemm_tf32(float *d_dev, const float *a_dev, const float *b_dev, int M, int N, int K,
+                 int lda, int ldb, int ldd, ce_stream_t stream);
+
+/* Same contraction on the SIMT cores with the reference's bitwise contract:
+ * each output accumulated from 0.0f in increasing k with separate multiply
+ * and add (applications/loom_private/decoder/decoder.cu:79-125). Any
+ * alignment; the control path of CE_PREC_FP32. */
+int ce_gemm_fp32(float *d_dev, const float *a_dev, const float *b_dev, int M, int N, int K,
+                 int lda, int ldb, int ldd, ce_stream_t stream);
+
+/* Round-to-nearest-even conversion fp32 -> bf16 of a [rows][cols] matrix
+ * into a [rows][ld_out] buffer; columns cols..ld_out-1 are written as 0.
+ * (experiments/blackwell/lowprec/decoder_lowprec.cu:222-238, to_bf16_kernel.) */
+int ce_convert_bf16(uint16_t *out_dev, const float *in_dev, int rows, int cols, int ld_out,
+                    ce_stream_t stream);
+
+/* RMSNorm that also writes the normalized rows as bf16 into a [rows][ld_bf16]
+ * buffer (padding columns 0), the fused producer of the GEMM A operand.
+ * out_dev may be NULL (bf16 only). */
+int ce_rmsnorm_bf16(float *out_dev, uint16_t *out_bf16_dev, int ld_bf16, const float *x_dev,
+                    const float *w_dev, int rows, int cols, float eps, ce_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* Op-trio plan: rmsnorm -> GEMM on the normalized batch, plus softmax. */
+
+/* A plan owns the prepared weights (converted once, like the reference's
+ * setup-time weight conversion, decoder_lowprec.cu:573-579) and the
+ * activation workspace for one shape and precision. Create and set_weights
+ * allocate and may synchronize; everything else is enqueue-only. */
+typedef struct ce_plan ce_plan;
+
+int ce_plan_create(ce_plan **plan, int batch, int size, int rows, int precision);
+int ce_plan_destroy(ce_plan *plan);
+
+/* Converts the fp32 weight matrix [rows][size] (device) into the plan's
+ * layout for its precision. Setup only (allocates on first call). */
+int ce_plan_set_weights(ce_plan *plan, const float *w_dev, ce_stream_t stream);
+
+/* out[b][r] = sum_k W[r][k] * xnorm[b][k], xnorm = rmsnorm(x, norm_w, eps).
+ * normalized_dev (fp32 [batch][size]) may be NULL. */
+int ce_plan_rmsnorm_gemm(ce_plan *plan, float *out_dev, float *normalized_dev,
+                         const float *x_dev, const float *norm_w_dev, float eps,
+                         ce_stream_t stream);
+
+/* The two halves of ce_plan_trio, for callers that time or overlap them:
+ * ce_plan_rows writes normalized (may be NULL), the plan's GEMM operand and,
+ * when logits != NULL, softmax, in one launch; ce_plan_gemm multiplies the
+ * plan's current operand by the prepared weights into out [batch][rows]. */
+int ce_plan_rows(ce_plan *plan, float *normalized_dev, float *softmax_dev, const float *x_dev,
+                 const float *norm_w_dev, const float *logits_dev, float eps,
+                 ce_stream_t stream);
+int ce_plan_gemm(ce_plan *plan, float *out_dev, ce_stream_t stream);
+
+/* One step of the BASELINE op trio: normalized = rmsnorm(x), softmax of an
+ * independent logits buffer, out = GEMM of the normalized batch. */
+int ce_plan_trio(ce_plan *plan, float *normalized_dev, float *softmax_dev, float *out_dev,
+                 const float *x_dev, const float *norm_w_dev, const float *logits_dev,
+                 float eps, ce_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CE_B200_H */

@@ -1,0 +1,75 @@
+"""The C ABI library loads, exports every symbol include/ce_b200.h declares,
+its host-side generators match the oracle bit for bit, and argument errors
+come back as CE_ERR_USAGE before any device work. No GPU needed."""
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    names = []
+    for fn in sorted(os.listdir(os.path.join(ROOT, "include"))):
+        if fn.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", fn)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names += re.findall(r"\b(ce_\w+)\s*\(", text)
+    return sorted(set(names))
+
+
+def test_library_exports_every_declared_symbol(ce):
+    L = ce.lib()
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(L, n)]
+    assert not missing, missing
+    assert ce.lib().ce_version().decode().startswith("ce_b200")
+
+
+@pytest.mark.parametrize("random,seed", [(0, 0), (1, 1), (1, 99)])
+def test_llama2c_generator_matches_oracle(ce, O, random, seed):
+    shape = (7, 130, 33)
+    got = ce.fill_llama2c_host(random, seed, *shape)
+    want = O.llama2c_inputs(random, seed, *shape)
+    for g, w in zip(got, want):
+        assert np.array_equal(g, w)
+
+
+def test_llama2c_generator_large_is_parallel_and_exact(ce, O):
+    # big enough to take the multithreaded path of the library
+    got = ce.fill_llama2c_host(1, 3, 64, 4096, 4)
+    want = O.llama2c_inputs(1, 3, 64, 4096, 4)
+    for g, w in zip(got, want):
+        assert np.array_equal(g, w)
+
+
+@pytest.mark.parametrize("first,count", [(0, 1), (0, 1001), (1, 1000), (12345, 70001)])
+def test_normal_and_uniform_generators_match_oracle(ce, O, first, count):
+    full = O.normals(5, 2, first + count, 0.125)
+    assert np.array_equal(ce.fill_normal_host(5, 2, count, 0.125, first=first), full[first:])
+    fu = O.uniforms(5, 4, first + count, 0.5, 1.5)
+    assert np.array_equal(ce.fill_uniform_host(5, 4, count, 0.5, 1.5, first=first), fu[first:])
+
+
+def test_trio_inputs_match_oracle(ce, O):
+    for a, b in zip(ce.trio_inputs_host(0, 8, 288, 768), O.trio_inputs(0, 8, 288, 768)):
+        assert np.array_equal(a, b)
+
+
+def test_usage_errors_before_device_work(ce):
+    L = ce.lib()
+    assert L.ce_rmsnorm(None, None, None, 0, 16, 1e-5, None) == ce.ERR_USAGE
+    code, msg = ce.last_error()
+    assert code == ce.ERR_USAGE and "rows" in msg
+    assert L.ce_softmax(None, None, 4, 0, None) == ce.ERR_USAGE
+    assert L.ce_gemv(None, None, None, -1, 4, None) == ce.ERR_USAGE
+    h = __import__("ctypes").c_void_p()
+    assert L.ce_plan_create(__import__("ctypes").byref(h), 8, 288, 768, 9) == ce.ERR_USAGE
+    assert L.ce_plan_create(__import__("ctypes").byref(h), 0, 288, 768, 2) == ce.ERR_USAGE
+    assert L.ce_fill_llama2c_host(1, 1, 0, 4, 4, None, None, None, None) == ce.ERR_USAGE
+    with pytest.raises(ce.CeError) as e:
+        ce.check(L.ce_rmsnorm(None, None, None, 1, 0, 1e-5, None))
+    assert e.value.status == ce.ERR_USAGE
