@@ -21,7 +21,6 @@ namespace {
 
 constexpr int kRowThreads = 512;      // register path: threads per row
 constexpr int kGenericThreads = 512;  // generic path
-constexpr int kGemvWarps = 16;        // GEMV rows per 512-thread block
 constexpr int kGemvUnroll = 8;        // float4 loads in flight per lane
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -427,9 +426,10 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
     w.softmax_rows = batch_softmax;
     w.gemv_rows = gemv_rows;
     w.eps = eps;
-    // The GEMV blocks use the same block size; at least 256 threads keeps
-    // enough warps per GEMV block.
-    if (gemv_rows > 0 && threads < 256) threads = 256;
+    // At least 256 threads per block whatever the launch contains, so the
+    // reduction order of a row (and so its bits) does not depend on whether
+    // GEMV blocks share the launch; the GEMV blocks use the same size.
+    if (threads < 256) threads = 256;
     int rc = launch_iteration(w, nv, threads, s);
     if (rc != CE_OK) return rc;
   } else {
