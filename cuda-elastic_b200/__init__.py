@@ -268,7 +268,7 @@ class Plan:
     one shape and precision. Weights are converted once by set_weights."""
 
     def __init__(self, batch, size, rows, precision=PREC_BF16):
-        self.batch, self.size, self.rows, self.precision = batch, size, rows, precision
+        self.batch, self.size, self.n_rows, self.precision = batch, size, rows, precision
         h = ctypes.c_void_p()
         check(lib().ce_plan_create(ctypes.byref(h), batch, size, rows, precision))
         self._h = h
