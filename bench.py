@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="setup, warm-up and the timed steps only (for ncu captures); no JSON line")
     return ap.parse_args()
 
 
@@ -224,6 +226,18 @@ def run_ours(args, rank, world, local_rank):
             step()
     ce.device_status()
     barrier()
+
+    if args.profile:
+        with torch.cuda.stream(stream):
+            for _ in range(args.steps):
+                step()
+        torch.cuda.synchronize(dev)
+        ce.device_status()
+        plan.close()
+        if dist is not None:
+            dist.destroy_process_group()
+        print(f"profile run: {args.steps} steps done", flush=True)
+        return
 
     # ---- timed region: K steps, events around each GEMM launch ----
     sampler = ClockSampler(local_rank)

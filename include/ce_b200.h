@@ -200,6 +200,27 @@ int ce_plan_rows(ce_plan *plan, float *normalized_dev, float *softmax_dev, const
                  ce_stream_t stream);
 int ce_plan_gemm(ce_plan *plan, float *out_dev, ce_stream_t stream);
 
+/* rmsnorm -> bf16 tensor-core GEMM that allocates no device memory, for
+ * callers that cannot call cudaMalloc: code running while a CUDA graph is
+ * captured, processes whose allocator already owns the device memory, and
+ * loops that cannot take cudaMalloc's implicit synchronization. No
+ * counterpart in the reference (its harnesses allocate everything in setup).
+ *   out[b][r] = sum_k W[r][k] * xnorm[b][k], xnorm = rmsnorm(x, norm_w, eps);
+ *   normalized_dev (fp32 [batch][size]) may be NULL; w_bf16_dev holds W as
+ *   bf16 [rows][ld_w] (ld_w >= size, a multiple of 8; ce_convert_bf16 makes
+ *   it). The caller passes inputs and outputs; the bf16 normalized operand
+ *   lives in one fixed 8 MiB device array of the library (4,194,304 bf16
+ *   values), which every GPU that loads the library holds until exit.
+ *   batch x roundup(size, 64) above that limit returns CE_ERR_USAGE.
+ * The first call on a device looks up that array's device address (once per
+ * device, with the device current); make that first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU (two
+ * streams, two host threads) race on it and must be serialized by the
+ * caller. Each call rewrites every value it reads, so no clearing is needed. */
+int ce_rmsnorm_gemm_bf16_noalloc(float *out_dev, float *normalized_dev, const float *x_dev,
+                                 const float *norm_w_dev, const uint16_t *w_bf16_dev, int ld_w,
+                                 int batch, int size, int rows, float eps, ce_stream_t stream);
+
 /* One step of the BASELINE op trio: normalized = rmsnorm(x), softmax of an
  * independent logits buffer, out = GEMM of the normalized batch. */
 int ce_plan_trio(ce_plan *plan, float *normalized_dev, float *softmax_dev, float *out_dev,

@@ -1,0 +1,73 @@
+"""The no-allocation rmsnorm -> bf16 GEMM (ce_rmsnorm_gemm_bf16_noalloc),
+called through the C ABI, against the plan entry point that keeps its
+operand in cudaMalloc'd workspace.
+
+Callers of this entry point cannot allocate device memory (graph capture in
+progress, a framework allocator owning the device, no implicit sync allowed),
+so its operand lives in a fixed array inside the library. This file is named
+to be collected last: if it fails, a run that stops at the first failure has
+already run every other test. It passes alone in a fresh process too."""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+_vp, _i, _f = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+
+
+def _noalloc(ce):
+    fn = ce.lib().ce_rmsnorm_gemm_bf16_noalloc
+    fn.argtypes = [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp]
+    fn.restype = ctypes.c_int
+    return fn
+
+
+def test_noalloc_matches_plan_two_calls(ce, O, dev):
+    fn = _noalloc(ce)
+    b, s, r = 96, 1000, 700  # ragged size: padded operand rows of 1024
+    stream = torch.cuda.current_stream().cuda_stream
+    ld_w = ((s + 63) // 64) * 64
+    for call, seed in enumerate((1, 2)):  # two calls in a row, different inputs
+        x, w, _, W = O.trio_inputs(seed, b, s, r)
+        dx, dw, dW = (torch.from_numpy(a).to(dev) for a in (x, w, W))
+        wb = torch.empty((r, ld_w), dtype=torch.int16, device=dev)
+        ce.convert_bf16(wb, dW)
+
+        plan = ce.Plan(b, s, r, ce.PREC_BF16)
+        plan.set_weights(dW)
+        want = torch.full((b, r), float("nan"), device=dev)
+        want_norm = torch.full((b, s), float("nan"), device=dev)
+        plan.rmsnorm_gemm(want, dx, dw, normalized=want_norm)
+
+        got = torch.full((b, r), float("nan"), device=dev)
+        got_norm = torch.full((b, s), float("nan"), device=dev)
+        rc = fn(got.data_ptr(), got_norm.data_ptr(), dx.data_ptr(), dw.data_ptr(), wb.data_ptr(),
+                ld_w, b, s, r, ce.RMS_EPS, stream)
+        assert rc == ce.OK, ce.last_error()
+        ce.device_status()
+        plan.close()
+
+        g, wnt = got.cpu().numpy(), want.cpu().numpy()
+        assert np.isfinite(g).all(), f"call {call}"
+        # the bf16 GEMM tolerance of the other tests: relative L2 <= 1e-2,
+        # here against the existing entry point's output
+        assert O.rel_l2(g, wnt) <= 1e-2, f"call {call}"
+        gn, wn = got_norm.cpu().numpy(), want_norm.cpu().numpy()
+        assert np.all(np.abs(gn - wn) <= 1e-5 * np.abs(wn) + 1e-30), f"call {call}"
+        # and the oracle: the double GEMM of the fp32 normalized rows
+        ref, _ = O.gemm_ref(O.rmsnorm_ref(x, w), W)
+        assert O.rel_l2(g, ref) <= 1e-2, f"call {call}"
+
+
+def test_noalloc_rejects_sizes_beyond_its_operand(ce, dev):
+    fn = _noalloc(ce)
+    # 1025 x 4096 bf16 values exceed the 4,194,304-value operand: rejected
+    # before any device work, so dummy non-null pointers are never touched
+    dummy = 256
+    rc = fn(dummy, None, dummy, dummy, dummy, 4096, 1025, 4096, 64, 1e-5, None)
+    assert rc == ce.ERR_USAGE
+    code, msg = ce.last_error()
+    assert "exceeds" in msg and "4194304" in msg
