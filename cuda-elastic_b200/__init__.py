@@ -76,6 +76,8 @@ _SIGNATURES = {
     "ce_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_bf16_tile": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_tf32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "ce_gemm_tuning": [_i],
+    "ce_gemm_config": [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_fp32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_convert_bf16": [_vp, _vp, _i, _i, _i, _vp],
     "ce_rmsnorm_bf16": [_vp, _vp, _i, _vp, _vp, _i, _i, _f, _vp],
@@ -236,6 +238,16 @@ def gemm_bf16(d, a, b, k=None, tile_n=0, stream=None):
     K = lda if k is None else k
     check(lib().ce_gemm_bf16_tile(_ptr(d), _ptr(a), _ptr(b), M, N, K, lda, ldb, d.shape[1], tile_n,
                                   _stream(stream)))
+    return d
+
+
+def gemm_config(precision, d, a, b, k=None, cta_group=0, tile_n=0, stream=None):
+    """Tensor-core GEMM with a forced kernel (cta_group 1 or 2) and tile width."""
+    M, lda = a.shape
+    N, ldb = b.shape
+    K = lda if k is None else k
+    check(lib().ce_gemm_config(precision, _ptr(d), _ptr(a), _ptr(b), M, N, K, lda, ldb, d.shape[1],
+                               cta_group, tile_n, _stream(stream)))
     return d
 
 

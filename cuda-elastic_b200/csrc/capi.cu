@@ -24,13 +24,14 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
 int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
-              cudaStream_t s);
+              cudaStream_t s, int force_group = 0);
 int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,
               int ldd, const float *row_scale, const float *col_scale, int force_bn,
-              cudaStream_t s);
+              cudaStream_t s, int force_group = 0);
 int gemm_simt_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda,
                    int ldb, int ldd, cudaStream_t s);
 int gemm_status();
+int gemm_set_prefetch(int kblocks);
 
 // ---------------------------------------------------------------------------
 // Status
@@ -271,12 +272,23 @@ int ce_gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, i
   return gemm_bf16(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, (cudaStream_t)stream);
 }
 
-// Same as ce_gemm_bf16 with a forced tile width (test hook: 128, 160, 192,
-// 224 or 256 output columns per tile; 0 = automatic).
 int ce_gemm_bf16_tile(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
                       int ldb, int ldd, int tile_n, ce_stream_t stream) {
   return gemm_bf16(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, tile_n,
-                   (cudaStream_t)stream);
+                   (cudaStream_t)stream, 1);
+}
+
+int ce_gemm_tuning(int l2_prefetch_kblocks) { return gemm_set_prefetch(l2_prefetch_kblocks); }
+
+int ce_gemm_config(int precision, float *d, const void *a, const void *b, int M, int N, int K,
+                   int lda, int ldb, int ldd, int cta_group, int tile_n, ce_stream_t stream) {
+  if (precision == CE_PREC_BF16)
+    return gemm_bf16(d, static_cast<const uint16_t *>(a), static_cast<const uint16_t *>(b), M, N,
+                     K, lda, ldb, ldd, nullptr, nullptr, tile_n, (cudaStream_t)stream, cta_group);
+  if (precision == CE_PREC_TF32)
+    return gemm_tf32(d, static_cast<const float *>(a), static_cast<const float *>(b), M, N, K, lda,
+                     ldb, ldd, nullptr, nullptr, tile_n, (cudaStream_t)stream, cta_group);
+  return set_error(CE_ERR_USAGE, format("ce_gemm_config: precision %d has no tensor-core kernel", precision));
 }
 
 int ce_gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,

@@ -131,6 +131,65 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, Device
   return __all_sync(0xffffffffu, r) != 0;
 }
 
+// --- clusters (CTA pairs of the 2-SM tensor-core path) ---------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+// Arrive on an mbarrier of any CTA of the cluster (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];"
+               ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx_cluster(uint32_t cluster_addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;"
+               ::"r"(cluster_addr), "r"(bytes) : "memory");
+}
+// try_wait with cluster-scope acquire, for barriers that other CTAs of the
+// cluster arrive on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, DeviceStatus *st,
+                                                  unsigned where) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long start = globaltimer();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((spin & 255u) == 0u) {
+      if (globaltimer() - start > kWaitLimitNs) {
+        report_timeout(st, where);
+        return false;
+      }
+      if (st != nullptr && *(volatile unsigned *)&st->code != 0u) return false;
+    }
+  }
+}
+__device__ __forceinline__ bool warp_wait_cluster(uint64_t *bar, uint32_t parity, DeviceStatus *st,
+                                                  unsigned where) {
+  const bool r = mbar_wait_cluster(bar, parity, st, where);
+  return __all_sync(0xffffffffu, r) != 0;
+}
+
 // --- TMA -------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const void *desc) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(desc) : "memory");
@@ -144,6 +203,24 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const void *desc, ui
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];"
       ::"r"(smem_u32(smem_dst)), "l"(desc), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Prefetch of a 2-D tile into L2 (no shared memory written, no barrier).
+__device__ __forceinline__ void tma_prefetch_2d(const void *desc, int x, int y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+               ::"l"(desc), "r"(x), "r"(y) : "memory");
+}
+
+// 2-D tiled load of the CTA-pair form: data lands in this CTA's shared
+// memory, completion is signalled on an mbarrier that may belong to the peer
+// CTA of the pair (shared::cluster address). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const void *desc,
+                                                 uint32_t bar_cluster_addr, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(smem_u32(smem_dst)), "l"(desc), "r"(bar_cluster_addr), "r"(x), "r"(y)
       : "memory");
 }
 
@@ -170,6 +247,47 @@ __device__ __forceinline__ void tc_fence_after() {
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                ::"r"(smem_u32(bar)) : "memory");
+}
+
+// CTA-pair (cta_group::2) forms: allocation and release are issued by the
+// same warp in both CTAs of the pair; the MMA and its commits by one thread
+// of the even CTA.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
+               ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;"
+               ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Arrives on the mbarrier at a shared::cluster address (either CTA of the
+// pair) when all prior tcgen05 operations of this thread have completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(bar_cluster_addr) : "memory");
+}
+template <int kKind>  // 0: kind::f16, 1: kind::tf32, 2: kind::f8f6f4
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  if constexpr (kKind == 0) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else if constexpr (kKind == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  }
 }
 
 // D(tmem) (+)= A(smem desc) x B(smem desc)^T, one instruction.

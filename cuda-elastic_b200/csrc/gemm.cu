@@ -32,7 +32,6 @@ static __device__ DeviceStatus g_gemm_status;
 namespace {
 
 constexpr int BM = 128;
-constexpr int kStages = 4;
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 512;
 constexpr int kRowBytes = 128;  // K bytes per stage (one swizzle row)
@@ -62,7 +61,9 @@ struct Smem {
   static constexpr int a_bytes = BM * kRowBytes;
   static constexpr int b_bytes = BN * kRowBytes;
   static constexpr int stage_bytes = a_bytes + b_bytes;
-  static constexpr int bar_offset = kStages * stage_bytes;
+  static constexpr int max_stages = (232448 - 2048) / stage_bytes;
+  static constexpr int stages = max_stages > 8 ? 8 : max_stages;
+  static constexpr int bar_offset = stages * stage_bytes;
   // full[kStages], empty[kStages], tmem_full[2], tmem_empty[2], drain, tmem holder
   static constexpr int total = bar_offset + 256 + 1024;  // + alignment slack
 };
@@ -82,6 +83,7 @@ struct GemmArgs {
   const float *col_scale;  // optional per-n scale (nullptr = 1)
   int M, N, K, ldd;
   int tiles_m, tiles_n, k_blocks;
+  int prefetch;  // L2 prefetch distance in k-blocks (0 = none)
 };
 
 template <int kKind, int BN>
@@ -99,8 +101,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_offset);
-  uint64_t *empty = full + kStages;
-  uint64_t *tmem_full = empty + kStages;
+  uint64_t *empty = full + S::stages;
+  uint64_t *tmem_full = empty + S::stages;
   uint64_t *tmem_empty = tmem_full + 2;
   uint64_t *drain = tmem_empty + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
@@ -110,7 +112,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   const int num_tiles = args.tiles_m * args.tiles_n;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S::stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -149,6 +151,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (lane == 0) {
           uint8_t *a_dst = smem + stage * S::stage_bytes;
           uint8_t *b_dst = a_dst + S::a_bytes;
+          if (args.prefetch > 0 && kb + args.prefetch < args.k_blocks) {
+            tma_prefetch_2d(&tmA, (kb + args.prefetch) * kElemsPerRow, m0);
+            tma_prefetch_2d(&tmB, (kb + args.prefetch) * kElemsPerRow, n0);
+          }
           mbar_arrive_expect_tx(&full[stage], S::stage_bytes);
           tma_load_2d(a_dst, &tmA, &full[stage], kb * kElemsPerRow, m0);
           tma_load_2d(b_dst, &tmB, &full[stage], kb * kElemsPerRow, n0);
@@ -156,14 +162,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         __syncwarp();
         issued_mask |= 1u << stage;
         issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == kStages) {
+        if (++stage == S::stages) {
           stage = 0;
           phase ^= 1u;
         }
       }
     }
     // Every copy this warp issued must land before the CTA can exit.
-    for (int s = 0; s < kStages; ++s)
+    for (int s = 0; s < S::stages; ++s)
       if (issued_mask & (1u << s)) warp_wait(&full[s], (issued_parity >> s) & 1u, st, 2);
   } else if (warp == 1) {
     // ---------------- MMA issuer (lane 0 issues)
@@ -195,7 +201,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           tc_commit(&empty[stage]);
         }
         __syncwarp();
-        if (++stage == kStages) {
+        if (++stage == S::stages) {
           stage = 0;
           phase ^= 1u;
         }
@@ -263,6 +269,230 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair kernel (tcgen05 cta_group::2): a cluster of 2 CTAs on 2 SMs owns a
+// 256 x BN output tile. Each CTA stages its own 128 rows of A and its own
+// BN/2 rows of B (plain TMA loads into its own shared memory, completion
+// signalled on the even CTA's barrier); one thread of the even CTA issues
+// M=256 MMAs that read both CTAs' shared memory and write both CTAs' TMEM
+// (each holds its 128 rows x BN fp32 accumulator). Per SM this halves the B
+// bytes staged per multiply-add compared with the 1-CTA kernel.
+
+template <int BN>
+struct SmemPair {
+  static constexpr int a_bytes = BM * kRowBytes;
+  static constexpr int b_bytes = (BN / 2) * kRowBytes;
+  static constexpr int stage_bytes = a_bytes + b_bytes;
+  static constexpr int max_stages = (232448 - 2048) / stage_bytes;
+  static constexpr int stages = max_stages > 8 ? 8 : max_stages;
+  static constexpr int bar_offset = stages * stage_bytes;
+  static constexpr int total = bar_offset + 256 + 1024;
+};
+
+template <int kKind, int BN>
+__host__ __device__ constexpr uint32_t instr_desc_pair() {
+  return (1u << 4) | (Kind<kKind>::fmt << 7) | (Kind<kKind>::fmt << 10) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+template <int kKind, int BN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 GemmArgs args) {
+  using S = SmemPair<BN>;
+  constexpr int kSt = S::stages;
+  constexpr int kElemsPerRow = kRowBytes / Kind<kKind>::elem;
+  constexpr int kUmmaK = 32 / Kind<kKind>::elem;
+  constexpr int kMmasPerStage = kElemsPerRow / kUmmaK;
+  constexpr uint32_t kIdesc = instr_desc_pair<kKind, BN>();
+  constexpr uint32_t kAccStride = 256;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_offset);
+  uint64_t *empty = full + kSt;
+  uint64_t *tmem_full = empty + kSt;
+  uint64_t *tmem_empty = tmem_full + 2;
+  uint64_t *drain = tmem_empty + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+
+  DeviceStatus *st = &g_gemm_status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 issues the MMAs
+  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kSt; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 8);  // one arrival per epilogue warp of both CTAs
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_holder, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs are initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  const uint32_t full0_leader = cluster_map(smem_u32(&full[0]), 0);
+  const uint32_t tmem_empty0_leader = cluster_map(smem_u32(&tmem_empty[0]), 0);
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs)
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool okay = true;
+    for (int t = pair; t < num_tiles && okay; t += npairs) {
+      const int m0 = (t % args.tiles_m) * (2 * BM) + (int)rank * BM;
+      const int n0 = (t / args.tiles_m) * BN + (int)rank * (BN / 2);
+      for (int kb = 0; kb < args.k_blocks; ++kb) {
+        if (!warp_wait_cluster(&empty[stage], phase ^ 1u, st, 11)) {
+          okay = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t *a_dst = smem + stage * S::stage_bytes;
+          uint8_t *b_dst = a_dst + S::a_bytes;
+          if (args.prefetch > 0 && kb + args.prefetch < args.k_blocks) {
+            tma_prefetch_2d(&tmA, (kb + args.prefetch) * kElemsPerRow, m0);
+            tma_prefetch_2d(&tmB, (kb + args.prefetch) * kElemsPerRow, n0);
+          }
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * S::stage_bytes);
+          const uint32_t bar = full0_leader + 8u * (uint32_t)stage;
+          tma_load_2d_pair(a_dst, &tmA, bar, kb * kElemsPerRow, m0);
+          tma_load_2d_pair(b_dst, &tmB, bar, kb * kElemsPerRow, n0);
+        }
+        __syncwarp();
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == kSt) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    // The even CTA's MMAs consume every stage either CTA issued and then
+    // arrive on both CTAs' empty barriers: waiting for that consumption of
+    // each stage's last issue also waits for its copies to land.
+    for (int s = 0; s < kSt; ++s)
+      if (issued_mask & (1u << s)) warp_wait_cluster(&empty[s], (issued_parity >> s) & 1u, st, 12);
+  } else if (warp == 1) {
+    if (rank == 0) {
+      // ---------------- MMA issuer (even CTA only)
+      int stage = 0;
+      uint32_t phase = 0;
+      bool okay = true;
+      int local = 0;
+      for (int t = pair; t < num_tiles && okay; t += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!warp_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, st, 13)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)acc * kAccStride;
+        for (int kb = 0; kb < args.k_blocks; ++kb) {
+          if (!warp_wait_cluster(&full[stage], phase, st, 14)) {
+            okay = false;
+            break;
+          }
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a_addr = smem_u32(smem + stage * S::stage_bytes);
+            const uint32_t b_addr = a_addr + S::a_bytes;
+#pragma unroll
+            for (int k = 0; k < kMmasPerStage; ++k) {
+              const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32);
+              const uint64_t b_desc = smem_desc_sw128(b_addr + k * 32);
+              tc_mma_pair<kKind>(d_tmem, a_desc, b_desc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+            }
+            const uint32_t e = smem_u32(&empty[stage]);
+            tc_commit_pair(cluster_map(e, 0));
+            tc_commit_pair(cluster_map(e, 1));
+          }
+          __syncwarp();
+          if (++stage == kSt) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (okay && lane == 0) {
+          const uint32_t f = smem_u32(&tmem_full[acc]);
+          tc_commit_pair(cluster_map(f, 0));
+          tc_commit_pair(cluster_map(f, 1));
+        }
+        __syncwarp();
+      }
+      if (lane == 0) tc_commit_pair(cluster_map(smem_u32(drain), 0));
+      __syncwarp();
+      warp_wait_cluster(drain, 0, st, 15);
+    }
+  } else {
+    // ---------------- Epilogue (warps 2-5 of both CTAs)
+    const int quarter = warp & 3;
+    int local = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!warp_wait_cluster(&tmem_full[acc], acc_phase, st, 16)) break;
+      tc_fence_after();
+      const int m0 = (t % args.tiles_m) * (2 * BM) + (int)rank * BM;
+      const int n0 = (t / args.tiles_m) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const float rs = (args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f;
+      float *drow = args.d + (size_t)row * args.ldd;
+      const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.d) & 15u) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kAccStride + c, r);
+        tmem_ld_wait();
+        if (row < args.M) {
+          const int col0 = n0 + c;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(r[j]) * rs;
+            if (args.col_scale != nullptr && col0 + j < args.N) x *= args.col_scale[col0 + j];
+            v[j] = x;
+          }
+          if (vec_ok && col0 + 32 <= args.N) {
+            float4 *dst = reinterpret_cast<float4 *>(drow + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.N) drow[col0 + j] = v[j];
+          }
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      if (lane == 0) mbar_arrive_cluster(tmem_empty0_leader + 8u * (uint32_t)acc);
+      __syncwarp();
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -296,37 +526,72 @@ int make_operand_map(CUtensorMap *map, const void *base, CUtensorMapDataType dty
   return CE_OK;
 }
 
+// Opts a kernel into its dynamic shared memory size. The attribute is per
+// kernel and device, so the flag is per instantiation (template on the
+// kernel itself) and per device.
+template <auto kernel>
+int configure_smem(int bytes) {
+  static bool configured[64] = {};
+  int dev = 0;
+  CE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    CE_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  return CE_OK;
+}
+
 template <int kKind, int BN>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int grid,
                 cudaStream_t s) {
   using S = Smem<BN>;
-  static bool configured[64] = {};  // the attribute is per function and device
-  int dev = 0;
-  CE_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    CE_CUDA_TRY(cudaFuncSetAttribute(gemm_kernel<kKind, BN>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, S::total));
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
+  int rc = configure_smem<gemm_kernel<kKind, BN>>(S::total);
+  if (rc) return rc;
   gemm_kernel<kKind, BN><<<grid, kThreads, S::total, s>>>(ta, tb, args);
   CE_LAUNCH_CHECK("gemm_kernel");
   return CE_OK;
 }
 
-// Tile width choice: the candidate that minimises (waves x BN), i.e. the
-// busiest SM's column count; ties go to the wider tile.
-int choose_bn(int M, int N, int sms) {
+template <int kKind, int BN>
+int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
+                     int grid, cudaStream_t s) {
+  using S = SmemPair<BN>;
+  int rc = configure_smem<gemm_pair_kernel<kKind, BN>>(S::total);
+  if (rc) return rc;
+  gemm_pair_kernel<kKind, BN><<<grid, kThreads, S::total, s>>>(ta, tb, args);
+  CE_LAUNCH_CHECK("gemm_pair_kernel");
+  return CE_OK;
+}
+
+struct GemmChoice {
+  int pair;  // 1: CTA-pair kernel (256-row tiles), 0: single-CTA kernel (128-row tiles)
+  int bn;
+};
+
+// Kernel and tile width: minimise (waves x BN) / efficiency, where a wave is
+// one tile per SM (single-CTA) or per SM pair, and the CTA-pair kernel is
+// credited with its lower staging cost per multiply-add (measured: about
+// 0.67 of peak tensor throughput for the single-CTA kernel).
+int g_prefetch_kblocks = 0;  // set by ce_gemm_tuning (setup time)
+
+GemmChoice choose_tiles(int M, int N, int sms) {
   static const int kCandidates[] = {256, 224, 192, 160, 128};
-  int best = 256;
-  long long best_cost = -1;
-  const int tiles_m = (M + BM - 1) / BM;
-  for (int bn : kCandidates) {
-    const long long tiles = (long long)tiles_m * ((N + bn - 1) / bn);
-    const long long waves = (tiles + sms - 1) / sms;
-    const long long cost = waves * bn;
-    if (best_cost < 0 || cost < best_cost) {
-      best_cost = cost;
-      best = bn;
+  GemmChoice best{0, 256};
+  double best_cost = -1;
+  for (int pair = 0; pair < 2; ++pair) {
+    const int rows = pair ? 2 * BM : BM;
+    const int units = pair ? sms / 2 : sms;
+    const double eff = pair ? 0.85 : 0.67;
+    if (pair && M <= BM) continue;
+    const long long tiles_m = (M + rows - 1) / rows;
+    for (int bn : kCandidates) {
+      const long long tiles = tiles_m * ((N + bn - 1) / bn);
+      const long long waves = (tiles + units - 1) / units;
+      const double cost = (double)(waves * bn) / eff;
+      if (best_cost < 0 || cost < best_cost - 1e-9) {
+        best_cost = cost;
+        best = GemmChoice{pair, bn};
+      }
     }
   }
   return best;
@@ -335,7 +600,7 @@ int choose_bn(int M, int N, int sms) {
 template <int kKind>
 int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
                   int ldd, const float *row_scale, const float *col_scale, int force_bn,
-                  cudaStream_t s) {
+                  int force_group, cudaStream_t s) {
   constexpr int elem = Kind<kKind>::elem;
   const CUtensorMapDataType dt = kKind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : kKind == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -347,13 +612,21 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   CE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0,
              "operand base pointers must be 16-byte aligned");
   CE_REQUIRE(d != nullptr, "null output");
+  CE_REQUIRE(force_group == 0 || force_group == 1 || force_group == 2,
+             "cta group must be 0 (automatic), 1 or 2 (got %d)", force_group);
+  CE_REQUIRE(force_bn == 0 || force_bn == 128 || force_bn == 160 || force_bn == 192 ||
+                 force_bn == 224 || force_bn == 256,
+             "tile width must be 0, 128, 160, 192, 224 or 256 (got %d)", force_bn);
   if (!is_sm100()) return set_error(CE_ERR_USAGE, "tcgen05 GEMM needs an sm_100 device");
   const int sms = sm_count();
-  const int bn = force_bn > 0 ? force_bn : choose_bn(M, N, sms);
+  GemmChoice c = choose_tiles(M, N, sms);
+  if (force_group != 0) c.pair = force_group == 2;
+  if (force_bn != 0) c.bn = force_bn;
+  const int rows_per_tile = c.pair ? 2 * BM : BM;
   CUtensorMap ta, tb;
   int rc = make_operand_map(&ta, a, dt, elem, K, M, lda, BM);
   if (rc) return rc;
-  rc = make_operand_map(&tb, b, dt, elem, K, N, ldb, bn);
+  rc = make_operand_map(&tb, b, dt, elem, K, N, ldb, c.pair ? c.bn / 2 : c.bn);
   if (rc) return rc;
   GemmArgs args;
   args.d = d;
@@ -363,39 +636,61 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.N = N;
   args.K = K;
   args.ldd = ldd;
-  args.tiles_m = (M + BM - 1) / BM;
-  args.tiles_n = (N + bn - 1) / bn;
+  args.tiles_m = (M + rows_per_tile - 1) / rows_per_tile;
+  args.tiles_n = (N + c.bn - 1) / c.bn;
   args.k_blocks = (K + (kRowBytes / elem) - 1) / (kRowBytes / elem);
+  args.prefetch = g_prefetch_kblocks;
   const int tiles = args.tiles_m * args.tiles_n;
-  const int grid = tiles < sms ? tiles : sms;
-  switch (bn) {
-    case 256: return launch_gemm<kKind, 256>(ta, tb, args, grid, s);
-    case 224: return launch_gemm<kKind, 224>(ta, tb, args, grid, s);
-    case 192: return launch_gemm<kKind, 192>(ta, tb, args, grid, s);
-    case 160: return launch_gemm<kKind, 160>(ta, tb, args, grid, s);
-    case 128: return launch_gemm<kKind, 128>(ta, tb, args, grid, s);
-    default: return set_error(CE_ERR_USAGE, format("unsupported tile width %d", bn));
+  if (c.pair) {
+    const int pairs = tiles < sms / 2 ? tiles : sms / 2;
+    const int grid = 2 * pairs;
+    switch (c.bn) {
+      case 256: return launch_gemm_pair<kKind, 256>(ta, tb, args, grid, s);
+      case 224: return launch_gemm_pair<kKind, 224>(ta, tb, args, grid, s);
+      case 192: return launch_gemm_pair<kKind, 192>(ta, tb, args, grid, s);
+      case 160: return launch_gemm_pair<kKind, 160>(ta, tb, args, grid, s);
+      case 128: return launch_gemm_pair<kKind, 128>(ta, tb, args, grid, s);
+    }
+  } else {
+    const int grid = tiles < sms ? tiles : sms;
+    switch (c.bn) {
+      case 256: return launch_gemm<kKind, 256>(ta, tb, args, grid, s);
+      case 224: return launch_gemm<kKind, 224>(ta, tb, args, grid, s);
+      case 192: return launch_gemm<kKind, 192>(ta, tb, args, grid, s);
+      case 160: return launch_gemm<kKind, 160>(ta, tb, args, grid, s);
+      case 128: return launch_gemm<kKind, 128>(ta, tb, args, grid, s);
+    }
   }
+  return set_error(CE_ERR_USAGE, format("unsupported tile width %d", c.bn));
 }
 
 }  // namespace
 
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
-              cudaStream_t s) {
-  return gemm_dispatch<0>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn, s);
+              cudaStream_t s, int force_group) {
+  return gemm_dispatch<0>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn,
+                          force_group, s);
 }
 
 int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,
               int ldd, const float *row_scale, const float *col_scale, int force_bn,
-              cudaStream_t s) {
-  return gemm_dispatch<1>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn, s);
+              cudaStream_t s, int force_group) {
+  return gemm_dispatch<1>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn,
+                          force_group, s);
 }
 
 int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
-              cudaStream_t s) {
-  return gemm_dispatch<2>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn, s);
+              cudaStream_t s, int force_group) {
+  return gemm_dispatch<2>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn,
+                          force_group, s);
+}
+
+int gemm_set_prefetch(int kblocks) {
+  CE_REQUIRE(kblocks >= 0 && kblocks <= 64, "prefetch distance must be in [0, 64] (got %d)", kblocks);
+  g_prefetch_kblocks = kblocks;
+  return CE_OK;
 }
 
 // Synchronizes the device, reads and clears the GEMM status word.

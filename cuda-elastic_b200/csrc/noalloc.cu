@@ -21,7 +21,7 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    int cols, int gemv_rows, float eps, cudaStream_t s);
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
-              cudaStream_t s);
+              cudaStream_t s, int force_group = 0);
 
 // 4,194,304 bf16 values (8 MiB): batch x roundup(size, 64) must fit, e.g.
 // 256 x 16384 or 1024 x 4096.

@@ -138,11 +138,25 @@ int ce_llama2c_iteration(float *normalized_dev, float *softmax_dev, float *produ
 int ce_gemm_bf16(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev, int M, int N,
                  int K, int lda, int ldb, int ldd, ce_stream_t stream);
 
-/* ce_gemm_bf16 with a forced output-tile width (128, 160, 192, 224 or 256
- * columns; 0 = automatic). Test hook in the spirit of the reference's forced
- * tiles (decoder_optimized.cu:543-557, DECODER_OPT_TILE). */
+/* ce_gemm_bf16 on the single-CTA kernel (128-row tiles) with a forced
+ * output-tile width (128, 160, 192, 224 or 256 columns; 0 = automatic). */
 int ce_gemm_bf16_tile(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev, int M, int N,
                       int K, int lda, int ldb, int ldd, int tile_n, ce_stream_t stream);
+
+/* Tensor-core GEMM with a forced kernel: precision CE_PREC_BF16 (a, b bf16
+ * bits) or CE_PREC_TF32 (a, b fp32); cta_group 1 = single-CTA kernel
+ * (128 x tile_n tiles), 2 = CTA-pair kernel (256 x tile_n tiles on two SMs,
+ * tcgen05 cta_group::2), 0 = automatic; tile_n 128/160/192/224/256 or 0.
+ * Test hook in the spirit of the reference's forced tiles and schedules
+ * (decoder_optimized.cu:543-557, DECODER_OPT_TILE / _SCHEDULE). */
+int ce_gemm_config(int precision, float *d_dev, const void *a_dev, const void *b_dev, int M, int N,
+                   int K, int lda, int ldb, int ldd, int cta_group, int tile_n,
+                   ce_stream_t stream);
+
+/* Library-wide GEMM tuning, set at setup time (not during a capture): the
+ * TMA producer prefetches operand tiles this many k-blocks ahead into L2
+ * (0 = off, at most 64). */
+int ce_gemm_tuning(int l2_prefetch_kblocks);
 
 /* Same contraction on fp32 operands with tcgen05 kind::tf32 (the tensor
  * core reads the upper 19 bits of each fp32 value). lda, ldb multiples of 4

@@ -130,3 +130,55 @@ def test_bf16_gemm_sheet_shape(ce, O, dev):
     assert np.isfinite(hd).all()
     rows = np.random.default_rng(0).choice(M, 48, replace=False)
     _check_bf16(O, hd[rows], x[rows], W)
+
+
+@pytest.mark.parametrize("cta_group", [1, 2])
+@pytest.mark.parametrize("tile_n", [128, 160, 192, 224, 256])
+def test_forced_kernel_and_tile_bf16(ce, O, dev, cta_group, tile_n):
+    """Both kernels (single CTA, CTA pair) at every tile width, on a shape
+    that is ragged in M, N and K."""
+    M, N, K = 300, 1000, 520
+    rng = np.random.default_rng(tile_n + 7 * cta_group)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K)).astype(np.float32)
+    da, db = _bf16_dev(O.bf16_bits(A), dev), _bf16_dev(O.bf16_bits(B), dev)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_config(ce.PREC_BF16, d, da, db, cta_group=cta_group, tile_n=tile_n)
+    ce.device_status()
+    _check_bf16(O, d.cpu().numpy(), A, B)
+
+
+@pytest.mark.parametrize("cta_group", [1, 2])
+@pytest.mark.parametrize("shape", [(520, 300, 100), (256, 224, 32), (1100, 700, 1028)])
+def test_forced_kernel_tf32(ce, O, dev, cta_group, shape):
+    M, N, K = shape
+    rng = np.random.default_rng(M + cta_group)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K)).astype(np.float32)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_config(ce.PREC_TF32, d, torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev),
+                   cta_group=cta_group)
+    ce.device_status()
+    ref, mag = O.gemm_ref(A, B)
+    dd = d.cpu().numpy().astype(np.float64)
+    bound = (2.0 * 2.0 ** -10 + O.gamma_worst(K)) * mag + 1e-30
+    assert np.all(np.abs(dd - ref) <= bound)
+
+
+@pytest.mark.parametrize("cta_group", [1, 2])
+def test_kernels_agree_on_sheet_shape(ce, O, dev, cta_group):
+    """Single-CTA and CTA-pair kernels on the BASELINE GEMM shape: the output
+    within the bf16 bound on sampled rows."""
+    M, N, K = 1024, 8192, 16384
+    rng = np.random.default_rng(cta_group)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = (rng.standard_normal((N, K)) / 128.0).astype(np.float32)
+    da = torch.from_numpy(O.bf16_bits(A).view(np.int16)).to(dev)
+    db = torch.from_numpy(O.bf16_bits(B).view(np.int16)).to(dev)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_config(ce.PREC_BF16, d, da, db, cta_group=cta_group)
+    ce.device_status()
+    hd = d.cpu().numpy()
+    assert np.isfinite(hd).all()
+    rows = np.random.default_rng(2).choice(M, 24, replace=False)
+    _check_bf16(O, hd[rows], A[rows], B)
