@@ -88,6 +88,14 @@ _SIGNATURES = {
     "ce_plan_trio": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
     "ce_plan_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
     "ce_plan_gemm": [_vp, _vp, _vp],
+    "ce_decoder_create": [ctypes.POINTER(_vp), _i64, _i64, _i64, _i64, _i, _vp],
+    "ce_decoder_destroy": [_vp],
+    "ce_decoder_set_model": [_vp, _vp, _vp, _vp, _vp],
+    "ce_decoder_enqueue_compute": [_vp, _vp],
+    "ce_decoder_enqueue_application": [_vp, _vp],
+    "ce_decoder_poison": [_vp, _vp],
+    "ce_decoder_copy_outputs": [_vp, _i, _vp, _vp, _vp, _vp],
+    "ce_decoder_inject_fault": [_vp, _i],
 }
 _RESTYPES = {"ce_version": ctypes.c_char_p}
 
@@ -316,3 +324,58 @@ class Plan:
         check(lib().ce_plan_trio(self._h, _ptr(normalized), _ptr(softmax_out), _ptr(out), _ptr(x),
                                  _ptr(norm_w), _ptr(logits), eps, _stream(stream)))
         return out
+
+
+class Decoder:
+    """The loom_private llama2c decoder workload (B sequences x S greedy steps
+    on the synthetic model, or on caller weights). Mirrors lp::Workload:
+    setup at construction, enqueue_compute / enqueue_application (both
+    capturable), poison_outputs, and outputs() as the check's diagnostics
+    copy."""
+
+    def __init__(self, batch, width, vocab, steps, precision=PREC_FP32, stream=None):
+        self.batch, self.width, self.vocab, self.steps = batch, width, vocab, steps
+        self.precision = precision
+        h = ctypes.c_void_p()
+        check(lib().ce_decoder_create(ctypes.byref(h), batch, width, vocab, steps, precision,
+                                      _stream(stream)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().ce_decoder_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_model(self, embedding, classifier, norm_w, stream=None):
+        check(lib().ce_decoder_set_model(self._h, _ptr(embedding), _ptr(classifier), _ptr(norm_w),
+                                         _stream(stream)))
+
+    def enqueue_compute(self, stream=None):
+        check(lib().ce_decoder_enqueue_compute(self._h, _stream(stream)))
+
+    def enqueue_application(self, stream=None):
+        check(lib().ce_decoder_enqueue_application(self._h, _stream(stream)))
+
+    def poison_outputs(self, stream=None):
+        check(lib().ce_decoder_poison(self._h, _stream(stream)))
+
+    def inject_fault(self, fault):
+        check(lib().ce_decoder_inject_fault(self._h, fault))
+
+    def outputs(self, from_device=False, which=("generated", "normalized", "logits", "probabilities")):
+        """Host copies: generated [B][S] int32, normalized [S][B][W],
+        logits and probabilities [S][B][V] float32."""
+        B, W, V, S = self.batch, self.width, self.vocab, self.steps
+        g = np.empty((B, S), np.int32) if "generated" in which else None
+        n = np.empty((S, B, W), np.float32) if "normalized" in which else None
+        lg = np.empty((S, B, V), np.float32) if "logits" in which else None
+        p = np.empty((S, B, V), np.float32) if "probabilities" in which else None
+        check(lib().ce_decoder_copy_outputs(self._h, int(bool(from_device)), _ptr(g), _ptr(n),
+                                            _ptr(lg), _ptr(p)))
+        return g, n, lg, p

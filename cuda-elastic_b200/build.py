@@ -23,7 +23,7 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
           "--expt-relaxed-constexpr", "-I", os.path.join(ROOT, "include")]
 # Files whose arithmetic order is part of their contract: no contraction of
 # a multiply and an add into an FMA.
-NO_FMAD = {"simt_gemm.cu"}
+NO_FMAD = {"simt_gemm.cu", "decoder.cu"}
 
 
 def nvcc():

@@ -11,142 +11,16 @@
 //     not 16-byte aligned, take a generic two-pass path in the same files.
 // Reference kernels replaced: llama2c/llama2c_cuda_graph.cu:58-162 and the
 // fused llama2c/llama2c_sota.cu:263-298.
-#include <cuda_bf16.h>
-#include <float.h>
-
-#include "common.cuh"
+#include "row_ops.cuh"
 
 namespace ce {
 namespace {
 
+using namespace rowops;
+
 constexpr int kRowThreads = 512;      // register path: threads per row
 constexpr int kGenericThreads = 512;  // generic path
 constexpr int kGemvUnroll = 8;        // float4 loads in flight per lane
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
-
-// Block-wide sum / max, result broadcast to every thread. `scratch` holds 32
-// floats; the trailing barrier lets the caller reuse it immediately.
-__device__ __forceinline__ float block_sum(float v, float *scratch) {
-  v = warp_sum(v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  v = lane < (int)(blockDim.x >> 5) ? scratch[lane] : 0.0f;
-  v = warp_sum(v);
-  __syncthreads();
-  return v;
-}
-__device__ __forceinline__ float block_max(float v, float *scratch) {
-  v = warp_max(v);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  v = lane < (int)(blockDim.x >> 5) ? scratch[lane] : -FLT_MAX;
-  v = warp_max(v);
-  __syncthreads();
-  return v;
-}
-
-// ---------------------------------------------------------------------------
-// Register-resident row bodies. Each thread owns float4 slots
-// threadIdx.x + j * blockDim.x, j < NV, of a row of cols4 float4s.
-
-template <int NV>
-__device__ __forceinline__ void load_row(float4 (&v)[NV], const float4 *row, int cols4) {
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * blockDim.x;
-    v[j] = i < cols4 ? __ldcs(row + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-}
-
-// RMSNorm of one row: out = x * scale * w, scale = 1 / sqrtf(ss / cols + eps)
-// (IEEE division and square root, the llama2.c order of run.c's rmsnorm as
-// restated in applications/loom_private/decoder/decoder.cu:71-76).
-template <int NV>
-__device__ __forceinline__ void rmsnorm_row(const float4 *x, const float4 *w, float4 *out,
-                                            uint2 *out_bf16, int cols4, int cols,
-                                            float eps, float *scratch) {
-  float4 v[NV];
-  load_row<NV>(v, x, cols4);
-  float ss = 0.f;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
-  ss = block_sum(ss, scratch);
-  const float scale = 1.0f / sqrtf(ss / (float)cols + eps);
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * blockDim.x;
-    if (i < cols4) {
-      const float4 g = __ldg(w + i);
-      float4 o;
-      o.x = g.x * (scale * v[j].x);
-      o.y = g.y * (scale * v[j].y);
-      o.z = g.z * (scale * v[j].z);
-      o.w = g.w * (scale * v[j].w);
-      if (out != nullptr) __stcs(out + i, o);
-      if (out_bf16 != nullptr) {
-        __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y);
-        __nv_bfloat162 hi = __floats2bfloat162_rn(o.z, o.w);
-        uint2 packed;
-        packed.x = *reinterpret_cast<uint32_t *>(&lo);
-        packed.y = *reinterpret_cast<uint32_t *>(&hi);
-        out_bf16[i] = packed;
-      }
-    }
-  }
-}
-
-// Softmax of one row held in registers: max, then e = expf(l - max) kept in
-// registers, their sum, then e / sum. One read, one write.
-template <int NV>
-__device__ __forceinline__ void softmax_row(const float4 *logits, float4 *out, int cols4,
-                                            float *scratch) {
-  float4 v[NV];
-  load_row<NV>(v, logits, cols4);
-  float m = -FLT_MAX;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * blockDim.x;
-    if (i < cols4) m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
-  }
-  m = block_max(m, scratch);
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * blockDim.x;
-    if (i < cols4) {
-      v[j].x = expf(v[j].x - m);
-      v[j].y = expf(v[j].y - m);
-      v[j].z = expf(v[j].z - m);
-      v[j].w = expf(v[j].w - m);
-      s += (v[j].x + v[j].y) + (v[j].z + v[j].w);
-    }
-  }
-  s = block_sum(s, scratch);
-#pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * blockDim.x;
-    if (i < cols4) {
-      float4 o;
-      o.x = v[j].x / s;
-      o.y = v[j].y / s;
-      o.z = v[j].z / s;
-      o.w = v[j].w / s;
-      __stcs(out + i, o);
-    }
-  }
-}
 
 // GEMV rows: warp w of the block computes product[row0 + w].
 __device__ __forceinline__ void gemv_rows_vec(const float4 *matrix, const float4 *x, float *product,

@@ -241,6 +241,58 @@ int ce_plan_trio(ce_plan *plan, float *normalized_dev, float *softmax_dev, float
                  const float *x_dev, const float *norm_w_dev, const float *logits_dev,
                  float eps, ce_stream_t stream);
 
+/* ------------------------------------------------------------------ */
+/* loom_private llama2c decoder (applications/loom_private/decoder/).   */
+
+/* A decoder workload: B sequences decoded greedily for S dependent steps
+ * through rmsnorm -> classifier -> softmax + first argmax, the token fed back
+ * on the device. Mirrors the reference's lp::Workload
+ * (applications/loom_private/common/lp_harness.cuh:240-267) as implemented by
+ * decoder.cu:200-367. */
+typedef struct ce_decoder ce_decoder;
+
+/* Validates the dimensions with the limits and messages of make_decoder
+ * (decoder.cu:369-408; the device limit is raised to B200 memory: 160 GiB),
+ * allocates every buffer, generates the synthetic model on the device
+ * (init_model_kernel, decoder.cu:31-43) and writes the prompts b mod vocab
+ * into the decoder's pinned buffer. precision: CE_PREC_FP32 (the contract's
+ * bitwise order), CE_PREC_TF32 (width % 4 == 0) or CE_PREC_BF16. Setup call:
+ * allocates and synchronizes the stream. */
+int ce_decoder_create(ce_decoder **dec, int64_t batch, int64_t width, int64_t vocab, int64_t steps,
+                      int precision, ce_stream_t stream);
+int ce_decoder_destroy(ce_decoder *dec);
+
+/* Replaces the synthetic model by caller weights (device fp32: embedding and
+ * classifier [vocab][width], norm weight [width]); setup call. */
+int ce_decoder_set_model(ce_decoder *dec, const float *embedding_dev, const float *classifier_dev,
+                         const float *norm_w_dev, ce_stream_t stream);
+
+/* Token reset from the resident prompts, then every step (decoder.cu:276-296).
+ * Capturable. */
+int ce_decoder_enqueue_compute(ce_decoder *dec, ce_stream_t stream);
+
+/* Prompt upload (pinned H2D), compute, generated-token download (pinned D2H)
+ * (decoder.cu:267-274). Capturable. */
+int ce_decoder_enqueue_application(ce_decoder *dec, ce_stream_t stream);
+
+/* 0xFF into every output, the device prompts and tokens, and the pinned
+ * generated buffer (decoder.cu:298-312); synchronizes the stream. */
+int ce_decoder_poison(ce_decoder *dec, ce_stream_t stream);
+
+/* Synchronous diagnostics copy of the outputs into host memory (any pointer
+ * may be NULL): generated [batch][steps] (from the pinned buffer of the last
+ * application scope, or from the device when from_device != 0), normalized
+ * [steps][batch][width], logits and probabilities [steps][batch][vocab]
+ * (decoder.cu:318-331). */
+int ce_decoder_copy_outputs(ce_decoder *dec, int from_device, int32_t *generated_host,
+                            float *normalized_host, float *logits_host,
+                            float *probabilities_host);
+
+/* The reference's host-side fault hook (decoder.cu:346-358): fault 1 flips
+ * the low bit of the last generated token in the pinned buffer; 0 does
+ * nothing; 2 and 3 are applied by the caller to its diagnostics copy. */
+int ce_decoder_inject_fault(ce_decoder *dec, int fault);
+
 #ifdef __cplusplus
 }
 #endif

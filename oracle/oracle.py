@@ -290,7 +290,15 @@ def decoder_tokens(batch, vocab, steps):
     return t.reshape(batch, steps)
 
 
-def fnv1a64(arrays, h=0xcbf29ce484222325):
+# lp::fnv1a64's initial state is the literal 1469598103934665603
+# (applications/loom_private/common/lp_harness.cuh:108), one decimal digit
+# short of the published FNV-1a 64 offset basis 14695981039346656037; the
+# reference's digests (e.g. the decoder's 4fcc3e102976547b) are defined with
+# it, so the oracle uses the same state.
+LP_FNV_STATE = 1469598103934665603
+
+
+def fnv1a64(arrays, h=LP_FNV_STATE):
     """lp::fnv1a64 chained over the byte images of arrays
     (applications/loom_private/common/lp_harness.cuh:107-115)."""
     for a in arrays:
@@ -318,3 +326,93 @@ def trio_fp32(x, w, logits, W, eps=RMS_EPS, threads=0):
                                np.ascontiguousarray(logits), np.ascontiguousarray(W),
                                norm, soft, out, b, k, n, float(eps), threads)
     return norm, soft, out, used
+
+
+def decoder_sampled(batch):
+    """Up to 8 sequences spread evenly over the batch, both ends included
+    (applications/loom_private/decoder/oracle.cpp:97-102)."""
+    count = min(8, batch)
+    out = []
+    for i in range(count):
+        b = 0 if count == 1 else i * (batch - 1) // (count - 1)
+        if not out or out[-1] != b:
+            out.append(b)
+    return out
+
+
+def decoder_reference(batch, width, vocab, steps):
+    """decoder_oracle::compute (oracle.cpp:31-123) for the synthetic model:
+    analytic tokens, and the double-precision rmsnorm -> classifier ->
+    softmax -> argmax of the sampled sequences. The classifier row r has a
+    single 1 at column (r + vocab - 1) mod vocab, so its dense double sum is
+    that one product (every other term is an exact zero)."""
+    tokens = decoder_tokens(batch, vocab, steps)
+    sampled = decoder_sampled(batch)
+    n = len(sampled)
+    normalized = np.empty((n, steps, width))
+    logits = np.empty((n, steps, vocab))
+    probs = np.empty((n, steps, vocab))
+    consistent = True
+    perm = (np.arange(vocab) + vocab - 1) % vocab
+    for i, b in enumerate(sampled):
+        token = b % vocab
+        for s in range(steps):
+            act = np.ones(width)
+            act[token] = 4.0
+            ss = float((act * act).sum())
+            scale = 1.0 / np.sqrt(ss / width + 1.0e-5)
+            o = 1.0 * (scale * act)
+            lg = o[perm]
+            p = np.exp(lg - lg.max())
+            p = p / p.sum()
+            best = int(np.argmax(p))  # first maximum
+            if best != (token + 1) % vocab:
+                consistent = False
+            normalized[i, s], logits[i, s], probs[i, s] = o, lg, p
+            token = best
+    return {"tokens": tokens, "sampled": sampled, "normalized": normalized, "logits": logits,
+            "probabilities": probs, "self_consistent": consistent}
+
+
+def decoder_check(ref, generated, normalized, logits, probabilities):
+    """decoder_oracle::check (oracle.cpp:125-229). generated [B][S] int32,
+    normalized [S][B][W], logits / probabilities [S][B][V] float32. Returns
+    (pass, report) where report lists the first mismatches of each kind."""
+    tokens = ref["tokens"]
+    B, S = tokens.shape
+    W = normalized.shape[2]
+    V = logits.shape[2]
+    report = {"token": [], "invariant": [], "dense": []}
+    bad = np.argwhere(generated != tokens)
+    for b, s in bad[:8]:
+        report["token"].append(f"token mismatch sequence {b} step {s}: expected {tokens[b, s]}, "
+                               f"actual {generated[b, s]}")
+    token_errors = len(bad)
+    square_bound = np.float32(2.0e-5) + np.float32(1.2e-7) * np.float32(W)
+    prob_bound = np.float32(1.0e-6) + np.float32(1.2e-7) * np.float32(V)
+    sq = (normalized.astype(np.float64) ** 2).sum(axis=2)          # [S][B]
+    square_mean = (sq / W).astype(np.float32)
+    psum = probabilities.astype(np.float64).sum(axis=2).astype(np.float32)
+    sq_err = np.abs(square_mean - np.float32(1.0))
+    p_err = np.abs(psum - np.float32(1.0))
+    inv_bad = ~((sq_err <= square_bound) & (p_err <= prob_bound))  # NaN fails
+    for s, b in np.argwhere(inv_bad)[:8]:
+        report["invariant"].append(f"invariant failure sequence {b} step {s}")
+    invariant_errors = int(inv_bad.sum())
+    dense_errors = 0
+    for i, b in enumerate(ref["sampled"]):
+        for s in range(S):
+            for what, obs, exp, rel in (("normalized", normalized[s, b], ref["normalized"][i, s], 2.0e-6),
+                                        ("logit", logits[s, b], ref["logits"][i, s], 2.0e-6),
+                                        ("probability", probabilities[s, b], ref["probabilities"][i, s], 2.0e-5)):
+                ok = np.abs(obs.astype(np.float64) - exp) <= rel * np.abs(exp) + 1.0e-12
+                if not ok.all():
+                    idx = np.argwhere(~ok).ravel()
+                    dense_errors += len(idx)
+                    if len(report["dense"]) < 8:
+                        j = idx[0]
+                        report["dense"].append(f"{what} mismatch sequence {b} step {s} index {j}: "
+                                               f"expected {exp[j]:.9g}, actual {obs[j]:.9g}")
+    passed = ref["self_consistent"] and token_errors == 0 and invariant_errors == 0 and dense_errors == 0
+    report.update(token_errors=token_errors, invariant_errors=invariant_errors, dense_errors=dense_errors)
+    return passed, report

@@ -73,3 +73,25 @@ def test_usage_errors_before_device_work(ce):
     with pytest.raises(ce.CeError) as e:
         ce.check(L.ce_rmsnorm(None, None, None, 1, 0, 1e-5, None))
     assert e.value.status == ce.ERR_USAGE
+
+
+# The reference's invalid-dimension cases (decoder/tests/run_tests.sh:52-62):
+# rejected with CE_ERR_USAGE (its exit code 2) and the same message, before
+# any device work.
+@pytest.mark.parametrize("dims,pattern", [
+    ((1024, 8, 1, 4), "vocab must satisfy"),
+    ((1024, 16, 17, 4), "vocab must satisfy"),
+    ((1024, 32, 8, 1), "steps must be"),
+    ((0, 16384, 8192, 4), "batch must be"),
+    ((1024, 0, 8192, 4), "width must be"),
+    ((1, 16777201, 2, 2), "width must be"),
+    ((1048576, 16384, 8192, 4), "GiB"),
+    ((1024, 16384, 8192, 1025), "steps must be"),
+])
+def test_decoder_invalid_dimensions(ce, dims, pattern):
+    import ctypes
+    h = ctypes.c_void_p()
+    rc = ce.lib().ce_decoder_create(ctypes.byref(h), *dims, ce.PREC_FP32, None)
+    assert rc == ce.ERR_USAGE
+    assert pattern in ce.last_error()[1]
+    assert not h.value

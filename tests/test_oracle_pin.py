@@ -213,3 +213,63 @@ def test_golden_decoder(O):
     g = _golden("decoder.npz")
     B, W, V, S = (int(v) for v in g["shape"])
     assert np.array_equal(O.decoder_tokens(B, V, S).ravel(), g["tokens"])
+
+
+def _decoder_outputs_from_reference(O, B, W, V, S):
+    """Exact float32 outputs of the synthetic model computed on the host in
+    the contract's order (used only to exercise the checkers)."""
+    ref = O.decoder_reference(B, W, V, S)
+    tokens = ref["tokens"]
+    gen = tokens.copy()
+    norm = np.empty((S, B, W), np.float32)
+    logit = np.empty((S, B, V), np.float32)
+    prob = np.empty((S, B, V), np.float32)
+    perm = (np.arange(V) + V - 1) % V
+    for b in range(B):
+        t = b % V
+        for s in range(S):
+            x = np.ones(W, np.float32); x[t] = 4.0
+            ss = np.float32(W + 15)
+            scale = np.float32(1.0) / np.sqrt(ss / np.float32(W) + np.float32(1e-5))
+            o = np.float32(1.0) * (scale * x)
+            lg = o[perm]
+            e = np.exp(lg - lg.max()).astype(np.float32)
+            p = (e / e.sum(dtype=np.float32)).astype(np.float32)
+            norm[s, b], logit[s, b], prob[s, b] = o, lg, p
+            t = tokens[b, s]
+    return ref, gen, norm, logit, prob
+
+
+@pytest.mark.parametrize("shape", [(40, 96, 16, 5), (3, 2, 2, 2), (9, 64, 33, 3)])
+def test_decoder_check_matches_reference(O, shape):
+    """The oracle's decoder check gives the reference checker's verdict on
+    correct outputs and on each injected fault (decoder.cu:346-358)."""
+    import ctypes
+    R = _ref(O)
+    B, W, V, S = shape
+    ref, gen, norm, logit, prob = _decoder_outputs_from_reference(O, B, W, V, S)
+    # dense references agree with the reference's own oracle
+    tokens = np.empty(B * S, np.int32)
+    sampled = np.empty(8, np.int64)
+    n = ctypes.c_int()
+    nd = np.empty(8 * S * W); lg = np.empty(8 * S * V); pr = np.empty(8 * S * V)
+    assert R.ref_decoder_compute(B, W, V, S, tokens, sampled, ctypes.byref(n), nd, lg, pr) == 1
+    assert list(sampled[:n.value]) == ref["sampled"]
+    k = n.value
+    assert np.allclose(nd[:k * S * W].reshape(k, S, W), ref["normalized"], rtol=1e-15, atol=0)
+    assert np.array_equal(lg[:k * S * V].reshape(k, S, V), ref["logits"])
+    assert np.allclose(pr[:k * S * V].reshape(k, S, V), ref["probabilities"], rtol=1e-13, atol=1e-300)
+    for fault in (0, 1, 2, 3):
+        g, nn, ll, pp = gen.copy(), norm.copy(), logit.copy(), prob.copy()
+        if fault == 1:
+            g[B - 1, S - 1] ^= 1
+        elif fault == 2:
+            nn[S - 1, B // 2, 0] *= 2.0
+        elif fault == 3:
+            pp[S - 1, 0, V // 2] *= np.float32(1.001)
+        want = R.ref_decoder_check(B, W, V, S, np.ascontiguousarray(g.ravel()),
+                                   np.ascontiguousarray(nn.ravel()), np.ascontiguousarray(ll.ravel()),
+                                   np.ascontiguousarray(pp.ravel()))
+        got, report = O.decoder_check(ref, g, nn, ll, pp)
+        assert bool(want) == got, (fault, report)
+        assert got == (fault == 0), (fault, report)
