@@ -42,6 +42,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="target CPU time of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the decoder tokens/s section")
     ap.add_argument("--profile", action="store_true",
                     help="setup, warm-up and the timed steps only (for ncu captures); no JSON line")
     return ap.parse_args()
@@ -325,6 +326,30 @@ def run_ours(args, rank, world, local_rank):
     min_bytes = 805470208.0  # llama2c_cuda_graph.cu:340-345 at this shape
     del mat
 
+    # ---- loom_private decoder, large shape (1024 seq x 4 steps, W 16384, V 8192) ----
+    decoder = {}
+    if not args.no_decoder:
+        for prec_name, prec_val in (("bf16", ce.PREC_BF16), ("fp32_contract", ce.PREC_FP32)):
+            dec = ce.Decoder(1024, 16384, 8192, 4, prec_val, stream=s)
+            res = {}
+            for scope in ("application", "compute"):
+                fn = dec.enqueue_application if scope == "application" else dec.enqueue_compute
+                reps = 10 if prec_name == "bf16" else 2
+                with torch.cuda.stream(stream):
+                    fn(stream=s)
+                    d0 = torch.cuda.Event(enable_timing=True)
+                    d1 = torch.cuda.Event(enable_timing=True)
+                    d0.record(stream)
+                    for _ in range(reps):
+                        fn(stream=s)
+                    d1.record(stream)
+                torch.cuda.synchronize(dev)
+                ms = d0.elapsed_time(d1) / reps
+                res[scope] = {"ms_per_invocation": ms, "tokens_per_s": 4096 / (ms * 1e-3)}
+            ce.device_status()
+            dec.close()
+            decoder[prec_name] = res
+
     pk, pk_kind = peaks()
     long_region = total_ms > 1000.0
     peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
@@ -363,6 +388,9 @@ def run_ours(args, rank, world, local_rank):
                               "unit": "GB/s"},
             "legacy_iteration": {"ms_per_iter": legacy_ms, "min_bytes_per_iter": min_bytes,
                                  "achieved_gbps": min_bytes / (legacy_ms * 1e-3) / 1e9},
+            "decoder": {"workload": "loom_private llama2c decoder, synthetic model, 1024 sequences x "
+                                    "4 greedy steps, width 16384, vocab 8192 (4096 tokens per invocation)",
+                        **decoder},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "clocks": clocks,

@@ -17,6 +17,9 @@ ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libce_b200.so")
+HOST = os.path.join(PKG, "host")
+# Drop-in front ends (host C++ over the C ABI): executable -> sources in host/.
+EXECUTABLES = {"llama2c_b200": ["llama2c_b200.cpp", "llama2c_check.cpp"]}
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",
@@ -77,6 +80,19 @@ def build(verbose=False, ptxas_verbose=False):
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    for exe, srcs in EXECUTABLES.items():
+        out = os.path.join(PKG, exe)
+        paths = [os.path.join(HOST, f) for f in srcs]
+        deps = paths + [LIB] + [os.path.join(HOST, f) for f in os.listdir(HOST) if f.endswith(".h")]
+        if _stale(out, deps):
+            cmd = [nvcc(), "-O2", "-std=c++17", "-I", os.path.join(ROOT, "include"), "-I", HOST,
+                   "-o", out] + paths + ["-L", PKG, "-lce_b200", "-Xlinker", "-rpath,$ORIGIN",
+                                         "-cudart", "static", "-lpthread"]
+            if verbose:
+                print(" ".join(cmd), flush=True)
+            r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode != 0:
+                raise RuntimeError(f"build of {exe} failed:\n{r.stdout}\n{r.stderr}")
     return LIB
 
 

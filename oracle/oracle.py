@@ -416,3 +416,29 @@ def decoder_check(ref, generated, normalized, logits, probabilities):
     passed = ref["self_consistent"] and token_errors == 0 and invariant_errors == 0 and dense_errors == 0
     report.update(token_errors=token_errors, invariant_errors=invariant_errors, dense_errors=dense_errors)
     return passed, report
+
+
+def read_l2cdump1(path):
+    """Reader of the L2CDUMP1 dump (llama2c/llama2c_common.h:16-32):
+    header, normalized[B*S] f32, softmax[B*S] f32, product[R] f32,
+    product_tolerance[R] f32, product_reference[R] f64."""
+    with open(path, "rb") as f:
+        raw = f.read()
+    if raw[:8] != b"L2CDUMP1":
+        raise ValueError(f"{path}: not an L2CDUMP1 dump")
+    batch, size, rows, inputs = np.frombuffer(raw, np.int32, 4, 8)
+    seed = int(np.frombuffer(raw, np.uint64, 1, 24)[0])
+    off = 32
+    vec = int(batch) * int(size)
+    out = {"batch": int(batch), "size": int(size), "rows": int(rows), "random": int(inputs),
+           "seed": seed}
+    for name, dt, n in (("normalized", np.float32, vec), ("softmax", np.float32, vec),
+                        ("product", np.float32, int(rows)), ("product_tolerance", np.float32, int(rows)),
+                        ("product_reference", np.float64, int(rows))):
+        out[name] = np.frombuffer(raw, dt, n, off).copy()
+        off += n * np.dtype(dt).itemsize
+    if off != len(raw):
+        raise ValueError(f"{path}: {len(raw) - off} trailing bytes")
+    out["normalized"] = out["normalized"].reshape(int(batch), int(size))
+    out["softmax"] = out["softmax"].reshape(int(batch), int(size))
+    return out

@@ -95,3 +95,19 @@ def test_decoder_invalid_dimensions(ce, dims, pattern):
     assert rc == ce.ERR_USAGE
     assert pattern in ce.last_error()[1]
     assert not h.value
+
+
+def _llama2c_exe():
+    return os.path.join(ROOT, "cuda-elastic_b200", "llama2c_b200")
+
+
+@pytest.mark.parametrize("args,pattern", [(["bogus"], "Usage:"), (["0"], "Usage:"),
+                                          (["1", "2", "3", "4", "5", "6", "7"], "Usage:"),
+                                          (["random=x1"], "bad seed")])
+def test_llama2c_cli_usage_errors(args, pattern):
+    """Command-line errors exit with EXIT_FAILURE before any device work, with
+    the reference's messages (llama2c_cuda_graph.cu:195-258)."""
+    import subprocess
+    r = subprocess.run([_llama2c_exe()] + args, capture_output=True, text=True, timeout=60)
+    assert r.returncode == 1
+    assert pattern in r.stderr
