@@ -80,6 +80,9 @@ _SIGNATURES = {
     "ce_gemm_config": [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_fp32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_convert_bf16": [_vp, _vp, _i, _i, _i, _vp],
+    "ce_quantize_e4m3_rows": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "ce_rmsnorm_e4m3": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _f, _vp],
+    "ce_gemm_e4m3": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_rmsnorm_bf16": [_vp, _vp, _i, _vp, _vp, _i, _i, _f, _vp],
     "ce_plan_create": [ctypes.POINTER(_vp), _i, _i, _i, _i],
     "ce_plan_destroy": [_vp],
@@ -274,6 +277,30 @@ def gemm_fp32(d, a, b, k=None, stream=None):
     K = lda if k is None else k
     check(lib().ce_gemm_fp32(_ptr(d), _ptr(a), _ptr(b), M, N, K, lda, ldb, d.shape[1],
                              _stream(stream)))
+    return d
+
+
+def quantize_e4m3_rows(codes, scales, x, stream=None):
+    """Per-row E4M3 quantization: codes uint8 [rows][ld], scales float32 [rows]."""
+    rows, cols = x.shape
+    check(lib().ce_quantize_e4m3_rows(_ptr(codes), _ptr(scales), _ptr(x), rows, cols, codes.shape[1],
+                                      _stream(stream)))
+    return codes, scales
+
+
+def rmsnorm_e4m3(out, codes, scales, x, w, eps=RMS_EPS, stream=None):
+    rows, cols = x.shape
+    check(lib().ce_rmsnorm_e4m3(_ptr(out), _ptr(codes), codes.shape[1], _ptr(scales), _ptr(x),
+                                _ptr(w), rows, cols, eps, _stream(stream)))
+    return codes, scales
+
+
+def gemm_e4m3(d, a, a_scale, b, b_scale, k=None, stream=None):
+    M, lda = a.shape
+    N, ldb = b.shape
+    K = lda if k is None else k
+    check(lib().ce_gemm_e4m3(_ptr(d), _ptr(a), _ptr(a_scale), _ptr(b), _ptr(b_scale), M, N, K, lda,
+                             ldb, d.shape[1], _stream(stream)))
     return d
 
 

@@ -20,7 +20,8 @@ namespace ce {
 int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, const float *input,
                    const float *weight, float *softmax, const float *logits, float *product,
                    const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
-                   int cols, int gemv_rows, float eps, cudaStream_t s);
+                   int cols, int gemv_rows, float eps, cudaStream_t s,
+                   uint8_t *normalized_e4m3 = nullptr, int ld_e4m3 = 0, float *e4m3_scale = nullptr);
 int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
@@ -31,6 +32,11 @@ int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int
 int gemm_simt_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda,
                    int ldb, int ldd, cudaStream_t s);
 int gemm_status();
+int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K, int lda,
+              int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
+              cudaStream_t s, int force_group = 0);
+int quantize_rows_e4m3(uint8_t *codes, float *scales, const float *x, int rows, int cols, int ld,
+                       cudaStream_t s);
 int gemm_set_prefetch(int kblocks);
 
 // ---------------------------------------------------------------------------
@@ -288,6 +294,9 @@ int ce_gemm_config(int precision, float *d, const void *a, const void *b, int M,
   if (precision == CE_PREC_TF32)
     return gemm_tf32(d, static_cast<const float *>(a), static_cast<const float *>(b), M, N, K, lda,
                      ldb, ldd, nullptr, nullptr, tile_n, (cudaStream_t)stream, cta_group);
+  if (precision == CE_PREC_FP8_E4M3)
+    return gemm_e4m3(d, static_cast<const uint8_t *>(a), static_cast<const uint8_t *>(b), M, N, K,
+                     lda, ldb, ldd, nullptr, nullptr, tile_n, (cudaStream_t)stream, cta_group);
   return set_error(CE_ERR_USAGE, format("ce_gemm_config: precision %d has no tensor-core kernel", precision));
 }
 
@@ -299,6 +308,25 @@ int ce_gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, 
 int ce_gemm_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,
                  int ldd, ce_stream_t stream) {
   return gemm_simt_fp32(d, a, b, M, N, K, lda, ldb, ldd, (cudaStream_t)stream);
+}
+
+int ce_quantize_e4m3_rows(uint8_t *codes, float *scales, const float *x, int rows, int cols,
+                          int ld, ce_stream_t stream) {
+  return quantize_rows_e4m3(codes, scales, x, rows, cols, ld, (cudaStream_t)stream);
+}
+
+int ce_rmsnorm_e4m3(float *out, uint8_t *codes, int ld, float *scales, const float *x,
+                    const float *w, int rows, int cols, float eps, ce_stream_t stream) {
+  CE_REQUIRE(rows >= 1 && cols >= 1, "rows and cols must be >= 1 (got %d, %d)", rows, cols);
+  CE_REQUIRE(codes && scales && x && w, "null argument");
+  return rows_iteration(out, nullptr, 0, x, w, nullptr, nullptr, nullptr, nullptr, nullptr, rows, 0,
+                        cols, 0, eps, (cudaStream_t)stream, codes, ld, scales);
+}
+
+int ce_gemm_e4m3(float *d, const uint8_t *a, const float *a_scale, const uint8_t *b,
+                 const float *b_scale, int M, int N, int K, int lda, int ldb, int ldd,
+                 ce_stream_t stream) {
+  return gemm_e4m3(d, a, b, M, N, K, lda, ldb, ldd, a_scale, b_scale, 0, (cudaStream_t)stream);
 }
 
 int ce_convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld_out,
@@ -315,8 +343,10 @@ int ce_convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld_o
 struct ce_plan {
   int batch = 0, size = 0, rows = 0, precision = 0, device = 0;
   int ld = 0;                    // padded K of the prepared operands
-  void *weights = nullptr;       // bf16 / fp32 [rows][ld], or fp32 [rows][size] (FP32)
-  void *activations = nullptr;   // bf16 / fp32 [batch][ld]
+  void *weights = nullptr;       // bf16 / fp32 / e4m3 [rows][ld], or fp32 [rows][size] (FP32)
+  void *activations = nullptr;   // bf16 / fp32 / e4m3 [batch][ld]
+  float *w_scale = nullptr;      // e4m3: per weight row
+  float *a_scale = nullptr;      // e4m3: per activation row
   bool has_weights = false;
 };
 
@@ -326,8 +356,11 @@ int ce_plan_create(ce_plan **out, int batch, int size, int rows, int precision) 
   CE_REQUIRE(out != nullptr, "null plan pointer");
   *out = nullptr;
   CE_REQUIRE(batch >= 1 && size >= 1 && rows >= 1, "batch, size and rows must be >= 1");
-  CE_REQUIRE(precision == CE_PREC_FP32 || precision == CE_PREC_TF32 || precision == CE_PREC_BF16,
+  CE_REQUIRE(precision == CE_PREC_FP32 || precision == CE_PREC_TF32 || precision == CE_PREC_BF16 ||
+                 precision == CE_PREC_FP8_E4M3,
              "precision %d is not available in this build", precision);
+  CE_REQUIRE(precision != CE_PREC_FP8_E4M3 || (size % 4 == 0 && size <= 32768),
+             "the e4m3 plan needs size %% 4 == 0 and size <= 32768 (got %d)", size);
   ce_plan *p = new ce_plan();
   p->batch = batch;
   p->size = size;
@@ -335,9 +368,15 @@ int ce_plan_create(ce_plan **out, int batch, int size, int rows, int precision) 
   p->precision = precision;
   CE_CUDA_TRY(cudaGetDevice(&p->device));
   p->ld = precision == CE_PREC_FP32 ? size : ((size + 63) / 64) * 64;
-  const size_t elem = precision == CE_PREC_BF16 ? 2 : 4;
+  const size_t elem = precision == CE_PREC_BF16 ? 2 : precision == CE_PREC_FP8_E4M3 ? 1 : 4;
   cudaError_t e = cudaMalloc(&p->activations, (size_t)batch * p->ld * elem);
+  if (e == cudaSuccess && precision == CE_PREC_FP8_E4M3) {
+    e = cudaMalloc(&p->a_scale, (size_t)batch * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&p->w_scale, (size_t)rows * 4);
+  }
   if (e != cudaSuccess) {
+    if (p->activations) cudaFree(p->activations);
+    if (p->a_scale) cudaFree(p->a_scale);
     delete p;
     return cuda_error(e, "cudaMalloc(activations)");
   }
@@ -349,6 +388,8 @@ int ce_plan_destroy(ce_plan *p) {
   if (p == nullptr) return CE_OK;
   if (p->weights) cudaFree(p->weights);
   if (p->activations) cudaFree(p->activations);
+  if (p->a_scale) cudaFree(p->a_scale);
+  if (p->w_scale) cudaFree(p->w_scale);
   delete p;
   return CE_OK;
 }
@@ -356,9 +397,13 @@ int ce_plan_destroy(ce_plan *p) {
 int ce_plan_set_weights(ce_plan *p, const float *w, ce_stream_t stream) {
   CE_REQUIRE(p != nullptr && w != nullptr, "null plan or weights");
   cudaStream_t s = (cudaStream_t)stream;
-  const size_t elem = p->precision == CE_PREC_BF16 ? 2 : 4;
+  const size_t elem = p->precision == CE_PREC_BF16 ? 2 : p->precision == CE_PREC_FP8_E4M3 ? 1 : 4;
   if (p->weights == nullptr) CE_CUDA_TRY(cudaMalloc(&p->weights, (size_t)p->rows * p->ld * elem));
-  if (p->precision == CE_PREC_BF16) {
+  if (p->precision == CE_PREC_FP8_E4M3) {
+    int rc = quantize_rows_e4m3(static_cast<uint8_t *>(p->weights), p->w_scale, w, p->rows, p->size,
+                                p->ld, s);
+    if (rc) return rc;
+  } else if (p->precision == CE_PREC_BF16) {
     int rc = convert_bf16(static_cast<uint16_t *>(p->weights), w, p->rows, p->size, p->ld, s);
     if (rc) return rc;
   } else {
@@ -377,6 +422,10 @@ static int plan_gemm(ce_plan *p, float *out, cudaStream_t s) {
       return gemm_bf16(out, static_cast<const uint16_t *>(p->activations),
                        static_cast<const uint16_t *>(p->weights), p->batch, p->rows, p->size,
                        p->ld, p->ld, p->rows, nullptr, nullptr, 0, s);
+    case CE_PREC_FP8_E4M3:
+      return gemm_e4m3(out, static_cast<const uint8_t *>(p->activations),
+                       static_cast<const uint8_t *>(p->weights), p->batch, p->rows, p->size, p->ld,
+                       p->ld, p->rows, p->a_scale, p->w_scale, 0, s);
     case CE_PREC_TF32:
       return gemm_tf32(out, static_cast<const float *>(p->activations),
                        static_cast<const float *>(p->weights), p->batch, p->rows, p->size, p->ld,
@@ -393,6 +442,10 @@ static int plan_gemm(ce_plan *p, float *out, cudaStream_t s) {
 static int plan_rows(ce_plan *p, float *normalized, float *softmax, const float *x,
                      const float *norm_w, const float *logits, float eps, cudaStream_t s) {
   const int nsoft = logits ? p->batch : 0;
+  if (p->precision == CE_PREC_FP8_E4M3)
+    return rows_iteration(normalized, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr,
+                          nullptr, p->batch, nsoft, p->size, 0, eps, s,
+                          static_cast<uint8_t *>(p->activations), p->ld, p->a_scale);
   if (p->precision == CE_PREC_BF16)
     return rows_iteration(normalized, static_cast<uint16_t *>(p->activations), p->ld, x, norm_w,
                           softmax, logits, nullptr, nullptr, nullptr, p->batch, nsoft, p->size, 0,

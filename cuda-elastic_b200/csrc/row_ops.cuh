@@ -137,5 +137,76 @@ __device__ __forceinline__ void softmax_row(const float4 *logits, float4 *out, i
   }
 }
 
+// Clears the sign of every byte equal to 0x80 (E4M3 -0): the spec's
+// rounding rule encodes a magnitude that rounds to zero as +0 (code 0),
+// whereas the hardware conversion keeps the sign. Exact zero-byte test:
+// bytes of t that are 0 get 0x80 in z.
+__device__ __forceinline__ uint32_t e4m3_positive_zero(uint32_t codes) {
+  const uint32_t t = codes ^ 0x80808080u;
+  const uint32_t z = ~(((t & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | t | 0x7F7F7F7Fu);
+  return codes & ~z;
+}
+
+// Two fp32 values to two OCP E4M3 codes (round to nearest even, saturating
+// to +-448; NaN stays NaN; a zero result is +0): lo in the low byte, hi in
+// the high byte.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return e4m3_positive_zero((uint32_t)r);
+}
+
+// Per-row E4M3 quantization of values held in registers: amax over the row,
+// inv = 448 / amax and scale = amax / 448 (both IEEE fp32; 0 for an all-zero
+// row), code = E4M3(v * inv). codes holds 4 codes per float4 slot.
+template <int NV>
+__device__ __forceinline__ void quantize_row_e4m3(const float4 (&v)[NV], uint32_t *codes,
+                                                  float *scale_out, int cols4, float *scratch) {
+  float amax = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4)
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w))));
+  }
+  amax = block_max(amax, scratch);
+  const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+  if (threadIdx.x == 0) *scale_out = amax / 448.0f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4)
+      codes[i] = e4m3x2(v[j].x * inv, v[j].y * inv) | (e4m3x2(v[j].z * inv, v[j].w * inv) << 16);
+  }
+}
+
+// RMSNorm of one row (as rmsnorm_row) whose GEMM operand is E4M3 with a
+// per-row scale instead of bf16.
+template <int NV>
+__device__ __forceinline__ void rmsnorm_row_e4m3(const float4 *x, const float4 *w, float4 *out,
+                                                 uint32_t *codes, float *scale_out, int cols4,
+                                                 int cols, float eps, float *scratch) {
+  float4 v[NV];
+  load_row<NV>(v, x, cols4);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  ss = block_sum(ss, scratch);
+  const float scale = 1.0f / sqrtf(ss / (float)cols + eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4) {
+      const float4 g = __ldg(w + i);
+      v[j].x = g.x * (scale * v[j].x);
+      v[j].y = g.y * (scale * v[j].y);
+      v[j].z = g.z * (scale * v[j].z);
+      v[j].w = g.w * (scale * v[j].w);
+      if (out != nullptr) __stcs(out + i, v[j]);
+    }
+  }
+  quantize_row_e4m3<NV>(v, codes, scale_out, cols4, scratch);
+}
+
 }  // namespace rowops
 }  // namespace ce

@@ -66,6 +66,9 @@ struct IterationWork {
   float *normalized;
   uint2 *normalized_bf16;
   int ld_bf16_4;  // bf16 row stride in units of 4 elements
+  uint32_t *normalized_e4m3;  // E4M3 operand (4 codes per word) or nullptr
+  int ld_e4m3_4;              // its row stride in units of 4 codes
+  float *e4m3_scale;          // per-row dequantization scale
   const float *input;
   const float *weight;
   float *softmax;
@@ -105,7 +108,14 @@ iteration_kernel(IterationWork w) {
       return;
     }
   }
-  if (rms_row >= 0) {
+  if (rms_row >= 0 && w.normalized_e4m3 != nullptr) {
+    const size_t off = (size_t)rms_row * cols4;
+    rmsnorm_row_e4m3<NV>(reinterpret_cast<const float4 *>(w.input) + off,
+                         reinterpret_cast<const float4 *>(w.weight),
+                         w.normalized ? reinterpret_cast<float4 *>(w.normalized) + off : nullptr,
+                         w.normalized_e4m3 + (size_t)rms_row * w.ld_e4m3_4, w.e4m3_scale + rms_row,
+                         cols4, w.cols, w.eps, scratch);
+  } else if (rms_row >= 0) {
     const size_t off = (size_t)rms_row * cols4;
     rmsnorm_row<NV>(reinterpret_cast<const float4 *>(w.input) + off,
                     reinterpret_cast<const float4 *>(w.weight),
@@ -271,23 +281,34 @@ int launch_iteration(const IterationWork &w, int nv, int threads, cudaStream_t s
 int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, const float *input,
                    const float *weight, float *softmax, const float *logits, float *product,
                    const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
-                   int cols, int gemv_rows, float eps, cudaStream_t s) {
+                   int cols, int gemv_rows, float eps, cudaStream_t s, uint8_t *normalized_e4m3,
+                   int ld_e4m3, float *e4m3_scale) {
   CE_REQUIRE(cols >= 1, "cols must be >= 1 (got %d)", cols);
   CE_REQUIRE(batch_rms >= 0 && batch_softmax >= 0 && gemv_rows >= 0, "negative row count");
   if (batch_rms > 0) CE_REQUIRE(input && weight && (normalized || normalized_bf16), "rmsnorm needs input, weight and an output");
   if (batch_softmax > 0) CE_REQUIRE(logits && softmax, "softmax needs logits and an output");
   if (gemv_rows > 0) CE_REQUIRE(matrix && gemv_x && product, "gemv needs matrix, x and product");
   if (normalized_bf16) CE_REQUIRE(ld_bf16 >= cols && ld_bf16 % 8 == 0, "bf16 leading dimension must be >= cols and a multiple of 8 (got %d)", ld_bf16);
+  if (normalized_e4m3) {
+    CE_REQUIRE(ld_e4m3 >= cols && ld_e4m3 % 16 == 0, "e4m3 leading dimension must be >= cols and a multiple of 16 (got %d)", ld_e4m3);
+    CE_REQUIRE(e4m3_scale != nullptr && normalized_bf16 == nullptr, "e4m3 operand needs a scale buffer and excludes the bf16 operand");
+    CE_REQUIRE(cols % 4 == 0 && cols / 4 <= 16 * kRowThreads, "the e4m3 operand needs cols %% 4 == 0 and cols <= 32768 (got %d)", cols);
+  }
   int threads = 0;
   const int nv = (cols % 4 == 0) ? pick_nv(cols / 4, &threads) : 0;
   const bool vec = nv > 0 && aligned16(normalized) && aligned16(input) && aligned16(weight) &&
                    aligned16(softmax) && aligned16(logits) && aligned16(matrix) &&
-                   aligned16(gemv_x) && aligned16(normalized_bf16);
+                   aligned16(gemv_x) && aligned16(normalized_bf16) && aligned16(normalized_e4m3);
+  if (normalized_e4m3 != nullptr && !vec)
+    return set_error(CE_ERR_USAGE, std::string("the e4m3 operand needs 16-byte aligned rows"));
   if (vec) {
     IterationWork w;
     w.normalized = normalized;
     w.normalized_bf16 = reinterpret_cast<uint2 *>(normalized_bf16);
     w.ld_bf16_4 = ld_bf16 / 4;
+    w.normalized_e4m3 = reinterpret_cast<uint32_t *>(normalized_e4m3);
+    w.ld_e4m3_4 = ld_e4m3 / 4;
+    w.e4m3_scale = e4m3_scale;
     w.input = input;
     w.weight = weight;
     w.softmax = softmax;
@@ -324,6 +345,10 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
           product, matrix, gemv_x, gemv_rows, cols);
       CE_LAUNCH_CHECK("generic_gemv_kernel");
     }
+  }
+  if (normalized_e4m3 && ld_e4m3 > cols && batch_rms > 0) {
+    CE_CUDA_TRY(cudaMemset2DAsync(normalized_e4m3 + cols, (size_t)ld_e4m3, 0, (size_t)(ld_e4m3 - cols),
+                                  batch_rms, s));
   }
   if (normalized_bf16 && ld_bf16 > cols && batch_rms > 0) {
     pad_bf16_kernel<<<256, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16 *>(normalized_bf16),

@@ -46,7 +46,7 @@ typedef struct CUstream_st *ce_stream_t;
 #define CE_PREC_FP32 0        /* SIMT fp32, sequential k, separate mul+add */
 #define CE_PREC_TF32 1        /* tcgen05 kind::tf32 on fp32 operands */
 #define CE_PREC_BF16 2        /* tcgen05 kind::f16, bf16 operands */
-#define CE_PREC_FP8_E4M3 3    /* tcgen05 kind::f8f6f4, per-row fp32 scales */
+#define CE_PREC_FP8_E4M3 3    /* tcgen05 kind::f8f6f4, E4M3 with per-row fp32 scales */
 #define CE_PREC_MXFP6_E3M2 4  /* reserved: block-scaled E3M2, UE8M0 / 32 */
 #define CE_PREC_NVFP4_E2M1 5  /* reserved: block-scaled E2M1, UE4M3 / 16 */
 
@@ -144,7 +144,8 @@ int ce_gemm_bf16_tile(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev
                       int K, int lda, int ldb, int ldd, int tile_n, ce_stream_t stream);
 
 /* Tensor-core GEMM with a forced kernel: precision CE_PREC_BF16 (a, b bf16
- * bits) or CE_PREC_TF32 (a, b fp32); cta_group 1 = single-CTA kernel
+ * bits), CE_PREC_TF32 (a, b fp32) or CE_PREC_FP8_E4M3 (a, b E4M3 codes, no
+ * scales); cta_group 1 = single-CTA kernel
  * (128 x tile_n tiles), 2 = CTA-pair kernel (256 x tile_n tiles on two SMs,
  * tcgen05 cta_group::2), 0 = automatic; tile_n 128/160/192/224/256 or 0.
  * Test hook in the spirit of the reference's forced tiles and schedules
@@ -170,6 +171,31 @@ int ce_gemm_tf32(float *d_dev, const float *a_dev, const float *b_dev, int M, in
  * alignment; the control path of CE_PREC_FP32. */
 int ce_gemm_fp32(float *d_dev, const float *a_dev, const float *b_dev, int M, int N, int K,
                  int lda, int ldb, int ldd, ce_stream_t stream);
+
+/* E4M3 (OCP FP8, largest 448) quantization of a [rows][cols] fp32 matrix
+ * with one fp32 scale per row: amax = max |x| of the row, inv = 448 / amax,
+ * scale = amax / 448 (IEEE fp32; 0 for an all-zero row), code = E4M3(x * inv),
+ * round to nearest even, saturating. codes [rows][ld], columns past cols are
+ * 0. The FP8-E4M3 per-row mode of the op trio has no reference counterpart
+ * (BASELINE config 3); the conversion follows the spec's rounding rules
+ * (experiments/blackwell/lowprec/spec.json "rounding"). */
+int ce_quantize_e4m3_rows(uint8_t *codes_dev, float *scales_dev, const float *x_dev, int rows,
+                          int cols, int ld, ce_stream_t stream);
+
+/* RMSNorm whose GEMM operand is written as E4M3 codes [rows][ld] with one
+ * scale per row (the quantizer above applied to the normalized row, fused in
+ * the same launch). out_dev (fp32 [rows][cols]) may be NULL. Needs cols % 4
+ * == 0, cols <= 32768, ld % 16 == 0. */
+int ce_rmsnorm_e4m3(float *out_dev, uint8_t *codes_dev, int ld, float *scales_dev,
+                    const float *x_dev, const float *w_dev, int rows, int cols, float eps,
+                    ce_stream_t stream);
+
+/* D[m][n] = a_scale[m] * b_scale[n] * sum_k A[m][k] * B[n][k] with E4M3
+ * operands (tcgen05 kind::f8f6f4, fp32 accumulation). lda, ldb multiples of
+ * 16; a_scale / b_scale may be NULL (scale 1). */
+int ce_gemm_e4m3(float *d_dev, const uint8_t *a_dev, const float *a_scale_dev,
+                 const uint8_t *b_dev, const float *b_scale_dev, int M, int N, int K, int lda,
+                 int ldb, int ldd, ce_stream_t stream);
 
 /* Round-to-nearest-even conversion fp32 -> bf16 of a [rows][cols] matrix
  * into a [rows][ld_out] buffer; columns cols..ld_out-1 are written as 0.

@@ -442,3 +442,60 @@ def read_l2cdump1(path):
     out["normalized"] = out["normalized"].reshape(int(batch), int(size))
     out["softmax"] = out["softmax"].reshape(int(batch), int(size))
     return out
+
+
+_TABLES = {}
+_NCODES = {0: 8, 1: 32, 2: 127, 3: 255, 4: 127}   # magnitude codes per format
+_SIGN = {0: 8, 1: 32, 4: 128}
+
+
+def magnitude_table(fmt):
+    if fmt not in _TABLES:
+        _TABLES[fmt] = np.array([decode(fmt, c) for c in range(_NCODES[fmt])])
+    return _TABLES[fmt]
+
+
+def encode_array(fmt, v):
+    """Vectorised orc_encode (experiments/blackwell/lowprec/reference.cpp:67-82
+    rules): nearest code, ties to the code whose last magnitude bit is 0,
+    saturation at the largest magnitude, +0 for a zero magnitude. fmt 4 is
+    the signed OCP E4M3 of the FP8 mode (UE4M3's magnitudes plus a sign bit)."""
+    v = np.asarray(v, np.float64)
+    t = np.abs(v)
+    tab = magnitude_table(fmt)
+    top = len(tab) - 1
+    below = np.clip(np.searchsorted(tab, t, side="right") - 1, 0, top)
+    nxt = np.minimum(below + 1, top)
+    down = t - tab[below]
+    up = tab[nxt] - t
+    go_up = (below < top) & (tab[below] < t) & ((up < down) | ((up == down) & ((below & 1) == 1)))
+    best = np.where(go_up, below + 1, below).astype(np.uint32)
+    sign = _SIGN.get(fmt, 0)
+    if sign:
+        best = np.where((v < 0) & (best != 0), best | sign, best)
+    return best
+
+
+def decode_array(fmt, codes):
+    codes = np.asarray(codes, np.uint32)
+    sign = _SIGN.get(fmt, 0)
+    mag = codes & (sign - 1) if sign else codes
+    vals = magnitude_table(fmt)[np.minimum(mag, _NCODES[fmt] - 1)]
+    return np.where(sign and (codes & sign) != 0, -vals, vals) if sign else vals
+
+
+def quantize_e4m3_rows(x):
+    """FP8 per-row mode: amax = max|x| of the row, inv = 448 / amax, scale =
+    amax / 448 (fp32; 0 for a zero row), code = E4M3(x * inv) with the
+    rounding above. Returns (codes uint8 [rows][cols], scales float32)."""
+    x = np.asarray(x, np.float32)
+    amax = np.abs(x).max(axis=1)
+    with np.errstate(divide="ignore"):
+        inv = np.where(amax > 0, np.float32(448.0) / amax, np.float32(0.0)).astype(np.float32)
+    scale = (amax / np.float32(448.0)).astype(np.float32)
+    q = (x * inv[:, None]).astype(np.float32)
+    return encode_array(4, q).astype(np.uint8), scale
+
+
+def dequantize_e4m3_rows(codes, scales):
+    return decode_array(4, codes) * np.asarray(scales, np.float64)[:, None]

@@ -273,3 +273,20 @@ def test_decoder_check_matches_reference(O, shape):
         got, report = O.decoder_check(ref, g, nn, ll, pp)
         assert bool(want) == got, (fault, report)
         assert got == (fault == 0), (fault, report)
+
+
+def test_vector_encoder_matches_reference(O):
+    """encode_array agrees with the reference's encoder for every format it
+    defines, and signed E4M3 (fmt 4) takes UE4M3's magnitudes plus a sign."""
+    R = _ref(O)
+    rng = np.random.default_rng(9)
+    probes = np.concatenate([rng.standard_normal(3000) * 40, rng.standard_normal(2000) * 0.05,
+                             [0.0, 448.0, 464.0, 480.0, 1e-9, 6.0, 7.0, 28.0, 30.0]])
+    for fmt in (0, 1, 2):
+        p = probes if fmt < 2 else np.abs(probes)
+        want = np.array([R.ref_encode(fmt, float(v)) for v in p])
+        assert np.array_equal(O.encode_array(fmt, p), want), fmt
+    e4 = O.encode_array(4, probes)
+    ue = np.array([R.ref_encode(2, abs(float(v))) for v in probes])
+    assert np.array_equal(e4 & 127, ue)
+    assert np.array_equal((e4 & 128) != 0, (probes < 0) & (ue != 0))
