@@ -43,6 +43,7 @@ def parse():
                     help="target CPU time of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the decoder tokens/s section")
+    ap.add_argument("--no-precisions", action="store_true", help="skip the per-precision GEMM section")
     ap.add_argument("--profile", action="store_true",
                     help="setup, warm-up and the timed steps only (for ncu captures); no JSON line")
     return ap.parse_args()
@@ -326,6 +327,32 @@ def run_ours(args, rank, world, local_rank):
     min_bytes = 805470208.0  # llama2c_cuda_graph.cu:340-345 at this shape
     del mat
 
+    # ---- GEMM alone per precision (BASELINE config 3 reports TFLOP/s per precision) ----
+    precisions = {}
+    if not args.no_precisions:
+        for pname, pval, peak_key in (("bf16", ce.PREC_BF16, "bf16_tflops"),
+                                      ("fp8_e4m3", ce.PREC_FP8_E4M3, None),
+                                      ("tf32", ce.PREC_TF32, None)):
+            pplan = ce.Plan(BATCH, SIZE, ROWS, pval)
+            dWp = torch.from_numpy(W).to(dev)
+            pplan.set_weights(dWp, stream=s)
+            del dWp
+            with torch.cuda.stream(stream):
+                pplan.rows(norm, None, dx, dw, None, stream=s)
+                for _ in range(3):
+                    pplan.gemm(out, stream=s)
+                g0 = torch.cuda.Event(enable_timing=True)
+                g1 = torch.cuda.Event(enable_timing=True)
+                g0.record(stream)
+                for _ in range(20):
+                    pplan.gemm(out, stream=s)
+                g1.record(stream)
+            torch.cuda.synchronize(dev)
+            ms = g0.elapsed_time(g1) / 20
+            precisions[pname] = {"gemm_ms": ms, "tflops": flops_per_step() / (ms * 1e-3) / 1e12}
+            pplan.close()
+        ce.device_status()
+
     # ---- loom_private decoder, large shape (1024 seq x 4 steps, W 16384, V 8192) ----
     decoder = {}
     if not args.no_decoder:
@@ -345,7 +372,12 @@ def run_ours(args, rank, world, local_rank):
                     d1.record(stream)
                 torch.cuda.synchronize(dev)
                 ms = d0.elapsed_time(d1) / reps
-                res[scope] = {"ms_per_invocation": ms, "tokens_per_s": 4096 / (ms * 1e-3)}
+                t = torch.tensor([ms], device=dev, dtype=torch.float64)
+                if dist is not None:
+                    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+                # every rank decodes its own 1024 sequences (independent batches)
+                res[scope] = {"ms_per_invocation": ms, "tokens_per_s": world * 4096 / (ms * 1e-3)}
             ce.device_status()
             dec.close()
             decoder[prec_name] = res
@@ -388,6 +420,7 @@ def run_ours(args, rank, world, local_rank):
                               "unit": "GB/s"},
             "legacy_iteration": {"ms_per_iter": legacy_ms, "min_bytes_per_iter": min_bytes,
                                  "achieved_gbps": min_bytes / (legacy_ms * 1e-3) / 1e9},
+            "gemm_precisions": precisions,
             "decoder": {"workload": "loom_private llama2c decoder, synthetic model, 1024 sequences x "
                                     "4 greedy steps, width 16384, vocab 8192 (4096 tokens per invocation)",
                         **decoder},

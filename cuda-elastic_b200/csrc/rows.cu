@@ -285,7 +285,9 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    int ld_e4m3, float *e4m3_scale) {
   CE_REQUIRE(cols >= 1, "cols must be >= 1 (got %d)", cols);
   CE_REQUIRE(batch_rms >= 0 && batch_softmax >= 0 && gemv_rows >= 0, "negative row count");
-  if (batch_rms > 0) CE_REQUIRE(input && weight && (normalized || normalized_bf16), "rmsnorm needs input, weight and an output");
+  if (batch_rms > 0)
+    CE_REQUIRE(input && weight && (normalized || normalized_bf16 || normalized_e4m3),
+               "rmsnorm needs input, weight and an output");
   if (batch_softmax > 0) CE_REQUIRE(logits && softmax, "softmax needs logits and an output");
   if (gemv_rows > 0) CE_REQUIRE(matrix && gemv_x && product, "gemv needs matrix, x and product");
   if (normalized_bf16) CE_REQUIRE(ld_bf16 >= cols && ld_bf16 % 8 == 0, "bf16 leading dimension must be >= cols and a multiple of 8 (got %d)", ld_bf16);

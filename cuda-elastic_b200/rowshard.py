@@ -1,0 +1,95 @@
+"""Row-sharded (tensor-parallel) layer of the op trio GEMM and the decoder
+classifier across the GPUs of one node.
+
+The matrix W [rows][size] is split by output rows into contiguous slices,
+one per rank (the first rows % world ranks take one extra row). Each rank
+multiplies the full normalized batch by its slice with its own Plan
+(libce_b200), producing out[:, lo:hi]; an all-gather over the process group
+(NCCL over NVLink between GPUs, gloo in the CPU tests) joins the slices into
+every rank's full [batch][rows] output. This is the layer the north star
+names ("sharded by output rows ... joined by an NCCL all-gather"); the
+reference has no multi-GPU code.
+
+For the decoder classifier, sharded_softmax_argmax joins per-row partial
+softmax statistics instead of full logit rows: each rank reduces its slice to
+(max, sum of exp(l - max), first argmax), ranks exchange those triples, and
+every rank finishes its probabilities and the global first argmax locally
+(ties go to the lowest global index, the first-max rule of the reference's
+sample_argmax, decoder.cu:168-197).
+"""
+import numpy as np
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(n, world, rank):
+    """[lo, hi) of rank's contiguous slice of n rows."""
+    base, extra = divmod(n, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
+def all_bounds(n, world):
+    return [shard_bounds(n, world, r) for r in range(world)]
+
+
+def gather_row_shards(local, rows, group=None, out=None):
+    """All-gather of per-rank column blocks local [batch][hi - lo] into the
+    full out [batch][rows] on every rank. Blocks are padded to the widest
+    slice for the collective and placed at their column offsets."""
+    world = dist.get_world_size(group)
+    bounds = all_bounds(rows, world)
+    width = max(hi - lo for lo, hi in bounds)
+    batch = local.shape[0]
+    padded = local.new_zeros((batch, width))
+    padded[:, :local.shape[1]] = local
+    parts = [torch.empty_like(padded) for _ in range(world)]
+    dist.all_gather(parts, padded.contiguous(), group=group)
+    if out is None:
+        out = local.new_empty((batch, rows))
+    for (lo, hi), part in zip(bounds, parts):
+        out[:, lo:hi] = part[:, :hi - lo]
+    return out
+
+
+def combine_softmax_stats(maxes, sums, argmax):
+    """Joins per-shard softmax statistics of the same rows.
+
+    maxes, sums [world][batch]: each shard's row maximum and sum of
+    exp(l - max) over its slice; argmax [world][batch]: the global index of
+    each shard's first maximum. Returns (global max, global sum, global first
+    argmax) per row."""
+    maxes = np.asarray(maxes, np.float64)
+    m = maxes.max(axis=0)
+    s = (np.asarray(sums, np.float64) * np.exp(maxes - m[None, :])).sum(axis=0)
+    cand = np.where(maxes == m[None, :], np.asarray(argmax, np.int64), np.iinfo(np.int64).max)
+    return m, s, cand.min(axis=0)
+
+
+class RowShardedPlan:
+    """The op trio's rmsnorm -> GEMM with W split by output rows over the
+    ranks of a process group (see the module docstring)."""
+
+    def __init__(self, ce, batch, size, rows, precision, group=None):
+        self.ce = ce
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.rows = rows
+        self.lo, self.hi = shard_bounds(rows, self.world, self.rank)
+        self.local = ce.Plan(batch, size, self.hi - self.lo, precision)
+
+    def set_weights(self, W, stream=None):
+        """W: the full [rows][size] matrix (device) or this rank's slice."""
+        shard = W[self.lo:self.hi] if W.shape[0] == self.rows else W
+        self.local.set_weights(shard.contiguous(), stream=stream)
+
+    def rmsnorm_gemm(self, out, x, norm_w, normalized=None, local_out=None, stream=None):
+        n_local = self.hi - self.lo
+        if local_out is None:
+            local_out = torch.empty((x.shape[0], n_local), device=x.device)
+        self.local.rmsnorm_gemm(local_out, x, norm_w, normalized=normalized, stream=stream)
+        return gather_row_shards(local_out, self.rows, self.group, out=out)
+
+    def close(self):
+        self.local.close()
