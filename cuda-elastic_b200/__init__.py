@@ -81,6 +81,8 @@ _SIGNATURES = {
     "ce_gemm_fp32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_convert_bf16": [_vp, _vp, _i, _i, _i, _vp],
     "ce_quantize_e4m3_rows": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "ce_quantize_mxfp6": [_vp, _vp, _vp, _i, _i, _i, _vp],
+    "ce_quantize_nvfp4": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
     "ce_rmsnorm_e4m3": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _f, _vp],
     "ce_gemm_e4m3": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_rmsnorm_bf16": [_vp, _vp, _i, _vp, _vp, _i, _i, _f, _vp],
@@ -285,6 +287,23 @@ def quantize_e4m3_rows(codes, scales, x, stream=None):
     rows, cols = x.shape
     check(lib().ce_quantize_e4m3_rows(_ptr(codes), _ptr(scales), _ptr(x), rows, cols, codes.shape[1],
                                       _stream(stream)))
+    return codes, scales
+
+
+def quantize_mxfp6(codes, scales, x, stream=None):
+    """codes uint8 [rows][ld] (one per value), scales uint8 [rows][ceil(cols/32)]."""
+    rows, cols = x.shape
+    check(lib().ce_quantize_mxfp6(_ptr(codes), _ptr(scales), _ptr(x), rows, cols, codes.shape[1],
+                                  _stream(stream)))
+    return codes, scales
+
+
+def quantize_nvfp4(codes, scales, tensor_scales, scratch, x, stream=None):
+    """codes uint8 [rows][ld_bytes] (two per byte), scales uint8 [rows][ceil(cols/16)],
+    tensor_scales float32 [2] (encode, decode), scratch int32 [1]."""
+    rows, cols = x.shape
+    check(lib().ce_quantize_nvfp4(_ptr(codes), _ptr(scales), _ptr(tensor_scales), _ptr(scratch),
+                                  _ptr(x), rows, cols, codes.shape[1], _stream(stream)))
     return codes, scales
 
 

@@ -37,6 +37,10 @@ int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K,
               cudaStream_t s, int force_group = 0);
 int quantize_rows_e4m3(uint8_t *codes, float *scales, const float *x, int rows, int cols, int ld,
                        cudaStream_t s);
+int quantize_mxfp6(uint8_t *codes, uint8_t *scales, const float *x, int rows, int cols,
+                   int ld_codes, cudaStream_t s);
+int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
+                   const float *x, int rows, int cols, int ld_bytes, cudaStream_t s);
 int gemm_set_prefetch(int kblocks);
 
 // ---------------------------------------------------------------------------
@@ -313,6 +317,17 @@ int ce_gemm_fp32(float *d, const float *a, const float *b, int M, int N, int K, 
 int ce_quantize_e4m3_rows(uint8_t *codes, float *scales, const float *x, int rows, int cols,
                           int ld, ce_stream_t stream) {
   return quantize_rows_e4m3(codes, scales, x, rows, cols, ld, (cudaStream_t)stream);
+}
+
+int ce_quantize_mxfp6(uint8_t *codes, uint8_t *scales, const float *x, int rows, int cols,
+                      int ld_codes, ce_stream_t stream) {
+  return quantize_mxfp6(codes, scales, x, rows, cols, ld_codes, (cudaStream_t)stream);
+}
+
+int ce_quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *tensor_scales, uint32_t *scratch,
+                      const float *x, int rows, int cols, int ld_bytes, ce_stream_t stream) {
+  return quantize_nvfp4(codes, scales, tensor_scales, scratch, x, rows, cols, ld_bytes,
+                        (cudaStream_t)stream);
 }
 
 int ce_rmsnorm_e4m3(float *out, uint8_t *codes, int ld, float *scales, const float *x,

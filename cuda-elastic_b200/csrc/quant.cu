@@ -40,3 +40,161 @@ int quantize_rows_e4m3(uint8_t *codes, float *scales, const float *x, int rows, 
 }
 
 }  // namespace ce
+
+// ---------------------------------------------------------------------------
+// MXFP6 E3M2 and NVFP4 E2M1 (experiments/blackwell/lowprec/spec.json
+// "mxfp6", "nvfp4"; host restatement reference.cpp:105-150). Codes must
+// equal the spec's host quantizer bit for bit, so every step keeps the
+// spec's order: the hardware conversions round to nearest even and saturate
+// (E3M2 to 28, E2M1 to 6, E4M3 to 448), and a zero result is written as +0.
+
+namespace ce {
+namespace {
+
+__device__ __forceinline__ uint32_t e3m2x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e3m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  uint32_t c = r;
+  if ((c & 0xFFu) == 0x20u) c &= ~0xFFu;        // -0 -> +0
+  if ((c & 0xFF00u) == 0x2000u) c &= ~0xFF00u;
+  return c;
+}
+
+// Two fp32 values to two E2M1 codes in one byte (lo in the low nibble).
+__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
+  uint16_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}"
+      : "=h"(r) : "f"(hi), "f"(lo));
+  uint32_t c = r & 0xFFu;
+  if ((c & 0x0Fu) == 0x08u) c &= ~0x0Fu;         // -0 -> +0
+  if ((c & 0xF0u) == 0x80u) c &= ~0xF0u;
+  return c;
+}
+
+__device__ __forceinline__ float ue4m3_value(uint32_t code) {
+  const int e = (code >> 3) & 15, m = code & 7;
+  return e == 0 ? ldexpf((float)m / 8.0f, -6) : ldexpf(1.0f + (float)m / 8.0f, e - 7);
+}
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// One warp per 32-value block: codes one byte per value (6 used),
+// scales one UE8M0 byte per block, row-major [rows][nblocks].
+__global__ void quantize_mxfp6_kernel(uint8_t *codes, uint8_t *scales, const float *x, int rows,
+                                      int cols, int ld_codes, int nblocks) {
+  const int lane = threadIdx.x & 31;
+  const long long warp = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long total = (long long)rows * nblocks;
+  if (warp >= total) return;
+  const int row = (int)(warp / nblocks), blk = (int)(warp % nblocks);
+  const int col = blk * 32 + lane;
+  const float v = col < cols ? x[(size_t)row * cols + col] : 0.f;
+  const float amax = warp_max_f(fabsf(v));
+  int shared = 0;
+  uint32_t scale_code = 0;
+  if (amax != 0.f) {
+    shared = ilogbf(amax) - 4;   // floor(log2 amax) - (largest E3M2 exponent)
+    shared = max(-127, min(127, shared));
+    scale_code = (uint32_t)(shared + 127);
+  }
+  // v * 2^-shared is exact for every value that can round to a nonzero code
+  const float scaled = amax != 0.f ? v * ldexpf(1.0f, -shared) : 0.f;
+  // both lanes of a pair convert (even, odd) together and keep their byte
+  const float other = __shfl_xor_sync(0xffffffffu, scaled, 1);
+  const uint32_t pair = (lane & 1) ? e3m2x2(other, scaled) : e3m2x2(scaled, other);
+  const uint32_t mine = (lane & 1) ? (pair >> 8) & 0xFFu : pair & 0xFFu;
+  if (col < ld_codes) codes[(size_t)row * ld_codes + col] = col < cols ? (uint8_t)mine : (uint8_t)0;
+  if (lane == 0) scales[(size_t)row * nblocks + blk] = (uint8_t)scale_code;
+}
+
+// Tensor amax of |x| (x >= 0 compares as its bit pattern).
+__global__ void amax_kernel(unsigned int *amax_bits, const float *x, size_t n) {
+  float m = 0.f;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(x[i]));
+  m = warp_max_f(m);
+  if ((threadIdx.x & 31) == 0) atomicMax(amax_bits, __float_as_uint(m));
+}
+
+// NVFP4: encode scale s = 2688 / a_t (1 when a_t = 0), decode scale 1 / s.
+__global__ void nvfp4_tensor_scale_kernel(float *encode_decode, const unsigned int *amax_bits) {
+  const float a = __uint_as_float(*amax_bits);
+  const float s = a > 0.f ? 2688.0f / a : 1.0f;
+  encode_decode[0] = s;
+  encode_decode[1] = 1.0f / s;
+}
+
+// One 16-value block per half warp: codes packed two per byte (even index in
+// the low nibble) [rows][ld_bytes], scales one UE4M3 byte per block.
+__global__ void quantize_nvfp4_kernel(uint8_t *codes, uint8_t *scales, const float *x,
+                                      const float *encode_decode, int rows, int cols,
+                                      int ld_bytes, int nblocks) {
+  const int lane = threadIdx.x & 31;
+  const long long half = ((long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 2 + (lane >> 4);
+  const long long total = (long long)rows * nblocks;
+  const bool live = half < total;
+  const int row = live ? (int)(half / nblocks) : 0, blk = live ? (int)(half % nblocks) : 0;
+  const int i = lane & 15, col = blk * 16 + i;
+  const float v = (live && col < cols) ? x[(size_t)row * cols + col] : 0.f;
+  float amax = fabsf(v);
+#pragma unroll
+  for (int o = 8; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float s = encode_decode[0];
+  float target = amax / 6.0f;
+  target = target * s;
+  const uint32_t sc = e4m3x2(target, 0.f) & 0x7Fu;
+  const float f = ue4m3_value(sc);
+  float r = 0.f;
+  if (sc != 0) {
+    r = v * s;
+    r = r / f;
+  }
+  const float other = __shfl_xor_sync(0xffffffffu, r, 1);
+  if (live && (i & 1) == 0) {
+    const uint32_t byte = sc != 0 ? e2m1x2(r, other) : 0u;
+    if (col / 2 < ld_bytes) codes[(size_t)row * ld_bytes + col / 2] = col < cols ? (uint8_t)byte : (uint8_t)0;
+  }
+  if (live && i == 0) scales[(size_t)row * nblocks + blk] = (uint8_t)sc;
+}
+
+}  // namespace
+
+int quantize_mxfp6(uint8_t *codes, uint8_t *scales, const float *x, int rows, int cols,
+                   int ld_codes, cudaStream_t s) {
+  CE_REQUIRE(codes && scales && x, "null argument");
+  CE_REQUIRE(rows >= 1 && cols >= 1 && ld_codes >= cols, "bad mxfp6 shape %dx%d ld %d", rows, cols, ld_codes);
+  const int nblocks = (cols + 31) / 32;
+  const long long warps = (long long)rows * nblocks;
+  quantize_mxfp6_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>(codes, scales, x, rows, cols,
+                                                                    ld_codes, nblocks);
+  CE_LAUNCH_CHECK("quantize_mxfp6_kernel");
+  return CE_OK;
+}
+
+// encode_decode (device, 2 floats) receives the tensor scales; amax_bits
+// (device, 1 word) is the reduction scratch.
+int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
+                   const float *x, int rows, int cols, int ld_bytes, cudaStream_t s) {
+  CE_REQUIRE(codes && scales && encode_decode && amax_bits && x, "null argument");
+  CE_REQUIRE(rows >= 1 && cols >= 1 && ld_bytes * 2 >= cols, "bad nvfp4 shape %dx%d ld %d bytes", rows, cols, ld_bytes);
+  CE_CUDA_TRY(cudaMemsetAsync(amax_bits, 0, sizeof(unsigned int), s));
+  const size_t n = (size_t)rows * cols;
+  int blocks = (int)((n + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  amax_kernel<<<blocks, 256, 0, s>>>(amax_bits, x, n);
+  CE_LAUNCH_CHECK("amax_kernel");
+  nvfp4_tensor_scale_kernel<<<1, 1, 0, s>>>(encode_decode, amax_bits);
+  CE_LAUNCH_CHECK("nvfp4_tensor_scale_kernel");
+  const int nblocks = (cols + 15) / 16;
+  const long long halves = (long long)rows * nblocks;
+  quantize_nvfp4_kernel<<<(unsigned)((halves + 15) / 16), 256, 0, s>>>(
+      codes, scales, x, encode_decode, rows, cols, ld_bytes, nblocks);
+  CE_LAUNCH_CHECK("quantize_nvfp4_kernel");
+  return CE_OK;
+}
+
+}  // namespace ce

@@ -182,6 +182,27 @@ int ce_gemm_fp32(float *d_dev, const float *a_dev, const float *b_dev, int M, in
 int ce_quantize_e4m3_rows(uint8_t *codes_dev, float *scales_dev, const float *x_dev, int rows,
                           int cols, int ld, ce_stream_t stream);
 
+/* MXFP6 E3M2 quantization with one UE8M0 scale per 32 values along each
+ * row (experiments/blackwell/lowprec/decoder_lowprec.cu:243-286,
+ * quantize_mxfp6_kernel; rules of spec.json "mxfp6"): codes one byte per
+ * value (6 bits used) [rows][ld_codes], columns past cols 0; scales
+ * [rows][ceil(cols / 32)] row-major. Bit-exact with the spec's host
+ * quantizer (reference.cpp:105-122). */
+int ce_quantize_mxfp6(uint8_t *codes_dev, uint8_t *scales_dev, const float *x_dev, int rows,
+                      int cols, int ld_codes, ce_stream_t stream);
+
+/* NVFP4 E2M1 quantization (decoder_lowprec.cu:202-219, 294-340,
+ * tensor_amax_kernel and quantize_nvfp4_kernel; spec.json "nvfp4"): the
+ * tensor amax of x gives the encode scale s = 2688 / amax (1 when 0) and
+ * decode scale 1 / s, written to tensor_scales_dev[0..1]; each 16-value
+ * block gets the UE4M3 scale code of (amax_block / 6) * s and codes
+ * E2M1((v * s) / f), two per byte, even index in the low nibble
+ * [rows][ld_bytes]. scratch_dev is one device word used for the amax
+ * reduction. Bit-exact with reference.cpp:124-150. */
+int ce_quantize_nvfp4(uint8_t *codes_dev, uint8_t *scales_dev, float *tensor_scales_dev,
+                      uint32_t *scratch_dev, const float *x_dev, int rows, int cols, int ld_bytes,
+                      ce_stream_t stream);
+
 /* RMSNorm whose GEMM operand is written as E4M3 codes [rows][ld] with one
  * scale per row (the quantizer above applied to the normalized row, fused in
  * the same launch). out_dev (fp32 [rows][cols]) may be NULL. Needs cols % 4

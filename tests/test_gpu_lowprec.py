@@ -120,3 +120,61 @@ def test_plan_fp8_trio(ce, O, dev, shape):
     ref32, _ = O.gemm_ref(O.rmsnorm_ref(x[rows], w), W)
     assert O.rel_l2(ho, ref32) <= 0.08     # quantization error of both operands (e4m3)
     plan.close()
+
+
+def _crafted_rows(O, width, rows, seed):
+    x = O.normals(seed, 1, rows * width).reshape(rows, width).copy()
+    x[1, :32] = 0.0                               # zero block
+    x[2, 32:64] = 28.0 * 2.0 ** -3                 # exact largest-code block
+    x[3, :16] = np.float32(1e-30)                  # tiny block
+    x[4, 64:96] = np.linspace(-40, 40, 32)         # saturation
+    x[5, :] *= 1e-20
+    x[6, 96:128] = (np.arange(32) % 4) * 0.125     # ties
+    return np.ascontiguousarray(x.astype(np.float32))
+
+
+@pytest.mark.parametrize("shape", [(130, 1024), (7, 1000), (64, 16384)])
+def test_mxfp6_quantizer_bit_exact(ce, O, dev, shape):
+    rows, width = shape
+    x = _crafted_rows(O, width, rows, 2)
+    nb = (width + 31) // 32
+    codes = torch.full((rows, width), 0x55, dtype=torch.uint8, device=dev)
+    scales = torch.full((rows, nb), 0x55, dtype=torch.uint8, device=dev)
+    ce.quantize_mxfp6(codes, scales, torch.from_numpy(x).to(dev))
+    torch.cuda.synchronize()
+    L = O.orc()
+    wc = np.empty((rows, nb * 32), np.uint8)
+    ws = np.empty((rows, nb), np.uint8)
+    for r in range(rows):
+        row = np.zeros(nb * 32, np.float32)
+        row[:width] = x[r]
+        L.orc_quantize_mxfp6(row, width, wc[r], ws[r])
+    assert np.array_equal(codes.cpu().numpy(), wc[:, :width])
+    assert np.array_equal(scales.cpu().numpy(), ws)
+
+
+@pytest.mark.parametrize("shape", [(130, 1024), (7, 1000), (64, 16384)])
+def test_nvfp4_quantizer_bit_exact(ce, O, dev, shape):
+    rows, width = shape
+    x = _crafted_rows(O, width, rows, 3)
+    nb = (width + 15) // 16
+    ldb = (width + 1) // 2
+    codes = torch.full((rows, ldb), 0x55, dtype=torch.uint8, device=dev)
+    scales = torch.full((rows, nb), 0x55, dtype=torch.uint8, device=dev)
+    ts = torch.full((2,), float("nan"), device=dev)
+    scratch = torch.zeros(1, dtype=torch.int32, device=dev)
+    ce.quantize_nvfp4(codes, scales, ts, scratch, torch.from_numpy(x).to(dev))
+    torch.cuda.synchronize()
+    L = O.orc()
+    s = L.orc_nvfp4_encode_scale(float(np.abs(x).max()))
+    assert ts.cpu().numpy()[0] == np.float32(s)
+    assert ts.cpu().numpy()[1] == np.float32(1.0) / np.float32(s)
+    wc = np.empty((rows, nb * 16), np.uint8)
+    ws = np.empty((rows, nb), np.uint8)
+    for r in range(rows):
+        row = np.zeros(nb * 16, np.float32)
+        row[:width] = x[r]
+        L.orc_quantize_nvfp4(row, width, s, wc[r], ws[r])
+    packed = (wc[:, 0::2] | (wc[:, 1::2] << 4)).astype(np.uint8)[:, :ldb]
+    assert np.array_equal(scales.cpu().numpy(), ws)
+    assert np.array_equal(codes.cpu().numpy(), packed)
