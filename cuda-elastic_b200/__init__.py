@@ -83,6 +83,11 @@ _SIGNATURES = {
     "ce_quantize_e4m3_rows": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ce_quantize_mxfp6": [_vp, _vp, _vp, _i, _i, _i, _vp],
     "ce_quantize_nvfp4": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _vp],
+    "ce_sf_atom_bytes": [_i, _i, _i, _i, ctypes.POINTER(ctypes.c_size_t)],
+    "ce_sf_to_atoms": [_i, _vp, _vp, _i, _i, _i, _vp],
+    "ce_pack_mxfp6": [_vp, _vp, _i, _i, _i, _i, _vp],
+    "ce_gemm_mxfp6": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
+    "ce_gemm_nvfp4": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_rmsnorm_e4m3": [_vp, _vp, _i, _vp, _vp, _vp, _i, _i, _f, _vp],
     "ce_gemm_e4m3": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_rmsnorm_bf16": [_vp, _vp, _i, _vp, _vp, _i, _i, _f, _vp],
@@ -305,6 +310,46 @@ def quantize_nvfp4(codes, scales, tensor_scales, scratch, x, stream=None):
     check(lib().ce_quantize_nvfp4(_ptr(codes), _ptr(scales), _ptr(tensor_scales), _ptr(scratch),
                                   _ptr(x), rows, cols, codes.shape[1], _stream(stream)))
     return codes, scales
+
+
+BS_TILE_N = 224
+
+
+def sf_atoms(fmt, scales, rows, K, group_rows, stream=None):
+    """Scale atoms (uint8 device tensor) of row-major scales [rows][K/vec]."""
+    import torch
+    n = ctypes.c_size_t()
+    check(lib().ce_sf_atom_bytes(fmt, rows, K, group_rows, ctypes.byref(n)))
+    atoms = torch.empty(n.value, dtype=torch.uint8, device=scales.device)
+    check(lib().ce_sf_to_atoms(fmt, _ptr(atoms), _ptr(scales), rows, K, group_rows, _stream(stream)))
+    return atoms
+
+
+def pack_mxfp6(codes, stream=None):
+    """GEMM operand layout of E3M2 codes [rows][cols] (uint8 device tensor)."""
+    import torch
+    rows, cols = codes.shape
+    ld = ((cols + 15) // 16) * 16
+    op = torch.empty((rows, ld), dtype=torch.uint8, device=codes.device)
+    check(lib().ce_pack_mxfp6(_ptr(op), _ptr(codes), rows, cols, cols, ld, _stream(stream)))
+    return op
+
+
+def gemm_mxfp6(d, a, a_atoms, b, b_atoms, k=None, stream=None):
+    M, lda = a.shape
+    N, ldb = b.shape
+    K = lda if k is None else k
+    check(lib().ce_gemm_mxfp6(_ptr(d), _ptr(a), _ptr(a_atoms), _ptr(b), _ptr(b_atoms), M, N, K, lda,
+                              ldb, d.shape[1], _stream(stream)))
+    return d
+
+
+def gemm_nvfp4(d, a, a_atoms, a_scales, b, b_atoms, b_scales, k, stream=None):
+    M, lda = a.shape
+    N, ldb = b.shape
+    check(lib().ce_gemm_nvfp4(_ptr(d), _ptr(a), _ptr(a_atoms), _ptr(a_scales), _ptr(b), _ptr(b_atoms),
+                              _ptr(b_scales), M, N, k, lda, ldb, d.shape[1], _stream(stream)))
+    return d
 
 
 def rmsnorm_e4m3(out, codes, scales, x, w, eps=RMS_EPS, stream=None):

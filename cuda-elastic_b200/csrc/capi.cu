@@ -32,6 +32,18 @@ int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int
 int gemm_simt_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda,
                    int ldb, int ldd, cudaStream_t s);
 int gemm_status();
+int gemm_bs_status();
+int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
+               int ld_operand, cudaStream_t s);
+int sf_katoms(int fmt, int K);
+int sf_row_atoms(int rows, int group_rows);
+int sf_to_atoms(uint8_t *atoms, const uint8_t *scales, int rows, int nsf, int katoms,
+                int group_rows, cudaStream_t s);
+int gemm_mxfp6(float *d, const uint8_t *a, const uint8_t *sfa, const uint8_t *b,
+               const uint8_t *sfb, int M, int N, int K, int lda, int ldb, int ldd, cudaStream_t s);
+int gemm_nvfp4(float *d, const uint8_t *a, const uint8_t *sfa, const float *alpha_a,
+               const uint8_t *b, const uint8_t *sfb, const float *alpha_b, int M, int N, int K,
+               int lda_bytes, int ldb_bytes, int ldd, cudaStream_t s);
 int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
               cudaStream_t s, int force_group = 0);
@@ -170,7 +182,11 @@ int ce_device_info(int *sms, int *sm100) {
 
 // Synchronizes the device and returns CE_ERR_TIMEOUT if a bounded device
 // wait of a tensor-core kernel gave up since the last call (clearing it).
-int ce_device_status(void) { return gemm_status(); }
+int ce_device_status(void) {
+  const int a = gemm_status();
+  const int b = gemm_bs_status();
+  return a != CE_OK ? a : b;
+}
 
 int ce_fill_llama2c_host(int random, uint64_t seed, int batch, int size, int rows, float *input,
                          float *probabilities, float *weight, float *matrix) {
@@ -328,6 +344,43 @@ int ce_quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *tensor_scales, uin
                       const float *x, int rows, int cols, int ld_bytes, ce_stream_t stream) {
   return quantize_nvfp4(codes, scales, tensor_scales, scratch, x, rows, cols, ld_bytes,
                         (cudaStream_t)stream);
+}
+
+// Bytes of the scale-atom buffer: format 0 = MXFP6 (32 values per scale),
+// 1 = NVFP4 (16); rows grouped by group_rows (128 for the A operand,
+// CE_BS_TILE_N for the B operand).
+int ce_sf_atom_bytes(int format, int rows, int K, int group_rows, size_t *bytes) {
+  CE_REQUIRE(format == 0 || format == 1, "format must be 0 (MXFP6) or 1 (NVFP4)");
+  CE_REQUIRE(rows >= 1 && K >= 1 && group_rows >= 1 && bytes, "bad arguments");
+  *bytes = (size_t)sf_row_atoms(rows, group_rows) * sf_katoms(format, K) * 512;
+  return CE_OK;
+}
+
+int ce_sf_to_atoms(int format, uint8_t *atoms, const uint8_t *scales, int rows, int K,
+                   int group_rows, ce_stream_t stream) {
+  CE_REQUIRE(format == 0 || format == 1, "format must be 0 (MXFP6) or 1 (NVFP4)");
+  const int vec = format == 0 ? 32 : 16;
+  return sf_to_atoms(atoms, scales, rows, (K + vec - 1) / vec, sf_katoms(format, K), group_rows,
+                     (cudaStream_t)stream);
+}
+
+int ce_pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
+                  int ld_operand, ce_stream_t stream) {
+  return pack_mxfp6(operand, codes, rows, cols, ld_codes, ld_operand, (cudaStream_t)stream);
+}
+
+int ce_gemm_mxfp6(float *d, const uint8_t *a, const uint8_t *a_sf, const uint8_t *b,
+                  const uint8_t *b_sf, int M, int N, int K, int lda, int ldb, int ldd,
+                  ce_stream_t stream) {
+  return gemm_mxfp6(d, a, a_sf, b, b_sf, M, N, K, lda, ldb, ldd, (cudaStream_t)stream);
+}
+
+int ce_gemm_nvfp4(float *d, const uint8_t *a, const uint8_t *a_sf, const float *a_scales,
+                  const uint8_t *b, const uint8_t *b_sf, const float *b_scales, int M, int N, int K,
+                  int lda_bytes, int ldb_bytes, int ldd, ce_stream_t stream) {
+  return gemm_nvfp4(d, a, a_sf, a_scales ? a_scales + 1 : nullptr, b, b_sf,
+                    b_scales ? b_scales + 1 : nullptr, M, N, K, lda_bytes, ldb_bytes, ldd,
+                    (cudaStream_t)stream);
 }
 
 int ce_rmsnorm_e4m3(float *out, uint8_t *codes, int ld, float *scales, const float *x,

@@ -161,7 +161,87 @@ __global__ void quantize_nvfp4_kernel(uint8_t *codes, uint8_t *scales, const flo
   if (live && i == 0) scales[(size_t)row * nblocks + blk] = (uint8_t)sc;
 }
 
+// Row-major scales [rows][nsf] -> 512-byte atoms (see gemm_bs.cu): rows are
+// taken in groups of group_rows, each group padded to whole 128-row atom
+// rows; scale columns padded to katoms * 4. Padding bytes are 0.
+__global__ void sf_to_atoms_kernel(uint8_t *atoms, const uint8_t *scales, int rows, int nsf,
+                                   int katoms, int group_rows, size_t total) {
+  const int atoms_per_group = (group_rows + 127) / 128;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t atom = i / 512;
+    const int o = (int)(i % 512);
+    const int kb = (int)(atom % katoms);
+    const int ra = (int)(atom / katoms);
+    const int group = ra / atoms_per_group, sub = ra % atoms_per_group;
+    const int m = sub * 128 + ((o % 16) / 4) * 32 + o / 16;  // row within the group
+    const int c = kb * 4 + (o % 4);
+    const int row = group * group_rows + m;
+    atoms[i] = (m < group_rows && row < rows && c < nsf) ? scales[(size_t)row * nsf + c] : (uint8_t)0;
+  }
+}
+
+// MXFP6 GEMM operand: each group of 16 E3M2 codes (one byte each, low 6
+// bits) becomes 12 bytes of little-endian 6-bit fields (value i at bits
+// 6i..6i+5, the spec's packed order) followed by 4 zero bytes, so 16 values
+// occupy 16 bytes and a 32-value MMA step is 16-byte aligned in shared
+// memory, where the tensor core reads packed 6-bit fields.
+__global__ void pack_mxfp6_kernel(uint8_t *operand, const uint8_t *codes, int rows, int cols,
+                                  int ld_codes, int ld_operand, size_t groups_total) {
+  const int groups = ld_operand / 16;
+  for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < groups_total;
+       g += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(g / groups), grp = (int)(g % groups);
+    unsigned long long lo = 0, hi = 0;  // bits 0-63, 64-127 of the group
+    for (int i = 0; i < 16; ++i) {
+      const int col = grp * 16 + i;
+      const unsigned long long v = col < cols ? (codes[(size_t)row * ld_codes + col] & 63u) : 0u;
+      const int bit = 6 * i;
+      if (bit < 64) {
+        lo |= v << bit;
+        if (bit > 58) hi |= v >> (64 - bit);
+      } else {
+        hi |= v << (bit - 64);
+      }
+    }
+    uint4 out;
+    out.x = (uint32_t)lo;
+    out.y = (uint32_t)(lo >> 32);
+    out.z = (uint32_t)hi;
+    out.w = 0u;
+    *reinterpret_cast<uint4 *>(operand + (size_t)row * ld_operand + (size_t)grp * 16) = out;
+  }
+}
+
 }  // namespace
+
+int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
+               int ld_operand, cudaStream_t s) {
+  CE_REQUIRE(operand && codes, "null argument");
+  CE_REQUIRE(rows >= 1 && cols >= 1 && ld_codes >= cols && ld_operand >= ((cols + 15) / 16) * 16 &&
+                 ld_operand % 16 == 0,
+             "bad mxfp6 operand shape %dx%d ld %d/%d", rows, cols, ld_codes, ld_operand);
+  CE_REQUIRE((reinterpret_cast<uintptr_t>(operand) & 15u) == 0, "operand must be 16-byte aligned");
+  const size_t total = (size_t)rows * (ld_operand / 16);
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  pack_mxfp6_kernel<<<blocks, 256, 0, s>>>(operand, codes, rows, cols, ld_codes, ld_operand, total);
+  CE_LAUNCH_CHECK("pack_mxfp6_kernel");
+  return CE_OK;
+}
+
+int sf_to_atoms(uint8_t *atoms, const uint8_t *scales, int rows, int nsf, int katoms,
+                int group_rows, cudaStream_t s) {
+  CE_REQUIRE(atoms && scales, "null argument");
+  CE_REQUIRE(rows >= 1 && nsf >= 1 && katoms * 4 >= nsf && group_rows >= 1, "bad scale layout");
+  const int groups = (rows + group_rows - 1) / group_rows;
+  const size_t total = (size_t)groups * ((group_rows + 127) / 128) * katoms * 512;
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  sf_to_atoms_kernel<<<blocks, 256, 0, s>>>(atoms, scales, rows, nsf, katoms, group_rows, total);
+  CE_LAUNCH_CHECK("sf_to_atoms_kernel");
+  return CE_OK;
+}
 
 int quantize_mxfp6(uint8_t *codes, uint8_t *scales, const float *x, int rows, int cols,
                    int ld_codes, cudaStream_t s) {

@@ -47,8 +47,12 @@ typedef struct CUstream_st *ce_stream_t;
 #define CE_PREC_TF32 1        /* tcgen05 kind::tf32 on fp32 operands */
 #define CE_PREC_BF16 2        /* tcgen05 kind::f16, bf16 operands */
 #define CE_PREC_FP8_E4M3 3    /* tcgen05 kind::f8f6f4, E4M3 with per-row fp32 scales */
-#define CE_PREC_MXFP6_E3M2 4  /* reserved: block-scaled E3M2, UE8M0 / 32 */
-#define CE_PREC_NVFP4_E2M1 5  /* reserved: block-scaled E2M1, UE4M3 / 16 */
+#define CE_PREC_MXFP6_E3M2 4  /* tcgen05 kind::mxf8f6f4 block-scaled E3M2, UE8M0 / 32 */
+#define CE_PREC_NVFP4_E2M1 5  /* tcgen05 kind::mxf4nvf4 block-scaled E2M1, UE4M3 / 16 */
+
+/* Output-tile width of the block-scaled GEMMs; the B operand's scale atoms
+ * are grouped by this many rows. */
+#define CE_BS_TILE_N 224
 
 /* ------------------------------------------------------------------ */
 /* Library                                                             */
@@ -202,6 +206,46 @@ int ce_quantize_mxfp6(uint8_t *codes_dev, uint8_t *scales_dev, const float *x_de
 int ce_quantize_nvfp4(uint8_t *codes_dev, uint8_t *scales_dev, float *tensor_scales_dev,
                       uint32_t *scratch_dev, const float *x_dev, int rows, int cols, int ld_bytes,
                       ce_stream_t stream);
+
+/* Block-scaled GEMM operands keep their scales in 512-byte atoms of 128
+ * rows x 4 scale columns (byte (r % 32) * 16 + (r / 32) * 4 + c), atoms
+ * along K fastest, rows taken in groups of group_rows (128 for A, and
+ * CE_BS_TILE_N for B so that every output tile's scales start on an atom
+ * boundary), each group padded to whole atoms; padding bytes 0. This
+ * replaces the reference's CUTLASS Sm1xxBlkScaledConfig layout
+ * (experiments/blackwell/lowprec/spec.json "layout.scale_factors") with one
+ * shaped for this library's tiles. format: 0 = MXFP6 (one scale per 32
+ * values), 1 = NVFP4 (per 16). */
+int ce_sf_atom_bytes(int format, int rows, int K, int group_rows, size_t *bytes);
+int ce_sf_to_atoms(int format, uint8_t *atoms_dev, const uint8_t *scales_dev, int rows, int K,
+                   int group_rows, ce_stream_t stream);
+
+/* MXFP6 GEMM operand layout: every 16 E3M2 codes of a row (one byte each,
+ * as ce_quantize_mxfp6 writes them) become 12 bytes of little-endian 6-bit
+ * fields (value i at bits 6i..6i+5, the spec's packed bit order) followed by
+ * 4 zero bytes: the form in which the tensor core reads E3M2 from shared
+ * memory. ld_operand is a multiple of 16 bytes covering roundup(cols, 16). */
+int ce_pack_mxfp6(uint8_t *operand_dev, const uint8_t *codes_dev, int rows, int cols, int ld_codes,
+                  int ld_operand, ce_stream_t stream);
+
+/* MXFP6 GEMM (decoder_lowprec.cu:93-110): D[m][n] = sum_k a[m][k] b[n][k]
+ * with a, b E3M2 operands in the ce_pack_mxfp6 layout scaled per
+ * 32 values by their UE8M0 scales (atoms: A grouped by 128 rows, B by
+ * CE_BS_TILE_N), fp32 accumulation and output. K % 128 == 0; lda, ldb
+ * multiples of 16. */
+int ce_gemm_mxfp6(float *d_dev, const uint8_t *a_dev, const uint8_t *a_sf_dev,
+                  const uint8_t *b_dev, const uint8_t *b_sf_dev, int M, int N, int K, int lda,
+                  int ldb, int ldd, ce_stream_t stream);
+
+/* NVFP4 GEMM (decoder_lowprec.cu:111-127): E2M1 codes two per byte
+ * (ce_quantize_nvfp4 layout), UE4M3 scales per 16 values (atoms as above),
+ * times alpha = a_scales[1] * b_scales[1] (the tensors' decode scales,
+ * device memory, as written by ce_quantize_nvfp4; NULL = 1). K % 128 == 0;
+ * lda_bytes, ldb_bytes multiples of 16. */
+int ce_gemm_nvfp4(float *d_dev, const uint8_t *a_dev, const uint8_t *a_sf_dev,
+                  const float *a_scales_dev, const uint8_t *b_dev, const uint8_t *b_sf_dev,
+                  const float *b_scales_dev, int M, int N, int K, int lda_bytes, int ldb_bytes,
+                  int ldd, ce_stream_t stream);
 
 /* RMSNorm whose GEMM operand is written as E4M3 codes [rows][ld] with one
  * scale per row (the quantizer above applied to the normalized row, fused in

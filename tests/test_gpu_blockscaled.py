@@ -1,0 +1,111 @@
+"""GPU parity of the block-scaled GEMMs (tcgen05 kind::mxf8f6f4 and
+kind::mxf4nvf4 with block scales applied by the tensor core) against the
+double GEMM of the dequantized operands: the implementation-check bound of
+experiments/blackwell/lowprec/decoder_lowprec.cu:981-1052 (gamma_K sum|a b|
++ 2^-23 |expected|) and <= 1e-2 relative L2 (north star). Operands come from
+the device quantizers, which are bit-exact against the reference's host
+quantizer (tests/test_gpu_lowprec.py)."""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _operands(O, M, N, K, seed):
+    A = O.normals(seed, 1, M * K).reshape(M, K)
+    B = O.normals(seed, 2, N * K, float(np.float32(1.0 / np.sqrt(K)))).reshape(N, K)
+    return np.ascontiguousarray(A), np.ascontiguousarray(B)
+
+
+def _check(O, d, a, b, alpha=1.0):
+    ref, mag = O.gemm_ref(a, b)
+    ref *= alpha
+    mag *= abs(alpha)
+    k = a.shape[1]
+    bound = O.gamma_worst(k) * mag + 2.0 ** -22 * np.abs(ref) + 1e-30
+    err = np.abs(d.astype(np.float64) - ref)
+    assert np.all(err <= bound), float((err / bound).max())
+    assert O.rel_l2(d, ref) <= 1e-2
+
+
+def test_pack_mxfp6_layout(ce, O, dev):
+    """16 codes -> 12 bytes of 6-bit fields (value i at bits 6i..6i+5) + 4
+    zero bytes; ragged last group zero-filled."""
+    rng = np.random.default_rng(3)
+    rows, cols = 5, 40
+    codes = rng.integers(0, 64, (rows, cols)).astype(np.uint8)
+    op = ce.pack_mxfp6(torch.from_numpy(codes).to(dev)).cpu().numpy()
+    assert op.shape == (rows, 48)
+    for r in range(rows):
+        for g in range(3):
+            grp = np.zeros(16, np.int64)
+            n = min(16, cols - 16 * g)
+            grp[:n] = codes[r, 16 * g:16 * g + n]
+            bits = sum(int(v) << (6 * i) for i, v in enumerate(grp))
+            want = bits.to_bytes(12, "little") + bytes(4)
+            assert bytes(op[r, 16 * g:16 * g + 16]) == want
+
+
+def _mx_dequant(O, codes, scales):
+    vals = O.decode_array(1, codes)
+    return vals * np.exp2(np.repeat(scales.astype(np.float64) - 127.0, 32, axis=1)[:, :codes.shape[1]])
+
+
+def _nv_dequant(O, packed, scales, K):
+    lo = packed & 0x0F
+    hi = packed >> 4
+    codes = np.empty((packed.shape[0], packed.shape[1] * 2), np.uint8)
+    codes[:, 0::2], codes[:, 1::2] = lo, hi
+    vals = O.decode_array(0, codes[:, :K])
+    return vals * np.repeat(O.decode_array(2, scales), 16, axis=1)[:, :K]
+
+
+SHAPES = [(128, 224, 128), (300, 1000, 1024), (130, 450, 256), (1, 8, 384)]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_gemm_mxfp6(ce, O, dev, shape):
+    M, N, K = shape
+    A, B = _operands(O, M, N, K, 4)
+    out = []
+    for X in (A, B):
+        rows = X.shape[0]
+        codes = torch.empty((rows, K), dtype=torch.uint8, device=dev)
+        sc = torch.empty((rows, K // 32), dtype=torch.uint8, device=dev)
+        ce.quantize_mxfp6(codes, sc, torch.from_numpy(X).to(dev))
+        out.append((codes, sc))
+    (ca, sa), (cb, sb) = out
+    atoms_a = ce.sf_atoms(0, sa, M, K, 128)
+    atoms_b = ce.sf_atoms(0, sb, N, K, ce.BS_TILE_N)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_mxfp6(d, ce.pack_mxfp6(ca), atoms_a, ce.pack_mxfp6(cb), atoms_b, k=K)
+    ce.device_status()
+    a = _mx_dequant(O, ca.cpu().numpy(), sa.cpu().numpy())
+    b = _mx_dequant(O, cb.cpu().numpy(), sb.cpu().numpy())
+    _check(O, d.cpu().numpy(), a, b)
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_gemm_nvfp4(ce, O, dev, shape):
+    M, N, K = shape
+    A, B = _operands(O, M, N, K, 5)
+    out = []
+    for X in (A, B):
+        rows = X.shape[0]
+        codes = torch.empty((rows, K // 2), dtype=torch.uint8, device=dev)
+        sc = torch.empty((rows, K // 16), dtype=torch.uint8, device=dev)
+        ts = torch.empty(2, device=dev)
+        scratch = torch.zeros(1, dtype=torch.int32, device=dev)
+        ce.quantize_nvfp4(codes, sc, ts, scratch, torch.from_numpy(X).to(dev))
+        out.append((codes, sc, ts))
+    (ca, sa, ta), (cb, sb, tb) = out
+    atoms_a = ce.sf_atoms(1, sa, M, K, 128)
+    atoms_b = ce.sf_atoms(1, sb, N, K, ce.BS_TILE_N)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_nvfp4(d, ca, atoms_a, ta, cb, atoms_b, tb, K)
+    ce.device_status()
+    a = _nv_dequant(O, ca.cpu().numpy(), sa.cpu().numpy(), K)
+    b = _nv_dequant(O, cb.cpu().numpy(), sb.cpu().numpy(), K)
+    alpha = float(np.float32(ta.cpu().numpy()[1]) * np.float32(tb.cpu().numpy()[1]))
+    _check(O, d.cpu().numpy(), a, b, alpha)
