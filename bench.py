@@ -332,6 +332,8 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_precisions:
         for pname, pval, peak_key in (("bf16", ce.PREC_BF16, "bf16_tflops"),
                                       ("fp8_e4m3", ce.PREC_FP8_E4M3, None),
+                                      ("mxfp6_e3m2", ce.PREC_MXFP6_E3M2, None),
+                                      ("nvfp4_e2m1", ce.PREC_NVFP4_E2M1, None),
                                       ("tf32", ce.PREC_TF32, None)):
             pplan = ce.Plan(BATCH, SIZE, ROWS, pval)
             dWp = torch.from_numpy(W).to(dev)

@@ -31,6 +31,8 @@ PREC_FP32 = 0
 PREC_TF32 = 1
 PREC_BF16 = 2
 PREC_FP8_E4M3 = 3
+PREC_MXFP6_E3M2 = 4
+PREC_NVFP4_E2M1 = 5
 
 RMS_EPS = 1.0e-5  # kRmsEpsilon, llama2c/llama2c_common.h:44
 

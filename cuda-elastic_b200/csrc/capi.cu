@@ -415,8 +415,23 @@ struct ce_plan {
   void *activations = nullptr;   // bf16 / fp32 / e4m3 [batch][ld]
   float *w_scale = nullptr;      // e4m3: per weight row
   float *a_scale = nullptr;      // e4m3: per activation row
+  // block-scaled (MXFP6 / NVFP4): scale atoms, tensor scales, staging
+  uint8_t *w_atoms = nullptr;    // B scale atoms, grouped by CE_BS_TILE_N rows
+  uint8_t *a_atoms = nullptr;    // A scale atoms, grouped by 128 rows
+  uint8_t *a_sf = nullptr;       // A scales, row-major
+  uint8_t *a_codes = nullptr;    // MXFP6: unpacked A codes before packing
+  float *a_f32 = nullptr;        // normalized rows when the caller passes none
+  float *a_ts = nullptr;         // NVFP4 tensor scales of A (encode, decode)
+  float *w_ts = nullptr;         // NVFP4 tensor scales of W
+  uint32_t *scratch = nullptr;   // NVFP4 amax reduction word
   bool has_weights = false;
 };
+
+extern "C" int ce_plan_destroy(ce_plan *p);
+
+static bool block_scaled(int precision) {
+  return precision == CE_PREC_MXFP6_E3M2 || precision == CE_PREC_NVFP4_E2M1;
+}
 
 extern "C" {
 
@@ -425,8 +440,10 @@ int ce_plan_create(ce_plan **out, int batch, int size, int rows, int precision) 
   *out = nullptr;
   CE_REQUIRE(batch >= 1 && size >= 1 && rows >= 1, "batch, size and rows must be >= 1");
   CE_REQUIRE(precision == CE_PREC_FP32 || precision == CE_PREC_TF32 || precision == CE_PREC_BF16 ||
-                 precision == CE_PREC_FP8_E4M3,
+                 precision == CE_PREC_FP8_E4M3 || block_scaled(precision),
              "precision %d is not available in this build", precision);
+  CE_REQUIRE(!block_scaled(precision) || size % 128 == 0,
+             "block-scaled plans need size %% 128 == 0 (got %d)", size);
   CE_REQUIRE(precision != CE_PREC_FP8_E4M3 || (size % 4 == 0 && size <= 32768),
              "the e4m3 plan needs size %% 4 == 0 and size <= 32768 (got %d)", size);
   ce_plan *p = new ce_plan();
@@ -437,6 +454,25 @@ int ce_plan_create(ce_plan **out, int batch, int size, int rows, int precision) 
   CE_CUDA_TRY(cudaGetDevice(&p->device));
   p->ld = precision == CE_PREC_FP32 ? size : ((size + 63) / 64) * 64;
   const size_t elem = precision == CE_PREC_BF16 ? 2 : precision == CE_PREC_FP8_E4M3 ? 1 : 4;
+  if (block_scaled(precision)) {
+    const int fmt = precision == CE_PREC_MXFP6_E3M2 ? 0 : 1;
+    const int vec = fmt == 0 ? 32 : 16;
+    p->ld = fmt == 0 ? size : size / 2;  // operand bytes per row
+    cudaError_t e2 = cudaMalloc(&p->activations, (size_t)batch * p->ld);
+    if (e2 == cudaSuccess) e2 = cudaMalloc(&p->a_atoms, (size_t)sf_row_atoms(batch, 128) * sf_katoms(fmt, size) * 512);
+    if (e2 == cudaSuccess) e2 = cudaMalloc(&p->a_sf, (size_t)batch * (size / vec));
+    if (e2 == cudaSuccess) e2 = cudaMalloc(&p->a_f32, (size_t)batch * size * 4);
+    if (e2 == cudaSuccess && fmt == 0) e2 = cudaMalloc(&p->a_codes, (size_t)batch * size);
+    if (e2 == cudaSuccess && fmt == 1) e2 = cudaMalloc(&p->a_ts, 2 * sizeof(float));
+    if (e2 == cudaSuccess && fmt == 1) e2 = cudaMalloc(&p->w_ts, 2 * sizeof(float));
+    if (e2 == cudaSuccess && fmt == 1) e2 = cudaMalloc(&p->scratch, sizeof(uint32_t));
+    if (e2 != cudaSuccess) {
+      ce_plan_destroy(p);
+      return cuda_error(e2, "cudaMalloc(block-scaled plan)");
+    }
+    *out = p;
+    return CE_OK;
+  }
   cudaError_t e = cudaMalloc(&p->activations, (size_t)batch * p->ld * elem);
   if (e == cudaSuccess && precision == CE_PREC_FP8_E4M3) {
     e = cudaMalloc(&p->a_scale, (size_t)batch * 4);
@@ -456,8 +492,10 @@ int ce_plan_destroy(ce_plan *p) {
   if (p == nullptr) return CE_OK;
   if (p->weights) cudaFree(p->weights);
   if (p->activations) cudaFree(p->activations);
-  if (p->a_scale) cudaFree(p->a_scale);
-  if (p->w_scale) cudaFree(p->w_scale);
+  for (void *q : {(void *)p->a_scale, (void *)p->w_scale, (void *)p->w_atoms, (void *)p->a_atoms,
+                  (void *)p->a_sf, (void *)p->a_codes, (void *)p->a_f32, (void *)p->a_ts,
+                  (void *)p->w_ts, (void *)p->scratch})
+    if (q) cudaFree(q);
   delete p;
   return CE_OK;
 }
@@ -465,6 +503,42 @@ int ce_plan_destroy(ce_plan *p) {
 int ce_plan_set_weights(ce_plan *p, const float *w, ce_stream_t stream) {
   CE_REQUIRE(p != nullptr && w != nullptr, "null plan or weights");
   cudaStream_t s = (cudaStream_t)stream;
+  if (block_scaled(p->precision)) {
+    const int fmt = p->precision == CE_PREC_MXFP6_E3M2 ? 0 : 1;
+    const int vec = fmt == 0 ? 32 : 16;
+    const size_t w_bytes = (size_t)p->rows * (fmt == 0 ? p->size : p->size / 2);
+    if (p->weights == nullptr) CE_CUDA_TRY(cudaMalloc(&p->weights, w_bytes));
+    if (p->w_atoms == nullptr)
+      CE_CUDA_TRY(cudaMalloc(&p->w_atoms, (size_t)sf_row_atoms(p->rows, CE_BS_TILE_N) *
+                                              sf_katoms(fmt, p->size) * 512));
+    uint8_t *sf = nullptr, *codes = nullptr;
+    CE_CUDA_TRY(cudaMalloc(&sf, (size_t)p->rows * (p->size / vec)));
+    int rc;
+    if (fmt == 0) {
+      cudaError_t e = cudaMalloc(&codes, (size_t)p->rows * p->size);
+      if (e != cudaSuccess) {
+        cudaFree(sf);
+        return cuda_error(e, "cudaMalloc(weight codes)");
+      }
+      rc = quantize_mxfp6(codes, sf, w, p->rows, p->size, p->size, s);
+      if (rc == CE_OK)
+        rc = pack_mxfp6(static_cast<uint8_t *>(p->weights), codes, p->rows, p->size, p->size,
+                        p->size, s);
+    } else {
+      rc = quantize_nvfp4(static_cast<uint8_t *>(p->weights), sf, p->w_ts, p->scratch, w, p->rows,
+                          p->size, p->size / 2, s);
+    }
+    if (rc == CE_OK)
+      rc = sf_to_atoms(p->w_atoms, sf, p->rows, p->size / vec, sf_katoms(fmt, p->size),
+                       CE_BS_TILE_N, s);
+    cudaError_t e = cudaStreamSynchronize(s);
+    cudaFree(sf);
+    if (codes) cudaFree(codes);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_error(e, "cudaStreamSynchronize");
+    p->has_weights = true;
+    return CE_OK;
+  }
   const size_t elem = p->precision == CE_PREC_BF16 ? 2 : p->precision == CE_PREC_FP8_E4M3 ? 1 : 4;
   if (p->weights == nullptr) CE_CUDA_TRY(cudaMalloc(&p->weights, (size_t)p->rows * p->ld * elem));
   if (p->precision == CE_PREC_FP8_E4M3) {
@@ -486,6 +560,14 @@ int ce_plan_set_weights(ce_plan *p, const float *w, ce_stream_t stream) {
 
 static int plan_gemm(ce_plan *p, float *out, cudaStream_t s) {
   switch (p->precision) {
+    case CE_PREC_MXFP6_E3M2:
+      return gemm_mxfp6(out, static_cast<const uint8_t *>(p->activations), p->a_atoms,
+                        static_cast<const uint8_t *>(p->weights), p->w_atoms, p->batch, p->rows,
+                        p->size, p->size, p->size, p->rows, s);
+    case CE_PREC_NVFP4_E2M1:
+      return gemm_nvfp4(out, static_cast<const uint8_t *>(p->activations), p->a_atoms, p->a_ts + 1,
+                        static_cast<const uint8_t *>(p->weights), p->w_atoms, p->w_ts + 1, p->batch,
+                        p->rows, p->size, p->size / 2, p->size / 2, p->rows, s);
     case CE_PREC_BF16:
       return gemm_bf16(out, static_cast<const uint16_t *>(p->activations),
                        static_cast<const uint16_t *>(p->weights), p->batch, p->rows, p->size,
@@ -510,6 +592,28 @@ static int plan_gemm(ce_plan *p, float *out, cudaStream_t s) {
 static int plan_rows(ce_plan *p, float *normalized, float *softmax, const float *x,
                      const float *norm_w, const float *logits, float eps, cudaStream_t s) {
   const int nsoft = logits ? p->batch : 0;
+  if (block_scaled(p->precision)) {
+    // rmsnorm (+ softmax) in one launch, then the activation quantizer of
+    // the format (the reference's per-step conversion,
+    // decoder_lowprec.cu:469-482), then the scale atoms
+    float *xn = normalized ? normalized : p->a_f32;
+    int rc = rows_iteration(xn, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr, nullptr,
+                            p->batch, nsoft, p->size, 0, eps, s);
+    if (rc) return rc;
+    const int fmt = p->precision == CE_PREC_MXFP6_E3M2 ? 0 : 1;
+    const int vec = fmt == 0 ? 32 : 16;
+    if (fmt == 0) {
+      rc = quantize_mxfp6(p->a_codes, p->a_sf, xn, p->batch, p->size, p->size, s);
+      if (rc == CE_OK)
+        rc = pack_mxfp6(static_cast<uint8_t *>(p->activations), p->a_codes, p->batch, p->size,
+                        p->size, p->size, s);
+    } else {
+      rc = quantize_nvfp4(static_cast<uint8_t *>(p->activations), p->a_sf, p->a_ts, p->scratch, xn,
+                          p->batch, p->size, p->size / 2, s);
+    }
+    if (rc) return rc;
+    return sf_to_atoms(p->a_atoms, p->a_sf, p->batch, p->size / vec, sf_katoms(fmt, p->size), 128, s);
+  }
   if (p->precision == CE_PREC_FP8_E4M3)
     return rows_iteration(normalized, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr,
                           nullptr, p->batch, nsoft, p->size, 0, eps, s,

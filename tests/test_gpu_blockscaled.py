@@ -109,3 +109,49 @@ def test_gemm_nvfp4(ce, O, dev, shape):
     b = _nv_dequant(O, cb.cpu().numpy(), sb.cpu().numpy(), K)
     alpha = float(np.float32(ta.cpu().numpy()[1]) * np.float32(tb.cpu().numpy()[1]))
     _check(O, d.cpu().numpy(), a, b, alpha)
+
+
+@pytest.mark.parametrize("prec", ["mxfp6", "nvfp4"])
+@pytest.mark.parametrize("shape", [(8, 384, 768), (64, 1024, 512), (1024, 16384, 8192)])
+def test_plan_block_scaled(ce, O, dev, prec, shape):
+    """The op-trio plan in MXFP6 / NVFP4: weights quantized at setup,
+    activations quantized every step after the rmsnorm; the output against
+    the double GEMM of the dequantized operands (the spec's implementation
+    check), <= 1e-2 relative L2 (north star)."""
+    b, s, r = shape
+    x, w, logits, W = (O.trio_inputs if b < 1024 else ce.trio_inputs_host)(0, b, s, r)
+    pval = {"mxfp6": ce.PREC_MXFP6_E3M2, "nvfp4": ce.PREC_NVFP4_E2M1}[prec]
+    plan = ce.Plan(b, s, r, pval)
+    dW = torch.from_numpy(W).to(dev)
+    plan.set_weights(dW)
+    dx, dw, dl = (torch.from_numpy(a).to(dev) for a in (x, w, logits))
+    norm = torch.empty((b, s), device=dev)
+    soft = torch.empty((b, s), device=dev)
+    out = torch.full((b, r), float("nan"), device=dev)
+    plan.trio(norm, soft, out, dx, dw, dl)
+    ce.device_status()
+    rows = np.arange(b) if b <= 64 else np.random.default_rng(0).choice(b, 16, replace=False)
+    # the plan's operands, reproduced by the (bit-exact) standalone quantizers
+    ops = []
+    for X in (norm, dW):
+        n = X.shape[0]
+        if prec == "mxfp6":
+            c = torch.empty((n, s), dtype=torch.uint8, device=dev)
+            sc = torch.empty((n, s // 32), dtype=torch.uint8, device=dev)
+            ce.quantize_mxfp6(c, sc, X)
+            ops.append((_mx_dequant(O, c.cpu().numpy(), sc.cpu().numpy()), 1.0))
+        else:
+            c = torch.empty((n, s // 2), dtype=torch.uint8, device=dev)
+            sc = torch.empty((n, s // 16), dtype=torch.uint8, device=dev)
+            ts = torch.empty(2, device=dev)
+            scratch = torch.zeros(1, dtype=torch.int32, device=dev)
+            ce.quantize_nvfp4(c, sc, ts, scratch, X)
+            ops.append((_nv_dequant(O, c.cpu().numpy(), sc.cpu().numpy(), s), float(ts.cpu()[1])))
+    (a, da), (bq, db) = ops
+    alpha = float(np.float32(da) * np.float32(db))
+    ref, _ = O.gemm_ref(a[rows], bq)
+    ho = out.cpu().numpy()[rows]
+    assert O.rel_l2(ho, ref * alpha) <= 1e-2
+    ref32, _ = O.gemm_ref(O.rmsnorm_ref(x[rows], w), W)
+    assert O.rel_l2(ho, ref32) <= (0.12 if prec == "mxfp6" else 0.25)
+    plan.close()
