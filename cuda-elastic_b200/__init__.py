@@ -100,6 +100,7 @@ _SIGNATURES = {
     "ce_plan_trio": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
     "ce_plan_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
     "ce_plan_gemm": [_vp, _vp, _vp],
+    "ce_decoder_validate": [_i64, _i64, _i64, _i64, _i],
     "ce_decoder_create": [ctypes.POINTER(_vp), _i64, _i64, _i64, _i64, _i, _vp],
     "ce_decoder_destroy": [_vp],
     "ce_decoder_set_model": [_vp, _vp, _vp, _vp, _vp],

@@ -19,7 +19,8 @@ BUILD = os.path.join(PKG, "_build")
 LIB = os.path.join(PKG, "libce_b200.so")
 HOST = os.path.join(PKG, "host")
 # Drop-in front ends (host C++ over the C ABI): executable -> sources in host/.
-EXECUTABLES = {"llama2c_b200": ["llama2c_b200.cpp", "llama2c_check.cpp"]}
+EXECUTABLES = {"llama2c_b200": ["llama2c_b200.cpp", "llama2c_check.cpp"],
+               "decoder_b200": ["decoder_b200.cpp", "decoder_check.cpp", "lp_front.cpp"]}
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC",

@@ -209,10 +209,7 @@ extern "C" {
 
 // Validation and allocation of applications/loom_private/decoder/decoder.cu:
 // 369-408 (make_decoder, with its limits and messages) and setup (:241-265).
-int ce_decoder_create(ce_decoder **out, int64_t batch, int64_t width, int64_t vocab, int64_t steps,
-                      int precision, ce_stream_t stream) {
-  CE_REQUIRE(out != nullptr, "null decoder pointer");
-  *out = nullptr;
+int ce_decoder_validate(int64_t batch, int64_t width, int64_t vocab, int64_t steps, int precision) {
   CE_REQUIRE(batch >= 1 && batch <= (1LL << 20), "batch must be in [1, 1048576] (got %lld)",
              (long long)batch);
   CE_REQUIRE(width >= 2 && width <= (1LL << 24) - 16,
@@ -236,6 +233,14 @@ int ce_decoder_create(ce_decoder **out, int64_t batch, int64_t width, int64_t vo
              "dimensions need %.1f GiB of device memory and %.1f GiB of host diagnostics "
              "(limits 160 and 64 GiB)",
              device / (1LL << 30), diagnostics / (1LL << 30));
+  return CE_OK;
+}
+
+int ce_decoder_create(ce_decoder **out, int64_t batch, int64_t width, int64_t vocab, int64_t steps,
+                      int precision, ce_stream_t stream) {
+  CE_REQUIRE(out != nullptr, "null decoder pointer");
+  *out = nullptr;
+  if (int rc = ce_decoder_validate(batch, width, vocab, steps, precision)) return rc;
   ce_decoder *d = new ce_decoder();
   d->B = batch;
   d->W = width;

@@ -342,6 +342,12 @@ int ce_plan_trio(ce_plan *plan, float *normalized_dev, float *softmax_dev, float
  * decoder.cu:200-367. */
 typedef struct ce_decoder ce_decoder;
 
+/* The dimension and precision checks of ce_decoder_create alone, with the
+ * limits and messages of make_decoder (decoder.cu:369-408; device limit 160
+ * GiB): CE_OK or CE_ERR_USAGE with the message in ce_last_error. Makes no
+ * CUDA call, so a front end can reject a shape before it touches the device. */
+int ce_decoder_validate(int64_t batch, int64_t width, int64_t vocab, int64_t steps, int precision);
+
 /* Validates the dimensions with the limits and messages of make_decoder
  * (decoder.cu:369-408; the device limit is raised to B200 memory: 160 GiB),
  * allocates every buffer, generates the synthetic model on the device
