@@ -99,7 +99,8 @@ def test_tf32_gemm(ce, O, dev, shape):
     assert O.rel_l2(dd, ref) <= 1e-2
 
 
-@pytest.mark.parametrize("shape", [(8, 768, 288), (130, 70, 1001), (1, 1, 1)])
+@pytest.mark.parametrize("shape", [(8, 768, 288), (130, 70, 1001), (1, 1, 1), (300, 12600, 37),
+                                   (1024, 8192, 20), (512, 8192, 24)])
 def test_fp32_simt_gemm_is_sequential(ce, O, dev, shape):
     """Bitwise equal to sequential fp32 accumulation from 0 in increasing k
     with separate multiply and add (the decoder contract's order)."""
