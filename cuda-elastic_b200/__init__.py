@@ -109,6 +109,15 @@ _SIGNATURES = {
     "ce_decoder_poison": [_vp, _vp],
     "ce_decoder_copy_outputs": [_vp, _i, _vp, _vp, _vp, _vp],
     "ce_decoder_inject_fault": [_vp, _i],
+    "ce_llama_validate": [_vp, _i, _i, _i],
+    "ce_llama_create": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _vp],
+    "ce_llama_destroy": [_vp],
+    "ce_llama_init_random": [_vp, ctypes.c_uint64, _f, _i, _vp],
+    "ce_llama_start": [_vp, _vp, _i, _vp],
+    "ce_llama_enqueue_step": [_vp, _vp],
+    "ce_llama_read": [_vp, _i, _i, _vp, _i64, _i64],
+    "ce_llama_write": [_vp, _i, _i, _vp, _i64, _i64],
+    "ce_llama_status": [],
 }
 _RESTYPES = {"ce_version": ctypes.c_char_p}
 
@@ -473,3 +482,131 @@ class Decoder:
         check(lib().ce_decoder_copy_outputs(self._h, int(bool(from_device)), _ptr(g), _ptr(n),
                                             _ptr(lg), _ptr(p)))
         return g, n, lg, p
+
+
+# --------------------------------------------------------------------------
+# Llama-2 decoder step (ce_llama_*)
+
+LLAMA_TOK_EMB, LLAMA_WQKV, LLAMA_WO, LLAMA_W13, LLAMA_W2 = 0, 1, 2, 3, 4
+LLAMA_RMS_ATT, LLAMA_RMS_FFN, LLAMA_RMS_FINAL, LLAMA_WCLS = 5, 6, 7, 8
+LLAMA_KCACHE, LLAMA_VCACHE, LLAMA_LOGITS, LLAMA_TOKENS = 9, 10, 11, 12
+LLAMA_GENERATED, LLAMA_POS, LLAMA_RESIDUAL = 13, 14, 15
+
+
+class LlamaConfig(ctypes.Structure):
+    """llama2.c's Config (dim, hidden_dim, n_layers, n_heads, n_kv_heads,
+    vocab_size, seq_len)."""
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size", "seq_len")]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
+def llama_config(**kw):
+    c = LlamaConfig()
+    kw.setdefault("n_kv_heads", kw.get("n_heads"))
+    for n, _ in LlamaConfig._fields_:
+        setattr(c, n, int(kw[n]))
+    return c
+
+
+class Llama:
+    """Batched greedy decoding of a Llama-2 transformer on one GPU: weights,
+    KV cache and buffers live in the library; step() enqueues one decode step
+    for every sequence (capturable; position and step counters are on the
+    device, so a captured step replays for every token)."""
+
+    def __init__(self, cfg, batch, max_steps, precision=PREC_BF16, stream=None):
+        self.cfg = cfg if isinstance(cfg, LlamaConfig) else llama_config(**cfg)
+        self.batch, self.max_steps, self.precision = batch, max_steps, precision
+        self.hs = self.cfg.dim // self.cfg.n_heads
+        self.kv_dim = self.hs * self.cfg.n_kv_heads
+        h = ctypes.c_void_p()
+        check(lib().ce_llama_create(ctypes.byref(h), ctypes.byref(self.cfg), batch, max_steps,
+                                    precision, _stream(stream)))
+        self._h = h
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().ce_llama_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def init_random(self, seed=0, weight_std=0.02, kv_fill=0, stream=None):
+        check(lib().ce_llama_init_random(self._h, seed, weight_std, kv_fill, _stream(stream)))
+
+    def start(self, tokens, pos, stream=None):
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        assert t.shape == (self.batch,)
+        check(lib().ce_llama_start(self._h, t.ctypes.data, pos, _stream(stream)))
+
+    def step(self, stream=None):
+        check(lib().ce_llama_enqueue_step(self._h, _stream(stream)))
+
+    def read(self, which, layer=0, dtype=np.uint16, count=None, offset=0):
+        """Host copy of `count` elements of a tensor from element `offset`."""
+        item = np.dtype(dtype).itemsize
+        if count is None:
+            count = self._size(which) // item - offset
+        out = np.empty(count, dtype)
+        check(lib().ce_llama_read(self._h, which, layer, out.ctypes.data, offset * item, count * item))
+        return out
+
+    def write(self, which, array, layer=0, offset=0):
+        a = np.ascontiguousarray(array)
+        check(lib().ce_llama_write(self._h, which, layer, a.ctypes.data, offset * a.itemsize, a.nbytes))
+
+    def _size(self, which):
+        c, B = self.cfg, self.batch
+        sizes = {LLAMA_TOK_EMB: c.vocab_size * c.dim * 2, LLAMA_WQKV: (c.dim + 2 * self.kv_dim) * c.dim * 2,
+                 LLAMA_WO: c.dim * c.dim * 2, LLAMA_W13: 2 * c.hidden_dim * c.dim * 2,
+                 LLAMA_W2: c.dim * c.hidden_dim * 2, LLAMA_RMS_ATT: c.dim * 4, LLAMA_RMS_FFN: c.dim * 4,
+                 LLAMA_RMS_FINAL: c.dim * 4, LLAMA_WCLS: c.vocab_size * c.dim * 2,
+                 LLAMA_KCACHE: B * c.n_kv_heads * c.seq_len * self.hs * 2,
+                 LLAMA_VCACHE: B * c.n_kv_heads * c.seq_len * self.hs * 2,
+                 LLAMA_LOGITS: B * c.vocab_size * 4, LLAMA_TOKENS: B * 4,
+                 LLAMA_GENERATED: B * self.max_steps * 4, LLAMA_POS: 4, LLAMA_RESIDUAL: B * c.dim * 4}
+        return sizes[which]
+
+    def generated(self):
+        return self.read(LLAMA_GENERATED, dtype=np.int32).reshape(self.batch, self.max_steps)
+
+    def logits(self):
+        return self.read(LLAMA_LOGITS, dtype=np.float32).reshape(self.batch, self.cfg.vocab_size)
+
+    def cache_rows(self, layer, seq, which=LLAMA_KCACHE, positions=None):
+        """bf16 bits [kv_heads][positions][hs] of one sequence's cache."""
+        c = self.cfg
+        n = c.seq_len if positions is None else positions
+        per_head = c.seq_len * self.hs
+        out = np.empty((c.n_kv_heads, n, self.hs), np.uint16)
+        for kh in range(c.n_kv_heads):
+            off = (seq * c.n_kv_heads + kh) * per_head
+            out[kh] = self.read(which, layer, np.uint16, n * self.hs, off).reshape(n, self.hs)
+        return out
+
+    def weights(self):
+        """Every weight as host arrays (bf16 bits as uint16, RMSNorm fp32)."""
+        c = self.cfg
+        w = {"tok_emb": self.read(LLAMA_TOK_EMB).reshape(c.vocab_size, c.dim),
+             "wcls": self.read(LLAMA_WCLS).reshape(c.vocab_size, c.dim),
+             "rms_final": self.read(LLAMA_RMS_FINAL, dtype=np.float32)}
+        for key, which, shape in (("wqkv", LLAMA_WQKV, (c.dim + 2 * self.kv_dim, c.dim)),
+                                  ("wo", LLAMA_WO, (c.dim, c.dim)),
+                                  ("w13", LLAMA_W13, (2 * c.hidden_dim, c.dim)),
+                                  ("w2", LLAMA_W2, (c.dim, c.hidden_dim))):
+            w[key] = [self.read(which, l).reshape(shape) for l in range(c.n_layers)]
+        w["rms_att"] = [self.read(LLAMA_RMS_ATT, l, np.float32) for l in range(c.n_layers)]
+        w["rms_ffn"] = [self.read(LLAMA_RMS_FFN, l, np.float32) for l in range(c.n_layers)]
+        return w
+
+
+def llama_status():
+    """Reads and clears the decode kernels' status (raises on a failure)."""
+    check(lib().ce_llama_status())

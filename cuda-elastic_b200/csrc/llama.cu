@@ -1,0 +1,749 @@
+// Batched greedy decode step of a Llama-2 transformer (the llama2.c model:
+// token embedding, n_layers x [RMSNorm -> QKV -> RoPE -> causal attention
+// over the KV cache -> output projection -> residual, RMSNorm -> SwiGLU FFN
+// -> residual], final RMSNorm, classifier, greedy argmax), the full decoder
+// step that the llama2c decoder workload of the reference
+// (applications/loom_private/decoder/decoder.cu:267-296) runs only the last
+// stage of. The arithmetic is the standard Llama-2 decoder, restated from the
+// mathematics: rmsnorm o = w * x / sqrt(mean(x^2) + 1e-5); RoPE rotates each
+// (even, odd) pair of q and k at head-dimension index j by pos * 10000^(-j/hs);
+// attention softmax(q k^T / sqrt(hs)) v per head over positions 0..pos;
+// SwiGLU w2(silu(w1 x) * w3 x) with silu(g) = g / (1 + e^-g).
+//
+// B200 layout. The residual stream x is fp32 [batch][dim]; every GEMM operand
+// is bf16 (the normalized rows, the attention output, the SwiGLU product) and
+// every GEMM accumulates and writes fp32 through the tcgen05 engine of
+// gemm.cu. Weights are bf16 [out][in] (K-major), the per-layer QKV rows
+// stacked [q; k; v] and the FFN's w1 and w3 stacked [w1; w3] so each is one
+// GEMM. The KV cache is bf16 [layer][batch][kv_head][seq_len][head_size]: the
+// keys of one (sequence, head) are one contiguous run that a single bulk copy
+// moves into shared memory. Decode attention is split over position chunks
+// (flash-decoding): one 128-thread CTA per (chunk, head, sequence) stages its
+// K and V rows with cp.async.bulk, and a combine pass merges the chunks'
+// (max, sum, output) triples. The current position and step live in device
+// memory, advanced by the last launch of the step, so one captured step
+// graph replays for every token.
+#include <cuda_bf16.h>
+
+#include <cmath>
+#include <type_traits>
+#include <vector>
+
+#include "common.cuh"
+#include "row_ops.cuh"
+
+namespace ce {
+
+int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+              int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
+              cudaStream_t s, int force_group = 0);
+
+static __device__ DeviceStatus g_llama_status;
+
+namespace {
+
+using rowops::block_max;
+using rowops::block_sum;
+
+constexpr int kRowThreads = 256;
+constexpr int kAttnThreads = 128;
+constexpr int kChunkBytes = 32768;  // K bytes of one attention chunk (V the same)
+
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// splitmix64 of a counter: the deterministic source of the random init.
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// N(0, std) bf16 values (Box-Muller on two 24-bit uniforms of one counter)
+// into the first `filled` elements of each of the n / filled runs of `run`
+// elements at out (filled == run: one contiguous fill of n elements). The
+// value at element e is a function of (seed, stream, e) only.
+__global__ void init_normal_bf16_kernel(uint16_t *out, size_t n, uint64_t seed, uint64_t stream,
+                                        float std, size_t run, size_t filled) {
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t k = (size_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += step) {
+    const size_t i = (k / filled) * run + k % filled;
+    const uint64_t r = mix64(seed ^ mix64(stream * 0x632BE59BD9B4E019ull + i));
+    const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((r >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+    __nv_bfloat16 h = __float2bfloat16_rn(z * std);
+    out[i] = *reinterpret_cast<uint16_t *>(&h);
+  }
+}
+
+__global__ void fill_f32_kernel(float *out, size_t n, float v) {
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) out[i] = v;
+}
+
+// One row of the residual stream per block: x = embedding[token] (first
+// layer), or x += delta (after a sublayer), then xb = bf16(w * (x * scale)),
+// scale = 1 / sqrtf(sum(x^2) / dim + eps). An out-of-range token makes the
+// row NaN so the failure shows in every output.
+template <int NV>
+__global__ void __launch_bounds__(kRowThreads)
+residual_rmsnorm_kernel(float *x, const float *delta, const uint16_t *emb, const int *tokens,
+                        int vocab, const float *w, uint16_t *xb, int dim, float eps) {
+  __shared__ float scratch[32];
+  const int b = blockIdx.x, cols4 = dim / 4;
+  float4 *xr = reinterpret_cast<float4 *>(x + (size_t)b * dim);
+  float4 v[NV];
+  if (emb != nullptr) {
+    const int tok = tokens[b];
+    const bool ok = tok >= 0 && tok < vocab;
+    const uint2 *er = reinterpret_cast<const uint2 *>(emb + (size_t)(ok ? tok : 0) * dim);
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * kRowThreads;
+      if (i < cols4) {
+        const uint2 e = er[i];
+        v[j] = make_float4(__uint_as_float(e.x << 16), __uint_as_float(e.x & 0xFFFF0000u),
+                           __uint_as_float(e.y << 16), __uint_as_float(e.y & 0xFFFF0000u));
+        if (!ok) v[j] = make_float4(NAN, NAN, NAN, NAN);
+        xr[i] = v[j];
+      }
+    }
+  } else {
+    const float4 *dr = delta ? reinterpret_cast<const float4 *>(delta + (size_t)b * dim) : nullptr;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * kRowThreads;
+      if (i < cols4) {
+        v[j] = xr[i];
+        if (dr) {
+          const float4 d = dr[i];
+          v[j].x += d.x, v[j].y += d.y, v[j].z += d.z, v[j].w += d.w;
+          xr[i] = v[j];
+        }
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j)
+    if (threadIdx.x + j * kRowThreads < cols4)
+      ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  ss = block_sum(ss, scratch);
+  const float scale = 1.0f / sqrtf(ss / (float)dim + eps);
+  uint2 *out = reinterpret_cast<uint2 *>(xb + (size_t)b * dim);
+  const float4 *wr = reinterpret_cast<const float4 *>(w);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * kRowThreads;
+    if (i < cols4) {
+      const float4 g = wr[i];
+      uint2 o;
+      o.x = pack_bf16x2(g.x * (v[j].x * scale), g.y * (v[j].y * scale));
+      o.y = pack_bf16x2(g.z * (v[j].z * scale), g.w * (v[j].w * scale));
+      out[i] = o;
+    }
+  }
+}
+
+// RoPE on q and k of one sequence (in place in the fp32 QKV rows), then k
+// and v to the bf16 cache at the current position. rope holds (cos, sin) of
+// pos * 10000^(-2i/hs) for every position and pair index i.
+__global__ void rope_append_kernel(float *qkv, int ld_qkv, uint16_t *kcache, uint16_t *vcache,
+                                   const float2 *rope, const int *pos_ptr, int dim, int kv_dim,
+                                   int hs, int kv_heads, int seq_len) {
+  const int b = blockIdx.x;
+  const int pos = *pos_ptr;
+  if (pos < 0 || pos >= seq_len) {
+    if (threadIdx.x == 0) report_timeout(&g_llama_status, 900u);  // position out of the cache
+    return;
+  }
+  float *row = qkv + (size_t)b * ld_qkv;
+  const float2 *rp = rope + (size_t)pos * (hs / 2);
+  for (int p = threadIdx.x; p < dim / 2; p += blockDim.x) {
+    const int i = 2 * p;
+    const float2 cs = rp[(i % hs) / 2];
+    const float q0 = row[i], q1 = row[i + 1];
+    row[i] = q0 * cs.x - q1 * cs.y;
+    row[i + 1] = q0 * cs.y + q1 * cs.x;
+  }
+  const size_t per_head = (size_t)seq_len * hs;
+  for (int p = threadIdx.x; p < kv_dim / 2; p += blockDim.x) {
+    const int i = 2 * p, kh = i / hs, d = i % hs;
+    const float2 cs = rp[d / 2];
+    const float k0 = row[dim + i], k1 = row[dim + i + 1];
+    const size_t at = ((size_t)b * kv_heads + kh) * per_head + (size_t)pos * hs + d;
+    *reinterpret_cast<uint32_t *>(kcache + at) = pack_bf16x2(k0 * cs.x - k1 * cs.y, k0 * cs.y + k1 * cs.x);
+    *reinterpret_cast<uint32_t *>(vcache + at) = pack_bf16x2(row[dim + kv_dim + i], row[dim + kv_dim + i + 1]);
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Decode attention over one chunk of positions for one (sequence, head):
+// partial max m, sum l of exp(s - m) and unnormalized output o[hs] of the
+// chunk, s = q . k_t / sqrt(hs). Written as part[(b*H + h)*nchunk + c] =
+// {m, l, o[0..hs)}.
+template <int HS>
+__global__ void __launch_bounds__(kAttnThreads)
+attn_chunk_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const uint16_t *vcache,
+                  const int *pos_ptr, int n_heads, int kv_heads, int seq_len, int chunk, int nchunk,
+                  float *part) {
+  constexpr int kPairs = HS / 2;                   // bf16 pairs per row
+  constexpr int kGroups = kAttnThreads / kPairs;   // position groups of the output pass
+  constexpr int kRowVec = HS * 2 / 16;             // 16-byte pieces per K row
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint16_t *ks = reinterpret_cast<uint16_t *>(smem);
+  uint16_t *vs = ks + (size_t)chunk * HS;
+  float *ps = reinterpret_cast<float *>(vs + (size_t)chunk * HS);  // [chunk] scores / weights
+  float *qs = ps + chunk;                                           // [HS]
+  float *red = qs + HS;                                             // [kAttnThreads * 2] + 32
+  __shared__ __align__(8) uint64_t bar;
+
+  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int n = *pos_ptr + 1;
+  float *out = part + (((size_t)b * n_heads + h) * nchunk + c) * (HS + 2);
+  const int t0 = c * chunk;
+  if (n < 1 || n > seq_len || t0 >= n) {
+    if (threadIdx.x < HS + 2) out[threadIdx.x] = threadIdx.x == 0 ? -INFINITY : 0.f;
+    return;
+  }
+  const int cnt = min(chunk, n - t0);
+  const int kh = h / (n_heads / kv_heads);
+  const size_t base = (((size_t)b * kv_heads + kh) * seq_len + t0) * HS;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = (uint32_t)cnt * HS * 2;
+    mbar_arrive_expect_tx(&bar, 2 * bytes);
+    bulk_g2s(ks, kcache + base, bytes, &bar);
+    bulk_g2s(vs, vcache + base, bytes, &bar);
+  }
+  const float qscale = rsqrtf((float)HS);
+  for (int d = threadIdx.x; d < HS; d += kAttnThreads) qs[d] = qkv[(size_t)b * ld_qkv + h * HS + d] * qscale;
+  const bool arrived = mbar_wait(&bar, 0, &g_llama_status, 901u);
+  if (!__syncthreads_and(arrived)) {
+    if (threadIdx.x < HS + 2) out[threadIdx.x] = NAN;
+    return;
+  }
+  // scores: one position per thread, 16-byte pieces read in a rotated order
+  // so the 8 threads of a shared-memory phase touch 8 different banks groups
+  const int lane = threadIdx.x & 31;
+  float mx = -INFINITY;
+  for (int t = threadIdx.x; t < cnt; t += kAttnThreads) {
+    const uint4 *kr = reinterpret_cast<const uint4 *>(ks + (size_t)t * HS);
+    float s = 0.f;
+#pragma unroll
+    for (int jj = 0; jj < kRowVec; ++jj) {
+      const int j = (jj + lane) % kRowVec;
+      const uint4 kv = kr[j];
+      const float *q = qs + j * 8;
+      s += q[0] * __uint_as_float(kv.x << 16) + q[1] * __uint_as_float(kv.x & 0xFFFF0000u);
+      s += q[2] * __uint_as_float(kv.y << 16) + q[3] * __uint_as_float(kv.y & 0xFFFF0000u);
+      s += q[4] * __uint_as_float(kv.z << 16) + q[5] * __uint_as_float(kv.z & 0xFFFF0000u);
+      s += q[6] * __uint_as_float(kv.w << 16) + q[7] * __uint_as_float(kv.w & 0xFFFF0000u);
+    }
+    ps[t] = s;
+    mx = fmaxf(mx, s);
+  }
+  mx = block_max(mx, red + 2 * kAttnThreads);
+  float sum = 0.f;
+  for (int t = threadIdx.x; t < cnt; t += kAttnThreads) {
+    const float e = expf(ps[t] - mx);
+    ps[t] = e;
+    sum += e;
+  }
+  sum = block_sum(sum, red + 2 * kAttnThreads);  // its trailing barrier publishes ps
+  // output: thread (pair p, group g) sums positions t = g mod kGroups
+  const int p = threadIdx.x % kPairs, g = threadIdx.x / kPairs;
+  float o0 = 0.f, o1 = 0.f;
+  for (int t = g; t < cnt; t += kGroups) {
+    const uint32_t vv = *reinterpret_cast<const uint32_t *>(vs + (size_t)t * HS + 2 * p);
+    const float w = ps[t];
+    o0 += w * __uint_as_float(vv << 16);
+    o1 += w * __uint_as_float(vv & 0xFFFF0000u);
+  }
+  red[2 * threadIdx.x] = o0;
+  red[2 * threadIdx.x + 1] = o1;
+  __syncthreads();
+  if (threadIdx.x < kPairs) {
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+    for (int gg = 0; gg < kGroups; ++gg) {
+      a0 += red[2 * (gg * kPairs + threadIdx.x)];
+      a1 += red[2 * (gg * kPairs + threadIdx.x) + 1];
+    }
+    out[2 + 2 * threadIdx.x] = a0;
+    out[3 + 2 * threadIdx.x] = a1;
+  }
+  if (threadIdx.x == 0) {
+    out[0] = mx;
+    out[1] = sum;
+  }
+}
+
+// Merges the chunks of one (sequence, head): att = sum_c o_c e^(m_c - M) /
+// sum_c l_c e^(m_c - M), written as bf16 into the o-projection operand.
+template <int HS>
+__global__ void attn_combine_kernel(const float *part, int nchunk, int n_heads, uint16_t *att, int dim) {
+  const int bh = blockIdx.x, d = threadIdx.x;
+  const float *pp = part + (size_t)bh * nchunk * (HS + 2);
+  float M = -INFINITY;
+  for (int c = 0; c < nchunk; ++c) M = fmaxf(M, pp[c * (HS + 2)]);
+  float L = 0.f, o = 0.f;
+  for (int c = 0; c < nchunk; ++c) {
+    const float m = pp[c * (HS + 2)];
+    if (m == -INFINITY) continue;
+    const float f = expf(m - M);
+    L += pp[c * (HS + 2) + 1] * f;
+    o += pp[c * (HS + 2) + 2 + d] * f;
+  }
+  const int b = bh / n_heads, h = bh % n_heads;
+  __nv_bfloat16 r = __float2bfloat16_rn(o / L);
+  att[(size_t)b * dim + h * HS + d] = *reinterpret_cast<uint16_t *>(&r);
+}
+
+// hb = bf16(silu(h1) * h3), h = [h1 | h3] per row, silu(g) = g / (1 + e^-g).
+__global__ void swiglu_kernel(const float *h, uint16_t *hb, int rows, int hidden) {
+  const size_t n = (size_t)rows * hidden / 2;
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const size_t r = (2 * i) / hidden, c = (2 * i) % hidden;
+    const float2 g = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + c);
+    const float2 u = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + hidden + c);
+    const float a = g.x / (1.0f + expf(-g.x)) * u.x;
+    const float bb = g.y / (1.0f + expf(-g.y)) * u.y;
+    *reinterpret_cast<uint32_t *>(hb + r * hidden + c) = pack_bf16x2(a, bb);
+  }
+}
+
+// Greedy token of each row: index of the first maximum logit (NaN never
+// wins); written to tokens[b] and generated[b][step] while step < cap.
+__global__ void __launch_bounds__(kRowThreads)
+argmax_kernel(const float *logits, int vocab, int *tokens, int *generated, int cap, const int *step_ptr) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int b = blockIdx.x;
+  const float *row = logits + (size_t)b * vocab;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < vocab; i += kRowThreads) {
+    const float v = row[i];
+    if (v > best) best = v, idx = i;  // strided order: first max of this thread
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, best, off);
+    const int oi = __shfl_down_sync(0xffffffffu, idx, off);
+    if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sv[w] = best, si[w] = idx;
+  __syncthreads();
+  if (w == 0) {
+    best = lane < kRowThreads / 32 ? sv[lane] : -INFINITY;
+    idx = lane < kRowThreads / 32 ? si[lane] : 0x7fffffff;
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, best, off);
+      const int oi = __shfl_down_sync(0xffffffffu, idx, off);
+      if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
+    }
+    if (lane == 0) {
+      if (idx == 0x7fffffff) idx = 0;  // every logit NaN
+      tokens[b] = idx;
+      const int step = *step_ptr;
+      if (step >= 0 && step < cap) generated[(size_t)b * cap + step] = idx;
+    }
+  }
+}
+
+__global__ void advance_kernel(int *pos, int *step) {
+  *pos += 1;
+  *step += 1;
+}
+
+template <typename F>
+int launch_rows(int nv, F &&f) {
+  switch (nv) {
+    case 1: f(std::integral_constant<int, 1>{}); break;
+    case 2: f(std::integral_constant<int, 2>{}); break;
+    case 4: f(std::integral_constant<int, 4>{}); break;
+    case 8: f(std::integral_constant<int, 8>{}); break;
+    default: return set_error(CE_ERR_USAGE, "dim too large for the row kernels");
+  }
+  return CE_OK;
+}
+
+size_t attn_smem_bytes(int chunk, int hs) {
+  return (size_t)chunk * hs * 2 * 2 + (size_t)chunk * 4 + (size_t)hs * 4 + (2 * kAttnThreads + 32) * 4;
+}
+
+// Opts the attention kernels into their dynamic shared memory, once per device.
+int configure_attention() {
+  static bool done[64] = {};
+  int dev = 0;
+  CE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 0 && dev < 64 && done[dev]) return CE_OK;
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)attn_smem_bytes(kChunkBytes / 128, 64)));
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)attn_smem_bytes(kChunkBytes / 256, 128)));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return CE_OK;
+}
+
+int pow2_at_least(int v) {
+  int p = 1;
+  while (p < v) p *= 2;
+  return p;
+}
+
+}  // namespace
+}  // namespace ce
+
+using namespace ce;
+
+struct ce_llama {
+  ce_llama_config c{};
+  int B = 0, cap = 0, precision = 0;
+  int hs = 0, kv_dim = 0, qkv_rows = 0, chunk = 0, nchunk = 0, nv = 0;
+  size_t layer_kv = 0;  // cache elements of one layer (batch x kv_heads x seq_len x hs)
+  // weights
+  uint16_t *tok_emb = nullptr, *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr,
+           *wcls = nullptr;
+  float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
+  float2 *rope = nullptr;
+  // cache and activations
+  uint16_t *kcache = nullptr, *vcache = nullptr, *xb = nullptr, *att = nullptr, *hb = nullptr;
+  float *x = nullptr, *delta = nullptr, *qkv = nullptr, *h = nullptr, *logits = nullptr,
+        *part = nullptr;
+  int *tokens = nullptr, *generated = nullptr, *pos = nullptr, *step = nullptr;
+};
+
+namespace {
+
+void free_llama(ce_llama *m) {
+  for (void *p : {(void *)m->tok_emb, (void *)m->wqkv, (void *)m->wo, (void *)m->w13, (void *)m->w2,
+                  (void *)m->wcls, (void *)m->rms_att, (void *)m->rms_ffn, (void *)m->rms_final,
+                  (void *)m->rope, (void *)m->kcache, (void *)m->vcache, (void *)m->xb, (void *)m->att,
+                  (void *)m->hb, (void *)m->x, (void *)m->delta, (void *)m->qkv, (void *)m->h,
+                  (void *)m->logits, (void *)m->part, (void *)m->tokens, (void *)m->generated,
+                  (void *)m->pos, (void *)m->step})
+    if (p) cudaFree(p);
+  delete m;
+}
+
+size_t wqkv_elems(const ce_llama *m) { return (size_t)m->qkv_rows * m->c.dim; }
+size_t wo_elems(const ce_llama *m) { return (size_t)m->c.dim * m->c.dim; }
+size_t w13_elems(const ce_llama *m) { return (size_t)2 * m->c.hidden_dim * m->c.dim; }
+size_t w2_elems(const ce_llama *m) { return (size_t)m->c.dim * m->c.hidden_dim; }
+
+struct TensorView {
+  void *ptr;
+  size_t bytes;
+};
+
+// Device tensor `which` of layer `layer` (layer ignored for global tensors).
+int tensor_of(ce_llama *m, int which, int layer, TensorView *v) {
+  const ce_llama_config &c = m->c;
+  const bool per_layer = which == CE_LLAMA_WQKV || which == CE_LLAMA_WO || which == CE_LLAMA_W13 ||
+                         which == CE_LLAMA_W2 || which == CE_LLAMA_RMS_ATT || which == CE_LLAMA_RMS_FFN ||
+                         which == CE_LLAMA_KCACHE || which == CE_LLAMA_VCACHE;
+  CE_REQUIRE(!per_layer || (layer >= 0 && layer < c.n_layers), "layer %d out of range", layer);
+  const size_t L = (size_t)layer;
+  switch (which) {
+    case CE_LLAMA_TOK_EMB: *v = {m->tok_emb, (size_t)c.vocab_size * c.dim * 2}; break;
+    case CE_LLAMA_WQKV: *v = {m->wqkv + L * wqkv_elems(m), wqkv_elems(m) * 2}; break;
+    case CE_LLAMA_WO: *v = {m->wo + L * wo_elems(m), wo_elems(m) * 2}; break;
+    case CE_LLAMA_W13: *v = {m->w13 + L * w13_elems(m), w13_elems(m) * 2}; break;
+    case CE_LLAMA_W2: *v = {m->w2 + L * w2_elems(m), w2_elems(m) * 2}; break;
+    case CE_LLAMA_RMS_ATT: *v = {m->rms_att + L * c.dim, (size_t)c.dim * 4}; break;
+    case CE_LLAMA_RMS_FFN: *v = {m->rms_ffn + L * c.dim, (size_t)c.dim * 4}; break;
+    case CE_LLAMA_RMS_FINAL: *v = {m->rms_final, (size_t)c.dim * 4}; break;
+    case CE_LLAMA_WCLS: *v = {m->wcls, (size_t)c.vocab_size * c.dim * 2}; break;
+    case CE_LLAMA_KCACHE: *v = {m->kcache + L * m->layer_kv, m->layer_kv * 2}; break;
+    case CE_LLAMA_VCACHE: *v = {m->vcache + L * m->layer_kv, m->layer_kv * 2}; break;
+    case CE_LLAMA_LOGITS: *v = {m->logits, (size_t)m->B * c.vocab_size * 4}; break;
+    case CE_LLAMA_TOKENS: *v = {m->tokens, (size_t)m->B * 4}; break;
+    case CE_LLAMA_GENERATED: *v = {m->generated, (size_t)m->B * m->cap * 4}; break;
+    case CE_LLAMA_POS: *v = {m->pos, 4}; break;
+    case CE_LLAMA_RESIDUAL: *v = {m->x, (size_t)m->B * c.dim * 4}; break;
+    default: return set_error(CE_ERR_USAGE, format("unknown llama tensor %d", which));
+  }
+  return CE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ce_llama_validate(const ce_llama_config *c, int batch, int max_steps, int precision) {
+  CE_REQUIRE(c != nullptr, "null config");
+  CE_REQUIRE(c->dim >= 8 && c->dim % 8 == 0 && c->dim <= 8192, "dim must be a multiple of 8 in [8, 8192] (got %d)", c->dim);
+  CE_REQUIRE(c->hidden_dim >= 8 && c->hidden_dim % 8 == 0, "hidden_dim must be a positive multiple of 8 (got %d)", c->hidden_dim);
+  CE_REQUIRE(c->n_layers >= 1 && c->n_layers <= 1024, "n_layers must be in [1, 1024] (got %d)", c->n_layers);
+  CE_REQUIRE(c->n_heads >= 1 && c->dim % c->n_heads == 0, "n_heads must divide dim (dim %d, n_heads %d)", c->dim, c->n_heads);
+  CE_REQUIRE(c->n_kv_heads >= 1 && c->n_heads % c->n_kv_heads == 0, "n_kv_heads must divide n_heads (got %d, %d)", c->n_kv_heads, c->n_heads);
+  const int hs = c->dim / c->n_heads;
+  CE_REQUIRE(hs == 64 || hs == 128, "head size dim / n_heads must be 64 or 128 (got %d)", hs);
+  CE_REQUIRE(c->vocab_size >= 2, "vocab_size must be >= 2 (got %d)", c->vocab_size);
+  CE_REQUIRE(c->vocab_size % 4 == 0, "vocab_size must be a multiple of 4 (got %d)", c->vocab_size);
+  CE_REQUIRE(c->seq_len >= 1 && c->seq_len <= (1 << 20), "seq_len must be in [1, 2^20] (got %d)", c->seq_len);
+  CE_REQUIRE(batch >= 1 && batch <= 65535, "batch must be in [1, 65535] (got %d)", batch);
+  CE_REQUIRE(max_steps >= 1, "max_steps must be >= 1 (got %d)", max_steps);
+  CE_REQUIRE(precision == CE_PREC_BF16, "llama weight precision %d is not available", precision);
+  const double kv = 2.0 * c->n_layers * (double)batch * (c->dim / c->n_heads) * c->n_kv_heads * c->seq_len * 2;
+  const double w = 2.0 * ((double)c->n_layers * ((double)(c->dim + 2 * hs * c->n_kv_heads) * c->dim +
+                                                 (double)c->dim * c->dim + 3.0 * c->hidden_dim * c->dim) +
+                          2.0 * (double)c->vocab_size * c->dim);
+  CE_REQUIRE(kv + w <= 170.0 * (1LL << 30),
+             "model and KV cache need %.1f GiB of device memory (limit 170 GiB)", (kv + w) / (1LL << 30));
+  return CE_OK;
+}
+
+int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
+                    int precision, ce_stream_t stream) {
+  CE_REQUIRE(out != nullptr, "null model pointer");
+  *out = nullptr;
+  if (int rc = ce_llama_validate(cfg, batch, max_steps, precision)) return rc;
+  if (int rc = configure_attention()) return rc;
+  ce_llama *m = new ce_llama();
+  m->c = *cfg;
+  m->B = batch;
+  m->cap = max_steps;
+  m->precision = precision;
+  m->hs = cfg->dim / cfg->n_heads;
+  m->kv_dim = m->hs * cfg->n_kv_heads;
+  m->qkv_rows = cfg->dim + 2 * m->kv_dim;
+  m->chunk = kChunkBytes / (m->hs * 2);
+  m->nchunk = (cfg->seq_len + m->chunk - 1) / m->chunk;
+  m->nv = pow2_at_least((cfg->dim / 4 + kRowThreads - 1) / kRowThreads);
+  m->layer_kv = (size_t)batch * cfg->n_kv_heads * cfg->seq_len * m->hs;
+  const ce_llama_config &c = *cfg;
+  const size_t L = c.n_layers;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t e = cudaSuccess;
+#define CE_ALLOC(ptr, bytes)                           \
+  do {                                                 \
+    e = cudaMalloc(&(ptr), (bytes));                   \
+    if (e != cudaSuccess) {                            \
+      free_llama(m);                                   \
+      return cuda_error(e, "cudaMalloc(" #ptr ")");    \
+    }                                                  \
+  } while (0)
+  CE_ALLOC(m->tok_emb, (size_t)c.vocab_size * c.dim * 2);
+  CE_ALLOC(m->wqkv, L * wqkv_elems(m) * 2);
+  CE_ALLOC(m->wo, L * wo_elems(m) * 2);
+  CE_ALLOC(m->w13, L * w13_elems(m) * 2);
+  CE_ALLOC(m->w2, L * w2_elems(m) * 2);
+  CE_ALLOC(m->wcls, (size_t)c.vocab_size * c.dim * 2);
+  CE_ALLOC(m->rms_att, L * c.dim * 4);
+  CE_ALLOC(m->rms_ffn, L * c.dim * 4);
+  CE_ALLOC(m->rms_final, (size_t)c.dim * 4);
+  CE_ALLOC(m->rope, (size_t)c.seq_len * (m->hs / 2) * sizeof(float2));
+  CE_ALLOC(m->kcache, L * m->layer_kv * 2);
+  CE_ALLOC(m->vcache, L * m->layer_kv * 2);
+  CE_ALLOC(m->xb, (size_t)batch * c.dim * 2);
+  CE_ALLOC(m->att, (size_t)batch * c.dim * 2);
+  CE_ALLOC(m->hb, (size_t)batch * c.hidden_dim * 2);
+  CE_ALLOC(m->x, (size_t)batch * c.dim * 4);
+  CE_ALLOC(m->delta, (size_t)batch * c.dim * 4);
+  CE_ALLOC(m->qkv, (size_t)batch * m->qkv_rows * 4);
+  CE_ALLOC(m->h, (size_t)batch * 2 * c.hidden_dim * 4);
+  CE_ALLOC(m->logits, (size_t)batch * c.vocab_size * 4);
+  CE_ALLOC(m->part, (size_t)batch * c.n_heads * m->nchunk * (m->hs + 2) * 4);
+  CE_ALLOC(m->tokens, (size_t)batch * 4);
+  CE_ALLOC(m->generated, (size_t)batch * max_steps * 4);
+  CE_ALLOC(m->pos, 4);
+  CE_ALLOC(m->step, 4);
+#undef CE_ALLOC
+  // RoPE table: (cos, sin) of pos * 10000^(-2i/hs), computed in double once
+  std::vector<float2> table((size_t)c.seq_len * (m->hs / 2));
+  for (int p = 0; p < c.seq_len; ++p)
+    for (int i = 0; i < m->hs / 2; ++i) {
+      const double freq = std::pow(10000.0, -(2.0 * i) / (double)m->hs);
+      const double a = (double)p * freq;
+      table[(size_t)p * (m->hs / 2) + i] = make_float2((float)std::cos(a), (float)std::sin(a));
+    }
+  e = cudaMemcpyAsync(m->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->pos, 0, 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->step, 0, 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->generated, 0xFF, (size_t)batch * max_steps * 4, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // the host table goes out of scope
+  if (e != cudaSuccess) {
+    free_llama(m);
+    return cuda_error(e, "llama set-up");
+  }
+  *out = m;
+  return CE_OK;
+}
+
+int ce_llama_destroy(ce_llama *m) {
+  if (m) free_llama(m);
+  return CE_OK;
+}
+
+int ce_llama_init_random(ce_llama *m, uint64_t seed, float weight_std, int kv_fill, ce_stream_t stream) {
+  CE_REQUIRE(m != nullptr, "null model");
+  CE_REQUIRE(kv_fill >= 0 && kv_fill <= m->c.seq_len, "kv_fill must be in [0, seq_len] (got %d)", kv_fill);
+  cudaStream_t s = (cudaStream_t)stream;
+  const ce_llama_config &c = m->c;
+  const size_t L = c.n_layers;
+  const int grid = 4 * sm_count(), threads = 256;
+  struct Item {
+    uint16_t *p;
+    size_t n;
+    float std;
+  };
+  const Item items[] = {{m->tok_emb, (size_t)c.vocab_size * c.dim, weight_std},
+                        {m->wqkv, L * wqkv_elems(m), weight_std},
+                        {m->wo, L * wo_elems(m), weight_std},
+                        {m->w13, L * w13_elems(m), weight_std},
+                        {m->w2, L * w2_elems(m), weight_std},
+                        {m->wcls, (size_t)c.vocab_size * c.dim, weight_std}};
+  uint64_t stream_id = 1;
+  for (const Item &it : items) {
+    init_normal_bf16_kernel<<<grid, threads, 0, s>>>(it.p, it.n, seed, stream_id++, it.std, it.n, it.n);
+    CE_LAUNCH_CHECK("init_normal_bf16_kernel");
+  }
+  fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_att, L * c.dim, 1.0f);
+  fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_ffn, L * c.dim, 1.0f);
+  fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_final, (size_t)c.dim, 1.0f);
+  CE_LAUNCH_CHECK("fill_f32_kernel");
+  // KV cache: positions [0, kv_fill) of every (layer, sequence, head) N(0, 1)
+  CE_CUDA_TRY(cudaMemsetAsync(m->kcache, 0, L * m->layer_kv * 2, s));
+  CE_CUDA_TRY(cudaMemsetAsync(m->vcache, 0, L * m->layer_kv * 2, s));
+  if (kv_fill > 0) {
+    const size_t runs = L * m->B * c.n_kv_heads;  // contiguous [seq_len][hs] runs
+    const size_t run = (size_t)c.seq_len * m->hs, filled = (size_t)kv_fill * m->hs;
+    for (int which = 0; which < 2; ++which) {
+      init_normal_bf16_kernel<<<grid, threads, 0, s>>>(which ? m->vcache : m->kcache, runs * filled, seed,
+                                                       100 + which, 1.0f, run, filled);
+      CE_LAUNCH_CHECK("init_normal_bf16_kernel");
+    }
+  }
+  CE_CUDA_TRY(cudaStreamSynchronize(s));
+  return CE_OK;
+}
+
+int ce_llama_start(ce_llama *m, const int32_t *tokens_host, int pos, ce_stream_t stream) {
+  CE_REQUIRE(m != nullptr && tokens_host != nullptr, "null argument");
+  CE_REQUIRE(pos >= 0 && pos < m->c.seq_len, "pos must be in [0, seq_len) (got %d)", pos);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int zero = 0;
+  CE_CUDA_TRY(cudaMemcpyAsync(m->tokens, tokens_host, (size_t)m->B * 4, cudaMemcpyHostToDevice, s));
+  CE_CUDA_TRY(cudaMemcpyAsync(m->pos, &pos, 4, cudaMemcpyHostToDevice, s));
+  CE_CUDA_TRY(cudaMemcpyAsync(m->step, &zero, 4, cudaMemcpyHostToDevice, s));
+  CE_CUDA_TRY(cudaMemsetAsync(m->generated, 0xFF, (size_t)m->B * m->cap * 4, s));
+  CE_CUDA_TRY(cudaStreamSynchronize(s));
+  return CE_OK;
+}
+
+int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
+  CE_REQUIRE(m != nullptr, "null model");
+  cudaStream_t s = (cudaStream_t)stream;
+  const ce_llama_config &c = m->c;
+  const int B = m->B, D = c.dim, Hd = c.hidden_dim;
+  const float eps = 1e-5f;
+  auto norm = [&](const float *delta, const uint16_t *emb, const float *w) {
+    return launch_rows(m->nv, [&](auto nv) {
+      residual_rmsnorm_kernel<decltype(nv)::value><<<B, kRowThreads, 0, s>>>(
+          m->x, delta, emb, m->tokens, c.vocab_size, w, m->xb, D, eps);
+    });
+  };
+  const size_t attn_smem = attn_smem_bytes(m->chunk, m->hs);
+  for (int l = 0; l < c.n_layers; ++l) {
+    int rc = norm(l == 0 ? nullptr : m->delta, l == 0 ? m->tok_emb : nullptr, m->rms_att + (size_t)l * D);
+    if (rc) return rc;
+    CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
+    rc = gemm_bf16(m->qkv, m->xb, m->wqkv + l * wqkv_elems(m), B, m->qkv_rows, D, D, D, m->qkv_rows,
+                   nullptr, nullptr, 0, s);
+    if (rc) return rc;
+    uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
+    rope_append_kernel<<<B, 256, 0, s>>>(m->qkv, m->qkv_rows, kc, vc, m->rope, m->pos, D, m->kv_dim,
+                                         m->hs, c.n_kv_heads, c.seq_len);
+    CE_LAUNCH_CHECK("rope_append_kernel");
+    const dim3 agrid(m->nchunk, c.n_heads, B);
+    if (m->hs == 64) {
+      attn_chunk_kernel<64><<<agrid, kAttnThreads, attn_smem, s>>>(m->qkv, m->qkv_rows, kc, vc, m->pos, c.n_heads,
+                                                                   c.n_kv_heads, c.seq_len, m->chunk, m->nchunk, m->part);
+      CE_LAUNCH_CHECK("attn_chunk_kernel");
+      attn_combine_kernel<64><<<B * c.n_heads, 64, 0, s>>>(m->part, m->nchunk, c.n_heads, m->att, D);
+    } else {
+      attn_chunk_kernel<128><<<agrid, kAttnThreads, attn_smem, s>>>(m->qkv, m->qkv_rows, kc, vc, m->pos, c.n_heads,
+                                                                    c.n_kv_heads, c.seq_len, m->chunk, m->nchunk, m->part);
+      CE_LAUNCH_CHECK("attn_chunk_kernel");
+      attn_combine_kernel<128><<<B * c.n_heads, 128, 0, s>>>(m->part, m->nchunk, c.n_heads, m->att, D);
+    }
+    CE_LAUNCH_CHECK("attn_combine_kernel");
+    rc = gemm_bf16(m->delta, m->att, m->wo + l * wo_elems(m), B, D, D, D, D, D, nullptr, nullptr, 0, s);
+    if (rc) return rc;
+    rc = norm(m->delta, nullptr, m->rms_ffn + (size_t)l * D);
+    if (rc) return rc;
+    CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
+    rc = gemm_bf16(m->h, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, 2 * Hd, nullptr, nullptr, 0, s);
+    if (rc) return rc;
+    swiglu_kernel<<<4 * sm_count(), 256, 0, s>>>(m->h, m->hb, B, Hd);
+    CE_LAUNCH_CHECK("swiglu_kernel");
+    rc = gemm_bf16(m->delta, m->hb, m->w2 + l * w2_elems(m), B, D, Hd, Hd, Hd, D, nullptr, nullptr, 0, s);
+    if (rc) return rc;
+  }
+  int rc = norm(m->delta, nullptr, m->rms_final);
+  if (rc) return rc;
+  CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
+  rc = gemm_bf16(m->logits, m->xb, m->wcls, B, c.vocab_size, D, D, D, c.vocab_size, nullptr, nullptr, 0, s);
+  if (rc) return rc;
+  argmax_kernel<<<B, kRowThreads, 0, s>>>(m->logits, c.vocab_size, m->tokens, m->generated, m->cap, m->step);
+  CE_LAUNCH_CHECK("argmax_kernel");
+  advance_kernel<<<1, 1, 0, s>>>(m->pos, m->step);
+  CE_LAUNCH_CHECK("advance_kernel");
+  return CE_OK;
+}
+
+int ce_llama_read(ce_llama *m, int which, int layer, void *host, int64_t offset, int64_t bytes) {
+  CE_REQUIRE(m != nullptr && host != nullptr, "null argument");
+  TensorView v;
+  if (int rc = tensor_of(m, which, layer, &v)) return rc;
+  CE_REQUIRE(offset >= 0 && bytes >= 0 && (size_t)(offset + bytes) <= v.bytes,
+             "range [%lld, %lld) outside the tensor (%zu bytes)", (long long)offset, (long long)(offset + bytes), v.bytes);
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  CE_CUDA_TRY(cudaMemcpy(host, (uint8_t *)v.ptr + offset, (size_t)bytes, cudaMemcpyDeviceToHost));
+  return CE_OK;
+}
+
+int ce_llama_write(ce_llama *m, int which, int layer, const void *host, int64_t offset, int64_t bytes) {
+  CE_REQUIRE(m != nullptr && host != nullptr, "null argument");
+  TensorView v;
+  if (int rc = tensor_of(m, which, layer, &v)) return rc;
+  CE_REQUIRE(offset >= 0 && bytes >= 0 && (size_t)(offset + bytes) <= v.bytes,
+             "range [%lld, %lld) outside the tensor (%zu bytes)", (long long)offset, (long long)(offset + bytes), v.bytes);
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  CE_CUDA_TRY(cudaMemcpy((uint8_t *)v.ptr + offset, host, (size_t)bytes, cudaMemcpyHostToDevice));
+  return CE_OK;
+}
+
+// Reads and clears the status word of the decode kernels (position out of
+// the cache, or a staging wait that gave up); synchronizes the device.
+int ce_llama_status(void) {
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  DeviceStatus h{};
+  CE_CUDA_TRY(cudaMemcpyFromSymbol(&h, g_llama_status, sizeof(h)));
+  if (h.code == 0) return CE_OK;
+  const DeviceStatus zero{};
+  CE_CUDA_TRY(cudaMemcpyToSymbol(g_llama_status, &zero, sizeof(zero)));
+  if (h.where == 900u) return set_error(CE_ERR_USAGE, "decode position reached the end of the KV cache");
+  return set_error(CE_ERR_TIMEOUT, format("attention staging wait gave up (site %u, block %u)", h.where, h.block));
+}
+
+}  // extern "C"

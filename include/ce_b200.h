@@ -390,6 +390,82 @@ int ce_decoder_copy_outputs(ce_decoder *dec, int from_device, int32_t *generated
  * nothing; 2 and 3 are applied by the caller to its diagnostics copy. */
 int ce_decoder_inject_fault(ce_decoder *dec, int fault);
 
+/* ---------------------------------------------------------------------------
+ * Llama-2 decoder step (the full transformer of the north star's "loom_private
+ * llama2c decoder step": attention over the KV cache, SwiGLU FFN, classifier;
+ * the reference runs only its final rmsnorm -> classifier -> argmax stage,
+ * applications/loom_private/decoder/decoder.cu:267-296). Batched greedy decode:
+ * every sequence of the batch is at the same position. Weights bf16
+ * [out][in], residual stream fp32, KV cache bf16 [layer][batch][kv_head]
+ * [seq_len][head_size]. Field names follow llama2.c's Config.
+ */
+typedef struct ce_llama ce_llama;
+
+typedef struct ce_llama_config {
+  int32_t dim;        /* model width; multiple of 8 */
+  int32_t hidden_dim; /* SwiGLU width; multiple of 8 */
+  int32_t n_layers;
+  int32_t n_heads;    /* head size dim / n_heads must be 64 or 128 */
+  int32_t n_kv_heads; /* divides n_heads (grouped-query attention) */
+  int32_t vocab_size; /* multiple of 4 */
+  int32_t seq_len;    /* KV cache positions */
+} ce_llama_config;
+
+/* Tensors readable / writable through ce_llama_read / ce_llama_write. */
+#define CE_LLAMA_TOK_EMB 0    /* bf16 [vocab][dim] */
+#define CE_LLAMA_WQKV 1       /* bf16 [dim + 2 kv_dim][dim] of a layer: rows q, k, v */
+#define CE_LLAMA_WO 2         /* bf16 [dim][dim] of a layer */
+#define CE_LLAMA_W13 3        /* bf16 [2 hidden][dim] of a layer: rows w1, w3 */
+#define CE_LLAMA_W2 4         /* bf16 [dim][hidden] of a layer */
+#define CE_LLAMA_RMS_ATT 5    /* fp32 [dim] of a layer */
+#define CE_LLAMA_RMS_FFN 6    /* fp32 [dim] of a layer */
+#define CE_LLAMA_RMS_FINAL 7  /* fp32 [dim] */
+#define CE_LLAMA_WCLS 8       /* bf16 [vocab][dim] */
+#define CE_LLAMA_KCACHE 9     /* bf16 [batch][kv_heads][seq_len][head_size] of a layer */
+#define CE_LLAMA_VCACHE 10    /* same */
+#define CE_LLAMA_LOGITS 11    /* fp32 [batch][vocab] of the last step */
+#define CE_LLAMA_TOKENS 12    /* int32 [batch]: current token of each sequence */
+#define CE_LLAMA_GENERATED 13 /* int32 [batch][max_steps]: token of each step (-1 unset) */
+#define CE_LLAMA_POS 14       /* int32: position of the next step */
+#define CE_LLAMA_RESIDUAL 15  /* fp32 [batch][dim]: residual stream after the last layer */
+
+/* Shape and memory checks of ce_llama_create alone (no CUDA call). */
+int ce_llama_validate(const ce_llama_config *cfg, int batch, int max_steps, int precision);
+
+/* Allocates weights, KV cache and buffers for `batch` sequences and up to
+ * max_steps generated tokens per start; precision CE_PREC_BF16. */
+int ce_llama_create(ce_llama **model, const ce_llama_config *cfg, int batch, int max_steps,
+                    int precision, ce_stream_t stream);
+int ce_llama_destroy(ce_llama *model);
+
+/* Random model on the device: every matrix N(0, weight_std) (bf16), RMSNorm
+ * weights 1, and KV positions [0, kv_fill) of every layer, sequence and head
+ * N(0, 1) (bf16), the rest of the cache 0. Deterministic in seed. */
+int ce_llama_init_random(ce_llama *model, uint64_t seed, float weight_std, int kv_fill,
+                         ce_stream_t stream);
+
+/* Sets the current token of every sequence (host int32 [batch]) and the
+ * position of the next step, and clears the generated tokens. Synchronous. */
+int ce_llama_start(ce_llama *model, const int32_t *tokens_host, int pos, ce_stream_t stream);
+
+/* One decode step for the whole batch: reads each sequence's current token
+ * and the device position, appends k and v at that position, writes the
+ * logits, the greedy next token (first maximum) into the current tokens and
+ * generated[b][step], and advances position and step on the device.
+ * Capturable: a captured step replays for every token. */
+int ce_llama_enqueue_step(ce_llama *model, ce_stream_t stream);
+
+/* Synchronous copies of a byte range of a tensor (CE_LLAMA_*; layer for the
+ * per-layer ones) to and from host memory. */
+int ce_llama_read(ce_llama *model, int which, int layer, void *host, int64_t offset, int64_t bytes);
+int ce_llama_write(ce_llama *model, int which, int layer, const void *host, int64_t offset,
+                   int64_t bytes);
+
+/* Reads and clears the decode kernels' status word: CE_OK, CE_ERR_USAGE when
+ * a step ran past the end of the KV cache, CE_ERR_TIMEOUT when a staging wait
+ * gave up. Synchronizes the device. */
+int ce_llama_status(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,158 @@
+"""CPU oracle of the Llama-2 decoder step -- TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may
+import this module, and only as the checker (or the timed CPU baseline).
+
+Parity unpinned: the reference has no transformer (its loom_private decoder
+runs only the final rmsnorm -> classifier -> argmax stage,
+applications/loom_private/decoder/decoder.cu:267-296, and llama2.c's run.c,
+whose forward() the reference cites by hash only, is not in the reference
+tree). This is a restatement of the standard Llama-2 decoder mathematics in
+float64 numpy:
+
+  x = embedding[token]
+  per layer: xb = rmsnorm(x, w_att); q, k, v = xb Wq^T, xb Wk^T, xb Wv^T;
+             RoPE rotates each (even, odd) pair at head-dimension index j by
+             pos * 10000^(-j / head_size); k, v appended to the cache;
+             per head: softmax(q k^T / sqrt(head_size)) over positions 0..pos, times v;
+             x += att Wo^T; xb = rmsnorm(x, w_ffn);
+             x += (silu(xb W1^T) * (xb W3^T)) W2^T,  silu(g) = g / (1 + e^-g)
+  logits = rmsnorm(x, w_final) Wcls^T; next token = first argmax
+  rmsnorm(x, w) = w * x / sqrt(mean(x^2) + 1e-5)
+
+It rounds to bf16 at the points where the device path stores bf16 (the GEMM
+operands: normalized rows, attention output, SwiGLU product; the appended
+k and v), so the comparison measures the device's arithmetic, not the
+format. Weights and the initial KV cache are inputs copied from the device.
+"""
+import numpy as np
+
+from .oracle import bf16_bits, bf16_value
+
+EPS = 1e-5
+
+
+def bf16_round(x):
+    """Values rounded to bf16 (through float32, as the device rounds its fp32
+    values), returned as float64."""
+    return bf16_value(bf16_bits(np.asarray(x, np.float32))).astype(np.float64)
+
+
+def to64(bits):
+    return bf16_value(bits).astype(np.float64)
+
+
+def rmsnorm(x, w):
+    return w * (x / np.sqrt((x * x).mean(axis=-1, keepdims=True) + EPS))
+
+
+def rope_angles(pos, hs):
+    """(cos, sin) of pos * 10000^(-2i / hs), i < hs / 2."""
+    i = np.arange(hs // 2, dtype=np.float64)
+    a = pos * np.power(10000.0, -2.0 * i / hs)
+    return np.cos(a), np.sin(a)
+
+
+def rope(v, pos, hs):
+    """Rotates the (even, odd) pairs of v [..., n * hs] head by head."""
+    c, s = rope_angles(pos, hs)
+    shp = v.shape
+    w = v.reshape(shp[:-1] + (shp[-1] // hs, hs // 2, 2))
+    e, o = w[..., 0], w[..., 1]
+    out = np.empty_like(w)
+    out[..., 0] = e * c - o * s
+    out[..., 1] = e * s + o * c
+    return out.reshape(shp)
+
+
+class LlamaOracle:
+    """Teacher-forced greedy decoding of a few sequences.
+
+    cfg: dict with dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size,
+    seq_len. weights: the device weights as host arrays (bf16 bits for the
+    matrices, fp32 RMSNorm weights), as Llama.weights() returns them.
+    """
+
+    def __init__(self, cfg, weights):
+        self.c = dict(cfg)
+        self.hs = self.c["dim"] // self.c["n_heads"]
+        self.kv_dim = self.hs * self.c["n_kv_heads"]
+        self.emb = to64(weights["tok_emb"])
+        self.wcls = to64(weights["wcls"])
+        self.rms_final = np.asarray(weights["rms_final"], np.float64)
+        self.wqkv = [to64(w) for w in weights["wqkv"]]
+        self.wo = [to64(w) for w in weights["wo"]]
+        self.w13 = [to64(w) for w in weights["w13"]]
+        self.w2 = [to64(w) for w in weights["w2"]]
+        self.rms_att = [np.asarray(w, np.float64) for w in weights["rms_att"]]
+        self.rms_ffn = [np.asarray(w, np.float64) for w in weights["rms_ffn"]]
+
+    def step(self, tokens, pos, kcache, vcache):
+        """One decode step of the sequences whose current tokens are given.
+
+        kcache, vcache: per layer float64 [n][kv_heads][seq_len][hs] (bf16
+        values), updated in place at pos. Returns logits [n][vocab]."""
+        c, hs = self.c, self.hs
+        D, Hd, H, KH = c["dim"], c["hidden_dim"], c["n_heads"], c["n_kv_heads"]
+        x = self.emb[np.asarray(tokens)]
+        group = H // KH
+        for l in range(c["n_layers"]):
+            xb = bf16_round(rmsnorm(x, self.rms_att[l]))
+            qkv = xb @ self.wqkv[l].T
+            q = rope(qkv[:, :D], pos, hs)
+            k = rope(qkv[:, D:D + self.kv_dim], pos, hs)
+            v = qkv[:, D + self.kv_dim:]
+            n = x.shape[0]
+            kcache[l][:, :, pos, :] = bf16_round(k).reshape(n, KH, hs)
+            vcache[l][:, :, pos, :] = bf16_round(v).reshape(n, KH, hs)
+            qh = q.reshape(n, H, hs)
+            att = np.empty((n, H, hs))
+            for h in range(H):
+                kh = h // group
+                keys = kcache[l][:, kh, :pos + 1, :]          # [n][pos+1][hs]
+                vals = vcache[l][:, kh, :pos + 1, :]
+                s = np.einsum("nd,ntd->nt", qh[:, h, :], keys) / np.sqrt(hs)
+                p = np.exp(s - s.max(axis=1, keepdims=True))
+                p /= p.sum(axis=1, keepdims=True)
+                att[:, h, :] = np.einsum("nt,ntd->nd", p, vals)
+            x = x + bf16_round(att.reshape(n, D)) @ self.wo[l].T
+            xb = bf16_round(rmsnorm(x, self.rms_ffn[l]))
+            hh = xb @ self.w13[l].T
+            g, u = hh[:, :Hd], hh[:, Hd:]
+            x = x + bf16_round(g / (1.0 + np.exp(-g)) * u) @ self.w2[l].T
+        return bf16_round(rmsnorm(x, self.rms_final)) @ self.wcls.T
+
+    def decode(self, tokens0, pos0, forced, kcache, vcache):
+        """Teacher-forced decode: step s feeds tokens0 (s = 0) or forced[:, s-1].
+        Returns (logits [S][n][vocab], argmax [S][n], top-2 gap [S][n])."""
+        forced = np.asarray(forced)
+        S = forced.shape[1]
+        logits, best, gap = [], [], []
+        tok = np.asarray(tokens0)
+        for s in range(S):
+            lg = self.step(tok, pos0 + s, kcache, vcache)
+            top2 = np.sort(lg, axis=1)[:, -2:]
+            logits.append(lg)
+            best.append(np.argmax(lg, axis=1))  # first maximum
+            gap.append(top2[:, 1] - top2[:, 0])
+            tok = forced[:, s]
+        return np.stack(logits), np.stack(best), np.stack(gap)
+
+
+def cache_from_device(model, seqs, positions):
+    """Per layer float64 [n][kv_heads][seq_len][hs] K and V caches of the given
+    sequences, with device positions [0, positions) copied in."""
+    import importlib
+    ce = importlib.import_module("cuda_elastic_b200")
+    c = model.cfg
+    kc, vc = [], []
+    for l in range(c.n_layers):
+        k = np.zeros((len(seqs), c.n_kv_heads, c.seq_len, model.hs))
+        v = np.zeros_like(k)
+        for i, b in enumerate(seqs):
+            if positions > 0:
+                k[i, :, :positions] = to64(model.cache_rows(l, b, ce.LLAMA_KCACHE, positions))
+                v[i, :, :positions] = to64(model.cache_rows(l, b, ce.LLAMA_VCACHE, positions))
+        kc.append(k)
+        vc.append(v)
+    return kc, vc
