@@ -109,6 +109,7 @@ _SIGNATURES = {
     "ce_decoder_poison": [_vp, _vp],
     "ce_decoder_copy_outputs": [_vp, _i, _vp, _vp, _vp, _vp],
     "ce_decoder_inject_fault": [_vp, _i],
+    "ce_gemm_bf16_split": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _vp],
     "ce_llama_validate": [_vp, _i, _i, _i],
     "ce_llama_create": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _vp],
     "ce_llama_destroy": [_vp],
@@ -268,6 +269,17 @@ def gemm_bf16(d, a, b, k=None, tile_n=0, stream=None):
     K = lda if k is None else k
     check(lib().ce_gemm_bf16_tile(_ptr(d), _ptr(a), _ptr(b), M, N, K, lda, ldb, d.shape[1], tile_n,
                                   _stream(stream)))
+    return d
+
+
+def gemm_bf16_split(d, a, b, splits, stream=None):
+    """Split-K bf16 GEMM: d [splits][M][N] fp32 receives one partial per split
+    (their sum is A B^T)."""
+    M, lda = a.shape
+    N, ldb = b.shape
+    assert d.shape == (splits, M, N)
+    check(lib().ce_gemm_bf16_split(_ptr(d), _ptr(a), _ptr(b), M, N, lda, lda, ldb, N, splits, M * N,
+                                   _stream(stream)))
     return d
 
 

@@ -31,6 +31,8 @@ int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int
               cudaStream_t s, int force_group = 0);
 int gemm_simt_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda,
                    int ldb, int ldd, cudaStream_t s);
+int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s);
 int gemm_status();
 int gemm_bs_status();
 int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
@@ -318,6 +320,12 @@ int ce_gemm_config(int precision, float *d, const void *a, const void *b, int M,
     return gemm_e4m3(d, static_cast<const uint8_t *>(a), static_cast<const uint8_t *>(b), M, N, K,
                      lda, ldb, ldd, nullptr, nullptr, tile_n, (cudaStream_t)stream, cta_group);
   return set_error(CE_ERR_USAGE, format("ce_gemm_config: precision %d has no tensor-core kernel", precision));
+}
+
+int ce_gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+                       int ldb, int ldd, int splits, int64_t split_stride, ce_stream_t stream) {
+  return gemm_bf16_split(d, a, b, M, N, K, lda, ldb, ldd, splits, (long long)split_stride,
+                         (cudaStream_t)stream);
 }
 
 int ce_gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,

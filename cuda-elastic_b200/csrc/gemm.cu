@@ -84,7 +84,27 @@ struct GemmArgs {
   int M, N, K, ldd;
   int tiles_m, tiles_n, k_blocks;
   int prefetch;  // L2 prefetch distance in k-blocks (0 = none)
+  int splits;    // k ranges per tile (split-K); split s writes d + s * split_stride
+  long long split_stride;
 };
+
+// Work unit u of a launch: output tile u % tiles, k-block range of split
+// u / tiles (balanced, never empty: splits <= k_blocks).
+struct Unit {
+  int tile, kb0, kb1;
+  float *d;
+};
+
+__device__ __forceinline__ Unit unit_of(const GemmArgs &args, int u) {
+  const int tiles = args.tiles_m * args.tiles_n;
+  const int split = u / tiles;
+  Unit w;
+  w.tile = u - split * tiles;
+  w.kb0 = (int)((long long)split * args.k_blocks / args.splits);
+  w.kb1 = (int)((long long)(split + 1) * args.k_blocks / args.splits);
+  w.d = args.d + (size_t)split * (size_t)args.split_stride;
+  return w;
+}
 
 template <int kKind, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -109,7 +129,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
   DeviceStatus *st = &g_gemm_status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int num_tiles = args.tiles_m * args.tiles_n * args.splits;  // work units
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::stages; ++s) {
@@ -141,9 +161,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     uint32_t issued_mask = 0, issued_parity = 0;
     bool okay = true;
     for (int t = blockIdx.x; t < num_tiles && okay; t += gridDim.x) {
-      const int m0 = (t % args.tiles_m) * BM;
-      const int n0 = (t / args.tiles_m) * BN;
-      for (int kb = 0; kb < args.k_blocks; ++kb) {
+      const Unit w = unit_of(args, t);
+      const int m0 = (w.tile % args.tiles_m) * BM;
+      const int n0 = (w.tile / args.tiles_m) * BN;
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (!warp_wait(&empty[stage], phase ^ 1u, st, 1)) {
           okay = false;
           break;
@@ -151,7 +172,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         if (lane == 0) {
           uint8_t *a_dst = smem + stage * S::stage_bytes;
           uint8_t *b_dst = a_dst + S::a_bytes;
-          if (args.prefetch > 0 && kb + args.prefetch < args.k_blocks) {
+          if (args.prefetch > 0 && kb + args.prefetch < w.kb1) {
             tma_prefetch_2d(&tmA, (kb + args.prefetch) * kElemsPerRow, m0);
             tma_prefetch_2d(&tmB, (kb + args.prefetch) * kElemsPerRow, n0);
           }
@@ -183,7 +204,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       if (!warp_wait(&tmem_empty[acc], acc_phase ^ 1u, st, 3)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + (uint32_t)acc * kAccStride;
-      for (int kb = 0; kb < args.k_blocks; ++kb) {
+      const Unit w = unit_of(args, t);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (!warp_wait(&full[stage], phase, st, 4)) {
           okay = false;
           break;
@@ -196,7 +218,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           for (int k = 0; k < kMmasPerStage; ++k) {
             const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32);
             const uint64_t b_desc = smem_desc_sw128(b_addr + k * 32);
-            tc_mma<kKind>(d_tmem, a_desc, b_desc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+            tc_mma<kKind>(d_tmem, a_desc, b_desc, kIdesc, ((kb - w.kb0) | k) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
         }
@@ -222,12 +244,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!warp_wait(&tmem_full[acc], acc_phase, st, 6)) break;
       tc_fence_after();
-      const int m0 = (t % args.tiles_m) * BM;
-      const int n0 = (t / args.tiles_m) * BN;
+      const Unit w = unit_of(args, t);
+      const int m0 = (w.tile % args.tiles_m) * BM;
+      const int n0 = (w.tile / args.tiles_m) * BN;
       const int row = m0 + quarter * 32 + lane;
       const float rs = (args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f;
-      float *drow = args.d + (size_t)row * args.ldd;
-      const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.d) & 15u) == 0);
+      float *drow = w.d + (size_t)row * args.ldd;
+      const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(w.d) & 15u) == 0);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -319,7 +342,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   DeviceStatus *st = &g_gemm_status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();  // 0 issues the MMAs
-  const int num_tiles = args.tiles_m * args.tiles_n;
+  const int num_tiles = args.tiles_m * args.tiles_n * args.splits;  // work units
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
 
   if (threadIdx.x == 0) {
@@ -354,9 +377,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint32_t issued_mask = 0, issued_parity = 0;
     bool okay = true;
     for (int t = pair; t < num_tiles && okay; t += npairs) {
-      const int m0 = (t % args.tiles_m) * (2 * BM) + (int)rank * BM;
-      const int n0 = (t / args.tiles_m) * BN + (int)rank * (BN / 2);
-      for (int kb = 0; kb < args.k_blocks; ++kb) {
+      const Unit w = unit_of(args, t);
+      const int m0 = (w.tile % args.tiles_m) * (2 * BM) + (int)rank * BM;
+      const int n0 = (w.tile / args.tiles_m) * BN + (int)rank * (BN / 2);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (!warp_wait_cluster(&empty[stage], phase ^ 1u, st, 11)) {
           okay = false;
           break;
@@ -364,7 +388,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (lane == 0) {
           uint8_t *a_dst = smem + stage * S::stage_bytes;
           uint8_t *b_dst = a_dst + S::a_bytes;
-          if (args.prefetch > 0 && kb + args.prefetch < args.k_blocks) {
+          if (args.prefetch > 0 && kb + args.prefetch < w.kb1) {
             tma_prefetch_2d(&tmA, (kb + args.prefetch) * kElemsPerRow, m0);
             tma_prefetch_2d(&tmB, (kb + args.prefetch) * kElemsPerRow, n0);
           }
@@ -400,7 +424,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (!warp_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, st, 13)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)acc * kAccStride;
-        for (int kb = 0; kb < args.k_blocks; ++kb) {
+        const Unit w = unit_of(args, t);
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!warp_wait_cluster(&full[stage], phase, st, 14)) {
             okay = false;
             break;
@@ -413,7 +438,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             for (int k = 0; k < kMmasPerStage; ++k) {
               const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32);
               const uint64_t b_desc = smem_desc_sw128(b_addr + k * 32);
-              tc_mma_pair<kKind>(d_tmem, a_desc, b_desc, kIdesc, (kb | k) != 0 ? 1u : 0u);
+              tc_mma_pair<kKind>(d_tmem, a_desc, b_desc, kIdesc, ((kb - w.kb0) | k) != 0 ? 1u : 0u);
             }
             const uint32_t e = smem_u32(&empty[stage]);
             tc_commit_pair(cluster_map(e, 0));
@@ -445,12 +470,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!warp_wait_cluster(&tmem_full[acc], acc_phase, st, 16)) break;
       tc_fence_after();
-      const int m0 = (t % args.tiles_m) * (2 * BM) + (int)rank * BM;
-      const int n0 = (t / args.tiles_m) * BN;
+      const Unit w = unit_of(args, t);
+      const int m0 = (w.tile % args.tiles_m) * (2 * BM) + (int)rank * BM;
+      const int n0 = (w.tile / args.tiles_m) * BN;
       const int row = m0 + quarter * 32 + lane;
       const float rs = (args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f;
-      float *drow = args.d + (size_t)row * args.ldd;
-      const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(args.d) & 15u) == 0);
+      float *drow = w.d + (size_t)row * args.ldd;
+      const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(w.d) & 15u) == 0);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 32) {
         uint32_t r[32];
@@ -575,7 +601,10 @@ struct GemmChoice {
 int g_prefetch_kblocks = 0;  // set by ce_gemm_tuning (setup time)
 
 GemmChoice choose_tiles(int M, int N, int sms) {
-  static const int kCandidates[] = {256, 224, 192, 160, 128};
+  // 96- and 64-wide tiles only enter when 128-wide tiles cannot give every
+  // SM (or SM pair) a tile: decode-sized GEMMs (few rows, narrow N), where
+  // more CTAs streaming the weights beat fewer wide tiles.
+  static const int kCandidates[] = {256, 224, 192, 160, 128, 96, 64};
   GemmChoice best{0, 256};
   double best_cost = -1;
   for (int pair = 0; pair < 2; ++pair) {
@@ -584,7 +613,9 @@ GemmChoice choose_tiles(int M, int N, int sms) {
     const double eff = pair ? 0.85 : 0.67;
     if (pair && M <= BM) continue;
     const long long tiles_m = (M + rows - 1) / rows;
+    const bool narrow_ok = tiles_m * ((N + 127) / 128) < units;
     for (int bn : kCandidates) {
+      if (bn < 128 && !narrow_ok) continue;
       const long long tiles = tiles_m * ((N + bn - 1) / bn);
       const long long waves = (tiles + units - 1) / units;
       const double cost = (double)(waves * bn) / eff;
@@ -600,7 +631,7 @@ GemmChoice choose_tiles(int M, int N, int sms) {
 template <int kKind>
 int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
                   int ldd, const float *row_scale, const float *col_scale, int force_bn,
-                  int force_group, cudaStream_t s) {
+                  int force_group, cudaStream_t s, int splits = 1, long long split_stride = 0) {
   constexpr int elem = Kind<kKind>::elem;
   const CUtensorMapDataType dt = kKind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : kKind == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -614,9 +645,14 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   CE_REQUIRE(d != nullptr, "null output");
   CE_REQUIRE(force_group == 0 || force_group == 1 || force_group == 2,
              "cta group must be 0 (automatic), 1 or 2 (got %d)", force_group);
-  CE_REQUIRE(force_bn == 0 || force_bn == 128 || force_bn == 160 || force_bn == 192 ||
-                 force_bn == 224 || force_bn == 256,
-             "tile width must be 0, 128, 160, 192, 224 or 256 (got %d)", force_bn);
+  CE_REQUIRE(force_bn == 0 || force_bn == 64 || force_bn == 96 || force_bn == 128 || force_bn == 160 ||
+                 force_bn == 192 || force_bn == 224 || force_bn == 256,
+             "tile width must be 0, 64, 96, 128, 160, 192, 224 or 256 (got %d)", force_bn);
+  const int k_blocks_all = (K + (kRowBytes / elem) - 1) / (kRowBytes / elem);
+  CE_REQUIRE(splits >= 1 && splits <= k_blocks_all,
+             "split count must be in [1, %d] for K = %d (got %d)", k_blocks_all, K, splits);
+  CE_REQUIRE(splits == 1 || split_stride >= (long long)(M - 1) * ldd + N,
+             "split stride %lld is smaller than one output", split_stride);
   if (!is_sm100()) return set_error(CE_ERR_USAGE, "tcgen05 GEMM needs an sm_100 device");
   const int sms = sm_count();
   GemmChoice c = choose_tiles(M, N, sms);
@@ -640,7 +676,9 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.tiles_n = (N + c.bn - 1) / c.bn;
   args.k_blocks = (K + (kRowBytes / elem) - 1) / (kRowBytes / elem);
   args.prefetch = g_prefetch_kblocks;
-  const int tiles = args.tiles_m * args.tiles_n;
+  args.splits = splits;
+  args.split_stride = splits > 1 ? split_stride : 0;
+  const int tiles = args.tiles_m * args.tiles_n * splits;
   if (c.pair) {
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
     const int grid = 2 * pairs;
@@ -650,6 +688,8 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
       case 192: return launch_gemm_pair<kKind, 192>(ta, tb, args, grid, s);
       case 160: return launch_gemm_pair<kKind, 160>(ta, tb, args, grid, s);
       case 128: return launch_gemm_pair<kKind, 128>(ta, tb, args, grid, s);
+      case 96: return launch_gemm_pair<kKind, 96>(ta, tb, args, grid, s);
+      case 64: return launch_gemm_pair<kKind, 64>(ta, tb, args, grid, s);
     }
   } else {
     const int grid = tiles < sms ? tiles : sms;
@@ -659,6 +699,8 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
       case 192: return launch_gemm<kKind, 192>(ta, tb, args, grid, s);
       case 160: return launch_gemm<kKind, 160>(ta, tb, args, grid, s);
       case 128: return launch_gemm<kKind, 128>(ta, tb, args, grid, s);
+      case 96: return launch_gemm<kKind, 96>(ta, tb, args, grid, s);
+      case 64: return launch_gemm<kKind, 64>(ta, tb, args, grid, s);
     }
   }
   return set_error(CE_ERR_USAGE, format("unsupported tile width %d", c.bn));
@@ -685,6 +727,33 @@ int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K,
               cudaStream_t s, int force_group) {
   return gemm_dispatch<2>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, force_bn,
                           force_group, s);
+}
+
+// Split-K bf16 GEMM: split s of `splits` accumulates its balanced range of
+// k-blocks and writes its fp32 partial at d + s * split_stride; the caller
+// sums the partials (in split order, so the result is deterministic).
+int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s) {
+  return gemm_dispatch<0>(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, 0, s, splits,
+                          split_stride);
+}
+
+// Split count that fills the SMs for a bf16 GEMM of this shape: the tiles
+// of the automatic choice, times splits, up to one wave, with at least
+// min_kblocks k-blocks per split; at most max_splits.
+int gemm_bf16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks) {
+  const int sms = sm_count();
+  if (sms <= 0) return 1;
+  const GemmChoice c = choose_tiles(M, N, sms);
+  const int rows = c.pair ? 2 * BM : BM;
+  const int units = c.pair ? sms / 2 : sms;
+  const long long tiles = (long long)((M + rows - 1) / rows) * ((N + c.bn - 1) / c.bn);
+  const int k_blocks = (K + 63) / 64;
+  long long sp = units / (tiles > 0 ? tiles : 1);
+  sp = sp < (long long)max_splits ? sp : (long long)max_splits;
+  const long long by_k = k_blocks / (min_kblocks > 0 ? min_kblocks : 1);
+  sp = sp < by_k ? sp : by_k;
+  return sp < 1 ? 1 : (int)sp;
 }
 
 int gemm_set_prefetch(int kblocks) {

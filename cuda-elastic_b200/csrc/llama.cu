@@ -37,6 +37,9 @@ namespace ce {
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
               cudaStream_t s, int force_group = 0);
+int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
+                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s);
+int gemm_bf16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
 
 static __device__ DeviceStatus g_llama_status;
 
@@ -87,13 +90,15 @@ __global__ void fill_f32_kernel(float *out, size_t n, float v) {
 }
 
 // One row of the residual stream per block: x = embedding[token] (first
-// layer), or x += delta (after a sublayer), then xb = bf16(w * (x * scale)),
+// layer), or x += delta (after a sublayer; delta is the sum of nsplit
+// split-K partials split_stride floats apart), then xb = bf16(w * (x * scale)),
 // scale = 1 / sqrtf(sum(x^2) / dim + eps). An out-of-range token makes the
 // row NaN so the failure shows in every output.
 template <int NV>
 __global__ void __launch_bounds__(kRowThreads)
-residual_rmsnorm_kernel(float *x, const float *delta, const uint16_t *emb, const int *tokens,
-                        int vocab, const float *w, uint16_t *xb, int dim, float eps) {
+residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_stride,
+                        const uint16_t *emb, const int *tokens, int vocab, const float *w,
+                        uint16_t *xb, int dim, float eps) {
   __shared__ float scratch[32];
   const int b = blockIdx.x, cols4 = dim / 4;
   float4 *xr = reinterpret_cast<float4 *>(x + (size_t)b * dim);
@@ -121,7 +126,12 @@ residual_rmsnorm_kernel(float *x, const float *delta, const uint16_t *emb, const
       if (i < cols4) {
         v[j] = xr[i];
         if (dr) {
-          const float4 d = dr[i];
+          // the sublayer's output: its split-K partials summed in split order
+          float4 d = dr[i];
+          for (int sp = 1; sp < nsplit; ++sp) {
+            const float4 e = dr[i + sp * (split_stride / 4)];
+            d.x += e.x, d.y += e.y, d.z += e.z, d.w += e.w;
+          }
           v[j].x += d.x, v[j].y += d.y, v[j].z += d.z, v[j].w += d.w;
           xr[i] = v[j];
         }
@@ -153,9 +163,10 @@ residual_rmsnorm_kernel(float *x, const float *delta, const uint16_t *emb, const
 // RoPE on q and k of one sequence (in place in the fp32 QKV rows), then k
 // and v to the bf16 cache at the current position. rope holds (cos, sin) of
 // pos * 10000^(-2i/hs) for every position and pair index i.
-__global__ void rope_append_kernel(float *qkv, int ld_qkv, uint16_t *kcache, uint16_t *vcache,
-                                   const float2 *rope, const int *pos_ptr, int dim, int kv_dim,
-                                   int hs, int kv_heads, int seq_len) {
+__global__ void rope_append_kernel(float *qkv, int ld_qkv, int nsplit, size_t split_stride,
+                                   uint16_t *kcache, uint16_t *vcache, const float2 *rope,
+                                   const int *pos_ptr, int dim, int kv_dim, int hs, int kv_heads,
+                                   int seq_len) {
   const int b = blockIdx.x;
   const int pos = *pos_ptr;
   if (pos < 0 || pos >= seq_len) {
@@ -163,22 +174,31 @@ __global__ void rope_append_kernel(float *qkv, int ld_qkv, uint16_t *kcache, uin
     return;
   }
   float *row = qkv + (size_t)b * ld_qkv;
+  // pair i of the QKV row: its split-K partials summed in split order
+  auto pair_at = [&](int i) {
+    float2 v = *reinterpret_cast<const float2 *>(row + i);
+    for (int sp = 1; sp < nsplit; ++sp) {
+      const float2 e = *reinterpret_cast<const float2 *>(row + sp * split_stride + i);
+      v.x += e.x, v.y += e.y;
+    }
+    return v;
+  };
   const float2 *rp = rope + (size_t)pos * (hs / 2);
   for (int p = threadIdx.x; p < dim / 2; p += blockDim.x) {
     const int i = 2 * p;
     const float2 cs = rp[(i % hs) / 2];
-    const float q0 = row[i], q1 = row[i + 1];
-    row[i] = q0 * cs.x - q1 * cs.y;
-    row[i + 1] = q0 * cs.y + q1 * cs.x;
+    const float2 q = pair_at(i);
+    row[i] = q.x * cs.x - q.y * cs.y;  // rotated q, read by the attention from partial 0
+    row[i + 1] = q.x * cs.y + q.y * cs.x;
   }
   const size_t per_head = (size_t)seq_len * hs;
   for (int p = threadIdx.x; p < kv_dim / 2; p += blockDim.x) {
     const int i = 2 * p, kh = i / hs, d = i % hs;
     const float2 cs = rp[d / 2];
-    const float k0 = row[dim + i], k1 = row[dim + i + 1];
+    const float2 k = pair_at(dim + i), v = pair_at(dim + kv_dim + i);
     const size_t at = ((size_t)b * kv_heads + kh) * per_head + (size_t)pos * hs + d;
-    *reinterpret_cast<uint32_t *>(kcache + at) = pack_bf16x2(k0 * cs.x - k1 * cs.y, k0 * cs.y + k1 * cs.x);
-    *reinterpret_cast<uint32_t *>(vcache + at) = pack_bf16x2(row[dim + kv_dim + i], row[dim + kv_dim + i + 1]);
+    *reinterpret_cast<uint32_t *>(kcache + at) = pack_bf16x2(k.x * cs.x - k.y * cs.y, k.x * cs.y + k.y * cs.x);
+    *reinterpret_cast<uint32_t *>(vcache + at) = pack_bf16x2(v.x, v.y);
   }
 }
 
@@ -315,14 +335,21 @@ __global__ void attn_combine_kernel(const float *part, int nchunk, int n_heads, 
   att[(size_t)b * dim + h * HS + d] = *reinterpret_cast<uint16_t *>(&r);
 }
 
-// hb = bf16(silu(h1) * h3), h = [h1 | h3] per row, silu(g) = g / (1 + e^-g).
-__global__ void swiglu_kernel(const float *h, uint16_t *hb, int rows, int hidden) {
+// hb = bf16(silu(h1) * h3), h = [h1 | h3] per row (the sum of nsplit split-K
+// partials split_stride floats apart), silu(g) = g / (1 + e^-g).
+__global__ void swiglu_kernel(const float *h, int nsplit, size_t split_stride, uint16_t *hb, int rows,
+                              int hidden) {
   const size_t n = (size_t)rows * hidden / 2;
   const size_t step = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
     const size_t r = (2 * i) / hidden, c = (2 * i) % hidden;
-    const float2 g = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + c);
-    const float2 u = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + hidden + c);
+    float2 g = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + c);
+    float2 u = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + hidden + c);
+    for (int sp = 1; sp < nsplit; ++sp) {
+      const float2 g2 = *reinterpret_cast<const float2 *>(h + sp * split_stride + r * 2 * hidden + c);
+      const float2 u2 = *reinterpret_cast<const float2 *>(h + sp * split_stride + r * 2 * hidden + hidden + c);
+      g.x += g2.x, g.y += g2.y, u.x += u2.x, u.y += u2.y;
+    }
     const float a = g.x / (1.0f + expf(-g.x)) * u.x;
     const float bb = g.y / (1.0f + expf(-g.y)) * u.y;
     *reinterpret_cast<uint32_t *>(hb + r * hidden + c) = pack_bf16x2(a, bb);
@@ -418,6 +445,7 @@ struct ce_llama {
   ce_llama_config c{};
   int B = 0, cap = 0, precision = 0;
   int hs = 0, kv_dim = 0, qkv_rows = 0, chunk = 0, nchunk = 0, nv = 0;
+  int sp_qkv = 1, sp_o = 1, sp_13 = 1, sp_2 = 1;  // split-K counts of the layer GEMMs
   size_t layer_kv = 0;  // cache elements of one layer (batch x kv_heads x seq_len x hs)
   // weights
   uint16_t *tok_emb = nullptr, *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr,
@@ -530,6 +558,13 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   m->nchunk = (cfg->seq_len + m->chunk - 1) / m->chunk;
   m->nv = pow2_at_least((cfg->dim / 4 + kRowThreads - 1) / kRowThreads);
   m->layer_kv = (size_t)batch * cfg->n_kv_heads * cfg->seq_len * m->hs;
+  // split-K for the GEMMs whose tiles alone leave SMs idle at decode sizes;
+  // at least 4 k-blocks (256 of K) per split
+  m->sp_qkv = gemm_bf16_auto_splits(batch, m->qkv_rows, cfg->dim, 8, 4);
+  m->sp_o = gemm_bf16_auto_splits(batch, cfg->dim, cfg->dim, 8, 4);
+  m->sp_13 = gemm_bf16_auto_splits(batch, 2 * cfg->hidden_dim, cfg->dim, 8, 4);
+  m->sp_2 = gemm_bf16_auto_splits(batch, cfg->dim, cfg->hidden_dim, 8, 4);
+  const int sp_delta = m->sp_o > m->sp_2 ? m->sp_o : m->sp_2;
   const ce_llama_config &c = *cfg;
   const size_t L = c.n_layers;
   cudaStream_t s = (cudaStream_t)stream;
@@ -558,9 +593,9 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   CE_ALLOC(m->att, (size_t)batch * c.dim * 2);
   CE_ALLOC(m->hb, (size_t)batch * c.hidden_dim * 2);
   CE_ALLOC(m->x, (size_t)batch * c.dim * 4);
-  CE_ALLOC(m->delta, (size_t)batch * c.dim * 4);
-  CE_ALLOC(m->qkv, (size_t)batch * m->qkv_rows * 4);
-  CE_ALLOC(m->h, (size_t)batch * 2 * c.hidden_dim * 4);
+  CE_ALLOC(m->delta, (size_t)sp_delta * batch * c.dim * 4);
+  CE_ALLOC(m->qkv, (size_t)m->sp_qkv * batch * m->qkv_rows * 4);
+  CE_ALLOC(m->h, (size_t)m->sp_13 * batch * 2 * c.hidden_dim * 4);
   CE_ALLOC(m->logits, (size_t)batch * c.vocab_size * 4);
   CE_ALLOC(m->part, (size_t)batch * c.n_heads * m->nchunk * (m->hs + 2) * 4);
   CE_ALLOC(m->tokens, (size_t)batch * 4);
@@ -656,23 +691,26 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
   const ce_llama_config &c = m->c;
   const int B = m->B, D = c.dim, Hd = c.hidden_dim;
   const float eps = 1e-5f;
-  auto norm = [&](const float *delta, const uint16_t *emb, const float *w) {
+  const size_t delta_stride = (size_t)B * D, qkv_stride = (size_t)B * m->qkv_rows,
+               h_stride = (size_t)B * 2 * Hd;
+  auto norm = [&](const float *delta, int nsplit, const uint16_t *emb, const float *w) {
     return launch_rows(m->nv, [&](auto nv) {
       residual_rmsnorm_kernel<decltype(nv)::value><<<B, kRowThreads, 0, s>>>(
-          m->x, delta, emb, m->tokens, c.vocab_size, w, m->xb, D, eps);
+          m->x, delta, nsplit, delta_stride, emb, m->tokens, c.vocab_size, w, m->xb, D, eps);
     });
   };
   const size_t attn_smem = attn_smem_bytes(m->chunk, m->hs);
   for (int l = 0; l < c.n_layers; ++l) {
-    int rc = norm(l == 0 ? nullptr : m->delta, l == 0 ? m->tok_emb : nullptr, m->rms_att + (size_t)l * D);
+    int rc = norm(l == 0 ? nullptr : m->delta, m->sp_2, l == 0 ? m->tok_emb : nullptr,
+                  m->rms_att + (size_t)l * D);
     if (rc) return rc;
     CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
-    rc = gemm_bf16(m->qkv, m->xb, m->wqkv + l * wqkv_elems(m), B, m->qkv_rows, D, D, D, m->qkv_rows,
-                   nullptr, nullptr, 0, s);
+    rc = gemm_bf16_split(m->qkv, m->xb, m->wqkv + l * wqkv_elems(m), B, m->qkv_rows, D, D, D, m->qkv_rows,
+                         m->sp_qkv, (long long)qkv_stride, s);
     if (rc) return rc;
     uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
-    rope_append_kernel<<<B, 256, 0, s>>>(m->qkv, m->qkv_rows, kc, vc, m->rope, m->pos, D, m->kv_dim,
-                                         m->hs, c.n_kv_heads, c.seq_len);
+    rope_append_kernel<<<B, 256, 0, s>>>(m->qkv, m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, m->rope,
+                                         m->pos, D, m->kv_dim, m->hs, c.n_kv_heads, c.seq_len);
     CE_LAUNCH_CHECK("rope_append_kernel");
     const dim3 agrid(m->nchunk, c.n_heads, B);
     if (m->hs == 64) {
@@ -687,19 +725,22 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
       attn_combine_kernel<128><<<B * c.n_heads, 128, 0, s>>>(m->part, m->nchunk, c.n_heads, m->att, D);
     }
     CE_LAUNCH_CHECK("attn_combine_kernel");
-    rc = gemm_bf16(m->delta, m->att, m->wo + l * wo_elems(m), B, D, D, D, D, D, nullptr, nullptr, 0, s);
+    rc = gemm_bf16_split(m->delta, m->att, m->wo + l * wo_elems(m), B, D, D, D, D, D, m->sp_o,
+                         (long long)delta_stride, s);
     if (rc) return rc;
-    rc = norm(m->delta, nullptr, m->rms_ffn + (size_t)l * D);
+    rc = norm(m->delta, m->sp_o, nullptr, m->rms_ffn + (size_t)l * D);
     if (rc) return rc;
     CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
-    rc = gemm_bf16(m->h, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, 2 * Hd, nullptr, nullptr, 0, s);
+    rc = gemm_bf16_split(m->h, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, 2 * Hd, m->sp_13,
+                         (long long)h_stride, s);
     if (rc) return rc;
-    swiglu_kernel<<<4 * sm_count(), 256, 0, s>>>(m->h, m->hb, B, Hd);
+    swiglu_kernel<<<4 * sm_count(), 256, 0, s>>>(m->h, m->sp_13, h_stride, m->hb, B, Hd);
     CE_LAUNCH_CHECK("swiglu_kernel");
-    rc = gemm_bf16(m->delta, m->hb, m->w2 + l * w2_elems(m), B, D, Hd, Hd, Hd, D, nullptr, nullptr, 0, s);
+    rc = gemm_bf16_split(m->delta, m->hb, m->w2 + l * w2_elems(m), B, D, Hd, Hd, Hd, D, m->sp_2,
+                         (long long)delta_stride, s);
     if (rc) return rc;
   }
-  int rc = norm(m->delta, nullptr, m->rms_final);
+  int rc = norm(m->delta, m->sp_2, nullptr, m->rms_final);
   if (rc) return rc;
   CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
   rc = gemm_bf16(m->logits, m->xb, m->wcls, B, c.vocab_size, D, D, D, c.vocab_size, nullptr, nullptr, 0, s);

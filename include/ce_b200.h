@@ -151,12 +151,23 @@ int ce_gemm_bf16_tile(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev
  * bits), CE_PREC_TF32 (a, b fp32) or CE_PREC_FP8_E4M3 (a, b E4M3 codes, no
  * scales); cta_group 1 = single-CTA kernel
  * (128 x tile_n tiles), 2 = CTA-pair kernel (256 x tile_n tiles on two SMs,
- * tcgen05 cta_group::2), 0 = automatic; tile_n 128/160/192/224/256 or 0.
+ * tcgen05 cta_group::2), 0 = automatic; tile_n 64/96/128/160/192/224/256 or 0.
  * Test hook in the spirit of the reference's forced tiles and schedules
  * (decoder_optimized.cu:543-557, DECODER_OPT_TILE / _SCHEDULE). */
 int ce_gemm_config(int precision, float *d_dev, const void *a_dev, const void *b_dev, int M, int N,
                    int K, int lda, int ldb, int ldd, int cta_group, int tile_n,
                    ce_stream_t stream);
+
+/* Split-K bf16 GEMM for decode-sized shapes (few rows, so the output tiles
+ * alone leave SMs idle): split s of `splits` (1 <= splits <= ceil(K / 64))
+ * accumulates its balanced share of K and writes its fp32 partial
+ * D_s = A[:, K_s] B[:, K_s]^T at d_dev + s * split_stride (elements, at
+ * least (M - 1) * ldd + N); the caller sums the partials, in split order for
+ * a deterministic result. No counterpart in the reference (its GEMMs are
+ * whole-K tiles, decoder_lowprec.cu:85-127). */
+int ce_gemm_bf16_split(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev, int M, int N,
+                       int K, int lda, int ldb, int ldd, int splits, int64_t split_stride,
+                       ce_stream_t stream);
 
 /* Library-wide GEMM tuning, set at setup time (not during a capture): the
  * TMA producer prefetches operand tiles this many k-blocks ahead into L2

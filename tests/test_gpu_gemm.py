@@ -50,7 +50,7 @@ def test_bf16_gemm(ce, O, dev, shape):
     _check_bf16(O, d.cpu().numpy(), A, B)
 
 
-@pytest.mark.parametrize("tile_n", [128, 160, 192, 224, 256])
+@pytest.mark.parametrize("tile_n", [64, 96, 128, 160, 192, 224, 256])
 def test_bf16_gemm_every_tile_width(ce, O, dev, tile_n):
     M, N, K = 300, 1000, 520
     rng = np.random.default_rng(tile_n)
@@ -61,6 +61,38 @@ def test_bf16_gemm_every_tile_width(ce, O, dev, tile_n):
     ce.gemm_bf16(d, da, db, tile_n=tile_n)
     ce.device_status()
     _check_bf16(O, d.cpu().numpy(), A, B)
+
+
+@pytest.mark.parametrize("shape,splits", [((256, 768, 768), 3), ((300, 1000, 520), 9),
+                                          ((64, 2304, 4096), 8), ((5, 96, 64), 1), ((130, 200, 1000), 16)])
+def test_bf16_split_k_partials_sum_to_the_product(ce, O, dev, shape, splits):
+    """Every split writes its own partial; their sum (in split order) meets
+    the bf16 GEMM bound, and each partial is the product over its own
+    balanced k-block range."""
+    M, N, K = shape
+    rng = np.random.default_rng(M + splits)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K)).astype(np.float32)
+    da, db = _bf16_dev(O.bf16_bits(A), dev), _bf16_dev(O.bf16_bits(B), dev)
+    d = torch.full((splits, M, N), float("nan"), device=dev)
+    ce.gemm_bf16_split(d, da, db, splits)
+    ce.device_status()
+    parts = d.cpu().numpy().astype(np.float64)
+    _check_bf16(O, parts.sum(axis=0).astype(np.float32), A, B)
+    kb = (K + 63) // 64
+    Ab, Bb = O.bf16_value(O.bf16_bits(A)).astype(np.float64), O.bf16_value(O.bf16_bits(B)).astype(np.float64)
+    for sp in range(splits):
+        k0, k1 = 64 * (sp * kb // splits), min(K, 64 * ((sp + 1) * kb // splits))
+        ref = Ab[:, k0:k1] @ Bb[:, k0:k1].T
+        assert np.allclose(parts[sp], ref, rtol=1e-5, atol=1e-4 * np.sqrt(k1 - k0))
+
+
+def test_bf16_split_k_rejects_bad_splits(ce, dev):
+    a = torch.zeros((8, 128), dtype=torch.int16, device=dev)
+    b = torch.zeros((16, 128), dtype=torch.int16, device=dev)
+    d = torch.zeros((3, 8, 16), device=dev)
+    with pytest.raises(ce.CeError, match="split count"):
+        ce.gemm_bf16_split(d, a, b, 3)  # K = 128 is 2 k-blocks
 
 
 def test_bf16_gemm_ragged_k_with_padded_rows(ce, O, dev):
@@ -134,7 +166,7 @@ def test_bf16_gemm_sheet_shape(ce, O, dev):
 
 
 @pytest.mark.parametrize("cta_group", [1, 2])
-@pytest.mark.parametrize("tile_n", [128, 160, 192, 224, 256])
+@pytest.mark.parametrize("tile_n", [64, 96, 128, 160, 192, 224, 256])
 def test_forced_kernel_and_tile_bf16(ce, O, dev, cta_group, tile_n):
     """Both kernels (single CTA, CTA pair) at every tile width, on a shape
     that is ragged in M, N and K."""
