@@ -116,6 +116,7 @@ _SIGNATURES = {
     "ce_llama_init_random": [_vp, ctypes.c_uint64, _f, _i, _vp],
     "ce_llama_start": [_vp, _vp, _i, _vp],
     "ce_llama_enqueue_step": [_vp, _vp],
+    "ce_llama_set_pdl": [_vp, _i],
     "ce_llama_read": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_write": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_status": [],
@@ -560,6 +561,9 @@ class Llama:
 
     def step(self, stream=None):
         check(lib().ce_llama_enqueue_step(self._h, _stream(stream)))
+
+    def set_pdl(self, enable):
+        check(lib().ce_llama_set_pdl(self._h, int(bool(enable))))
 
     def read(self, which, layer=0, dtype=np.uint16, count=None, offset=0):
         """Host copy of `count` elements of a tensor from element `offset`."""

@@ -32,7 +32,7 @@ int gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int
 int gemm_simt_fp32(float *d, const float *a, const float *b, int M, int N, int K, int lda,
                    int ldb, int ldd, cudaStream_t s);
 int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
-                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s);
+                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s, bool pdl);
 int gemm_status();
 int gemm_bs_status();
 int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
@@ -325,7 +325,7 @@ int ce_gemm_config(int precision, float *d, const void *a, const void *b, int M,
 int ce_gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
                        int ldb, int ldd, int splits, int64_t split_stride, ce_stream_t stream) {
   return gemm_bf16_split(d, a, b, M, N, K, lda, ldb, ldd, splits, (long long)split_stride,
-                         (cudaStream_t)stream);
+                         (cudaStream_t)stream, false);
 }
 
 int ce_gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,

@@ -9,6 +9,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 
 #include "../../include/ce_b200.h"
 
@@ -129,6 +130,18 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, Device
                                           unsigned where) {
   const bool r = mbar_wait(bar, parity, st, where);
   return __all_sync(0xffffffffu, r) != 0;
+}
+
+// --- programmatic dependent launch -------------------------------------------
+// A kernel launched with the programmatic-serialization attribute may start
+// while its predecessor in the stream still runs. pdl_wait blocks until the
+// predecessor has completed and its memory is visible; nothing that reads a
+// buffer an earlier kernel writes, or writes a buffer an earlier kernel
+// reads, may come before it. pdl_launch_dependents lets the successor start
+// its own prologue. Both are no-ops for a kernel launched normally.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // --- clusters (CTA pairs of the 2-SM tensor-core path) ---------------------
@@ -348,4 +361,25 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Launches kernel<<<grid, block, smem, s>>>(args...), with programmatic
+// stream serialization when pdl is set (the kernel must call pdl_wait before
+// touching memory that earlier kernels use).
+template <typename... KArgs, typename... Args>
+int launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                  bool pdl, const char *what, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return e == cudaSuccess ? CE_OK : cuda_error(e, what);
+}
+
 }  // namespace ce
+

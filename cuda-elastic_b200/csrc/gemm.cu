@@ -153,6 +153,16 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  // Programmatic launch: warm L2 with this CTA's first B k-blocks (an L2
+  // prefetch is safe whatever runs before), then wait for the predecessor.
+  if (warp == 0 && lane == 0 && (int)blockIdx.x < num_tiles) {
+    const Unit w = unit_of(args, blockIdx.x);
+    const int n0 = (w.tile / args.tiles_m) * BN;
+    for (int kb = w.kb0; kb < w.kb1 && kb < w.kb0 + S::stages; ++kb)
+      tma_prefetch_2d(&tmB, kb * kElemsPerRow, n0);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------- TMA producer (lane 0 issues; the warp stays converged)
@@ -367,6 +377,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   cluster_sync();  // barriers of both CTAs are initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
+  if (warp == 0 && lane == 0 && pair < num_tiles) {  // see gemm_kernel
+    const Unit w = unit_of(args, pair);
+    const int n0 = (w.tile / args.tiles_m) * BN + (int)rank * (BN / 2);
+    for (int kb = w.kb0; kb < w.kb1 && kb < w.kb0 + kSt; ++kb)
+      tma_prefetch_2d(&tmB, kb * kElemsPerRow, n0);
+  }
+  pdl_launch_dependents();
+  pdl_wait();
   const uint32_t full0_leader = cluster_map(smem_u32(&full[0]), 0);
   const uint32_t tmem_empty0_leader = cluster_map(smem_u32(&tmem_empty[0]), 0);
 
@@ -569,24 +587,22 @@ int configure_smem(int bytes) {
 
 template <int kKind, int BN>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int grid,
-                cudaStream_t s) {
+                cudaStream_t s, bool pdl) {
   using S = Smem<BN>;
   int rc = configure_smem<gemm_kernel<kKind, BN>>(S::total);
   if (rc) return rc;
-  gemm_kernel<kKind, BN><<<grid, kThreads, S::total, s>>>(ta, tb, args);
-  CE_LAUNCH_CHECK("gemm_kernel");
-  return CE_OK;
+  return launch_kernel(gemm_kernel<kKind, BN>, dim3(grid), dim3(kThreads), S::total, s, pdl,
+                       "gemm_kernel", ta, tb, args);
 }
 
 template <int kKind, int BN>
 int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
-                     int grid, cudaStream_t s) {
+                     int grid, cudaStream_t s, bool pdl) {
   using S = SmemPair<BN>;
   int rc = configure_smem<gemm_pair_kernel<kKind, BN>>(S::total);
   if (rc) return rc;
-  gemm_pair_kernel<kKind, BN><<<grid, kThreads, S::total, s>>>(ta, tb, args);
-  CE_LAUNCH_CHECK("gemm_pair_kernel");
-  return CE_OK;
+  return launch_kernel(gemm_pair_kernel<kKind, BN>, dim3(grid), dim3(kThreads), S::total, s, pdl,
+                       "gemm_pair_kernel", ta, tb, args);
 }
 
 struct GemmChoice {
@@ -631,7 +647,8 @@ GemmChoice choose_tiles(int M, int N, int sms) {
 template <int kKind>
 int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
                   int ldd, const float *row_scale, const float *col_scale, int force_bn,
-                  int force_group, cudaStream_t s, int splits = 1, long long split_stride = 0) {
+                  int force_group, cudaStream_t s, int splits = 1, long long split_stride = 0,
+                  bool pdl = false) {
   constexpr int elem = Kind<kKind>::elem;
   const CUtensorMapDataType dt = kKind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : kKind == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -683,24 +700,24 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
     const int grid = 2 * pairs;
     switch (c.bn) {
-      case 256: return launch_gemm_pair<kKind, 256>(ta, tb, args, grid, s);
-      case 224: return launch_gemm_pair<kKind, 224>(ta, tb, args, grid, s);
-      case 192: return launch_gemm_pair<kKind, 192>(ta, tb, args, grid, s);
-      case 160: return launch_gemm_pair<kKind, 160>(ta, tb, args, grid, s);
-      case 128: return launch_gemm_pair<kKind, 128>(ta, tb, args, grid, s);
-      case 96: return launch_gemm_pair<kKind, 96>(ta, tb, args, grid, s);
-      case 64: return launch_gemm_pair<kKind, 64>(ta, tb, args, grid, s);
+      case 256: return launch_gemm_pair<kKind, 256>(ta, tb, args, grid, s, pdl);
+      case 224: return launch_gemm_pair<kKind, 224>(ta, tb, args, grid, s, pdl);
+      case 192: return launch_gemm_pair<kKind, 192>(ta, tb, args, grid, s, pdl);
+      case 160: return launch_gemm_pair<kKind, 160>(ta, tb, args, grid, s, pdl);
+      case 128: return launch_gemm_pair<kKind, 128>(ta, tb, args, grid, s, pdl);
+      case 96: return launch_gemm_pair<kKind, 96>(ta, tb, args, grid, s, pdl);
+      case 64: return launch_gemm_pair<kKind, 64>(ta, tb, args, grid, s, pdl);
     }
   } else {
     const int grid = tiles < sms ? tiles : sms;
     switch (c.bn) {
-      case 256: return launch_gemm<kKind, 256>(ta, tb, args, grid, s);
-      case 224: return launch_gemm<kKind, 224>(ta, tb, args, grid, s);
-      case 192: return launch_gemm<kKind, 192>(ta, tb, args, grid, s);
-      case 160: return launch_gemm<kKind, 160>(ta, tb, args, grid, s);
-      case 128: return launch_gemm<kKind, 128>(ta, tb, args, grid, s);
-      case 96: return launch_gemm<kKind, 96>(ta, tb, args, grid, s);
-      case 64: return launch_gemm<kKind, 64>(ta, tb, args, grid, s);
+      case 256: return launch_gemm<kKind, 256>(ta, tb, args, grid, s, pdl);
+      case 224: return launch_gemm<kKind, 224>(ta, tb, args, grid, s, pdl);
+      case 192: return launch_gemm<kKind, 192>(ta, tb, args, grid, s, pdl);
+      case 160: return launch_gemm<kKind, 160>(ta, tb, args, grid, s, pdl);
+      case 128: return launch_gemm<kKind, 128>(ta, tb, args, grid, s, pdl);
+      case 96: return launch_gemm<kKind, 96>(ta, tb, args, grid, s, pdl);
+      case 64: return launch_gemm<kKind, 64>(ta, tb, args, grid, s, pdl);
     }
   }
   return set_error(CE_ERR_USAGE, format("unsupported tile width %d", c.bn));
@@ -731,11 +748,13 @@ int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K,
 
 // Split-K bf16 GEMM: split s of `splits` accumulates its balanced range of
 // k-blocks and writes its fp32 partial at d + s * split_stride; the caller
-// sums the partials (in split order, so the result is deterministic).
+// sums the partials (in split order, so the result is deterministic). pdl:
+// launch with programmatic stream serialization (the kernel waits for its
+// predecessor before reading A or writing D).
 int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
-                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s) {
+                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s, bool pdl) {
   return gemm_dispatch<0>(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, 0, s, splits,
-                          split_stride);
+                          split_stride, pdl);
 }
 
 // Split count that fills the SMs for a bf16 GEMM of this shape: the tiles

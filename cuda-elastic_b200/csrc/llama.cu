@@ -38,7 +38,7 @@ int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int 
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
               cudaStream_t s, int force_group = 0);
 int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
-                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s);
+                    int ldb, int ldd, int splits, long long split_stride, cudaStream_t s, bool pdl);
 int gemm_bf16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
 
 static __device__ DeviceStatus g_llama_status;
@@ -50,7 +50,7 @@ using rowops::block_sum;
 
 constexpr int kRowThreads = 256;
 constexpr int kAttnThreads = 128;
-constexpr int kChunkBytes = 32768;  // K bytes of one attention chunk (V the same)
+constexpr int kChunkBytes = 16384;  // K bytes of one attention chunk (V the same)
 
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -100,6 +100,8 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
                         const uint16_t *emb, const int *tokens, int vocab, const float *w,
                         uint16_t *xb, int dim, float eps) {
   __shared__ float scratch[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x, cols4 = dim / 4;
   float4 *xr = reinterpret_cast<float4 *>(x + (size_t)b * dim);
   float4 v[NV];
@@ -167,6 +169,8 @@ __global__ void rope_append_kernel(float *qkv, int ld_qkv, int nsplit, size_t sp
                                    uint16_t *kcache, uint16_t *vcache, const float2 *rope,
                                    const int *pos_ptr, int dim, int kv_dim, int hs, int kv_heads,
                                    int seq_len) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x;
   const int pos = *pos_ptr;
   if (pos < 0 || pos >= seq_len) {
@@ -227,8 +231,10 @@ attn_chunk_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const ui
   float *ps = reinterpret_cast<float *>(vs + (size_t)chunk * HS);  // [chunk] scores / weights
   float *qs = ps + chunk;                                           // [HS]
   float *red = qs + HS;                                             // [kAttnThreads * 2] + 32
-  __shared__ __align__(8) uint64_t bar;
+  __shared__ __align__(8) uint64_t bar[2];  // K landed, V landed
 
+  pdl_launch_dependents();
+  pdl_wait();
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int n = *pos_ptr + 1;
   float *out = part + (((size_t)b * n_heads + h) * nchunk + c) * (HS + 2);
@@ -241,20 +247,25 @@ attn_chunk_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const ui
   const int kh = h / (n_heads / kv_heads);
   const size_t base = (((size_t)b * kv_heads + kh) * seq_len + t0) * HS;
   if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_barrier_init();
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     const uint32_t bytes = (uint32_t)cnt * HS * 2;
-    mbar_arrive_expect_tx(&bar, 2 * bytes);
-    bulk_g2s(ks, kcache + base, bytes, &bar);
-    bulk_g2s(vs, vcache + base, bytes, &bar);
+    mbar_arrive_expect_tx(&bar[0], bytes);
+    bulk_g2s(ks, kcache + base, bytes, &bar[0]);
+    mbar_arrive_expect_tx(&bar[1], bytes);
+    bulk_g2s(vs, vcache + base, bytes, &bar[1]);
   }
   const float qscale = rsqrtf((float)HS);
   for (int d = threadIdx.x; d < HS; d += kAttnThreads) qs[d] = qkv[(size_t)b * ld_qkv + h * HS + d] * qscale;
-  const bool arrived = mbar_wait(&bar, 0, &g_llama_status, 901u);
+  // scores need only K; V keeps landing meanwhile
+  const bool arrived = mbar_wait(&bar[0], 0, &g_llama_status, 901u);
   if (!__syncthreads_and(arrived)) {
+    // V's copy may still be in flight: wait (bounded) before the CTA exits
+    mbar_wait(&bar[1], 0, &g_llama_status, 902u);
     if (threadIdx.x < HS + 2) out[threadIdx.x] = NAN;
     return;
   }
@@ -286,6 +297,11 @@ attn_chunk_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const ui
     sum += e;
   }
   sum = block_sum(sum, red + 2 * kAttnThreads);  // its trailing barrier publishes ps
+  const bool v_arrived = mbar_wait(&bar[1], 0, &g_llama_status, 902u);
+  if (!__syncthreads_and(v_arrived)) {
+    if (threadIdx.x < HS + 2) out[threadIdx.x] = NAN;
+    return;
+  }
   // output: thread (pair p, group g) sums positions t = g mod kGroups
   const int p = threadIdx.x % kPairs, g = threadIdx.x / kPairs;
   float o0 = 0.f, o1 = 0.f;
@@ -318,6 +334,8 @@ attn_chunk_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const ui
 // sum_c l_c e^(m_c - M), written as bf16 into the o-projection operand.
 template <int HS>
 __global__ void attn_combine_kernel(const float *part, int nchunk, int n_heads, uint16_t *att, int dim) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int bh = blockIdx.x, d = threadIdx.x;
   const float *pp = part + (size_t)bh * nchunk * (HS + 2);
   float M = -INFINITY;
@@ -339,6 +357,8 @@ __global__ void attn_combine_kernel(const float *part, int nchunk, int n_heads, 
 // partials split_stride floats apart), silu(g) = g / (1 + e^-g).
 __global__ void swiglu_kernel(const float *h, int nsplit, size_t split_stride, uint16_t *hb, int rows,
                               int hidden) {
+  pdl_launch_dependents();
+  pdl_wait();
   const size_t n = (size_t)rows * hidden / 2;
   const size_t step = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
@@ -362,6 +382,8 @@ __global__ void __launch_bounds__(kRowThreads)
 argmax_kernel(const float *logits, int vocab, int *tokens, int *generated, int cap, const int *step_ptr) {
   __shared__ float sv[32];
   __shared__ int si[32];
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x;
   const float *row = logits + (size_t)b * vocab;
   float best = -INFINITY;
@@ -396,6 +418,8 @@ argmax_kernel(const float *logits, int vocab, int *tokens, int *generated, int c
 }
 
 __global__ void advance_kernel(int *pos, int *step) {
+  pdl_launch_dependents();
+  pdl_wait();
   *pos += 1;
   *step += 1;
 }
@@ -446,6 +470,7 @@ struct ce_llama {
   int B = 0, cap = 0, precision = 0;
   int hs = 0, kv_dim = 0, qkv_rows = 0, chunk = 0, nchunk = 0, nv = 0;
   int sp_qkv = 1, sp_o = 1, sp_13 = 1, sp_2 = 1;  // split-K counts of the layer GEMMs
+  bool pdl = true;  // programmatic dependent launch between the step's kernels
   size_t layer_kv = 0;  // cache elements of one layer (batch x kv_heads x seq_len x hs)
   // weights
   uint16_t *tok_emb = nullptr, *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr,
@@ -693,11 +718,15 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
   const float eps = 1e-5f;
   const size_t delta_stride = (size_t)B * D, qkv_stride = (size_t)B * m->qkv_rows,
                h_stride = (size_t)B * 2 * Hd;
+  const bool pdl = m->pdl;
   auto norm = [&](const float *delta, int nsplit, const uint16_t *emb, const float *w) {
-    return launch_rows(m->nv, [&](auto nv) {
-      residual_rmsnorm_kernel<decltype(nv)::value><<<B, kRowThreads, 0, s>>>(
-          m->x, delta, nsplit, delta_stride, emb, m->tokens, c.vocab_size, w, m->xb, D, eps);
+    int lrc = CE_OK;
+    const int rc = launch_rows(m->nv, [&](auto nv) {
+      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
+                          "residual_rmsnorm_kernel", m->x, delta, nsplit, delta_stride, emb,
+                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps);
     });
+    return rc ? rc : lrc;
   };
   const size_t attn_smem = attn_smem_bytes(m->chunk, m->hs);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -706,49 +735,57 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     if (rc) return rc;
     CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
     rc = gemm_bf16_split(m->qkv, m->xb, m->wqkv + l * wqkv_elems(m), B, m->qkv_rows, D, D, D, m->qkv_rows,
-                         m->sp_qkv, (long long)qkv_stride, s);
+                         m->sp_qkv, (long long)qkv_stride, s, pdl);
     if (rc) return rc;
     uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
-    rope_append_kernel<<<B, 256, 0, s>>>(m->qkv, m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, m->rope,
-                                         m->pos, D, m->kv_dim, m->hs, c.n_kv_heads, c.seq_len);
-    CE_LAUNCH_CHECK("rope_append_kernel");
+    rc = launch_kernel(rope_append_kernel, dim3(B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
+                       m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
+                       (const int *)m->pos, D, m->kv_dim, m->hs, c.n_kv_heads, c.seq_len);
+    if (rc) return rc;
     const dim3 agrid(m->nchunk, c.n_heads, B);
-    if (m->hs == 64) {
-      attn_chunk_kernel<64><<<agrid, kAttnThreads, attn_smem, s>>>(m->qkv, m->qkv_rows, kc, vc, m->pos, c.n_heads,
-                                                                   c.n_kv_heads, c.seq_len, m->chunk, m->nchunk, m->part);
-      CE_LAUNCH_CHECK("attn_chunk_kernel");
-      attn_combine_kernel<64><<<B * c.n_heads, 64, 0, s>>>(m->part, m->nchunk, c.n_heads, m->att, D);
-    } else {
-      attn_chunk_kernel<128><<<agrid, kAttnThreads, attn_smem, s>>>(m->qkv, m->qkv_rows, kc, vc, m->pos, c.n_heads,
-                                                                    c.n_kv_heads, c.seq_len, m->chunk, m->nchunk, m->part);
-      CE_LAUNCH_CHECK("attn_chunk_kernel");
-      attn_combine_kernel<128><<<B * c.n_heads, 128, 0, s>>>(m->part, m->nchunk, c.n_heads, m->att, D);
-    }
-    CE_LAUNCH_CHECK("attn_combine_kernel");
+    auto attention = [&](auto hs_tag) {
+      constexpr int HS = decltype(hs_tag)::value;
+      int arc = launch_kernel(attn_chunk_kernel<HS>, agrid, dim3(kAttnThreads), attn_smem, s, pdl,
+                              "attn_chunk_kernel", (const float *)m->qkv, m->qkv_rows,
+                              (const uint16_t *)kc, (const uint16_t *)vc, (const int *)m->pos, c.n_heads,
+                              c.n_kv_heads, c.seq_len, m->chunk, m->nchunk, m->part);
+      if (arc) return arc;
+      return launch_kernel(attn_combine_kernel<HS>, dim3(B * c.n_heads), dim3(HS), 0, s, pdl,
+                           "attn_combine_kernel", (const float *)m->part, m->nchunk, c.n_heads, m->att, D);
+    };
+    rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{}) : attention(std::integral_constant<int, 128>{});
+    if (rc) return rc;
     rc = gemm_bf16_split(m->delta, m->att, m->wo + l * wo_elems(m), B, D, D, D, D, D, m->sp_o,
-                         (long long)delta_stride, s);
+                         (long long)delta_stride, s, pdl);
     if (rc) return rc;
     rc = norm(m->delta, m->sp_o, nullptr, m->rms_ffn + (size_t)l * D);
     if (rc) return rc;
     CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
     rc = gemm_bf16_split(m->h, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, 2 * Hd, m->sp_13,
-                         (long long)h_stride, s);
+                         (long long)h_stride, s, pdl);
     if (rc) return rc;
-    swiglu_kernel<<<4 * sm_count(), 256, 0, s>>>(m->h, m->sp_13, h_stride, m->hb, B, Hd);
-    CE_LAUNCH_CHECK("swiglu_kernel");
+    rc = launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
+                       (const float *)m->h, m->sp_13, h_stride, m->hb, B, Hd);
+    if (rc) return rc;
     rc = gemm_bf16_split(m->delta, m->hb, m->w2 + l * w2_elems(m), B, D, Hd, Hd, Hd, D, m->sp_2,
-                         (long long)delta_stride, s);
+                         (long long)delta_stride, s, pdl);
     if (rc) return rc;
   }
   int rc = norm(m->delta, m->sp_2, nullptr, m->rms_final);
   if (rc) return rc;
   CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
-  rc = gemm_bf16(m->logits, m->xb, m->wcls, B, c.vocab_size, D, D, D, c.vocab_size, nullptr, nullptr, 0, s);
+  rc = gemm_bf16_split(m->logits, m->xb, m->wcls, B, c.vocab_size, D, D, D, c.vocab_size, 1, 0, s, pdl);
   if (rc) return rc;
-  argmax_kernel<<<B, kRowThreads, 0, s>>>(m->logits, c.vocab_size, m->tokens, m->generated, m->cap, m->step);
-  CE_LAUNCH_CHECK("argmax_kernel");
-  advance_kernel<<<1, 1, 0, s>>>(m->pos, m->step);
-  CE_LAUNCH_CHECK("advance_kernel");
+  rc = launch_kernel(argmax_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "argmax_kernel",
+                     (const float *)m->logits, c.vocab_size, m->tokens, m->generated, m->cap,
+                     (const int *)m->step);
+  if (rc) return rc;
+  return launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_kernel", m->pos, m->step);
+}
+
+int ce_llama_set_pdl(ce_llama *m, int enable) {
+  CE_REQUIRE(m != nullptr, "null model");
+  m->pdl = enable != 0;
   return CE_OK;
 }
 

@@ -466,6 +466,12 @@ int ce_llama_start(ce_llama *model, const int32_t *tokens_host, int pos, ce_stre
  * Capturable: a captured step replays for every token. */
 int ce_llama_enqueue_step(ce_llama *model, ce_stream_t stream);
 
+/* Programmatic dependent launch between the kernels of a step (default on):
+ * each kernel's prologue, and the GEMMs' L2 prefetch of their first weight
+ * blocks, overlap the previous kernel's tail. 0 turns it off (plain stream
+ * order); results are the same bits either way. */
+int ce_llama_set_pdl(ce_llama *model, int enable);
+
 /* Synchronous copies of a byte range of a tensor (CE_LLAMA_*; layer for the
  * per-layer ones) to and from host memory. */
 int ce_llama_read(ce_llama *model, int which, int layer, void *host, int64_t offset, int64_t bytes);

@@ -99,6 +99,34 @@ def test_graph_replay_equals_direct(ce):
     assert outs[0][2] == outs[1][2] == 13
 
 
+def test_programmatic_launch_changes_no_bits(ce):
+    """Programmatic dependent launch only overlaps prologues: the same bits
+    with it on and off, in direct steps and in a replayed graph."""
+    cfg = dict(dim=512, hidden_dim=1024, n_layers=3, n_heads=8, n_kv_heads=4, vocab_size=2048, seq_len=300)
+    outs = []
+    for pdl in (False, True):
+        m = ce.Llama(cfg, 40, 6)
+        try:
+            m.set_pdl(pdl)
+            m.init_random(seed=11, kv_fill=200)
+            m.start(np.arange(40, dtype=np.int32) * 31, 200)
+            m.step()
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                m.step()
+            for _ in range(5):
+                g.replay()
+            torch.cuda.synchronize()
+            del g
+            ce.llama_status()
+            outs.append((m.generated().copy(), m.logits().copy(), m.read(ce.LLAMA_RESIDUAL, dtype=np.float32)))
+        finally:
+            m.close()
+    for a, b in zip(outs[0], outs[1]):
+        assert np.array_equal(a, b)
+
+
 def test_110m_shape_sampled_sequences(ce, O):
     """BASELINE config 4 shape (dim 768, 12 layers, 12 heads, SwiGLU 2048,
     vocab 32000, seq_len 1024), batch 256 with the cache filled to position
