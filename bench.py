@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the decoder tokens/s section")
     ap.add_argument("--no-precisions", action="store_true", help="skip the per-precision GEMM section")
+    ap.add_argument("--no-llama", action="store_true", help="skip the Llama-2 decode section")
     ap.add_argument("--profile", action="store_true",
                     help="setup, warm-up and the timed steps only (for ncu captures); no JSON line")
     return ap.parse_args()
@@ -183,6 +184,61 @@ def run_reference(args, rank):
 
 # ---------------------------------------------------------------------------
 # GPU arm
+
+LLAMA_110M = dict(dim=768, hidden_dim=2048, n_layers=12, n_heads=12, vocab_size=32000, seq_len=1024)
+
+
+def llama_decode(ce, dev, stream, s, dist, world, hbm_gbs, batch=256, kv_fill=512, tokens=64):
+    """Greedy decode of `tokens` tokens for `batch` sequences of the 110M-shaped
+    Llama-2 (random N(0, 0.02) bf16 weights, KV cache N(0, 1) to position
+    kv_fill - 1): one direct step, one captured step graph, then the graph
+    replayed `tokens` times from a fresh start, between CUDA events. Every rank
+    decodes its own batch (replicas); tokens/s is summed over ranks."""
+    import numpy as np
+    cfg = LLAMA_110M
+    m = ce.Llama(cfg, batch, tokens, stream=s)
+    m.init_random(seed=1, weight_std=0.02, kv_fill=kv_fill, stream=s)
+    start_tokens = np.random.default_rng(0).integers(0, cfg["vocab_size"], batch).astype(np.int32)
+    with torch.cuda.stream(stream):
+        m.start(start_tokens, kv_fill, stream=s)
+        m.step(stream=s)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        m.step()
+    with torch.cuda.stream(stream):
+        m.start(start_tokens, kv_fill, stream=s)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(tokens):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ce.llama_status()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    hs = cfg["dim"] // cfg["n_heads"]
+    L, D, Hd, V = cfg["n_layers"], cfg["dim"], cfg["hidden_dim"], cfg["vocab_size"]
+    kv_bytes = sum(2 * L * batch * cfg["n_heads"] * (kv_fill + k + 1) * hs * 2 for k in range(tokens))
+    w_bytes = tokens * 2 * (L * (3 * D * D + D * D + 3 * Hd * D) + V * D)
+    achieved = (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9
+    del g
+    m.close()
+    return {"workload": f"Llama-2 110M shape (dim 768, 12 layers, 12 heads, SwiGLU 2048, vocab 32000, "
+                        f"seq_len 1024), bf16 weights N(0,0.02), KV cache N(0,1) to position {kv_fill - 1}, "
+                        f"batch {batch}, {tokens} greedy tokens, one captured step graph replayed",
+            "tokens_per_s": world * batch * tokens / (ms * 1e-3), "ms_per_step": ms / tokens,
+            "n_gpus": world, "parallelism": f"replicas x{world} (independent batches)",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
+                         "frac": achieved / hbm_gbs,
+                         "bytes_per_step": (kv_bytes + w_bytes) / tokens,
+                         "note": "KV cache read (K and V, positions 0..pos, every layer and head) plus "
+                                 "every weight once per step"}}
+
 
 def run_ours(args, rank, world, local_rank):
     import torch
@@ -384,6 +440,11 @@ def run_ours(args, rank, world, local_rank):
             dec.close()
             decoder[prec_name] = res
 
+    # ---- Llama-2 decode, BASELINE config 4 (110M shape), batch 256 from position 512 ----
+    llama = {}
+    if not args.no_llama:
+        llama = llama_decode(ce, dev, stream, s, dist, world, peaks()[0].get("hbm_gbs", 6650.0))
+
     pk, pk_kind = peaks()
     long_region = total_ms > 1000.0
     peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
@@ -426,6 +487,7 @@ def run_ours(args, rank, world, local_rank):
             "decoder": {"workload": "loom_private llama2c decoder, synthetic model, 1024 sequences x "
                                     "4 greedy steps, width 16384, vocab 8192 (4096 tokens per invocation)",
                         **decoder},
+            "llama_decode": llama,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "clocks": clocks,

@@ -19,6 +19,7 @@
 //     records CE_ERR_TIMEOUT in g_gemm_status, the CTA drains its own TMA
 //     copies and MMAs (bounded), frees its TMEM and exits.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -86,7 +87,35 @@ struct GemmArgs {
   int prefetch;  // L2 prefetch distance in k-blocks (0 = none)
   int splits;    // k ranges per tile (split-K); split s writes d + s * split_stride
   long long split_stride;
+  // Epilogue 1 (SwiGLU): the B rows interleave w1 and w3, so output columns
+  // (2i, 2i+1) are (g_i, u_i); the epilogue writes bf16(silu(g_i) * u_i) to
+  // column i of out_bf16 (row stride ld_out) instead of the fp32 d.
+  int epilogue;
+  uint16_t *out_bf16;
+  int ld_out;
 };
+
+// SwiGLU epilogue of one row's 32 accumulator columns starting at col0 (even).
+__device__ __forceinline__ void store_swiglu(const GemmArgs &args, int row, int col0, const float (&v)[32]) {
+  uint16_t *orow = args.out_bf16 + (size_t)row * args.ld_out;
+  uint32_t packed[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const float g0 = v[4 * k], u0 = v[4 * k + 1], g1 = v[4 * k + 2], u1 = v[4 * k + 3];
+    __nv_bfloat162 h = __floats2bfloat162_rn(g0 / (1.0f + expf(-g0)) * u0, g1 / (1.0f + expf(-g1)) * u1);
+    packed[k] = *reinterpret_cast<uint32_t *>(&h);
+  }
+  const int oc = col0 / 2;
+  if (col0 + 32 <= args.N && (args.ld_out & 7) == 0 && (reinterpret_cast<uintptr_t>(orow) & 15u) == 0) {
+    uint4 *dst = reinterpret_cast<uint4 *>(orow + oc);
+    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+      if (col0 + 2 * k + 1 < args.N) orow[oc + k] = (uint16_t)(packed[k / 2] >> (16 * (k & 1)));
+  }
+}
 
 // Work unit u of a launch: output tile u % tiles, k-block range of split
 // u / tiles (balanced, never empty: splits <= k_blocks).
@@ -275,7 +304,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
             if (args.col_scale != nullptr && col0 + j < args.N) x *= args.col_scale[col0 + j];
             v[j] = x;
           }
-          if (vec_ok && col0 + 32 <= args.N) {
+          if (args.epilogue == 1) {
+            store_swiglu(args, row, col0, v);
+          } else if (vec_ok && col0 + 32 <= args.N) {
             float4 *dst = reinterpret_cast<float4 *>(drow + col0);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -509,7 +540,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             if (args.col_scale != nullptr && col0 + j < args.N) x *= args.col_scale[col0 + j];
             v[j] = x;
           }
-          if (vec_ok && col0 + 32 <= args.N) {
+          if (args.epilogue == 1) {
+            store_swiglu(args, row, col0, v);
+          } else if (vec_ok && col0 + 32 <= args.N) {
             float4 *dst = reinterpret_cast<float4 *>(drow + col0);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
@@ -648,7 +681,7 @@ template <int kKind>
 int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
                   int ldd, const float *row_scale, const float *col_scale, int force_bn,
                   int force_group, cudaStream_t s, int splits = 1, long long split_stride = 0,
-                  bool pdl = false) {
+                  bool pdl = false, uint16_t *swiglu_out = nullptr, int swiglu_ld = 0) {
   constexpr int elem = Kind<kKind>::elem;
   const CUtensorMapDataType dt = kKind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : kKind == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -659,7 +692,9 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
              "operand row strides must be multiples of 16 bytes (lda=%d ldb=%d)", lda, ldb);
   CE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(b) & 15u) == 0,
              "operand base pointers must be 16-byte aligned");
-  CE_REQUIRE(d != nullptr, "null output");
+  CE_REQUIRE(d != nullptr || swiglu_out != nullptr, "null output");
+  CE_REQUIRE(swiglu_out == nullptr || (splits == 1 && N % 2 == 0 && swiglu_ld >= N / 2),
+             "the SwiGLU epilogue needs one split, an even N and ld_out >= N / 2");
   CE_REQUIRE(force_group == 0 || force_group == 1 || force_group == 2,
              "cta group must be 0 (automatic), 1 or 2 (got %d)", force_group);
   CE_REQUIRE(force_bn == 0 || force_bn == 64 || force_bn == 96 || force_bn == 128 || force_bn == 160 ||
@@ -695,6 +730,9 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.prefetch = g_prefetch_kblocks;
   args.splits = splits;
   args.split_stride = splits > 1 ? split_stride : 0;
+  args.epilogue = swiglu_out != nullptr ? 1 : 0;
+  args.out_bf16 = swiglu_out;
+  args.ld_out = swiglu_ld;
   const int tiles = args.tiles_m * args.tiles_n * splits;
   if (c.pair) {
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
@@ -773,6 +811,15 @@ int gemm_bf16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks) 
   const long long by_k = k_blocks / (min_kblocks > 0 ? min_kblocks : 1);
   sp = sp < by_k ? sp : by_k;
   return sp < 1 ? 1 : (int)sp;
+}
+
+// bf16 GEMM whose epilogue applies SwiGLU to interleaved (w1, w3) output
+// column pairs: out[m][i] = bf16(silu(D[m][2i]) * D[m][2i+1]), D = A B^T, no
+// fp32 output. N = 2 x hidden.
+int gemm_bf16_swiglu(uint16_t *out, int ld_out, const uint16_t *a, const uint16_t *b, int M, int N,
+                     int K, int lda, int ldb, cudaStream_t s, bool pdl) {
+  return gemm_dispatch<0>(nullptr, a, b, M, N, K, lda, ldb, N, nullptr, nullptr, 0, 0, s, 1, 0, pdl,
+                          out, ld_out);
 }
 
 int gemm_set_prefetch(int kblocks) {

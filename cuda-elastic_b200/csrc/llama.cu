@@ -14,13 +14,14 @@
 // is bf16 (the normalized rows, the attention output, the SwiGLU product) and
 // every GEMM accumulates and writes fp32 through the tcgen05 engine of
 // gemm.cu. Weights are bf16 [out][in] (K-major), the per-layer QKV rows
-// stacked [q; k; v] and the FFN's w1 and w3 stacked [w1; w3] so each is one
-// GEMM. The KV cache is bf16 [layer][batch][kv_head][seq_len][head_size]: the
+// stacked [q; k; v] and the FFN's w1 and w3 rows interleaved (w1_0, w3_0,
+// w1_1, ...) so each is one GEMM and the SwiGLU pairs meet in one tile of
+// the w1|w3 GEMM, whose epilogue writes the w2 operand directly. The KV cache is bf16 [layer][batch][kv_head][seq_len][head_size]: the
 // keys of one (sequence, head) are one contiguous run that a single bulk copy
 // moves into shared memory. Decode attention is split over position chunks
 // (flash-decoding): one 128-thread CTA per (chunk, head, sequence) stages its
-// K and V rows with cp.async.bulk, and a combine pass merges the chunks'
-// (max, sum, output) triples. The current position and step live in device
+// K and V rows with cp.async.bulk, and the last CTA of each (sequence, head)
+// to finish merges the chunks' (max, sum, output) triples. The current position and step live in device
 // memory, advanced by the last launch of the step, so one captured step
 // graph replays for every token.
 #include <cuda_bf16.h>
@@ -40,6 +41,8 @@ int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int 
 int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
                     int ldb, int ldd, int splits, long long split_stride, cudaStream_t s, bool pdl);
 int gemm_bf16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
+int gemm_bf16_swiglu(uint16_t *out, int ld_out, const uint16_t *a, const uint16_t *b, int M, int N,
+                     int K, int lda, int ldb, cudaStream_t s, bool pdl);
 
 static __device__ DeviceStatus g_llama_status;
 
@@ -50,7 +53,9 @@ using rowops::block_sum;
 
 constexpr int kRowThreads = 256;
 constexpr int kAttnThreads = 128;
-constexpr int kChunkBytes = 16384;  // K bytes of one attention chunk (V the same)
+constexpr int kChunkBytes = 8192;   // K bytes of one attention chunk (V the same)
+constexpr int kAttnStages = 2;      // chunks of K and V in flight per attention CTA
+constexpr long long kAttnWantPerSm = 6;  // attention CTAs per SM below which chunks split
 
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -213,148 +218,190 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc, uint3
       : "memory");
 }
 
-// Decode attention over one chunk of positions for one (sequence, head):
-// partial max m, sum l of exp(s - m) and unnormalized output o[hs] of the
-// chunk, s = q . k_t / sqrt(hs). Written as part[(b*H + h)*nchunk + c] =
-// {m, l, o[0..hs)}.
+// Decode attention of one (sequence, head), or of one of `splits` balanced
+// ranges of its position chunks: the CTA streams its chunks of K and V rows
+// through a 2-stage ring of bulk copies (separate K and V barriers, so the
+// scores of a chunk run while its V rows land) and keeps an online softmax:
+// running max m, sum l and unnormalized output o, rescaled by e^(m_old -
+// m_new) per chunk, s = q . k_t / sqrt(hs). With one split the CTA writes
+// att = bf16(o / l) itself; with several, each writes its (m, l, o) to part
+// and the last of the (sequence, head)'s CTAs to arrive (an arrival counter
+// that it resets) merges them in split order.
 template <int HS>
 __global__ void __launch_bounds__(kAttnThreads)
-attn_chunk_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const uint16_t *vcache,
-                  const int *pos_ptr, int n_heads, int kv_heads, int seq_len, int chunk, int nchunk,
-                  float *part) {
+attn_decode_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const uint16_t *vcache,
+                   const int *pos_ptr, int n_heads, int kv_heads, int seq_len, int chunk, int splits,
+                   float *part, int *arrivals, uint16_t *att, int dim) {
   constexpr int kPairs = HS / 2;                   // bf16 pairs per row
   constexpr int kGroups = kAttnThreads / kPairs;   // position groups of the output pass
   constexpr int kRowVec = HS * 2 / 16;             // 16-byte pieces per K row
   extern __shared__ __align__(128) uint8_t smem[];
-  uint16_t *ks = reinterpret_cast<uint16_t *>(smem);
-  uint16_t *vs = ks + (size_t)chunk * HS;
-  float *ps = reinterpret_cast<float *>(vs + (size_t)chunk * HS);  // [chunk] scores / weights
-  float *qs = ps + chunk;                                           // [HS]
-  float *red = qs + HS;                                             // [kAttnThreads * 2] + 32
-  __shared__ __align__(8) uint64_t bar[2];  // K landed, V landed
+  __shared__ __align__(8) uint64_t bar[kAttnStages][2];  // [stage][K, V]
+  __shared__ int is_last;
+  const size_t stage_elems = (size_t)chunk * HS;
+  uint16_t *ring = reinterpret_cast<uint16_t *>(smem);  // [stage][K | V][chunk][HS]
+  float *ps = reinterpret_cast<float *>(ring + 2 * kAttnStages * stage_elems);  // [chunk]
+  float *qs = ps + chunk;                                          // [HS]
+  float *red = qs + HS;                                            // [2 * threads] + 32
 
   pdl_launch_dependents();
   pdl_wait();
-  const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int sp = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int bh = b * n_heads + h;
   const int n = *pos_ptr + 1;
-  float *out = part + (((size_t)b * n_heads + h) * nchunk + c) * (HS + 2);
-  const int t0 = c * chunk;
-  if (n < 1 || n > seq_len || t0 >= n) {
-    if (threadIdx.x < HS + 2) out[threadIdx.x] = threadIdx.x == 0 ? -INFINITY : 0.f;
-    return;
-  }
-  const int cnt = min(chunk, n - t0);
+  const bool valid = n >= 1 && n <= seq_len;
+  const int nch = valid ? (n + chunk - 1) / chunk : 0;
+  const int c0 = (int)((long long)sp * nch / splits), c1 = (int)((long long)(sp + 1) * nch / splits);
   const int kh = h / (n_heads / kv_heads);
-  const size_t base = (((size_t)b * kv_heads + kh) * seq_len + t0) * HS;
-  if (threadIdx.x == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+  const size_t base = ((size_t)b * kv_heads + kh) * seq_len * HS;
+
+  if (tid == 0) {
+    for (int st = 0; st < kAttnStages; ++st) {
+      mbar_init(&bar[st][0], 1);
+      mbar_init(&bar[st][1], 1);
+    }
     fence_barrier_init();
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t bytes = (uint32_t)cnt * HS * 2;
-    mbar_arrive_expect_tx(&bar[0], bytes);
-    bulk_g2s(ks, kcache + base, bytes, &bar[0]);
-    mbar_arrive_expect_tx(&bar[1], bytes);
-    bulk_g2s(vs, vcache + base, bytes, &bar[1]);
-  }
+  auto issue = [&](int c, int st) {  // thread 0: K and V rows of chunk c into stage st
+    const int t0 = c * chunk;
+    const uint32_t bytes = (uint32_t)min(chunk, n - t0) * HS * 2;
+    uint16_t *kd = ring + (size_t)st * 2 * stage_elems;
+    mbar_arrive_expect_tx(&bar[st][0], bytes);
+    bulk_g2s(kd, kcache + base + (size_t)t0 * HS, bytes, &bar[st][0]);
+    mbar_arrive_expect_tx(&bar[st][1], bytes);
+    bulk_g2s(kd + stage_elems, vcache + base + (size_t)t0 * HS, bytes, &bar[st][1]);
+  };
+  if (tid == 0)
+    for (int c = c0; c < c1 && c < c0 + kAttnStages; ++c) issue(c, c - c0);
   const float qscale = rsqrtf((float)HS);
-  for (int d = threadIdx.x; d < HS; d += kAttnThreads) qs[d] = qkv[(size_t)b * ld_qkv + h * HS + d] * qscale;
-  // scores need only K; V keeps landing meanwhile
-  const bool arrived = mbar_wait(&bar[0], 0, &g_llama_status, 901u);
-  if (!__syncthreads_and(arrived)) {
-    // V's copy may still be in flight: wait (bounded) before the CTA exits
-    mbar_wait(&bar[1], 0, &g_llama_status, 902u);
-    if (threadIdx.x < HS + 2) out[threadIdx.x] = NAN;
-    return;
-  }
-  // scores: one position per thread, 16-byte pieces read in a rotated order
-  // so the 8 threads of a shared-memory phase touch 8 different banks groups
-  const int lane = threadIdx.x & 31;
-  float mx = -INFINITY;
-  for (int t = threadIdx.x; t < cnt; t += kAttnThreads) {
-    const uint4 *kr = reinterpret_cast<const uint4 *>(ks + (size_t)t * HS);
-    float s = 0.f;
-#pragma unroll
-    for (int jj = 0; jj < kRowVec; ++jj) {
-      const int j = (jj + lane) % kRowVec;
-      const uint4 kv = kr[j];
-      const float *q = qs + j * 8;
-      s += q[0] * __uint_as_float(kv.x << 16) + q[1] * __uint_as_float(kv.x & 0xFFFF0000u);
-      s += q[2] * __uint_as_float(kv.y << 16) + q[3] * __uint_as_float(kv.y & 0xFFFF0000u);
-      s += q[4] * __uint_as_float(kv.z << 16) + q[5] * __uint_as_float(kv.z & 0xFFFF0000u);
-      s += q[6] * __uint_as_float(kv.w << 16) + q[7] * __uint_as_float(kv.w & 0xFFFF0000u);
+  for (int d = tid; d < HS; d += kAttnThreads) qs[d] = qkv[(size_t)b * ld_qkv + h * HS + d] * qscale;
+
+  const int lane = tid & 31, p = tid % kPairs, g = tid / kPairs;
+  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+  bool ok = valid;
+  int c = c0;
+  for (; ok && c < c1; ++c) {
+    const int i = c - c0, st = i % kAttnStages;
+    const uint32_t parity = (uint32_t)(i / kAttnStages) & 1u;
+    const int cnt = min(chunk, n - c * chunk);
+    const uint16_t *ks = ring + (size_t)st * 2 * stage_elems, *vs = ks + stage_elems;
+    if (!__syncthreads_and(mbar_wait(&bar[st][0], parity, &g_llama_status, 901u))) {
+      ok = false;
+      break;
     }
-    ps[t] = s;
-    mx = fmaxf(mx, s);
+    float cmax = -INFINITY;
+    for (int t = tid; t < cnt; t += kAttnThreads) {
+      const uint4 *kr = reinterpret_cast<const uint4 *>(ks + (size_t)t * HS);
+      float sc = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < kRowVec; ++jj) {
+        const int j = (jj + lane) % kRowVec;  // rotated: 8 lanes of a phase hit 8 bank groups
+        const uint4 kv = kr[j];
+        const float *q = qs + j * 8;
+        sc += q[0] * __uint_as_float(kv.x << 16) + q[1] * __uint_as_float(kv.x & 0xFFFF0000u);
+        sc += q[2] * __uint_as_float(kv.y << 16) + q[3] * __uint_as_float(kv.y & 0xFFFF0000u);
+        sc += q[4] * __uint_as_float(kv.z << 16) + q[5] * __uint_as_float(kv.z & 0xFFFF0000u);
+        sc += q[6] * __uint_as_float(kv.w << 16) + q[7] * __uint_as_float(kv.w & 0xFFFF0000u);
+      }
+      ps[t] = sc;
+      cmax = fmaxf(cmax, sc);
+    }
+    cmax = block_max(cmax, red + 2 * kAttnThreads);
+    const float m_new = fmaxf(m, cmax);
+    const float rescale = expf(m - m_new);  // 0 for the first chunk (m = -inf)
+    float csum = 0.f;
+    for (int t = tid; t < cnt; t += kAttnThreads) {
+      const float e = expf(ps[t] - m_new);
+      ps[t] = e;
+      csum += e;
+    }
+    csum = block_sum(csum, red + 2 * kAttnThreads);  // its trailing barrier publishes ps
+    l = l * rescale + csum;
+    m = m_new;
+    if (!__syncthreads_and(mbar_wait(&bar[st][1], parity, &g_llama_status, 902u))) {
+      ok = false;
+      break;
+    }
+    o0 *= rescale;
+    o1 *= rescale;
+    for (int t = g; t < cnt; t += kGroups) {
+      const uint32_t vv = *reinterpret_cast<const uint32_t *>(vs + (size_t)t * HS + 2 * p);
+      const float w = ps[t];
+      o0 += w * __uint_as_float(vv << 16);
+      o1 += w * __uint_as_float(vv & 0xFFFF0000u);
+    }
+    __syncthreads();  // stage st and ps are free
+    if (tid == 0 && c + kAttnStages < c1) issue(c + kAttnStages, st);
   }
-  mx = block_max(mx, red + 2 * kAttnThreads);
-  float sum = 0.f;
-  for (int t = threadIdx.x; t < cnt; t += kAttnThreads) {
-    const float e = expf(ps[t] - mx);
-    ps[t] = e;
-    sum += e;
+  if (!ok) {
+    // a staging wait gave up: let this CTA's copies still in flight land
+    // (bounded waits) before it exits, and leave NaN outputs
+    for (int cc = c; cc < c1 && cc < c + kAttnStages; ++cc) {
+      const int i = cc - c0;
+      mbar_wait(&bar[i % kAttnStages][0], (uint32_t)(i / kAttnStages) & 1u, &g_llama_status, 903u);
+      mbar_wait(&bar[i % kAttnStages][1], (uint32_t)(i / kAttnStages) & 1u, &g_llama_status, 903u);
+    }
+    m = NAN;
   }
-  sum = block_sum(sum, red + 2 * kAttnThreads);  // its trailing barrier publishes ps
-  const bool v_arrived = mbar_wait(&bar[1], 0, &g_llama_status, 902u);
-  if (!__syncthreads_and(v_arrived)) {
-    if (threadIdx.x < HS + 2) out[threadIdx.x] = NAN;
-    return;
-  }
-  // output: thread (pair p, group g) sums positions t = g mod kGroups
-  const int p = threadIdx.x % kPairs, g = threadIdx.x / kPairs;
-  float o0 = 0.f, o1 = 0.f;
-  for (int t = g; t < cnt; t += kGroups) {
-    const uint32_t vv = *reinterpret_cast<const uint32_t *>(vs + (size_t)t * HS + 2 * p);
-    const float w = ps[t];
-    o0 += w * __uint_as_float(vv << 16);
-    o1 += w * __uint_as_float(vv & 0xFFFF0000u);
-  }
-  red[2 * threadIdx.x] = o0;
-  red[2 * threadIdx.x + 1] = o1;
+  // outputs of the groups summed per pair
+  red[2 * tid] = o0;
+  red[2 * tid + 1] = o1;
   __syncthreads();
-  if (threadIdx.x < kPairs) {
-    float a0 = 0.f, a1 = 0.f;
+  float a0 = 0.f, a1 = 0.f;
+  if (tid < kPairs) {
 #pragma unroll
     for (int gg = 0; gg < kGroups; ++gg) {
-      a0 += red[2 * (gg * kPairs + threadIdx.x)];
-      a1 += red[2 * (gg * kPairs + threadIdx.x) + 1];
+      a0 += red[2 * (gg * kPairs + tid)];
+      a1 += red[2 * (gg * kPairs + tid) + 1];
     }
-    out[2 + 2 * threadIdx.x] = a0;
-    out[3 + 2 * threadIdx.x] = a1;
   }
-  if (threadIdx.x == 0) {
-    out[0] = mx;
-    out[1] = sum;
+  if (splits == 1) {
+    if (tid < kPairs) {
+      const float inv = (ok && l > 0.f) ? 1.0f / l : NAN;
+      *reinterpret_cast<uint32_t *>(att + (size_t)b * dim + h * HS + 2 * tid) = pack_bf16x2(a0 * inv, a1 * inv);
+    }
+    return;
+  }
+  float *out = part + ((size_t)bh * splits + sp) * (HS + 2);
+  if (tid < kPairs) {
+    out[2 + 2 * tid] = a0;
+    out[3 + 2 * tid] = a1;
+  }
+  if (tid == 0) {
+    out[0] = (c1 > c0 || !ok) ? m : -INFINITY;
+    out[1] = l;
+  }
+  __syncthreads();  // this CTA's partial is written
+  if (tid == 0) {
+    __threadfence();
+    const int before = atomicAdd(&arrivals[bh], 1);
+    is_last = before == splits - 1;
+    if (is_last) arrivals[bh] = 0;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const float *pp = part + (size_t)bh * splits * (HS + 2);
+  for (int d = tid; d < HS; d += kAttnThreads) {
+    float M = -INFINITY;
+    for (int k = 0; k < splits; ++k) M = fmaxf(M, __ldcg(pp + k * (HS + 2)));
+    float L = 0.f, o = 0.f;
+    for (int k = 0; k < splits; ++k) {
+      const float mk = __ldcg(pp + k * (HS + 2));
+      if (mk == -INFINITY) continue;
+      const float f = expf(mk - M);
+      L += __ldcg(pp + k * (HS + 2) + 1) * f;
+      o += __ldcg(pp + k * (HS + 2) + 2 + d) * f;
+    }
+    __nv_bfloat16 r = __float2bfloat16_rn(o / L);
+    att[(size_t)b * dim + h * HS + d] = *reinterpret_cast<uint16_t *>(&r);
   }
 }
 
-// Merges the chunks of one (sequence, head): att = sum_c o_c e^(m_c - M) /
-// sum_c l_c e^(m_c - M), written as bf16 into the o-projection operand.
-template <int HS>
-__global__ void attn_combine_kernel(const float *part, int nchunk, int n_heads, uint16_t *att, int dim) {
-  pdl_launch_dependents();
-  pdl_wait();
-  const int bh = blockIdx.x, d = threadIdx.x;
-  const float *pp = part + (size_t)bh * nchunk * (HS + 2);
-  float M = -INFINITY;
-  for (int c = 0; c < nchunk; ++c) M = fmaxf(M, pp[c * (HS + 2)]);
-  float L = 0.f, o = 0.f;
-  for (int c = 0; c < nchunk; ++c) {
-    const float m = pp[c * (HS + 2)];
-    if (m == -INFINITY) continue;
-    const float f = expf(m - M);
-    L += pp[c * (HS + 2) + 1] * f;
-    o += pp[c * (HS + 2) + 2 + d] * f;
-  }
-  const int b = bh / n_heads, h = bh % n_heads;
-  __nv_bfloat16 r = __float2bfloat16_rn(o / L);
-  att[(size_t)b * dim + h * HS + d] = *reinterpret_cast<uint16_t *>(&r);
-}
-
-// hb = bf16(silu(h1) * h3), h = [h1 | h3] per row (the sum of nsplit split-K
-// partials split_stride floats apart), silu(g) = g / (1 + e^-g).
+// hb = bf16(silu(g) * u), h = interleaved (g_i, u_i) pairs per row (the sum
+// of nsplit split-K partials split_stride floats apart), silu(g) = g / (1 + e^-g).
+// Used when the w1|w3 GEMM runs split; otherwise its epilogue does this.
 __global__ void swiglu_kernel(const float *h, int nsplit, size_t split_stride, uint16_t *hb, int rows,
                               int hidden) {
   pdl_launch_dependents();
@@ -363,15 +410,13 @@ __global__ void swiglu_kernel(const float *h, int nsplit, size_t split_stride, u
   const size_t step = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
     const size_t r = (2 * i) / hidden, c = (2 * i) % hidden;
-    float2 g = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + c);
-    float2 u = *reinterpret_cast<const float2 *>(h + r * 2 * hidden + hidden + c);
+    float4 gu = *reinterpret_cast<const float4 *>(h + r * 2 * hidden + 2 * c);  // g_c, u_c, g_c+1, u_c+1
     for (int sp = 1; sp < nsplit; ++sp) {
-      const float2 g2 = *reinterpret_cast<const float2 *>(h + sp * split_stride + r * 2 * hidden + c);
-      const float2 u2 = *reinterpret_cast<const float2 *>(h + sp * split_stride + r * 2 * hidden + hidden + c);
-      g.x += g2.x, g.y += g2.y, u.x += u2.x, u.y += u2.y;
+      const float4 e = *reinterpret_cast<const float4 *>(h + sp * split_stride + r * 2 * hidden + 2 * c);
+      gu.x += e.x, gu.y += e.y, gu.z += e.z, gu.w += e.w;
     }
-    const float a = g.x / (1.0f + expf(-g.x)) * u.x;
-    const float bb = g.y / (1.0f + expf(-g.y)) * u.y;
+    const float a = gu.x / (1.0f + expf(-gu.x)) * gu.y;
+    const float bb = gu.z / (1.0f + expf(-gu.z)) * gu.w;
     *reinterpret_cast<uint32_t *>(hb + r * hidden + c) = pack_bf16x2(a, bb);
   }
 }
@@ -437,7 +482,8 @@ int launch_rows(int nv, F &&f) {
 }
 
 size_t attn_smem_bytes(int chunk, int hs) {
-  return (size_t)chunk * hs * 2 * 2 + (size_t)chunk * 4 + (size_t)hs * 4 + (2 * kAttnThreads + 32) * 4;
+  return (size_t)chunk * hs * 2 * 2 * kAttnStages + (size_t)chunk * 4 + (size_t)hs * 4 +
+         (2 * kAttnThreads + 32) * 4;
 }
 
 // Opts the attention kernels into their dynamic shared memory, once per device.
@@ -446,9 +492,9 @@ int configure_attention() {
   int dev = 0;
   CE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && done[dev]) return CE_OK;
-  CE_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)attn_smem_bytes(kChunkBytes / 128, 64)));
-  CE_CUDA_TRY(cudaFuncSetAttribute(attn_chunk_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)attn_smem_bytes(kChunkBytes / 256, 128)));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return CE_OK;
@@ -471,6 +517,7 @@ struct ce_llama {
   int hs = 0, kv_dim = 0, qkv_rows = 0, chunk = 0, nchunk = 0, nv = 0;
   int sp_qkv = 1, sp_o = 1, sp_13 = 1, sp_2 = 1;  // split-K counts of the layer GEMMs
   bool pdl = true;  // programmatic dependent launch between the step's kernels
+  int attn_splits = 1;  // CTAs per (sequence, head) in the attention
   size_t layer_kv = 0;  // cache elements of one layer (batch x kv_heads x seq_len x hs)
   // weights
   uint16_t *tok_emb = nullptr, *wqkv = nullptr, *wo = nullptr, *w13 = nullptr, *w2 = nullptr,
@@ -482,6 +529,7 @@ struct ce_llama {
   float *x = nullptr, *delta = nullptr, *qkv = nullptr, *h = nullptr, *logits = nullptr,
         *part = nullptr;
   int *tokens = nullptr, *generated = nullptr, *pos = nullptr, *step = nullptr;
+  int *arrivals = nullptr;  // per (sequence, head) chunk arrivals of the attention merge
 };
 
 namespace {
@@ -492,7 +540,7 @@ void free_llama(ce_llama *m) {
                   (void *)m->rope, (void *)m->kcache, (void *)m->vcache, (void *)m->xb, (void *)m->att,
                   (void *)m->hb, (void *)m->x, (void *)m->delta, (void *)m->qkv, (void *)m->h,
                   (void *)m->logits, (void *)m->part, (void *)m->tokens, (void *)m->generated,
-                  (void *)m->pos, (void *)m->step})
+                  (void *)m->pos, (void *)m->step, (void *)m->arrivals})
     if (p) cudaFree(p);
   delete m;
 }
@@ -582,6 +630,14 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   m->chunk = kChunkBytes / (m->hs * 2);
   m->nchunk = (cfg->seq_len + m->chunk - 1) / m->chunk;
   m->nv = pow2_at_least((cfg->dim / 4 + kRowThreads - 1) / kRowThreads);
+  {
+    // enough attention CTAs for about two waves of 3 per SM, never more
+    // splits than chunks of the full cache
+    const long long pairs = (long long)batch * cfg->n_heads;
+    const long long want = kAttnWantPerSm * sm_count();
+    long long sp = (want + pairs - 1) / pairs;
+    m->attn_splits = (int)std::max(1LL, std::min<long long>(sp, m->nchunk));
+  }
   m->layer_kv = (size_t)batch * cfg->n_kv_heads * cfg->seq_len * m->hs;
   // split-K for the GEMMs whose tiles alone leave SMs idle at decode sizes;
   // at least 4 k-blocks (256 of K) per split
@@ -622,11 +678,12 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   CE_ALLOC(m->qkv, (size_t)m->sp_qkv * batch * m->qkv_rows * 4);
   CE_ALLOC(m->h, (size_t)m->sp_13 * batch * 2 * c.hidden_dim * 4);
   CE_ALLOC(m->logits, (size_t)batch * c.vocab_size * 4);
-  CE_ALLOC(m->part, (size_t)batch * c.n_heads * m->nchunk * (m->hs + 2) * 4);
+  CE_ALLOC(m->part, (size_t)batch * c.n_heads * m->attn_splits * (m->hs + 2) * 4);
   CE_ALLOC(m->tokens, (size_t)batch * 4);
   CE_ALLOC(m->generated, (size_t)batch * max_steps * 4);
   CE_ALLOC(m->pos, 4);
   CE_ALLOC(m->step, 4);
+  CE_ALLOC(m->arrivals, (size_t)batch * c.n_heads * 4);
 #undef CE_ALLOC
   // RoPE table: (cos, sin) of pos * 10000^(-2i/hs), computed in double once
   std::vector<float2> table((size_t)c.seq_len * (m->hs / 2));
@@ -639,6 +696,7 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   e = cudaMemcpyAsync(m->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->pos, 0, 4, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->step, 0, 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->arrivals, 0, (size_t)batch * c.n_heads * 4, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->generated, 0xFF, (size_t)batch * max_steps * 4, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // the host table goes out of scope
   if (e != cudaSuccess) {
@@ -742,16 +800,14 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
                        m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
                        (const int *)m->pos, D, m->kv_dim, m->hs, c.n_kv_heads, c.seq_len);
     if (rc) return rc;
-    const dim3 agrid(m->nchunk, c.n_heads, B);
+    const dim3 agrid(m->attn_splits, c.n_heads, B);
     auto attention = [&](auto hs_tag) {
       constexpr int HS = decltype(hs_tag)::value;
-      int arc = launch_kernel(attn_chunk_kernel<HS>, agrid, dim3(kAttnThreads), attn_smem, s, pdl,
-                              "attn_chunk_kernel", (const float *)m->qkv, m->qkv_rows,
-                              (const uint16_t *)kc, (const uint16_t *)vc, (const int *)m->pos, c.n_heads,
-                              c.n_kv_heads, c.seq_len, m->chunk, m->nchunk, m->part);
-      if (arc) return arc;
-      return launch_kernel(attn_combine_kernel<HS>, dim3(B * c.n_heads), dim3(HS), 0, s, pdl,
-                           "attn_combine_kernel", (const float *)m->part, m->nchunk, c.n_heads, m->att, D);
+      return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(kAttnThreads), attn_smem, s, pdl,
+                           "attn_decode_kernel", (const float *)m->qkv, m->qkv_rows,
+                           (const uint16_t *)kc, (const uint16_t *)vc, (const int *)m->pos, c.n_heads,
+                           c.n_kv_heads, c.seq_len, m->chunk, m->attn_splits, m->part, m->arrivals,
+                           m->att, D);
     };
     rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{}) : attention(std::integral_constant<int, 128>{});
     if (rc) return rc;
@@ -761,12 +817,17 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     rc = norm(m->delta, m->sp_o, nullptr, m->rms_ffn + (size_t)l * D);
     if (rc) return rc;
     CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
-    rc = gemm_bf16_split(m->h, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, 2 * Hd, m->sp_13,
-                         (long long)h_stride, s, pdl);
-    if (rc) return rc;
-    rc = launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
-                       (const float *)m->h, m->sp_13, h_stride, m->hb, B, Hd);
-    if (rc) return rc;
+    if (m->sp_13 == 1) {  // SwiGLU in the GEMM epilogue, straight to the bf16 operand
+      rc = gemm_bf16_swiglu(m->hb, Hd, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, s, pdl);
+      if (rc) return rc;
+    } else {
+      rc = gemm_bf16_split(m->h, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, 2 * Hd, m->sp_13,
+                           (long long)h_stride, s, pdl);
+      if (rc) return rc;
+      rc = launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
+                         (const float *)m->h, m->sp_13, h_stride, m->hb, B, Hd);
+      if (rc) return rc;
+    }
     rc = gemm_bf16_split(m->delta, m->hb, m->w2 + l * w2_elems(m), B, D, Hd, Hd, Hd, D, m->sp_2,
                          (long long)delta_stride, s, pdl);
     if (rc) return rc;

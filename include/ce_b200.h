@@ -426,7 +426,7 @@ typedef struct ce_llama_config {
 #define CE_LLAMA_TOK_EMB 0    /* bf16 [vocab][dim] */
 #define CE_LLAMA_WQKV 1       /* bf16 [dim + 2 kv_dim][dim] of a layer: rows q, k, v */
 #define CE_LLAMA_WO 2         /* bf16 [dim][dim] of a layer */
-#define CE_LLAMA_W13 3        /* bf16 [2 hidden][dim] of a layer: rows w1, w3 */
+#define CE_LLAMA_W13 3        /* bf16 [2 hidden][dim] of a layer: rows w1_0, w3_0, w1_1, w3_1, ... */
 #define CE_LLAMA_W2 4         /* bf16 [dim][hidden] of a layer */
 #define CE_LLAMA_RMS_ATT 5    /* fp32 [dim] of a layer */
 #define CE_LLAMA_RMS_FFN 6    /* fp32 [dim] of a layer */

@@ -70,7 +70,8 @@ class LlamaOracle:
 
     cfg: dict with dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size,
     seq_len. weights: the device weights as host arrays (bf16 bits for the
-    matrices, fp32 RMSNorm weights), as Llama.weights() returns them.
+    matrices, fp32 RMSNorm weights), as Llama.weights() returns them; the
+    w13 rows interleave w1 and w3 (w1_0, w3_0, w1_1, ...).
     """
 
     def __init__(self, cfg, weights):
@@ -117,8 +118,8 @@ class LlamaOracle:
                 att[:, h, :] = np.einsum("nt,ntd->nd", p, vals)
             x = x + bf16_round(att.reshape(n, D)) @ self.wo[l].T
             xb = bf16_round(rmsnorm(x, self.rms_ffn[l]))
-            hh = xb @ self.w13[l].T
-            g, u = hh[:, :Hd], hh[:, Hd:]
+            hh = xb @ self.w13[l].T          # rows interleave w1 and w3
+            g, u = hh[:, 0::2], hh[:, 1::2]
             x = x + bf16_round(g / (1.0 + np.exp(-g)) * u) @ self.w2[l].T
         return bf16_round(rmsnorm(x, self.rms_final)) @ self.wcls.T
 

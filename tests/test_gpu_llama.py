@@ -58,6 +58,10 @@ def run_and_check(ce, O, cfg, batch, kv_fill, steps, seqs=None, seed=1):
     (dict(dim=256, hidden_dim=512, n_layers=2, n_heads=4, n_kv_heads=2, vocab_size=1000, seq_len=48), 3, 0, 5),
     (dict(dim=256, hidden_dim=384, n_layers=3, n_heads=2, vocab_size=260, seq_len=40), 4, 7, 4),
     (dict(dim=128, hidden_dim=256, n_layers=1, n_heads=2, vocab_size=128, seq_len=640), 2, 300, 3),
+    # K = 1024 over few output tiles: the w1|w3 GEMM runs split and SwiGLU runs as its own kernel
+    (dict(dim=1024, hidden_dim=256, n_layers=1, n_heads=8, vocab_size=256, seq_len=32), 4, 5, 3),
+    # 2 x hidden = 400: the SwiGLU epilogue's last tile is ragged
+    (dict(dim=128, hidden_dim=200, n_layers=2, n_heads=2, vocab_size=64, seq_len=32), 3, 4, 3),
 ])
 def test_small_configs_match_oracle(ce, O, cfg, batch, kv_fill, steps):
     run_and_check(ce, O, cfg, batch, kv_fill, steps)

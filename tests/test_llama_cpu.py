@@ -94,7 +94,7 @@ def _loop_step(c, W, tok, pos, kc, vc):
         x = [x[i] + o[i] for i in range(D)]
         xb = list(rnd(norm(x, W["rms_ffn"][l])))
         hh = matvec(llama_ref.to64(W["w13"][l]), xb)
-        sw = [hh[i] / (1 + math.exp(-hh[i])) * hh[Hd + i] for i in range(Hd)]
+        sw = [hh[2 * i] / (1 + math.exp(-hh[2 * i])) * hh[2 * i + 1] for i in range(Hd)]
         o = matvec(llama_ref.to64(W["w2"][l]), list(rnd(sw)))
         x = [x[i] + o[i] for i in range(D)]
     return matvec(llama_ref.to64(W["wcls"]), list(rnd(norm(x, W["rms_final"]))))
