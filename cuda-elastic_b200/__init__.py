@@ -110,6 +110,8 @@ _SIGNATURES = {
     "ce_decoder_copy_outputs": [_vp, _i, _vp, _vp, _vp, _vp],
     "ce_decoder_inject_fault": [_vp, _i],
     "ce_gemm_bf16_split": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _vp],
+    "ce_w4_pack": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "ce_gemm_w4a16": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp],
     "ce_llama_validate": [_vp, _i, _i, _i],
     "ce_llama_create": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _vp],
     "ce_llama_destroy": [_vp],
@@ -281,6 +283,21 @@ def gemm_bf16_split(d, a, b, splits, stream=None):
     assert d.shape == (splits, M, N)
     check(lib().ce_gemm_bf16_split(_ptr(d), _ptr(a), _ptr(b), M, N, lda, lda, ldb, N, splits, M * N,
                                    _stream(stream)))
+    return d
+
+
+def w4_pack(codes_t, scales_t, codes, scales, n, k, stream=None):
+    """NVFP4 weights (ce_quantize_nvfp4 layout) -> the W4A16 GEMM's k-block-major layout."""
+    check(lib().ce_w4_pack(_ptr(codes_t), _ptr(scales_t), _ptr(codes), _ptr(scales), n, k,
+                           codes.shape[1], scales.shape[1], _stream(stream)))
+
+
+def gemm_w4a16(d, a, codes_t, scales_t, alpha=None, n=None, stream=None):
+    """d [M][N] fp32 = alpha * A W^T, A bf16 bits [M][K], W packed by w4_pack."""
+    M, K = a.shape
+    N = d.shape[1] if n is None else n
+    check(lib().ce_gemm_w4a16(_ptr(d), _ptr(a), _ptr(codes_t), _ptr(scales_t), _ptr(alpha), M, N, K, K,
+                              d.shape[1], _stream(stream)))
     return d
 
 

@@ -33,6 +33,11 @@ int gemm_simt_fp32(float *d, const float *a, const float *b, int M, int N, int K
                    int ldb, int ldd, cudaStream_t s);
 int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
                     int ldb, int ldd, int splits, long long split_stride, cudaStream_t s, bool pdl);
+int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t,
+               const float *alpha, int M, int N, int K, int lda, int ldd, int splits,
+               long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
+int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
+            int ld_bytes, int nsf, cudaStream_t s);
 int gemm_status();
 int gemm_bs_status();
 int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
@@ -326,6 +331,17 @@ int ce_gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, in
                        int ldb, int ldd, int splits, int64_t split_stride, ce_stream_t stream) {
   return gemm_bf16_split(d, a, b, M, N, K, lda, ldb, ldd, splits, (long long)split_stride,
                          (cudaStream_t)stream, false);
+}
+
+int ce_w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N,
+               int K, int ld_bytes, int nsf, ce_stream_t stream) {
+  return w4_pack(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf, (cudaStream_t)stream);
+}
+
+int ce_gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t,
+                  const float *alpha, int M, int N, int K, int lda, int ldd, ce_stream_t stream) {
+  return gemm_w4a16(d, a, codes_t, scales_t, alpha, M, N, K, lda, ldd, 1, 0, nullptr, 0,
+                    (cudaStream_t)stream, false);
 }
 
 int ce_gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,

@@ -570,6 +570,306 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 }
 
 // ---------------------------------------------------------------------------
+// W4A16 GEMM: NVFP4 weights (E2M1 codes, UE4M3 scale per 16 values, one fp32
+// tensor decode scale alpha) against bf16 activations, the dequantization
+// fused into the GEMM. The weights stay 4.5 bits per value in HBM and are
+// expanded to bf16 in shared memory right before the tensor cores read them:
+//   warp 0     producer: TMA for the bf16 A tile; bulk copies of one 64-wide
+//              k-block of the B tile's codes ([kb][N][32 bytes]) and scales
+//              ([kb][N][4 bytes]), the k-block-major layout of gemm_w4_pack;
+//   warps 6-9  converters: code x scale (exact in bf16: at most 6 significant
+//              bits) into the 128-byte-swizzled K-major bf16 operand layout,
+//              then a proxy fence so the tensor cores see the stores;
+//   warp 1     MMA issuer (kind::f16, bf16 x bf16) once both are in;
+//   warps 2-5  epilogue: alpha x accumulator, with the split-K and SwiGLU
+//              modes of the bf16 GEMM.
+
+constexpr int kW4Threads = 320;
+
+template <int BN>
+struct SmemW4 {
+  static constexpr int a_bytes = BM * kRowBytes;
+  static constexpr int b_bytes = BN * kRowBytes;   // expanded bf16 operand
+  static constexpr int code_bytes = BN * 32;       // 64 E2M1 codes per row
+  static constexpr int scale_bytes = BN * 4;       // 4 UE4M3 scales per row
+  static constexpr int raw = a_bytes + b_bytes + code_bytes + scale_bytes;
+  static constexpr int stage_bytes = ((raw + 1023) / 1024) * 1024;  // keep the swizzled tiles 1 KB aligned
+  static constexpr int max_stages = (232448 - 2048) / stage_bytes;
+  static constexpr int stages = max_stages > 6 ? 6 : max_stages;
+  static constexpr int bar_offset = stages * stage_bytes;
+  static constexpr int total = bar_offset + 512 + 1024;
+};
+
+struct W4Args {
+  GemmArgs g;
+  const uint8_t *codes;   // [k_blocks][N][32]
+  const uint8_t *scales;  // [k_blocks][N][4]
+  const float *alpha;     // weight decode scale (device) or nullptr
+};
+
+__device__ __forceinline__ void bulk_g2s_gemm(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Unsigned E4M3 (bias 7, three mantissa bits; exponent 0 subnormal).
+__device__ __forceinline__ float ue4m3_value(uint32_t c) {
+  const uint32_t e = (c >> 3) & 15u, m = c & 7u;
+  return e == 0 ? (float)m * 0.001953125f : __uint_as_float(((e + 120u) << 23) | (m << 20));
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kW4Threads, 1)
+gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tmA, W4Args wargs) {
+  using S = SmemW4<BN>;
+  const GemmArgs &args = wargs.g;
+  constexpr int kMmasPerStage = 4;                 // 64 bf16 of K per stage, 16 per MMA
+  constexpr uint32_t kIdesc = instr_desc<0, BN>();
+  constexpr uint32_t kAccStride = 256;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_offset);
+  uint64_t *conv = full + S::stages;
+  uint64_t *empty = conv + S::stages;
+  uint64_t *tmem_full = empty + S::stages;
+  uint64_t *tmem_empty = tmem_full + 2;
+  uint64_t *drain = tmem_empty + 2;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  __shared__ float e2m1[16];
+
+  DeviceStatus *st = &g_gemm_status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_units = args.tiles_m * args.tiles_n * args.splits;
+
+  if (threadIdx.x < 16) {
+    const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+    e2m1[threadIdx.x] = threadIdx.x < 8 ? mag[threadIdx.x] : -mag[threadIdx.x - 8];
+  }
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);  // one arrival per converter warp
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0) {
+    // ---------------- producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued_mask = 0, issued_parity = 0;
+    bool okay = true;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
+      const Unit w = unit_of(args, t);
+      const int m0 = (w.tile % args.tiles_m) * BM;
+      const int n0 = (w.tile / args.tiles_m) * BN;
+      const int rows = min(BN, args.N - n0);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&empty[stage], phase ^ 1u, st, 41)) {
+          okay = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t *a_dst = smem + stage * S::stage_bytes;
+          uint8_t *c_dst = a_dst + S::a_bytes + S::b_bytes;
+          uint8_t *s_dst = c_dst + S::code_bytes;
+          mbar_arrive_expect_tx(&full[stage], S::a_bytes + rows * 36);
+          tma_load_2d(a_dst, &tmA, &full[stage], kb * 64, m0);
+          const size_t rowbase = (size_t)kb * args.N + n0;
+          bulk_g2s_gemm(c_dst, wargs.codes + rowbase * 32, rows * 32, &full[stage]);
+          bulk_g2s_gemm(s_dst, wargs.scales + rowbase * 4, rows * 4, &full[stage]);
+        }
+        __syncwarp();
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == S::stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    for (int s = 0; s < S::stages; ++s)
+      if (issued_mask & (1u << s)) warp_wait(&full[s], (issued_parity >> s) & 1u, st, 42);
+  } else if (warp >= 6) {
+    // ---------------- converters: E2M1 x UE4M3 -> swizzled bf16
+    const int ct = threadIdx.x - 192;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool okay = true;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
+      const Unit w = unit_of(args, t);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&full[stage], phase, st, 43)) {
+          okay = false;
+          break;
+        }
+        uint8_t *a_s = smem + stage * S::stage_bytes;
+        uint8_t *b_s = a_s + S::a_bytes;
+        const uint8_t *c_s = b_s + S::b_bytes;
+        const uint8_t *s_s = c_s + S::code_bytes;
+#pragma unroll 2
+        for (int u = ct; u < BN * 8; u += 128) {
+          const int r = u >> 3, c = u & 7;  // row, 16-byte chunk (8 values) of the row
+          const uint32_t q = *reinterpret_cast<const uint32_t *>(c_s + r * 32 + c * 4);
+          const float sc = ue4m3_value(s_s[r * 4 + (c >> 1)]);
+          uint32_t o[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float lo = e2m1[(q >> (8 * j)) & 15u] * sc;
+            const float hi = e2m1[(q >> (8 * j + 4)) & 15u] * sc;
+            __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+            o[j] = *reinterpret_cast<uint32_t *>(&v);
+          }
+          *reinterpret_cast<uint4 *>(b_s + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&conv[stage]);
+        if (++stage == S::stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    bool okay = true;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!warp_wait(&tmem_empty[acc], acc_phase ^ 1u, st, 44)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tmem_base + (uint32_t)acc * kAccStride;
+      const Unit w = unit_of(args, t);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&full[stage], phase, st, 45) || !warp_wait(&conv[stage], phase, st, 46)) {
+          okay = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(smem + stage * S::stage_bytes);
+          const uint32_t b_addr = a_addr + S::a_bytes;
+#pragma unroll
+          for (int k = 0; k < kMmasPerStage; ++k) {
+            const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32);
+            const uint64_t b_desc = smem_desc_sw128(b_addr + k * 32);
+            tc_mma<0>(d_tmem, a_desc, b_desc, kIdesc, ((kb - w.kb0) | k) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+        }
+        __syncwarp();
+        if (++stage == S::stages) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (okay && lane == 0) tc_commit(&tmem_full[acc]);
+      __syncwarp();
+    }
+    if (lane == 0) tc_commit(drain);
+    __syncwarp();
+    warp_wait(drain, 0, st, 47);
+  } else {
+    // ---------------- epilogue (warps 2-5)
+    const int quarter = warp & 3;
+    const float alpha = wargs.alpha != nullptr ? *wargs.alpha : 1.0f;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_units; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!warp_wait(&tmem_full[acc], acc_phase, st, 48)) break;
+      tc_fence_after();
+      const Unit w = unit_of(args, t);
+      const int m0 = (w.tile % args.tiles_m) * BM;
+      const int n0 = (w.tile / args.tiles_m) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      float *drow = w.d + (size_t)row * args.ldd;
+      const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(w.d) & 15u) == 0);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kAccStride + c, r);
+        tmem_ld_wait();
+        if (row < args.M) {
+          const int col0 = n0 + c;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+          if (args.epilogue == 1) {
+            store_swiglu(args, row, col0, v);
+          } else if (vec_ok && col0 + 32 <= args.N) {
+            float4 *dst = reinterpret_cast<float4 *>(drow + col0);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < args.N) drow[col0 + j] = v[j];
+          }
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// k-block-major copy of row-major NVFP4 weights: codes [N][ld_bytes] (two
+// per byte) and scales [N][nsf] -> codes_t [K/64][N][32], scales_t [K/64][N][4].
+__global__ void w4_pack_kernel(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes,
+                               const uint8_t *scales, int N, int K, int ld_bytes, int nsf) {
+  const int kbs = K / 64;
+  const size_t words = (size_t)kbs * N * 8;  // 4-byte words of codes_t
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += step) {
+    const size_t kb = i / ((size_t)N * 8), rem = i % ((size_t)N * 8);
+    const size_t n = rem / 8, j = rem % 8;
+    const uint8_t *src = codes + n * ld_bytes + kb * 32 + j * 4;
+    uint32_t v = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) | ((uint32_t)src[3] << 24);
+    reinterpret_cast<uint32_t *>(codes_t)[i] = v;
+    if (j == 0) {
+      const uint8_t *ss = scales + n * nsf + kb * 4;
+      reinterpret_cast<uint32_t *>(scales_t)[kb * N + n] =
+          (uint32_t)ss[0] | ((uint32_t)ss[1] << 8) | ((uint32_t)ss[2] << 16) | ((uint32_t)ss[3] << 24);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Host side
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -820,6 +1120,76 @@ int gemm_bf16_swiglu(uint16_t *out, int ld_out, const uint16_t *a, const uint16_
                      int K, int lda, int ldb, cudaStream_t s, bool pdl) {
   return gemm_dispatch<0>(nullptr, a, b, M, N, K, lda, ldb, N, nullptr, nullptr, 0, 0, s, 1, 0, pdl,
                           out, ld_out);
+}
+
+// W4A16 GEMM (see gemm_w4a16_kernel): d = alpha x A W^T with W in the
+// k-block-major NVFP4 layout of w4_pack; split-K partials and the SwiGLU
+// epilogue as in gemm_bf16_split / gemm_bf16_swiglu.
+int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t,
+               const float *alpha, int M, int N, int K, int lda, int ldd, int splits,
+               long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl) {
+  CE_REQUIRE(M >= 1 && N >= 1 && K >= 64, "W4A16 GEMM dims (M=%d N=%d K=%d)", M, N, K);
+  CE_REQUIRE(K % 64 == 0 && N % 4 == 0, "W4A16 GEMM needs K %% 64 == 0 and N %% 4 == 0 (K=%d N=%d)", K, N);
+  CE_REQUIRE(lda >= K && (lda * 2) % 16 == 0, "lda must be >= K and a multiple of 8 (got %d)", lda);
+  CE_REQUIRE(a && codes_t && scales_t && (d || swiglu_out), "null operand");
+  CE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(codes_t) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(scales_t) & 15u) == 0,
+             "operands must be 16-byte aligned");
+  const int k_blocks = K / 64;
+  CE_REQUIRE(splits >= 1 && splits <= k_blocks, "split count must be in [1, %d] (got %d)", k_blocks, splits);
+  CE_REQUIRE(swiglu_out == nullptr || (splits == 1 && N % 2 == 0 && swiglu_ld >= N / 2),
+             "the SwiGLU epilogue needs one split, an even N and ld_out >= N / 2");
+  CE_REQUIRE(swiglu_out != nullptr || ldd >= N, "ldd must be >= N");
+  if (!is_sm100()) return set_error(CE_ERR_USAGE, "tcgen05 GEMM needs an sm_100 device");
+  const int sms = sm_count();
+  // tile width: 128 unless narrower tiles give more CTAs at decode sizes
+  const int tiles_m = (M + BM - 1) / BM;
+  const int bn = (long long)tiles_m * ((N + 127) / 128) * splits < sms ? 64 : 128;
+  CUtensorMap ta;
+  int rc = make_operand_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BM);
+  if (rc) return rc;
+  W4Args w{};
+  w.g.d = d;
+  w.g.M = M;
+  w.g.N = N;
+  w.g.K = K;
+  w.g.ldd = ldd;
+  w.g.tiles_m = tiles_m;
+  w.g.tiles_n = (N + bn - 1) / bn;
+  w.g.k_blocks = k_blocks;
+  w.g.splits = splits;
+  w.g.split_stride = splits > 1 ? split_stride : 0;
+  w.g.epilogue = swiglu_out != nullptr ? 1 : 0;
+  w.g.out_bf16 = swiglu_out;
+  w.g.ld_out = swiglu_ld;
+  w.codes = codes_t;
+  w.scales = scales_t;
+  w.alpha = alpha;
+  const int units = w.g.tiles_m * w.g.tiles_n * splits;
+  const int grid = units < sms ? units : sms;
+  if (bn == 64) {
+    rc = configure_smem<gemm_w4a16_kernel<64>>(SmemW4<64>::total);
+    if (rc) return rc;
+    return launch_kernel(gemm_w4a16_kernel<64>, dim3(grid), dim3(kW4Threads), SmemW4<64>::total, s, pdl,
+                         "gemm_w4a16_kernel", ta, w);
+  }
+  rc = configure_smem<gemm_w4a16_kernel<128>>(SmemW4<128>::total);
+  if (rc) return rc;
+  return launch_kernel(gemm_w4a16_kernel<128>, dim3(grid), dim3(kW4Threads), SmemW4<128>::total, s, pdl,
+                       "gemm_w4a16_kernel", ta, w);
+}
+
+int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
+            int ld_bytes, int nsf, cudaStream_t s) {
+  CE_REQUIRE(codes_t && scales_t && codes && scales, "null argument");
+  CE_REQUIRE(N >= 1 && K >= 64 && K % 64 == 0 && ld_bytes * 2 >= K && nsf * 16 >= K,
+             "bad NVFP4 weight shape %dx%d (ld_bytes %d, scales per row %d)", N, K, ld_bytes, nsf);
+  const size_t words = (size_t)(K / 64) * N * 8;
+  int blocks = (int)((words + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  w4_pack_kernel<<<blocks, 256, 0, s>>>(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf);
+  CE_LAUNCH_CHECK("w4_pack_kernel");
+  return CE_OK;
 }
 
 int gemm_set_prefetch(int kblocks) {

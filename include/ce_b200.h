@@ -169,6 +169,25 @@ int ce_gemm_bf16_split(float *d_dev, const uint16_t *a_dev, const uint16_t *b_de
                        int K, int lda, int ldb, int ldd, int splits, int64_t split_stride,
                        ce_stream_t stream);
 
+/* Repacks NVFP4 weights from the ce_quantize_nvfp4 layout (codes [N][ld_bytes],
+ * two per byte; UE4M3 scales [N][nsf], nsf = K / 16) into the k-block-major
+ * layout the W4A16 GEMM streams: codes_t [K/64][N][32], scales_t [K/64][N][4].
+ * K % 64 == 0. Setup-time. */
+int ce_w4_pack(uint8_t *codes_t_dev, uint8_t *scales_t_dev, const uint8_t *codes_dev,
+               const uint8_t *scales_dev, int N, int K, int ld_bytes, int nsf, ce_stream_t stream);
+
+/* W4A16 GEMM with the dequantization fused: D[m][n] = alpha * sum_k
+ * A[m][k] * W[n][k], A bf16 [M][lda], W NVFP4 in the ce_w4_pack layout
+ * (E2M1 code x UE4M3 scale, expanded to bf16 in shared memory right before
+ * the tensor cores read it), alpha = the weight's decode scale (device fp32,
+ * element 1 of ce_quantize_nvfp4's tensor scales; NULL = 1), fp32
+ * accumulation and output. K % 64 == 0, N % 4 == 0. The reference's NVFP4
+ * GEMM quantizes the activations too (decoder_lowprec.cu:111-127); this one
+ * keeps them bf16. */
+int ce_gemm_w4a16(float *d_dev, const uint16_t *a_dev, const uint8_t *codes_t_dev,
+                  const uint8_t *scales_t_dev, const float *alpha_dev, int M, int N, int K, int lda,
+                  int ldd, ce_stream_t stream);
+
 /* Library-wide GEMM tuning, set at setup time (not during a capture): the
  * TMA producer prefetches operand tiles this many k-blocks ahead into L2
  * (0 = off, at most 64). */

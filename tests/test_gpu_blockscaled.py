@@ -155,3 +155,46 @@ def test_plan_block_scaled(ce, O, dev, prec, shape):
     ref32, _ = O.gemm_ref(O.rmsnorm_ref(x[rows], w), W)
     assert O.rel_l2(ho, ref32) <= (0.12 if prec == "mxfp6" else 0.25)
     plan.close()
+
+
+W4_SHAPES = [(64, 4096, 1024), (256, 768, 2048), (130, 452, 320), (1, 8, 64), (300, 1000, 1024)]
+
+
+@pytest.mark.parametrize("shape", W4_SHAPES)
+def test_gemm_w4a16_nvfp4_weights_bf16_activations(ce, O, dev, shape):
+    """NVFP4 weights expanded to bf16 inside the GEMM (the decode GEMM of the
+    7B-shaped decoder): against the double GEMM of the bf16 activations and
+    the dequantized weights, times the weight decode scale."""
+    M, N, K = shape
+    A, B = _operands(O, M, N, K, 6)
+    codes = torch.empty((N, K // 2), dtype=torch.uint8, device=dev)
+    sc = torch.empty((N, K // 16), dtype=torch.uint8, device=dev)
+    ts = torch.empty(2, device=dev)
+    scratch = torch.zeros(1, dtype=torch.int32, device=dev)
+    ce.quantize_nvfp4(codes, sc, ts, scratch, torch.from_numpy(B).to(dev))
+    ct = torch.empty((K // 64) * N * 32, dtype=torch.uint8, device=dev)
+    st = torch.empty((K // 64) * N * 4, dtype=torch.uint8, device=dev)
+    ce.w4_pack(ct, st, codes, sc, N, K)
+    abits = O.bf16_bits(A)
+    da = torch.from_numpy(abits.view(np.int16)).to(dev)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_w4a16(d, da, ct, st, ts[1:])
+    ce.device_status()
+    a = O.bf16_value(abits).astype(np.float64)
+    b = _nv_dequant(O, codes.cpu().numpy(), sc.cpu().numpy(), K)
+    _check(O, d.cpu().numpy(), a, b, float(ts.cpu().numpy()[1]))
+
+
+def test_w4_pack_layout(ce, O, dev):
+    N, K = 12, 192
+    rng = np.random.default_rng(2)
+    codes = rng.integers(0, 256, (N, K // 2), dtype=np.uint8)
+    sc = rng.integers(0, 120, (N, K // 16), dtype=np.uint8)
+    ct = torch.empty((K // 64) * N * 32, dtype=torch.uint8, device=dev)
+    st = torch.empty((K // 64) * N * 4, dtype=torch.uint8, device=dev)
+    ce.w4_pack(ct, st, torch.from_numpy(codes).to(dev), torch.from_numpy(sc).to(dev), N, K)
+    ct = ct.cpu().numpy().reshape(K // 64, N, 32)
+    st = st.cpu().numpy().reshape(K // 64, N, 4)
+    for kb in range(K // 64):
+        assert np.array_equal(ct[kb], codes[:, kb * 32:(kb + 1) * 32])
+        assert np.array_equal(st[kb], sc[:, kb * 4:(kb + 1) * 4])
