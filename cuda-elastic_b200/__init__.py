@@ -119,6 +119,7 @@ _SIGNATURES = {
     "ce_llama_start": [_vp, _vp, _i, _vp],
     "ce_llama_enqueue_step": [_vp, _vp],
     "ce_llama_set_pdl": [_vp, _i],
+    "ce_llama_read_nvfp4": [_vp, _i, _i, _vp, _vp, _vp],
     "ce_llama_read": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_write": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_status": [],
@@ -624,17 +625,41 @@ class Llama:
             out[kh] = self.read(which, layer, np.uint16, n * self.hs, off).reshape(n, self.hs)
         return out
 
-    def weights(self):
-        """Every weight as host arrays (bf16 bits as uint16, RMSNorm fp32)."""
+    def nvfp4_weight(self, which, layer=0):
+        """NVFP4 model: (codes uint8 [rows][cols / 2] two per byte, even index
+        in the low nibble; UE4M3 scales uint8 [rows][cols / 16]; decode scale)
+        of one weight matrix, un-packed from the W4A16 k-block-major layout."""
+        rows, cols = self._shape(which)
+        codes = np.empty(rows * cols // 2, np.uint8)
+        scales = np.empty(rows * cols // 16, np.uint8)
+        alpha = np.empty(2, np.float32)
+        check(lib().ce_llama_read_nvfp4(self._h, which, layer, codes.ctypes.data, scales.ctypes.data,
+                                        alpha.ctypes.data))
+        kb = cols // 64
+        codes = codes.reshape(kb, rows, 32).transpose(1, 0, 2).reshape(rows, cols // 2)
+        scales = scales.reshape(kb, rows, 4).transpose(1, 0, 2).reshape(rows, cols // 16)
+        return codes, scales, float(alpha[1])
+
+    def _shape(self, which):
         c = self.cfg
+        return {LLAMA_WQKV: (c.dim + 2 * self.kv_dim, c.dim), LLAMA_WO: (c.dim, c.dim),
+                LLAMA_W13: (2 * c.hidden_dim, c.dim), LLAMA_W2: (c.dim, c.hidden_dim),
+                LLAMA_WCLS: (c.vocab_size, c.dim)}[which]
+
+    def weights(self):
+        """Every weight as host arrays: bf16 bits (uint16) for a bf16 model,
+        (codes, scales, decode scale) tuples from nvfp4_weight for the GEMM
+        weights of an NVFP4 model; the embedding is bf16 bits and the RMSNorm
+        weights fp32 either way."""
+        c = self.cfg
+        nv = self.precision == PREC_NVFP4_E2M1
         w = {"tok_emb": self.read(LLAMA_TOK_EMB).reshape(c.vocab_size, c.dim),
-             "wcls": self.read(LLAMA_WCLS).reshape(c.vocab_size, c.dim),
+             "wcls": self.nvfp4_weight(LLAMA_WCLS) if nv else self.read(LLAMA_WCLS).reshape(c.vocab_size, c.dim),
              "rms_final": self.read(LLAMA_RMS_FINAL, dtype=np.float32)}
-        for key, which, shape in (("wqkv", LLAMA_WQKV, (c.dim + 2 * self.kv_dim, c.dim)),
-                                  ("wo", LLAMA_WO, (c.dim, c.dim)),
-                                  ("w13", LLAMA_W13, (2 * c.hidden_dim, c.dim)),
-                                  ("w2", LLAMA_W2, (c.dim, c.hidden_dim))):
-            w[key] = [self.read(which, l).reshape(shape) for l in range(c.n_layers)]
+        for key, which in (("wqkv", LLAMA_WQKV), ("wo", LLAMA_WO), ("w13", LLAMA_W13), ("w2", LLAMA_W2)):
+            shape = self._shape(which)
+            w[key] = [self.nvfp4_weight(which, l) if nv else self.read(which, l).reshape(shape)
+                      for l in range(c.n_layers)]
         w["rms_att"] = [self.read(LLAMA_RMS_ATT, l, np.float32) for l in range(c.n_layers)]
         w["rms_ffn"] = [self.read(LLAMA_RMS_FFN, l, np.float32) for l in range(c.n_layers)]
         return w

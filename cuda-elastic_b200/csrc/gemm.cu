@@ -1144,7 +1144,7 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
   const int sms = sm_count();
   // tile width: 128 unless narrower tiles give more CTAs at decode sizes
   const int tiles_m = (M + BM - 1) / BM;
-  const int bn = (long long)tiles_m * ((N + 127) / 128) * splits < sms ? 64 : 128;
+  const int bn = (long long)tiles_m * ((N + 127) / 128) < sms ? 64 : 128;
   CUtensorMap ta;
   int rc = make_operand_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BM);
   if (rc) return rc;
@@ -1177,6 +1177,22 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
   if (rc) return rc;
   return launch_kernel(gemm_w4a16_kernel<128>, dim3(grid), dim3(kW4Threads), SmemW4<128>::total, s, pdl,
                        "gemm_w4a16_kernel", ta, w);
+}
+
+// Split count that fills the SMs for a W4A16 GEMM of this shape (tiles of
+// the width gemm_w4a16 picks, times splits, up to one CTA per SM), with at
+// least min_kblocks 64-wide k-blocks per split; at most max_splits.
+int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks) {
+  const int sms = sm_count();
+  if (sms <= 0) return 1;
+  const long long tiles_m = (M + BM - 1) / BM;
+  const int bn = tiles_m * ((N + 127) / 128) < sms ? 64 : 128;
+  const long long tiles = tiles_m * ((N + bn - 1) / bn);
+  long long sp = sms / (tiles > 0 ? tiles : 1);
+  sp = sp < (long long)max_splits ? sp : (long long)max_splits;
+  const long long by_k = (K / 64) / (min_kblocks > 0 ? min_kblocks : 1);
+  sp = sp < by_k ? sp : by_k;
+  return sp < 1 ? 1 : (int)sp;
 }
 
 int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,

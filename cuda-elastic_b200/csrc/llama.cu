@@ -26,6 +26,7 @@
 // graph replays for every token.
 #include <cuda_bf16.h>
 
+#include <algorithm>
 #include <cmath>
 #include <type_traits>
 #include <vector>
@@ -43,6 +44,14 @@ int gemm_bf16_split(float *d, const uint16_t *a, const uint16_t *b, int M, int N
 int gemm_bf16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
 int gemm_bf16_swiglu(uint16_t *out, int ld_out, const uint16_t *a, const uint16_t *b, int M, int N,
                      int K, int lda, int ldb, cudaStream_t s, bool pdl);
+int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t,
+               const float *alpha, int M, int N, int K, int lda, int ldd, int splits,
+               long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
+int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
+int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
+            int ld_bytes, int nsf, cudaStream_t s);
+int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
+                   const float *x, int rows, int cols, int ld_bytes, cudaStream_t s);
 
 static __device__ DeviceStatus g_llama_status;
 
@@ -86,6 +95,17 @@ __global__ void init_normal_bf16_kernel(uint16_t *out, size_t n, uint64_t seed, 
     const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
     __nv_bfloat16 h = __float2bfloat16_rn(z * std);
     out[i] = *reinterpret_cast<uint16_t *>(&h);
+  }
+}
+
+// As init_normal_bf16_kernel, fp32 values (the source of quantized weights).
+__global__ void init_normal_f32_kernel(float *out, size_t n, uint64_t seed, uint64_t stream, float std) {
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const uint64_t r = mix64(seed ^ mix64(stream * 0x632BE59BD9B4E019ull + i));
+    const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((r >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    out[i] = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2) * std;
   }
 }
 
@@ -511,6 +531,14 @@ int pow2_at_least(int v) {
 
 using namespace ce;
 
+// One NVFP4 weight matrix in the W4A16 GEMM's layout.
+struct QMat {
+  uint8_t *codes;   // [cols/64][rows][32]
+  uint8_t *scales;  // [cols/64][rows][4]
+  float *alpha;     // (encode, decode) tensor scales; the GEMM uses alpha[1]
+  int rows, cols;
+};
+
 struct ce_llama {
   ce_llama_config c{};
   int B = 0, cap = 0, precision = 0;
@@ -530,6 +558,11 @@ struct ce_llama {
         *part = nullptr;
   int *tokens = nullptr, *generated = nullptr, *pos = nullptr, *step = nullptr;
   int *arrivals = nullptr;  // per (sequence, head) chunk arrivals of the attention merge
+  // NVFP4 weights (precision CE_PREC_NVFP4_E2M1): matrix 4 l + k of layer l
+  // is k = 0 wqkv, 1 wo, 2 w13, 3 w2; matrix 4 n_layers is the classifier
+  uint8_t *q_codes = nullptr, *q_scales = nullptr;
+  float *q_alpha = nullptr;
+  std::vector<QMat> qm;
 };
 
 namespace {
@@ -540,7 +573,8 @@ void free_llama(ce_llama *m) {
                   (void *)m->rope, (void *)m->kcache, (void *)m->vcache, (void *)m->xb, (void *)m->att,
                   (void *)m->hb, (void *)m->x, (void *)m->delta, (void *)m->qkv, (void *)m->h,
                   (void *)m->logits, (void *)m->part, (void *)m->tokens, (void *)m->generated,
-                  (void *)m->pos, (void *)m->step, (void *)m->arrivals})
+                  (void *)m->pos, (void *)m->step, (void *)m->arrivals, (void *)m->q_codes,
+                  (void *)m->q_scales, (void *)m->q_alpha})
     if (p) cudaFree(p);
   delete m;
 }
@@ -549,6 +583,15 @@ size_t wqkv_elems(const ce_llama *m) { return (size_t)m->qkv_rows * m->c.dim; }
 size_t wo_elems(const ce_llama *m) { return (size_t)m->c.dim * m->c.dim; }
 size_t w13_elems(const ce_llama *m) { return (size_t)2 * m->c.hidden_dim * m->c.dim; }
 size_t w2_elems(const ce_llama *m) { return (size_t)m->c.dim * m->c.hidden_dim; }
+
+// (rows, cols) of weight kind k: 0 wqkv, 1 wo, 2 w13, 3 w2, 4 classifier.
+void mat_shape(const ce_llama *m, int k, int *rows, int *cols) {
+  const ce_llama_config &c = m->c;
+  const int r[5] = {m->qkv_rows, c.dim, 2 * c.hidden_dim, c.dim, c.vocab_size};
+  const int q[5] = {c.dim, c.dim, c.dim, c.hidden_dim, c.dim};
+  *rows = r[k];
+  *cols = q[k];
+}
 
 struct TensorView {
   void *ptr;
@@ -562,6 +605,10 @@ int tensor_of(ce_llama *m, int which, int layer, TensorView *v) {
                          which == CE_LLAMA_W2 || which == CE_LLAMA_RMS_ATT || which == CE_LLAMA_RMS_FFN ||
                          which == CE_LLAMA_KCACHE || which == CE_LLAMA_VCACHE;
   CE_REQUIRE(!per_layer || (layer >= 0 && layer < c.n_layers), "layer %d out of range", layer);
+  const bool bf16_weight = which == CE_LLAMA_WQKV || which == CE_LLAMA_WO || which == CE_LLAMA_W13 ||
+                           which == CE_LLAMA_W2 || which == CE_LLAMA_WCLS;
+  CE_REQUIRE(!bf16_weight || m->precision == CE_PREC_BF16,
+             "tensor %d is not stored in this precision (see ce_llama_read_nvfp4)", which);
   const size_t L = (size_t)layer;
   switch (which) {
     case CE_LLAMA_TOK_EMB: *v = {m->tok_emb, (size_t)c.vocab_size * c.dim * 2}; break;
@@ -603,11 +650,16 @@ int ce_llama_validate(const ce_llama_config *c, int batch, int max_steps, int pr
   CE_REQUIRE(c->seq_len >= 1 && c->seq_len <= (1 << 20), "seq_len must be in [1, 2^20] (got %d)", c->seq_len);
   CE_REQUIRE(batch >= 1 && batch <= 65535, "batch must be in [1, 65535] (got %d)", batch);
   CE_REQUIRE(max_steps >= 1, "max_steps must be >= 1 (got %d)", max_steps);
-  CE_REQUIRE(precision == CE_PREC_BF16, "llama weight precision %d is not available", precision);
+  CE_REQUIRE(precision == CE_PREC_BF16 || precision == CE_PREC_NVFP4_E2M1,
+             "llama weight precision %d is not available (bf16 or NVFP4)", precision);
+  CE_REQUIRE(precision != CE_PREC_NVFP4_E2M1 || (c->dim % 64 == 0 && c->hidden_dim % 64 == 0),
+             "NVFP4 weights need dim and hidden_dim multiples of 64 (got %d, %d)", c->dim, c->hidden_dim);
   const double kv = 2.0 * c->n_layers * (double)batch * (c->dim / c->n_heads) * c->n_kv_heads * c->seq_len * 2;
-  const double w = 2.0 * ((double)c->n_layers * ((double)(c->dim + 2 * hs * c->n_kv_heads) * c->dim +
-                                                 (double)c->dim * c->dim + 3.0 * c->hidden_dim * c->dim) +
-                          2.0 * (double)c->vocab_size * c->dim);
+  const double per_value = precision == CE_PREC_NVFP4_E2M1 ? 0.5625 : 2.0;
+  const double w = per_value * ((double)c->n_layers * ((double)(c->dim + 2 * hs * c->n_kv_heads) * c->dim +
+                                                       (double)c->dim * c->dim + 3.0 * c->hidden_dim * c->dim) +
+                                (double)c->vocab_size * c->dim) +
+                   2.0 * (double)c->vocab_size * c->dim;
   CE_REQUIRE(kv + w <= 170.0 * (1LL << 30),
              "model and KV cache need %.1f GiB of device memory (limit 170 GiB)", (kv + w) / (1LL << 30));
   return CE_OK;
@@ -641,10 +693,11 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   m->layer_kv = (size_t)batch * cfg->n_kv_heads * cfg->seq_len * m->hs;
   // split-K for the GEMMs whose tiles alone leave SMs idle at decode sizes;
   // at least 4 k-blocks (256 of K) per split
-  m->sp_qkv = gemm_bf16_auto_splits(batch, m->qkv_rows, cfg->dim, 8, 4);
-  m->sp_o = gemm_bf16_auto_splits(batch, cfg->dim, cfg->dim, 8, 4);
-  m->sp_13 = gemm_bf16_auto_splits(batch, 2 * cfg->hidden_dim, cfg->dim, 8, 4);
-  m->sp_2 = gemm_bf16_auto_splits(batch, cfg->dim, cfg->hidden_dim, 8, 4);
+  auto splits = precision == CE_PREC_NVFP4_E2M1 ? gemm_w4a16_auto_splits : gemm_bf16_auto_splits;
+  m->sp_qkv = splits(batch, m->qkv_rows, cfg->dim, 8, 4);
+  m->sp_o = splits(batch, cfg->dim, cfg->dim, 8, 4);
+  m->sp_13 = splits(batch, 2 * cfg->hidden_dim, cfg->dim, 8, 4);
+  m->sp_2 = splits(batch, cfg->dim, cfg->hidden_dim, 8, 4);
   const int sp_delta = m->sp_o > m->sp_2 ? m->sp_o : m->sp_2;
   const ce_llama_config &c = *cfg;
   const size_t L = c.n_layers;
@@ -659,11 +712,36 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
     }                                                  \
   } while (0)
   CE_ALLOC(m->tok_emb, (size_t)c.vocab_size * c.dim * 2);
-  CE_ALLOC(m->wqkv, L * wqkv_elems(m) * 2);
-  CE_ALLOC(m->wo, L * wo_elems(m) * 2);
-  CE_ALLOC(m->w13, L * w13_elems(m) * 2);
-  CE_ALLOC(m->w2, L * w2_elems(m) * 2);
-  CE_ALLOC(m->wcls, (size_t)c.vocab_size * c.dim * 2);
+  if (precision == CE_PREC_NVFP4_E2M1) {
+    size_t codes = 0, scales = 0;
+    const int nmat = 4 * c.n_layers + 1;
+    for (int i = 0; i < nmat; ++i) {
+      int r, q;
+      mat_shape(m, i == 4 * c.n_layers ? 4 : i % 4, &r, &q);
+      codes += (size_t)r * q / 2;
+      scales += (size_t)r * q / 16;
+    }
+    CE_ALLOC(m->q_codes, codes);
+    CE_ALLOC(m->q_scales, scales);
+    CE_ALLOC(m->q_alpha, (size_t)nmat * 2 * 4);
+    codes = scales = 0;
+    for (int i = 0; i < nmat; ++i) {
+      QMat q{};
+      mat_shape(m, i == 4 * c.n_layers ? 4 : i % 4, &q.rows, &q.cols);
+      q.codes = m->q_codes + codes;
+      q.scales = m->q_scales + scales;
+      q.alpha = m->q_alpha + 2 * i;
+      codes += (size_t)q.rows * q.cols / 2;
+      scales += (size_t)q.rows * q.cols / 16;
+      m->qm.push_back(q);
+    }
+  } else {
+    CE_ALLOC(m->wqkv, L * wqkv_elems(m) * 2);
+    CE_ALLOC(m->wo, L * wo_elems(m) * 2);
+    CE_ALLOC(m->w13, L * w13_elems(m) * 2);
+    CE_ALLOC(m->w2, L * w2_elems(m) * 2);
+    CE_ALLOC(m->wcls, (size_t)c.vocab_size * c.dim * 2);
+  }
   CE_ALLOC(m->rms_att, L * c.dim * 4);
   CE_ALLOC(m->rms_ffn, L * c.dim * 4);
   CE_ALLOC(m->rms_final, (size_t)c.dim * 4);
@@ -732,8 +810,38 @@ int ce_llama_init_random(ce_llama *m, uint64_t seed, float weight_std, int kv_fi
                         {m->wcls, (size_t)c.vocab_size * c.dim, weight_std}};
   uint64_t stream_id = 1;
   for (const Item &it : items) {
-    init_normal_bf16_kernel<<<grid, threads, 0, s>>>(it.p, it.n, seed, stream_id++, it.std, it.n, it.n);
+    const uint64_t id = stream_id++;
+    if (it.p == nullptr) continue;  // NVFP4 model: quantized below
+    init_normal_bf16_kernel<<<grid, threads, 0, s>>>(it.p, it.n, seed, id, it.std, it.n, it.n);
     CE_LAUNCH_CHECK("init_normal_bf16_kernel");
+  }
+  if (m->precision == CE_PREC_NVFP4_E2M1) {
+    // every matrix: fp32 N(0, std), then the NVFP4 quantizer (tensor amax,
+    // UE4M3 per 16 values, E2M1 codes), then the W4A16 GEMM's layout
+    size_t biggest = 0;
+    for (const QMat &q : m->qm) biggest = std::max(biggest, (size_t)q.rows * q.cols);
+    float *tmp = nullptr;
+    uint8_t *tcodes = nullptr, *tscales = nullptr;
+    unsigned int *amax = nullptr;
+    cudaError_t e = cudaMalloc(&tmp, biggest * 4);
+    if (e == cudaSuccess) e = cudaMalloc(&tcodes, biggest / 2);
+    if (e == cudaSuccess) e = cudaMalloc(&tscales, biggest / 16);
+    if (e == cudaSuccess) e = cudaMalloc(&amax, 4);
+    int rc = e == cudaSuccess ? CE_OK : cuda_error(e, "cudaMalloc(quantization scratch)");
+    for (size_t i = 0; i < m->qm.size() && rc == CE_OK; ++i) {
+      const QMat &q = m->qm[i];
+      const size_t n = (size_t)q.rows * q.cols;
+      init_normal_f32_kernel<<<grid, threads, 0, s>>>(tmp, n, seed, 1000 + i, weight_std);
+      e = cudaPeekAtLastError();
+      if (e != cudaSuccess) rc = cuda_error(e, "init_normal_f32_kernel");
+      if (rc == CE_OK) rc = quantize_nvfp4(tcodes, tscales, q.alpha, amax, tmp, q.rows, q.cols, q.cols / 2, s);
+      if (rc == CE_OK) rc = w4_pack(q.codes, q.scales, tcodes, tscales, q.rows, q.cols, q.cols / 2, q.cols / 16, s);
+    }
+    e = cudaStreamSynchronize(s);
+    if (rc == CE_OK && e != cudaSuccess) rc = cuda_error(e, "NVFP4 weight set-up");
+    for (void *p : {(void *)tmp, (void *)tcodes, (void *)tscales, (void *)amax})
+      if (p) cudaFree(p);
+    if (rc) return rc;
   }
   fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_att, L * c.dim, 1.0f);
   fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_ffn, L * c.dim, 1.0f);
@@ -777,6 +885,23 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
   const size_t delta_stride = (size_t)B * D, qkv_stride = (size_t)B * m->qkv_rows,
                h_stride = (size_t)B * 2 * Hd;
   const bool pdl = m->pdl;
+  const bool w4 = m->precision == CE_PREC_NVFP4_E2M1;
+  // y = a W^T of weight kind k (0 wqkv, 1 wo, 2 w13, 3 w2, 4 classifier) of
+  // layer l; sw_out set: the SwiGLU epilogue writes the bf16 w2 operand
+  auto gemm = [&](int k, int l, float *d, const uint16_t *a, int ldd, int splits, long long stride,
+                  uint16_t *sw_out) -> int {
+    int N, K;
+    mat_shape(m, k, &N, &K);
+    if (w4) {
+      const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
+      return gemm_w4a16(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out,
+                        sw_out ? N / 2 : 0, s, pdl);
+    }
+    const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
+                        : k == 2 ? m->w13 + l * w13_elems(m) : k == 3 ? m->w2 + l * w2_elems(m) : m->wcls;
+    if (sw_out) return gemm_bf16_swiglu(sw_out, N / 2, a, w, B, N, K, K, K, s, pdl);
+    return gemm_bf16_split(d, a, w, B, N, K, K, K, ldd, splits, stride, s, pdl);
+  };
   auto norm = [&](const float *delta, int nsplit, const uint16_t *emb, const float *w) {
     int lrc = CE_OK;
     const int rc = launch_rows(m->nv, [&](auto nv) {
@@ -792,8 +917,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
                   m->rms_att + (size_t)l * D);
     if (rc) return rc;
     CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
-    rc = gemm_bf16_split(m->qkv, m->xb, m->wqkv + l * wqkv_elems(m), B, m->qkv_rows, D, D, D, m->qkv_rows,
-                         m->sp_qkv, (long long)qkv_stride, s, pdl);
+    rc = gemm(0, l, m->qkv, m->xb, m->qkv_rows, m->sp_qkv, (long long)qkv_stride, nullptr);
     if (rc) return rc;
     uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
     rc = launch_kernel(rope_append_kernel, dim3(B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
@@ -811,31 +935,28 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     };
     rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{}) : attention(std::integral_constant<int, 128>{});
     if (rc) return rc;
-    rc = gemm_bf16_split(m->delta, m->att, m->wo + l * wo_elems(m), B, D, D, D, D, D, m->sp_o,
-                         (long long)delta_stride, s, pdl);
+    rc = gemm(1, l, m->delta, m->att, D, m->sp_o, (long long)delta_stride, nullptr);
     if (rc) return rc;
     rc = norm(m->delta, m->sp_o, nullptr, m->rms_ffn + (size_t)l * D);
     if (rc) return rc;
     CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
     if (m->sp_13 == 1) {  // SwiGLU in the GEMM epilogue, straight to the bf16 operand
-      rc = gemm_bf16_swiglu(m->hb, Hd, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, s, pdl);
+      rc = gemm(2, l, nullptr, m->xb, 2 * Hd, 1, 0, m->hb);
       if (rc) return rc;
     } else {
-      rc = gemm_bf16_split(m->h, m->xb, m->w13 + l * w13_elems(m), B, 2 * Hd, D, D, D, 2 * Hd, m->sp_13,
-                           (long long)h_stride, s, pdl);
+      rc = gemm(2, l, m->h, m->xb, 2 * Hd, m->sp_13, (long long)h_stride, nullptr);
       if (rc) return rc;
       rc = launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
                          (const float *)m->h, m->sp_13, h_stride, m->hb, B, Hd);
       if (rc) return rc;
     }
-    rc = gemm_bf16_split(m->delta, m->hb, m->w2 + l * w2_elems(m), B, D, Hd, Hd, Hd, D, m->sp_2,
-                         (long long)delta_stride, s, pdl);
+    rc = gemm(3, l, m->delta, m->hb, D, m->sp_2, (long long)delta_stride, nullptr);
     if (rc) return rc;
   }
   int rc = norm(m->delta, m->sp_2, nullptr, m->rms_final);
   if (rc) return rc;
   CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
-  rc = gemm_bf16_split(m->logits, m->xb, m->wcls, B, c.vocab_size, D, D, D, c.vocab_size, 1, 0, s, pdl);
+  rc = gemm(4, 0, m->logits, m->xb, c.vocab_size, 1, 0, nullptr);
   if (rc) return rc;
   rc = launch_kernel(argmax_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "argmax_kernel",
                      (const float *)m->logits, c.vocab_size, m->tokens, m->generated, m->cap,
@@ -858,6 +979,22 @@ int ce_llama_read(ce_llama *m, int which, int layer, void *host, int64_t offset,
              "range [%lld, %lld) outside the tensor (%zu bytes)", (long long)offset, (long long)(offset + bytes), v.bytes);
   CE_CUDA_TRY(cudaDeviceSynchronize());
   CE_CUDA_TRY(cudaMemcpy(host, (uint8_t *)v.ptr + offset, (size_t)bytes, cudaMemcpyDeviceToHost));
+  return CE_OK;
+}
+
+int ce_llama_read_nvfp4(ce_llama *m, int which, int layer, uint8_t *codes_host, uint8_t *scales_host,
+                        float *alpha_host) {
+  CE_REQUIRE(m != nullptr, "null model");
+  CE_REQUIRE(m->precision == CE_PREC_NVFP4_E2M1, "the model's weights are not NVFP4");
+  const int k = which == CE_LLAMA_WQKV ? 0 : which == CE_LLAMA_WO ? 1 : which == CE_LLAMA_W13 ? 2
+                : which == CE_LLAMA_W2 ? 3 : which == CE_LLAMA_WCLS ? 4 : -1;
+  CE_REQUIRE(k >= 0, "tensor %d is not an NVFP4 weight", which);
+  CE_REQUIRE(k == 4 || (layer >= 0 && layer < m->c.n_layers), "layer %d out of range", layer);
+  const QMat &q = m->qm[k == 4 ? 4 * m->c.n_layers : 4 * layer + k];
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  if (codes_host) CE_CUDA_TRY(cudaMemcpy(codes_host, q.codes, (size_t)q.rows * q.cols / 2, cudaMemcpyDeviceToHost));
+  if (scales_host) CE_CUDA_TRY(cudaMemcpy(scales_host, q.scales, (size_t)q.rows * q.cols / 16, cudaMemcpyDeviceToHost));
+  if (alpha_host) CE_CUDA_TRY(cudaMemcpy(alpha_host, q.alpha, 8, cudaMemcpyDeviceToHost));
   return CE_OK;
 }
 

@@ -463,12 +463,16 @@ typedef struct ce_llama_config {
 int ce_llama_validate(const ce_llama_config *cfg, int batch, int max_steps, int precision);
 
 /* Allocates weights, KV cache and buffers for `batch` sequences and up to
- * max_steps generated tokens per start; precision CE_PREC_BF16. */
+ * max_steps generated tokens per start. precision CE_PREC_BF16 (bf16
+ * weights) or CE_PREC_NVFP4_E2M1 (every GEMM weight NVFP4, expanded to bf16
+ * inside the W4A16 GEMM; the token embedding stays bf16; dim and hidden_dim
+ * multiples of 64). Activations are bf16 GEMM operands either way. */
 int ce_llama_create(ce_llama **model, const ce_llama_config *cfg, int batch, int max_steps,
                     int precision, ce_stream_t stream);
 int ce_llama_destroy(ce_llama *model);
 
-/* Random model on the device: every matrix N(0, weight_std) (bf16), RMSNorm
+/* Random model on the device: every matrix N(0, weight_std) (bf16, or fp32
+ * quantized to NVFP4 by the ce_quantize_nvfp4 rule per matrix), RMSNorm
  * weights 1, and KV positions [0, kv_fill) of every layer, sequence and head
  * N(0, 1) (bf16), the rest of the cache 0. Deterministic in seed. */
 int ce_llama_init_random(ce_llama *model, uint64_t seed, float weight_std, int kv_fill,
@@ -496,6 +500,13 @@ int ce_llama_set_pdl(ce_llama *model, int enable);
 int ce_llama_read(ce_llama *model, int which, int layer, void *host, int64_t offset, int64_t bytes);
 int ce_llama_write(ce_llama *model, int which, int layer, const void *host, int64_t offset,
                    int64_t bytes);
+
+/* NVFP4 model only: host copies of one weight matrix (CE_LLAMA_WQKV, _WO,
+ * _W13, _W2 of a layer, or _WCLS) in the W4A16 layout: codes [cols/64][rows][32],
+ * scales [cols/64][rows][4], alpha = (encode, decode) tensor scales; the
+ * weight is e2m1(code) * ue4m3(scale) * alpha[1]. Any pointer may be NULL. */
+int ce_llama_read_nvfp4(ce_llama *model, int which, int layer, uint8_t *codes_host,
+                        uint8_t *scales_host, float *alpha_host);
 
 /* Reads and clears the decode kernels' status word: CE_OK, CE_ERR_USAGE when
  * a step ran past the end of the KV cache, CE_ERR_TIMEOUT when a staging wait

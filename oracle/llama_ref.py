@@ -27,7 +27,7 @@ format. Weights and the initial KV cache are inputs copied from the device.
 """
 import numpy as np
 
-from .oracle import bf16_bits, bf16_value
+from .oracle import bf16_bits, bf16_value, decode_array
 
 EPS = 1e-5
 
@@ -38,8 +38,18 @@ def bf16_round(x):
     return bf16_value(bf16_bits(np.asarray(x, np.float32))).astype(np.float64)
 
 
-def to64(bits):
-    return bf16_value(bits).astype(np.float64)
+def to64(w):
+    """A weight as float64 values: bf16 bits (uint16 array), or an NVFP4
+    (codes two per byte with the even index in the low nibble, UE4M3 scales per
+    16 values, decode scale) tuple dequantized as e2m1(code) * ue4m3(scale) *
+    decode scale (the ce_quantize_nvfp4 format)."""
+    if isinstance(w, tuple):
+        codes, scales, alpha = w
+        nib = np.empty((codes.shape[0], codes.shape[1] * 2), np.uint8)
+        nib[:, 0::2], nib[:, 1::2] = codes & 0x0F, codes >> 4
+        vals = decode_array(0, nib).astype(np.float64)
+        return vals * np.repeat(decode_array(2, scales).astype(np.float64), 16, axis=1) * alpha
+    return bf16_value(w).astype(np.float64)
 
 
 def rmsnorm(x, w):

@@ -21,10 +21,10 @@ LOGIT_REL_L2 = 1e-2
 NEAR_TIE = 2e-3  # top-2 logit gap below which a token difference is a tie
 
 
-def run_and_check(ce, O, cfg, batch, kv_fill, steps, seqs=None, seed=1):
+def run_and_check(ce, O, cfg, batch, kv_fill, steps, seqs=None, seed=1, precision=None):
     dev = torch.device("cuda:0")
     torch.cuda.set_device(dev)
-    m = ce.Llama(cfg, batch, steps)
+    m = ce.Llama(cfg, batch, steps, precision=ce.PREC_BF16 if precision is None else precision)
     try:
         m.init_random(seed=seed, weight_std=0.02, kv_fill=kv_fill)
         rng = np.random.default_rng(seed)
@@ -44,10 +44,19 @@ def run_and_check(ce, O, cfg, batch, kv_fill, steps, seqs=None, seed=1):
         lg, best, gap = orc.decode(tokens0[seqs], kv_fill, gen, kc, vc)
         for s in range(steps):
             assert O.rel_l2(dev_logits[s], lg[s]) <= LOGIT_REL_L2, (s, O.rel_l2(dev_logits[s], lg[s]))
-        agree = best.T == gen
-        ties = gap.T < NEAR_TIE
-        assert (agree | ties).all(), np.argwhere(~(agree | ties))
-        assert agree.mean() >= 0.999 or (~agree).sum() <= (ties.sum())
+        # A greedy token may differ from the oracle's only where the device's
+        # own logit error on that row could account for it: the oracle logit
+        # of the device's token is within twice the row's largest logit error
+        # (and NEAR_TIE) of the oracle's maximum.
+        for s in range(steps):
+            for i in range(len(seqs)):
+                if gen[i, s] == best[s, i]:
+                    continue
+                err = np.abs(dev_logits[s][i] - lg[s, i]).max()
+                short = lg[s, i].max() - lg[s, i, gen[i, s]]
+                assert short <= max(2 * err, NEAR_TIE), (
+                    f"step {s} seq {seqs[i]}: device token {gen[i, s]} is {short:.3g} below the oracle "
+                    f"maximum (token {best[s, i]}); largest logit error {err:.3g}")
         return m, gen, dev_logits
     finally:
         m.close()
@@ -65,6 +74,26 @@ def run_and_check(ce, O, cfg, batch, kv_fill, steps, seqs=None, seed=1):
 ])
 def test_small_configs_match_oracle(ce, O, cfg, batch, kv_fill, steps):
     run_and_check(ce, O, cfg, batch, kv_fill, steps)
+
+
+@pytest.mark.parametrize("cfg,batch,kv_fill,steps", [
+    (dict(dim=128, hidden_dim=256, n_layers=2, n_heads=2, vocab_size=512, seq_len=64), 5, 10, 5),
+    (dict(dim=256, hidden_dim=320, n_layers=2, n_heads=2, n_kv_heads=1, vocab_size=1000, seq_len=48), 3, 7, 4),
+    (dict(dim=1024, hidden_dim=256, n_layers=1, n_heads=8, vocab_size=256, seq_len=32), 4, 5, 3),
+])
+def test_nvfp4_weights_match_oracle(ce, O, cfg, batch, kv_fill, steps):
+    """Every GEMM weight NVFP4 (the device quantizer's codes, scales and
+    decode scale), expanded inside the W4A16 GEMM: against the oracle run on
+    the dequantized weights."""
+    run_and_check(ce, O, cfg, batch, kv_fill, steps, precision=ce.PREC_NVFP4_E2M1)
+
+
+def test_7b_layer_shape_nvfp4(ce, O):
+    """One layer at the 7B shape of BASELINE config 5 (dim 4096, 32 heads,
+    SwiGLU 11008, vocab 32000, seq_len 2048) with NVFP4 weights, batch 64,
+    the cache filled to position 1023: 3 steps, 2 sampled sequences."""
+    cfg = dict(dim=4096, hidden_dim=11008, n_layers=1, n_heads=32, vocab_size=32000, seq_len=2048)
+    run_and_check(ce, O, cfg, 64, 1024, 3, seqs=[5, 63], precision=ce.PREC_NVFP4_E2M1)
 
 
 def test_graph_replay_equals_direct(ce):
