@@ -294,7 +294,7 @@ def w4_pack(codes_t, scales_t, codes, scales, n, k, stream=None):
 
 
 def gemm_w4a16(d, a, codes_t, scales_t, alpha=None, n=None, stream=None):
-    """d [M][N] fp32 = alpha * A W^T, A bf16 bits [M][K], W packed by w4_pack."""
+    """d [M][N] fp32 = alpha * A W^T, A fp16 bits [M][K], W packed by w4_pack."""
     M, K = a.shape
     N = d.shape[1] if n is None else n
     check(lib().ce_gemm_w4a16(_ptr(d), _ptr(a), _ptr(codes_t), _ptr(scales_t), _ptr(alpha), M, N, K, K,

@@ -20,6 +20,7 @@
 //     copies and MMAs (bounded), frees its TMEM and exits.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
 #include <mutex>
@@ -91,8 +92,9 @@ struct GemmArgs {
   // (2i, 2i+1) are (g_i, u_i); the epilogue writes bf16(silu(g_i) * u_i) to
   // column i of out_bf16 (row stride ld_out) instead of the fp32 d.
   int epilogue;
-  uint16_t *out_bf16;
+  uint16_t *out_bf16;  // bf16, or fp16 when out_f16
   int ld_out;
+  int out_f16;
 };
 
 // SwiGLU epilogue of one row's 32 accumulator columns starting at col0 (even).
@@ -102,8 +104,14 @@ __device__ __forceinline__ void store_swiglu(const GemmArgs &args, int row, int 
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const float g0 = v[4 * k], u0 = v[4 * k + 1], g1 = v[4 * k + 2], u1 = v[4 * k + 3];
-    __nv_bfloat162 h = __floats2bfloat162_rn(g0 / (1.0f + expf(-g0)) * u0, g1 / (1.0f + expf(-g1)) * u1);
-    packed[k] = *reinterpret_cast<uint32_t *>(&h);
+    const float h0 = g0 / (1.0f + expf(-g0)) * u0, h1 = g1 / (1.0f + expf(-g1)) * u1;
+    if (args.out_f16) {
+      __half2 h = __floats2half2_rn(h0, h1);
+      packed[k] = *reinterpret_cast<uint32_t *>(&h);
+    } else {
+      __nv_bfloat162 h = __floats2bfloat162_rn(h0, h1);
+      packed[k] = *reinterpret_cast<uint32_t *>(&h);
+    }
   }
   const int oc = col0 / 2;
   if (col0 + 32 <= args.N && (args.ld_out & 7) == 0 && (reinterpret_cast<uintptr_t>(orow) & 15u) == 0) {
@@ -571,33 +579,52 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
 // ---------------------------------------------------------------------------
 // W4A16 GEMM: NVFP4 weights (E2M1 codes, UE4M3 scale per 16 values, one fp32
-// tensor decode scale alpha) against bf16 activations, the dequantization
-// fused into the GEMM. The weights stay 4.5 bits per value in HBM and are
-// expanded to bf16 in shared memory right before the tensor cores read them:
-//   warp 0     producer: TMA for the bf16 A tile; bulk copies of one 64-wide
-//              k-block of the B tile's codes ([kb][N][32 bytes]) and scales
-//              ([kb][N][4 bytes]), the k-block-major layout of gemm_w4_pack;
-//   warps 6-9  converters: code x scale (exact in bf16: at most 6 significant
-//              bits) into the 128-byte-swizzled K-major bf16 operand layout,
-//              then a proxy fence so the tensor cores see the stores;
-//   warp 1     MMA issuer (kind::f16, bf16 x bf16) once both are in;
+// tensor decode scale alpha) against 16-bit activations, the dequantization
+// fused into the GEMM. At decode sizes the weights are the only HBM stream,
+// so they travel in their own deep ring, apart from the activation tiles:
+//   warp 0     weight producer: bulk copies of one 64-wide k-block of the B
+//              tile's codes ([kb][N][32 bytes]) and scales ([kb][N][4]), the
+//              k-block-major layout of w4_pack, kW4WStages k-blocks ahead;
+//   warp 10    activation producer: TMA for the fp16 A tile into the operand
+//              ring (kW4OStages slots, each A plus the expanded B);
+//   warps 6-9  converters: cvt.rn.f16x2.e2m1x2 and a half2 multiply by the
+//              UE4M3 scale (cvt.rn.f16x2.e4m3x2) write the fp16 B operand in
+//              the 128-byte-swizzled K-major layout (every product is exact:
+//              at most 6 significant bits, magnitudes 2^-10 .. 2688), then a
+//              proxy fence so the tensor cores see the stores;
+//   warp 1     MMA issuer (kind::f16, fp16 x fp16) once A and B are in;
 //   warps 2-5  epilogue: alpha x accumulator, with the split-K and SwiGLU
-//              modes of the bf16 GEMM.
+//              (fp16 out) modes of the bf16 GEMM.
 
-constexpr int kW4Threads = 320;
+constexpr int kW4ConvWarps = 8;
+constexpr int kW4Threads = (7 + kW4ConvWarps) * 32;  // see the role list above
+constexpr int kW4AProducerWarp = 6 + kW4ConvWarps;
+constexpr int kW4WMaxStages = 16;  // raw weight k-blocks in flight (fewer for wide tiles)
+constexpr int kW4BStages = 4;    // expanded fp16 weight tiles
+constexpr int kW4AMaxStages = 16;
+constexpr int kW4SmemBudget = 232448 - 1024;
 
 template <int BN>
 struct SmemW4 {
-  static constexpr int a_bytes = BM * kRowBytes;
-  static constexpr int b_bytes = BN * kRowBytes;   // expanded bf16 operand
-  static constexpr int code_bytes = BN * 32;       // 64 E2M1 codes per row
-  static constexpr int scale_bytes = BN * 4;       // 4 UE4M3 scales per row
-  static constexpr int raw = a_bytes + b_bytes + code_bytes + scale_bytes;
-  static constexpr int stage_bytes = ((raw + 1023) / 1024) * 1024;  // keep the swizzled tiles 1 KB aligned
-  static constexpr int max_stages = (232448 - 2048) / stage_bytes;
-  static constexpr int stages = max_stages > 6 ? 6 : max_stages;
-  static constexpr int bar_offset = stages * stage_bytes;
-  static constexpr int total = bar_offset + 512 + 1024;
+  static constexpr int b_bytes = BN * kRowBytes;        // expanded fp16 operand
+  static constexpr int code_bytes = BN * 32;            // 64 E2M1 codes per row
+  static constexpr int scale_bytes = BN * 4;            // 4 UE4M3 scales per row
+  static constexpr int w_stage = code_bytes + scale_bytes;
+  static constexpr int w_fit = 73728 / w_stage;           // about 72 KB of raw weights
+  static constexpr int w_stages = w_fit > kW4WMaxStages ? kW4WMaxStages : w_fit;
+  static constexpr int b_offset = 0;                    // B ring, 1 KB aligned slots
+  static constexpr int w_offset = kW4BStages * b_bytes;
+  static constexpr int a_offset = ((w_offset + w_stages * w_stage + 1023) / 1024) * 1024;
+  static constexpr int bar_bytes = 1024;
+  // A ring: slots of a_slot bytes (8 KB when M <= 64: a 64-row box; the
+  // 128-row MMA then reads 8 KB past the slot, rows it never stores) up to
+  // the budget, one full 16 KB tile of slack after the last slot.
+  static int a_stages(int a_slot) {
+    const int room = kW4SmemBudget - a_offset - bar_bytes - BM * kRowBytes;
+    const int n = room / a_slot + 1;
+    return n > kW4AMaxStages ? kW4AMaxStages : n;
+  }
+  static int total(int a_slot) { return a_offset + a_stages(a_slot) * a_slot + BM * kRowBytes - a_slot + bar_bytes + 1024; }
 };
 
 struct W4Args {
@@ -605,6 +632,8 @@ struct W4Args {
   const uint8_t *codes;   // [k_blocks][N][32]
   const uint8_t *scales;  // [k_blocks][N][4]
   const float *alpha;     // weight decode scale (device) or nullptr
+  int a_slot;             // bytes per A ring slot (8192 or 16384)
+  int a_stages;
 };
 
 __device__ __forceinline__ void bulk_g2s_gemm(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
@@ -614,10 +643,18 @@ __device__ __forceinline__ void bulk_g2s_gemm(void *smem_dst, const void *gsrc, 
       : "memory");
 }
 
-// Unsigned E4M3 (bias 7, three mantissa bits; exponent 0 subnormal).
-__device__ __forceinline__ float ue4m3_value(uint32_t c) {
-  const uint32_t e = (c >> 3) & 15u, m = c & 7u;
-  return e == 0 ? (float)m * 0.001953125f : __uint_as_float(((e + 120u) << 23) | (m << 20));
+// Two E2M1 codes (one byte, even index in the low nibble) to fp16x2.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+  uint32_t d;
+  asm("{ .reg .b8 t; cvt.u8.u32 t, %1; cvt.rn.f16x2.e2m1x2 %0, t; }" : "=r"(d) : "r"(byte));
+  return d;
+}
+// A UE4M3 scale byte to fp16, broadcast into both halves.
+__device__ __forceinline__ uint32_t ue4m3_to_f16x2(uint32_t code) {
+  uint32_t d;
+  const unsigned short pair = (unsigned short)(code | (code << 8));
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(pair));
+  return d;
 }
 
 template <int BN>
@@ -625,35 +662,41 @@ __global__ void __launch_bounds__(kW4Threads, 1)
 gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tmA, W4Args wargs) {
   using S = SmemW4<BN>;
   const GemmArgs &args = wargs.g;
-  constexpr int kMmasPerStage = 4;                 // 64 bf16 of K per stage, 16 per MMA
-  constexpr uint32_t kIdesc = instr_desc<0, BN>();
+  constexpr int kMmasPerStage = 4;                 // 64 fp16 of K per stage, 16 per MMA
+  constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);  // fp16 x fp16 -> fp32
   constexpr uint32_t kAccStride = 256;
+  const int a_stages = wargs.a_stages, a_slot = wargs.a_slot;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::bar_offset);
-  uint64_t *conv = full + S::stages;
-  uint64_t *empty = conv + S::stages;
-  uint64_t *tmem_full = empty + S::stages;
+  uint64_t *wfull = reinterpret_cast<uint64_t *>(smem + S::a_offset + a_stages * a_slot + BM * kRowBytes - a_slot);
+  uint64_t *wempty = wfull + kW4WMaxStages;
+  uint64_t *bready = wempty + kW4WMaxStages;
+  uint64_t *bempty = bready + kW4BStages;
+  uint64_t *afull = bempty + kW4BStages;
+  uint64_t *aempty = afull + kW4AMaxStages;
+  uint64_t *tmem_full = aempty + kW4AMaxStages;
   uint64_t *tmem_empty = tmem_full + 2;
   uint64_t *drain = tmem_empty + 2;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
-  __shared__ float e2m1[16];
 
   DeviceStatus *st = &g_gemm_status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_units = args.tiles_m * args.tiles_n * args.splits;
 
-  if (threadIdx.x < 16) {
-    const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
-    e2m1[threadIdx.x] = threadIdx.x < 8 ? mag[threadIdx.x] : -mag[threadIdx.x - 8];
-  }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < S::stages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);  // one arrival per converter warp
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < S::w_stages; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], kW4ConvWarps);
+    }
+    for (int s = 0; s < kW4BStages; ++s) {
+      mbar_init(&bready[s], kW4ConvWarps);
+      mbar_init(&bempty[s], 1);
+    }
+    for (int s = 0; s < a_stages; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&aempty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
@@ -675,87 +718,115 @@ gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tmA, W4Args wargs) {
   pdl_wait();
 
   if (warp == 0) {
-    // ---------------- producer
-    int stage = 0;
-    uint32_t phase = 0;
-    uint32_t issued_mask = 0, issued_parity = 0;
+    // ---------------- weight producer
+    int ws = 0;
+    uint32_t wph = 0, issued_mask = 0, issued_parity = 0;
     bool okay = true;
     for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
       const Unit w = unit_of(args, t);
-      const int m0 = (w.tile % args.tiles_m) * BM;
       const int n0 = (w.tile / args.tiles_m) * BN;
       const int rows = min(BN, args.N - n0);
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
-        if (!warp_wait(&empty[stage], phase ^ 1u, st, 41)) {
+        if (!warp_wait(&wempty[ws], wph ^ 1u, st, 41)) {
           okay = false;
           break;
         }
         if (lane == 0) {
-          uint8_t *a_dst = smem + stage * S::stage_bytes;
-          uint8_t *c_dst = a_dst + S::a_bytes + S::b_bytes;
-          uint8_t *s_dst = c_dst + S::code_bytes;
-          mbar_arrive_expect_tx(&full[stage], S::a_bytes + rows * 36);
-          tma_load_2d(a_dst, &tmA, &full[stage], kb * 64, m0);
+          uint8_t *c_dst = smem + S::w_offset + ws * S::w_stage;
           const size_t rowbase = (size_t)kb * args.N + n0;
-          bulk_g2s_gemm(c_dst, wargs.codes + rowbase * 32, rows * 32, &full[stage]);
-          bulk_g2s_gemm(s_dst, wargs.scales + rowbase * 4, rows * 4, &full[stage]);
+          mbar_arrive_expect_tx(&wfull[ws], rows * 36);
+          bulk_g2s_gemm(c_dst, wargs.codes + rowbase * 32, rows * 32, &wfull[ws]);
+          bulk_g2s_gemm(c_dst + S::code_bytes, wargs.scales + rowbase * 4, rows * 4, &wfull[ws]);
         }
         __syncwarp();
-        issued_mask |= 1u << stage;
-        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == S::stages) {
-          stage = 0;
-          phase ^= 1u;
+        issued_mask |= 1u << ws;
+        issued_parity = (issued_parity & ~(1u << ws)) | (wph << ws);
+        if (++ws == S::w_stages) {
+          ws = 0;
+          wph ^= 1u;
         }
       }
     }
-    for (int s = 0; s < S::stages; ++s)
-      if (issued_mask & (1u << s)) warp_wait(&full[s], (issued_parity >> s) & 1u, st, 42);
+    for (int s = 0; s < S::w_stages; ++s)
+      if (issued_mask & (1u << s)) warp_wait(&wfull[s], (issued_parity >> s) & 1u, st, 42);
+  } else if (warp == kW4AProducerWarp) {
+    // ---------------- activation producer
+    int as = 0;
+    uint32_t aph = 0, issued_mask = 0, issued_parity = 0;
+    bool okay = true;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
+      const Unit w = unit_of(args, t);
+      const int m0 = (w.tile % args.tiles_m) * BM;
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&aempty[as], aph ^ 1u, st, 49)) {
+          okay = false;
+          break;
+        }
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&afull[as], a_slot);
+          tma_load_2d(smem + S::a_offset + as * a_slot, &tmA, &afull[as], kb * 64, m0);
+        }
+        __syncwarp();
+        issued_mask |= 1u << as;
+        issued_parity = (issued_parity & ~(1u << as)) | (aph << as);
+        if (++as == a_stages) {
+          as = 0;
+          aph ^= 1u;
+        }
+      }
+    }
+    for (int s = 0; s < a_stages; ++s)
+      if (issued_mask & (1u << s)) warp_wait(&afull[s], (issued_parity >> s) & 1u, st, 50);
   } else if (warp >= 6) {
-    // ---------------- converters: E2M1 x UE4M3 -> swizzled bf16
+    // ---------------- converters: E2M1 x UE4M3 -> swizzled fp16
+    constexpr int kConvThreads = kW4ConvWarps * 32;
     const int ct = threadIdx.x - 192;
-    int stage = 0;
-    uint32_t phase = 0;
+    int ws = 0, bs = 0;
+    uint32_t wph = 0, bph = 0;
     bool okay = true;
     for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
       const Unit w = unit_of(args, t);
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
-        if (!warp_wait(&full[stage], phase, st, 43)) {
+        if (!warp_wait(&wfull[ws], wph, st, 43) || !warp_wait(&bempty[bs], bph ^ 1u, st, 51)) {
           okay = false;
           break;
         }
-        uint8_t *a_s = smem + stage * S::stage_bytes;
-        uint8_t *b_s = a_s + S::a_bytes;
-        const uint8_t *c_s = b_s + S::b_bytes;
+        uint8_t *b_s = smem + S::b_offset + bs * S::b_bytes;
+        const uint8_t *c_s = smem + S::w_offset + ws * S::w_stage;
         const uint8_t *s_s = c_s + S::code_bytes;
 #pragma unroll 2
-        for (int u = ct; u < BN * 8; u += 128) {
+        for (int u = ct; u < BN * 8; u += kConvThreads) {
           const int r = u >> 3, c = u & 7;  // row, 16-byte chunk (8 values) of the row
           const uint32_t q = *reinterpret_cast<const uint32_t *>(c_s + r * 32 + c * 4);
-          const float sc = ue4m3_value(s_s[r * 4 + (c >> 1)]);
+          const uint32_t sc = ue4m3_to_f16x2(s_s[r * 4 + (c >> 1)]);
           uint32_t o[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float lo = e2m1[(q >> (8 * j)) & 15u] * sc;
-            const float hi = e2m1[(q >> (8 * j + 4)) & 15u] * sc;
-            __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
-            o[j] = *reinterpret_cast<uint32_t *>(&v);
+            uint32_t v = e2m1x2_to_f16x2((q >> (8 * j)) & 0xFFu);
+            asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(o[j]) : "r"(v), "r"(sc));
           }
           *reinterpret_cast<uint4 *>(b_s + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
-        if (lane == 0) mbar_arrive(&conv[stage]);
-        if (++stage == S::stages) {
-          stage = 0;
-          phase ^= 1u;
+        if (lane == 0) {
+          mbar_arrive(&bready[bs]);
+          mbar_arrive(&wempty[ws]);
+        }
+        if (++ws == S::w_stages) {
+          ws = 0;
+          wph ^= 1u;
+        }
+        if (++bs == kW4BStages) {
+          bs = 0;
+          bph ^= 1u;
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer
-    int stage = 0;
-    uint32_t phase = 0;
+    int as = 0, bs = 0;
+    uint32_t aph = 0, bph = 0;
     bool okay = true;
     int local = 0;
     for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x, ++local) {
@@ -766,26 +837,31 @@ gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tmA, W4Args wargs) {
       const uint32_t d_tmem = tmem_base + (uint32_t)acc * kAccStride;
       const Unit w = unit_of(args, t);
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
-        if (!warp_wait(&full[stage], phase, st, 45) || !warp_wait(&conv[stage], phase, st, 46)) {
+        if (!warp_wait(&afull[as], aph, st, 45) || !warp_wait(&bready[bs], bph, st, 46)) {
           okay = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
-          const uint32_t a_addr = smem_u32(smem + stage * S::stage_bytes);
-          const uint32_t b_addr = a_addr + S::a_bytes;
+          const uint32_t a_addr = smem_u32(smem + S::a_offset + as * a_slot);
+          const uint32_t b_addr = smem_u32(smem + S::b_offset + bs * S::b_bytes);
 #pragma unroll
           for (int k = 0; k < kMmasPerStage; ++k) {
             const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32);
             const uint64_t b_desc = smem_desc_sw128(b_addr + k * 32);
             tc_mma<0>(d_tmem, a_desc, b_desc, kIdesc, ((kb - w.kb0) | k) != 0 ? 1u : 0u);
           }
-          tc_commit(&empty[stage]);
+          tc_commit(&aempty[as]);
+          tc_commit(&bempty[bs]);
         }
         __syncwarp();
-        if (++stage == S::stages) {
-          stage = 0;
-          phase ^= 1u;
+        if (++as == a_stages) {
+          as = 0;
+          aph ^= 1u;
+        }
+        if (++bs == kW4BStages) {
+          bs = 0;
+          bph ^= 1u;
         }
       }
       if (okay && lane == 0) tc_commit(&tmem_full[acc]);
@@ -794,7 +870,7 @@ gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tmA, W4Args wargs) {
     if (lane == 0) tc_commit(drain);
     __syncwarp();
     warp_wait(drain, 0, st, 47);
-  } else {
+  } else if (warp >= 2 && warp <= 5) {
     // ---------------- epilogue (warps 2-5)
     const int quarter = warp & 3;
     const float alpha = wargs.alpha != nullptr ? *wargs.alpha : 1.0f;
@@ -1033,6 +1109,7 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.epilogue = swiglu_out != nullptr ? 1 : 0;
   args.out_bf16 = swiglu_out;
   args.ld_out = swiglu_ld;
+  args.out_f16 = 0;
   const int tiles = args.tiles_m * args.tiles_n * splits;
   if (c.pair) {
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
@@ -1122,6 +1199,35 @@ int gemm_bf16_swiglu(uint16_t *out, int ld_out, const uint16_t *a, const uint16_
                           out, ld_out);
 }
 
+// Time of the busiest CTA of a W4A16 launch, in units of one weight row of
+// one k-block: waves x (k-blocks per split + kW4UnitKb) x (kW4StepRows +
+// width). Each
+// k-block also costs a fixed pipeline round (measured about 0.4 us, worth
+// some 400 rows of conversion and MMA), so wide tiles and few waves win.
+// A work unit also pays its pipeline fill and epilogue (its fp32 partial
+// written and summed again), about kW4UnitKb k-blocks' worth.
+constexpr long long kW4StepRows = 400;
+constexpr long long kW4UnitKb = 6;
+
+long long w4_cost(int M, int N, int K, int splits, int width, int sms) {
+  const long long units = (long long)((M + BM - 1) / BM) * ((N + width - 1) / width) * splits;
+  const long long kb = (K / 64 + splits - 1) / splits;
+  return ((units + sms - 1) / sms) * (kb + kW4UnitKb) * (kW4StepRows + width);
+}
+
+// Tile width of a W4A16 GEMM with `splits` k ranges: the one in
+// {64, ..., 224} with the smallest w4_cost.
+int w4_tile_width(int M, int N, int K, int splits, int sms) {
+  static const int kWidths[] = {64, 96, 128, 160, 192, 224};
+  int best = 128;
+  long long best_cost = -1;
+  for (int w : kWidths) {
+    const long long cost = w4_cost(M, N, K, splits, w, sms);
+    if (best_cost < 0 || cost < best_cost) best = w, best_cost = cost;
+  }
+  return best;
+}
+
 // W4A16 GEMM (see gemm_w4a16_kernel): d = alpha x A W^T with W in the
 // k-block-major NVFP4 layout of w4_pack; split-K partials and the SwiGLU
 // epilogue as in gemm_bf16_split / gemm_bf16_swiglu.
@@ -1142,13 +1248,15 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
   CE_REQUIRE(swiglu_out != nullptr || ldd >= N, "ldd must be >= N");
   if (!is_sm100()) return set_error(CE_ERR_USAGE, "tcgen05 GEMM needs an sm_100 device");
   const int sms = sm_count();
-  // tile width: 128 unless narrower tiles give more CTAs at decode sizes
   const int tiles_m = (M + BM - 1) / BM;
-  const int bn = (long long)tiles_m * ((N + 127) / 128) < sms ? 64 : 128;
+  const int bn = w4_tile_width(M, N, K, splits, sms);
+  // A tiles: a 64-row box (8 KB slots, a deeper ring) when the rows fit
+  const int a_rows = M <= 64 ? 64 : BM;
   CUtensorMap ta;
-  int rc = make_operand_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, lda, BM);
+  int rc = make_operand_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, M, lda, a_rows);
   if (rc) return rc;
   W4Args w{};
+  w.a_slot = a_rows * kRowBytes;
   w.g.d = d;
   w.g.M = M;
   w.g.N = N;
@@ -1162,21 +1270,29 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
   w.g.epilogue = swiglu_out != nullptr ? 1 : 0;
   w.g.out_bf16 = swiglu_out;
   w.g.ld_out = swiglu_ld;
+  w.g.out_f16 = 1;
   w.codes = codes_t;
   w.scales = scales_t;
   w.alpha = alpha;
   const int units = w.g.tiles_m * w.g.tiles_n * splits;
   const int grid = units < sms ? units : sms;
-  if (bn == 64) {
-    rc = configure_smem<gemm_w4a16_kernel<64>>(SmemW4<64>::total);
-    if (rc) return rc;
-    return launch_kernel(gemm_w4a16_kernel<64>, dim3(grid), dim3(kW4Threads), SmemW4<64>::total, s, pdl,
-                         "gemm_w4a16_kernel", ta, w);
+  switch (bn) {
+#define CE_W4_LAUNCH(W)                                                                          \
+  case W:                                                                                        \
+    w.a_stages = SmemW4<W>::a_stages(w.a_slot);                                                  \
+    rc = configure_smem<gemm_w4a16_kernel<W>>(kW4SmemBudget);                                    \
+    if (rc) return rc;                                                                           \
+    return launch_kernel(gemm_w4a16_kernel<W>, dim3(grid), dim3(kW4Threads), SmemW4<W>::total(w.a_slot), s, \
+                         pdl, "gemm_w4a16_kernel", ta, w);
+    CE_W4_LAUNCH(64)
+    CE_W4_LAUNCH(96)
+    CE_W4_LAUNCH(128)
+    CE_W4_LAUNCH(160)
+    CE_W4_LAUNCH(192)
+    CE_W4_LAUNCH(224)
+#undef CE_W4_LAUNCH
   }
-  rc = configure_smem<gemm_w4a16_kernel<128>>(SmemW4<128>::total);
-  if (rc) return rc;
-  return launch_kernel(gemm_w4a16_kernel<128>, dim3(grid), dim3(kW4Threads), SmemW4<128>::total, s, pdl,
-                       "gemm_w4a16_kernel", ta, w);
+  return set_error(CE_ERR_USAGE, format("unsupported W4A16 tile width %d", bn));
 }
 
 // Split count that fills the SMs for a W4A16 GEMM of this shape (tiles of
@@ -1185,14 +1301,15 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
 int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks) {
   const int sms = sm_count();
   if (sms <= 0) return 1;
-  const long long tiles_m = (M + BM - 1) / BM;
-  const int bn = tiles_m * ((N + 127) / 128) < sms ? 64 : 128;
-  const long long tiles = tiles_m * ((N + bn - 1) / bn);
-  long long sp = sms / (tiles > 0 ? tiles : 1);
-  sp = sp < (long long)max_splits ? sp : (long long)max_splits;
-  const long long by_k = (K / 64) / (min_kblocks > 0 ? min_kblocks : 1);
-  sp = sp < by_k ? sp : by_k;
-  return sp < 1 ? 1 : (int)sp;
+  const long long kb = K / 64;
+  const long long by_k = kb / (min_kblocks > 0 ? min_kblocks : 1);
+  int best = 1;
+  long long best_cost = -1;
+  for (int sp = 1; sp <= max_splits && sp <= by_k; ++sp) {
+    const long long cost = w4_cost(M, N, K, sp, w4_tile_width(M, N, K, sp, sms), sms);
+    if (best_cost < 0 || cost < best_cost) best = sp, best_cost = cost;
+  }
+  return best;
 }
 
 int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,

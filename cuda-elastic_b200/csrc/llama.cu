@@ -25,6 +25,7 @@
 // memory, advanced by the last launch of the step, so one captured step
 // graph replays for every token.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cmath>
@@ -70,6 +71,16 @@ constexpr long long kAttnWantPerSm = 6;  // attention CTAs per SM below which ch
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&v);
+}
+
+// A GEMM operand pair: bf16, or fp16 for the NVFP4 model (whose W4A16 GEMM
+// multiplies fp16 x fp16).
+__device__ __forceinline__ uint32_t pack_operand(float lo, float hi, int f16) {
+  if (f16) {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+  }
+  return pack_bf16x2(lo, hi);
 }
 
 // splitmix64 of a counter: the deterministic source of the random init.
@@ -123,7 +134,7 @@ template <int NV>
 __global__ void __launch_bounds__(kRowThreads)
 residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_stride,
                         const uint16_t *emb, const int *tokens, int vocab, const float *w,
-                        uint16_t *xb, int dim, float eps) {
+                        uint16_t *xb, int dim, float eps, int f16) {
   __shared__ float scratch[32];
   pdl_launch_dependents();
   pdl_wait();
@@ -180,8 +191,8 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
     if (i < cols4) {
       const float4 g = wr[i];
       uint2 o;
-      o.x = pack_bf16x2(g.x * (v[j].x * scale), g.y * (v[j].y * scale));
-      o.y = pack_bf16x2(g.z * (v[j].z * scale), g.w * (v[j].w * scale));
+      o.x = pack_operand(g.x * (v[j].x * scale), g.y * (v[j].y * scale), f16);
+      o.y = pack_operand(g.z * (v[j].z * scale), g.w * (v[j].w * scale), f16);
       out[i] = o;
     }
   }
@@ -251,7 +262,7 @@ template <int HS>
 __global__ void __launch_bounds__(kAttnThreads)
 attn_decode_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const uint16_t *vcache,
                    const int *pos_ptr, int n_heads, int kv_heads, int seq_len, int chunk, int splits,
-                   float *part, int *arrivals, uint16_t *att, int dim) {
+                   float *part, int *arrivals, uint16_t *att, int dim, int f16) {
   constexpr int kPairs = HS / 2;                   // bf16 pairs per row
   constexpr int kGroups = kAttnThreads / kPairs;   // position groups of the output pass
   constexpr int kRowVec = HS * 2 / 16;             // 16-byte pieces per K row
@@ -379,7 +390,7 @@ attn_decode_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const u
   if (splits == 1) {
     if (tid < kPairs) {
       const float inv = (ok && l > 0.f) ? 1.0f / l : NAN;
-      *reinterpret_cast<uint32_t *>(att + (size_t)b * dim + h * HS + 2 * tid) = pack_bf16x2(a0 * inv, a1 * inv);
+      *reinterpret_cast<uint32_t *>(att + (size_t)b * dim + h * HS + 2 * tid) = pack_operand(a0 * inv, a1 * inv, f16);
     }
     return;
   }
@@ -414,8 +425,8 @@ attn_decode_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const u
       L += __ldcg(pp + k * (HS + 2) + 1) * f;
       o += __ldcg(pp + k * (HS + 2) + 2 + d) * f;
     }
-    __nv_bfloat16 r = __float2bfloat16_rn(o / L);
-    att[(size_t)b * dim + h * HS + d] = *reinterpret_cast<uint16_t *>(&r);
+    const uint32_t r = pack_operand(o / L, 0.f, f16);
+    att[(size_t)b * dim + h * HS + d] = (uint16_t)(r & 0xFFFFu);
   }
 }
 
@@ -423,7 +434,7 @@ attn_decode_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const u
 // of nsplit split-K partials split_stride floats apart), silu(g) = g / (1 + e^-g).
 // Used when the w1|w3 GEMM runs split; otherwise its epilogue does this.
 __global__ void swiglu_kernel(const float *h, int nsplit, size_t split_stride, uint16_t *hb, int rows,
-                              int hidden) {
+                              int hidden, int f16) {
   pdl_launch_dependents();
   pdl_wait();
   const size_t n = (size_t)rows * hidden / 2;
@@ -437,7 +448,7 @@ __global__ void swiglu_kernel(const float *h, int nsplit, size_t split_stride, u
     }
     const float a = gu.x / (1.0f + expf(-gu.x)) * gu.y;
     const float bb = gu.z / (1.0f + expf(-gu.z)) * gu.w;
-    *reinterpret_cast<uint32_t *>(hb + r * hidden + c) = pack_bf16x2(a, bb);
+    *reinterpret_cast<uint32_t *>(hb + r * hidden + c) = pack_operand(a, bb, f16);
   }
 }
 
@@ -501,6 +512,11 @@ int launch_rows(int nv, F &&f) {
   return CE_OK;
 }
 
+// K bytes of one attention chunk: 128 positions of head size 64, 64 of 128
+// (measured best: smaller chunks pay their barriers too often, larger ones
+// cost occupancy).
+constexpr int attn_chunk_bytes(int hs) { return hs == 128 ? 16384 : kChunkBytes; }
+
 size_t attn_smem_bytes(int chunk, int hs) {
   return (size_t)chunk * hs * 2 * 2 * kAttnStages + (size_t)chunk * 4 + (size_t)hs * 4 +
          (2 * kAttnThreads + 32) * 4;
@@ -513,9 +529,9 @@ int configure_attention() {
   CE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && done[dev]) return CE_OK;
   CE_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)attn_smem_bytes(kChunkBytes / 128, 64)));
+                                   (int)attn_smem_bytes(attn_chunk_bytes(64) / 128, 64)));
   CE_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)attn_smem_bytes(kChunkBytes / 256, 128)));
+                                   (int)attn_smem_bytes(attn_chunk_bytes(128) / 256, 128)));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return CE_OK;
 }
@@ -679,7 +695,7 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   m->hs = cfg->dim / cfg->n_heads;
   m->kv_dim = m->hs * cfg->n_kv_heads;
   m->qkv_rows = cfg->dim + 2 * m->kv_dim;
-  m->chunk = kChunkBytes / (m->hs * 2);
+  m->chunk = attn_chunk_bytes(m->hs) / (m->hs * 2);
   m->nchunk = (cfg->seq_len + m->chunk - 1) / m->chunk;
   m->nv = pow2_at_least((cfg->dim / 4 + kRowThreads - 1) / kRowThreads);
   {
@@ -887,7 +903,8 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
   const bool pdl = m->pdl;
   const bool w4 = m->precision == CE_PREC_NVFP4_E2M1;
   // y = a W^T of weight kind k (0 wqkv, 1 wo, 2 w13, 3 w2, 4 classifier) of
-  // layer l; sw_out set: the SwiGLU epilogue writes the bf16 w2 operand
+  // layer l; sw_out set: the SwiGLU epilogue writes the w2 operand (bf16, or
+  // fp16 for the NVFP4 model)
   auto gemm = [&](int k, int l, float *d, const uint16_t *a, int ldd, int splits, long long stride,
                   uint16_t *sw_out) -> int {
     int N, K;
@@ -907,7 +924,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     const int rc = launch_rows(m->nv, [&](auto nv) {
       lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
                           "residual_rmsnorm_kernel", m->x, delta, nsplit, delta_stride, emb,
-                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps);
+                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4);
     });
     return rc ? rc : lrc;
   };
@@ -931,7 +948,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
                            "attn_decode_kernel", (const float *)m->qkv, m->qkv_rows,
                            (const uint16_t *)kc, (const uint16_t *)vc, (const int *)m->pos, c.n_heads,
                            c.n_kv_heads, c.seq_len, m->chunk, m->attn_splits, m->part, m->arrivals,
-                           m->att, D);
+                           m->att, D, (int)w4);
     };
     rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{}) : attention(std::integral_constant<int, 128>{});
     if (rc) return rc;
@@ -947,7 +964,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
       rc = gemm(2, l, m->h, m->xb, 2 * Hd, m->sp_13, (long long)h_stride, nullptr);
       if (rc) return rc;
       rc = launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
-                         (const float *)m->h, m->sp_13, h_stride, m->hb, B, Hd);
+                         (const float *)m->h, m->sp_13, h_stride, m->hb, B, Hd, (int)w4);
       if (rc) return rc;
     }
     rc = gemm(3, l, m->delta, m->hb, D, m->sp_2, (long long)delta_stride, nullptr);

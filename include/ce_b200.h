@@ -177,13 +177,13 @@ int ce_w4_pack(uint8_t *codes_t_dev, uint8_t *scales_t_dev, const uint8_t *codes
                const uint8_t *scales_dev, int N, int K, int ld_bytes, int nsf, ce_stream_t stream);
 
 /* W4A16 GEMM with the dequantization fused: D[m][n] = alpha * sum_k
- * A[m][k] * W[n][k], A bf16 [M][lda], W NVFP4 in the ce_w4_pack layout
- * (E2M1 code x UE4M3 scale, expanded to bf16 in shared memory right before
- * the tensor cores read it), alpha = the weight's decode scale (device fp32,
- * element 1 of ce_quantize_nvfp4's tensor scales; NULL = 1), fp32
- * accumulation and output. K % 64 == 0, N % 4 == 0. The reference's NVFP4
- * GEMM quantizes the activations too (decoder_lowprec.cu:111-127); this one
- * keeps them bf16. */
+ * A[m][k] * W[n][k], A fp16 [M][lda], W NVFP4 in the ce_w4_pack layout
+ * (E2M1 code x UE4M3 scale, expanded to fp16 in shared memory right before
+ * the tensor cores read it; every such product is exact in fp16), alpha =
+ * the weight's decode scale (device fp32, element 1 of ce_quantize_nvfp4's
+ * tensor scales; NULL = 1), fp32 accumulation and output. K % 64 == 0,
+ * N % 4 == 0. The reference's NVFP4 GEMM quantizes the activations too
+ * (decoder_lowprec.cu:111-127); this one keeps them 16-bit. */
 int ce_gemm_w4a16(float *d_dev, const uint16_t *a_dev, const uint8_t *codes_t_dev,
                   const uint8_t *scales_t_dev, const float *alpha_dev, int M, int N, int K, int lda,
                   int ldd, ce_stream_t stream);
@@ -464,9 +464,9 @@ int ce_llama_validate(const ce_llama_config *cfg, int batch, int max_steps, int 
 
 /* Allocates weights, KV cache and buffers for `batch` sequences and up to
  * max_steps generated tokens per start. precision CE_PREC_BF16 (bf16
- * weights) or CE_PREC_NVFP4_E2M1 (every GEMM weight NVFP4, expanded to bf16
- * inside the W4A16 GEMM; the token embedding stays bf16; dim and hidden_dim
- * multiples of 64). Activations are bf16 GEMM operands either way. */
+ * weights, bf16 GEMM operands) or CE_PREC_NVFP4_E2M1 (every GEMM weight
+ * NVFP4, expanded to fp16 inside the W4A16 GEMM, fp16 GEMM operands; the
+ * token embedding stays bf16; dim and hidden_dim multiples of 64). */
 int ce_llama_create(ce_llama **model, const ce_llama_config *cfg, int batch, int max_steps,
                     int precision, ce_stream_t stream);
 int ce_llama_destroy(ce_llama *model);

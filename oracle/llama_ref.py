@@ -20,10 +20,10 @@ float64 numpy:
   logits = rmsnorm(x, w_final) Wcls^T; next token = first argmax
   rmsnorm(x, w) = w * x / sqrt(mean(x^2) + 1e-5)
 
-It rounds to bf16 at the points where the device path stores bf16 (the GEMM
-operands: normalized rows, attention output, SwiGLU product; the appended
-k and v), so the comparison measures the device's arithmetic, not the
-format. Weights and the initial KV cache are inputs copied from the device.
+It rounds where the device path stores 16-bit values (the GEMM operands:
+normalized rows, attention output, SwiGLU product, in bf16 or, for the NVFP4
+model, fp16; the appended k and v in bf16), so the comparison measures the
+device's arithmetic, not the format. Weights and the initial KV cache are inputs copied from the device.
 """
 import numpy as np
 
@@ -36,6 +36,11 @@ def bf16_round(x):
     """Values rounded to bf16 (through float32, as the device rounds its fp32
     values), returned as float64."""
     return bf16_value(bf16_bits(np.asarray(x, np.float32))).astype(np.float64)
+
+
+def f16_round(x):
+    """Values rounded to fp16 (through float32), returned as float64."""
+    return np.asarray(x, np.float32).astype(np.float16).astype(np.float64)
 
 
 def to64(w):
@@ -84,8 +89,10 @@ class LlamaOracle:
     w13 rows interleave w1 and w3 (w1_0, w3_0, w1_1, ...).
     """
 
-    def __init__(self, cfg, weights):
+    def __init__(self, cfg, weights, operand="bf16"):
         self.c = dict(cfg)
+        # rounding of the GEMM operands: bf16, or fp16 (the NVFP4 model)
+        self.op = f16_round if operand == "f16" else bf16_round
         self.hs = self.c["dim"] // self.c["n_heads"]
         self.kv_dim = self.hs * self.c["n_kv_heads"]
         self.emb = to64(weights["tok_emb"])
@@ -108,7 +115,7 @@ class LlamaOracle:
         x = self.emb[np.asarray(tokens)]
         group = H // KH
         for l in range(c["n_layers"]):
-            xb = bf16_round(rmsnorm(x, self.rms_att[l]))
+            xb = self.op(rmsnorm(x, self.rms_att[l]))
             qkv = xb @ self.wqkv[l].T
             q = rope(qkv[:, :D], pos, hs)
             k = rope(qkv[:, D:D + self.kv_dim], pos, hs)
@@ -126,12 +133,12 @@ class LlamaOracle:
                 p = np.exp(s - s.max(axis=1, keepdims=True))
                 p /= p.sum(axis=1, keepdims=True)
                 att[:, h, :] = np.einsum("nt,ntd->nd", p, vals)
-            x = x + bf16_round(att.reshape(n, D)) @ self.wo[l].T
-            xb = bf16_round(rmsnorm(x, self.rms_ffn[l]))
+            x = x + self.op(att.reshape(n, D)) @ self.wo[l].T
+            xb = self.op(rmsnorm(x, self.rms_ffn[l]))
             hh = xb @ self.w13[l].T          # rows interleave w1 and w3
             g, u = hh[:, 0::2], hh[:, 1::2]
-            x = x + bf16_round(g / (1.0 + np.exp(-g)) * u) @ self.w2[l].T
-        return bf16_round(rmsnorm(x, self.rms_final)) @ self.wcls.T
+            x = x + self.op(g / (1.0 + np.exp(-g)) * u) @ self.w2[l].T
+        return self.op(rmsnorm(x, self.rms_final)) @ self.wcls.T
 
     def decode(self, tokens0, pos0, forced, kcache, vcache):
         """Teacher-forced decode: step s feeds tokens0 (s = 0) or forced[:, s-1].

@@ -32,7 +32,8 @@ def run_and_check(ce, O, cfg, batch, kv_fill, steps, seqs=None, seed=1, precisio
         m.start(tokens0, kv_fill)
         seqs = list(range(batch)) if seqs is None else seqs
         kc, vc = cache_from_device(m, seqs, kv_fill)
-        orc = LlamaOracle(m.cfg.as_dict(), m.weights())
+        orc = LlamaOracle(m.cfg.as_dict(), m.weights(),
+                          operand="f16" if m.precision == ce.PREC_NVFP4_E2M1 else "bf16")
         dev_logits = []
         for _ in range(steps):
             m.step()
