@@ -120,6 +120,11 @@ _SIGNATURES = {
     "ce_llama_enqueue_step": [_vp, _vp],
     "ce_llama_set_pdl": [_vp, _i],
     "ce_llama_read_nvfp4": [_vp, _i, _i, _vp, _vp, _vp],
+    "ce_llama_validate_shard": [_vp, _i, _i, _i, _i, _i],
+    "ce_llama_create_shard": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _i, _i, _vp],
+    "ce_llama_bind_exchange": [_vp, _vp, _vp, _vp, _vp],
+    "ce_llama_enqueue_segment": [_vp, _i, _i, _vp],
+    "ce_llama_shard_rows": [_vp, _i, _i, _i, _vp, _vp],
     "ce_llama_read": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_write": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_status": [],
@@ -522,6 +527,7 @@ LLAMA_TOK_EMB, LLAMA_WQKV, LLAMA_WO, LLAMA_W13, LLAMA_W2 = 0, 1, 2, 3, 4
 LLAMA_RMS_ATT, LLAMA_RMS_FFN, LLAMA_RMS_FINAL, LLAMA_WCLS = 5, 6, 7, 8
 LLAMA_KCACHE, LLAMA_VCACHE, LLAMA_LOGITS, LLAMA_TOKENS = 9, 10, 11, 12
 LLAMA_GENERATED, LLAMA_POS, LLAMA_RESIDUAL = 13, 14, 15
+SEG_ATTN, SEG_OPROJ, SEG_FFN_IN, SEG_FFN_OUT, SEG_HEAD, SEG_PICK = 0, 1, 2, 3, 4, 5
 
 
 class LlamaConfig(ctypes.Structure):
@@ -548,14 +554,15 @@ class Llama:
     for every sequence (capturable; position and step counters are on the
     device, so a captured step replays for every token)."""
 
-    def __init__(self, cfg, batch, max_steps, precision=PREC_BF16, stream=None):
+    def __init__(self, cfg, batch, max_steps, precision=PREC_BF16, stream=None, rank=0, world=1):
         self.cfg = cfg if isinstance(cfg, LlamaConfig) else llama_config(**cfg)
         self.batch, self.max_steps, self.precision = batch, max_steps, precision
+        self.rank, self.world = rank, world
         self.hs = self.cfg.dim // self.cfg.n_heads
-        self.kv_dim = self.hs * self.cfg.n_kv_heads
+        self.kv_dim = self.hs * self.cfg.n_kv_heads // world  # this shard's k (and v) rows
         h = ctypes.c_void_p()
-        check(lib().ce_llama_create(ctypes.byref(h), ctypes.byref(self.cfg), batch, max_steps,
-                                    precision, _stream(stream)))
+        check(lib().ce_llama_create_shard(ctypes.byref(h), ctypes.byref(self.cfg), batch, max_steps,
+                                          precision, rank, world, _stream(stream)))
         self._h = h
 
     def close(self):
@@ -597,31 +604,35 @@ class Llama:
         check(lib().ce_llama_write(self._h, which, layer, a.ctypes.data, offset * a.itemsize, a.nbytes))
 
     def _size(self, which):
-        c, B = self.cfg, self.batch
-        sizes = {LLAMA_TOK_EMB: c.vocab_size * c.dim * 2, LLAMA_WQKV: (c.dim + 2 * self.kv_dim) * c.dim * 2,
-                 LLAMA_WO: c.dim * c.dim * 2, LLAMA_W13: 2 * c.hidden_dim * c.dim * 2,
-                 LLAMA_W2: c.dim * c.hidden_dim * 2, LLAMA_RMS_ATT: c.dim * 4, LLAMA_RMS_FFN: c.dim * 4,
-                 LLAMA_RMS_FINAL: c.dim * 4, LLAMA_WCLS: c.vocab_size * c.dim * 2,
-                 LLAMA_KCACHE: B * c.n_kv_heads * c.seq_len * self.hs * 2,
-                 LLAMA_VCACHE: B * c.n_kv_heads * c.seq_len * self.hs * 2,
-                 LLAMA_LOGITS: B * c.vocab_size * 4, LLAMA_TOKENS: B * 4,
+        c, B, n = self.cfg, self.batch, self.world
+        kvh = c.n_kv_heads // n
+        sizes = {LLAMA_TOK_EMB: c.vocab_size * c.dim * 2, LLAMA_RMS_ATT: c.dim * 4, LLAMA_RMS_FFN: c.dim * 4,
+                 LLAMA_RMS_FINAL: c.dim * 4,
+                 LLAMA_KCACHE: B * kvh * c.seq_len * self.hs * 2,
+                 LLAMA_VCACHE: B * kvh * c.seq_len * self.hs * 2,
+                 LLAMA_LOGITS: B * (c.vocab_size // n) * 4, LLAMA_TOKENS: B * 4,
                  LLAMA_GENERATED: B * self.max_steps * 4, LLAMA_POS: 4, LLAMA_RESIDUAL: B * c.dim * 4}
+        if which in (LLAMA_WQKV, LLAMA_WO, LLAMA_W13, LLAMA_W2, LLAMA_WCLS):
+            r, k = self._shape(which)
+            return r * k * 2
         return sizes[which]
 
     def generated(self):
         return self.read(LLAMA_GENERATED, dtype=np.int32).reshape(self.batch, self.max_steps)
 
     def logits(self):
-        return self.read(LLAMA_LOGITS, dtype=np.float32).reshape(self.batch, self.cfg.vocab_size)
+        """This shard's logits [batch][vocab_size / world]."""
+        return self.read(LLAMA_LOGITS, dtype=np.float32).reshape(self.batch, self.cfg.vocab_size // self.world)
 
     def cache_rows(self, layer, seq, which=LLAMA_KCACHE, positions=None):
-        """bf16 bits [kv_heads][positions][hs] of one sequence's cache."""
+        """bf16 bits [kv_heads][positions][hs] of one sequence's cache (this shard's heads)."""
         c = self.cfg
         n = c.seq_len if positions is None else positions
         per_head = c.seq_len * self.hs
-        out = np.empty((c.n_kv_heads, n, self.hs), np.uint16)
-        for kh in range(c.n_kv_heads):
-            off = (seq * c.n_kv_heads + kh) * per_head
+        kvh = c.n_kv_heads // self.world
+        out = np.empty((kvh, n, self.hs), np.uint16)
+        for kh in range(kvh):
+            off = (seq * kvh + kh) * per_head
             out[kh] = self.read(which, layer, np.uint16, n * self.hs, off).reshape(n, self.hs)
         return out
 
@@ -641,10 +652,16 @@ class Llama:
         return codes, scales, float(alpha[1])
 
     def _shape(self, which):
-        c = self.cfg
-        return {LLAMA_WQKV: (c.dim + 2 * self.kv_dim, c.dim), LLAMA_WO: (c.dim, c.dim),
-                LLAMA_W13: (2 * c.hidden_dim, c.dim), LLAMA_W2: (c.dim, c.hidden_dim),
-                LLAMA_WCLS: (c.vocab_size, c.dim)}[which]
+        c, n = self.cfg, self.world
+        return {LLAMA_WQKV: (c.dim // n + 2 * self.kv_dim, c.dim), LLAMA_WO: (c.dim // n, c.dim),
+                LLAMA_W13: (2 * c.hidden_dim // n, c.dim), LLAMA_W2: (c.dim // n, c.hidden_dim),
+                LLAMA_WCLS: (c.vocab_size // n, c.dim)}[which]
+
+    def segment(self, seg, layer=0, stream=None):
+        check(lib().ce_llama_enqueue_segment(self._h, seg, layer, _stream(stream)))
+
+    def bind_exchange(self, att, delta, hb, top):
+        check(lib().ce_llama_bind_exchange(self._h, _ptr(att), _ptr(delta), _ptr(hb), _ptr(top)))
 
     def weights(self):
         """Every weight as host arrays: bf16 bits (uint16) for a bf16 model,
@@ -668,3 +685,13 @@ class Llama:
 def llama_status():
     """Reads and clears the decode kernels' status (raises on a failure)."""
     check(lib().ce_llama_status())
+
+
+def llama_shard_rows(cfg, rank, world, which):
+    """Global rows of rank's rows of a sharded weight (no CUDA call)."""
+    c = cfg if isinstance(cfg, LlamaConfig) else llama_config(**cfg)
+    n = ctypes.c_int()
+    check(lib().ce_llama_shard_rows(ctypes.byref(c), rank, world, which, None, ctypes.byref(n)))
+    out = np.empty(n.value, np.int32)
+    check(lib().ce_llama_shard_rows(ctypes.byref(c), rank, world, which, out.ctypes.data, ctypes.byref(n)))
+    return out

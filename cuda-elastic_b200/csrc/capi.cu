@@ -37,7 +37,7 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
                const float *alpha, int M, int N, int K, int lda, int ldd, int splits,
                long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
 int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
-            int ld_bytes, int nsf, cudaStream_t s);
+            int ld_bytes, int nsf, cudaStream_t s, const int *row_map = nullptr);
 int gemm_status();
 int gemm_bs_status();
 int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,

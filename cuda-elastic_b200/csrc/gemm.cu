@@ -927,18 +927,20 @@ gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tmA, W4Args wargs) {
 // k-block-major copy of row-major NVFP4 weights: codes [N][ld_bytes] (two
 // per byte) and scales [N][nsf] -> codes_t [K/64][N][32], scales_t [K/64][N][4].
 __global__ void w4_pack_kernel(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes,
-                               const uint8_t *scales, int N, int K, int ld_bytes, int nsf) {
+                               const uint8_t *scales, int N, int K, int ld_bytes, int nsf,
+                               const int *row_map) {
   const int kbs = K / 64;
   const size_t words = (size_t)kbs * N * 8;  // 4-byte words of codes_t
   const size_t step = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < words; i += step) {
     const size_t kb = i / ((size_t)N * 8), rem = i % ((size_t)N * 8);
     const size_t n = rem / 8, j = rem % 8;
-    const uint8_t *src = codes + n * ld_bytes + kb * 32 + j * 4;
+    const size_t sr = row_map ? (size_t)row_map[n] : n;  // source row
+    const uint8_t *src = codes + sr * ld_bytes + kb * 32 + j * 4;
     uint32_t v = (uint32_t)src[0] | ((uint32_t)src[1] << 8) | ((uint32_t)src[2] << 16) | ((uint32_t)src[3] << 24);
     reinterpret_cast<uint32_t *>(codes_t)[i] = v;
     if (j == 0) {
-      const uint8_t *ss = scales + n * nsf + kb * 4;
+      const uint8_t *ss = scales + sr * nsf + kb * 4;
       reinterpret_cast<uint32_t *>(scales_t)[kb * N + n] =
           (uint32_t)ss[0] | ((uint32_t)ss[1] << 8) | ((uint32_t)ss[2] << 16) | ((uint32_t)ss[3] << 24);
     }
@@ -1312,15 +1314,17 @@ int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks)
   return best;
 }
 
+// row_map (device, N entries; nullptr = identity): packed row n comes from
+// source row row_map[n] (a shard's rows of a whole quantized matrix).
 int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
-            int ld_bytes, int nsf, cudaStream_t s) {
+            int ld_bytes, int nsf, cudaStream_t s, const int *row_map) {
   CE_REQUIRE(codes_t && scales_t && codes && scales, "null argument");
   CE_REQUIRE(N >= 1 && K >= 64 && K % 64 == 0 && ld_bytes * 2 >= K && nsf * 16 >= K,
              "bad NVFP4 weight shape %dx%d (ld_bytes %d, scales per row %d)", N, K, ld_bytes, nsf);
   const size_t words = (size_t)(K / 64) * N * 8;
   int blocks = (int)((words + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  w4_pack_kernel<<<blocks, 256, 0, s>>>(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf);
+  w4_pack_kernel<<<blocks, 256, 0, s>>>(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf, row_map);
   CE_LAUNCH_CHECK("w4_pack_kernel");
   return CE_OK;
 }

@@ -16,14 +16,24 @@
 // gemm.cu. Weights are bf16 [out][in] (K-major), the per-layer QKV rows
 // stacked [q; k; v] and the FFN's w1 and w3 rows interleaved (w1_0, w3_0,
 // w1_1, ...) so each is one GEMM and the SwiGLU pairs meet in one tile of
-// the w1|w3 GEMM, whose epilogue writes the w2 operand directly. The KV cache is bf16 [layer][batch][kv_head][seq_len][head_size]: the
-// keys of one (sequence, head) are one contiguous run that a single bulk copy
-// moves into shared memory. Decode attention is split over position chunks
-// (flash-decoding): one 128-thread CTA per (chunk, head, sequence) stages its
-// K and V rows with cp.async.bulk, and the last CTA of each (sequence, head)
-// to finish merges the chunks' (max, sum, output) triples. The current position and step live in device
-// memory, advanced by the last launch of the step, so one captured step
-// graph replays for every token.
+// the w1|w3 GEMM, whose epilogue writes the w2 operand directly. The KV
+// cache is bf16 [layer][batch][kv_head][seq_len][head_size]: the keys of one
+// (sequence, head) are one contiguous run that bulk copies move into shared
+// memory. Decode attention streams each (sequence, head) through one CTA with
+// an online softmax (attn_decode_kernel). The current position and step live
+// in device memory, advanced by the last launch of the step, so one captured
+// step graph replays for every token.
+//
+// Row-sharded tensor parallelism (world > 1): rank r of n holds the rows of
+// every weight that produce its slice of each output (its n_heads / n query
+// heads and n_kv_heads / n KV heads of the QKV rows and of the cache, dim / n
+// rows of wo and w2, hidden / n interleaved w1|w3 pairs, vocab / n classifier
+// rows) and computes them on the full, replicated activations; the host joins
+// the slices with all-gathers between the segments of ce_llama_enqueue_segment
+// (attention output, o-projection output, SwiGLU product, w2 output, and the
+// per-rank greedy candidates). The residual stream is replicated: every rank
+// adds the same gathered outputs. Each rank generates exactly its rows of
+// the same global random model, so the sharded and unsharded models agree.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -50,7 +60,7 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
                long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
 int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
 int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
-            int ld_bytes, int nsf, cudaStream_t s);
+            int ld_bytes, int nsf, cudaStream_t s, const int *row_map = nullptr);
 int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
                    const float *x, int rows, int cols, int ld_bytes, cudaStream_t s);
 
@@ -96,16 +106,40 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
 // elements at out (filled == run: one contiguous fill of n elements). The
 // value at element e is a function of (seed, stream, e) only.
 __global__ void init_normal_bf16_kernel(uint16_t *out, size_t n, uint64_t seed, uint64_t stream,
-                                        float std, size_t run, size_t filled) {
+                                        float std, size_t run, size_t filled, size_t group_runs = 1,
+                                        size_t global_group_runs = 1, size_t group_offset = 0) {
+  // local run r of a group of group_runs is global run (r / group_runs) *
+  // global_group_runs + group_offset + r % group_runs (the KV heads of a shard)
   const size_t step = (size_t)gridDim.x * blockDim.x;
   for (size_t k = (size_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += step) {
-    const size_t i = (k / filled) * run + k % filled;
+    const size_t run_local = k / filled;
+    const size_t rg = (run_local / group_runs) * global_group_runs + group_offset + run_local % group_runs;
+    const size_t i = rg * run + k % filled;
     const uint64_t r = mix64(seed ^ mix64(stream * 0x632BE59BD9B4E019ull + i));
     const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
     const float u2 = (float)((r >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
     const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
     __nv_bfloat16 h = __float2bfloat16_rn(z * std);
-    out[i] = *reinterpret_cast<uint16_t *>(&h);
+    out[k / filled * run + k % filled] = *reinterpret_cast<uint16_t *>(&h);
+  }
+}
+
+// Rows of stacked per-layer bf16 matrices: local element (l, i, c) of
+// [layers][rows][cols] takes the value of global element (l, map[i], c) of
+// [layers][global_rows][cols] (stream `stream` of seed).
+__global__ void init_rows_bf16_kernel(uint16_t *out, int layers, int rows, int cols, int global_rows,
+                                      const int *map, uint64_t seed, uint64_t stream, float std) {
+  const size_t n = (size_t)layers * rows * cols;
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t k = (size_t)blockIdx.x * blockDim.x + threadIdx.x; k < n; k += step) {
+    const size_t c = k % cols, li = k / cols;
+    const size_t l = li / rows, i = li % rows;
+    const size_t g = ((size_t)l * global_rows + map[i]) * cols + c;
+    const uint64_t r = mix64(seed ^ mix64(stream * 0x632BE59BD9B4E019ull + g));
+    const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((r >> 16) & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    __nv_bfloat16 h = __float2bfloat16_rn(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2) * std);
+    out[k] = *reinterpret_cast<uint16_t *>(&h);
   }
 }
 
@@ -134,7 +168,7 @@ template <int NV>
 __global__ void __launch_bounds__(kRowThreads)
 residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_stride,
                         const uint16_t *emb, const int *tokens, int vocab, const float *w,
-                        uint16_t *xb, int dim, float eps, int f16) {
+                        uint16_t *xb, int dim, float eps, int f16, int shard_cols) {
   __shared__ float scratch[32];
   pdl_launch_dependents();
   pdl_wait();
@@ -164,11 +198,19 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
       if (i < cols4) {
         v[j] = xr[i];
         if (dr) {
-          // the sublayer's output: its split-K partials summed in split order
-          float4 d = dr[i];
-          for (int sp = 1; sp < nsplit; ++sp) {
-            const float4 e = dr[i + sp * (split_stride / 4)];
-            d.x += e.x, d.y += e.y, d.z += e.z, d.w += e.w;
+          float4 d;
+          if (shard_cols > 0) {
+            // gathered shards: [shard][batch][shard_cols], shard_cols * batch apart
+            const int col = 4 * i, sh = col / shard_cols;
+            d = *reinterpret_cast<const float4 *>(delta + (size_t)sh * split_stride +
+                                                  (size_t)b * shard_cols + (col - sh * shard_cols));
+          } else {
+            // the sublayer's output: its split-K partials summed in split order
+            d = dr[i];
+            for (int sp = 1; sp < nsplit; ++sp) {
+              const float4 e = dr[i + sp * (split_stride / 4)];
+              d.x += e.x, d.y += e.y, d.z += e.z, d.w += e.w;
+            }
           }
           v[j].x += d.x, v[j].y += d.y, v[j].z += d.z, v[j].w += d.w;
           xr[i] = v[j];
@@ -500,6 +542,94 @@ __global__ void advance_kernel(int *pos, int *step) {
   *step += 1;
 }
 
+// [shards][batch][cols] 16-bit slices to [batch][shards * cols] rows (cols % 8 == 0).
+__global__ void join_shards_kernel(const uint16_t *src, uint16_t *dst, int shards, int batch, int cols) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int v8 = cols / 8;
+  const size_t n = (size_t)shards * batch * v8;
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const size_t sh = i / ((size_t)batch * v8), rem = i % ((size_t)batch * v8);
+    const size_t b = rem / v8, c = rem % v8;
+    reinterpret_cast<uint4 *>(dst)[b * (size_t)shards * v8 + sh * v8 + c] = reinterpret_cast<const uint4 *>(src)[i];
+  }
+}
+
+// dst[b][j] = sum over s (in split order) of src[s][b][j], fp32, n4 float4s per split.
+__global__ void sum_splits_kernel(const float *src, float *dst, int splits, size_t n4) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += step) {
+    float4 a = reinterpret_cast<const float4 *>(src)[i];
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 e = reinterpret_cast<const float4 *>(src)[i + sp * n4];
+      a.x += e.x, a.y += e.y, a.z += e.z, a.w += e.w;
+    }
+    reinterpret_cast<float4 *>(dst)[i] = a;
+  }
+}
+
+// First maximum of each row of this shard's logits [batch][cols]: (value,
+// global index first + idx) as a float2 whose second lane holds the index
+// bits (NaN never wins; an all-NaN row gives (-inf, first)).
+__global__ void __launch_bounds__(kRowThreads)
+shard_top1_kernel(const float *logits, int cols, int first, float2 *top) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x;
+  const float *row = logits + (size_t)b * cols;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < cols; i += kRowThreads) {
+    const float v = row[i];
+    if (v > best) best = v, idx = i;
+  }
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_down_sync(0xffffffffu, best, off);
+    const int oi = __shfl_down_sync(0xffffffffu, idx, off);
+    if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sv[w] = best, si[w] = idx;
+  __syncthreads();
+  if (w == 0) {
+    best = lane < kRowThreads / 32 ? sv[lane] : -INFINITY;
+    idx = lane < kRowThreads / 32 ? si[lane] : 0x7fffffff;
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ov = __shfl_down_sync(0xffffffffu, best, off);
+      const int oi = __shfl_down_sync(0xffffffffu, idx, off);
+      if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
+    }
+    if (lane == 0) top[b] = make_float2(best, __int_as_float(first + (idx == 0x7fffffff ? 0 : idx)));
+  }
+}
+
+// The global greedy token of each row from the shards' candidates
+// top[shards][batch]: largest value, lowest index on ties (the first maximum
+// over the whole vocabulary).
+__global__ void pick_top_kernel(const float2 *top, int shards, int batch, int *tokens, int *generated,
+                                int cap, const int *step_ptr) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int s = 0; s < shards; ++s) {
+    const float2 t = top[(size_t)s * batch + b];
+    const int ti = __float_as_int(t.y);
+    if (t.x > best || (t.x == best && ti < idx)) best = t.x, idx = ti;
+  }
+  if (idx == 0x7fffffff) idx = 0;
+  tokens[b] = idx;
+  const int step = *step_ptr;
+  if (step >= 0 && step < cap) generated[(size_t)b * cap + step] = idx;
+}
+
 template <typename F>
 int launch_rows(int nv, F &&f) {
   switch (nv) {
@@ -558,6 +688,15 @@ struct QMat {
 struct ce_llama {
   ce_llama_config c{};
   int B = 0, cap = 0, precision = 0;
+  // shard: rank of world; local heads, KV heads, attention width (heads x hs),
+  // hidden slice and vocabulary slice (all global when world == 1)
+  int rank = 0, world = 1, lH = 0, lKH = 0, lD = 0, lHd = 0, lV = 0;
+  // exchange buffers of the sharded segments (caller-owned device memory):
+  // [world][batch][lD] 16-bit, [world][batch][lD] fp32, [world][batch][lHd]
+  // 16-bit, [world][batch] float2
+  uint16_t *x_att = nullptr, *x_hb = nullptr;
+  float *x_delta = nullptr;
+  float2 *x_top = nullptr;
   int hs = 0, kv_dim = 0, qkv_rows = 0, chunk = 0, nchunk = 0, nv = 0;
   int sp_qkv = 1, sp_o = 1, sp_13 = 1, sp_2 = 1;  // split-K counts of the layer GEMMs
   bool pdl = true;  // programmatic dependent launch between the step's kernels
@@ -596,17 +735,46 @@ void free_llama(ce_llama *m) {
 }
 
 size_t wqkv_elems(const ce_llama *m) { return (size_t)m->qkv_rows * m->c.dim; }
-size_t wo_elems(const ce_llama *m) { return (size_t)m->c.dim * m->c.dim; }
-size_t w13_elems(const ce_llama *m) { return (size_t)2 * m->c.hidden_dim * m->c.dim; }
-size_t w2_elems(const ce_llama *m) { return (size_t)m->c.dim * m->c.hidden_dim; }
+size_t wo_elems(const ce_llama *m) { return (size_t)m->lD * m->c.dim; }
+size_t w13_elems(const ce_llama *m) { return (size_t)2 * m->lHd * m->c.dim; }
+size_t w2_elems(const ce_llama *m) { return (size_t)m->lD * m->c.hidden_dim; }
 
-// (rows, cols) of weight kind k: 0 wqkv, 1 wo, 2 w13, 3 w2, 4 classifier.
+// (rows, cols) of this shard's weight kind k: 0 wqkv, 1 wo, 2 w13, 3 w2,
+// 4 classifier.
 void mat_shape(const ce_llama *m, int k, int *rows, int *cols) {
   const ce_llama_config &c = m->c;
-  const int r[5] = {m->qkv_rows, c.dim, 2 * c.hidden_dim, c.dim, c.vocab_size};
+  const int r[5] = {m->qkv_rows, m->lD, 2 * m->lHd, m->lD, m->lV};
   const int q[5] = {c.dim, c.dim, c.dim, c.hidden_dim, c.dim};
   *rows = r[k];
   *cols = q[k];
+}
+
+// Global row of each of this shard's rows of weight kind k (see mat_shape),
+// for a model of config c split over world ranks.
+void shard_rows(const ce_llama_config &c, int rank, int world, int k, std::vector<int> *rows) {
+  const int hs = c.dim / c.n_heads, kvd = hs * c.n_kv_heads;
+  const int lD = c.dim / world, lKV = kvd / world, lHd = c.hidden_dim / world, lV = c.vocab_size / world;
+  rows->clear();
+  auto add = [&](int g0, int n) {
+    for (int i = 0; i < n; ++i) rows->push_back(g0 + i);
+  };
+  switch (k) {
+    case 0:  // q rows of this rank's heads, then its k and v rows
+      add(rank * lD, lD);
+      add(c.dim + rank * lKV, lKV);
+      add(c.dim + kvd + rank * lKV, lKV);
+      break;
+    case 1: add(rank * lD, lD); break;
+    case 2: add(rank * 2 * lHd, 2 * lHd); break;  // interleaved (w1, w3) pairs
+    case 3: add(rank * lD, lD); break;
+    default: add(rank * lV, lV); break;
+  }
+}
+
+int global_rows(const ce_llama_config &c, int k) {
+  const int kvd = c.dim / c.n_heads * c.n_kv_heads;
+  const int r[5] = {c.dim + 2 * kvd, c.dim, 2 * c.hidden_dim, c.dim, c.vocab_size};
+  return r[k];
 }
 
 struct TensorView {
@@ -635,10 +803,10 @@ int tensor_of(ce_llama *m, int which, int layer, TensorView *v) {
     case CE_LLAMA_RMS_ATT: *v = {m->rms_att + L * c.dim, (size_t)c.dim * 4}; break;
     case CE_LLAMA_RMS_FFN: *v = {m->rms_ffn + L * c.dim, (size_t)c.dim * 4}; break;
     case CE_LLAMA_RMS_FINAL: *v = {m->rms_final, (size_t)c.dim * 4}; break;
-    case CE_LLAMA_WCLS: *v = {m->wcls, (size_t)c.vocab_size * c.dim * 2}; break;
+    case CE_LLAMA_WCLS: *v = {m->wcls, (size_t)m->lV * c.dim * 2}; break;
     case CE_LLAMA_KCACHE: *v = {m->kcache + L * m->layer_kv, m->layer_kv * 2}; break;
     case CE_LLAMA_VCACHE: *v = {m->vcache + L * m->layer_kv, m->layer_kv * 2}; break;
-    case CE_LLAMA_LOGITS: *v = {m->logits, (size_t)m->B * c.vocab_size * 4}; break;
+    case CE_LLAMA_LOGITS: *v = {m->logits, (size_t)m->B * m->lV * 4}; break;
     case CE_LLAMA_TOKENS: *v = {m->tokens, (size_t)m->B * 4}; break;
     case CE_LLAMA_GENERATED: *v = {m->generated, (size_t)m->B * m->cap * 4}; break;
     case CE_LLAMA_POS: *v = {m->pos, 4}; break;
@@ -681,39 +849,61 @@ int ce_llama_validate(const ce_llama_config *c, int batch, int max_steps, int pr
   return CE_OK;
 }
 
-int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
-                    int precision, ce_stream_t stream) {
+int ce_llama_validate_shard(const ce_llama_config *c, int batch, int max_steps, int precision, int rank,
+                            int world) {
+  if (int rc = ce_llama_validate(c, batch, max_steps, precision)) return rc;
+  CE_REQUIRE(world >= 1 && rank >= 0 && rank < world, "rank %d of world %d", rank, world);
+  if (world == 1) return CE_OK;
+  CE_REQUIRE(c->n_heads % world == 0 && c->n_kv_heads % world == 0,
+             "the heads (%d query, %d key/value) must split evenly over %d ranks", c->n_heads, c->n_kv_heads, world);
+  CE_REQUIRE(c->hidden_dim % (8 * world) == 0, "hidden_dim / world must be a multiple of 8 (hidden %d, world %d)",
+             c->hidden_dim, world);
+  CE_REQUIRE(c->vocab_size % (4 * world) == 0, "vocab_size / world must be a multiple of 4 (vocab %d, world %d)",
+             c->vocab_size, world);
+  CE_REQUIRE((c->dim / world) % 8 == 0, "dim / world must be a multiple of 8 (dim %d, world %d)", c->dim, world);
+  return CE_OK;
+}
+
+int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
+                          int precision, int rank, int world, ce_stream_t stream) {
   CE_REQUIRE(out != nullptr, "null model pointer");
   *out = nullptr;
-  if (int rc = ce_llama_validate(cfg, batch, max_steps, precision)) return rc;
+  if (int rc = ce_llama_validate_shard(cfg, batch, max_steps, precision, rank, world)) return rc;
   if (int rc = configure_attention()) return rc;
   ce_llama *m = new ce_llama();
   m->c = *cfg;
   m->B = batch;
   m->cap = max_steps;
   m->precision = precision;
+  m->rank = rank;
+  m->world = world;
   m->hs = cfg->dim / cfg->n_heads;
-  m->kv_dim = m->hs * cfg->n_kv_heads;
-  m->qkv_rows = cfg->dim + 2 * m->kv_dim;
+  m->lH = cfg->n_heads / world;
+  m->lKH = cfg->n_kv_heads / world;
+  m->lD = m->lH * m->hs;
+  m->lHd = cfg->hidden_dim / world;
+  m->lV = cfg->vocab_size / world;
+  m->kv_dim = m->hs * m->lKH;  // this shard's k (and v) rows
+  m->qkv_rows = m->lD + 2 * m->kv_dim;
   m->chunk = attn_chunk_bytes(m->hs) / (m->hs * 2);
   m->nchunk = (cfg->seq_len + m->chunk - 1) / m->chunk;
   m->nv = pow2_at_least((cfg->dim / 4 + kRowThreads - 1) / kRowThreads);
   {
     // enough attention CTAs for about two waves of 3 per SM, never more
     // splits than chunks of the full cache
-    const long long pairs = (long long)batch * cfg->n_heads;
+    const long long pairs = (long long)batch * m->lH;
     const long long want = kAttnWantPerSm * sm_count();
     long long sp = (want + pairs - 1) / pairs;
     m->attn_splits = (int)std::max(1LL, std::min<long long>(sp, m->nchunk));
   }
-  m->layer_kv = (size_t)batch * cfg->n_kv_heads * cfg->seq_len * m->hs;
+  m->layer_kv = (size_t)batch * m->lKH * cfg->seq_len * m->hs;
   // split-K for the GEMMs whose tiles alone leave SMs idle at decode sizes;
   // at least 4 k-blocks (256 of K) per split
   auto splits = precision == CE_PREC_NVFP4_E2M1 ? gemm_w4a16_auto_splits : gemm_bf16_auto_splits;
   m->sp_qkv = splits(batch, m->qkv_rows, cfg->dim, 8, 4);
-  m->sp_o = splits(batch, cfg->dim, cfg->dim, 8, 4);
-  m->sp_13 = splits(batch, 2 * cfg->hidden_dim, cfg->dim, 8, 4);
-  m->sp_2 = splits(batch, cfg->dim, cfg->hidden_dim, 8, 4);
+  m->sp_o = splits(batch, m->lD, cfg->dim, 8, 4);
+  m->sp_13 = splits(batch, 2 * m->lHd, cfg->dim, 8, 4);
+  m->sp_2 = splits(batch, m->lD, cfg->hidden_dim, 8, 4);
   const int sp_delta = m->sp_o > m->sp_2 ? m->sp_o : m->sp_2;
   const ce_llama_config &c = *cfg;
   const size_t L = c.n_layers;
@@ -756,7 +946,7 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
     CE_ALLOC(m->wo, L * wo_elems(m) * 2);
     CE_ALLOC(m->w13, L * w13_elems(m) * 2);
     CE_ALLOC(m->w2, L * w2_elems(m) * 2);
-    CE_ALLOC(m->wcls, (size_t)c.vocab_size * c.dim * 2);
+    CE_ALLOC(m->wcls, (size_t)m->lV * c.dim * 2);
   }
   CE_ALLOC(m->rms_att, L * c.dim * 4);
   CE_ALLOC(m->rms_ffn, L * c.dim * 4);
@@ -770,14 +960,14 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   CE_ALLOC(m->x, (size_t)batch * c.dim * 4);
   CE_ALLOC(m->delta, (size_t)sp_delta * batch * c.dim * 4);
   CE_ALLOC(m->qkv, (size_t)m->sp_qkv * batch * m->qkv_rows * 4);
-  CE_ALLOC(m->h, (size_t)m->sp_13 * batch * 2 * c.hidden_dim * 4);
-  CE_ALLOC(m->logits, (size_t)batch * c.vocab_size * 4);
-  CE_ALLOC(m->part, (size_t)batch * c.n_heads * m->attn_splits * (m->hs + 2) * 4);
+  CE_ALLOC(m->h, (size_t)m->sp_13 * batch * 2 * m->lHd * 4);
+  CE_ALLOC(m->logits, (size_t)batch * m->lV * 4);
+  CE_ALLOC(m->part, (size_t)batch * m->lH * m->attn_splits * (m->hs + 2) * 4);
   CE_ALLOC(m->tokens, (size_t)batch * 4);
   CE_ALLOC(m->generated, (size_t)batch * max_steps * 4);
   CE_ALLOC(m->pos, 4);
   CE_ALLOC(m->step, 4);
-  CE_ALLOC(m->arrivals, (size_t)batch * c.n_heads * 4);
+  CE_ALLOC(m->arrivals, (size_t)batch * m->lH * 4);
 #undef CE_ALLOC
   // RoPE table: (cos, sin) of pos * 10000^(-2i/hs), computed in double once
   std::vector<float2> table((size_t)c.seq_len * (m->hs / 2));
@@ -790,7 +980,7 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   e = cudaMemcpyAsync(m->rope, table.data(), table.size() * sizeof(float2), cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->pos, 0, 4, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->step, 0, 4, s);
-  if (e == cudaSuccess) e = cudaMemsetAsync(m->arrivals, 0, (size_t)batch * c.n_heads * 4, s);
+  if (e == cudaSuccess) e = cudaMemsetAsync(m->arrivals, 0, (size_t)batch * m->lH * 4, s);
   if (e == cudaSuccess) e = cudaMemsetAsync(m->generated, 0xFF, (size_t)batch * max_steps * 4, s);
   if (e == cudaSuccess) e = cudaStreamSynchronize(s);  // the host table goes out of scope
   if (e != cudaSuccess) {
@@ -799,6 +989,11 @@ int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int m
   }
   *out = m;
   return CE_OK;
+}
+
+int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
+                    int precision, ce_stream_t stream) {
+  return ce_llama_create_shard(out, cfg, batch, max_steps, precision, 0, 1, stream);
 }
 
 int ce_llama_destroy(ce_llama *m) {
@@ -813,29 +1008,49 @@ int ce_llama_init_random(ce_llama *m, uint64_t seed, float weight_std, int kv_fi
   const ce_llama_config &c = m->c;
   const size_t L = c.n_layers;
   const int grid = 4 * sm_count(), threads = 256;
-  struct Item {
-    uint16_t *p;
-    size_t n;
-    float std;
-  };
-  const Item items[] = {{m->tok_emb, (size_t)c.vocab_size * c.dim, weight_std},
-                        {m->wqkv, L * wqkv_elems(m), weight_std},
-                        {m->wo, L * wo_elems(m), weight_std},
-                        {m->w13, L * w13_elems(m), weight_std},
-                        {m->w2, L * w2_elems(m), weight_std},
-                        {m->wcls, (size_t)c.vocab_size * c.dim, weight_std}};
-  uint64_t stream_id = 1;
-  for (const Item &it : items) {
-    const uint64_t id = stream_id++;
-    if (it.p == nullptr) continue;  // NVFP4 model: quantized below
-    init_normal_bf16_kernel<<<grid, threads, 0, s>>>(it.p, it.n, seed, id, it.std, it.n, it.n);
-    CE_LAUNCH_CHECK("init_normal_bf16_kernel");
+  // Streams of the random model: 1 embedding, 2 wqkv, 3 wo, 4 w13, 5 w2,
+  // 6 classifier (bf16 weights; values indexed by the global element, so a
+  // shard generates exactly its rows), 1000 + i NVFP4 matrix i, 100 / 101
+  // the K / V cache.
+  init_normal_bf16_kernel<<<grid, threads, 0, s>>>(m->tok_emb, (size_t)c.vocab_size * c.dim, seed, 1, weight_std,
+                                                   (size_t)c.vocab_size * c.dim, (size_t)c.vocab_size * c.dim);
+  CE_LAUNCH_CHECK("init_normal_bf16_kernel");
+  // row maps of this shard, kinds 0..4
+  std::vector<int> rows[5];
+  size_t most = 1;
+  for (int k = 0; k < 5; ++k) {
+    shard_rows(c, m->rank, m->world, k, &rows[k]);
+    most = std::max(most, rows[k].size());
   }
-  if (m->precision == CE_PREC_NVFP4_E2M1) {
-    // every matrix: fp32 N(0, std), then the NVFP4 quantizer (tensor amax,
-    // UE4M3 per 16 values, E2M1 codes), then the W4A16 GEMM's layout
+  int *d_map = nullptr;
+  CE_CUDA_TRY(cudaMalloc(&d_map, 5 * most * sizeof(int)));
+  int rc = CE_OK;
+  for (int k = 0; k < 5 && rc == CE_OK; ++k) {
+    const cudaError_t e = cudaMemcpy(d_map + k * most, rows[k].data(), rows[k].size() * sizeof(int),
+                                     cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) rc = cuda_error(e, "cudaMemcpy(row map)");
+  }
+  if (rc == CE_OK && m->precision == CE_PREC_BF16) {
+    uint16_t *w[5] = {m->wqkv, m->wo, m->w13, m->w2, m->wcls};
+    for (int k = 0; k < 5 && rc == CE_OK; ++k) {
+      int r, q;
+      mat_shape(m, k, &r, &q);
+      init_rows_bf16_kernel<<<grid, threads, 0, s>>>(w[k], k == 4 ? 1 : c.n_layers, r, q, global_rows(c, k),
+                                                     d_map + k * most, seed, 2 + k, weight_std);
+      const cudaError_t e = cudaPeekAtLastError();
+      if (e != cudaSuccess) rc = cuda_error(e, "init_rows_bf16_kernel");
+    }
+  }
+  if (rc == CE_OK && m->precision == CE_PREC_NVFP4_E2M1) {
+    // every matrix: the global matrix in fp32 N(0, std), the NVFP4 quantizer
+    // over all of it (tensor amax, UE4M3 per 16 values, E2M1 codes), then
+    // this shard's rows in the W4A16 GEMM's layout
     size_t biggest = 0;
-    for (const QMat &q : m->qm) biggest = std::max(biggest, (size_t)q.rows * q.cols);
+    for (int k = 0; k < 5; ++k) {
+      int r, q;
+      mat_shape(m, k, &r, &q);
+      biggest = std::max(biggest, (size_t)global_rows(c, k) * q);
+    }
     float *tmp = nullptr;
     uint8_t *tcodes = nullptr, *tscales = nullptr;
     unsigned int *amax = nullptr;
@@ -843,22 +1058,28 @@ int ce_llama_init_random(ce_llama *m, uint64_t seed, float weight_std, int kv_fi
     if (e == cudaSuccess) e = cudaMalloc(&tcodes, biggest / 2);
     if (e == cudaSuccess) e = cudaMalloc(&tscales, biggest / 16);
     if (e == cudaSuccess) e = cudaMalloc(&amax, 4);
-    int rc = e == cudaSuccess ? CE_OK : cuda_error(e, "cudaMalloc(quantization scratch)");
+    rc = e == cudaSuccess ? CE_OK : cuda_error(e, "cudaMalloc(quantization scratch)");
     for (size_t i = 0; i < m->qm.size() && rc == CE_OK; ++i) {
       const QMat &q = m->qm[i];
-      const size_t n = (size_t)q.rows * q.cols;
-      init_normal_f32_kernel<<<grid, threads, 0, s>>>(tmp, n, seed, 1000 + i, weight_std);
+      const int k = i == m->qm.size() - 1 ? 4 : (int)(i % 4);
+      const int grows = global_rows(c, k);
+      init_normal_f32_kernel<<<grid, threads, 0, s>>>(tmp, (size_t)grows * q.cols, seed, 1000 + i, weight_std);
       e = cudaPeekAtLastError();
       if (e != cudaSuccess) rc = cuda_error(e, "init_normal_f32_kernel");
-      if (rc == CE_OK) rc = quantize_nvfp4(tcodes, tscales, q.alpha, amax, tmp, q.rows, q.cols, q.cols / 2, s);
-      if (rc == CE_OK) rc = w4_pack(q.codes, q.scales, tcodes, tscales, q.rows, q.cols, q.cols / 2, q.cols / 16, s);
+      if (rc == CE_OK) rc = quantize_nvfp4(tcodes, tscales, q.alpha, amax, tmp, grows, q.cols, q.cols / 2, s);
+      if (rc == CE_OK)
+        rc = w4_pack(q.codes, q.scales, tcodes, tscales, q.rows, q.cols, q.cols / 2, q.cols / 16, s,
+                     d_map + k * most);
     }
     e = cudaStreamSynchronize(s);
     if (rc == CE_OK && e != cudaSuccess) rc = cuda_error(e, "NVFP4 weight set-up");
     for (void *p : {(void *)tmp, (void *)tcodes, (void *)tscales, (void *)amax})
       if (p) cudaFree(p);
-    if (rc) return rc;
   }
+  const cudaError_t se = cudaStreamSynchronize(s);
+  if (rc == CE_OK && se != cudaSuccess) rc = cuda_error(se, "weight set-up");
+  cudaFree(d_map);
+  if (rc) return rc;
   fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_att, L * c.dim, 1.0f);
   fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_ffn, L * c.dim, 1.0f);
   fill_f32_kernel<<<grid, threads, 0, s>>>(m->rms_final, (size_t)c.dim, 1.0f);
@@ -867,11 +1088,12 @@ int ce_llama_init_random(ce_llama *m, uint64_t seed, float weight_std, int kv_fi
   CE_CUDA_TRY(cudaMemsetAsync(m->kcache, 0, L * m->layer_kv * 2, s));
   CE_CUDA_TRY(cudaMemsetAsync(m->vcache, 0, L * m->layer_kv * 2, s));
   if (kv_fill > 0) {
-    const size_t runs = L * m->B * c.n_kv_heads;  // contiguous [seq_len][hs] runs
+    const size_t runs = L * m->B * m->lKH;  // contiguous [seq_len][hs] runs of this shard's KV heads
     const size_t run = (size_t)c.seq_len * m->hs, filled = (size_t)kv_fill * m->hs;
     for (int which = 0; which < 2; ++which) {
       init_normal_bf16_kernel<<<grid, threads, 0, s>>>(which ? m->vcache : m->kcache, runs * filled, seed,
-                                                       100 + which, 1.0f, run, filled);
+                                                       100 + which, 1.0f, run, filled, (size_t)m->lKH,
+                                                       (size_t)c.n_kv_heads, (size_t)m->rank * m->lKH);
       CE_LAUNCH_CHECK("init_normal_bf16_kernel");
     }
   }
@@ -894,6 +1116,7 @@ int ce_llama_start(ce_llama *m, const int32_t *tokens_host, int pos, ce_stream_t
 
 int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
   CE_REQUIRE(m != nullptr, "null model");
+  CE_REQUIRE(m->world == 1, "a sharded model steps through ce_llama_enqueue_segment");
   cudaStream_t s = (cudaStream_t)stream;
   const ce_llama_config &c = m->c;
   const int B = m->B, D = c.dim, Hd = c.hidden_dim;
@@ -924,7 +1147,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     const int rc = launch_rows(m->nv, [&](auto nv) {
       lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
                           "residual_rmsnorm_kernel", m->x, delta, nsplit, delta_stride, emb,
-                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4);
+                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, 0);
     });
     return rc ? rc : lrc;
   };
@@ -980,6 +1203,148 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
                      (const int *)m->step);
   if (rc) return rc;
   return launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_kernel", m->pos, m->step);
+}
+
+int ce_llama_bind_exchange(ce_llama *m, uint16_t *att, float *delta, uint16_t *hb, float *top) {
+  CE_REQUIRE(m != nullptr, "null model");
+  CE_REQUIRE(att && delta && hb && top, "null exchange buffer");
+  CE_REQUIRE(((reinterpret_cast<uintptr_t>(att) | reinterpret_cast<uintptr_t>(delta) |
+               reinterpret_cast<uintptr_t>(hb) | reinterpret_cast<uintptr_t>(top)) & 15u) == 0,
+             "exchange buffers must be 16-byte aligned");
+  m->x_att = att;
+  m->x_delta = delta;
+  m->x_hb = hb;
+  m->x_top = reinterpret_cast<float2 *>(top);
+  return CE_OK;
+}
+
+int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t stream) {
+  CE_REQUIRE(m != nullptr, "null model");
+  CE_REQUIRE(m->x_att && m->x_delta && m->x_hb && m->x_top, "exchange buffers are not bound");
+  const ce_llama_config &c = m->c;
+  CE_REQUIRE(segment == CE_LLAMA_SEG_HEAD || segment == CE_LLAMA_SEG_PICK || (layer >= 0 && layer < c.n_layers),
+             "layer %d out of range", layer);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int B = m->B, D = c.dim, n = m->world, r = m->rank;
+  const int lD = m->lD, lHd = m->lHd;
+  const bool pdl = m->pdl, w4 = m->precision == CE_PREC_NVFP4_E2M1;
+  const size_t slot_d = (size_t)B * lD;  // one rank's slot of the delta / attention exchange
+  const float eps = 1e-5f;
+  auto gemm = [&](int k, int l, float *d, const uint16_t *a, int ldd, int splits, long long stride,
+                  uint16_t *sw_out, int sw_ld) -> int {
+    int N, K;
+    mat_shape(m, k, &N, &K);
+    if (w4) {
+      const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
+      return gemm_w4a16(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out, sw_ld, s,
+                        pdl);
+    }
+    const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
+                        : k == 2 ? m->w13 + l * w13_elems(m) : k == 3 ? m->w2 + l * w2_elems(m) : m->wcls;
+    if (sw_out) return gemm_bf16_swiglu(sw_out, sw_ld, a, w, B, N, K, K, K, s, pdl);
+    return gemm_bf16_split(d, a, w, B, N, K, K, K, ldd, splits, stride, s, pdl);
+  };
+  // residual add of the gathered delta ([rank][batch][lD]) or the embedding,
+  // then RMSNorm into xb
+  auto norm = [&](bool embed, const float *w) {
+    int lrc = CE_OK;
+    const int rc = launch_rows(m->nv, [&](auto nv) {
+      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
+                          "residual_rmsnorm_kernel", m->x, embed ? (const float *)nullptr : (const float *)m->x_delta,
+                          1, slot_d, embed ? (const uint16_t *)m->tok_emb : (const uint16_t *)nullptr,
+                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, lD);
+    });
+    return rc ? rc : lrc;
+  };
+  // the o-projection / w2 output: GEMM into the split partials, summed into
+  // this rank's slot of the delta exchange
+  auto to_delta_slot = [&](int k, int l, const uint16_t *a, int splits) -> int {
+    const long long stride = (long long)B * lD;
+    int rc = gemm(k, l, m->delta, a, lD, splits, stride, nullptr, 0);
+    if (rc) return rc;
+    const size_t n4 = slot_d / 4;
+    return launch_kernel(sum_splits_kernel, dim3((unsigned)std::min<size_t>((n4 + 255) / 256, 4 * sm_count())),
+                         dim3(256), 0, s, pdl, "sum_splits_kernel", (const float *)m->delta,
+                         m->x_delta + (size_t)r * slot_d, splits, n4);
+  };
+  const int join_grid = 2 * sm_count();
+  const int l = layer;
+  int rc = CE_OK;
+  switch (segment) {
+    case CE_LLAMA_SEG_ATTN: {
+      rc = norm(l == 0, m->rms_att + (size_t)l * D);
+      if (rc) return rc;
+      const size_t qkv_stride = (size_t)B * m->qkv_rows;
+      rc = gemm(0, l, m->qkv, m->xb, m->qkv_rows, m->sp_qkv, (long long)qkv_stride, nullptr, 0);
+      if (rc) return rc;
+      uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
+      rc = launch_kernel(rope_append_kernel, dim3(B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
+                         m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope, (const int *)m->pos,
+                         lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
+      if (rc) return rc;
+      const dim3 agrid(m->attn_splits, m->lH, B);
+      const size_t smem = attn_smem_bytes(m->chunk, m->hs);
+      uint16_t *slot = m->x_att + (size_t)r * slot_d;
+      auto attention = [&](auto hs_tag) {
+        constexpr int HS = decltype(hs_tag)::value;
+        return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(kAttnThreads), smem, s, pdl,
+                             "attn_decode_kernel", (const float *)m->qkv, m->qkv_rows, (const uint16_t *)kc,
+                             (const uint16_t *)vc, (const int *)m->pos, m->lH, m->lKH, c.seq_len, m->chunk,
+                             m->attn_splits, m->part, m->arrivals, slot, lD, (int)w4);
+      };
+      return m->hs == 64 ? attention(std::integral_constant<int, 64>{})
+                         : attention(std::integral_constant<int, 128>{});
+    }
+    case CE_LLAMA_SEG_OPROJ:
+      rc = launch_kernel(join_shards_kernel, dim3(join_grid), dim3(256), 0, s, pdl, "join_shards_kernel",
+                         (const uint16_t *)m->x_att, m->att, n, B, lD);
+      if (rc) return rc;
+      return to_delta_slot(1, l, m->att, m->sp_o);
+    case CE_LLAMA_SEG_FFN_IN: {
+      rc = norm(false, m->rms_ffn + (size_t)l * D);
+      if (rc) return rc;
+      uint16_t *slot = m->x_hb + (size_t)r * B * lHd;
+      if (m->sp_13 == 1) return gemm(2, l, nullptr, m->xb, 2 * lHd, 1, 0, slot, lHd);
+      const size_t h_stride = (size_t)B * 2 * lHd;
+      rc = gemm(2, l, m->h, m->xb, 2 * lHd, m->sp_13, (long long)h_stride, nullptr, 0);
+      if (rc) return rc;
+      return launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
+                           (const float *)m->h, m->sp_13, h_stride, slot, B, lHd, (int)w4);
+    }
+    case CE_LLAMA_SEG_FFN_OUT:
+      rc = launch_kernel(join_shards_kernel, dim3(join_grid), dim3(256), 0, s, pdl, "join_shards_kernel",
+                         (const uint16_t *)m->x_hb, m->hb, n, B, lHd);
+      if (rc) return rc;
+      return to_delta_slot(3, l, m->hb, m->sp_2);
+    case CE_LLAMA_SEG_HEAD:
+      rc = norm(false, m->rms_final);
+      if (rc) return rc;
+      rc = gemm(4, 0, m->logits, m->xb, m->lV, 1, 0, nullptr, 0);
+      if (rc) return rc;
+      return launch_kernel(shard_top1_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "shard_top1_kernel",
+                           (const float *)m->logits, m->lV, r * m->lV, m->x_top + (size_t)r * B);
+    case CE_LLAMA_SEG_PICK:
+      rc = launch_kernel(pick_top_kernel, dim3((B + 127) / 128), dim3(128), 0, s, pdl, "pick_top_kernel",
+                         (const float2 *)m->x_top, n, B, m->tokens, m->generated, m->cap, (const int *)m->step);
+      if (rc) return rc;
+      return launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_kernel", m->pos, m->step);
+    default:
+      return set_error(CE_ERR_USAGE, format("unknown segment %d", segment));
+  }
+}
+
+int ce_llama_shard_rows(const ce_llama_config *cfg, int rank, int world, int which, int32_t *rows_out,
+                        int *count) {
+  CE_REQUIRE(cfg != nullptr && count != nullptr, "null argument");
+  const int k = which == CE_LLAMA_WQKV ? 0 : which == CE_LLAMA_WO ? 1 : which == CE_LLAMA_W13 ? 2
+                : which == CE_LLAMA_W2 ? 3 : which == CE_LLAMA_WCLS ? 4 : -1;
+  CE_REQUIRE(k >= 0, "tensor %d is not a sharded weight", which);
+  if (int rc = ce_llama_validate_shard(cfg, 1, 1, CE_PREC_BF16, rank, world)) return rc;
+  std::vector<int> rows;
+  shard_rows(*cfg, rank, world, k, &rows);
+  if (rows_out) std::copy(rows.begin(), rows.end(), rows_out);
+  *count = (int)rows.size();
+  return CE_OK;
 }
 
 int ce_llama_set_pdl(ce_llama *m, int enable) {

@@ -1,5 +1,5 @@
-"""Row-sharded (tensor-parallel) layer of the op trio GEMM and the decoder
-classifier across the GPUs of one node.
+"""Row-sharded (tensor-parallel) layer of the op trio GEMM, the decoder
+classifier and the Llama-2 decoder step across the GPUs of one node.
 
 The matrix W [rows][size] is split by output rows into contiguous slices,
 one per rank (the first rows % world ranks take one extra row). Each rank
@@ -93,3 +93,52 @@ class RowShardedPlan:
 
     def close(self):
         self.local.close()
+
+
+class ShardedLlama:
+    """A Llama-2 decoder step row-sharded over the ranks of a process group
+    (one GPU each): the library's ce_llama segments compute this rank's slice
+    of each output into caller-owned exchange buffers, and in-place
+    all-gathers (NCCL over NVLink) join the slices between them. All work is
+    enqueued on one stream, so a whole step can be captured in a CUDA graph
+    (torch captures NCCL collectives)."""
+
+    def __init__(self, ce, cfg, batch, max_steps, precision, group=None, stream=None):
+        self.ce = ce
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.model = ce.Llama(cfg, batch, max_steps, precision=precision, stream=stream,
+                              rank=self.rank, world=self.world)
+        c = self.model.cfg
+        n, B = self.world, batch
+        dev = torch.device("cuda", torch.cuda.current_device())
+        # 16-bit operands travel as bfloat16 tensors (NCCL has no int16 type);
+        # the gather copies bits, so fp16 operands pass through unchanged
+        self.att = torch.zeros((n, B, c.dim // n), dtype=torch.bfloat16, device=dev)
+        self.delta = torch.zeros((n, B, c.dim // n), dtype=torch.float32, device=dev)
+        self.hb = torch.zeros((n, B, c.hidden_dim // n), dtype=torch.bfloat16, device=dev)
+        self.top = torch.zeros((n, B, 2), dtype=torch.float32, device=dev)
+        self.model.bind_exchange(self.att, self.delta, self.hb, self.top)
+
+    def _gather(self, buf):
+        # in place: this rank's slot is the input of the all-gather
+        dist.all_gather_into_tensor(buf, buf[self.rank], group=self.group)
+
+    def step(self, stream=None):
+        m, ce = self.model, self.ce
+        for layer in range(m.cfg.n_layers):
+            m.segment(ce.SEG_ATTN, layer, stream=stream)
+            self._gather(self.att)
+            m.segment(ce.SEG_OPROJ, layer, stream=stream)
+            self._gather(self.delta)
+            m.segment(ce.SEG_FFN_IN, layer, stream=stream)
+            self._gather(self.hb)
+            m.segment(ce.SEG_FFN_OUT, layer, stream=stream)
+            self._gather(self.delta)
+        m.segment(ce.SEG_HEAD, stream=stream)
+        self._gather(self.top)
+        m.segment(ce.SEG_PICK, stream=stream)
+
+    def close(self):
+        self.model.close()

@@ -459,6 +459,16 @@ typedef struct ce_llama_config {
 #define CE_LLAMA_POS 14       /* int32: position of the next step */
 #define CE_LLAMA_RESIDUAL 15  /* fp32 [batch][dim]: residual stream after the last layer */
 
+/* Segments of one decode step of a row-sharded model (ce_llama_enqueue_segment). */
+#define CE_LLAMA_SEG_ATTN 0    /* residual + RMSNorm, this rank's QKV rows, RoPE, KV append,
+                                  attention of its heads into its slot of the att exchange */
+#define CE_LLAMA_SEG_OPROJ 1   /* gathered att -> this rank's wo rows -> its slot of the delta exchange */
+#define CE_LLAMA_SEG_FFN_IN 2  /* residual + RMSNorm, this rank's w1|w3 pairs, SwiGLU -> its hb slot */
+#define CE_LLAMA_SEG_FFN_OUT 3 /* gathered hb -> this rank's w2 rows -> its delta slot */
+#define CE_LLAMA_SEG_HEAD 4    /* residual + final RMSNorm, this rank's classifier rows, its
+                                  greedy candidate -> its top slot */
+#define CE_LLAMA_SEG_PICK 5    /* gathered candidates -> tokens and generated; advance */
+
 /* Shape and memory checks of ce_llama_create alone (no CUDA call). */
 int ce_llama_validate(const ce_llama_config *cfg, int batch, int max_steps, int precision);
 
@@ -488,6 +498,37 @@ int ce_llama_start(ce_llama *model, const int32_t *tokens_host, int pos, ce_stre
  * generated[b][step], and advances position and step on the device.
  * Capturable: a captured step replays for every token. */
 int ce_llama_enqueue_step(ce_llama *model, ce_stream_t stream);
+
+/* Row-sharded tensor parallelism over `world` ranks (one process per GPU):
+ * rank `rank` holds the rows of every weight that produce its slice of each
+ * output (n_heads / world query heads and n_kv_heads / world KV heads, dim /
+ * world rows of wo and w2, hidden_dim / world interleaved w1|w3 pairs,
+ * vocab_size / world classifier rows) and the KV cache of its heads, and
+ * generates exactly those rows of the same global random model as an
+ * unsharded one (NVFP4: quantized over the whole matrix). world 1 is
+ * ce_llama_create. The north star's "sharded by output rows ... joined by an
+ * all-gather"; the reference has no multi-GPU code. */
+int ce_llama_validate_shard(const ce_llama_config *cfg, int batch, int max_steps, int precision,
+                            int rank, int world);
+int ce_llama_create_shard(ce_llama **model, const ce_llama_config *cfg, int batch, int max_steps,
+                          int precision, int rank, int world, ce_stream_t stream);
+
+/* Caller-owned device exchange buffers of a sharded step, all-gathered by
+ * the caller between segments (each rank writes its own slot r):
+ * att   16-bit [world][batch][dim / world]         (after SEG_ATTN)
+ * delta fp32   [world][batch][dim / world]         (after SEG_OPROJ, SEG_FFN_OUT)
+ * hb    16-bit [world][batch][hidden_dim / world]  (after SEG_FFN_IN)
+ * top   fp32   [world][batch][2] (value, index bits) (after SEG_HEAD).
+ * A step: for each layer ATTN, gather att, OPROJ, gather delta, FFN_IN,
+ * gather hb, FFN_OUT, gather delta; then HEAD, gather top, PICK. */
+int ce_llama_bind_exchange(ce_llama *model, uint16_t *att_dev, float *delta_dev, uint16_t *hb_dev,
+                           float *top_dev);
+int ce_llama_enqueue_segment(ce_llama *model, int segment, int layer, ce_stream_t stream);
+
+/* Global rows of rank's rows of weight `which` (CE_LLAMA_WQKV, _WO, _W13,
+ * _W2, _WCLS) in local order; rows_out may be NULL to get the count. No CUDA call. */
+int ce_llama_shard_rows(const ce_llama_config *cfg, int rank, int world, int which,
+                        int32_t *rows_out, int *count);
 
 /* Programmatic dependent launch between the kernels of a step (default on):
  * each kernel's prologue, and the GEMMs' L2 prefetch of their first weight

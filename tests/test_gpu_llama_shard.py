@@ -1,0 +1,140 @@
+"""The Llama-2 decoder step row-sharded over 2 GPUs (one process each, NCCL
+all-gathers between the library's segments) against the same model
+unsharded on one GPU: the residual stream after the last layer and every
+rank's logit slice within relative L2 1e-3 of the unsharded ones, and the
+greedy tokens equal wherever the unsharded logits are not a near tie; bf16
+and NVFP4 weights; a captured step graph (NCCL included) replays bit for bit
+like direct steps. Needs at least 2 visible GPUs; skipped otherwise."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, case, q):
+    import datetime
+    import importlib
+    import sys
+    sys.path.insert(0, ROOT)
+    import torch.distributed as dist
+    import __graft_entry__
+    ce = __graft_entry__.load_package()
+    rs = importlib.import_module("cuda_elastic_b200.rowshard")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        q.put(_body(rank, world, case, ce, rs, dist))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, False, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def _body(rank, world, case, ce, rs, dist):
+    cfg, prec_name, batch, fill, steps, graph = case
+    prec = {"bf16": ce.PREC_BF16, "nvfp4": ce.PREC_NVFP4_E2M1}[prec_name]
+    tokens0 = np.random.default_rng(5).integers(0, cfg["vocab_size"], batch).astype(np.int32)
+    sh = rs.ShardedLlama(ce, cfg, batch, steps, prec)
+    sh.model.init_random(seed=3, kv_fill=fill)
+    sh.model.start(tokens0, fill)
+    if graph:
+        sh.step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            sh.step()
+        for _ in range(steps - 1):
+            g.replay()
+        torch.cuda.synchronize()
+        del g
+    else:
+        for _ in range(steps):
+            sh.step()
+        torch.cuda.synchronize()
+    ce.llama_status()
+    gen = sh.model.generated().copy()
+    x = sh.model.read(ce.LLAMA_RESIDUAL, dtype=np.float32)
+    logits = sh.model.logits().astype(np.float64)
+    # direct steps of the same sharded model again: graph and direct agree bitwise
+    sh.model.start(tokens0, fill)
+    sh.model.init_random(seed=3, kv_fill=fill)
+    sh.model.start(tokens0, fill)
+    for _ in range(steps):
+        sh.step()
+    torch.cuda.synchronize()
+    gen2, x2 = sh.model.generated().copy(), sh.model.read(ce.LLAMA_RESIDUAL, dtype=np.float32)
+    sh.close()
+    # the unsharded model on this GPU
+    m = ce.Llama(cfg, batch, steps, precision=prec)
+    m.init_random(seed=3, kv_fill=fill)
+    m.start(tokens0, fill)
+    for _ in range(steps):
+        m.step()
+    torch.cuda.synchronize()
+    ce.llama_status()
+    ref_gen, ref_x = m.generated(), m.read(ce.LLAMA_RESIDUAL, dtype=np.float32)
+    lv = cfg["vocab_size"] // world
+    ref_logits = m.logits().astype(np.float64)
+    m.close()
+    dist.barrier()
+
+    def rel(a, b):
+        a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
+        return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+    ok = rel(x, ref_x) <= 1e-3 and rel(logits, ref_logits[:, rank * lv:(rank + 1) * lv]) <= 1e-3
+    diff = np.argwhere(gen != ref_gen)
+    # a differing token must come after a step whose top-2 gap the numerical
+    # error can bridge; the last step's logits are checked explicitly
+    err = np.abs(logits - ref_logits[:, rank * lv:(rank + 1) * lv]).max()
+    last = [b for b, s in diff if s == steps - 1]
+    top2 = np.sort(ref_logits, axis=1)[:, -2:]
+    ok = ok and all(top2[b, 1] - top2[b, 0] <= 4 * err for b in last)
+    ok = ok and len(diff) <= max(1, gen.size // 50)
+    same = np.array_equal(gen, gen2) and np.array_equal(x, x2)
+    return (rank, bool(ok and same), dict(x=rel(x, ref_x), logits=rel(logits, ref_logits[:, rank * lv:(rank + 1) * lv]),
+                                          token_diffs=len(diff), graph_equals_direct=bool(same)))
+
+
+CASES = [
+    (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4, vocab_size=1024, seq_len=96),
+     "bf16", 12, 40, 5, False),
+    (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=4, vocab_size=1024, seq_len=200),
+     "nvfp4", 9, 150, 4, True),
+    (dict(dim=1024, hidden_dim=2816, n_layers=2, n_heads=8, vocab_size=4096, seq_len=128),
+     "nvfp4", 64, 100, 3, False),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=["bf16-gqa", "nvfp4-graph", "nvfp4-batch64"])
+def test_sharded_decoder_matches_unsharded(case):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] for r in results), results
+    assert all(p.exitcode == 0 for p in procs)

@@ -129,3 +129,42 @@ def test_oracle_matches_loop_restatement():
     want = np.array(_loop_step(c, W, 7, pos, kl, vl))
     assert np.allclose(got, want, rtol=1e-9, atol=1e-9)
     assert np.allclose(kc[1][0], np.array(kl[1]), rtol=0, atol=0)  # appended keys agree
+
+
+@pytest.mark.parametrize("cfg,world", [
+    (dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, vocab_size=32000, seq_len=2048), 8),
+    (dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, vocab_size=32000, seq_len=2048), 2),
+    (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4, vocab_size=1024, seq_len=64), 4),
+])
+def test_shard_rows_partition_every_weight(ce, cfg, world):
+    """Every rank's rows of every sharded weight, concatenated in rank order,
+    are each global row exactly once; QKV rows are q, k, v of the rank's
+    heads; the w1|w3 pairs stay whole."""
+    c = ce.llama_config(**cfg)
+    hs = c.dim // c.n_heads
+    kvd = hs * c.n_kv_heads
+    total = {ce.LLAMA_WQKV: c.dim + 2 * kvd, ce.LLAMA_WO: c.dim, ce.LLAMA_W13: 2 * c.hidden_dim,
+             ce.LLAMA_W2: c.dim, ce.LLAMA_WCLS: c.vocab_size}
+    for which, n in total.items():
+        parts = [ce.llama_shard_rows(c, r, world, which) for r in range(world)]
+        allr = np.concatenate(parts)
+        assert sorted(allr.tolist()) == list(range(n))
+        if which == ce.LLAMA_W13:
+            assert all(len(p) % 2 == 0 and p[0] % 2 == 0 for p in parts)
+    q = ce.llama_shard_rows(c, 1, world, ce.LLAMA_WQKV)
+    lq, lkv = c.dim // world, kvd // world
+    assert q[0] == lq and q[lq] == c.dim + lkv and q[lq + lkv] == c.dim + kvd + lkv
+
+
+@pytest.mark.parametrize("change,world,pattern", [
+    (dict(n_heads=4), 8, "heads"),
+    (dict(hidden_dim=40), 2, "hidden_dim / world"),
+    (dict(vocab_size=1004), 8, "vocab_size / world"),
+])
+def test_validate_shard_rejects_uneven_splits(ce, change, world, pattern):
+    cfg = dict(dim=1024, hidden_dim=2048, n_layers=2, n_heads=8, vocab_size=32000, seq_len=64)
+    cfg.update(change)
+    c = ce.llama_config(**cfg)
+    rc = ce.lib().ce_llama_validate_shard(ctypes.byref(c), 8, 4, ce.PREC_BF16, 0, world)
+    assert rc == ce.ERR_USAGE
+    assert pattern in ce.last_error()[1]
