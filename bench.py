@@ -44,7 +44,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decoder", action="store_true", help="skip the decoder tokens/s section")
     ap.add_argument("--no-precisions", action="store_true", help="skip the per-precision GEMM section")
-    ap.add_argument("--no-llama", action="store_true", help="skip the Llama-2 decode section")
+    ap.add_argument("--no-llama", action="store_true", help="skip the Llama-2 110M decode section")
+    ap.add_argument("--no-llama7b", action="store_true", help="skip the row-sharded 7B decode section")
     ap.add_argument("--profile", action="store_true",
                     help="setup, warm-up and the timed steps only (for ncu captures); no JSON line")
     return ap.parse_args()
@@ -194,7 +195,7 @@ def llama_decode(ce, dev, stream, s, dist, world, hbm_gbs, batch=256, kv_fill=51
     kv_fill - 1): one direct step, one captured step graph, then the graph
     replayed `tokens` times from a fresh start, between CUDA events. Every rank
     decodes its own batch (replicas); tokens/s is summed over ranks."""
-    import numpy as np
+    import torch
     cfg = LLAMA_110M
     m = ce.Llama(cfg, batch, tokens, stream=s)
     m.init_random(seed=1, weight_std=0.02, kv_fill=kv_fill, stream=s)
@@ -238,6 +239,94 @@ def llama_decode(ce, dev, stream, s, dist, world, hbm_gbs, batch=256, kv_fill=51
                          "bytes_per_step": (kv_bytes + w_bytes) / tokens,
                          "note": "KV cache read (K and V, positions 0..pos, every layer and head) plus "
                                  "every weight once per step"}}
+
+
+LLAMA_7B = dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, vocab_size=32000, seq_len=2048)
+
+
+def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=1024, tokens=32):
+    """Greedy decode of `tokens` tokens for world * per_gpu sequences of the
+    7B-shaped Llama-2 with NVFP4 weights (random N(0, 0.02), quantized on the
+    device), KV cache N(0, 1) to position kv_fill - 1 of 2048. At world > 1
+    the model is row-sharded over the ranks (every rank holds 1/world of each
+    weight's rows and of the KV heads, for all sequences; NCCL all-gathers
+    join the slices, four per layer and one for the classifier's top-1): the
+    batch grows with the ranks, so the per-rank KV and GEMM work stay fixed
+    (weak scaling). One direct step, one captured step graph (collectives
+    included), then the graph replayed `tokens` times from a fresh start
+    between CUDA events; the time is the max over ranks."""
+    import torch
+    cfg = LLAMA_7B
+    batch = per_gpu * world
+    t_setup = time.time()
+    if world == 1:
+        sh = None
+        m = ce.Llama(cfg, batch, tokens, precision=ce.PREC_NVFP4_E2M1, stream=stream.cuda_stream)
+        step = m.step
+    else:
+        import importlib
+        rs = importlib.import_module("cuda_elastic_b200.rowshard")
+        with torch.cuda.stream(stream):
+            sh = rs.ShardedLlama(ce, cfg, batch, tokens, ce.PREC_NVFP4_E2M1)
+        m = sh.model
+        step = sh.step
+    start_tokens = np.random.default_rng(0).integers(0, cfg["vocab_size"], batch).astype(np.int32)
+    with torch.cuda.stream(stream):
+        m.init_random(seed=1, weight_std=0.02, kv_fill=kv_fill)
+        m.start(start_tokens, kv_fill)
+        step()
+    torch.cuda.synchronize(dev)
+    ce.llama_status()
+    setup_s = time.time() - t_setup
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        m.start(start_tokens, kv_fill)
+    torch.cuda.synchronize(dev)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(tokens):
+            g.replay()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ce.llama_status()
+    ms = e0.elapsed_time(e1)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    del g  # the graph holds NCCL calls: released before the process group
+    if sh is not None:
+        sh.close()
+    else:
+        m.close()
+    hs = cfg["dim"] // cfg["n_heads"]
+    L, D, Hd, V = cfg["n_layers"], cfg["dim"], cfg["hidden_dim"], cfg["vocab_size"]
+    # per rank: its KV heads of every sequence, its rows of every weight
+    # (NVFP4: half a byte per value plus one UE4M3 scale per 16 values)
+    kv_bytes = sum(2 * L * batch * (cfg["n_heads"] // world) * (kv_fill + k + 1) * hs * 2 for k in range(tokens))
+    w_bytes = tokens * 0.5625 * (L * (3 * D * D + D * D + 3 * Hd * D) + V * D) / world
+    achieved = (kv_bytes + w_bytes) / (ms * 1e-3) / 1e9
+    return {"workload": f"Llama-2 7B shape (dim 4096, 32 layers, 32 heads, SwiGLU 11008, vocab 32000, "
+                        f"seq_len 2048), NVFP4 weights from N(0,0.02), fp16 activations, KV cache N(0,1) "
+                        f"to position {kv_fill - 1}, batch {batch} ({per_gpu} per GPU), {tokens} greedy "
+                        f"tokens, one captured step graph replayed",
+            "tokens_per_s": batch * tokens / (ms * 1e-3), "ms_per_step": ms / tokens,
+            "n_gpus": world, "batch": batch, "setup_s": setup_s,
+            "parallelism": f"row-sharded tp{world} (NCCL all-gather, 4 per layer + 1)" if world > 1
+                           else "single GPU",
+            "scaling": "weak",
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
+                         "frac": achieved / hbm_gbs,
+                         "bytes_per_step": (kv_bytes + w_bytes) / tokens,
+                         "note": "per rank: KV cache read of its heads (K and V, positions 0..pos, every "
+                                 "layer) plus its rows of every NVFP4 weight once per step"}}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -445,6 +534,11 @@ def run_ours(args, rank, world, local_rank):
     if not args.no_llama:
         llama = llama_decode(ce, dev, stream, s, dist, world, peaks()[0].get("hbm_gbs", 6650.0))
 
+    # ---- Llama-2 7B decode: row-sharded over the ranks ----
+    llama7b = {}
+    if not args.no_llama7b:
+        llama7b = llama7b_decode(ce, dev, stream, dist, world, peaks()[0].get("hbm_gbs", 6650.0))
+
     pk, pk_kind = peaks()
     long_region = total_ms > 1000.0
     peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
@@ -488,6 +582,7 @@ def run_ours(args, rank, world, local_rank):
                                     "4 greedy steps, width 16384, vocab 8192 (4096 tokens per invocation)",
                         **decoder},
             "llama_decode": llama,
+            "llama7b_decode": llama7b,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "clocks": clocks,
