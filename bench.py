@@ -48,6 +48,11 @@ def parse():
     ap.add_argument("--no-llama7b", action="store_true", help="skip the row-sharded 7B decode section")
     ap.add_argument("--profile", action="store_true",
                     help="setup, warm-up and the timed steps only (for ncu captures); no JSON line")
+    ap.add_argument("--profile-llama", choices=["110m", "7b"],
+                    help="decoder steps for ncu only (no JSON line): setup, one warm step, then --steps "
+                         "direct steps between cudaProfilerStart/Stop (use ncu --profile-from-start off)")
+    ap.add_argument("--llama-layers", type=int, default=0,
+                    help="with --profile-llama: layers of the model (0 = the configuration's own)")
     return ap.parse_args()
 
 
@@ -596,11 +601,45 @@ def run_ours(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def profile_llama(args):
+    """--profile-llama: one GPU, the 110M (bf16, batch 256, cache to 511) or 7B
+    (NVFP4, batch 64, cache to 1023) decoder, optionally with fewer layers so
+    that an ncu capture holds a few GB; the profiled region is --steps direct
+    steps."""
+    import torch
+    import __graft_entry__
+    ce = __graft_entry__.load_package()
+    torch.cuda.set_device(0)
+    if args.profile_llama == "110m":
+        cfg, batch, fill, prec = dict(LLAMA_110M), 256, 512, ce.PREC_BF16
+    else:
+        cfg, batch, fill, prec = dict(LLAMA_7B), 64, 1024, ce.PREC_NVFP4_E2M1
+    if args.llama_layers > 0:
+        cfg["n_layers"] = args.llama_layers
+    m = ce.Llama(cfg, batch, args.steps + 1, precision=prec)
+    m.init_random(seed=1, weight_std=0.02, kv_fill=fill)
+    m.start(np.random.default_rng(0).integers(0, cfg["vocab_size"], batch).astype(np.int32), fill)
+    m.step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.start()
+    for _ in range(args.steps):
+        m.step()
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ce.llama_status()
+    m.close()
+    print(f"profile-llama {args.profile_llama}: {cfg['n_layers']} layers, batch {batch}, "
+          f"{args.steps} steps done", flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.profile_llama:
+        profile_llama(args)
+        return
     if args.impl == "reference":
         run_reference(args, rank)
         return

@@ -19,8 +19,9 @@
 // the w1|w3 GEMM, whose epilogue writes the w2 operand directly. The KV
 // cache is bf16 [layer][batch][kv_head][seq_len][head_size]: the keys of one
 // (sequence, head) are one contiguous run that bulk copies move into shared
-// memory. Decode attention streams each (sequence, head) through one CTA with
-// an online softmax (attn_decode_kernel). The current position and step live
+// memory. Decode attention streams each (sequence, head), or a balanced
+// share of its positions, through one single-warp CTA with an online softmax
+// (attn_decode_kernel). The current position and step live
 // in device memory, advanced by the last launch of the step, so one captured
 // step graph replays for every token.
 //
@@ -72,10 +73,11 @@ using rowops::block_max;
 using rowops::block_sum;
 
 constexpr int kRowThreads = 256;
-constexpr int kAttnThreads = 128;
-constexpr int kChunkBytes = 8192;   // K bytes of one attention chunk (V the same)
-constexpr int kAttnStages = 2;      // chunks of K and V in flight per attention CTA
-constexpr long long kAttnWantPerSm = 6;  // attention CTAs per SM below which chunks split
+constexpr int kAttnChunk = 32;  // positions of one attention chunk: one per lane
+// chunks of K and V in flight per attention CTA (one warp); measured on the
+// 110M and 7B shapes: 2 beats 3, 4 and 6 (more resident CTAs per SM hide
+// more latency than a deeper ring per CTA)
+constexpr int attn_stages(int) { return 2; }
 
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -291,184 +293,207 @@ __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc, uint3
       : "memory");
 }
 
+__device__ __forceinline__ float bf16_lo(uint32_t x) { return __uint_as_float(x << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t x) { return __uint_as_float(x & 0xFFFF0000u); }
+
+// o[0 .. VPL) += w * the VPL bf16 values at v (8- or 4-byte aligned)
+template <int VPL>
+__device__ __forceinline__ void attn_accumulate(float *o, const uint16_t *v, float w) {
+  if constexpr (VPL == 4) {
+    const uint2 x = *reinterpret_cast<const uint2 *>(v);
+    o[0] += w * bf16_lo(x.x), o[1] += w * bf16_hi(x.x), o[2] += w * bf16_lo(x.y), o[3] += w * bf16_hi(x.y);
+  } else {
+    const uint32_t x = *reinterpret_cast<const uint32_t *>(v);
+    o[0] += w * bf16_lo(x), o[1] += w * bf16_hi(x);
+  }
+}
+
 // Decode attention of one (sequence, head), or of one of `splits` balanced
-// ranges of its position chunks: the CTA streams its chunks of K and V rows
-// through a 2-stage ring of bulk copies (separate K and V barriers, so the
-// scores of a chunk run while its V rows land) and keeps an online softmax:
-// running max m, sum l and unnormalized output o, rescaled by e^(m_old -
-// m_new) per chunk, s = q . k_t / sqrt(hs). With one split the CTA writes
-// att = bf16(o / l) itself; with several, each writes its (m, l, o) to part
-// and the last of the (sequence, head)'s CTAs to arrive (an arrival counter
-// that it resets) merges them in split order.
+// ranges of its position chunks, by one warp: the warp streams its chunks of
+// 32 K and V rows through a ring of attn_stages(HS) bulk copies (separate K
+// and V barriers, so the scores of a chunk run while its V rows land) and
+// keeps an online softmax: running max m, per-lane sums and the
+// unnormalized output o, rescaled by e^(m_old - m_new) per chunk, s = q . k_t
+// / sqrt(hs). Lane t scores position t of the chunk: its K row is read in
+// 16-byte pieces rotated by the lane (lanes of one shared-memory phase hit 8
+// different bank groups) against q held in registers in the same rotation.
+// For the output each lane owns hs / 32 consecutive dimensions of every V
+// row (coalesced) with the chunk's weights broadcast from shared memory. No
+// block barrier anywhere: small CTAs, many per SM, hide each other's
+// latencies. With one split the CTA writes att = bf16(o / l) itself; with
+// several, each writes its (m, l, o) to part and the last of the (sequence,
+// head)'s CTAs to arrive (an arrival counter that it resets) merges them in
+// split order.
 template <int HS>
-__global__ void __launch_bounds__(kAttnThreads)
+__global__ void __launch_bounds__(32)
 attn_decode_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const uint16_t *vcache,
-                   const int *pos_ptr, int n_heads, int kv_heads, int seq_len, int chunk, int splits,
+                   const int *pos_ptr, int n_heads, int kv_heads, int seq_len, int splits,
                    float *part, int *arrivals, uint16_t *att, int dim, int f16) {
-  constexpr int kPairs = HS / 2;                   // bf16 pairs per row
-  constexpr int kGroups = kAttnThreads / kPairs;   // position groups of the output pass
-  constexpr int kRowVec = HS * 2 / 16;             // 16-byte pieces per K row
+  constexpr int ST = attn_stages(HS);
+  constexpr int R = HS / 8;                        // 16-byte pieces per K row
+  constexpr int VPL = HS / 32;                     // output dimensions per lane
+  constexpr size_t kStage = (size_t)kAttnChunk * HS;  // elements of one K (or V) chunk
+  static_assert(VPL == 2 || VPL == 4, "head size 64 or 128");
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bar[kAttnStages][2];  // [stage][K, V]
-  __shared__ int is_last;
-  const size_t stage_elems = (size_t)chunk * HS;
-  uint16_t *ring = reinterpret_cast<uint16_t *>(smem);  // [stage][K | V][chunk][HS]
-  float *ps = reinterpret_cast<float *>(ring + 2 * kAttnStages * stage_elems);  // [chunk]
-  float *qs = ps + chunk;                                          // [HS]
-  float *red = qs + HS;                                            // [2 * threads] + 32
+  __shared__ __align__(8) uint64_t bar[ST][2];      // [stage][K, V]
+  uint16_t *ring = reinterpret_cast<uint16_t *>(smem);               // [stage][K | V][32][HS]
+  float *es = reinterpret_cast<float *>(ring + 2 * ST * kStage);      // [32] weights of a chunk
 
   pdl_launch_dependents();
   pdl_wait();
-  const int sp = blockIdx.x, h = blockIdx.y, b = blockIdx.z, tid = threadIdx.x;
+  const int sp = blockIdx.x, h = blockIdx.y, b = blockIdx.z, lane = threadIdx.x;
   const int bh = b * n_heads + h;
   const int n = *pos_ptr + 1;
   const bool valid = n >= 1 && n <= seq_len;
-  const int nch = valid ? (n + chunk - 1) / chunk : 0;
+  const int nch = valid ? (n + kAttnChunk - 1) / kAttnChunk : 0;
   const int c0 = (int)((long long)sp * nch / splits), c1 = (int)((long long)(sp + 1) * nch / splits);
   const int kh = h / (n_heads / kv_heads);
   const size_t base = ((size_t)b * kv_heads + kh) * seq_len * HS;
 
-  if (tid == 0) {
-    for (int st = 0; st < kAttnStages; ++st) {
+  if (lane == 0) {
+    for (int st = 0; st < ST; ++st) {
       mbar_init(&bar[st][0], 1);
       mbar_init(&bar[st][1], 1);
     }
     fence_barrier_init();
   }
-  __syncthreads();
-  auto issue = [&](int c, int st) {  // thread 0: K and V rows of chunk c into stage st
-    const int t0 = c * chunk;
-    const uint32_t bytes = (uint32_t)min(chunk, n - t0) * HS * 2;
-    uint16_t *kd = ring + (size_t)st * 2 * stage_elems;
+  __syncwarp();
+  auto issue = [&](int c, int st) {  // lane 0: K and V rows of chunk c into stage st
+    const int t0 = c * kAttnChunk;
+    const uint32_t bytes = (uint32_t)min(kAttnChunk, n - t0) * HS * 2;
+    uint16_t *kd = ring + (size_t)st * 2 * kStage;
     mbar_arrive_expect_tx(&bar[st][0], bytes);
     bulk_g2s(kd, kcache + base + (size_t)t0 * HS, bytes, &bar[st][0]);
     mbar_arrive_expect_tx(&bar[st][1], bytes);
-    bulk_g2s(kd + stage_elems, vcache + base + (size_t)t0 * HS, bytes, &bar[st][1]);
+    bulk_g2s(kd + kStage, vcache + base + (size_t)t0 * HS, bytes, &bar[st][1]);
   };
-  if (tid == 0)
-    for (int c = c0; c < c1 && c < c0 + kAttnStages; ++c) issue(c, c - c0);
-  const float qscale = rsqrtf((float)HS);
-  for (int d = tid; d < HS; d += kAttnThreads) qs[d] = qkv[(size_t)b * ld_qkv + h * HS + d] * qscale;
+  if (lane == 0)
+    for (int c = c0; c < c1 && c < c0 + ST; ++c) issue(c, c - c0);
 
-  const int lane = tid & 31, p = tid % kPairs, g = tid / kPairs;
-  float m = -INFINITY, l = 0.f, o0 = 0.f, o1 = 0.f;
+  // q / sqrt(hs) in registers, piece jj holding q[8j .. 8j+7] for the piece
+  // j = (jj + lane) mod R that this lane reads of its K row at step jj
+  const float qscale = rsqrtf((float)HS);
+  const float *qg = qkv + (size_t)b * ld_qkv + (size_t)h * HS;
+  float qr[R][8];
+#pragma unroll
+  for (int jj = 0; jj < R; ++jj) {
+    const int j = (jj + lane) & (R - 1);
+    const float4 x0 = *reinterpret_cast<const float4 *>(qg + j * 8);
+    const float4 x1 = *reinterpret_cast<const float4 *>(qg + j * 8 + 4);
+    qr[jj][0] = x0.x * qscale, qr[jj][1] = x0.y * qscale, qr[jj][2] = x0.z * qscale, qr[jj][3] = x0.w * qscale;
+    qr[jj][4] = x1.x * qscale, qr[jj][5] = x1.y * qscale, qr[jj][6] = x1.z * qscale, qr[jj][7] = x1.w * qscale;
+  }
+
+  float m = -INFINITY, lsum = 0.f, o[VPL];
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) o[v] = 0.f;
   bool ok = valid;
   int c = c0;
   for (; ok && c < c1; ++c) {
-    const int i = c - c0, st = i % kAttnStages;
-    const uint32_t parity = (uint32_t)(i / kAttnStages) & 1u;
-    const int cnt = min(chunk, n - c * chunk);
-    const uint16_t *ks = ring + (size_t)st * 2 * stage_elems, *vs = ks + stage_elems;
-    if (!__syncthreads_and(mbar_wait(&bar[st][0], parity, &g_llama_status, 901u))) {
+    const int i = c - c0, st = i % ST;
+    const uint32_t parity = (uint32_t)(i / ST) & 1u;
+    const int cnt = min(kAttnChunk, n - c * kAttnChunk);
+    const uint16_t *ks = ring + (size_t)st * 2 * kStage, *vs = ks + kStage;
+    if (!warp_wait(&bar[st][0], parity, &g_llama_status, 901u)) {
       ok = false;
       break;
     }
-    float cmax = -INFINITY;
-    for (int t = tid; t < cnt; t += kAttnThreads) {
-      const uint4 *kr = reinterpret_cast<const uint4 *>(ks + (size_t)t * HS);
-      float sc = 0.f;
+    float sc = -INFINITY;
+    if (lane < cnt) {
+      const uint4 *kr = reinterpret_cast<const uint4 *>(ks + (size_t)lane * HS);
+      float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-      for (int jj = 0; jj < kRowVec; ++jj) {
-        const int j = (jj + lane) % kRowVec;  // rotated: 8 lanes of a phase hit 8 bank groups
-        const uint4 kv = kr[j];
-        const float *q = qs + j * 8;
-        sc += q[0] * __uint_as_float(kv.x << 16) + q[1] * __uint_as_float(kv.x & 0xFFFF0000u);
-        sc += q[2] * __uint_as_float(kv.y << 16) + q[3] * __uint_as_float(kv.y & 0xFFFF0000u);
-        sc += q[4] * __uint_as_float(kv.z << 16) + q[5] * __uint_as_float(kv.z & 0xFFFF0000u);
-        sc += q[6] * __uint_as_float(kv.w << 16) + q[7] * __uint_as_float(kv.w & 0xFFFF0000u);
+      for (int jj = 0; jj < R; ++jj) {
+        const uint4 kv = kr[(jj + lane) & (R - 1)];
+        a0 += qr[jj][0] * bf16_lo(kv.x) + qr[jj][1] * bf16_hi(kv.x);
+        a1 += qr[jj][2] * bf16_lo(kv.y) + qr[jj][3] * bf16_hi(kv.y);
+        a0 += qr[jj][4] * bf16_lo(kv.z) + qr[jj][5] * bf16_hi(kv.z);
+        a1 += qr[jj][6] * bf16_lo(kv.w) + qr[jj][7] * bf16_hi(kv.w);
       }
-      ps[t] = sc;
-      cmax = fmaxf(cmax, sc);
+      sc = a0 + a1;
     }
-    cmax = block_max(cmax, red + 2 * kAttnThreads);
+    float cmax = sc;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) cmax = fmaxf(cmax, __shfl_xor_sync(0xffffffffu, cmax, off));
     const float m_new = fmaxf(m, cmax);
     const float rescale = expf(m - m_new);  // 0 for the first chunk (m = -inf)
-    float csum = 0.f;
-    for (int t = tid; t < cnt; t += kAttnThreads) {
-      const float e = expf(ps[t] - m_new);
-      ps[t] = e;
-      csum += e;
-    }
-    csum = block_sum(csum, red + 2 * kAttnThreads);  // its trailing barrier publishes ps
-    l = l * rescale + csum;
+    const float e = lane < cnt ? expf(sc - m_new) : 0.f;
+    lsum = lsum * rescale + e;
     m = m_new;
-    if (!__syncthreads_and(mbar_wait(&bar[st][1], parity, &g_llama_status, 902u))) {
+    es[lane] = e;
+    __syncwarp();
+    if (!warp_wait(&bar[st][1], parity, &g_llama_status, 902u)) {
       ok = false;
       break;
     }
-    o0 *= rescale;
-    o1 *= rescale;
-    for (int t = g; t < cnt; t += kGroups) {
-      const uint32_t vv = *reinterpret_cast<const uint32_t *>(vs + (size_t)t * HS + 2 * p);
-      const float w = ps[t];
-      o0 += w * __uint_as_float(vv << 16);
-      o1 += w * __uint_as_float(vv & 0xFFFF0000u);
+#pragma unroll
+    for (int v = 0; v < VPL; ++v) o[v] *= rescale;
+    const uint16_t *vr = vs + lane * VPL;
+    if (cnt == kAttnChunk) {
+#pragma unroll 8
+      for (int t = 0; t < kAttnChunk; ++t) attn_accumulate<VPL>(o, vr + (size_t)t * HS, es[t]);
+    } else {
+      for (int t = 0; t < cnt; ++t) attn_accumulate<VPL>(o, vr + (size_t)t * HS, es[t]);
     }
-    __syncthreads();  // stage st and ps are free
-    if (tid == 0 && c + kAttnStages < c1) issue(c + kAttnStages, st);
+    __syncwarp();  // stage st and es are free
+    if (lane == 0 && c + ST < c1) issue(c + ST, st);
   }
   if (!ok) {
     // a staging wait gave up: let this CTA's copies still in flight land
     // (bounded waits) before it exits, and leave NaN outputs
-    for (int cc = c; cc < c1 && cc < c + kAttnStages; ++cc) {
+    for (int cc = c; cc < c1 && cc < c + ST; ++cc) {
       const int i = cc - c0;
-      mbar_wait(&bar[i % kAttnStages][0], (uint32_t)(i / kAttnStages) & 1u, &g_llama_status, 903u);
-      mbar_wait(&bar[i % kAttnStages][1], (uint32_t)(i / kAttnStages) & 1u, &g_llama_status, 903u);
+      mbar_wait(&bar[i % ST][0], (uint32_t)(i / ST) & 1u, &g_llama_status, 903u);
+      mbar_wait(&bar[i % ST][1], (uint32_t)(i / ST) & 1u, &g_llama_status, 903u);
     }
     m = NAN;
   }
-  // outputs of the groups summed per pair
-  red[2 * tid] = o0;
-  red[2 * tid + 1] = o1;
-  __syncthreads();
-  float a0 = 0.f, a1 = 0.f;
-  if (tid < kPairs) {
 #pragma unroll
-    for (int gg = 0; gg < kGroups; ++gg) {
-      a0 += red[2 * (gg * kPairs + tid)];
-      a1 += red[2 * (gg * kPairs + tid) + 1];
-    }
-  }
+  for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, off);
   if (splits == 1) {
-    if (tid < kPairs) {
-      const float inv = (ok && l > 0.f) ? 1.0f / l : NAN;
-      *reinterpret_cast<uint32_t *>(att + (size_t)b * dim + h * HS + 2 * tid) = pack_operand(a0 * inv, a1 * inv, f16);
+    const float inv = (ok && lsum > 0.f) ? 1.0f / lsum : NAN;
+    uint16_t *dst = att + (size_t)b * dim + (size_t)h * HS + lane * VPL;
+    if constexpr (VPL == 4) {
+      uint2 w;
+      w.x = pack_operand(o[0] * inv, o[1] * inv, f16);
+      w.y = pack_operand(o[2] * inv, o[3] * inv, f16);
+      *reinterpret_cast<uint2 *>(dst) = w;
+    } else {
+      *reinterpret_cast<uint32_t *>(dst) = pack_operand(o[0] * inv, o[1] * inv, f16);
     }
     return;
   }
   float *out = part + ((size_t)bh * splits + sp) * (HS + 2);
-  if (tid < kPairs) {
-    out[2 + 2 * tid] = a0;
-    out[3 + 2 * tid] = a1;
-  }
-  if (tid == 0) {
+#pragma unroll
+  for (int v = 0; v < VPL; ++v) out[2 + lane * VPL + v] = o[v];
+  if (lane == 0) {
     out[0] = (c1 > c0 || !ok) ? m : -INFINITY;
-    out[1] = l;
+    out[1] = lsum;
   }
-  __syncthreads();  // this CTA's partial is written
-  if (tid == 0) {
-    __threadfence();
+  __threadfence();
+  __syncwarp();  // this CTA's partial is written
+  int last = 0;
+  if (lane == 0) {
     const int before = atomicAdd(&arrivals[bh], 1);
-    is_last = before == splits - 1;
-    if (is_last) arrivals[bh] = 0;
+    last = before == splits - 1;
+    if (last) arrivals[bh] = 0;
   }
-  __syncthreads();
-  if (!is_last) return;
+  if (!__shfl_sync(0xffffffffu, last, 0)) return;
   __threadfence();
   const float *pp = part + (size_t)bh * splits * (HS + 2);
-  for (int d = tid; d < HS; d += kAttnThreads) {
+  for (int d = lane; d < HS; d += 32) {
     float M = -INFINITY;
     for (int k = 0; k < splits; ++k) M = fmaxf(M, __ldcg(pp + k * (HS + 2)));
-    float L = 0.f, o = 0.f;
+    float L = 0.f, acc = 0.f;
     for (int k = 0; k < splits; ++k) {
       const float mk = __ldcg(pp + k * (HS + 2));
       if (mk == -INFINITY) continue;
       const float f = expf(mk - M);
       L += __ldcg(pp + k * (HS + 2) + 1) * f;
-      o += __ldcg(pp + k * (HS + 2) + 2 + d) * f;
+      acc += __ldcg(pp + k * (HS + 2) + 2 + d) * f;
     }
-    const uint32_t r = pack_operand(o / L, 0.f, f16);
-    att[(size_t)b * dim + h * HS + d] = (uint16_t)(r & 0xFFFFu);
+    const uint32_t r = pack_operand(acc / L, 0.f, f16);
+    att[(size_t)b * dim + (size_t)h * HS + d] = (uint16_t)(r & 0xFFFFu);
   }
 }
 
@@ -642,14 +667,10 @@ int launch_rows(int nv, F &&f) {
   return CE_OK;
 }
 
-// K bytes of one attention chunk: 128 positions of head size 64, 64 of 128
-// (measured best: smaller chunks pay their barriers too often, larger ones
-// cost occupancy).
-constexpr int attn_chunk_bytes(int hs) { return hs == 128 ? 16384 : kChunkBytes; }
-
-size_t attn_smem_bytes(int chunk, int hs) {
-  return (size_t)chunk * hs * 2 * 2 * kAttnStages + (size_t)chunk * 4 + (size_t)hs * 4 +
-         (2 * kAttnThreads + 32) * 4;
+// Dynamic shared memory of one attention CTA: its ring of K and V chunks and
+// the chunk's weights.
+constexpr size_t attn_smem_bytes(int hs) {
+  return (size_t)attn_stages(hs) * 2 * kAttnChunk * hs * 2 + kAttnChunk * 4;
 }
 
 // Opts the attention kernels into their dynamic shared memory, once per device.
@@ -659,11 +680,35 @@ int configure_attention() {
   CE_CUDA_TRY(cudaGetDevice(&dev));
   if (dev >= 0 && dev < 64 && done[dev]) return CE_OK;
   CE_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)attn_smem_bytes(attn_chunk_bytes(64) / 128, 64)));
+                                   (int)attn_smem_bytes(64)));
   CE_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)attn_smem_bytes(attn_chunk_bytes(128) / 256, 128)));
+                                   (int)attn_smem_bytes(128)));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return CE_OK;
+}
+
+// Splits of each (sequence, head)'s positions among attention CTAs: the
+// count whose CTAs fill the resident slots' last wave best (every CTA costs
+// the same, the positions being common to all sequences), each split keeping
+// at least 8 chunks of the full cache; a little is charged per split for the
+// merge.
+int attn_choose_splits(int hs, long long pairs, int seq_len) {
+  int per_sm = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+          &per_sm, hs == 64 ? attn_decode_kernel<64> : attn_decode_kernel<128>, 32, attn_smem_bytes(hs)) !=
+          cudaSuccess ||
+      per_sm < 1)
+    per_sm = 1;
+  const double slots = (double)per_sm * sm_count();
+  const int max_splits = std::max(1, std::min(16, (seq_len + kAttnChunk - 1) / kAttnChunk / 8));
+  int best = 1;
+  double best_score = -1.0;
+  for (int sp = 1; sp <= max_splits; ++sp) {
+    const double x = (double)pairs * sp / slots;
+    const double score = x / std::ceil(x) - 0.01 * (sp - 1);
+    if (score > best_score + 1e-9) best = sp, best_score = score;
+  }
+  return best;
 }
 
 int pow2_at_least(int v) {
@@ -697,7 +742,7 @@ struct ce_llama {
   uint16_t *x_att = nullptr, *x_hb = nullptr;
   float *x_delta = nullptr;
   float2 *x_top = nullptr;
-  int hs = 0, kv_dim = 0, qkv_rows = 0, chunk = 0, nchunk = 0, nv = 0;
+  int hs = 0, kv_dim = 0, qkv_rows = 0, nv = 0;
   int sp_qkv = 1, sp_o = 1, sp_13 = 1, sp_2 = 1;  // split-K counts of the layer GEMMs
   bool pdl = true;  // programmatic dependent launch between the step's kernels
   int attn_splits = 1;  // CTAs per (sequence, head) in the attention
@@ -885,17 +930,8 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
   m->lV = cfg->vocab_size / world;
   m->kv_dim = m->hs * m->lKH;  // this shard's k (and v) rows
   m->qkv_rows = m->lD + 2 * m->kv_dim;
-  m->chunk = attn_chunk_bytes(m->hs) / (m->hs * 2);
-  m->nchunk = (cfg->seq_len + m->chunk - 1) / m->chunk;
   m->nv = pow2_at_least((cfg->dim / 4 + kRowThreads - 1) / kRowThreads);
-  {
-    // enough attention CTAs for about two waves of 3 per SM, never more
-    // splits than chunks of the full cache
-    const long long pairs = (long long)batch * m->lH;
-    const long long want = kAttnWantPerSm * sm_count();
-    long long sp = (want + pairs - 1) / pairs;
-    m->attn_splits = (int)std::max(1LL, std::min<long long>(sp, m->nchunk));
-  }
+  m->attn_splits = attn_choose_splits(m->hs, (long long)batch * m->lH, cfg->seq_len);
   m->layer_kv = (size_t)batch * m->lKH * cfg->seq_len * m->hs;
   // split-K for the GEMMs whose tiles alone leave SMs idle at decode sizes;
   // at least 4 k-blocks (256 of K) per split
@@ -1151,7 +1187,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     });
     return rc ? rc : lrc;
   };
-  const size_t attn_smem = attn_smem_bytes(m->chunk, m->hs);
+  const size_t attn_smem = attn_smem_bytes(m->hs);
   for (int l = 0; l < c.n_layers; ++l) {
     int rc = norm(l == 0 ? nullptr : m->delta, m->sp_2, l == 0 ? m->tok_emb : nullptr,
                   m->rms_att + (size_t)l * D);
@@ -1167,10 +1203,10 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     const dim3 agrid(m->attn_splits, c.n_heads, B);
     auto attention = [&](auto hs_tag) {
       constexpr int HS = decltype(hs_tag)::value;
-      return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(kAttnThreads), attn_smem, s, pdl,
+      return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(32), attn_smem, s, pdl,
                            "attn_decode_kernel", (const float *)m->qkv, m->qkv_rows,
                            (const uint16_t *)kc, (const uint16_t *)vc, (const int *)m->pos, c.n_heads,
-                           c.n_kv_heads, c.seq_len, m->chunk, m->attn_splits, m->part, m->arrivals,
+                           c.n_kv_heads, c.seq_len, m->attn_splits, m->part, m->arrivals,
                            m->att, D, (int)w4);
     };
     rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{}) : attention(std::integral_constant<int, 128>{});
@@ -1283,13 +1319,13 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
                          lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
       if (rc) return rc;
       const dim3 agrid(m->attn_splits, m->lH, B);
-      const size_t smem = attn_smem_bytes(m->chunk, m->hs);
+      const size_t smem = attn_smem_bytes(m->hs);
       uint16_t *slot = m->x_att + (size_t)r * slot_d;
       auto attention = [&](auto hs_tag) {
         constexpr int HS = decltype(hs_tag)::value;
-        return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(kAttnThreads), smem, s, pdl,
+        return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(32), smem, s, pdl,
                              "attn_decode_kernel", (const float *)m->qkv, m->qkv_rows, (const uint16_t *)kc,
-                             (const uint16_t *)vc, (const int *)m->pos, m->lH, m->lKH, c.seq_len, m->chunk,
+                             (const uint16_t *)vc, (const int *)m->pos, m->lH, m->lKH, c.seq_len,
                              m->attn_splits, m->part, m->arrivals, slot, lD, (int)w4);
       };
       return m->hs == 64 ? attention(std::integral_constant<int, 64>{})
