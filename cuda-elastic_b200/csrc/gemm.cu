@@ -1140,6 +1140,410 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   return set_error(CE_ERR_USAGE, format("unsupported tile width %d", c.bn));
 }
 
+
+// ---------------------------------------------------------------------------
+// W4A16 GEMM, decode form (gemm_w4t): d[b][n] = alpha * sum_k x[b][k] w[n][k]
+// with the NVFP4 weights as the M operand of the MMA, expanded straight into
+// tensor memory. At decode sizes the batch is small, so the weights are the
+// 128-row operand and the batch is the N dimension (no padded rows); the
+// expanded fp16 weights go registers -> TMEM (tcgen05.st) -> tensor core
+// (the A operand of tcgen05.mma may live in TMEM), so shared memory only
+// carries the packed weights and the activation tiles. One stage covers 128
+// of K for a tile of TR weight rows (one or two M=128 halves).
+//   warp 0     weight producer: one bulk copy of the stage's codes (TR x 64
+//              bytes) and one of its scales (TR x 8 bytes), in the packed
+//              layout of w4t_pack; weights are constant, so this starts
+//              before the programmatic-launch wait;
+//   warp 1     TMEM allocator and MMA issuer (kind::f16, A from TMEM);
+//   warp 2     activation producer: two TMA boxes of 64 x NB per stage;
+//   warps 4-7  epilogue (TMEM lane quarter = warp % 4): alpha x accumulator,
+//              split-K partials or the SwiGLU product;
+//   warps 8-15 converters, two per lane quarter: cvt.rn.f16x2.e2m1x2 and a
+//              half2 multiply by the UE4M3 scale, then tcgen05.st of 32
+//              columns (64 values of one row) per piece.
+// The activation slot and the TMEM stage of a stage are freed together by
+// one tcgen05.commit.
+constexpr int kW4tThreads = 16 * 32;
+constexpr int kW4tMaxStages = 4;   // activation slots = TMEM weight stages
+constexpr int kW4tMaxWStages = 8;  // packed weight stages in shared memory
+constexpr int kW4tSmemBudget = 232448 - 1024;
+
+struct W4tArgs {
+  float *d;
+  uint16_t *swiglu_out;  // fp16 SwiGLU product [M][ld_out], or nullptr
+  const uint8_t *codes;  // [KB][Npad/32][4][32][16]
+  const uint8_t *scales; // [KB][Npad/32][32][8]
+  const float *alpha;
+  int M, N, K, ldd, ld_out;
+  int npad;              // packed rows (multiple of 256)
+  int kb_total;          // 128-wide k blocks
+  int nb;                // batch columns per tile (multiple of 16)
+  int tiles_n, tiles_b, splits;
+  long long split_stride;
+  int stages, w_stages;
+  int act_stage_bytes;   // 2 x nb x 128
+  int acc_cols;          // TMEM columns before the weight stages
+};
+
+struct W4tUnit {
+  int tile_n, tile_b, kb0, kb1;
+  float *d;
+};
+
+__device__ __forceinline__ W4tUnit w4t_unit(const W4tArgs &a, int u) {
+  W4tUnit w;
+  w.tile_b = u % a.tiles_b;
+  const int rest = u / a.tiles_b;
+  const int split = rest % a.splits;
+  w.tile_n = rest / a.splits;
+  w.kb0 = (int)((long long)split * a.kb_total / a.splits);
+  w.kb1 = (int)((long long)(split + 1) * a.kb_total / a.splits);
+  w.d = a.d != nullptr ? a.d + (size_t)split * a.split_stride : nullptr;
+  return w;
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]),
+        "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+        "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+        "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+        "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// D(tmem) (+)= A(tmem) x B(smem desc)^T, kind::f16, one instruction.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+template <int TR>
+__global__ void __launch_bounds__(kW4tThreads, 1)
+gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
+  constexpr int kHalves = TR / 128;
+  constexpr int kCodeBytes = TR * 64;              // 128 codes per row
+  constexpr int kStageBytes = kCodeBytes + TR * 8; // + 8 scales per row
+  constexpr int kStageCols = kHalves * 64;         // TMEM columns of a stage's weights
+  constexpr int kPieces = kHalves * 2;             // (half, 64-wide k chunk) pieces per stage
+  const int S = args.stages, SW = args.w_stages, NB = args.nb;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t *act = smem;                                         // [S][2][NB][128]
+  uint8_t *wring = smem + (size_t)S * args.act_stage_bytes;    // [SW][codes | scales]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(wring + (size_t)SW * kStageBytes);
+  uint64_t *wfull = bars, *wempty = bars + kW4tMaxWStages;
+  uint64_t *afull = wempty + kW4tMaxWStages, *tready = afull + kW4tMaxStages;
+  uint64_t *sempty = tready + kW4tMaxStages;
+  uint64_t *accfull = sempty + kW4tMaxStages, *accempty = accfull + 1, *drain = accempty + 1;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+
+  DeviceStatus *st = &g_gemm_status;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_units = args.tiles_n * args.tiles_b * args.splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < SW; ++s) {
+      mbar_init(&wfull[s], 1);
+      mbar_init(&wempty[s], 8);
+    }
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&afull[s], 1);
+      mbar_init(&tready[s], 8);
+      mbar_init(&sempty[s], 1);
+    }
+    mbar_init(accfull, 1);
+    mbar_init(accempty, 4);
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- weight producer (constant data: no launch wait)
+    int ws = 0;
+    uint32_t wph = 0, issued_mask = 0, issued_parity = 0;
+    bool okay = true;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
+      const W4tUnit w = w4t_unit(args, t);
+      const size_t row0 = (size_t)w.tile_n * TR;
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&wempty[ws], wph ^ 1u, st, 61)) {
+          okay = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t *dst = wring + (size_t)ws * kStageBytes;
+          const size_t rows = (size_t)kb * args.npad + row0;
+          mbar_arrive_expect_tx(&wfull[ws], kStageBytes);
+          bulk_g2s_gemm(dst, args.codes + rows * 64, kCodeBytes, &wfull[ws]);
+          bulk_g2s_gemm(dst + kCodeBytes, args.scales + rows * 8, TR * 8, &wfull[ws]);
+        }
+        __syncwarp();
+        issued_mask |= 1u << ws;
+        issued_parity = (issued_parity & ~(1u << ws)) | (wph << ws);
+        if (++ws == SW) {
+          ws = 0;
+          wph ^= 1u;
+        }
+      }
+    }
+    for (int s = 0; s < SW; ++s)
+      if (issued_mask & (1u << s)) warp_wait(&wfull[s], (issued_parity >> s) & 1u, st, 62);
+  } else if (warp == 2) {
+    // ---------------- activation producer
+    pdl_wait();
+    int as = 0;
+    uint32_t aph = 0, issued_mask = 0, issued_parity = 0;
+    bool okay = true;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
+      const W4tUnit w = w4t_unit(args, t);
+      const int b0 = w.tile_b * NB;
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&sempty[as], aph ^ 1u, st, 63)) {
+          okay = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t *dst = act + (size_t)as * args.act_stage_bytes;
+          mbar_arrive_expect_tx(&afull[as], (uint32_t)args.act_stage_bytes);
+          tma_load_2d(dst, &tmA, &afull[as], kb * 128, b0);
+          tma_load_2d(dst + args.act_stage_bytes / 2, &tmA, &afull[as], kb * 128 + 64, b0);
+        }
+        __syncwarp();
+        issued_mask |= 1u << as;
+        issued_parity = (issued_parity & ~(1u << as)) | (aph << as);
+        if (++as == S) {
+          as = 0;
+          aph ^= 1u;
+        }
+      }
+    }
+    for (int s = 0; s < S; ++s)
+      if (issued_mask & (1u << s)) warp_wait(&afull[s], (issued_parity >> s) & 1u, st, 64);
+  } else if (warp >= 8) {
+    // ---------------- converters: E2M1 x UE4M3 -> fp16 pairs -> TMEM
+    const int quarter = warp & 3, pair = (warp - 8) >> 2;
+    int ws = 0, ts = 0;
+    uint32_t wph = 0, tph = 0;
+    bool okay = true;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
+      const W4tUnit w = w4t_unit(args, t);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&wfull[ws], wph, st, 65) || !warp_wait(&sempty[ts], tph ^ 1u, st, 66)) {
+          okay = false;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t *wsm = wring + (size_t)ws * kStageBytes;
+        uint4 cq[kPieces / 2][2];
+        uint32_t sq[kPieces / 2];
+#pragma unroll
+        for (int i = 0; i < kPieces / 2; ++i) {
+          const int p = pair + 2 * i, h = p >> 1, c = p & 1;
+          const int g = h * 4 + quarter;  // 32-row group of the tile
+          const uint4 *src = reinterpret_cast<const uint4 *>(wsm + (size_t)(g * 4 + c * 2) * 512) + lane;
+          cq[i][0] = src[0];
+          cq[i][1] = src[32];
+          sq[i] = *reinterpret_cast<const uint32_t *>(wsm + kCodeBytes + (size_t)(g * 32 + lane) * 8 + c * 4);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&wempty[ws]);
+#pragma unroll
+        for (int i = 0; i < kPieces / 2; ++i) {
+          const int p = pair + 2 * i, h = p >> 1, c = p & 1;
+          uint32_t r[32];
+          const uint32_t words[8] = {cq[i][0].x, cq[i][0].y, cq[i][0].z, cq[i][0].w,
+                                     cq[i][1].x, cq[i][1].y, cq[i][1].z, cq[i][1].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {  // 16 values (8 bytes of codes) per scale
+            const uint32_t sc = ue4m3_to_f16x2((sq[i] >> (8 * q)) & 0xFFu);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t byte = (words[q * 2 + j / 4] >> (8 * (j & 3))) & 0xFFu;
+              const uint32_t v = e2m1x2_to_f16x2(byte);
+              asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[q * 8 + j]) : "r"(v), "r"(sc));
+            }
+          }
+          const uint32_t col = (uint32_t)args.acc_cols + (uint32_t)ts * kStageCols + h * 64 + c * 32;
+          tmem_st_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + col, r);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tready[ts]);
+        if (++ws == SW) {
+          ws = 0;
+          wph ^= 1u;
+        }
+        if (++ts == S) {
+          ts = 0;
+          tph ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    const uint32_t idesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    int s = 0;
+    uint32_t ph = 0;
+    bool okay = true;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x, ++local) {
+      if (!warp_wait(accempty, (uint32_t)(local & 1) ^ 1u, st, 67)) break;
+      tc_fence_after();
+      const W4tUnit w = w4t_unit(args, t);
+      for (int kb = w.kb0; kb < w.kb1; ++kb) {
+        if (!warp_wait(&afull[s], ph, st, 68) || !warp_wait(&tready[s], ph, st, 69)) {
+          okay = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a_addr = smem_u32(act + (size_t)s * args.act_stage_bytes);
+          const uint32_t t_col = (uint32_t)args.acc_cols + (uint32_t)s * kStageCols;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint64_t b_desc = smem_desc_sw128(a_addr + (uint32_t)c * (args.act_stage_bytes / 2) + k * 32);
+#pragma unroll
+              for (int h = 0; h < kHalves; ++h)
+                tc_mma_ts(tmem_base + (uint32_t)(h * NB), tmem_base + t_col + h * 64 + c * 32 + k * 8, b_desc,
+                          idesc, (kb > w.kb0 || c > 0 || k > 0) ? 1u : 0u);
+            }
+          tc_commit(&sempty[s]);
+        }
+        __syncwarp();
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (okay && lane == 0) tc_commit(accfull);
+      __syncwarp();
+    }
+    if (lane == 0) tc_commit(drain);
+    __syncwarp();
+    warp_wait(drain, 0, st, 70);
+  } else if (warp >= 4 && warp <= 7) {
+    // ---------------- epilogue
+    pdl_wait();
+    const int quarter = warp & 3;
+    const float alpha = args.alpha != nullptr ? *args.alpha : 1.0f;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_units; t += gridDim.x, ++local) {
+      if (!warp_wait(accfull, (uint32_t)(local & 1), st, 71)) break;
+      tc_fence_after();
+      const W4tUnit w = w4t_unit(args, t);
+      const int b0 = w.tile_b * NB;
+#pragma unroll
+      for (int h = 0; h < kHalves; ++h) {
+        const int n = w.tile_n * TR + h * 128 + quarter * 32 + lane;
+        for (int c0 = 0; c0 < NB; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * NB + c0), r);
+          tmem_ld_wait();
+          if (args.swiglu_out != nullptr) {
+            // rows (2i, 2i+1) = (g_i, u_i) sit in adjacent lanes
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float v = __uint_as_float(r[j]) * alpha;
+              const float u = __shfl_xor_sync(0xffffffffu, v, 1);
+              const int b = b0 + c0 + j;
+              if ((lane & 1) == 0 && n < args.N && b < args.M && c0 + j < NB) {
+                const __half hv = __float2half_rn(v / (1.0f + expf(-v)) * u);
+                args.swiglu_out[(size_t)b * args.ld_out + n / 2] = *reinterpret_cast<const uint16_t *>(&hv);
+              }
+            }
+          } else if (n < args.N) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int b = b0 + c0 + j;
+              if (b < args.M && c0 + j < NB) w.d[(size_t)b * args.ldd + n] = __uint_as_float(r[j]) * alpha;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(accempty);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Packs NVFP4 weights (codes [N][ld_bytes] two per byte, even index in the
+// low nibble; UE4M3 scales [N][nsf], one per 16 values) into the layout of
+// gemm_w4t_kernel: per 128-wide k block and 32-row group, the codes as four
+// 16-byte columns of 32 rows ([KB][npad/32][4][32][16]) and the scales as 32
+// rows of 8 bytes ([KB][npad/32][32][8]); rows past N and k past K are zero.
+// Output row n takes source row map[n] when map is given.
+__global__ void w4t_pack_kernel(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales,
+                                int N, int K, int ld_bytes, int nsf, int npad, int kb_total, const int *map) {
+  const size_t total = (size_t)kb_total * npad * 4;  // one thread per 16-byte code piece
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+    const int r = (int)(i % 32);
+    const int j = (int)((i / 32) % 4);
+    const size_t gk = i / 128;                 // kb * (npad / 32) + group
+    const int g = (int)(gk % (npad / 32));
+    const int kb = (int)(gk / (npad / 32));
+    const int n = g * 32 + r;
+    const int src_row = n < N ? (map != nullptr ? map[n] : n) : -1;
+    const int byte0 = kb * 64 + j * 16;        // code bytes of the piece in the source row
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (src_row >= 0 && byte0 + 16 <= K / 2) {
+      const uint8_t *p = codes + (size_t)src_row * ld_bytes + byte0;
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        w[q] = (uint32_t)p[4 * q] | ((uint32_t)p[4 * q + 1] << 8) | ((uint32_t)p[4 * q + 2] << 16) |
+               ((uint32_t)p[4 * q + 3] << 24);
+      v = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    reinterpret_cast<uint4 *>(codes_t)[i] = v;
+    if (j == 0) {
+      uint32_t lo = 0, hi = 0;
+      if (src_row >= 0) {
+        const uint8_t *q = scales + (size_t)src_row * nsf + kb * 8;
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t b = kb * 8 + e < K / 16 ? q[e] : 0u;
+          if (e < 4) lo |= b << (8 * e);
+          else hi |= b << (8 * (e - 4));
+        }
+      }
+      reinterpret_cast<uint2 *>(scales_t)[gk * 32 + r] = make_uint2(lo, hi);
+    }
+  }
+}
+
 }  // namespace
 
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
@@ -1282,6 +1686,8 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
 #define CE_W4_LAUNCH(W)                                                                          \
   case W:                                                                                        \
     w.a_stages = SmemW4<W>::a_stages(w.a_slot);                                                  \
+    if (w.a_stages < 2 || SmemW4<W>::total(w.a_slot) > kW4SmemBudget)                            \
+      return set_error(CE_ERR_USAGE, format("W4A16 tile width %d does not fit shared memory", W)); \
     rc = configure_smem<gemm_w4a16_kernel<W>>(kW4SmemBudget);                                    \
     if (rc) return rc;                                                                           \
     return launch_kernel(gemm_w4a16_kernel<W>, dim3(grid), dim3(kW4Threads), SmemW4<W>::total(w.a_slot), s, \
@@ -1327,6 +1733,142 @@ int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uin
   w4_pack_kernel<<<blocks, 256, 0, s>>>(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf, row_map);
   CE_LAUNCH_CHECK("w4_pack_kernel");
   return CE_OK;
+}
+
+// Tile plan of gemm_w4t for a batch of M rows: 256 weight rows per tile
+// (two M=128 halves) while the batch fits 128 TMEM columns, else 128; batch
+// columns per tile (a multiple of 16, at most 256); TMEM weight stages =
+// activation slots (what TMEM and shared memory hold), packed weight stages.
+struct W4tPlan {
+  int tr, nb, tiles_b, stages, w_stages, act_stage, acc_cols;
+  int smem;
+};
+
+W4tPlan w4t_plan(int M) {
+  W4tPlan p{};
+  const int m16 = (M + 15) / 16 * 16;
+  p.tr = m16 <= 128 ? 256 : 128;
+  p.nb = m16 <= 256 ? m16 : 256;
+  p.tiles_b = (M + p.nb - 1) / p.nb;
+  const int halves = p.tr / 128;
+  p.acc_cols = (halves * p.nb + 63) / 64 * 64;
+  int tstages = ((int)kTmemCols - p.acc_cols) / (halves * 64);
+  if (tstages > kW4tMaxStages) tstages = kW4tMaxStages;
+  p.act_stage = 2 * p.nb * kRowBytes;
+  const int w_stage = p.tr * 72, fixed = 2048;  // barriers + alignment slack
+  int S = tstages;
+  while (S > 2 && S * p.act_stage + 3 * w_stage + fixed > kW4tSmemBudget) --S;
+  p.stages = S;
+  int SW = (kW4tSmemBudget - S * p.act_stage - fixed) / w_stage;
+  p.w_stages = SW > kW4tMaxWStages ? kW4tMaxWStages : SW;
+  p.smem = S * p.act_stage + p.w_stages * w_stage + fixed;
+  return p;
+}
+
+// Split count for gemm_w4t: units of (weight tile, batch tile, k range) are
+// spread over the SMs; a unit costs its 128-wide k blocks plus about three
+// blocks of fill and epilogue.
+int gemm_w4t_auto_splits(int M, int N, int K, int max_splits) {
+  const int sms = sm_count();
+  if (sms <= 0) return 1;
+  const W4tPlan p = w4t_plan(M);
+  const long long kb = (K + 127) / 128;
+  const long long tiles = (long long)((N + p.tr - 1) / p.tr) * p.tiles_b;
+  int best = 1;
+  long long best_cost = -1;
+  for (int sp = 1; sp <= max_splits && sp <= kb; ++sp) {
+    const long long units = tiles * sp;
+    const long long cost = ((units + sms - 1) / sms) * ((kb + sp - 1) / sp + 3);
+    if (best_cost < 0 || cost < best_cost) best = sp, best_cost = cost;
+  }
+  return best;
+}
+
+// Bytes of the packed NVFP4 weights of gemm_w4t (codes, scales) for N x K.
+void w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes) {
+  const size_t kb = (size_t)(K + 127) / 128, npad = (size_t)(N + 255) / 256 * 256;
+  if (codes_bytes) *codes_bytes = kb * npad * 64;
+  if (scales_bytes) *scales_bytes = kb * npad * 8;
+}
+
+int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
+             int ld_bytes, int nsf, cudaStream_t s, const int *row_map) {
+  CE_REQUIRE(codes_t && scales_t && codes && scales, "null argument");
+  CE_REQUIRE(N >= 1 && K >= 64 && K % 64 == 0 && ld_bytes * 2 >= K && nsf * 16 >= K,
+             "bad NVFP4 weight shape %dx%d (ld_bytes %d, scales per row %d)", N, K, ld_bytes, nsf);
+  CE_REQUIRE((reinterpret_cast<uintptr_t>(codes_t) & 15u) == 0 && (reinterpret_cast<uintptr_t>(scales_t) & 7u) == 0,
+             "packed buffers must be 16-byte (codes) and 8-byte (scales) aligned");
+  const int kb_total = (K + 127) / 128, npad = (N + 255) / 256 * 256;
+  const size_t pieces = (size_t)kb_total * npad * 4;
+  int blocks = (int)((pieces + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  w4t_pack_kernel<<<blocks, 256, 0, s>>>(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf, npad, kb_total,
+                                         row_map);
+  CE_LAUNCH_CHECK("w4t_pack_kernel");
+  return CE_OK;
+}
+
+// W4A16 GEMM, decode form (gemm_w4t_kernel): d = alpha x A W^T with A fp16
+// [M][lda] and W packed by w4t_pack; split s of `splits` k ranges writes
+// d + s * split_stride; with swiglu_out the rows of W interleave w1 and w3
+// and the fp16 SwiGLU product goes to swiglu_out [M][swiglu_ld] instead.
+int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
+             int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
+             int swiglu_ld, cudaStream_t s, bool pdl) {
+  CE_REQUIRE(M >= 1 && N >= 1 && K >= 64 && K % 64 == 0, "W4A16 GEMM dims (M=%d N=%d K=%d; K %% 64 == 0)", M, N,
+             K);
+  CE_REQUIRE(lda >= K && (lda * 2) % 16 == 0, "lda must be >= K and a multiple of 8 (got %d)", lda);
+  CE_REQUIRE(a && codes_t && scales_t && (d || swiglu_out), "null operand");
+  CE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(codes_t) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(scales_t) & 15u) == 0,
+             "operands must be 16-byte aligned");
+  const int kb_total = (K + 127) / 128;
+  CE_REQUIRE(splits >= 1 && splits <= kb_total, "split count must be in [1, %d] (got %d)", kb_total, splits);
+  CE_REQUIRE(swiglu_out == nullptr || (splits == 1 && N % 2 == 0 && swiglu_ld >= N / 2),
+             "the SwiGLU epilogue needs one split, an even N and ld_out >= N / 2");
+  CE_REQUIRE(swiglu_out != nullptr || ldd >= N, "ldd must be >= N");
+  if (!is_sm100()) return set_error(CE_ERR_USAGE, "tcgen05 GEMM needs an sm_100 device");
+  const W4tPlan p = w4t_plan(M);
+  if (p.stages < 2 || p.w_stages < 2 || p.smem > kW4tSmemBudget)
+    return set_error(CE_ERR_USAGE, format("W4A16 plan for M=%d does not fit shared memory", M));
+  CUtensorMap ta;
+  int rc = make_operand_map(&ta, a, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, K, M, lda, p.nb);
+  if (rc) return rc;
+  W4tArgs w{};
+  w.d = d;
+  w.swiglu_out = swiglu_out;
+  w.codes = codes_t;
+  w.scales = scales_t;
+  w.alpha = alpha;
+  w.M = M;
+  w.N = N;
+  w.K = K;
+  w.ldd = ldd;
+  w.ld_out = swiglu_ld;
+  w.npad = (N + 255) / 256 * 256;
+  w.kb_total = kb_total;
+  w.nb = p.nb;
+  w.tiles_n = (N + p.tr - 1) / p.tr;
+  w.tiles_b = p.tiles_b;
+  w.splits = splits;
+  w.split_stride = splits > 1 ? split_stride : 0;
+  w.stages = p.stages;
+  w.w_stages = p.w_stages;
+  w.act_stage_bytes = p.act_stage;
+  w.acc_cols = p.acc_cols;
+  const int sms = sm_count();
+  const int units = w.tiles_n * w.tiles_b * splits;
+  const int grid = units < sms ? units : sms;
+  if (p.tr == 256) {
+    rc = configure_smem<gemm_w4t_kernel<256>>(kW4tSmemBudget);
+    if (rc) return rc;
+    return launch_kernel(gemm_w4t_kernel<256>, dim3(grid), dim3(kW4tThreads), (size_t)p.smem, s, pdl,
+                         "gemm_w4t_kernel", ta, w);
+  }
+  rc = configure_smem<gemm_w4t_kernel<128>>(kW4tSmemBudget);
+  if (rc) return rc;
+  return launch_kernel(gemm_w4t_kernel<128>, dim3(grid), dim3(kW4tThreads), (size_t)p.smem, s, pdl,
+                       "gemm_w4t_kernel", ta, w);
 }
 
 int gemm_set_prefetch(int kblocks) {

@@ -60,6 +60,13 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
                const float *alpha, int M, int N, int K, int lda, int ldd, int splits,
                long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
 int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
+int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
+             int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
+             int swiglu_ld, cudaStream_t s, bool pdl);
+int gemm_w4t_auto_splits(int M, int N, int K, int max_splits);
+void w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes);
+int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
+             int ld_bytes, int nsf, cudaStream_t s, const int *row_map);
 int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
             int ld_bytes, int nsf, cudaStream_t s, const int *row_map = nullptr);
 int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
@@ -242,21 +249,25 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
   }
 }
 
-// RoPE on q and k of one sequence (in place in the fp32 QKV rows), then k
-// and v to the bf16 cache at the current position. rope holds (cos, sin) of
-// pos * 10000^(-2i/hs) for every position and pair index i.
-__global__ void rope_append_kernel(float *qkv, int ld_qkv, int nsplit, size_t split_stride,
-                                   uint16_t *kcache, uint16_t *vcache, const float2 *rope,
-                                   const int *pos_ptr, int dim, int kv_dim, int hs, int kv_heads,
-                                   int seq_len) {
+// RoPE on q and k (in place in the fp32 QKV rows), then k and v to the bf16
+// cache at the current position: one thread per (sequence, pair), the q
+// pairs of a row first, then its k/v pairs; grid (pair blocks, batch). rope
+// holds (cos, sin) of pos * 10000^(-2i/hs) for every position and pair index i.
+__global__ void __launch_bounds__(256)
+rope_append_kernel(float *qkv, int ld_qkv, int nsplit, size_t split_stride, uint16_t *kcache,
+                   uint16_t *vcache, const float2 *rope, const int *pos_ptr, int dim, int kv_dim, int hs,
+                   int kv_heads, int seq_len) {
   pdl_launch_dependents();
   pdl_wait();
-  const int b = blockIdx.x;
+  const int b = blockIdx.y;
+  const int p = blockIdx.x * blockDim.x + threadIdx.x;
   const int pos = *pos_ptr;
   if (pos < 0 || pos >= seq_len) {
     if (threadIdx.x == 0) report_timeout(&g_llama_status, 900u);  // position out of the cache
     return;
   }
+  const int qpairs = dim / 2;
+  if (p >= qpairs + kv_dim / 2) return;
   float *row = qkv + (size_t)b * ld_qkv;
   // pair i of the QKV row: its split-K partials summed in split order
   auto pair_at = [&](int i) {
@@ -268,22 +279,20 @@ __global__ void rope_append_kernel(float *qkv, int ld_qkv, int nsplit, size_t sp
     return v;
   };
   const float2 *rp = rope + (size_t)pos * (hs / 2);
-  for (int p = threadIdx.x; p < dim / 2; p += blockDim.x) {
+  if (p < qpairs) {
     const int i = 2 * p;
     const float2 cs = rp[(i % hs) / 2];
     const float2 q = pair_at(i);
-    row[i] = q.x * cs.x - q.y * cs.y;  // rotated q, read by the attention from partial 0
-    row[i + 1] = q.x * cs.y + q.y * cs.x;
+    // rotated q, read by the attention from partial 0
+    *reinterpret_cast<float2 *>(row + i) = make_float2(q.x * cs.x - q.y * cs.y, q.x * cs.y + q.y * cs.x);
+    return;
   }
-  const size_t per_head = (size_t)seq_len * hs;
-  for (int p = threadIdx.x; p < kv_dim / 2; p += blockDim.x) {
-    const int i = 2 * p, kh = i / hs, d = i % hs;
-    const float2 cs = rp[d / 2];
-    const float2 k = pair_at(dim + i), v = pair_at(dim + kv_dim + i);
-    const size_t at = ((size_t)b * kv_heads + kh) * per_head + (size_t)pos * hs + d;
-    *reinterpret_cast<uint32_t *>(kcache + at) = pack_bf16x2(k.x * cs.x - k.y * cs.y, k.x * cs.y + k.y * cs.x);
-    *reinterpret_cast<uint32_t *>(vcache + at) = pack_bf16x2(v.x, v.y);
-  }
+  const int i = 2 * (p - qpairs), kh = i / hs, d = i % hs;
+  const float2 cs = rp[d / 2];
+  const float2 k = pair_at(dim + i), v = pair_at(dim + kv_dim + i);
+  const size_t at = ((size_t)b * kv_heads + kh) * seq_len * hs + (size_t)pos * hs + d;
+  *reinterpret_cast<uint32_t *>(kcache + at) = pack_bf16x2(k.x * cs.x - k.y * cs.y, k.x * cs.y + k.y * cs.x);
+  *reinterpret_cast<uint32_t *>(vcache + at) = pack_bf16x2(v.x, v.y);
 }
 
 __device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gsrc, uint32_t bytes, uint64_t *bar) {
@@ -667,6 +676,12 @@ int launch_rows(int nv, F &&f) {
   return CE_OK;
 }
 
+// Grid of rope_append_kernel: blocks of 256 (sequence, pair) threads over the
+// dim / 2 q pairs and kv_dim / 2 k/v pairs of each of the batch rows.
+dim3 rope_grid(int dim, int kv_dim, int batch) {
+  return dim3((unsigned)((dim / 2 + kv_dim / 2 + 255) / 256), (unsigned)batch);
+}
+
 // Dynamic shared memory of one attention CTA: its ring of K and V chunks and
 // the chunk's weights.
 constexpr size_t attn_smem_bytes(int hs) {
@@ -722,10 +737,11 @@ int pow2_at_least(int v) {
 
 using namespace ce;
 
-// One NVFP4 weight matrix in the W4A16 GEMM's layout.
+// One NVFP4 weight matrix in the decode-form W4A16 GEMM's layout (w4t_pack).
 struct QMat {
-  uint8_t *codes;   // [cols/64][rows][32]
-  uint8_t *scales;  // [cols/64][rows][4]
+  uint8_t *codes;   // [ceil(cols/128)][roundup(rows, 256)/32][4][32][16]
+  uint8_t *scales;  // [ceil(cols/128)][roundup(rows, 256)/32][32][8]
+  size_t codes_bytes, scales_bytes;
   float *alpha;     // (encode, decode) tensor scales; the GEMM uses alpha[1]
   int rows, cols;
 };
@@ -935,11 +951,14 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
   m->layer_kv = (size_t)batch * m->lKH * cfg->seq_len * m->hs;
   // split-K for the GEMMs whose tiles alone leave SMs idle at decode sizes;
   // at least 4 k-blocks (256 of K) per split
-  auto splits = precision == CE_PREC_NVFP4_E2M1 ? gemm_w4a16_auto_splits : gemm_bf16_auto_splits;
-  m->sp_qkv = splits(batch, m->qkv_rows, cfg->dim, 8, 4);
-  m->sp_o = splits(batch, m->lD, cfg->dim, 8, 4);
-  m->sp_13 = splits(batch, 2 * m->lHd, cfg->dim, 8, 4);
-  m->sp_2 = splits(batch, m->lD, cfg->hidden_dim, 8, 4);
+  auto splits = [&](int N, int K) {
+    return precision == CE_PREC_NVFP4_E2M1 ? gemm_w4t_auto_splits(batch, N, K, 8)
+                                           : gemm_bf16_auto_splits(batch, N, K, 8, 4);
+  };
+  m->sp_qkv = splits(m->qkv_rows, cfg->dim);
+  m->sp_o = splits(m->lD, cfg->dim);
+  m->sp_13 = splits(2 * m->lHd, cfg->dim);
+  m->sp_2 = splits(m->lD, cfg->hidden_dim);
   const int sp_delta = m->sp_o > m->sp_2 ? m->sp_o : m->sp_2;
   const ce_llama_config &c = *cfg;
   const size_t L = c.n_layers;
@@ -960,8 +979,10 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
     for (int i = 0; i < nmat; ++i) {
       int r, q;
       mat_shape(m, i == 4 * c.n_layers ? 4 : i % 4, &r, &q);
-      codes += (size_t)r * q / 2;
-      scales += (size_t)r * q / 16;
+      size_t cb = 0, sb = 0;
+      w4t_packed_bytes(r, q, &cb, &sb);
+      codes += cb;
+      scales += sb;
     }
     CE_ALLOC(m->q_codes, codes);
     CE_ALLOC(m->q_scales, scales);
@@ -970,11 +991,12 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
     for (int i = 0; i < nmat; ++i) {
       QMat q{};
       mat_shape(m, i == 4 * c.n_layers ? 4 : i % 4, &q.rows, &q.cols);
+      w4t_packed_bytes(q.rows, q.cols, &q.codes_bytes, &q.scales_bytes);
       q.codes = m->q_codes + codes;
       q.scales = m->q_scales + scales;
       q.alpha = m->q_alpha + 2 * i;
-      codes += (size_t)q.rows * q.cols / 2;
-      scales += (size_t)q.rows * q.cols / 16;
+      codes += q.codes_bytes;
+      scales += q.scales_bytes;
       m->qm.push_back(q);
     }
   } else {
@@ -1104,8 +1126,8 @@ int ce_llama_init_random(ce_llama *m, uint64_t seed, float weight_std, int kv_fi
       if (e != cudaSuccess) rc = cuda_error(e, "init_normal_f32_kernel");
       if (rc == CE_OK) rc = quantize_nvfp4(tcodes, tscales, q.alpha, amax, tmp, grows, q.cols, q.cols / 2, s);
       if (rc == CE_OK)
-        rc = w4_pack(q.codes, q.scales, tcodes, tscales, q.rows, q.cols, q.cols / 2, q.cols / 16, s,
-                     d_map + k * most);
+        rc = w4t_pack(q.codes, q.scales, tcodes, tscales, q.rows, q.cols, q.cols / 2, q.cols / 16, s,
+                      d_map + k * most);
     }
     e = cudaStreamSynchronize(s);
     if (rc == CE_OK && e != cudaSuccess) rc = cuda_error(e, "NVFP4 weight set-up");
@@ -1170,8 +1192,8 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     mat_shape(m, k, &N, &K);
     if (w4) {
       const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
-      return gemm_w4a16(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out,
-                        sw_out ? N / 2 : 0, s, pdl);
+      return gemm_w4t(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out,
+                      sw_out ? N / 2 : 0, s, pdl);
     }
     const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
                         : k == 2 ? m->w13 + l * w13_elems(m) : k == 3 ? m->w2 + l * w2_elems(m) : m->wcls;
@@ -1196,7 +1218,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     rc = gemm(0, l, m->qkv, m->xb, m->qkv_rows, m->sp_qkv, (long long)qkv_stride, nullptr);
     if (rc) return rc;
     uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
-    rc = launch_kernel(rope_append_kernel, dim3(B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
+    rc = launch_kernel(rope_append_kernel, rope_grid(D, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
                        m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
                        (const int *)m->pos, D, m->kv_dim, m->hs, c.n_kv_heads, c.seq_len);
     if (rc) return rc;
@@ -1272,8 +1294,8 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
     mat_shape(m, k, &N, &K);
     if (w4) {
       const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
-      return gemm_w4a16(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out, sw_ld, s,
-                        pdl);
+      return gemm_w4t(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out, sw_ld, s,
+                      pdl);
     }
     const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
                         : k == 2 ? m->w13 + l * w13_elems(m) : k == 3 ? m->w2 + l * w2_elems(m) : m->wcls;
@@ -1314,7 +1336,7 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
       rc = gemm(0, l, m->qkv, m->xb, m->qkv_rows, m->sp_qkv, (long long)qkv_stride, nullptr, 0);
       if (rc) return rc;
       uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
-      rc = launch_kernel(rope_append_kernel, dim3(B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
+      rc = launch_kernel(rope_append_kernel, rope_grid(lD, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
                          m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope, (const int *)m->pos,
                          lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
       if (rc) return rc;
@@ -1410,8 +1432,8 @@ int ce_llama_read_nvfp4(ce_llama *m, int which, int layer, uint8_t *codes_host, 
   CE_REQUIRE(k == 4 || (layer >= 0 && layer < m->c.n_layers), "layer %d out of range", layer);
   const QMat &q = m->qm[k == 4 ? 4 * m->c.n_layers : 4 * layer + k];
   CE_CUDA_TRY(cudaDeviceSynchronize());
-  if (codes_host) CE_CUDA_TRY(cudaMemcpy(codes_host, q.codes, (size_t)q.rows * q.cols / 2, cudaMemcpyDeviceToHost));
-  if (scales_host) CE_CUDA_TRY(cudaMemcpy(scales_host, q.scales, (size_t)q.rows * q.cols / 16, cudaMemcpyDeviceToHost));
+  if (codes_host) CE_CUDA_TRY(cudaMemcpy(codes_host, q.codes, q.codes_bytes, cudaMemcpyDeviceToHost));
+  if (scales_host) CE_CUDA_TRY(cudaMemcpy(scales_host, q.scales, q.scales_bytes, cudaMemcpyDeviceToHost));
   if (alpha_host) CE_CUDA_TRY(cudaMemcpy(alpha_host, q.alpha, 8, cudaMemcpyDeviceToHost));
   return CE_OK;
 }

@@ -188,6 +188,32 @@ int ce_gemm_w4a16(float *d_dev, const uint16_t *a_dev, const uint8_t *codes_t_de
                   const uint8_t *scales_t_dev, const float *alpha_dev, int M, int N, int K, int lda,
                   int ldd, ce_stream_t stream);
 
+/* Bytes of the decode-form packed NVFP4 weights (ce_w4t_pack) of an N x K
+ * weight: codes ceil(K/128) * roundup(N, 256) * 64, scales ceil(K/128) *
+ * roundup(N, 256) * 8. Host-only. */
+int ce_w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes);
+
+/* Repacks NVFP4 weights (the ce_quantize_nvfp4 layout, as ce_w4_pack takes
+ * them) into the decode-form layout of ce_gemm_w4t: per 128-wide k block and
+ * 32-row group, codes_t [K/128][N/32][4][32][16] (four 16-byte columns of 32
+ * rows) and scales_t [K/128][N/32][32][8], zero past N (rounded up to 256)
+ * and past K (rounded up to 128). K % 64 == 0. Setup-time. */
+int ce_w4t_pack(uint8_t *codes_t_dev, uint8_t *scales_t_dev, const uint8_t *codes_dev,
+                const uint8_t *scales_dev, int N, int K, int ld_bytes, int nsf, ce_stream_t stream);
+
+/* W4A16 GEMM, decode form: the same product as ce_gemm_w4a16 (D[m][n] =
+ * alpha * sum_k A[m][k] W[n][k], A fp16 [M][lda], fp32 accumulation) with
+ * the weights as the 128-row operand of the tensor cores, expanded to fp16
+ * in tensor memory, and the batch (M) as the narrow operand, for the small
+ * batches of a decode step. W in the ce_w4t_pack layout; K % 64 == 0. Split
+ * s of `splits` (1 <= splits <= ceil(K / 128)) writes its fp32 partial at
+ * d_dev + s * split_stride; the caller sums the partials in split order.
+ * Replaces the NVFP4 classifier GEMM of the reference's low-precision
+ * decoder (decoder_lowprec.cu:111-127), keeping the activations 16-bit. */
+int ce_gemm_w4t(float *d_dev, const uint16_t *a_dev, const uint8_t *codes_t_dev,
+                const uint8_t *scales_t_dev, const float *alpha_dev, int M, int N, int K, int lda,
+                int ldd, int splits, int64_t split_stride, ce_stream_t stream);
+
 /* Library-wide GEMM tuning, set at setup time (not during a capture): the
  * TMA producer prefetches operand tiles this many k-blocks ahead into L2
  * (0 = off, at most 64). */
@@ -543,9 +569,10 @@ int ce_llama_write(ce_llama *model, int which, int layer, const void *host, int6
                    int64_t bytes);
 
 /* NVFP4 model only: host copies of one weight matrix (CE_LLAMA_WQKV, _WO,
- * _W13, _W2 of a layer, or _WCLS) in the W4A16 layout: codes [cols/64][rows][32],
- * scales [cols/64][rows][4], alpha = (encode, decode) tensor scales; the
- * weight is e2m1(code) * ue4m3(scale) * alpha[1]. Any pointer may be NULL. */
+ * _W13, _W2 of a layer, or _WCLS; this shard's rows) in the ce_w4t_pack
+ * layout, buffer sizes from ce_w4t_packed_bytes(rows, cols); alpha =
+ * (encode, decode) tensor scales; the weight is e2m1(code) * ue4m3(scale) *
+ * alpha[1]. Any pointer may be NULL. */
 int ce_llama_read_nvfp4(ce_llama *model, int which, int layer, uint8_t *codes_host,
                         uint8_t *scales_host, float *alpha_host);
 

@@ -198,3 +198,68 @@ def test_w4_pack_layout(ce, O, dev):
     for kb in range(K // 64):
         assert np.array_equal(ct[kb], codes[:, kb * 32:(kb + 1) * 32])
         assert np.array_equal(st[kb], sc[:, kb * 4:(kb + 1) * 4])
+
+
+W4T_SHAPES = [(64, 4096, 1024, 1), (64, 4352, 4096, 4), (9, 2752, 4096, 3), (130, 452, 320, 1),
+              (1, 8, 64, 1), (300, 1000, 1024, 2), (512, 512, 4096, 8), (100, 1000, 1216, 2), (256, 768, 2048, 1)]
+
+
+@pytest.mark.parametrize("shape", W4T_SHAPES)
+def test_gemm_w4t_decode_form(ce, O, dev, shape):
+    """The decode-form W4A16 GEMM (weights the 128-row MMA operand, expanded
+    to fp16 in tensor memory; batch the narrow operand): batches of 1 to 512
+    (one and two 128-row halves per tile, several batch tiles), N not a
+    multiple of 256, K not a multiple of 128, split-K partials summed in
+    split order; against the double GEMM of the fp16 activations and the
+    dequantized weights, times the decode scale."""
+    M, N, K, splits = shape
+    A, B = _operands(O, M, N, K, 7)
+    codes = torch.empty((N, K // 2), dtype=torch.uint8, device=dev)
+    sc = torch.empty((N, K // 16), dtype=torch.uint8, device=dev)
+    ts = torch.empty(2, device=dev)
+    scratch = torch.zeros(1, dtype=torch.int32, device=dev)
+    ce.quantize_nvfp4(codes, sc, ts, scratch, torch.from_numpy(B).to(dev))
+    cb, sb = ce.w4t_packed_bytes(N, K)
+    ct = torch.full((cb,), 0xAB, dtype=torch.uint8, device=dev)
+    st = torch.full((sb,), 0xAB, dtype=torch.uint8, device=dev)
+    ce.w4t_pack(ct, st, codes, sc, N, K)
+    a16 = A.astype(np.float16)
+    da = torch.from_numpy(a16.view(np.int16)).to(dev)
+    d = torch.full((splits, M, N), float("nan"), device=dev)
+    ce.gemm_w4t(d, da, ct, st, ts[1:], splits=splits)
+    ce.device_status()
+    parts = d.cpu().numpy()
+    out = parts[0].astype(np.float32)
+    for s in range(1, splits):
+        out = out + parts[s]
+    a = a16.astype(np.float64)
+    b = _nv_dequant(O, codes.cpu().numpy(), sc.cpu().numpy(), K)
+    _check(O, out, a, b, float(ts.cpu().numpy()[1]))
+
+
+def test_w4t_pack_layout(ce, O, dev):
+    """ce_w4t_pack against a numpy restatement of its layout: per 128-wide k
+    block and 32-row group, four 16-byte code columns of 32 rows, then 32
+    rows of 8 scale bytes; zero past N and past K."""
+    N, K = 40, 320
+    rng = np.random.default_rng(3)
+    codes = rng.integers(0, 256, (N, K // 2), dtype=np.uint8)
+    sc = rng.integers(0, 120, (N, K // 16), dtype=np.uint8)
+    cb, sb = ce.w4t_packed_bytes(N, K)
+    kb, npad = (K + 127) // 128, (N + 255) // 256 * 256
+    assert (cb, sb) == (kb * npad * 64, kb * npad * 8)
+    ct = torch.full((cb,), 0xAB, dtype=torch.uint8, device=dev)
+    st = torch.full((sb,), 0xAB, dtype=torch.uint8, device=dev)
+    ce.w4t_pack(ct, st, torch.from_numpy(codes).to(dev), torch.from_numpy(sc).to(dev), N, K)
+    ct = ct.cpu().numpy().reshape(kb, npad // 32, 4, 32, 16)
+    st = st.cpu().numpy().reshape(kb, npad // 32, 32, 8)
+    cpad = np.zeros((npad, kb * 64), np.uint8)
+    cpad[:N, :K // 2] = codes
+    spad = np.zeros((npad, kb * 8), np.uint8)
+    spad[:N, :K // 16] = sc
+    for k in range(kb):
+        for g in range(npad // 32):
+            rows = slice(g * 32, g * 32 + 32)
+            for j in range(4):
+                assert np.array_equal(ct[k, g, j], cpad[rows, k * 64 + j * 16:k * 64 + j * 16 + 16])
+            assert np.array_equal(st[k, g], spad[rows, k * 8:k * 8 + 8])

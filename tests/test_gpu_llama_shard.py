@@ -1,8 +1,10 @@
 """The Llama-2 decoder step row-sharded over 2 GPUs (one process each, NCCL
 all-gathers between the library's segments) against the same model
-unsharded on one GPU: the residual stream after the last layer and every
-rank's logit slice within relative L2 1e-3 of the unsharded ones, and the
-greedy tokens equal wherever the unsharded logits are not a near tie; bf16
+unsharded on one GPU: every step's logits (the rank slices gathered) within
+relative L2 1e-3 of the unsharded ones on the sequences whose inputs still
+agree, the residual stream after the last layer within 1e-3 on the
+sequences that never diverged, and a greedy token differing only at a near
+tie the logit error can bridge (at most 1 in 20 sequences); bf16
 and NVFP4 weights; a captured step graph (NCCL included) replays bit for bit
 like direct steps. Needs at least 2 visible GPUs; skipped otherwise."""
 import os
@@ -46,6 +48,15 @@ def _worker(rank, world, port, case, q):
         dist.destroy_process_group()
 
 
+def _full_logits(model, dist, world):
+    """The logits of every sequence over the whole vocabulary: the rank
+    slices (classifier rows rank * vocab / world ...) gathered in rank order."""
+    local = torch.from_numpy(np.ascontiguousarray(model.logits())).cuda()
+    parts = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(parts, local)
+    return torch.cat(parts, dim=1).cpu().numpy().astype(np.float64)
+
+
 def _body(rank, world, case, ce, rs, dist):
     cfg, prec_name, batch, fill, steps, graph = case
     prec = {"bf16": ce.PREC_BF16, "nvfp4": ce.PREC_NVFP4_E2M1}[prec_name]
@@ -70,27 +81,28 @@ def _body(rank, world, case, ce, rs, dist):
     ce.llama_status()
     gen = sh.model.generated().copy()
     x = sh.model.read(ce.LLAMA_RESIDUAL, dtype=np.float32)
-    logits = sh.model.logits().astype(np.float64)
-    # direct steps of the same sharded model again: graph and direct agree bitwise
-    sh.model.start(tokens0, fill)
+    # direct steps of the same sharded model again, the logits of every step
+    # gathered: graph and direct agree bitwise
     sh.model.init_random(seed=3, kv_fill=fill)
     sh.model.start(tokens0, fill)
+    sh_logits = []
     for _ in range(steps):
         sh.step()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        sh_logits.append(_full_logits(sh.model, dist, world))
     gen2, x2 = sh.model.generated().copy(), sh.model.read(ce.LLAMA_RESIDUAL, dtype=np.float32)
     sh.close()
     # the unsharded model on this GPU
     m = ce.Llama(cfg, batch, steps, precision=prec)
     m.init_random(seed=3, kv_fill=fill)
     m.start(tokens0, fill)
+    ref_logits = []
     for _ in range(steps):
         m.step()
-    torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        ref_logits.append(m.logits().astype(np.float64))
     ce.llama_status()
     ref_gen, ref_x = m.generated(), m.read(ce.LLAMA_RESIDUAL, dtype=np.float32)
-    lv = cfg["vocab_size"] // world
-    ref_logits = m.logits().astype(np.float64)
     m.close()
     dist.barrier()
 
@@ -98,18 +110,30 @@ def _body(rank, world, case, ce, rs, dist):
         a, b = np.asarray(a, np.float64), np.asarray(b, np.float64)
         return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
 
-    ok = rel(x, ref_x) <= 1e-3 and rel(logits, ref_logits[:, rank * lv:(rank + 1) * lv]) <= 1e-3
-    diff = np.argwhere(gen != ref_gen)
-    # a differing token must come after a step whose top-2 gap the numerical
-    # error can bridge; the last step's logits are checked explicitly
-    err = np.abs(logits - ref_logits[:, rank * lv:(rank + 1) * lv]).max()
-    last = [b for b, s in diff if s == steps - 1]
-    top2 = np.sort(ref_logits, axis=1)[:, -2:]
-    ok = ok and all(top2[b, 1] - top2[b, 0] <= 4 * err for b in last)
-    ok = ok and len(diff) <= max(1, gen.size // 50)
+    # A sequence's inputs agree until the first step whose greedy token
+    # differs; up to and including that step its logits must agree, and the
+    # differing token must be a near tie the logit error can bridge.
+    first = np.full(batch, steps)
+    for b in range(batch):
+        d = np.nonzero(gen2[b] != ref_gen[b])[0]
+        if len(d):
+            first[b] = d[0]
+    worst, ties_ok = 0.0, True
+    for s in range(steps):
+        rows = np.nonzero(first >= s)[0]
+        if len(rows):
+            worst = max(worst, rel(sh_logits[s][rows], ref_logits[s][rows]))
+        for b in np.nonzero(first == s)[0]:
+            err = np.abs(sh_logits[s][b] - ref_logits[s][b]).max()
+            short = ref_logits[s][b][ref_gen[b, s]] - ref_logits[s][b][gen2[b, s]]
+            ties_ok = ties_ok and short <= 4 * err + 1e-6
+    same_rows = np.nonzero(first == steps)[0]
+    xr = rel(x2[same_rows], ref_x[same_rows]) if len(same_rows) else 0.0
+    diverged = int((first < steps).sum())
+    ok = worst <= 1e-3 and xr <= 1e-3 and ties_ok and diverged <= max(1, batch // 20)
     same = np.array_equal(gen, gen2) and np.array_equal(x, x2)
-    return (rank, bool(ok and same), dict(x=rel(x, ref_x), logits=rel(logits, ref_logits[:, rank * lv:(rank + 1) * lv]),
-                                          token_diffs=len(diff), graph_equals_direct=bool(same)))
+    return (rank, bool(ok and same), dict(logits=worst, x=xr, diverged=diverged, ties_ok=bool(ties_ok),
+                                          graph_equals_direct=bool(same)))
 
 
 CASES = [
