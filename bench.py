@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--no-precisions", action="store_true", help="skip the per-precision GEMM section")
     ap.add_argument("--no-llama", action="store_true", help="skip the Llama-2 110M decode section")
     ap.add_argument("--no-llama7b", action="store_true", help="skip the row-sharded 7B decode section")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="join of the row-sharded decoder's slices: the library's peer-memory puts "
+                         "(CUDA IPC over NVLink) or NCCL all-gathers")
     ap.add_argument("--profile", action="store_true",
                     help="setup, warm-up and the timed steps only (for ncu captures); no JSON line")
     ap.add_argument("--profile-llama", choices=["110m", "7b"],
@@ -249,13 +252,14 @@ def llama_decode(ce, dev, stream, s, dist, world, hbm_gbs, batch=256, kv_fill=51
 LLAMA_7B = dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, vocab_size=32000, seq_len=2048)
 
 
-def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=1024, tokens=32):
+def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=1024, tokens=32, exchange="p2p"):
     """Greedy decode of `tokens` tokens for world * per_gpu sequences of the
     7B-shaped Llama-2 with NVFP4 weights (random N(0, 0.02), quantized on the
     device), KV cache N(0, 1) to position kv_fill - 1 of 2048. At world > 1
     the model is row-sharded over the ranks (every rank holds 1/world of each
     weight's rows and of the KV heads, for all sequences; NCCL all-gathers
-    join the slices, four per layer and one for the classifier's top-1): the
+    join the slices, four per layer and one for the classifier's top-1, as
+    the library's peer-memory puts or NCCL all-gathers): the
     batch grows with the ranks, so the per-rank KV and GEMM work stay fixed
     (weak scaling). One direct step, one captured step graph (collectives
     included), then the graph replayed `tokens` times from a fresh start
@@ -272,7 +276,7 @@ def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=10
         import importlib
         rs = importlib.import_module("cuda_elastic_b200.rowshard")
         with torch.cuda.stream(stream):
-            sh = rs.ShardedLlama(ce, cfg, batch, tokens, ce.PREC_NVFP4_E2M1)
+            sh = rs.ShardedLlama(ce, cfg, batch, tokens, ce.PREC_NVFP4_E2M1, mode=exchange)
         m = sh.model
         step = sh.step
     start_tokens = np.random.default_rng(0).integers(0, cfg["vocab_size"], batch).astype(np.int32)
@@ -324,8 +328,8 @@ def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=10
                         f"tokens, one captured step graph replayed",
             "tokens_per_s": batch * tokens / (ms * 1e-3), "ms_per_step": ms / tokens,
             "n_gpus": world, "batch": batch, "setup_s": setup_s,
-            "parallelism": f"row-sharded tp{world} (NCCL all-gather, 4 per layer + 1)" if world > 1
-                           else "single GPU",
+            "parallelism": (f"row-sharded tp{world} ({'peer-memory puts over NVLink' if exchange == 'p2p' else 'NCCL all-gathers'}, "
+                            f"4 per layer + 1)") if world > 1 else "single GPU",
             "scaling": "weak",
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
                          "frac": achieved / hbm_gbs,
@@ -542,7 +546,8 @@ def run_ours(args, rank, world, local_rank):
     # ---- Llama-2 7B decode: row-sharded over the ranks ----
     llama7b = {}
     if not args.no_llama7b:
-        llama7b = llama7b_decode(ce, dev, stream, dist, world, peaks()[0].get("hbm_gbs", 6650.0))
+        llama7b = llama7b_decode(ce, dev, stream, dist, world, peaks()[0].get("hbm_gbs", 6650.0),
+                                 exchange=args.exchange)
 
     pk, pk_kind = peaks()
     long_region = total_ms > 1000.0

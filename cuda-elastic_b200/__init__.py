@@ -126,6 +126,8 @@ _SIGNATURES = {
     "ce_llama_validate_shard": [_vp, _i, _i, _i, _i, _i],
     "ce_llama_create_shard": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _i, _i, _vp],
     "ce_llama_bind_exchange": [_vp, _vp, _vp, _vp, _vp],
+    "ce_llama_exchange_open": [_vp, _vp],
+    "ce_llama_exchange_connect": [_vp, ctypes.c_char_p],
     "ce_llama_enqueue_segment": [_vp, _i, _i, _vp],
     "ce_llama_shard_rows": [_vp, _i, _i, _i, _vp, _vp],
     "ce_llama_read": [_vp, _i, _i, _vp, _i64, _i64],
@@ -553,6 +555,7 @@ LLAMA_TOK_EMB, LLAMA_WQKV, LLAMA_WO, LLAMA_W13, LLAMA_W2 = 0, 1, 2, 3, 4
 LLAMA_RMS_ATT, LLAMA_RMS_FFN, LLAMA_RMS_FINAL, LLAMA_WCLS = 5, 6, 7, 8
 LLAMA_KCACHE, LLAMA_VCACHE, LLAMA_LOGITS, LLAMA_TOKENS = 9, 10, 11, 12
 LLAMA_GENERATED, LLAMA_POS, LLAMA_RESIDUAL = 13, 14, 15
+IPC_HANDLE_BYTES = 64  # CE_IPC_HANDLE_BYTES
 SEG_ATTN, SEG_OPROJ, SEG_FFN_IN, SEG_FFN_OUT, SEG_HEAD, SEG_PICK = 0, 1, 2, 3, 4, 5
 
 
@@ -691,6 +694,18 @@ class Llama:
 
     def bind_exchange(self, att, delta, hb, top):
         check(lib().ce_llama_bind_exchange(self._h, _ptr(att), _ptr(delta), _ptr(hb), _ptr(top)))
+
+    def exchange_open(self):
+        """Allocates this rank's peer-exchange block; returns its CUDA IPC handle (bytes)."""
+        h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(lib().ce_llama_exchange_open(self._h, h))
+        return h.raw
+
+    def exchange_connect(self, handles):
+        """Maps every rank's exchange block (handles: all ranks' handles concatenated in rank order)."""
+        if len(handles) != IPC_HANDLE_BYTES * self.world:
+            raise ValueError("need one IPC handle per rank")
+        check(lib().ce_llama_exchange_connect(self._h, handles))
 
     def weights(self):
         """Every weight as host arrays: bf16 bits (uint16) for a bf16 model,

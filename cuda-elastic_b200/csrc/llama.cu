@@ -40,6 +40,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <type_traits>
 #include <vector>
 
@@ -664,6 +665,86 @@ __global__ void pick_top_kernel(const float2 *top, int shards, int batch, int *t
   if (step >= 0 && step < cap) generated[(size_t)b * cap + step] = idx;
 }
 
+// --- peer-memory exchange of the row-sharded step ---------------------------
+// Each rank's exchange block (CUDA IPC shared) holds, per exchange kind (0
+// attention output, 1 delta, 2 SwiGLU product, 3 classifier candidates), the
+// slots [rank][batch][cols] and a flag per sending rank. A put copies this
+// rank's slot into every peer's block, and the last of its CTAs to finish
+// (an arrival counter it resets) fences at system scope and stores the
+// exchange's epoch into each peer's flag for this rank; a wait spins (bounded)
+// until every peer's flag for the kind has reached the epoch. Epoch =
+// generation << 32 | (step * per_step + index + 1), from the device step
+// counter, so one captured step graph serves every token; a buffer is
+// reused two exchanges later at the earliest, by when every rank has
+// consumed it (producing exchange k needs every rank's exchange k - 1, which
+// each rank produced after consuming k - 2).
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long exchange_epoch(const unsigned *gen_ptr, const int *step_ptr,
+                                                             int per_step, int index) {
+  return ((unsigned long long)*gen_ptr << 32) | (unsigned)(*step_ptr * per_step + index + 1);
+}
+
+__global__ void __launch_bounds__(256)
+exchange_put_kernel(uint8_t *const *blocks, int world, int rank, size_t slot_off, size_t bytes, size_t flag_off,
+                    int *counter, const unsigned *gen_ptr, const int *step_ptr, int per_step, int index) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  if ((bytes & 15) == 0) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(blocks[rank] + slot_off);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes / 16; i += step) {
+      const uint4 v = src[i];
+      for (int q = 0; q < world; ++q)
+        if (q != rank) reinterpret_cast<uint4 *>(blocks[q] + slot_off)[i] = v;
+    }
+  } else {  // 8-byte multiples (the classifier candidates of an odd batch)
+    const uint2 *src = reinterpret_cast<const uint2 *>(blocks[rank] + slot_off);
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes / 8; i += step) {
+      const uint2 v = src[i];
+      for (int q = 0; q < world; ++q)
+        if (q != rank) reinterpret_cast<uint2 *>(blocks[q] + slot_off)[i] = v;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(counter, 1) == (int)gridDim.x - 1) {
+    *counter = 0;
+    __threadfence_system();
+    const unsigned long long epoch = exchange_epoch(gen_ptr, step_ptr, per_step, index);
+    for (int q = 0; q < world; ++q)
+      if (q != rank) st_release_sys(reinterpret_cast<unsigned long long *>(blocks[q] + flag_off), epoch);
+  }
+}
+
+// flags: this rank's flags of one exchange kind, one per sending rank.
+__global__ void exchange_wait_kernel(const unsigned long long *flags, int world, int rank, const unsigned *gen_ptr,
+                                     const int *step_ptr, int per_step, int index, unsigned where) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int q = threadIdx.x;
+  if (q >= world || q == rank) return;
+  const unsigned long long epoch = exchange_epoch(gen_ptr, step_ptr, per_step, index);
+  unsigned long long start = 0;
+  for (uint32_t spin = 1; ld_acquire_sys(flags + q) < epoch; ++spin) {
+    if ((spin & 1023u) == 0u) {
+      const unsigned long long now = globaltimer();
+      if (start == 0) {
+        start = now;
+      } else if (now - start > kWaitLimitNs) {
+        report_timeout(&g_llama_status, where);  // a peer never delivered: the error is reported
+        return;
+      }
+    }
+  }
+}
+
 template <typename F>
 int launch_rows(int nv, F &&f) {
   switch (nv) {
@@ -758,6 +839,18 @@ struct ce_llama {
   uint16_t *x_att = nullptr, *x_hb = nullptr;
   float *x_delta = nullptr;
   float2 *x_top = nullptr;
+  // peer-memory exchange (ce_llama_exchange_open / _connect): this rank's
+  // block [att | delta | hb | top | flags], shared with the peers by CUDA IPC;
+  // x_att .. x_top then point into it
+  uint8_t *x_block = nullptr;
+  size_t x_off[5] = {};                   // byte offsets: att, delta, hb, top, flags
+  size_t x_block_bytes = 0;
+  std::vector<uint8_t *> peer_block;      // every rank's block as mapped here (own = x_block)
+  uint8_t **d_blocks = nullptr;           // device copy of peer_block
+  int *x_counter = nullptr;               // last-CTA counter of the put kernel
+  unsigned *x_gen = nullptr;              // run generation (advanced by ce_llama_start)
+  unsigned host_gen = 0;
+  bool p2p = false;
   int hs = 0, kv_dim = 0, qkv_rows = 0, nv = 0;
   int sp_qkv = 1, sp_o = 1, sp_13 = 1, sp_2 = 1;  // split-K counts of the layer GEMMs
   bool pdl = true;  // programmatic dependent launch between the step's kernels
@@ -784,6 +877,10 @@ struct ce_llama {
 namespace {
 
 void free_llama(ce_llama *m) {
+  for (size_t q = 0; q < m->peer_block.size(); ++q)
+    if (m->peer_block[q] != nullptr && (int)q != m->rank) cudaIpcCloseMemHandle(m->peer_block[q]);
+  for (void *p : {(void *)m->x_block, (void *)m->d_blocks, (void *)m->x_counter, (void *)m->x_gen})
+    if (p) cudaFree(p);
   for (void *p : {(void *)m->tok_emb, (void *)m->wqkv, (void *)m->wo, (void *)m->w13, (void *)m->w2,
                   (void *)m->wcls, (void *)m->rms_att, (void *)m->rms_ffn, (void *)m->rms_final,
                   (void *)m->rope, (void *)m->kcache, (void *)m->vcache, (void *)m->xb, (void *)m->att,
@@ -881,7 +978,23 @@ int tensor_of(ce_llama *m, int which, int layer, TensorView *v) {
 
 extern "C" {
 
-int ce_llama_validate(const ce_llama_config *c, int batch, int max_steps, int precision) {
+// Device memory of one rank's share of the model (its heads' KV cache, its
+// rows of every GEMM weight; the bf16 embedding on every rank) against the
+// 180 GB of a B200, with room for activations.
+int llama_memory_check(const ce_llama_config *c, int batch, int precision, int world) {
+  const int hs = c->dim / c->n_heads;
+  const double kv = 2.0 * c->n_layers * (double)batch * hs * c->n_kv_heads * c->seq_len * 2 / world;
+  const double per_value = precision == CE_PREC_NVFP4_E2M1 ? 0.5625 : 2.0;
+  const double w = per_value * ((double)c->n_layers * ((double)(c->dim + 2 * hs * c->n_kv_heads) * c->dim +
+                                                       (double)c->dim * c->dim + 3.0 * c->hidden_dim * c->dim) +
+                                (double)c->vocab_size * c->dim) / world +
+                   2.0 * (double)c->vocab_size * c->dim;
+  CE_REQUIRE(kv + w <= 170.0 * (1LL << 30),
+             "model and KV cache need %.1f GiB of device memory per GPU (limit 170 GiB)", (kv + w) / (1LL << 30));
+  return CE_OK;
+}
+
+int llama_shape_check(const ce_llama_config *c, int batch, int max_steps, int precision) {
   CE_REQUIRE(c != nullptr, "null config");
   CE_REQUIRE(c->dim >= 8 && c->dim % 8 == 0 && c->dim <= 8192, "dim must be a multiple of 8 in [8, 8192] (got %d)", c->dim);
   CE_REQUIRE(c->hidden_dim >= 8 && c->hidden_dim % 8 == 0, "hidden_dim must be a positive multiple of 8 (got %d)", c->hidden_dim);
@@ -899,22 +1012,19 @@ int ce_llama_validate(const ce_llama_config *c, int batch, int max_steps, int pr
              "llama weight precision %d is not available (bf16 or NVFP4)", precision);
   CE_REQUIRE(precision != CE_PREC_NVFP4_E2M1 || (c->dim % 64 == 0 && c->hidden_dim % 64 == 0),
              "NVFP4 weights need dim and hidden_dim multiples of 64 (got %d, %d)", c->dim, c->hidden_dim);
-  const double kv = 2.0 * c->n_layers * (double)batch * (c->dim / c->n_heads) * c->n_kv_heads * c->seq_len * 2;
-  const double per_value = precision == CE_PREC_NVFP4_E2M1 ? 0.5625 : 2.0;
-  const double w = per_value * ((double)c->n_layers * ((double)(c->dim + 2 * hs * c->n_kv_heads) * c->dim +
-                                                       (double)c->dim * c->dim + 3.0 * c->hidden_dim * c->dim) +
-                                (double)c->vocab_size * c->dim) +
-                   2.0 * (double)c->vocab_size * c->dim;
-  CE_REQUIRE(kv + w <= 170.0 * (1LL << 30),
-             "model and KV cache need %.1f GiB of device memory (limit 170 GiB)", (kv + w) / (1LL << 30));
   return CE_OK;
+}
+
+int ce_llama_validate(const ce_llama_config *c, int batch, int max_steps, int precision) {
+  if (int rc = llama_shape_check(c, batch, max_steps, precision)) return rc;
+  return llama_memory_check(c, batch, precision, 1);
 }
 
 int ce_llama_validate_shard(const ce_llama_config *c, int batch, int max_steps, int precision, int rank,
                             int world) {
-  if (int rc = ce_llama_validate(c, batch, max_steps, precision)) return rc;
+  if (int rc = llama_shape_check(c, batch, max_steps, precision)) return rc;
   CE_REQUIRE(world >= 1 && rank >= 0 && rank < world, "rank %d of world %d", rank, world);
-  if (world == 1) return CE_OK;
+  if (world == 1) return llama_memory_check(c, batch, precision, 1);
   CE_REQUIRE(c->n_heads % world == 0 && c->n_kv_heads % world == 0,
              "the heads (%d query, %d key/value) must split evenly over %d ranks", c->n_heads, c->n_kv_heads, world);
   CE_REQUIRE(c->hidden_dim % (8 * world) == 0, "hidden_dim / world must be a multiple of 8 (hidden %d, world %d)",
@@ -922,7 +1032,7 @@ int ce_llama_validate_shard(const ce_llama_config *c, int batch, int max_steps, 
   CE_REQUIRE(c->vocab_size % (4 * world) == 0, "vocab_size / world must be a multiple of 4 (vocab %d, world %d)",
              c->vocab_size, world);
   CE_REQUIRE((c->dim / world) % 8 == 0, "dim / world must be a multiple of 8 (dim %d, world %d)", c->dim, world);
-  return CE_OK;
+  return llama_memory_check(c, batch, precision, world);
 }
 
 int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
@@ -1168,6 +1278,13 @@ int ce_llama_start(ce_llama *m, const int32_t *tokens_host, int pos, ce_stream_t
   CE_CUDA_TRY(cudaMemcpyAsync(m->pos, &pos, 4, cudaMemcpyHostToDevice, s));
   CE_CUDA_TRY(cudaMemcpyAsync(m->step, &zero, 4, cudaMemcpyHostToDevice, s));
   CE_CUDA_TRY(cudaMemsetAsync(m->generated, 0xFF, (size_t)m->B * m->cap * 4, s));
+  if (m->x_gen != nullptr) {
+    // a new run: exchange epochs carry the generation, so flags left by an
+    // earlier run never satisfy this run's waits (every rank starts the same
+    // number of runs)
+    ++m->host_gen;
+    CE_CUDA_TRY(cudaMemcpyAsync(m->x_gen, &m->host_gen, 4, cudaMemcpyHostToDevice, s));
+  }
   CE_CUDA_TRY(cudaStreamSynchronize(s));
   return CE_OK;
 }
@@ -1276,6 +1393,62 @@ int ce_llama_bind_exchange(ce_llama *m, uint16_t *att, float *delta, uint16_t *h
   return CE_OK;
 }
 
+int ce_llama_exchange_open(ce_llama *m, void *handle_out) {
+  CE_REQUIRE(m != nullptr && handle_out != nullptr, "null argument");
+  CE_REQUIRE(m->world > 1, "peer exchange needs a sharded model (world > 1)");
+  CE_REQUIRE(m->world <= 32, "peer exchange supports at most 32 ranks (world %d)", m->world);
+  if (m->x_block == nullptr) {
+    const size_t n = m->world, B = m->B;
+    const size_t sizes[5] = {n * B * m->lD * 2, n * B * m->lD * 4, n * B * m->lHd * 2, n * B * 8, 4 * n * 8};
+    size_t off = 0;
+    for (int i = 0; i < 5; ++i) {
+      m->x_off[i] = off;
+      off += (sizes[i] + 255) / 256 * 256;
+    }
+    m->x_block_bytes = off;
+    CE_CUDA_TRY(cudaMalloc(&m->x_block, off));
+    CE_CUDA_TRY(cudaMemset(m->x_block, 0, off));
+    CE_CUDA_TRY(cudaMalloc(&m->x_counter, 4));
+    CE_CUDA_TRY(cudaMemset(m->x_counter, 0, 4));
+    CE_CUDA_TRY(cudaMalloc(&m->x_gen, 4));
+    CE_CUDA_TRY(cudaMemcpy(m->x_gen, &m->host_gen, 4, cudaMemcpyHostToDevice));
+    CE_CUDA_TRY(cudaMalloc(&m->d_blocks, n * sizeof(uint8_t *)));
+    m->x_att = reinterpret_cast<uint16_t *>(m->x_block + m->x_off[0]);
+    m->x_delta = reinterpret_cast<float *>(m->x_block + m->x_off[1]);
+    m->x_hb = reinterpret_cast<uint16_t *>(m->x_block + m->x_off[2]);
+    m->x_top = reinterpret_cast<float2 *>(m->x_block + m->x_off[3]);
+  }
+  cudaIpcMemHandle_t h;
+  CE_CUDA_TRY(cudaIpcGetMemHandle(&h, m->x_block));
+  static_assert(sizeof(cudaIpcMemHandle_t) <= CE_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memset(handle_out, 0, CE_IPC_HANDLE_BYTES);
+  std::memcpy(handle_out, &h, sizeof(h));
+  return CE_OK;
+}
+
+int ce_llama_exchange_connect(ce_llama *m, const void *handles) {
+  CE_REQUIRE(m != nullptr && handles != nullptr, "null argument");
+  CE_REQUIRE(m->x_block != nullptr, "call ce_llama_exchange_open first");
+  CE_REQUIRE(!m->p2p, "the exchange is already connected");
+  const int n = m->world;
+  m->peer_block.assign(n, nullptr);
+  for (int q = 0; q < n; ++q) {
+    if (q == m->rank) {
+      m->peer_block[q] = m->x_block;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, static_cast<const uint8_t *>(handles) + (size_t)q * CE_IPC_HANDLE_BYTES, sizeof(h));
+    void *p = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_error(e, format("cudaIpcOpenMemHandle(rank %d)", q).c_str());
+    m->peer_block[q] = static_cast<uint8_t *>(p);
+  }
+  CE_CUDA_TRY(cudaMemcpy(m->d_blocks, m->peer_block.data(), n * sizeof(uint8_t *), cudaMemcpyHostToDevice));
+  m->p2p = true;
+  return CE_OK;
+}
+
 int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t stream) {
   CE_REQUIRE(m != nullptr, "null model");
   CE_REQUIRE(m->x_att && m->x_delta && m->x_hb && m->x_top, "exchange buffers are not bound");
@@ -1326,10 +1499,30 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
                          m->x_delta + (size_t)r * slot_d, splits, n4);
   };
   const int join_grid = 2 * sm_count();
-  const int l = layer;
+  const int l = layer, L = c.n_layers;
+  // peer-memory exchange: put this rank's slot of kind k to every peer, and
+  // wait for every peer's slot of kind k (no-ops when the caller joins the
+  // slots with its own all-gathers)
+  const size_t kind_slot[4] = {slot_d * 2, slot_d * 4, (size_t)B * lHd * 2, (size_t)B * 8};
+  auto put = [&](int k, int per_step, int index) -> int {
+    if (!m->p2p) return CE_OK;
+    const size_t bytes = kind_slot[k];
+    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((bytes / 16 + 255) / 256, 2 * sm_count()));
+    return launch_kernel(exchange_put_kernel, dim3(blocks), dim3(256), 0, s, pdl, "exchange_put_kernel",
+                         (uint8_t *const *)m->d_blocks, n, r, m->x_off[k] + (size_t)r * bytes, bytes,
+                         m->x_off[4] + ((size_t)k * n + r) * 8, m->x_counter, (const unsigned *)m->x_gen,
+                         (const int *)m->step, per_step, index);
+  };
+  auto wait = [&](int k, int per_step, int index) -> int {
+    if (!m->p2p) return CE_OK;
+    return launch_kernel(exchange_wait_kernel, dim3(1), dim3(32), 0, s, pdl, "exchange_wait_kernel",
+                         (const unsigned long long *)(m->x_block + m->x_off[4]) + (size_t)k * n, n, r,
+                         (const unsigned *)m->x_gen, (const int *)m->step, per_step, index, 910u + (unsigned)k);
+  };
   int rc = CE_OK;
   switch (segment) {
     case CE_LLAMA_SEG_ATTN: {
+      if (l > 0 && (rc = wait(1, 2 * L, 2 * (l - 1) + 1))) return rc;
       rc = norm(l == 0, m->rms_att + (size_t)l * D);
       if (rc) return rc;
       const size_t qkv_stride = (size_t)B * m->qkv_rows;
@@ -1350,38 +1543,51 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
                              (const uint16_t *)vc, (const int *)m->pos, m->lH, m->lKH, c.seq_len,
                              m->attn_splits, m->part, m->arrivals, slot, lD, (int)w4);
       };
-      return m->hs == 64 ? attention(std::integral_constant<int, 64>{})
-                         : attention(std::integral_constant<int, 128>{});
+      rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{})
+                       : attention(std::integral_constant<int, 128>{});
+      return rc ? rc : put(0, L, l);
     }
     case CE_LLAMA_SEG_OPROJ:
+      if ((rc = wait(0, L, l))) return rc;
       rc = launch_kernel(join_shards_kernel, dim3(join_grid), dim3(256), 0, s, pdl, "join_shards_kernel",
                          (const uint16_t *)m->x_att, m->att, n, B, lD);
       if (rc) return rc;
-      return to_delta_slot(1, l, m->att, m->sp_o);
+      rc = to_delta_slot(1, l, m->att, m->sp_o);
+      return rc ? rc : put(1, 2 * L, 2 * l);
     case CE_LLAMA_SEG_FFN_IN: {
+      if ((rc = wait(1, 2 * L, 2 * l))) return rc;
       rc = norm(false, m->rms_ffn + (size_t)l * D);
       if (rc) return rc;
       uint16_t *slot = m->x_hb + (size_t)r * B * lHd;
-      if (m->sp_13 == 1) return gemm(2, l, nullptr, m->xb, 2 * lHd, 1, 0, slot, lHd);
+      if (m->sp_13 == 1) {
+        rc = gemm(2, l, nullptr, m->xb, 2 * lHd, 1, 0, slot, lHd);
+        return rc ? rc : put(2, L, l);
+      }
       const size_t h_stride = (size_t)B * 2 * lHd;
       rc = gemm(2, l, m->h, m->xb, 2 * lHd, m->sp_13, (long long)h_stride, nullptr, 0);
       if (rc) return rc;
-      return launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
-                           (const float *)m->h, m->sp_13, h_stride, slot, B, lHd, (int)w4);
+      rc = launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
+                         (const float *)m->h, m->sp_13, h_stride, slot, B, lHd, (int)w4);
+      return rc ? rc : put(2, L, l);
     }
     case CE_LLAMA_SEG_FFN_OUT:
+      if ((rc = wait(2, L, l))) return rc;
       rc = launch_kernel(join_shards_kernel, dim3(join_grid), dim3(256), 0, s, pdl, "join_shards_kernel",
                          (const uint16_t *)m->x_hb, m->hb, n, B, lHd);
       if (rc) return rc;
-      return to_delta_slot(3, l, m->hb, m->sp_2);
+      rc = to_delta_slot(3, l, m->hb, m->sp_2);
+      return rc ? rc : put(1, 2 * L, 2 * l + 1);
     case CE_LLAMA_SEG_HEAD:
+      if ((rc = wait(1, 2 * L, 2 * (L - 1) + 1))) return rc;
       rc = norm(false, m->rms_final);
       if (rc) return rc;
       rc = gemm(4, 0, m->logits, m->xb, m->lV, 1, 0, nullptr, 0);
       if (rc) return rc;
-      return launch_kernel(shard_top1_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "shard_top1_kernel",
-                           (const float *)m->logits, m->lV, r * m->lV, m->x_top + (size_t)r * B);
+      rc = launch_kernel(shard_top1_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "shard_top1_kernel",
+                         (const float *)m->logits, m->lV, r * m->lV, m->x_top + (size_t)r * B);
+      return rc ? rc : put(3, 1, 0);
     case CE_LLAMA_SEG_PICK:
+      if ((rc = wait(3, 1, 0))) return rc;
       rc = launch_kernel(pick_top_kernel, dim3((B + 127) / 128), dim3(128), 0, s, pdl, "pick_top_kernel",
                          (const float2 *)m->x_top, n, B, m->tokens, m->generated, m->cap, (const int *)m->step);
       if (rc) return rc;

@@ -98,18 +98,36 @@ class RowShardedPlan:
 class ShardedLlama:
     """A Llama-2 decoder step row-sharded over the ranks of a process group
     (one GPU each): the library's ce_llama segments compute this rank's slice
-    of each output into caller-owned exchange buffers, and in-place
-    all-gathers (NCCL over NVLink) join the slices between them. All work is
-    enqueued on one stream, so a whole step can be captured in a CUDA graph
-    (torch captures NCCL collectives)."""
+    of each output, and the slices are joined between segments by one of two
+    exchanges:
 
-    def __init__(self, ce, cfg, batch, max_steps, precision, group=None, stream=None):
+    mode "p2p" (default): the library's own peer-memory exchange. Every
+      rank's exchange block is shared with the others through CUDA IPC
+      (handles swapped once here with an all_gather_object); the segments
+      put their slot into every peer's block over NVLink and wait on the
+      peers' flags, so a step is kernels only.
+    mode "nccl": caller-owned exchange buffers joined by in-place
+      all_gather_into_tensor (NCCL) after each segment.
+
+    All work is enqueued on one stream, so a whole step can be captured in a
+    CUDA graph (torch captures NCCL collectives too)."""
+
+    def __init__(self, ce, cfg, batch, max_steps, precision, group=None, stream=None, mode="p2p"):
+        if mode not in ("p2p", "nccl"):
+            raise ValueError(f"unknown exchange mode {mode!r}")
         self.ce = ce
         self.group = group
+        self.mode = mode
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.model = ce.Llama(cfg, batch, max_steps, precision=precision, stream=stream,
                               rank=self.rank, world=self.world)
+        if mode == "p2p":
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.model.exchange_open(), group=group)
+            self.model.exchange_connect(b"".join(handles))
+            dist.barrier(group)
+            return
         c = self.model.cfg
         n, B = self.world, batch
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -123,22 +141,33 @@ class ShardedLlama:
 
     def _gather(self, buf):
         # in place: this rank's slot is the input of the all-gather
-        dist.all_gather_into_tensor(buf, buf[self.rank], group=self.group)
+        if self.mode == "nccl":
+            dist.all_gather_into_tensor(buf, buf[self.rank], group=self.group)
 
     def step(self, stream=None):
         m, ce = self.model, self.ce
+        nccl = self.mode == "nccl"
         for layer in range(m.cfg.n_layers):
             m.segment(ce.SEG_ATTN, layer, stream=stream)
-            self._gather(self.att)
+            if nccl:
+                self._gather(self.att)
             m.segment(ce.SEG_OPROJ, layer, stream=stream)
-            self._gather(self.delta)
+            if nccl:
+                self._gather(self.delta)
             m.segment(ce.SEG_FFN_IN, layer, stream=stream)
-            self._gather(self.hb)
+            if nccl:
+                self._gather(self.hb)
             m.segment(ce.SEG_FFN_OUT, layer, stream=stream)
-            self._gather(self.delta)
+            if nccl:
+                self._gather(self.delta)
         m.segment(ce.SEG_HEAD, stream=stream)
-        self._gather(self.top)
+        if nccl:
+            self._gather(self.top)
         m.segment(ce.SEG_PICK, stream=stream)
 
     def close(self):
+        if self.mode == "p2p":
+            # no rank frees its exchange block while a peer may still map it
+            torch.cuda.synchronize()
+            dist.barrier(self.group)
         self.model.close()

@@ -539,6 +539,25 @@ int ce_llama_validate_shard(const ce_llama_config *cfg, int batch, int max_steps
 int ce_llama_create_shard(ce_llama **model, const ce_llama_config *cfg, int batch, int max_steps,
                           int precision, int rank, int world, ce_stream_t stream);
 
+/* Peer-memory exchange for a sharded model, instead of caller-bound buffers
+ * joined by all-gathers: ce_llama_exchange_open allocates this rank's
+ * exchange block (the four slot arrays and one flag per kind and sending
+ * rank) and writes its CUDA IPC handle (CE_IPC_HANDLE_BYTES) to handle_out;
+ * after every rank has opened, each passes all ranks' handles (rank order,
+ * world x CE_IPC_HANDLE_BYTES) to ce_llama_exchange_connect, which maps the
+ * peers' blocks. From then on the segments exchange by themselves: after
+ * each producer a put copies this rank's slot into every peer's block over
+ * NVLink and stores the exchange's epoch into the peers' flags; before each
+ * consumer a wait spins (bounded; ce_llama_status reports a timeout) until
+ * every peer's flag is current. No NCCL call, so a captured step graph holds
+ * only kernels. Every rank must call ce_llama_start the same number of times
+ * (the epoch carries a run generation). Replaces the ncclAllGather joins of
+ * the row-sharded step (output-row sharding of the classifier GEMM,
+ * decoder.cu:83-125, extended to every layer of the step). */
+#define CE_IPC_HANDLE_BYTES 64
+int ce_llama_exchange_open(ce_llama *model, void *handle_out);
+int ce_llama_exchange_connect(ce_llama *model, const void *handles);
+
 /* Caller-owned device exchange buffers of a sharded step, all-gathered by
  * the caller between segments (each rank writes its own slot r):
  * att   16-bit [world][batch][dim / world]         (after SEG_ATTN)

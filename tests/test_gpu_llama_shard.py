@@ -6,7 +6,9 @@ agree, the residual stream after the last layer within 1e-3 on the
 sequences that never diverged, and a greedy token differing only at a near
 tie the logit error can bridge (at most 1 in 20 sequences); bf16
 and NVFP4 weights; a captured step graph (NCCL included) replays bit for bit
-like direct steps. Needs at least 2 visible GPUs; skipped otherwise."""
+like direct steps. Both exchanges: NCCL all-gathers, and the library's
+peer-memory puts and flag waits over CUDA IPC mappings. Needs at least 2
+visible GPUs; skipped otherwise."""
 import os
 import socket
 
@@ -58,10 +60,10 @@ def _full_logits(model, dist, world):
 
 
 def _body(rank, world, case, ce, rs, dist):
-    cfg, prec_name, batch, fill, steps, graph = case
+    cfg, prec_name, batch, fill, steps, graph, mode = case
     prec = {"bf16": ce.PREC_BF16, "nvfp4": ce.PREC_NVFP4_E2M1}[prec_name]
     tokens0 = np.random.default_rng(5).integers(0, cfg["vocab_size"], batch).astype(np.int32)
-    sh = rs.ShardedLlama(ce, cfg, batch, steps, prec)
+    sh = rs.ShardedLlama(ce, cfg, batch, steps, prec, mode=mode)
     sh.model.init_random(seed=3, kv_fill=fill)
     sh.model.start(tokens0, fill)
     if graph:
@@ -138,15 +140,18 @@ def _body(rank, world, case, ce, rs, dist):
 
 CASES = [
     (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4, vocab_size=1024, seq_len=96),
-     "bf16", 12, 40, 5, False),
+     "bf16", 12, 40, 5, False, "nccl"),
+    (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4, vocab_size=1024, seq_len=96),
+     "bf16", 12, 40, 5, True, "p2p"),
     (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=4, vocab_size=1024, seq_len=200),
-     "nvfp4", 9, 150, 4, True),
+     "nvfp4", 9, 150, 4, True, "p2p"),
     (dict(dim=1024, hidden_dim=2816, n_layers=2, n_heads=8, vocab_size=4096, seq_len=128),
-     "nvfp4", 64, 100, 3, False),
+     "nvfp4", 64, 100, 3, False, "p2p"),
 ]
 
 
-@pytest.mark.parametrize("case", CASES, ids=["bf16-gqa", "nvfp4-graph", "nvfp4-batch64"])
+@pytest.mark.parametrize("case", CASES, ids=["bf16-gqa-nccl", "bf16-gqa-p2p-graph", "nvfp4-graph-p2p",
+                                             "nvfp4-batch64-p2p"])
 def test_sharded_decoder_matches_unsharded(case):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")

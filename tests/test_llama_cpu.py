@@ -20,7 +20,7 @@ from oracle.oracle import bf16_bits
     (dict(n_heads=4), "head size dim / n_heads must be 64 or 128"),
     (dict(vocab_size=1001), "vocab_size must be a multiple of 4"),
     (dict(seq_len=0), "seq_len must be in"),
-    (dict(seq_len=1 << 20, n_layers=64), "GiB of device memory"),
+    (dict(seq_len=1 << 20, n_layers=64), "GiB of device memory per GPU"),
 ])
 def test_validate_rejects_bad_shapes(ce, change, pattern):
     cfg = dict(dim=768, hidden_dim=2048, n_layers=12, n_heads=12, vocab_size=32000, seq_len=1024)
@@ -168,3 +168,13 @@ def test_validate_shard_rejects_uneven_splits(ce, change, world, pattern):
     rc = ce.lib().ce_llama_validate_shard(ctypes.byref(c), 8, 4, ce.PREC_BF16, 0, world)
     assert rc == ce.ERR_USAGE
     assert pattern in ce.last_error()[1]
+
+
+def test_shard_memory_is_per_rank(ce):
+    """BASELINE config 5 at batch 512 (a 512 GiB KV cache) fits 8 ranks (their
+    heads' share each) but not one GPU."""
+    c = ce.llama_config(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, vocab_size=32000, seq_len=2048)
+    assert ce.lib().ce_llama_validate_shard(ctypes.byref(c), 512, 32, ce.PREC_NVFP4_E2M1, 3, 8) == ce.OK, ce.last_error()
+    assert ce.lib().ce_llama_validate_shard(ctypes.byref(c), 512, 32, ce.PREC_NVFP4_E2M1, 0, 1) == ce.ERR_USAGE
+    assert "GiB of device memory per GPU" in ce.last_error()[1]
+    assert ce.lib().ce_llama_validate_shard(ctypes.byref(c), 64, 32, ce.PREC_NVFP4_E2M1, 0, 1) == ce.OK
