@@ -28,7 +28,7 @@ int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const ui
              int ld_bytes, int nsf, cudaStream_t s, const int *row_map);
 int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
              int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
-             int swiglu_ld, cudaStream_t s, bool pdl);
+             int swiglu_ld, cudaStream_t s, bool pdl, const ExchangeWait *xw = nullptr);
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
               cudaStream_t s, int force_group = 0);

@@ -144,6 +144,80 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// --- peer-memory exchange between ranks (one GPU each) ---------------------
+// A producer writes its slice of an exchange into every rank's buffer (its
+// own and the peers', mapped by CUDA IPC over NVLink); after its last CTA has
+// written, it stores the exchange's epoch into each peer's flag for the
+// sending rank. A consumer waits until every peer's flag has reached the
+// epoch before it reads. Epoch = generation << 32 | (step * per_step +
+// index + 1): the generation advances per run, the step is the device step
+// counter, so one captured graph serves every step.
+struct ExchangeWait {
+  const unsigned long long *flags;  // this rank's flags of the exchange kind, one per sending rank; null = no wait
+  const unsigned *gen;
+  const int *step;
+  int world, rank, per_step, index;
+};
+struct ExchangePut {
+  uint8_t *const *blocks;  // every rank's exchange block as mapped here; null = local write only
+  size_t flag_off;         // byte offset of flags[kind][this rank] in a block
+  int *counter;            // arrival counter of the producer's CTAs (reset by the last)
+  const unsigned *gen;
+  const int *step;
+  int world, rank, per_step, index;
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long exchange_epoch(const unsigned *gen, const int *step, int per_step,
+                                                             int index) {
+  return ((unsigned long long)*gen << 32) | (unsigned)(*step * per_step + index + 1);
+}
+
+// Called by one warp: lane q waits (bounded) for peer q's flag. Returns false,
+// after recording `where`, if a peer never delivered.
+__device__ __forceinline__ bool exchange_wait_warp(const ExchangeWait &w, DeviceStatus *st, unsigned where) {
+  const int q = threadIdx.x & 31;
+  bool ok = true;
+  if (q < w.world && q != w.rank) {
+    const unsigned long long epoch = exchange_epoch(w.gen, w.step, w.per_step, w.index);
+    unsigned long long start = 0;
+    for (uint32_t spin = 1; ld_acquire_sys(w.flags + q) < epoch; ++spin) {
+      if ((spin & 1023u) == 0u) {
+        const unsigned long long now = globaltimer();
+        if (start == 0) {
+          start = now;
+        } else if (now - start > kWaitLimitNs) {
+          report_timeout(st, where);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// Called by every thread of a producer CTA after its writes: the last CTA of
+// the grid to arrive signals the peers. Contains __syncthreads.
+__device__ __forceinline__ void exchange_signal(const ExchangePut &p) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && atomicAdd(p.counter, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
+    *p.counter = 0;
+    __threadfence_system();
+    const unsigned long long epoch = exchange_epoch(p.gen, p.step, p.per_step, p.index);
+    for (int q = 0; q < p.world; ++q)
+      if (q != p.rank) st_release_sys(reinterpret_cast<unsigned long long *>(p.blocks[q] + p.flag_off), epoch);
+  }
+}
+
 // --- clusters (CTA pairs of the 2-SM tensor-core path) ---------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

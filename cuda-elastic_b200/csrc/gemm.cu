@@ -1155,7 +1155,9 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
 //              layout of w4t_pack; weights are constant, so this starts
 //              before the programmatic-launch wait;
 //   warp 1     TMEM allocator and MMA issuer (kind::f16, A from TMEM);
-//   warp 2     activation producer: two TMA boxes of 64 x NB per stage;
+//   warp 2     activation producer: two TMA boxes of 64 x NB per stage
+//              (first, when the activations come from the peers' exchange
+//              puts, a bounded wait on their flags);
 //   warps 4-7  epilogue (TMEM lane quarter = warp % 4): alpha x accumulator,
 //              split-K partials or the SwiGLU product;
 //   warps 8-15 converters, two per lane quarter: cvt.rn.f16x2.e2m1x2 and a
@@ -1183,6 +1185,7 @@ struct W4tArgs {
   int stages, w_stages;
   int act_stage_bytes;   // 2 x nb x 128
   int acc_cols;          // TMEM columns before the weight stages
+  ExchangeWait xw;       // activations delivered by peers' exchange puts (flags null: local)
 };
 
 struct W4tUnit {
@@ -1313,6 +1316,13 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
   } else if (warp == 2) {
     // ---------------- activation producer
     pdl_wait();
+    if (args.xw.flags != nullptr) {
+      // the activations are the peers' slices, written over NVLink: wait for
+      // their flags (the weight producer and converters run meanwhile), then
+      // order the TMA reads after the acquire
+      exchange_wait_warp(args.xw, st, 72);
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+    }
     int as = 0;
     uint32_t aph = 0, issued_mask = 0, issued_parity = 0;
     bool okay = true;
@@ -1814,7 +1824,7 @@ int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const ui
 // and the fp16 SwiGLU product goes to swiglu_out [M][swiglu_ld] instead.
 int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
              int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
-             int swiglu_ld, cudaStream_t s, bool pdl) {
+             int swiglu_ld, cudaStream_t s, bool pdl, const ExchangeWait *xw) {
   CE_REQUIRE(M >= 1 && N >= 1 && K >= 64 && K % 64 == 0, "W4A16 GEMM dims (M=%d N=%d K=%d; K %% 64 == 0)", M, N,
              K);
   CE_REQUIRE(lda >= K && (lda * 2) % 16 == 0, "lda must be >= K and a multiple of 8 (got %d)", lda);
@@ -1856,6 +1866,7 @@ int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t 
   w.w_stages = p.w_stages;
   w.act_stage_bytes = p.act_stage;
   w.acc_cols = p.acc_cols;
+  if (xw != nullptr) w.xw = *xw;
   const int sms = sm_count();
   const int units = w.tiles_n * w.tiles_b * splits;
   const int grid = units < sms ? units : sms;

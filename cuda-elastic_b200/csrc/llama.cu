@@ -63,7 +63,7 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
 int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
 int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
              int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
-             int swiglu_ld, cudaStream_t s, bool pdl);
+             int swiglu_ld, cudaStream_t s, bool pdl, const ExchangeWait *xw = nullptr);
 int gemm_w4t_auto_splits(int M, int N, int K, int max_splits);
 void w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes);
 int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
@@ -178,10 +178,14 @@ template <int NV>
 __global__ void __launch_bounds__(kRowThreads)
 residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_stride,
                         const uint16_t *emb, const int *tokens, int vocab, const float *w,
-                        uint16_t *xb, int dim, float eps, int f16, int shard_cols) {
+                        uint16_t *xb, int dim, float eps, int f16, int shard_cols, ExchangeWait xw) {
   __shared__ float scratch[32];
   pdl_launch_dependents();
   pdl_wait();
+  if (xw.flags != nullptr) {  // delta from the peers' exchange puts
+    if (threadIdx.x < 32) exchange_wait_warp(xw, &g_llama_status, 920u);
+    __syncthreads();
+  }
   const int b = blockIdx.x, cols4 = dim / 4;
   float4 *xr = reinterpret_cast<float4 *>(x + (size_t)b * dim);
   float4 v[NV];
@@ -606,11 +610,59 @@ __global__ void sum_splits_kernel(const float *src, float *dst, int splits, size
   }
 }
 
+// This rank's delta slice: the split-K partials src [splits][rows][cols]
+// (cols % 4 == 0) summed in split order and written at byte offset off
+// (row stride ld floats) of every rank's delta exchange, then the peers
+// are signalled.
+__global__ void sum_splits_put_kernel(const float *src, int splits, int rows, int cols, ExchangePut xp, size_t off,
+                                      int ld) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t n4 = (size_t)rows * cols / 4, plane = (size_t)rows * cols;
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += step) {
+    float4 a = reinterpret_cast<const float4 *>(src)[i];
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 e = reinterpret_cast<const float4 *>(src + sp * plane)[i];
+      a.x += e.x, a.y += e.y, a.z += e.z, a.w += e.w;
+    }
+    const size_t r = 4 * i / cols, c = 4 * i % cols;
+    const size_t at = off + (r * ld + c) * 4;
+    for (int q = 0; q < xp.world; ++q) *reinterpret_cast<float4 *>(xp.blocks[q] + at) = a;
+  }
+  exchange_signal(xp);
+}
+
+// This rank's SwiGLU product (as swiglu_kernel: h interleaves (g_i, u_i),
+// the sum of nsplit split-K partials) written at byte offset off (row stride
+// ld values) of every rank's product exchange, then the peers are signalled.
+__global__ void swiglu_put_kernel(const float *h, int nsplit, size_t split_stride, int rows, int hidden, int f16,
+                                  ExchangePut xp, size_t off, int ld) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const size_t n = (size_t)rows * hidden / 2;
+  const size_t step = (size_t)gridDim.x * blockDim.x;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) {
+    const size_t r = (2 * i) / hidden, c = (2 * i) % hidden;
+    float4 gu = *reinterpret_cast<const float4 *>(h + r * 2 * hidden + 2 * c);
+    for (int sp = 1; sp < nsplit; ++sp) {
+      const float4 e = *reinterpret_cast<const float4 *>(h + sp * split_stride + r * 2 * hidden + 2 * c);
+      gu.x += e.x, gu.y += e.y, gu.z += e.z, gu.w += e.w;
+    }
+    const float a = gu.x / (1.0f + expf(-gu.x)) * gu.y;
+    const float bb = gu.z / (1.0f + expf(-gu.z)) * gu.w;
+    const uint32_t v = pack_operand(a, bb, f16);
+    const size_t at = off + (r * ld + c) * 2;
+    for (int q = 0; q < xp.world; ++q) *reinterpret_cast<uint32_t *>(xp.blocks[q] + at) = v;
+  }
+  exchange_signal(xp);
+}
+
 // First maximum of each row of this shard's logits [batch][cols]: (value,
 // global index first + idx) as a float2 whose second lane holds the index
 // bits (NaN never wins; an all-NaN row gives (-inf, first)).
 __global__ void __launch_bounds__(kRowThreads)
-shard_top1_kernel(const float *logits, int cols, int first, float2 *top) {
+shard_top1_kernel(const float *logits, int cols, int first, float2 *top, ExchangePut xp, size_t top_off) {
   __shared__ float sv[32];
   __shared__ int si[32];
   pdl_launch_dependents();
@@ -639,17 +691,29 @@ shard_top1_kernel(const float *logits, int cols, int first, float2 *top) {
       const int oi = __shfl_down_sync(0xffffffffu, idx, off);
       if (ov > best || (ov == best && oi < idx)) best = ov, idx = oi;
     }
-    if (lane == 0) top[b] = make_float2(best, __int_as_float(first + (idx == 0x7fffffff ? 0 : idx)));
+    if (lane == 0) {
+      const float2 t = make_float2(best, __int_as_float(first + (idx == 0x7fffffff ? 0 : idx)));
+      if (xp.blocks == nullptr) {
+        top[b] = t;
+      } else {  // into every rank's candidate exchange
+        for (int q = 0; q < xp.world; ++q) *reinterpret_cast<float2 *>(xp.blocks[q] + top_off + (size_t)b * 8) = t;
+      }
+    }
   }
+  if (xp.blocks != nullptr) exchange_signal(xp);
 }
 
 // The global greedy token of each row from the shards' candidates
 // top[shards][batch]: largest value, lowest index on ties (the first maximum
 // over the whole vocabulary).
 __global__ void pick_top_kernel(const float2 *top, int shards, int batch, int *tokens, int *generated,
-                                int cap, const int *step_ptr) {
+                                int cap, const int *step_ptr, ExchangeWait xw) {
   pdl_launch_dependents();
   pdl_wait();
+  if (xw.flags != nullptr) {  // candidates from the peers' exchange puts
+    if (threadIdx.x < 32) exchange_wait_warp(xw, &g_llama_status, 923u);
+    __syncthreads();
+  }
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   float best = -INFINITY;
@@ -678,71 +742,30 @@ __global__ void pick_top_kernel(const float2 *top, int shards, int batch, int *t
 // reused two exchanges later at the earliest, by when every rank has
 // consumed it (producing exchange k needs every rank's exchange k - 1, which
 // each rank produced after consuming k - 2).
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ unsigned long long exchange_epoch(const unsigned *gen_ptr, const int *step_ptr,
-                                                             int per_step, int index) {
-  return ((unsigned long long)*gen_ptr << 32) | (unsigned)(*step_ptr * per_step + index + 1);
-}
-
+// Copies rows x row_bytes (16-byte multiple) at byte offset off, row stride
+// `stride`, of this rank's exchange block into every peer's block, then
+// signals the peers (the attention output, which many CTAs write).
 __global__ void __launch_bounds__(256)
-exchange_put_kernel(uint8_t *const *blocks, int world, int rank, size_t slot_off, size_t bytes, size_t flag_off,
-                    int *counter, const unsigned *gen_ptr, const int *step_ptr, int per_step, int index) {
+exchange_put_kernel(ExchangePut xp, size_t off, int rows, size_t row_bytes, size_t stride) {
   pdl_launch_dependents();
   pdl_wait();
+  const size_t per_row = row_bytes / 16, n16 = (size_t)rows * per_row;
   const size_t step = (size_t)gridDim.x * blockDim.x;
-  if ((bytes & 15) == 0) {
-    const uint4 *src = reinterpret_cast<const uint4 *>(blocks[rank] + slot_off);
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes / 16; i += step) {
-      const uint4 v = src[i];
-      for (int q = 0; q < world; ++q)
-        if (q != rank) reinterpret_cast<uint4 *>(blocks[q] + slot_off)[i] = v;
-    }
-  } else {  // 8-byte multiples (the classifier candidates of an odd batch)
-    const uint2 *src = reinterpret_cast<const uint2 *>(blocks[rank] + slot_off);
-    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < bytes / 8; i += step) {
-      const uint2 v = src[i];
-      for (int q = 0; q < world; ++q)
-        if (q != rank) reinterpret_cast<uint2 *>(blocks[q] + slot_off)[i] = v;
-    }
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n16; i += step) {
+    const size_t at = off + (i / per_row) * stride + (i % per_row) * 16;
+    const uint4 v = *reinterpret_cast<const uint4 *>(xp.blocks[xp.rank] + at);
+    for (int q = 0; q < xp.world; ++q)
+      if (q != xp.rank) *reinterpret_cast<uint4 *>(xp.blocks[q] + at) = v;
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0 && atomicAdd(counter, 1) == (int)gridDim.x - 1) {
-    *counter = 0;
-    __threadfence_system();
-    const unsigned long long epoch = exchange_epoch(gen_ptr, step_ptr, per_step, index);
-    for (int q = 0; q < world; ++q)
-      if (q != rank) st_release_sys(reinterpret_cast<unsigned long long *>(blocks[q] + flag_off), epoch);
-  }
+  exchange_signal(xp);
 }
 
-// flags: this rank's flags of one exchange kind, one per sending rank.
-__global__ void exchange_wait_kernel(const unsigned long long *flags, int world, int rank, const unsigned *gen_ptr,
-                                     const int *step_ptr, int per_step, int index, unsigned where) {
+// A consumer-side wait as its own launch (before a bf16 GEMM, which reads
+// its operand with TMA and has no wait of its own).
+__global__ void exchange_wait_kernel(ExchangeWait xw, unsigned where) {
   pdl_launch_dependents();
   pdl_wait();
-  const int q = threadIdx.x;
-  if (q >= world || q == rank) return;
-  const unsigned long long epoch = exchange_epoch(gen_ptr, step_ptr, per_step, index);
-  unsigned long long start = 0;
-  for (uint32_t spin = 1; ld_acquire_sys(flags + q) < epoch; ++spin) {
-    if ((spin & 1023u) == 0u) {
-      const unsigned long long now = globaltimer();
-      if (start == 0) {
-        start = now;
-      } else if (now - start > kWaitLimitNs) {
-        report_timeout(&g_llama_status, where);  // a peer never delivered: the error is reported
-        return;
-      }
-    }
-  }
+  exchange_wait_warp(xw, &g_llama_status, where);
 }
 
 template <typename F>
@@ -1322,7 +1345,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     const int rc = launch_rows(m->nv, [&](auto nv) {
       lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
                           "residual_rmsnorm_kernel", m->x, delta, nsplit, delta_stride, emb,
-                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, 0);
+                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, 0, ExchangeWait{});
     });
     return rc ? rc : lrc;
   };
@@ -1449,13 +1472,153 @@ int ce_llama_exchange_connect(ce_llama *m, const void *handles) {
   return CE_OK;
 }
 
+// One segment of the row-sharded step with the peer-memory exchange: the
+// exchange buffers are the consumers' operands ([batch][full width], this
+// rank's columns at rank x slice), producers write their slice into every
+// rank's buffer and signal, consumers wait on the flags (the W4A16 GEMM in
+// its activation producer, so the wait overlaps its weight streaming).
+int enqueue_segment_p2p(ce_llama *m, int segment, int l, cudaStream_t s) {
+  const ce_llama_config &c = m->c;
+  const int B = m->B, D = c.dim, Hd = c.hidden_dim, n = m->world, r = m->rank, L = c.n_layers;
+  const int lD = m->lD, lHd = m->lHd;
+  const bool pdl = m->pdl, w4 = m->precision == CE_PREC_NVFP4_E2M1;
+  const float eps = 1e-5f;
+  auto wait_of = [&](int kind, int per_step, int index) {
+    ExchangeWait w{};
+    w.flags = reinterpret_cast<const unsigned long long *>(m->x_block + m->x_off[4]) + (size_t)kind * n;
+    w.gen = m->x_gen;
+    w.step = m->step;
+    w.world = n;
+    w.rank = r;
+    w.per_step = per_step;
+    w.index = index;
+    return w;
+  };
+  auto put_of = [&](int kind, int per_step, int index) {
+    ExchangePut p{};
+    p.blocks = m->d_blocks;
+    p.flag_off = m->x_off[4] + ((size_t)kind * n + r) * 8;
+    p.counter = m->x_counter;
+    p.gen = m->x_gen;
+    p.step = m->step;
+    p.world = n;
+    p.rank = r;
+    p.per_step = per_step;
+    p.index = index;
+    return p;
+  };
+  const unsigned grid_put = (unsigned)(2 * sm_count());
+  // y = a W^T of weight kind k of layer l into split-K partials; xw: the
+  // operand a is an exchange buffer delivered by the peers
+  auto gemm = [&](int k, int l, float *d, const uint16_t *a, int lda, int ldd, int splits, long long stride,
+                  const ExchangeWait *xw) -> int {
+    int N, K;
+    mat_shape(m, k, &N, &K);
+    if (w4) {
+      const QMat &q = m->qm[k == 4 ? 4 * L : 4 * l + k];
+      return gemm_w4t(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, lda, ldd, splits, stride, nullptr, 0, s, pdl,
+                      xw);
+    }
+    if (xw != nullptr) {
+      const int rc = launch_kernel(exchange_wait_kernel, dim3(1), dim3(32), 0, s, pdl, "exchange_wait_kernel", *xw,
+                                   930u + (unsigned)k);
+      if (rc) return rc;
+    }
+    const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
+                        : k == 2 ? m->w13 + l * w13_elems(m) : k == 3 ? m->w2 + l * w2_elems(m) : m->wcls;
+    return gemm_bf16_split(d, a, w, B, N, K, lda, K, ldd, splits, stride, s, pdl);
+  };
+  // residual add of the exchanged delta [batch][dim] (after its wait) or the
+  // embedding, then RMSNorm into xb
+  auto norm = [&](bool embed, const float *w, ExchangeWait xw) {
+    int lrc = CE_OK;
+    const int rc = launch_rows(m->nv, [&](auto nv) {
+      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
+                          "residual_rmsnorm_kernel", m->x, embed ? (const float *)nullptr : (const float *)m->x_delta,
+                          1, (size_t)0, embed ? (const uint16_t *)m->tok_emb : (const uint16_t *)nullptr,
+                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, 0, xw);
+    });
+    return rc ? rc : lrc;
+  };
+  // the o-projection / w2 output: split-K partials summed into this rank's
+  // columns of every rank's delta exchange
+  auto to_delta = [&](int k, int l, const uint16_t *a, int lda, const ExchangeWait &xw, int splits, int index) {
+    int rc = gemm(k, l, m->delta, a, lda, lD, splits, (long long)B * lD, &xw);
+    if (rc) return rc;
+    return launch_kernel(sum_splits_put_kernel, dim3(grid_put), dim3(256), 0, s, pdl, "sum_splits_put_kernel",
+                         (const float *)m->delta, splits, B, lD, put_of(1, 2 * L, index),
+                         m->x_off[1] + (size_t)r * lD * 4, D);
+  };
+  int rc = CE_OK;
+  switch (segment) {
+    case CE_LLAMA_SEG_ATTN: {
+      rc = norm(l == 0, m->rms_att + (size_t)l * D, l == 0 ? ExchangeWait{} : wait_of(1, 2 * L, 2 * (l - 1) + 1));
+      if (rc) return rc;
+      const size_t qkv_stride = (size_t)B * m->qkv_rows;
+      rc = gemm(0, l, m->qkv, m->xb, D, m->qkv_rows, m->sp_qkv, (long long)qkv_stride, nullptr);
+      if (rc) return rc;
+      uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
+      rc = launch_kernel(rope_append_kernel, rope_grid(lD, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel",
+                         m->qkv, m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
+                         (const int *)m->pos, lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
+      if (rc) return rc;
+      const dim3 agrid(m->attn_splits, m->lH, B);
+      const size_t smem = attn_smem_bytes(m->hs);
+      uint16_t *out = m->x_att + (size_t)r * lD;  // this rank's columns of [batch][dim]
+      auto attention = [&](auto hs_tag) {
+        constexpr int HS = decltype(hs_tag)::value;
+        return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(32), smem, s, pdl, "attn_decode_kernel",
+                             (const float *)m->qkv, m->qkv_rows, (const uint16_t *)kc, (const uint16_t *)vc,
+                             (const int *)m->pos, m->lH, m->lKH, c.seq_len, m->attn_splits, m->part, m->arrivals,
+                             out, D, (int)w4);
+      };
+      rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{}) : attention(std::integral_constant<int, 128>{});
+      if (rc) return rc;
+      return launch_kernel(exchange_put_kernel, dim3(grid_put), dim3(256), 0, s, pdl, "exchange_put_kernel",
+                           put_of(0, L, l), m->x_off[0] + (size_t)r * lD * 2, B, (size_t)lD * 2, (size_t)D * 2);
+    }
+    case CE_LLAMA_SEG_OPROJ:
+      return to_delta(1, l, m->x_att, D, wait_of(0, L, l), m->sp_o, 2 * l);
+    case CE_LLAMA_SEG_FFN_IN: {
+      rc = norm(false, m->rms_ffn + (size_t)l * D, wait_of(1, 2 * L, 2 * l));
+      if (rc) return rc;
+      const size_t h_stride = (size_t)B * 2 * lHd;
+      rc = gemm(2, l, m->h, m->xb, D, 2 * lHd, m->sp_13, (long long)h_stride, nullptr);
+      if (rc) return rc;
+      return launch_kernel(swiglu_put_kernel, dim3(grid_put), dim3(256), 0, s, pdl, "swiglu_put_kernel",
+                           (const float *)m->h, m->sp_13, h_stride, B, lHd, (int)w4, put_of(2, L, l),
+                           m->x_off[2] + (size_t)r * lHd * 2, Hd);
+    }
+    case CE_LLAMA_SEG_FFN_OUT:
+      return to_delta(3, l, m->x_hb, Hd, wait_of(2, L, l), m->sp_2, 2 * l + 1);
+    case CE_LLAMA_SEG_HEAD:
+      rc = norm(false, m->rms_final, wait_of(1, 2 * L, 2 * (L - 1) + 1));
+      if (rc) return rc;
+      rc = gemm(4, 0, m->logits, m->xb, D, m->lV, 1, 0, nullptr);
+      if (rc) return rc;
+      return launch_kernel(shard_top1_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "shard_top1_kernel",
+                           (const float *)m->logits, m->lV, r * m->lV, (float2 *)nullptr, put_of(3, 1, 0),
+                           m->x_off[3] + (size_t)r * B * 8);
+    case CE_LLAMA_SEG_PICK:
+      rc = launch_kernel(pick_top_kernel, dim3((B + 127) / 128), dim3(128), 0, s, pdl, "pick_top_kernel",
+                         (const float2 *)m->x_top, n, B, m->tokens, m->generated, m->cap, (const int *)m->step,
+                         wait_of(3, 1, 0));
+      if (rc) return rc;
+      return launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_kernel", m->pos, m->step);
+    default:
+      return set_error(CE_ERR_USAGE, format("unknown segment %d", segment));
+  }
+}
+
 int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t stream) {
   CE_REQUIRE(m != nullptr, "null model");
-  CE_REQUIRE(m->x_att && m->x_delta && m->x_hb && m->x_top, "exchange buffers are not bound");
+  CE_REQUIRE(m->p2p || (m->x_att && m->x_delta && m->x_hb && m->x_top),
+             "exchange buffers are not bound (ce_llama_bind_exchange or ce_llama_exchange_connect)");
   const ce_llama_config &c = m->c;
   CE_REQUIRE(segment == CE_LLAMA_SEG_HEAD || segment == CE_LLAMA_SEG_PICK || (layer >= 0 && layer < c.n_layers),
              "layer %d out of range", layer);
   cudaStream_t s = (cudaStream_t)stream;
+  if (m->p2p) return enqueue_segment_p2p(m, segment, layer, s);
   const int B = m->B, D = c.dim, n = m->world, r = m->rank;
   const int lD = m->lD, lHd = m->lHd;
   const bool pdl = m->pdl, w4 = m->precision == CE_PREC_NVFP4_E2M1;
@@ -1483,7 +1646,7 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
       lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
                           "residual_rmsnorm_kernel", m->x, embed ? (const float *)nullptr : (const float *)m->x_delta,
                           1, slot_d, embed ? (const uint16_t *)m->tok_emb : (const uint16_t *)nullptr,
-                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, lD);
+                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, lD, ExchangeWait{});
     });
     return rc ? rc : lrc;
   };
@@ -1499,97 +1662,66 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
                          m->x_delta + (size_t)r * slot_d, splits, n4);
   };
   const int join_grid = 2 * sm_count();
-  const int l = layer, L = c.n_layers;
-  // peer-memory exchange: put this rank's slot of kind k to every peer, and
-  // wait for every peer's slot of kind k (no-ops when the caller joins the
-  // slots with its own all-gathers)
-  const size_t kind_slot[4] = {slot_d * 2, slot_d * 4, (size_t)B * lHd * 2, (size_t)B * 8};
-  auto put = [&](int k, int per_step, int index) -> int {
-    if (!m->p2p) return CE_OK;
-    const size_t bytes = kind_slot[k];
-    const unsigned blocks = (unsigned)std::max<size_t>(1, std::min<size_t>((bytes / 16 + 255) / 256, 2 * sm_count()));
-    return launch_kernel(exchange_put_kernel, dim3(blocks), dim3(256), 0, s, pdl, "exchange_put_kernel",
-                         (uint8_t *const *)m->d_blocks, n, r, m->x_off[k] + (size_t)r * bytes, bytes,
-                         m->x_off[4] + ((size_t)k * n + r) * 8, m->x_counter, (const unsigned *)m->x_gen,
-                         (const int *)m->step, per_step, index);
-  };
-  auto wait = [&](int k, int per_step, int index) -> int {
-    if (!m->p2p) return CE_OK;
-    return launch_kernel(exchange_wait_kernel, dim3(1), dim3(32), 0, s, pdl, "exchange_wait_kernel",
-                         (const unsigned long long *)(m->x_block + m->x_off[4]) + (size_t)k * n, n, r,
-                         (const unsigned *)m->x_gen, (const int *)m->step, per_step, index, 910u + (unsigned)k);
-  };
+  const int l = layer;
   int rc = CE_OK;
   switch (segment) {
     case CE_LLAMA_SEG_ATTN: {
-      if (l > 0 && (rc = wait(1, 2 * L, 2 * (l - 1) + 1))) return rc;
       rc = norm(l == 0, m->rms_att + (size_t)l * D);
       if (rc) return rc;
       const size_t qkv_stride = (size_t)B * m->qkv_rows;
       rc = gemm(0, l, m->qkv, m->xb, m->qkv_rows, m->sp_qkv, (long long)qkv_stride, nullptr, 0);
       if (rc) return rc;
       uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
-      rc = launch_kernel(rope_append_kernel, rope_grid(lD, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
-                         m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope, (const int *)m->pos,
-                         lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
+      rc = launch_kernel(rope_append_kernel, rope_grid(lD, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel",
+                         m->qkv, m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
+                         (const int *)m->pos, lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
       if (rc) return rc;
       const dim3 agrid(m->attn_splits, m->lH, B);
       const size_t smem = attn_smem_bytes(m->hs);
       uint16_t *slot = m->x_att + (size_t)r * slot_d;
       auto attention = [&](auto hs_tag) {
         constexpr int HS = decltype(hs_tag)::value;
-        return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(32), smem, s, pdl,
-                             "attn_decode_kernel", (const float *)m->qkv, m->qkv_rows, (const uint16_t *)kc,
-                             (const uint16_t *)vc, (const int *)m->pos, m->lH, m->lKH, c.seq_len,
-                             m->attn_splits, m->part, m->arrivals, slot, lD, (int)w4);
+        return launch_kernel(attn_decode_kernel<HS>, agrid, dim3(32), smem, s, pdl, "attn_decode_kernel",
+                             (const float *)m->qkv, m->qkv_rows, (const uint16_t *)kc, (const uint16_t *)vc,
+                             (const int *)m->pos, m->lH, m->lKH, c.seq_len, m->attn_splits, m->part, m->arrivals,
+                             slot, lD, (int)w4);
       };
-      rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{})
-                       : attention(std::integral_constant<int, 128>{});
-      return rc ? rc : put(0, L, l);
+      return m->hs == 64 ? attention(std::integral_constant<int, 64>{})
+                         : attention(std::integral_constant<int, 128>{});
     }
     case CE_LLAMA_SEG_OPROJ:
-      if ((rc = wait(0, L, l))) return rc;
       rc = launch_kernel(join_shards_kernel, dim3(join_grid), dim3(256), 0, s, pdl, "join_shards_kernel",
                          (const uint16_t *)m->x_att, m->att, n, B, lD);
       if (rc) return rc;
-      rc = to_delta_slot(1, l, m->att, m->sp_o);
-      return rc ? rc : put(1, 2 * L, 2 * l);
+      return to_delta_slot(1, l, m->att, m->sp_o);
     case CE_LLAMA_SEG_FFN_IN: {
-      if ((rc = wait(1, 2 * L, 2 * l))) return rc;
       rc = norm(false, m->rms_ffn + (size_t)l * D);
       if (rc) return rc;
       uint16_t *slot = m->x_hb + (size_t)r * B * lHd;
-      if (m->sp_13 == 1) {
-        rc = gemm(2, l, nullptr, m->xb, 2 * lHd, 1, 0, slot, lHd);
-        return rc ? rc : put(2, L, l);
-      }
+      if (m->sp_13 == 1) return gemm(2, l, nullptr, m->xb, 2 * lHd, 1, 0, slot, lHd);
       const size_t h_stride = (size_t)B * 2 * lHd;
       rc = gemm(2, l, m->h, m->xb, 2 * lHd, m->sp_13, (long long)h_stride, nullptr, 0);
       if (rc) return rc;
-      rc = launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
-                         (const float *)m->h, m->sp_13, h_stride, slot, B, lHd, (int)w4);
-      return rc ? rc : put(2, L, l);
+      return launch_kernel(swiglu_kernel, dim3(4 * sm_count()), dim3(256), 0, s, pdl, "swiglu_kernel",
+                           (const float *)m->h, m->sp_13, h_stride, slot, B, lHd, (int)w4);
     }
     case CE_LLAMA_SEG_FFN_OUT:
-      if ((rc = wait(2, L, l))) return rc;
       rc = launch_kernel(join_shards_kernel, dim3(join_grid), dim3(256), 0, s, pdl, "join_shards_kernel",
                          (const uint16_t *)m->x_hb, m->hb, n, B, lHd);
       if (rc) return rc;
-      rc = to_delta_slot(3, l, m->hb, m->sp_2);
-      return rc ? rc : put(1, 2 * L, 2 * l + 1);
+      return to_delta_slot(3, l, m->hb, m->sp_2);
     case CE_LLAMA_SEG_HEAD:
-      if ((rc = wait(1, 2 * L, 2 * (L - 1) + 1))) return rc;
       rc = norm(false, m->rms_final);
       if (rc) return rc;
       rc = gemm(4, 0, m->logits, m->xb, m->lV, 1, 0, nullptr, 0);
       if (rc) return rc;
-      rc = launch_kernel(shard_top1_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "shard_top1_kernel",
-                         (const float *)m->logits, m->lV, r * m->lV, m->x_top + (size_t)r * B);
-      return rc ? rc : put(3, 1, 0);
+      return launch_kernel(shard_top1_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "shard_top1_kernel",
+                           (const float *)m->logits, m->lV, r * m->lV, m->x_top + (size_t)r * B, ExchangePut{},
+                           (size_t)0);
     case CE_LLAMA_SEG_PICK:
-      if ((rc = wait(3, 1, 0))) return rc;
       rc = launch_kernel(pick_top_kernel, dim3((B + 127) / 128), dim3(128), 0, s, pdl, "pick_top_kernel",
-                         (const float2 *)m->x_top, n, B, m->tokens, m->generated, m->cap, (const int *)m->step);
+                         (const float2 *)m->x_top, n, B, m->tokens, m->generated, m->cap, (const int *)m->step,
+                         ExchangeWait{});
       if (rc) return rc;
       return launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_kernel", m->pos, m->step);
     default:
