@@ -112,9 +112,9 @@ _SIGNATURES = {
     "ce_gemm_bf16_split": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i64, _vp],
     "ce_w4_pack": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
     "ce_gemm_w4a16": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _vp],
-    "ce_w4t_packed_bytes": [_i, _i, ctypes.POINTER(ctypes.c_size_t), ctypes.POINTER(ctypes.c_size_t)],
-    "ce_w4t_pack": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _vp],
-    "ce_gemm_w4t": [_vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i64, _vp],
+    "ce_w4t_packed_bytes": [_i, _i, ctypes.POINTER(ctypes.c_size_t)],
+    "ce_w4t_pack": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "ce_gemm_w4t": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i64, _vp],
     "ce_llama_validate": [_vp, _i, _i, _i],
     "ce_llama_create": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _vp],
     "ce_llama_destroy": [_vp],
@@ -313,25 +313,35 @@ def gemm_w4a16(d, a, codes_t, scales_t, alpha=None, n=None, stream=None):
 
 
 def w4t_packed_bytes(n, k):
-    """(codes bytes, scales bytes) of ce_w4t_pack's layout for an n x k weight."""
-    cb, sb = ctypes.c_size_t(), ctypes.c_size_t()
-    check(lib().ce_w4t_packed_bytes(n, k, ctypes.byref(cb), ctypes.byref(sb)))
-    return cb.value, sb.value
+    """Bytes of ce_w4t_pack's layout for an n x k weight."""
+    b = ctypes.c_size_t()
+    check(lib().ce_w4t_packed_bytes(n, k, ctypes.byref(b)))
+    return b.value
 
 
-def w4t_pack(codes_t, scales_t, codes, scales, n, k, stream=None):
-    """NVFP4 weights (ce_quantize_nvfp4 layout) -> the decode-form W4A16 GEMM's layout."""
-    check(lib().ce_w4t_pack(_ptr(codes_t), _ptr(scales_t), _ptr(codes), _ptr(scales), n, k,
-                            codes.shape[1], scales.shape[1], _stream(stream)))
+def w4t_pack(packed, codes, scales, n, k, stream=None):
+    """NVFP4 weights (ce_quantize_nvfp4 layout) -> the decode-form W4A16 GEMM's packed layout."""
+    check(lib().ce_w4t_pack(_ptr(packed), _ptr(codes), _ptr(scales), n, k, codes.shape[1], scales.shape[1],
+                            _stream(stream)))
 
 
-def gemm_w4t(d, a, codes_t, scales_t, alpha=None, n=None, splits=1, stream=None):
+def w4t_unpack(packed, n, k):
+    """The inverse of w4t_pack on the host: (codes uint8 [n][k/2], scales uint8 [n][k/16])."""
+    kb, npad = (k + 127) // 128, (n + 255) // 256 * 256
+    blocks = np.asarray(packed, np.uint8).reshape(kb, npad // 128, 9216)
+    codes = blocks[:, :, :8192].reshape(kb, npad // 128, 4, 4, 32, 16)
+    codes = codes.transpose(1, 2, 4, 0, 3, 5).reshape(npad, kb * 64)
+    scales = blocks[:, :, 8192:].reshape(kb, npad // 128, 4, 32, 8).transpose(1, 2, 3, 0, 4).reshape(npad, kb * 8)
+    return np.ascontiguousarray(codes[:n, :k // 2]), np.ascontiguousarray(scales[:n, :k // 16])
+
+
+def gemm_w4t(d, a, packed, alpha=None, n=None, splits=1, stream=None):
     """d [M][N] fp32 = alpha * A W^T (decode form), A fp16 bits [M][K], W packed by w4t_pack;
     with splits > 1, d is [splits][M][N] partials."""
     M, K = a.shape
     N = d.shape[-1] if n is None else n
-    check(lib().ce_gemm_w4t(_ptr(d), _ptr(a), _ptr(codes_t), _ptr(scales_t), _ptr(alpha), M, N, K, K,
-                            d.shape[-1], splits, M * d.shape[-1], _stream(stream)))
+    check(lib().ce_gemm_w4t(_ptr(d), _ptr(a), _ptr(packed), _ptr(alpha), M, N, K, K, d.shape[-1], splits,
+                            M * d.shape[-1], _stream(stream)))
     return d
 
 
@@ -671,17 +681,11 @@ class Llama:
         of one weight matrix, un-packed from the decode-form W4A16 layout
         (ce_w4t_pack)."""
         rows, cols = self._shape(which)
-        cb, sb = w4t_packed_bytes(rows, cols)
-        codes = np.empty(cb, np.uint8)
-        scales = np.empty(sb, np.uint8)
+        packed = np.empty(w4t_packed_bytes(rows, cols), np.uint8)
         alpha = np.empty(2, np.float32)
-        check(lib().ce_llama_read_nvfp4(self._h, which, layer, codes.ctypes.data, scales.ctypes.data,
-                                        alpha.ctypes.data))
-        kb, npad = (cols + 127) // 128, (rows + 255) // 256 * 256
-        codes = codes.reshape(kb, npad // 32, 4, 32, 16).transpose(1, 3, 0, 2, 4).reshape(npad, kb * 64)
-        scales = scales.reshape(kb, npad // 32, 32, 8).transpose(1, 2, 0, 3).reshape(npad, kb * 8)
-        return (np.ascontiguousarray(codes[:rows, :cols // 2]), np.ascontiguousarray(scales[:rows, :cols // 16]),
-                float(alpha[1]))
+        check(lib().ce_llama_read_nvfp4(self._h, which, layer, packed.ctypes.data, None, alpha.ctypes.data))
+        codes, scales = w4t_unpack(packed, rows, cols)
+        return codes, scales, float(alpha[1])
 
     def _shape(self, which):
         c, n = self.cfg, self.world

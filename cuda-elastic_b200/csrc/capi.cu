@@ -23,12 +23,12 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    int cols, int gemv_rows, float eps, cudaStream_t s,
                    uint8_t *normalized_e4m3 = nullptr, int ld_e4m3 = 0, float *e4m3_scale = nullptr);
 int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
-void w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes);
-int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
-             int ld_bytes, int nsf, cudaStream_t s, const int *row_map);
-int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
-             int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
-             int swiglu_ld, cudaStream_t s, bool pdl, const ExchangeWait *xw = nullptr);
+size_t w4t_packed_bytes(int N, int K);
+int w4t_pack(uint8_t *packed, const uint8_t *codes, const uint8_t *scales, int N, int K, int ld_bytes, int nsf,
+             cudaStream_t s, const int *row_map);
+int gemm_w4t(float *d, const uint16_t *a, const uint8_t *packed, const float *alpha, int M, int N, int K, int lda,
+             int ldd, int splits, long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl,
+             const ExchangeWait *xw = nullptr);
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
               cudaStream_t s, int force_group = 0);
@@ -350,20 +350,21 @@ int ce_gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uin
                     (cudaStream_t)stream, false);
 }
 
-int ce_w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes) {
+int ce_w4t_packed_bytes(int N, int K, size_t *bytes) {
   CE_REQUIRE(N >= 1 && K >= 64 && K % 64 == 0, "bad NVFP4 weight shape %dx%d", N, K);
-  w4t_packed_bytes(N, K, codes_bytes, scales_bytes);
+  CE_REQUIRE(bytes != nullptr, "null argument");
+  *bytes = w4t_packed_bytes(N, K);
   return CE_OK;
 }
 
-int ce_w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
-                int ld_bytes, int nsf, ce_stream_t stream) {
-  return w4t_pack(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf, (cudaStream_t)stream, nullptr);
+int ce_w4t_pack(uint8_t *packed, const uint8_t *codes, const uint8_t *scales, int N, int K, int ld_bytes, int nsf,
+                ce_stream_t stream) {
+  return w4t_pack(packed, codes, scales, N, K, ld_bytes, nsf, (cudaStream_t)stream, nullptr);
 }
 
-int ce_gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
-                int M, int N, int K, int lda, int ldd, int splits, int64_t split_stride, ce_stream_t stream) {
-  return gemm_w4t(d, a, codes_t, scales_t, alpha, M, N, K, lda, ldd, splits, (long long)split_stride, nullptr, 0,
+int ce_gemm_w4t(float *d, const uint16_t *a, const uint8_t *packed, const float *alpha, int M, int N, int K, int lda,
+                int ldd, int splits, int64_t split_stride, ce_stream_t stream) {
+  return gemm_w4t(d, a, packed, alpha, M, N, K, lda, ldd, splits, (long long)split_stride, nullptr, 0,
                   (cudaStream_t)stream, false);
 }
 

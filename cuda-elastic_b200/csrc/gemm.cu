@@ -1150,22 +1150,35 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
 // (the A operand of tcgen05.mma may live in TMEM), so shared memory only
 // carries the packed weights and the activation tiles. One stage covers 128
 // of K for a tile of TR weight rows (one or two M=128 halves).
-//   warp 0     weight producer: one bulk copy of the stage's codes (TR x 64
-//              bytes) and one of its scales (TR x 8 bytes), in the packed
-//              layout of w4t_pack; weights are constant, so this starts
-//              before the programmatic-launch wait;
-//   warp 1     TMEM allocator and MMA issuer (kind::f16, A from TMEM);
-//   warp 2     activation producer: two TMA boxes of 64 x NB per stage
+//   warp 0     weight producer: one bulk copy per stage of the tile's codes
+//              and scales (TR x 72 bytes, contiguous in the layout of
+//              w4t_pack: a separate small copy for the scales costs the
+//              SM's bulk-copy path as much as a large one); weights are
+//              constant, so this starts before the programmatic-launch wait;
+//   warps 1-4  MMA issuers (kind::f16, A from TMEM), each with its own
+//              accumulator: one per (128-row half, 64-wide k chunk) when the
+//              batch fits 64 columns, one per half up to 128, one in all
+//              for 128-row tiles. A tcgen05.mma costs its issuing thread
+//              ~120 cycles whatever its size at these shapes (clock-timed on
+//              B200), so several issuers multiply the rate and overlap each
+//              other's barrier waits; warp 1 also owns the TMEM allocation;
+//   warp 5     activation producer: two TMA boxes of 64 x NB per stage
 //              (first, when the activations come from the peers' exchange
 //              puts, a bounded wait on their flags);
-//   warps 4-7  epilogue (TMEM lane quarter = warp % 4): alpha x accumulator,
-//              split-K partials or the SwiGLU product;
-//   warps 8-15 converters, two per lane quarter: cvt.rn.f16x2.e2m1x2 and a
-//              half2 multiply by the UE4M3 scale, then tcgen05.st of 32
-//              columns (64 values of one row) per piece.
-// The activation slot and the TMEM stage of a stage are freed together by
-// one tcgen05.commit.
-constexpr int kW4tThreads = 16 * 32;
+//   warps 8-11 epilogue (TMEM lane quarter = warp % 4): the chunk
+//              accumulators summed in order, alpha x sum, split-K partials
+//              or the SwiGLU product;
+//   warps 12-27 converters, four per lane quarter, one (half, chunk) piece
+//              of 64 values per row each: cvt.rn.f16x2.e2m1x2 and a half2
+//              multiply by the UE4M3 scale, then tcgen05.st of 32 columns.
+// The activation slot and the TMEM stage of a stage are filled under one
+// barrier (TMA bytes + the converters' arrivals) and freed together by one
+// tcgen05.commit per issuer.
+constexpr int kW4tWarps = 28;         // roles: see gemm_w4t_kernel
+constexpr int kW4tThreads = kW4tWarps * 32;
+constexpr int kW4tConvWarps = 16;     // four per TMEM lane quarter
+constexpr int kW4tFirstConv = 12;
+constexpr int kW4tFirstEpi = 8;
 constexpr int kW4tMaxStages = 4;   // activation slots = TMEM weight stages
 constexpr int kW4tMaxWStages = 8;  // packed weight stages in shared memory
 constexpr int kW4tSmemBudget = 232448 - 1024;
@@ -1173,8 +1186,7 @@ constexpr int kW4tSmemBudget = 232448 - 1024;
 struct W4tArgs {
   float *d;
   uint16_t *swiglu_out;  // fp16 SwiGLU product [M][ld_out], or nullptr
-  const uint8_t *codes;  // [KB][Npad/32][4][32][16]
-  const uint8_t *scales; // [KB][Npad/32][32][8]
+  const uint8_t *packed; // per 128-wide k block and 128-row group: 8 KB codes + 1 KB scales (w4t_pack)
   const float *alpha;
   int M, N, K, ldd, ld_out;
   int npad;              // packed rows (multiple of 256)
@@ -1185,6 +1197,7 @@ struct W4tArgs {
   int stages, w_stages;
   int act_stage_bytes;   // 2 x nb x 128
   int acc_cols;          // TMEM columns before the weight stages
+  int issuers;           // MMA-issuing warps, each with its own accumulator (1, 2 or 4)
   ExchangeWait xw;       // activations delivered by peers' exchange puts (flags null: local)
 };
 
@@ -1234,8 +1247,8 @@ template <int TR>
 __global__ void __launch_bounds__(kW4tThreads, 1)
 gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
   constexpr int kHalves = TR / 128;
-  constexpr int kCodeBytes = TR * 64;              // 128 codes per row
-  constexpr int kStageBytes = kCodeBytes + TR * 8; // + 8 scales per row
+  constexpr int kGroupBytes = 9216;                // 128 rows: 8 KB codes + 1 KB scales
+  constexpr int kStageBytes = kHalves * kGroupBytes;
   constexpr int kStageCols = kHalves * 64;         // TMEM columns of a stage's weights
   constexpr int kPieces = kHalves * 2;             // (half, 64-wide k chunk) pieces per stage
   const int S = args.stages, SW = args.w_stages, NB = args.nb;
@@ -1259,16 +1272,17 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < SW; ++s) {
       mbar_init(&wfull[s], 1);
-      mbar_init(&wempty[s], 8);
+      mbar_init(&wempty[s], kW4tConvWarps);
     }
     for (int s = 0; s < S; ++s) {
-      mbar_init(&afull[s], 1);
-      mbar_init(&tready[s], 8);
-      mbar_init(&sempty[s], 1);
+      // stage ready: the activation producer (with the TMA bytes) and every
+      // converter arrive; the MMA issuers wait on this one barrier
+      mbar_init(&afull[s], 1 + kW4tConvWarps);
+      mbar_init(&sempty[s], args.issuers);  // one commit per MMA issuer
     }
-    mbar_init(accfull, 1);
+    mbar_init(accfull, args.issuers);
     mbar_init(accempty, 4);
-    mbar_init(drain, 1);
+    mbar_init(drain, args.issuers);
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
   }
@@ -1295,12 +1309,11 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
           okay = false;
           break;
         }
-        if (lane == 0) {
+        if (lane == 0) {  // the tile's groups are contiguous: one copy per stage
           uint8_t *dst = wring + (size_t)ws * kStageBytes;
-          const size_t rows = (size_t)kb * args.npad + row0;
+          const size_t group = (size_t)kb * (args.npad / 128) + row0 / 128;
           mbar_arrive_expect_tx(&wfull[ws], kStageBytes);
-          bulk_g2s_gemm(dst, args.codes + rows * 64, kCodeBytes, &wfull[ws]);
-          bulk_g2s_gemm(dst + kCodeBytes, args.scales + rows * 8, TR * 8, &wfull[ws]);
+          bulk_g2s_gemm(dst, args.packed + group * kGroupBytes, kStageBytes, &wfull[ws]);
         }
         __syncwarp();
         issued_mask |= 1u << ws;
@@ -1313,7 +1326,7 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
     }
     for (int s = 0; s < SW; ++s)
       if (issued_mask & (1u << s)) warp_wait(&wfull[s], (issued_parity >> s) & 1u, st, 62);
-  } else if (warp == 2) {
+  } else if (warp == 5) {
     // ---------------- activation producer
     pdl_wait();
     if (args.xw.flags != nullptr) {
@@ -1351,43 +1364,36 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
     }
     for (int s = 0; s < S; ++s)
       if (issued_mask & (1u << s)) warp_wait(&afull[s], (issued_parity >> s) & 1u, st, 64);
-  } else if (warp >= 8) {
+  } else if (warp >= kW4tFirstConv) {
     // ---------------- converters: E2M1 x UE4M3 -> fp16 pairs -> TMEM
-    const int quarter = warp & 3, pair = (warp - 8) >> 2;
+    const int quarter = warp & 3, slot = (warp - kW4tFirstConv) >> 2;  // piece `slot` of each stage
+    const bool has = slot < kPieces;
+    const int h = slot >> 1, c = slot & 1;
     int ws = 0, ts = 0;
     uint32_t wph = 0, tph = 0;
     bool okay = true;
     for (int t = blockIdx.x; t < num_units && okay; t += gridDim.x) {
       const W4tUnit w = w4t_unit(args, t);
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
-        if (!warp_wait(&wfull[ws], wph, st, 65) || !warp_wait(&sempty[ts], tph ^ 1u, st, 66)) {
+        if (!warp_wait(&wfull[ws], wph, st, 65)) {
           okay = false;
           break;
         }
-        tc_fence_after();
         const uint8_t *wsm = wring + (size_t)ws * kStageBytes;
-        uint4 cq[kPieces / 2][2];
-        uint32_t sq[kPieces / 2];
-#pragma unroll
-        for (int i = 0; i < kPieces / 2; ++i) {
-          const int p = pair + 2 * i, h = p >> 1, c = p & 1;
-          const int g = h * 4 + quarter;  // 32-row group of the tile
-          const uint4 *src = reinterpret_cast<const uint4 *>(wsm + (size_t)(g * 4 + c * 2) * 512) + lane;
-          cq[i][0] = src[0];
-          cq[i][1] = src[32];
-          sq[i] = *reinterpret_cast<const uint32_t *>(wsm + kCodeBytes + (size_t)(g * 32 + lane) * 8 + c * 4);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&wempty[ws]);
-#pragma unroll
-        for (int i = 0; i < kPieces / 2; ++i) {
-          const int p = pair + 2 * i, h = p >> 1, c = p & 1;
-          uint32_t r[32];
-          const uint32_t words[8] = {cq[i][0].x, cq[i][0].y, cq[i][0].z, cq[i][0].w,
-                                     cq[i][1].x, cq[i][1].y, cq[i][1].z, cq[i][1].w};
+        uint32_t r[32];
+        if (has) {
+          const uint8_t *grp = wsm + (size_t)h * kGroupBytes;  // this half's 128 rows
+          const uint4 *src = reinterpret_cast<const uint4 *>(grp + (size_t)(quarter * 4 + c * 2) * 512) + lane;
+          const uint4 cq0 = src[0], cq1 = src[32];
+          const uint32_t sq = *reinterpret_cast<const uint32_t *>(grp + 8192 + (size_t)(quarter * 32 + lane) * 8 + c * 4);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&wempty[ws]);
+          // convert in registers while the MMAs of earlier stages still
+          // hold this stage's TMEM columns
+          const uint32_t words[8] = {cq0.x, cq0.y, cq0.z, cq0.w, cq1.x, cq1.y, cq1.z, cq1.w};
 #pragma unroll
           for (int q = 0; q < 4; ++q) {  // 16 values (8 bytes of codes) per scale
-            const uint32_t sc = ue4m3_to_f16x2((sq[i] >> (8 * q)) & 0xFFu);
+            const uint32_t sc = ue4m3_to_f16x2((sq >> (8 * q)) & 0xFFu);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
               const uint32_t byte = (words[q * 2 + j / 4] >> (8 * (j & 3))) & 0xFFu;
@@ -1395,13 +1401,23 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
               asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r[q * 8 + j]) : "r"(v), "r"(sc));
             }
           }
+        } else {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&wempty[ws]);
+        }
+        if (!warp_wait(&sempty[ts], tph ^ 1u, st, 66)) {
+          okay = false;
+          break;
+        }
+        tc_fence_after();
+        if (has) {
           const uint32_t col = (uint32_t)args.acc_cols + (uint32_t)ts * kStageCols + h * 64 + c * 32;
           tmem_st_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + col, r);
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tready[ts]);
+        if (lane == 0) mbar_arrive(&afull[ts]);
         if (++ws == SW) {
           ws = 0;
           wph ^= 1u;
@@ -1412,9 +1428,14 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
         }
       }
     }
-  } else if (warp == 1) {
-    // ---------------- MMA issuer
+  } else if (warp >= 1 && warp <= args.issuers) {
+    // ---------------- MMA issuers (see the role list)
+    const int i = warp - 1, nis = args.issuers;
     const uint32_t idesc = (1u << 4) | ((uint32_t)(NB >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+    // issuer i: its half, its chunks [c_lo, c_hi), its accumulator
+    const int h = nis == 4 ? i >> 1 : (nis == 2 ? i : 0);
+    const int c_lo = nis == 4 ? (i & 1) : 0, c_hi = nis == 4 ? c_lo + 1 : 2;
+    const uint32_t d_tmem = tmem_base + (uint32_t)(i * NB);
     int s = 0;
     uint32_t ph = 0;
     bool okay = true;
@@ -1424,23 +1445,20 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
       tc_fence_after();
       const W4tUnit w = w4t_unit(args, t);
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
-        if (!warp_wait(&afull[s], ph, st, 68) || !warp_wait(&tready[s], ph, st, 69)) {
+        if (!warp_wait(&afull[s], ph, st, 68)) {
           okay = false;
           break;
         }
         tc_fence_after();
         if (lane == 0) {
           const uint32_t a_addr = smem_u32(act + (size_t)s * args.act_stage_bytes);
-          const uint32_t t_col = (uint32_t)args.acc_cols + (uint32_t)s * kStageCols;
-#pragma unroll
-          for (int c = 0; c < 2; ++c)
+          const uint32_t t_col = (uint32_t)args.acc_cols + (uint32_t)s * kStageCols + h * 64;
+          for (int c = c_lo; c < c_hi; ++c)
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
               const uint64_t b_desc = smem_desc_sw128(a_addr + (uint32_t)c * (args.act_stage_bytes / 2) + k * 32);
-#pragma unroll
-              for (int h = 0; h < kHalves; ++h)
-                tc_mma_ts(tmem_base + (uint32_t)(h * NB), tmem_base + t_col + h * 64 + c * 32 + k * 8, b_desc,
-                          idesc, (kb > w.kb0 || c > 0 || k > 0) ? 1u : 0u);
+              tc_mma_ts(d_tmem, tmem_base + t_col + c * 32 + k * 8, b_desc, idesc,
+                        (kb > w.kb0 || c > c_lo || k > 0) ? 1u : 0u);
             }
           tc_commit(&sempty[s]);
         }
@@ -1456,10 +1474,11 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
     if (lane == 0) tc_commit(drain);
     __syncwarp();
     warp_wait(drain, 0, st, 70);
-  } else if (warp >= 4 && warp <= 7) {
+  } else if (warp >= kW4tFirstEpi && warp < kW4tFirstEpi + 4) {
     // ---------------- epilogue
     pdl_wait();
-    const int quarter = warp & 3;
+    const int quarter = warp & 3, nis = args.issuers;
+    const int per_half = nis == 4 ? 2 : 1;  // accumulators per 128-row half (k chunks)
     const float alpha = args.alpha != nullptr ? *args.alpha : 1.0f;
     int local = 0;
     for (int t = blockIdx.x; t < num_units; t += gridDim.x, ++local) {
@@ -1470,27 +1489,37 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
 #pragma unroll
       for (int h = 0; h < kHalves; ++h) {
         const int n = w.tile_n * TR + h * 128 + quarter * 32 + lane;
-        for (int c0 = 0; c0 < NB; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(h * NB + c0), r);
+        for (int c0 = 0; c0 < NB; c0 += 16) {
+          const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+          uint32_t r[16], r2[16];
+          float v[16];
+          tmem_ld_32x32b_x16(lane_base + (uint32_t)(h * per_half * NB + c0), r);
+          if (per_half == 2)  // the second k chunk's accumulator, added in order
+            tmem_ld_32x32b_x16(lane_base + (uint32_t)((h * 2 + 1) * NB + c0), r2);
           tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+          if (per_half == 2) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(r2[j]);
+          }
           if (args.swiglu_out != nullptr) {
             // rows (2i, 2i+1) = (g_i, u_i) sit in adjacent lanes
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float v = __uint_as_float(r[j]) * alpha;
-              const float u = __shfl_xor_sync(0xffffffffu, v, 1);
+            for (int j = 0; j < 16; ++j) {
+              const float x = v[j] * alpha;
+              const float u = __shfl_xor_sync(0xffffffffu, x, 1);
               const int b = b0 + c0 + j;
-              if ((lane & 1) == 0 && n < args.N && b < args.M && c0 + j < NB) {
-                const __half hv = __float2half_rn(v / (1.0f + expf(-v)) * u);
+              if ((lane & 1) == 0 && n < args.N && b < args.M) {
+                const __half hv = __float2half_rn(x / (1.0f + expf(-x)) * u);
                 args.swiglu_out[(size_t)b * args.ld_out + n / 2] = *reinterpret_cast<const uint16_t *>(&hv);
               }
             }
           } else if (n < args.N) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
+            for (int j = 0; j < 16; ++j) {
               const int b = b0 + c0 + j;
-              if (b < args.M && c0 + j < NB) w.d[(size_t)b * args.ldd + n] = __uint_as_float(r[j]) * alpha;
+              if (b < args.M) w.d[(size_t)b * args.ldd + n] = v[j] * alpha;
             }
           }
         }
@@ -1511,20 +1540,23 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
 
 // Packs NVFP4 weights (codes [N][ld_bytes] two per byte, even index in the
 // low nibble; UE4M3 scales [N][nsf], one per 16 values) into the layout of
-// gemm_w4t_kernel: per 128-wide k block and 32-row group, the codes as four
-// 16-byte columns of 32 rows ([KB][npad/32][4][32][16]) and the scales as 32
-// rows of 8 bytes ([KB][npad/32][32][8]); rows past N and k past K are zero.
-// Output row n takes source row map[n] when map is given.
-__global__ void w4t_pack_kernel(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales,
-                                int N, int K, int ld_bytes, int nsf, int npad, int kb_total, const int *map) {
+// gemm_w4t_kernel: per 128-wide k block kb and 128-row group hg a block of
+// 9216 bytes at (kb * npad / 128 + hg) * 9216: the codes of its four 32-row
+// quarters as four 16-byte columns of 32 rows ([4][4][32][16], 8 KB) and
+// then their scales as 32 rows of 8 bytes ([4][32][8], 1 KB); rows past N
+// and k past K are zero. Output row n takes source row map[n] when map is given.
+__global__ void w4t_pack_kernel(uint8_t *packed, const uint8_t *codes, const uint8_t *scales, int N, int K,
+                                int ld_bytes, int nsf, int npad, int kb_total, const int *map) {
   const size_t total = (size_t)kb_total * npad * 4;  // one thread per 16-byte code piece
   const size_t step = (size_t)gridDim.x * blockDim.x;
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
     const int r = (int)(i % 32);
     const int j = (int)((i / 32) % 4);
-    const size_t gk = i / 128;                 // kb * (npad / 32) + group
+    const size_t gk = i / 128;                 // kb * (npad / 32) + 32-row group
     const int g = (int)(gk % (npad / 32));
     const int kb = (int)(gk / (npad / 32));
+    const int hg = g / 4, q = g % 4;
+    uint8_t *blk = packed + ((size_t)kb * (npad / 128) + hg) * 9216;
     const int n = g * 32 + r;
     const int src_row = n < N ? (map != nullptr ? map[n] : n) : -1;
     const int byte0 = kb * 64 + j * 16;        // code bytes of the piece in the source row
@@ -1533,23 +1565,23 @@ __global__ void w4t_pack_kernel(uint8_t *codes_t, uint8_t *scales_t, const uint8
       const uint8_t *p = codes + (size_t)src_row * ld_bytes + byte0;
       uint32_t w[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        w[q] = (uint32_t)p[4 * q] | ((uint32_t)p[4 * q + 1] << 8) | ((uint32_t)p[4 * q + 2] << 16) |
-               ((uint32_t)p[4 * q + 3] << 24);
+      for (int e = 0; e < 4; ++e)
+        w[e] = (uint32_t)p[4 * e] | ((uint32_t)p[4 * e + 1] << 8) | ((uint32_t)p[4 * e + 2] << 16) |
+               ((uint32_t)p[4 * e + 3] << 24);
       v = make_uint4(w[0], w[1], w[2], w[3]);
     }
-    reinterpret_cast<uint4 *>(codes_t)[i] = v;
+    *reinterpret_cast<uint4 *>(blk + (size_t)(q * 4 + j) * 512 + r * 16) = v;
     if (j == 0) {
       uint32_t lo = 0, hi = 0;
       if (src_row >= 0) {
-        const uint8_t *q = scales + (size_t)src_row * nsf + kb * 8;
+        const uint8_t *s8 = scales + (size_t)src_row * nsf + kb * 8;
         for (int e = 0; e < 8; ++e) {
-          const uint32_t b = kb * 8 + e < K / 16 ? q[e] : 0u;
+          const uint32_t b = kb * 8 + e < K / 16 ? s8[e] : 0u;
           if (e < 4) lo |= b << (8 * e);
           else hi |= b << (8 * (e - 4));
         }
       }
-      reinterpret_cast<uint2 *>(scales_t)[gk * 32 + r] = make_uint2(lo, hi);
+      *reinterpret_cast<uint2 *>(blk + 8192 + (size_t)(q * 32 + r) * 8) = make_uint2(lo, hi);
     }
   }
 }
@@ -1750,7 +1782,7 @@ int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uin
 // columns per tile (a multiple of 16, at most 256); TMEM weight stages =
 // activation slots (what TMEM and shared memory hold), packed weight stages.
 struct W4tPlan {
-  int tr, nb, tiles_b, stages, w_stages, act_stage, acc_cols;
+  int tr, nb, tiles_b, stages, w_stages, act_stage, acc_cols, issuers;
   int smem;
 };
 
@@ -1761,7 +1793,8 @@ W4tPlan w4t_plan(int M) {
   p.nb = m16 <= 256 ? m16 : 256;
   p.tiles_b = (M + p.nb - 1) / p.nb;
   const int halves = p.tr / 128;
-  p.acc_cols = (halves * p.nb + 63) / 64 * 64;
+  p.issuers = p.tr == 256 ? (p.nb <= 64 ? 4 : 2) : 1;  // one accumulator each
+  p.acc_cols = (p.issuers * p.nb + 63) / 64 * 64;
   int tstages = ((int)kTmemCols - p.acc_cols) / (halves * 64);
   if (tstages > kW4tMaxStages) tstages = kW4tMaxStages;
   p.act_stage = 2 * p.nb * kRowBytes;
@@ -1794,26 +1827,23 @@ int gemm_w4t_auto_splits(int M, int N, int K, int max_splits) {
   return best;
 }
 
-// Bytes of the packed NVFP4 weights of gemm_w4t (codes, scales) for N x K.
-void w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes) {
+// Bytes of the packed NVFP4 weights of gemm_w4t for N x K.
+size_t w4t_packed_bytes(int N, int K) {
   const size_t kb = (size_t)(K + 127) / 128, npad = (size_t)(N + 255) / 256 * 256;
-  if (codes_bytes) *codes_bytes = kb * npad * 64;
-  if (scales_bytes) *scales_bytes = kb * npad * 8;
+  return kb * (npad / 128) * 9216;
 }
 
-int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
-             int ld_bytes, int nsf, cudaStream_t s, const int *row_map) {
-  CE_REQUIRE(codes_t && scales_t && codes && scales, "null argument");
+int w4t_pack(uint8_t *packed, const uint8_t *codes, const uint8_t *scales, int N, int K, int ld_bytes, int nsf,
+             cudaStream_t s, const int *row_map) {
+  CE_REQUIRE(packed && codes && scales, "null argument");
   CE_REQUIRE(N >= 1 && K >= 64 && K % 64 == 0 && ld_bytes * 2 >= K && nsf * 16 >= K,
              "bad NVFP4 weight shape %dx%d (ld_bytes %d, scales per row %d)", N, K, ld_bytes, nsf);
-  CE_REQUIRE((reinterpret_cast<uintptr_t>(codes_t) & 15u) == 0 && (reinterpret_cast<uintptr_t>(scales_t) & 7u) == 0,
-             "packed buffers must be 16-byte (codes) and 8-byte (scales) aligned");
+  CE_REQUIRE((reinterpret_cast<uintptr_t>(packed) & 15u) == 0, "the packed buffer must be 16-byte aligned");
   const int kb_total = (K + 127) / 128, npad = (N + 255) / 256 * 256;
   const size_t pieces = (size_t)kb_total * npad * 4;
   int blocks = (int)((pieces + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  w4t_pack_kernel<<<blocks, 256, 0, s>>>(codes_t, scales_t, codes, scales, N, K, ld_bytes, nsf, npad, kb_total,
-                                         row_map);
+  w4t_pack_kernel<<<blocks, 256, 0, s>>>(packed, codes, scales, N, K, ld_bytes, nsf, npad, kb_total, row_map);
   CE_LAUNCH_CHECK("w4t_pack_kernel");
   return CE_OK;
 }
@@ -1822,15 +1852,14 @@ int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const ui
 // [M][lda] and W packed by w4t_pack; split s of `splits` k ranges writes
 // d + s * split_stride; with swiglu_out the rows of W interleave w1 and w3
 // and the fp16 SwiGLU product goes to swiglu_out [M][swiglu_ld] instead.
-int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
-             int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
-             int swiglu_ld, cudaStream_t s, bool pdl, const ExchangeWait *xw) {
+int gemm_w4t(float *d, const uint16_t *a, const uint8_t *packed, const float *alpha, int M, int N, int K, int lda,
+             int ldd, int splits, long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl,
+             const ExchangeWait *xw) {
   CE_REQUIRE(M >= 1 && N >= 1 && K >= 64 && K % 64 == 0, "W4A16 GEMM dims (M=%d N=%d K=%d; K %% 64 == 0)", M, N,
              K);
   CE_REQUIRE(lda >= K && (lda * 2) % 16 == 0, "lda must be >= K and a multiple of 8 (got %d)", lda);
-  CE_REQUIRE(a && codes_t && scales_t && (d || swiglu_out), "null operand");
-  CE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(codes_t) & 15u) == 0 &&
-                 (reinterpret_cast<uintptr_t>(scales_t) & 15u) == 0,
+  CE_REQUIRE(a && packed && (d || swiglu_out), "null operand");
+  CE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15u) == 0 && (reinterpret_cast<uintptr_t>(packed) & 15u) == 0,
              "operands must be 16-byte aligned");
   const int kb_total = (K + 127) / 128;
   CE_REQUIRE(splits >= 1 && splits <= kb_total, "split count must be in [1, %d] (got %d)", kb_total, splits);
@@ -1847,8 +1876,7 @@ int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t 
   W4tArgs w{};
   w.d = d;
   w.swiglu_out = swiglu_out;
-  w.codes = codes_t;
-  w.scales = scales_t;
+  w.packed = packed;
   w.alpha = alpha;
   w.M = M;
   w.N = N;
@@ -1866,6 +1894,7 @@ int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t 
   w.w_stages = p.w_stages;
   w.act_stage_bytes = p.act_stage;
   w.acc_cols = p.acc_cols;
+  w.issuers = p.issuers;
   if (xw != nullptr) w.xw = *xw;
   const int sms = sm_count();
   const int units = w.tiles_n * w.tiles_b * splits;

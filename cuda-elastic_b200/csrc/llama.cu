@@ -61,13 +61,13 @@ int gemm_w4a16(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_
                const float *alpha, int M, int N, int K, int lda, int ldd, int splits,
                long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
 int gemm_w4a16_auto_splits(int M, int N, int K, int max_splits, int min_kblocks);
-int gemm_w4t(float *d, const uint16_t *a, const uint8_t *codes_t, const uint8_t *scales_t, const float *alpha,
-             int M, int N, int K, int lda, int ldd, int splits, long long split_stride, uint16_t *swiglu_out,
-             int swiglu_ld, cudaStream_t s, bool pdl, const ExchangeWait *xw = nullptr);
+int gemm_w4t(float *d, const uint16_t *a, const uint8_t *packed, const float *alpha, int M, int N, int K, int lda,
+             int ldd, int splits, long long split_stride, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl,
+             const ExchangeWait *xw = nullptr);
 int gemm_w4t_auto_splits(int M, int N, int K, int max_splits);
-void w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes);
-int w4t_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
-             int ld_bytes, int nsf, cudaStream_t s, const int *row_map);
+size_t w4t_packed_bytes(int N, int K);
+int w4t_pack(uint8_t *packed, const uint8_t *codes, const uint8_t *scales, int N, int K, int ld_bytes, int nsf,
+             cudaStream_t s, const int *row_map);
 int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uint8_t *scales, int N, int K,
             int ld_bytes, int nsf, cudaStream_t s, const int *row_map = nullptr);
 int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
@@ -841,11 +841,11 @@ int pow2_at_least(int v) {
 
 using namespace ce;
 
-// One NVFP4 weight matrix in the decode-form W4A16 GEMM's layout (w4t_pack).
+// One NVFP4 weight matrix in the decode-form W4A16 GEMM's layout (w4t_pack:
+// per 128-wide k block and 128-row group, 8 KB of codes then 1 KB of scales).
 struct QMat {
-  uint8_t *codes;   // [ceil(cols/128)][roundup(rows, 256)/32][4][32][16]
-  uint8_t *scales;  // [ceil(cols/128)][roundup(rows, 256)/32][32][8]
-  size_t codes_bytes, scales_bytes;
+  uint8_t *packed;
+  size_t bytes;
   float *alpha;     // (encode, decode) tensor scales; the GEMM uses alpha[1]
   int rows, cols;
 };
@@ -1107,29 +1107,23 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
   } while (0)
   CE_ALLOC(m->tok_emb, (size_t)c.vocab_size * c.dim * 2);
   if (precision == CE_PREC_NVFP4_E2M1) {
-    size_t codes = 0, scales = 0;
+    size_t codes = 0;  // bytes of every packed weight
     const int nmat = 4 * c.n_layers + 1;
     for (int i = 0; i < nmat; ++i) {
       int r, q;
       mat_shape(m, i == 4 * c.n_layers ? 4 : i % 4, &r, &q);
-      size_t cb = 0, sb = 0;
-      w4t_packed_bytes(r, q, &cb, &sb);
-      codes += cb;
-      scales += sb;
+      codes += w4t_packed_bytes(r, q);
     }
     CE_ALLOC(m->q_codes, codes);
-    CE_ALLOC(m->q_scales, scales);
     CE_ALLOC(m->q_alpha, (size_t)nmat * 2 * 4);
-    codes = scales = 0;
+    codes = 0;
     for (int i = 0; i < nmat; ++i) {
       QMat q{};
       mat_shape(m, i == 4 * c.n_layers ? 4 : i % 4, &q.rows, &q.cols);
-      w4t_packed_bytes(q.rows, q.cols, &q.codes_bytes, &q.scales_bytes);
-      q.codes = m->q_codes + codes;
-      q.scales = m->q_scales + scales;
+      q.bytes = w4t_packed_bytes(q.rows, q.cols);
+      q.packed = m->q_codes + codes;
       q.alpha = m->q_alpha + 2 * i;
-      codes += q.codes_bytes;
-      scales += q.scales_bytes;
+      codes += q.bytes;
       m->qm.push_back(q);
     }
   } else {
@@ -1259,7 +1253,7 @@ int ce_llama_init_random(ce_llama *m, uint64_t seed, float weight_std, int kv_fi
       if (e != cudaSuccess) rc = cuda_error(e, "init_normal_f32_kernel");
       if (rc == CE_OK) rc = quantize_nvfp4(tcodes, tscales, q.alpha, amax, tmp, grows, q.cols, q.cols / 2, s);
       if (rc == CE_OK)
-        rc = w4t_pack(q.codes, q.scales, tcodes, tscales, q.rows, q.cols, q.cols / 2, q.cols / 16, s,
+        rc = w4t_pack(q.packed, tcodes, tscales, q.rows, q.cols, q.cols / 2, q.cols / 16, s,
                       d_map + k * most);
     }
     e = cudaStreamSynchronize(s);
@@ -1332,7 +1326,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     mat_shape(m, k, &N, &K);
     if (w4) {
       const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
-      return gemm_w4t(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out,
+      return gemm_w4t(d, a, q.packed, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out,
                       sw_out ? N / 2 : 0, s, pdl);
     }
     const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
@@ -1516,7 +1510,7 @@ int enqueue_segment_p2p(ce_llama *m, int segment, int l, cudaStream_t s) {
     mat_shape(m, k, &N, &K);
     if (w4) {
       const QMat &q = m->qm[k == 4 ? 4 * L : 4 * l + k];
-      return gemm_w4t(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, lda, ldd, splits, stride, nullptr, 0, s, pdl,
+      return gemm_w4t(d, a, q.packed, q.alpha + 1, B, N, K, lda, ldd, splits, stride, nullptr, 0, s, pdl,
                       xw);
     }
     if (xw != nullptr) {
@@ -1630,7 +1624,7 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
     mat_shape(m, k, &N, &K);
     if (w4) {
       const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
-      return gemm_w4t(d, a, q.codes, q.scales, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out, sw_ld, s,
+      return gemm_w4t(d, a, q.packed, q.alpha + 1, B, N, K, K, ldd, splits, stride, sw_out, sw_ld, s,
                       pdl);
     }
     const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
@@ -1760,7 +1754,7 @@ int ce_llama_read(ce_llama *m, int which, int layer, void *host, int64_t offset,
   return CE_OK;
 }
 
-int ce_llama_read_nvfp4(ce_llama *m, int which, int layer, uint8_t *codes_host, uint8_t *scales_host,
+int ce_llama_read_nvfp4(ce_llama *m, int which, int layer, uint8_t *packed_host, uint8_t *unused_host,
                         float *alpha_host) {
   CE_REQUIRE(m != nullptr, "null model");
   CE_REQUIRE(m->precision == CE_PREC_NVFP4_E2M1, "the model's weights are not NVFP4");
@@ -1770,8 +1764,8 @@ int ce_llama_read_nvfp4(ce_llama *m, int which, int layer, uint8_t *codes_host, 
   CE_REQUIRE(k == 4 || (layer >= 0 && layer < m->c.n_layers), "layer %d out of range", layer);
   const QMat &q = m->qm[k == 4 ? 4 * m->c.n_layers : 4 * layer + k];
   CE_CUDA_TRY(cudaDeviceSynchronize());
-  if (codes_host) CE_CUDA_TRY(cudaMemcpy(codes_host, q.codes, q.codes_bytes, cudaMemcpyDeviceToHost));
-  if (scales_host) CE_CUDA_TRY(cudaMemcpy(scales_host, q.scales, q.scales_bytes, cudaMemcpyDeviceToHost));
+  (void)unused_host;
+  if (packed_host) CE_CUDA_TRY(cudaMemcpy(packed_host, q.packed, q.bytes, cudaMemcpyDeviceToHost));
   if (alpha_host) CE_CUDA_TRY(cudaMemcpy(alpha_host, q.alpha, 8, cudaMemcpyDeviceToHost));
   return CE_OK;
 }

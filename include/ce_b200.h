@@ -189,17 +189,18 @@ int ce_gemm_w4a16(float *d_dev, const uint16_t *a_dev, const uint8_t *codes_t_de
                   int ldd, ce_stream_t stream);
 
 /* Bytes of the decode-form packed NVFP4 weights (ce_w4t_pack) of an N x K
- * weight: codes ceil(K/128) * roundup(N, 256) * 64, scales ceil(K/128) *
- * roundup(N, 256) * 8. Host-only. */
-int ce_w4t_packed_bytes(int N, int K, size_t *codes_bytes, size_t *scales_bytes);
+ * weight: ceil(K/128) * roundup(N, 256) / 128 * 9216. Host-only. */
+int ce_w4t_packed_bytes(int N, int K, size_t *bytes);
 
-/* Repacks NVFP4 weights (the ce_quantize_nvfp4 layout, as ce_w4_pack takes
- * them) into the decode-form layout of ce_gemm_w4t: per 128-wide k block and
- * 32-row group, codes_t [K/128][N/32][4][32][16] (four 16-byte columns of 32
- * rows) and scales_t [K/128][N/32][32][8], zero past N (rounded up to 256)
- * and past K (rounded up to 128). K % 64 == 0. Setup-time. */
-int ce_w4t_pack(uint8_t *codes_t_dev, uint8_t *scales_t_dev, const uint8_t *codes_dev,
-                const uint8_t *scales_dev, int N, int K, int ld_bytes, int nsf, ce_stream_t stream);
+/* Packs NVFP4 weights (the ce_quantize_nvfp4 layout, as ce_w4_pack takes
+ * them) into the decode-form layout of ce_gemm_w4t: per 128-wide k block kb
+ * and 128-row group hg, a block of 9216 bytes at (kb * roundup(N, 256) / 128
+ * + hg) * 9216 holding the E2M1 codes of its four 32-row quarters as four
+ * 16-byte columns of 32 rows ([4][4][32][16]) and then their UE4M3 scales
+ * as 32 rows of 8 bytes ([4][32][8]); zero past N and past K. A 256-row
+ * tile's stage is one contiguous 18 KB copy. K % 64 == 0. Setup-time. */
+int ce_w4t_pack(uint8_t *packed_dev, const uint8_t *codes_dev, const uint8_t *scales_dev, int N, int K,
+                int ld_bytes, int nsf, ce_stream_t stream);
 
 /* W4A16 GEMM, decode form: the same product as ce_gemm_w4a16 (D[m][n] =
  * alpha * sum_k A[m][k] W[n][k], A fp16 [M][lda], fp32 accumulation) with
@@ -210,9 +211,8 @@ int ce_w4t_pack(uint8_t *codes_t_dev, uint8_t *scales_t_dev, const uint8_t *code
  * d_dev + s * split_stride; the caller sums the partials in split order.
  * Replaces the NVFP4 classifier GEMM of the reference's low-precision
  * decoder (decoder_lowprec.cu:111-127), keeping the activations 16-bit. */
-int ce_gemm_w4t(float *d_dev, const uint16_t *a_dev, const uint8_t *codes_t_dev,
-                const uint8_t *scales_t_dev, const float *alpha_dev, int M, int N, int K, int lda,
-                int ldd, int splits, int64_t split_stride, ce_stream_t stream);
+int ce_gemm_w4t(float *d_dev, const uint16_t *a_dev, const uint8_t *packed_dev, const float *alpha_dev,
+                int M, int N, int K, int lda, int ldd, int splits, int64_t split_stride, ce_stream_t stream);
 
 /* Library-wide GEMM tuning, set at setup time (not during a capture): the
  * TMA producer prefetches operand tiles this many k-blocks ahead into L2
@@ -588,12 +588,13 @@ int ce_llama_write(ce_llama *model, int which, int layer, const void *host, int6
                    int64_t bytes);
 
 /* NVFP4 model only: host copies of one weight matrix (CE_LLAMA_WQKV, _WO,
- * _W13, _W2 of a layer, or _WCLS; this shard's rows) in the ce_w4t_pack
- * layout, buffer sizes from ce_w4t_packed_bytes(rows, cols); alpha =
- * (encode, decode) tensor scales; the weight is e2m1(code) * ue4m3(scale) *
+ * _W13, _W2 of a layer, or _WCLS; this shard's rows): packed_host receives
+ * it in the ce_w4t_pack layout (ce_w4t_packed_bytes(rows, cols) bytes; codes
+ * and scales together), unused_host is not written; alpha = (encode,
+ * decode) tensor scales; the weight is e2m1(code) * ue4m3(scale) *
  * alpha[1]. Any pointer may be NULL. */
-int ce_llama_read_nvfp4(ce_llama *model, int which, int layer, uint8_t *codes_host,
-                        uint8_t *scales_host, float *alpha_host);
+int ce_llama_read_nvfp4(ce_llama *model, int which, int layer, uint8_t *packed_host,
+                        uint8_t *unused_host, float *alpha_host);
 
 /* Reads and clears the decode kernels' status word: CE_OK, CE_ERR_USAGE when
  * a step ran past the end of the KV cache, CE_ERR_TIMEOUT when a staging wait

@@ -219,14 +219,12 @@ def test_gemm_w4t_decode_form(ce, O, dev, shape):
     ts = torch.empty(2, device=dev)
     scratch = torch.zeros(1, dtype=torch.int32, device=dev)
     ce.quantize_nvfp4(codes, sc, ts, scratch, torch.from_numpy(B).to(dev))
-    cb, sb = ce.w4t_packed_bytes(N, K)
-    ct = torch.full((cb,), 0xAB, dtype=torch.uint8, device=dev)
-    st = torch.full((sb,), 0xAB, dtype=torch.uint8, device=dev)
-    ce.w4t_pack(ct, st, codes, sc, N, K)
+    packed = torch.full((ce.w4t_packed_bytes(N, K),), 0xAB, dtype=torch.uint8, device=dev)
+    ce.w4t_pack(packed, codes, sc, N, K)
     a16 = A.astype(np.float16)
     da = torch.from_numpy(a16.view(np.int16)).to(dev)
     d = torch.full((splits, M, N), float("nan"), device=dev)
-    ce.gemm_w4t(d, da, ct, st, ts[1:], splits=splits)
+    ce.gemm_w4t(d, da, packed, ts[1:], splits=splits)
     ce.device_status()
     parts = d.cpu().numpy()
     out = parts[0].astype(np.float32)
@@ -239,27 +237,32 @@ def test_gemm_w4t_decode_form(ce, O, dev, shape):
 
 def test_w4t_pack_layout(ce, O, dev):
     """ce_w4t_pack against a numpy restatement of its layout: per 128-wide k
-    block and 32-row group, four 16-byte code columns of 32 rows, then 32
-    rows of 8 scale bytes; zero past N and past K."""
+    block and 128-row group, 8 KB of codes (four 32-row quarters, each four
+    16-byte columns of 32 rows) then 1 KB of scales (32 rows of 8 bytes per
+    quarter); zero past N and past K; and the host unpacking inverts it."""
     N, K = 40, 320
     rng = np.random.default_rng(3)
     codes = rng.integers(0, 256, (N, K // 2), dtype=np.uint8)
     sc = rng.integers(0, 120, (N, K // 16), dtype=np.uint8)
-    cb, sb = ce.w4t_packed_bytes(N, K)
     kb, npad = (K + 127) // 128, (N + 255) // 256 * 256
-    assert (cb, sb) == (kb * npad * 64, kb * npad * 8)
-    ct = torch.full((cb,), 0xAB, dtype=torch.uint8, device=dev)
-    st = torch.full((sb,), 0xAB, dtype=torch.uint8, device=dev)
-    ce.w4t_pack(ct, st, torch.from_numpy(codes).to(dev), torch.from_numpy(sc).to(dev), N, K)
-    ct = ct.cpu().numpy().reshape(kb, npad // 32, 4, 32, 16)
-    st = st.cpu().numpy().reshape(kb, npad // 32, 32, 8)
+    nbytes = ce.w4t_packed_bytes(N, K)
+    assert nbytes == kb * (npad // 128) * 9216
+    packed = torch.full((nbytes,), 0xAB, dtype=torch.uint8, device=dev)
+    ce.w4t_pack(packed, torch.from_numpy(codes).to(dev), torch.from_numpy(sc).to(dev), N, K)
+    got = packed.cpu().numpy().reshape(kb, npad // 128, 9216)
     cpad = np.zeros((npad, kb * 64), np.uint8)
     cpad[:N, :K // 2] = codes
     spad = np.zeros((npad, kb * 8), np.uint8)
     spad[:N, :K // 16] = sc
     for k in range(kb):
-        for g in range(npad // 32):
-            rows = slice(g * 32, g * 32 + 32)
-            for j in range(4):
-                assert np.array_equal(ct[k, g, j], cpad[rows, k * 64 + j * 16:k * 64 + j * 16 + 16])
-            assert np.array_equal(st[k, g], spad[rows, k * 8:k * 8 + 8])
+        for hg in range(npad // 128):
+            blk = got[k, hg]
+            for q in range(4):
+                rows = slice(hg * 128 + q * 32, hg * 128 + q * 32 + 32)
+                for j in range(4):
+                    piece = blk[(q * 4 + j) * 512:(q * 4 + j + 1) * 512].reshape(32, 16)
+                    assert np.array_equal(piece, cpad[rows, k * 64 + j * 16:k * 64 + j * 16 + 16])
+                srow = blk[8192 + q * 256:8192 + (q + 1) * 256].reshape(32, 8)
+                assert np.array_equal(srow, spad[rows, k * 8:k * 8 + 8])
+    c2, s2 = ce.w4t_unpack(got.ravel(), N, K)
+    assert np.array_equal(c2, codes) and np.array_equal(s2, sc)
