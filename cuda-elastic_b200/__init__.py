@@ -127,6 +127,7 @@ _SIGNATURES = {
     "ce_llama_create_shard": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _i, _i, _vp],
     "ce_llama_bind_exchange": [_vp, _vp, _vp, _vp, _vp],
     "ce_llama_exchange_open": [_vp, _vp],
+    "ce_llama_set_sampling": [_vp, _f, _f, _u64],
     "ce_llama_exchange_connect": [_vp, ctypes.c_char_p],
     "ce_llama_enqueue_segment": [_vp, _i, _i, _vp],
     "ce_llama_shard_rows": [_vp, _i, _i, _i, _vp, _vp],
@@ -698,6 +699,10 @@ class Llama:
 
     def bind_exchange(self, att, delta, hb, top):
         check(lib().ce_llama_bind_exchange(self._h, _ptr(att), _ptr(delta), _ptr(hb), _ptr(top)))
+
+    def set_sampling(self, temperature=0.0, top_p=0.0, seed=0):
+        """Greedy (temperature 0) or sampled token choice for later steps (ce_llama_set_sampling)."""
+        check(lib().ce_llama_set_sampling(self._h, float(temperature), float(top_p), int(seed)))
 
     def exchange_open(self):
         """Allocates this rank's peer-exchange block; returns its CUDA IPC handle (bytes)."""

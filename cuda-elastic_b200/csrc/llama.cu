@@ -658,6 +658,202 @@ __global__ void swiglu_put_kernel(const float *h, int nsplit, size_t split_strid
   exchange_signal(xp);
 }
 
+// --- on-device sampling --------------------------------------------------
+// The token of each row drawn from softmax(logits / temperature) with the
+// coin u = (mix64(seed ^ mix64(step * 0x9E3779B97F4A7C15 + row + 1)) >> 40)
+// / 2^24, the sampler of llama2.c restated: without top-p, the first index
+// (vocabulary order) whose cumulative probability exceeds u; with top-p in
+// (0, 1), over the 1024 most probable tokens (ties to the lower index)
+// sorted by descending probability, the nucleus is the shortest prefix
+// whose cumulative probability exceeds top_p, and the token is the first of
+// it whose cumulative probability exceeds u times the nucleus' mass. One
+// 1024-thread block per row; all reductions in a fixed order.
+constexpr int kSampleThreads = 1024;
+constexpr int kSampleCands = 1024;
+
+__device__ __forceinline__ float sample_coin(uint64_t seed, int step, int row) {
+  const uint64_t r = mix64(seed ^ mix64((uint64_t)step * 0x9E3779B97F4A7C15ull + (uint64_t)row + 1));
+  return (float)(r >> 40) * (1.0f / 16777216.0f);
+}
+
+// Block-wide sum (or max) of one value per thread, the same order every time.
+template <bool kMax>
+__device__ __forceinline__ float sample_reduce(float v, float *red) {
+  for (int off = 16; off > 0; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, v, off);
+    v = kMax ? fmaxf(v, o) : v + o;
+  }
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = red[lane];
+    for (int off = 16; off > 0; off >>= 1) {
+      const float o = __shfl_xor_sync(0xffffffffu, v, off);
+      v = kMax ? fmaxf(v, o) : v + o;
+    }
+    if (lane == 0) red[32] = v;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// Exclusive block scan of one value per thread (thread order); returns this
+// thread's prefix, and the total in *total.
+__device__ __forceinline__ float sample_scan(float v, float *red, float *total) {
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float incl = v;
+  for (int off = 1; off < 32; off <<= 1) {
+    const float o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  __syncthreads();
+  if (lane == 31) red[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    float x = red[lane], xi = x;
+    for (int off = 1; off < 32; off <<= 1) {
+      const float o = __shfl_up_sync(0xffffffffu, xi, off);
+      if (lane >= off) xi += o;
+    }
+    red[lane] = xi - x;  // exclusive prefix of the warp sums
+    if (lane == 31) red[32] = xi;
+  }
+  __syncthreads();
+  *total = red[32];
+  return red[w] + incl - v;
+}
+
+// Block count of a predicate over the row, one chunk per thread.
+__device__ __forceinline__ int sample_count(int v, int *ired) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) ired[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = ired[lane];
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0) ired[32] = v;
+  }
+  __syncthreads();
+  return ired[32];
+}
+
+__global__ void __launch_bounds__(kSampleThreads)
+sample_kernel(const float *logits, int vocab, float temperature, float top_p, uint64_t seed, int *tokens,
+              int *generated, int cap, const int *step_ptr) {
+  __shared__ float red[33];
+  __shared__ int ired[33];
+  __shared__ unsigned long long cand[kSampleCands];
+  __shared__ float cprob[kSampleCands];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const float *row = logits + (size_t)b * vocab;
+  const int chunk = (vocab + kSampleThreads - 1) / kSampleThreads;
+  const int i0 = min(vocab, tid * chunk), i1 = min(vocab, i0 + chunk);
+  const int step = *step_ptr;
+  const float u = sample_coin(seed, step, b);
+  // softmax numerators e_i = exp((l_i - max) / T)
+  float mx = -INFINITY;
+  for (int i = i0; i < i1; ++i) mx = fmaxf(mx, row[i]);
+  mx = sample_reduce<true>(mx, red);
+  const float inv_t = 1.0f / temperature;
+  float part = 0.f;
+  for (int i = i0; i < i1; ++i) part += expf((row[i] - mx) * inv_t);
+  float total = 0.f;
+  const float before = sample_scan(part, red, &total);  // prefix of the chunks in vocabulary order
+  int token = vocab - 1;
+  if (!(top_p > 0.f && top_p < 1.f)) {
+    // inverse CDF in vocabulary order: the first i with prefix_i > u * total
+    const float target = u * total;
+    int found = 0x7fffffff;
+    if (before <= target && before + part > target) {
+      float acc = before;
+      for (int i = i0; i < i1; ++i) {
+        acc += expf((row[i] - mx) * inv_t);
+        if (acc > target) {
+          found = i;
+          break;
+        }
+      }
+      if (found == 0x7fffffff) found = i1 - 1;  // the chunk's own order of additions fell short: its end
+    }
+    const int f = sample_count(found == 0x7fffffff ? 0 : found + 1, ired);  // at most one thread contributes
+    if (f > 0) token = f - 1;
+  } else {
+    // the kSampleCands largest e_i: bisection on the float bits (e_i >= 0
+    // orders like its bits) for the largest threshold with enough entries
+    const int want = min(vocab, kSampleCands);
+    uint32_t lo = 0u, hi = 0x7F800000u;  // count(bits >= lo) >= want always
+    while (lo < hi) {
+      const uint32_t mid = lo + (hi - lo + 1) / 2;
+      int c = 0;
+      for (int i = i0; i < i1; ++i) c += __float_as_uint(expf((row[i] - mx) * inv_t)) >= mid;
+      if (sample_count(c, ired) >= want) lo = mid;
+      else hi = mid - 1;
+    }
+    // above the threshold: all; at it: the lowest indices up to `want`
+    int above = 0, at = 0;
+    for (int i = i0; i < i1; ++i) {
+      const uint32_t k = __float_as_uint(expf((row[i] - mx) * inv_t));
+      above += k > lo;
+      at += k == lo;
+    }
+    const int n_above = sample_count(above, ired);
+    float at_total = 0.f;
+    const int at_before = (int)sample_scan((float)at, red, &at_total);
+    if (tid == 0) ired[32] = 0;
+    __syncthreads();
+    int taken_at = 0;
+    for (int i = i0; i < i1; ++i) {
+      const float e = expf((row[i] - mx) * inv_t);
+      const uint32_t k = __float_as_uint(e);
+      bool take = k > lo;
+      if (k == lo) take = at_before + taken_at++ < want - n_above;
+      if (take) {
+        const int slot = atomicAdd(&ired[32], 1);
+        if (slot < kSampleCands)
+          cand[slot] = ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)i);
+      }
+    }
+    __syncthreads();
+    const int n = min(ired[32], kSampleCands);
+    for (int j = n + tid; j < kSampleCands; j += kSampleThreads) cand[j] = 0ull;  // pad below every entry
+    __syncthreads();
+    // bitonic sort, descending: probability, then lower index first
+    for (int size = 2; size <= kSampleCands; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        const int j = tid ^ stride;
+        if (j > tid) {
+          const unsigned long long a = cand[tid], c = cand[j];
+          const bool desc = (tid & size) == 0;
+          if (desc ? a < c : a > c) cand[tid] = c, cand[j] = a;
+        }
+        __syncthreads();
+      }
+    }
+    const float p = tid < n ? __uint_as_float((uint32_t)(cand[tid] >> 32)) / total : 0.f;
+    float ptot = 0.f;
+    const float cum_before = sample_scan(p, red, &ptot);
+    cprob[tid] = cum_before + p;  // inclusive cumulative probability
+    __syncthreads();
+    // nucleus: the first j whose cumulative probability exceeds top_p
+    const int last = sample_count((tid < n && cum_before <= top_p && cprob[tid] > top_p) ? tid + 1 : 0, ired);
+    const int end = last > 0 ? last - 1 : n - 1;
+    const float r = u * cprob[end];
+    const int pick = sample_count((tid <= end && cum_before <= r && cprob[tid] > r) ? tid + 1 : 0, ired);
+    const int j = pick > 0 ? pick - 1 : end;
+    token = (int)(0xFFFFFFFFu - (uint32_t)(cand[j] & 0xFFFFFFFFull));
+  }
+  if (tid == 0) {
+    tokens[b] = token;
+    if (step >= 0 && step < cap) generated[(size_t)b * cap + step] = token;
+  }
+}
+
 // First maximum of each row of this shard's logits [batch][cols]: (value,
 // global index first + idx) as a float2 whose second lane holds the index
 // bits (NaN never wins; an all-NaN row gives (-inf, first)).
@@ -874,6 +1070,9 @@ struct ce_llama {
   unsigned *x_gen = nullptr;              // run generation (advanced by ce_llama_start)
   unsigned host_gen = 0;
   bool p2p = false;
+  // token choice: greedy (temperature 0) or sampled (ce_llama_set_sampling)
+  float temperature = 0.f, top_p = 0.f;
+  uint64_t seed = 0;
   int hs = 0, kv_dim = 0, qkv_rows = 0, nv = 0;
   int sp_qkv = 1, sp_o = 1, sp_13 = 1, sp_2 = 1;  // split-K counts of the layer GEMMs
   bool pdl = true;  // programmatic dependent launch between the step's kernels
@@ -1390,7 +1589,11 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
   CE_LAUNCH_CHECK("residual_rmsnorm_kernel");
   rc = gemm(4, 0, m->logits, m->xb, c.vocab_size, 1, 0, nullptr);
   if (rc) return rc;
-  rc = launch_kernel(argmax_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "argmax_kernel",
+  rc = m->temperature > 0.f
+           ? launch_kernel(sample_kernel, dim3(B), dim3(kSampleThreads), 0, s, pdl, "sample_kernel",
+                           (const float *)m->logits, c.vocab_size, m->temperature, m->top_p, m->seed, m->tokens,
+                           m->generated, m->cap, (const int *)m->step)
+           : launch_kernel(argmax_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "argmax_kernel",
                      (const float *)m->logits, c.vocab_size, m->tokens, m->generated, m->cap,
                      (const int *)m->step);
   if (rc) return rc;
@@ -1734,6 +1937,18 @@ int ce_llama_shard_rows(const ce_llama_config *cfg, int rank, int world, int whi
   shard_rows(*cfg, rank, world, k, &rows);
   if (rows_out) std::copy(rows.begin(), rows.end(), rows_out);
   *count = (int)rows.size();
+  return CE_OK;
+}
+
+int ce_llama_set_sampling(ce_llama *m, float temperature, float top_p, uint64_t seed) {
+  CE_REQUIRE(m != nullptr, "null model");
+  CE_REQUIRE(temperature >= 0.f && temperature < 1e30f, "temperature must be >= 0 (got %g)", (double)temperature);
+  CE_REQUIRE(top_p >= 0.f && top_p <= 1.f, "top_p must be in [0, 1] (got %g)", (double)top_p);
+  CE_REQUIRE(temperature == 0.f || m->world == 1,
+             "sampling needs the whole vocabulary on one GPU (a sharded model picks greedily)");
+  m->temperature = temperature;
+  m->top_p = top_p;
+  m->seed = seed;
   return CE_OK;
 }
 

@@ -575,6 +575,20 @@ int ce_llama_enqueue_segment(ce_llama *model, int segment, int layer, ce_stream_
 int ce_llama_shard_rows(const ce_llama_config *cfg, int rank, int world, int which,
                         int32_t *rows_out, int *count);
 
+/* Token choice of each step: temperature 0 (the default) picks the first
+ * maximum logit; temperature > 0 samples from softmax(logits / temperature)
+ * with the coin u = (mix64(seed ^ mix64(step * 0x9E3779B97F4A7C15 + row +
+ * 1)) >> 40) / 2^24 (splitmix64 finalizer mix64): without top-p (0 or 1) the
+ * first token in vocabulary order whose cumulative probability exceeds u;
+ * with top_p in (0, 1), among the 1024 most probable tokens (ties to the
+ * lower index) in descending order, the shortest prefix whose cumulative
+ * probability exceeds top_p, and in it the first token whose cumulative
+ * probability exceeds u times the prefix's mass (the nucleus sampler of
+ * llama2.c, which the reference's decoder names but does not carry). Takes
+ * effect for steps enqueued afterwards (a captured graph keeps the values it
+ * was captured with). Single-GPU models only. */
+int ce_llama_set_sampling(ce_llama *model, float temperature, float top_p, uint64_t seed);
+
 /* Programmatic dependent launch between the kernels of a step (default on):
  * each kernel's prologue, and the GEMMs' L2 prefetch of their first weight
  * blocks, overlap the previous kernel's tail. 0 turns it off (plain stream

@@ -174,3 +174,52 @@ def cache_from_device(model, seqs, positions):
         kc.append(k)
         vc.append(v)
     return kc, vc
+
+
+# --- sampling (the decoder's ce_llama_set_sampling) -------------------------
+# Restates the device sampler: coin from splitmix64, softmax(logits / T),
+# inverse CDF in vocabulary order, or nucleus (top-p) over the 1024 most
+# probable tokens in descending order (llama2.c's sample_mult / sample_topp).
+_M64 = (1 << 64) - 1
+SAMPLE_CANDIDATES = 1024
+
+
+def mix64(z):
+    """splitmix64 finalizer of a 64-bit integer (the device's mix64)."""
+    z = (z + 0x9E3779B97F4A7C15) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+def sample_coin(seed, step, row):
+    """u in [0, 1): (mix64(seed ^ mix64(step * 0x9E3779B97F4A7C15 + row + 1)) >> 40) / 2^24."""
+    r = mix64((seed & _M64) ^ mix64((step * 0x9E3779B97F4A7C15 + row + 1) & _M64))
+    return float(np.float32((r >> 40) * (1.0 / 16777216.0)))
+
+
+def sample_row(logits, temperature, top_p, u):
+    """(token, margin) for one row: margin is how far the coin's target lies
+    from the nearest cumulative-probability boundary of the walk (small
+    margins are where fp32 and float64 arithmetic may choose differently)."""
+    lg = np.asarray(logits, np.float64)
+    e = np.exp((lg - lg.max()) / temperature)
+    total = e.sum()
+    if not (0.0 < top_p < 1.0):
+        cdf = np.cumsum(e)
+        target = u * total
+        idx = np.nonzero(cdf > target)[0]
+        tok = int(idx[0]) if len(idx) else len(lg) - 1
+        margin = min(abs(cdf[tok] - target), abs(cdf[tok - 1] - target) if tok > 0 else np.inf) / total
+        return tok, margin
+    order = np.lexsort((np.arange(len(e)), -e))[:SAMPLE_CANDIDATES]  # descending probability, lower index first
+    p = e[order] / total
+    cum = np.cumsum(p)
+    over = np.nonzero(cum > top_p)[0]
+    end = int(over[0]) if len(over) else len(p) - 1
+    r = u * cum[end]
+    pick = np.nonzero(cum[:end + 1] > r)[0]
+    j = int(pick[0]) if len(pick) else end
+    margin = min(abs(cum[j] - r), abs(cum[j - 1] - r) if j > 0 else np.inf,
+                 abs(cum[end] - top_p), abs(cum[end - 1] - top_p) if end > 0 else np.inf)
+    return int(order[j]), margin

@@ -185,3 +185,38 @@ def test_step_past_cache_end_reports(ce):
         ce.llama_status()              # the status word was cleared
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("vocab,temperature,top_p", [(1000, 0.8, 0.0), (1000, 1.2, 0.9), (4096, 0.7, 0.8),
+                                                     (4096, 1.0, 0.95), (4096, 0.05, 0.5)])
+def test_sampling_matches_oracle_sampler(ce, vocab, temperature, top_p):
+    """On-device sampling (ce_llama_set_sampling): every step's drawn token
+    equals the oracle sampler's on the device's own logits with the same
+    coin, except where the coin's target sits within 1e-4 of a cumulative
+    boundary (fp32 against float64 arithmetic); vocabularies below and above
+    the 1024-candidate cap of the top-p path."""
+    from oracle import llama_ref
+    cfg = dict(dim=256, hidden_dim=512, n_layers=2, n_heads=4, vocab_size=vocab, seq_len=64)
+    batch, steps, seed = 48, 4, 1234
+    m = ce.Llama(cfg, batch, steps)
+    try:
+        m.init_random(seed=5, weight_std=0.08, kv_fill=10)
+        m.set_sampling(temperature, top_p, seed)
+        m.start(np.arange(batch, dtype=np.int32) * 13 % vocab, 10)
+        agree = total = 0
+        for s in range(steps):
+            m.step()
+            torch.cuda.synchronize()
+            lg = m.logits().astype(np.float64)
+            tok = m.generated()[:, s]
+            for b in range(batch):
+                want, margin = llama_ref.sample_row(lg[b], temperature, top_p, llama_ref.sample_coin(seed, s, b))
+                total += 1
+                if tok[b] == want:
+                    agree += 1
+                else:
+                    assert margin < 1e-4, (s, b, int(tok[b]), want, margin)
+        ce.llama_status()
+        assert agree >= 0.99 * total, (agree, total)
+    finally:
+        m.close()

@@ -178,3 +178,24 @@ def test_shard_memory_is_per_rank(ce):
     assert ce.lib().ce_llama_validate_shard(ctypes.byref(c), 512, 32, ce.PREC_NVFP4_E2M1, 0, 1) == ce.ERR_USAGE
     assert "GiB of device memory per GPU" in ce.last_error()[1]
     assert ce.lib().ce_llama_validate_shard(ctypes.byref(c), 64, 32, ce.PREC_NVFP4_E2M1, 0, 1) == ce.OK
+
+
+def test_sampler_restatement_properties():
+    """The oracle sampler: a near-zero temperature gives the argmax, a tiny
+    top-p gives the most probable token, the coin is reproducible, and the
+    multinomial draw follows the probabilities."""
+    rng = np.random.default_rng(11)
+    lg = rng.standard_normal(300) * 2.0
+    for step in range(5):
+        u = llama_ref.sample_coin(7, step, 3)
+        assert u == llama_ref.sample_coin(7, step, 3) and 0.0 <= u < 1.0
+        assert llama_ref.sample_row(lg, 1e-3, 0.0, u)[0] == int(np.argmax(lg))
+        assert llama_ref.sample_row(lg, 1.0, 1e-6, u)[0] == int(np.argmax(lg))
+    small = np.log(np.array([0.5, 0.3, 0.2]))
+    counts = np.zeros(3)
+    for row in range(3000):
+        counts[llama_ref.sample_row(small, 1.0, 0.0, llama_ref.sample_coin(1, 0, row))[0]] += 1
+    assert np.allclose(counts / 3000, [0.5, 0.3, 0.2], atol=0.03)
+    # top-p 0.7 keeps only the two most probable tokens of (0.5, 0.3, 0.2)
+    kept = {llama_ref.sample_row(small, 1.0, 0.7, llama_ref.sample_coin(2, 0, row))[0] for row in range(500)}
+    assert kept == {0, 1}
