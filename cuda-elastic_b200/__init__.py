@@ -75,6 +75,7 @@ _SIGNATURES = {
     "ce_softmax": [_vp, _vp, _i, _i, _vp],
     "ce_gemv": [_vp, _vp, _vp, _i, _i, _vp],
     "ce_llama2c_iteration": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _f, _vp],
+    "ce_llama2c_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _f, _vp],
     "ce_gemm_bf16": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_bf16_tile": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_tf32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
@@ -272,6 +273,18 @@ def llama2c_iteration(normalized, softmax_out, product, inp, weight, probabiliti
     check(lib().ce_llama2c_iteration(_ptr(normalized), _ptr(softmax_out), _ptr(product), _ptr(inp),
                                      _ptr(weight), _ptr(probabilities), _ptr(matrix), batch, size,
                                      rows, eps, _stream(stream)))
+
+
+def llama2c_rows(normalized, softmax_out, product, inp, weight, probabilities, matrix,
+                 rms_rows, softmax_rows, matmul_rows, eps=RMS_EPS, stream=None):
+    """Part of the llama2c iteration in one launch: rmsnorm of the first
+    rms_rows input rows, softmax of the first softmax_rows probability rows,
+    GEMV of the first matmul_rows matrix rows (any count may be 0; the
+    SOTA harness's copy-mode split, llama2c_sota.cu:447-496)."""
+    size = inp.shape[1]
+    check(lib().ce_llama2c_rows(_ptr(normalized), _ptr(softmax_out), _ptr(product), _ptr(inp),
+                                _ptr(weight), _ptr(probabilities), _ptr(matrix), size, rms_rows,
+                                softmax_rows, matmul_rows, eps, _stream(stream)))
 
 
 # ---------------------------------------------------------------------------

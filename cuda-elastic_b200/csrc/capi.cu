@@ -306,6 +306,20 @@ int ce_llama2c_iteration(float *normalized, float *softmax, float *product, cons
                         matrix, input, batch, batch, size, rows, eps, (cudaStream_t)stream);
 }
 
+int ce_llama2c_rows(float *normalized, float *softmax, float *product, const float *input,
+                    const float *weight, const float *probabilities, const float *matrix, int size,
+                    int rms_rows, int softmax_rows, int matmul_rows, float eps, ce_stream_t stream) {
+  CE_REQUIRE(size >= 1, "size must be >= 1 (got %d)", size);
+  CE_REQUIRE(rms_rows >= 0 && softmax_rows >= 0 && matmul_rows >= 0,
+             "row counts must be >= 0 (got %d, %d, %d)", rms_rows, softmax_rows, matmul_rows);
+  CE_REQUIRE(rms_rows + softmax_rows + matmul_rows > 0, "no rows to compute");
+  return rows_iteration(rms_rows ? normalized : nullptr, nullptr, 0, rms_rows ? input : nullptr,
+                        rms_rows ? weight : nullptr, softmax_rows ? softmax : nullptr,
+                        softmax_rows ? probabilities : nullptr, matmul_rows ? product : nullptr,
+                        matmul_rows ? matrix : nullptr, matmul_rows ? input : nullptr, rms_rows,
+                        softmax_rows, size, matmul_rows, eps, (cudaStream_t)stream);
+}
+
 int ce_gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
                  int ldb, int ldd, ce_stream_t stream) {
   return gemm_bf16(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, (cudaStream_t)stream);

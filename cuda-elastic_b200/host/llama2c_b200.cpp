@@ -178,27 +178,45 @@ int main(int argc, char **argv) {
   const double min_bytes = o.repeats * (2.0 * vector_bytes + o.size * 4.0 + 2.0 * vector_bytes +
                                         (double)mat * 4 + ((double)o.size + o.rows) * 4);
 
+  // Fused layout: one launch per repeat. In copy mode the last repeat is
+  // split (llama2c_sota.cu:477-496): the rmsnorm rows run alone on s0 and
+  // their copy to the host starts at once, while softmax + GEMV run as a
+  // second launch on s1 followed by their copies; s0 joins s1 before the
+  // iteration ends. Streams layout: three forked streams, one op each.
   auto enqueue_iteration = [&]() {
-    CUDA_CHECK(cudaEventRecord(fork, s0));
     if (!o.fused) {
+      CUDA_CHECK(cudaEventRecord(fork, s0));
       CUDA_CHECK(cudaStreamWaitEvent(s1, fork, 0));
       CUDA_CHECK(cudaStreamWaitEvent(s2, fork, 0));
     }
     for (int r = 0; r < o.repeats; ++r) {
-      if (o.fused) {
+      const bool last_copy = r + 1 == o.repeats && o.copy_outputs;
+      if (o.fused && !last_copy) {
         CE_CHECK(ce_llama2c_iteration(d_norm, d_softmax, d_product, d_input, d_weight, d_prob,
                                       d_matrix, o.batch, o.size, o.rows, kRmsEpsilon, c0));
+      } else if (o.fused) {
+        CUDA_CHECK(cudaEventRecord(fork, s0));
+        CUDA_CHECK(cudaStreamWaitEvent(s1, fork, 0));
+        CE_CHECK(ce_llama2c_rows(d_norm, nullptr, nullptr, d_input, d_weight, nullptr, nullptr,
+                                 o.size, o.batch, 0, 0, kRmsEpsilon, c0));
+        CUDA_CHECK(cudaMemcpyAsync(h_norm, d_norm, vec * 4, cudaMemcpyDeviceToHost, s0));
+        CE_CHECK(ce_llama2c_rows(nullptr, d_softmax, d_product, d_input, nullptr, d_prob,
+                                 d_matrix, o.size, 0, o.batch, o.rows, kRmsEpsilon, c1));
+        CUDA_CHECK(cudaMemcpyAsync(h_softmax, d_softmax, vec * 4, cudaMemcpyDeviceToHost, s1));
+        CUDA_CHECK(cudaMemcpyAsync(h_product, d_product, (size_t)o.rows * 4,
+                                   cudaMemcpyDeviceToHost, s1));
+        CUDA_CHECK(cudaEventRecord(join1, s1));
+        CUDA_CHECK(cudaStreamWaitEvent(s0, join1, 0));
       } else {
         CE_CHECK(ce_rmsnorm(d_norm, d_input, d_weight, o.batch, o.size, kRmsEpsilon, c0));
         CE_CHECK(ce_softmax(d_softmax, d_prob, o.batch, o.size, c1));
         CE_CHECK(ce_gemv(d_product, d_matrix, d_input, o.rows, o.size, c2));
-      }
-      if (r + 1 == o.repeats && o.copy_outputs) {
-        CUDA_CHECK(cudaMemcpyAsync(h_norm, d_norm, vec * 4, cudaMemcpyDeviceToHost, s0));
-        CUDA_CHECK(cudaMemcpyAsync(h_softmax, d_softmax, vec * 4, cudaMemcpyDeviceToHost,
-                                   o.fused ? s0 : s1));
-        CUDA_CHECK(cudaMemcpyAsync(h_product, d_product, (size_t)o.rows * 4, cudaMemcpyDeviceToHost,
-                                   o.fused ? s0 : s2));
+        if (last_copy) {
+          CUDA_CHECK(cudaMemcpyAsync(h_norm, d_norm, vec * 4, cudaMemcpyDeviceToHost, s0));
+          CUDA_CHECK(cudaMemcpyAsync(h_softmax, d_softmax, vec * 4, cudaMemcpyDeviceToHost, s1));
+          CUDA_CHECK(cudaMemcpyAsync(h_product, d_product, (size_t)o.rows * 4,
+                                     cudaMemcpyDeviceToHost, s2));
+        }
       }
     }
     if (!o.fused) {
@@ -208,6 +226,10 @@ int main(int argc, char **argv) {
       CUDA_CHECK(cudaStreamWaitEvent(s0, join2, 0));
     }
   };
+  // Kernel launches per iteration (llama2c_sota.cu:475-476 for the fused
+  // layout; three per repeat for the streams layout).
+  const int kernels_per_iter =
+      o.fused ? o.repeats + (o.copy_outputs ? 1 : 0) : 3 * o.repeats;
 
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
@@ -314,7 +336,7 @@ int main(int argc, char **argv) {
       submit_us / o.launches, capture_ms, instantiate_ms, upload_ms, rms_waves, softmax_waves,
       matmul_waves, min_waves, min_bytes,
       min_bytes / (per_iter * 1.0e6), valid ? 1 : 0, o.random ? "random" : "deterministic",
-      (unsigned long long)o.seed, o.fused ? "fused" : "streams", o.fused ? 1 : 3);
+      (unsigned long long)o.seed, o.fused ? "fused" : "streams", kernels_per_iter);
   if (exec) cudaGraphExecDestroy(exec);
   if (graph) cudaGraphDestroy(graph);
   cudaFreeHost(h_norm);

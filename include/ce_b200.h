@@ -129,6 +129,20 @@ int ce_llama2c_iteration(float *normalized_dev, float *softmax_dev, float *produ
                          const float *probabilities_dev, const float *matrix_dev,
                          int batch, int size, int rows, float eps, ce_stream_t stream);
 
+/* Part of the llama2c iteration in one launch: rmsnorm of the first
+ * rms_rows rows of input, softmax of the first softmax_rows rows of
+ * probabilities, GEMV of the first matmul_rows rows of matrix with input row
+ * 0; any count may be 0 (its pointers are then unused), not all three. The
+ * copy mode of the SOTA harness splits its last repeat into an rmsnorm-only
+ * launch and a softmax + GEMV launch on a second stream so the normalized
+ * copy to the host overlaps the rest. Replaces the Work split (rms_work /
+ * rest_work), llama2c/llama2c_sota.cu:82-94 and :447-496. */
+int ce_llama2c_rows(float *normalized_dev, float *softmax_dev, float *product_dev,
+                    const float *input_dev, const float *weight_dev,
+                    const float *probabilities_dev, const float *matrix_dev, int size,
+                    int rms_rows, int softmax_rows, int matmul_rows, float eps,
+                    ce_stream_t stream);
+
 /* ------------------------------------------------------------------ */
 /* Tensor-core GEMM (tcgen05 + TMEM, operands by TMA).                 */
 

@@ -70,6 +70,12 @@ def test_usage_errors_before_device_work(ce):
     assert L.ce_plan_create(__import__("ctypes").byref(h), 8, 288, 768, 9) == ce.ERR_USAGE
     assert L.ce_plan_create(__import__("ctypes").byref(h), 0, 288, 768, 2) == ce.ERR_USAGE
     assert L.ce_fill_llama2c_host(1, 1, 0, 4, 4, None, None, None, None) == ce.ERR_USAGE
+    assert L.ce_llama2c_rows(None, None, None, None, None, None, None, 16, 0, 0, 0, 1e-5,
+                             None) == ce.ERR_USAGE
+    assert "no rows" in ce.last_error()[1]
+    assert L.ce_llama2c_rows(None, None, None, None, None, None, None, 16, 4, 0, 0, 1e-5,
+                             None) == ce.ERR_USAGE
+    assert "rmsnorm needs" in ce.last_error()[1]
     with pytest.raises(ce.CeError) as e:
         ce.check(L.ce_rmsnorm(None, None, None, 1, 0, 1e-5, None))
     assert e.value.status == ce.ERR_USAGE

@@ -41,6 +41,28 @@ def test_sheet_shape_auto(inputs):
     assert 20 <= int(f["launches"]) <= 5000
 
 
+@pytest.mark.parametrize("layout", ["fused", "streams"])
+@pytest.mark.parametrize("mode", ["graph", "direct"])
+def test_copy_mode_split_equals_nocopy(O, tmp_path, layout, mode):
+    """Copy mode (the last repeat's outputs copied to the host inside every
+    iteration; the fused layout splits that repeat into an rmsnorm launch
+    and a softmax + GEMV launch on a second stream) dumps bitwise the
+    outputs of nocopy mode, and reports the reference's launch count."""
+    b, s, r, repeats = 64, 1000, 300, 3
+    out = {}
+    for copy in ("copy", "nocopy"):
+        path = str(tmp_path / f"{copy}.bin")
+        res, f = run([mode, "4", str(b), str(s), str(r), str(repeats), "1", copy, "random=6",
+                      layout, f"--dump={path}"])
+        assert res.returncode == 0, res.stderr
+        assert f["valid"] == "1" and f["layout"] == layout
+        want = (repeats + (copy == "copy")) if layout == "fused" else 3 * repeats
+        assert int(f["kernels_per_iter"]) == want
+        out[copy] = O.read_l2cdump1(path)
+    for key in ("normalized", "softmax", "product"):
+        assert np.array_equal(out["copy"][key].view(np.uint32), out["nocopy"][key].view(np.uint32))
+
+
 def test_dump_matches_oracle(O, tmp_path):
     """--dump writes L2CDUMP1 whose outputs pass the oracle and whose
     per-row tolerance and double reference equal the oracle's."""

@@ -52,6 +52,33 @@ def test_single_ops_equal_fused_launch(ce, O, dev, shape):
     assert torch.equal(n1, n2) and torch.equal(s1, s2) and torch.equal(p1, p2)
 
 
+@pytest.mark.parametrize("shape", [(8, 288, 768), (33, 1001, 77)])
+def test_partial_launches_equal_fused_launch(ce, O, dev, shape):
+    """The copy-mode split (rmsnorm rows alone, then softmax + GEMV rows in a
+    second launch on another stream) gives bitwise the fused iteration's
+    values and leaves the other outputs untouched."""
+    b, s, r = shape
+    x, p, w, m = O.llama2c_inputs(1, 5, b, s, r)
+    dx, dp, dw, dm = (torch.from_numpy(a).to(dev) for a in (x, p, w, m))
+    n1, s1, p1 = _poisoned((b, s), dev), _poisoned((b, s), dev), _poisoned((r,), dev)
+    ce.llama2c_iteration(n1, s1, p1, dx, dw, dp, dm)
+    n2, s2, p2 = _poisoned((b, s), dev), _poisoned((b, s), dev), _poisoned((r,), dev)
+    ce.llama2c_rows(n2, None, None, dx, dw, None, None, b, 0, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(n1, n2)
+    assert torch.isnan(s2).all() and torch.isnan(p2).all()
+    side = torch.cuda.Stream()
+    with torch.cuda.stream(side):
+        ce.llama2c_rows(None, s2, p2, dx, None, dp, dm, 0, b, r, stream=side)
+    torch.cuda.synchronize()
+    assert torch.equal(s1, s2) and torch.equal(p1, p2)
+    # partial row counts: only the first rows are written
+    n3 = _poisoned((b, s), dev)
+    ce.llama2c_rows(n3, None, None, dx, dw, None, None, b // 2, 0, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(n3[: b // 2], n1[: b // 2]) and torch.isnan(n3[b // 2:]).all()
+
+
 def test_deterministic_identity_gemv(ce, O, dev):
     """Known answer (llama2c_common.h:195-196): with the shifted-identity
     matrix the GEMV is a gather, product[r] == input[r % size] exactly."""
