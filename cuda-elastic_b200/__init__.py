@@ -101,6 +101,7 @@ _SIGNATURES = {
     "ce_plan_trio": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
     "ce_plan_rows": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp],
     "ce_plan_gemm": [_vp, _vp, _vp],
+    "ce_plan_operands": [_vp, _vp, _vp, _vp],
     "ce_decoder_validate": [_i64, _i64, _i64, _i64, _i],
     "ce_decoder_create": [ctypes.POINTER(_vp), _i64, _i64, _i64, _i64, _i, _vp],
     "ce_decoder_destroy": [_vp],
@@ -515,6 +516,12 @@ class Plan:
         check(lib().ce_plan_trio(self._h, _ptr(normalized), _ptr(softmax_out), _ptr(out), _ptr(x),
                                  _ptr(norm_w), _ptr(logits), eps, _stream(stream)))
         return out
+
+    def operands(self, a=None, w=None, stream=None):
+        """The GEMM operands as the tensor cores multiply them, as fp32:
+        a [batch][size] (the latest rows stage), w [rows][size]."""
+        check(lib().ce_plan_operands(self._h, _ptr(a), _ptr(w), _stream(stream)))
+        return a, w
 
 
 class Decoder:

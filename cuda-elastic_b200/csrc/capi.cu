@@ -708,6 +708,49 @@ static int plan_rows(ce_plan *p, float *normalized, float *softmax, const float 
   return CE_OK;
 }
 
+int ce_plan_operands(ce_plan *p, float *a, float *w, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr, "null plan");
+  CE_REQUIRE(w == nullptr || p->has_weights, "ce_plan_set_weights has not been called");
+  cudaStream_t s = (cudaStream_t)stream;
+  for (int which = 0; which < 2; ++which) {
+    float *out = which == 0 ? a : w;
+    if (out == nullptr) continue;
+    DequantOperand d;
+    d.rows = which == 0 ? p->batch : p->rows;
+    d.cols = p->size;
+    d.out = out;
+    d.out_ld = p->size;
+    d.data = which == 0 ? p->activations : p->weights;
+    d.ld = p->ld;
+    switch (p->precision) {
+      case CE_PREC_BF16: d.format = kOperandBF16; break;
+      case CE_PREC_FP8_E4M3:
+        d.format = kOperandE4M3;
+        d.row_scale = which == 0 ? p->a_scale : p->w_scale;
+        break;
+      case CE_PREC_MXFP6_E3M2:
+      case CE_PREC_NVFP4_E2M1: {
+        const int fmt = p->precision == CE_PREC_MXFP6_E3M2 ? 0 : 1;
+        d.format = fmt == 0 ? kOperandMXFP6 : kOperandNVFP4;
+        d.ld = fmt == 0 ? p->size : p->size / 2;
+        d.nsf = p->size / (fmt == 0 ? 32 : 16);
+        // A keeps its row-major scales; W only its atoms (grouped by the
+        // GEMM's B tile rows)
+        d.atoms = which == 1;
+        d.sf = which == 0 ? p->a_sf : p->w_atoms;
+        d.katoms = sf_katoms(fmt, p->size);
+        d.group_rows = CE_BS_TILE_N;
+        if (fmt == 1) d.tensor_decode = (which == 0 ? p->a_ts : p->w_ts) + 1;
+        break;
+      }
+      default: d.format = kOperandF32;
+    }
+    const int rc = dequant_operand(d, s);
+    if (rc) return rc;
+  }
+  return CE_OK;
+}
+
 int ce_plan_rows(ce_plan *p, float *normalized, float *softmax, const float *x,
                  const float *norm_w, const float *logits, float eps, ce_stream_t stream) {
   CE_REQUIRE(p != nullptr && x && norm_w, "null argument");

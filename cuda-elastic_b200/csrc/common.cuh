@@ -152,6 +152,24 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 // epoch before it reads. Epoch = generation << 32 | (step * per_step +
 // index + 1): the generation advances per run, the step is the device step
 // counter, so one captured graph serves every step.
+// A GEMM operand in one of the library's stored formats, for
+// dequant_operand (quant.cu), which writes it back as fp32 [rows][out_ld].
+enum OperandFormat { kOperandF32 = 0, kOperandBF16, kOperandE4M3, kOperandMXFP6, kOperandNVFP4 };
+struct DequantOperand {
+  int format = kOperandF32;
+  const void *data = nullptr;    // elements (fp32 / bf16 / E4M3) or packed bytes
+  int ld = 0;                    // row stride: elements, or bytes for MXFP6 / NVFP4
+  int rows = 0, cols = 0;
+  const float *row_scale = nullptr;     // E4M3: one fp32 per row
+  const uint8_t *sf = nullptr;          // block scales: row-major [rows][nsf] or atoms
+  bool atoms = false;
+  int nsf = 0, katoms = 0, group_rows = 0;
+  const float *tensor_decode = nullptr; // NVFP4: the decode tensor scale
+  float *out = nullptr;
+  int out_ld = 0;
+};
+int dequant_operand(const DequantOperand &d, cudaStream_t s);
+
 struct ExchangeWait {
   const unsigned long long *flags;  // this rank's flags of the exchange kind, one per sending rank; null = no wait
   const unsigned *gen;

@@ -213,6 +213,76 @@ __global__ void pack_mxfp6_kernel(uint8_t *operand, const uint8_t *codes, int ro
   }
 }
 
+// Element values of the operand formats, from their definitions (sign,
+// exponent bias, subnormals at exponent field 0): E4M3 bias 7, E3M2 bias 3,
+// E2M1 bias 1; UE8M0 = 2^(e - 127).
+__device__ __forceinline__ float e4m3_value(uint32_t c) {
+  const int e = (c >> 3) & 15, m = c & 7;
+  const float v = e == 0 ? ldexpf((float)m, -9) : ldexpf((float)(8 + m), e - 10);
+  return (c & 0x80u) ? -v : v;
+}
+__device__ __forceinline__ float e3m2_value(uint32_t c) {
+  const int e = (c >> 2) & 7, m = c & 3;
+  const float v = e == 0 ? ldexpf((float)m, -4) : ldexpf((float)(4 + m), e - 5);
+  return (c & 0x20u) ? -v : v;
+}
+__device__ __forceinline__ float e2m1_value(uint32_t c) {
+  const int e = (c >> 1) & 3, m = c & 1;
+  const float v = e == 0 ? 0.5f * (float)m : ldexpf((float)(2 + m), e - 2);
+  return (c & 0x8u) ? -v : v;
+}
+
+// Index of scale (row, column c) in the 512-byte atom layout written by
+// sf_to_atoms_kernel: the inverse of its (o -> row, column) map.
+__device__ __forceinline__ size_t atom_index(int row, int c, int katoms, int group_rows) {
+  const int atoms_per_group = (group_rows + 127) / 128;
+  const int group = row / group_rows, m = row % group_rows;
+  const int ra = group * atoms_per_group + m / 128, mm = m % 128;
+  return ((size_t)ra * katoms + c / 4) * 512 + (mm % 32) * 16 + (mm / 32) * 4 + (c % 4);
+}
+
+// One GEMM operand [rows][cols] back to fp32, value by value, as the tensor
+// cores multiply it (codes x block scale x tensor scale; bf16 widened; fp32
+// and the E4M3 row scale as stored).
+__global__ void dequant_operand_kernel(DequantOperand d) {
+  const size_t total = (size_t)d.rows * d.cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const int row = (int)(i / d.cols), col = (int)(i % d.cols);
+    const uint8_t *base = static_cast<const uint8_t *>(d.data);
+    float v = 0.f;
+    switch (d.format) {
+      case kOperandF32:
+        v = static_cast<const float *>(d.data)[(size_t)row * d.ld + col];
+        break;
+      case kOperandBF16:
+        v = __uint_as_float((uint32_t)static_cast<const uint16_t *>(d.data)[(size_t)row * d.ld + col] << 16);
+        break;
+      case kOperandE4M3:
+        v = e4m3_value(base[(size_t)row * d.ld + col]) * d.row_scale[row];
+        break;
+      case kOperandMXFP6: {
+        const uint8_t *g = base + (size_t)row * d.ld + (size_t)(col / 16) * 16;
+        const int bit = 6 * (col % 16);
+        const uint32_t pair = (uint32_t)g[bit / 8] | ((uint32_t)g[bit / 8 + 1] << 8);
+        const int c = col / 32;
+        const uint32_t sf = d.atoms ? d.sf[atom_index(row, c, d.katoms, d.group_rows)]
+                                    : d.sf[(size_t)row * d.nsf + c];
+        v = e3m2_value((pair >> (bit % 8)) & 63u) * ldexpf(1.0f, (int)sf - 127);
+        break;
+      }
+      default: {  // kOperandNVFP4
+        const uint32_t byte = base[(size_t)row * d.ld + col / 2];
+        const int c = col / 16;
+        const uint32_t sf = d.atoms ? d.sf[atom_index(row, c, d.katoms, d.group_rows)]
+                                    : d.sf[(size_t)row * d.nsf + c];
+        v = e2m1_value((col & 1) ? byte >> 4 : byte & 15u) * ue4m3_value(sf) * d.tensor_decode[0];
+      }
+    }
+    d.out[(size_t)row * d.out_ld + col] = v;
+  }
+}
+
 }  // namespace
 
 int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
@@ -274,6 +344,19 @@ int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsign
   quantize_nvfp4_kernel<<<(unsigned)((halves + 15) / 16), 256, 0, s>>>(
       codes, scales, x, encode_decode, rows, cols, ld_bytes, nblocks);
   CE_LAUNCH_CHECK("quantize_nvfp4_kernel");
+  return CE_OK;
+}
+
+int dequant_operand(const DequantOperand &d, cudaStream_t s) {
+  CE_REQUIRE(d.data && d.out && d.rows >= 1 && d.cols >= 1 && d.out_ld >= d.cols, "bad operand");
+  CE_REQUIRE(d.format != kOperandE4M3 || d.row_scale, "the E4M3 operand needs its row scales");
+  CE_REQUIRE(d.format < kOperandMXFP6 || d.sf, "a block-scaled operand needs its scales");
+  CE_REQUIRE(d.format != kOperandNVFP4 || d.tensor_decode, "the NVFP4 operand needs its tensor scale");
+  const size_t total = (size_t)d.rows * d.cols;
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  dequant_operand_kernel<<<blocks, 256, 0, s>>>(d);
+  CE_LAUNCH_CHECK("dequant_operand_kernel");
   return CE_OK;
 }
 

@@ -32,6 +32,35 @@ void for_rows(int n, F body) {
   for (auto &th : pool) th.join();
 }
 
+// The general row rules (double reference): rmsnorm 3e-4 absolute; softmax
+// 1e-3 relative + 1e-9 absolute, finite, non-negative, sum within 3e-4 of 1.
+// Returns the row's square sum through *ss_out.
+bool general_row_ok(const float *input, const float *probabilities, const float *weight,
+                    const float *normalized, const float *softmax, int size, double *ss_out) {
+  const double eps = (double)1.0e-5f;
+  double ss = 0.0, mx = -DBL_MAX;
+  for (int i = 0; i < size; ++i) {
+    ss += (double)input[i] * input[i];
+    mx = std::fmax(mx, (double)probabilities[i]);
+  }
+  *ss_out = ss;
+  const double scale = 1.0 / std::sqrt(ss / size + eps);
+  double es = 0.0;
+  for (int i = 0; i < size; ++i) es += std::exp(probabilities[i] - mx);
+  double psum = 0.0;
+  bool ok = true;
+  for (int i = 0; i < size; ++i) {
+    const double e = input[i] * scale * weight[i];
+    if (!(std::fabs(normalized[i] - e) <= 3.0e-4)) ok = false;
+    const double ep = std::exp(probabilities[i] - mx) / es;
+    const double a = softmax[i];
+    if (!(std::fabs(a - ep) <= 1.0e-9 + 1.0e-3 * ep)) ok = false;
+    if (!std::isfinite(a) || a < 0.0) ok = false;
+    psum += a;
+  }
+  return ok && std::isfinite(psum) && std::fabs(psum - 1.0) <= 3.0e-4;
+}
+
 }  // namespace
 
 Llama2cCheck validate_llama2c(bool random, const float *input, const float *probabilities,
@@ -40,31 +69,11 @@ Llama2cCheck validate_llama2c(bool random, const float *input, const float *prob
                               int rows) {
   Llama2cCheck out;
   std::vector<char> ok_rows(batch, 1);
-  const double eps = (double)1.0e-5f;
-  // General rules (double reference): rmsnorm 3e-4 absolute; softmax 1e-3
-  // relative + 1e-9 absolute, finite, non-negative, sum within 3e-4 of 1.
   for_rows(batch, [&](int b) {
     const size_t off = (size_t)b * size;
-    double ss = 0.0, mx = -DBL_MAX;
-    for (int i = 0; i < size; ++i) {
-      ss += (double)input[off + i] * input[off + i];
-      mx = std::fmax(mx, (double)probabilities[off + i]);
-    }
-    const double scale = 1.0 / std::sqrt(ss / size + eps);
-    double es = 0.0;
-    for (int i = 0; i < size; ++i) es += std::exp(probabilities[off + i] - mx);
-    double psum = 0.0;
-    bool ok = true;
-    for (int i = 0; i < size; ++i) {
-      const double e = input[off + i] * scale * weight[i];
-      if (!(std::fabs(normalized[off + i] - e) <= 3.0e-4)) ok = false;
-      const double ep = std::exp(probabilities[off + i] - mx) / es;
-      const double a = softmax[off + i];
-      if (!(std::fabs(a - ep) <= 1.0e-9 + 1.0e-3 * ep)) ok = false;
-      if (!std::isfinite(a) || a < 0.0) ok = false;
-      psum += a;
-    }
-    if (!(std::isfinite(psum) && std::fabs(psum - 1.0) <= 3.0e-4)) ok = false;
+    double ss = 0.0;
+    bool ok = general_row_ok(input + off, probabilities + off, weight, normalized + off,
+                             softmax + off, size, &ss);
     if (!random) {
       // deterministic-input rules: float rmsnorm with a double square sum,
       // softmax of the input itself, 3e-4 / 1e-3 + 1e-9, positive outputs
@@ -133,6 +142,103 @@ bool write_l2cdump1(const std::string &path, bool random, uint64_t seed, int bat
             std::fwrite(product, 4, rows, f) == (size_t)rows &&
             std::fwrite(product_tolerance.data(), 4, rows, f) == (size_t)rows &&
             std::fwrite(product_reference.data(), 8, rows, f) == (size_t)rows;
+  ok = std::fclose(f) == 0 && ok;
+  if (!ok) std::fprintf(stderr, "failed to write dump file %s\n", path.c_str());
+  return ok;
+}
+
+TrioCheck validate_trio(const float *input, const float *logits, const float *weight,
+                        const float *matrix, const float *normalized, const float *softmax,
+                        const float *out, const float *a_operand, const float *w_operand,
+                        double operand_u, int batch, int size, int rows, int max_checked) {
+  TrioCheck c;
+  std::vector<char> ok_rows(batch, 1);
+  for_rows(batch, [&](int b) {
+    const size_t off = (size_t)b * size;
+    double ss = 0.0;
+    ok_rows[b] = general_row_ok(input + off, logits + off, weight, normalized + off,
+                                softmax + off, size, &ss) ? 1 : 0;
+  });
+  const int checked = std::min(batch, max_checked);
+  for (int i = 0; i < checked; ++i)
+    c.checked_rows.push_back((int32_t)(((long long)i * batch) / checked));
+  c.out_tolerance.assign((size_t)checked * rows, 0.0f);
+  c.out_reference.assign((size_t)checked * rows, 0.0);
+  // worst-case fp32 accumulation bound gamma_K = K u / (1 - K u), u = 2^-23,
+  // of the lowprec implementation check (decoder_lowprec.cu:981-1052)
+  const double u = std::ldexp(1.0, -23);
+  const double gamma = size * u / (1.0 - size * u) + operand_u;
+  const double eps = (double)1.0e-5f;
+  std::vector<double> err2(checked, 0.0), ref2(checked, 0.0), exact_err2(checked, 0.0),
+      exact2(checked, 0.0), worst(checked, 0.0);
+  std::vector<char> ok_out(checked, 1);
+  for_rows(checked, [&](int i) {
+    const int b = c.checked_rows[i];
+    const float *a = a_operand + (size_t)b * size;
+    const float *x = input + (size_t)b * size;
+    double ss = 0.0;
+    for (int k = 0; k < size; ++k) ss += (double)x[k] * x[k];
+    const double scale = 1.0 / std::sqrt(ss / size + eps);
+    std::vector<double> xn(size);
+    for (int k = 0; k < size; ++k) xn[k] = x[k] * scale * weight[k];
+    for (int n = 0; n < rows; ++n) {
+      const float *wq = w_operand + (size_t)n * size;
+      const float *wf = matrix + (size_t)n * size;
+      double sum = 0.0, mag = 0.0, exact = 0.0;
+      for (int k = 0; k < size; ++k) {
+        const double t = (double)a[k] * wq[k];
+        sum += t;
+        mag += std::fabs(t);
+        exact += xn[k] * wf[k];
+      }
+      const double tol = gamma * mag + std::ldexp(std::fabs(sum), -22) + FLT_MIN;
+      const double got = out[(size_t)b * rows + n];
+      const double d = std::fabs(got - sum);
+      if (!(d <= tol)) ok_out[i] = 0;
+      worst[i] = std::fmax(worst[i], d / tol);
+      err2[i] += (got - sum) * (got - sum);
+      ref2[i] += sum * sum;
+      exact_err2[i] += (got - exact) * (got - exact);
+      exact2[i] += exact * exact;
+      c.out_tolerance[(size_t)i * rows + n] = (float)tol;
+      c.out_reference[(size_t)i * rows + n] = sum;
+    }
+  });
+  double e2 = 0, r2 = 0, x2 = 0, xe2 = 0;
+  for (int i = 0; i < checked; ++i) {
+    e2 += err2[i];
+    r2 += ref2[i];
+    xe2 += exact_err2[i];
+    x2 += exact2[i];
+    c.worst_ratio = std::fmax(c.worst_ratio, worst[i]);
+  }
+  c.rel_l2 = r2 > 0 ? std::sqrt(e2 / r2) : std::sqrt(e2);
+  c.rel_l2_exact = x2 > 0 ? std::sqrt(xe2 / x2) : std::sqrt(xe2);
+  c.valid = std::all_of(ok_rows.begin(), ok_rows.end(), [](char v) { return v != 0; }) &&
+            std::all_of(ok_out.begin(), ok_out.end(), [](char v) { return v != 0; }) &&
+            c.rel_l2 <= 1.0e-2;
+  return c;
+}
+
+bool write_l2cdump2(const std::string &path, uint64_t seed, int precision, int batch, int size,
+                    int rows, const float *normalized, const float *softmax, const float *out,
+                    const TrioCheck &check) {
+  std::FILE *f = std::fopen(path.c_str(), "wb");
+  if (!f) {
+    std::fprintf(stderr, "cannot open dump file %s\n", path.c_str());
+    return false;
+  }
+  const size_t vec = (size_t)batch * size, outs = (size_t)batch * rows;
+  const size_t checked = check.checked_rows.size(), ref = checked * rows;
+  const int32_t header[4] = {batch, size, rows, 2};
+  const int32_t tail[2] = {precision, (int32_t)checked};
+  bool ok = std::fwrite("L2CDUMP2", 1, 8, f) == 8 && std::fwrite(header, sizeof header, 1, f) == 1 &&
+            std::fwrite(&seed, sizeof seed, 1, f) == 1 && std::fwrite(tail, sizeof tail, 1, f) == 1 &&
+            std::fwrite(normalized, 4, vec, f) == vec && std::fwrite(softmax, 4, vec, f) == vec &&
+            std::fwrite(out, 4, outs, f) == outs &&
+            std::fwrite(check.checked_rows.data(), 4, checked, f) == checked &&
+            std::fwrite(check.out_tolerance.data(), 4, ref, f) == ref &&
+            std::fwrite(check.out_reference.data(), 8, ref, f) == ref;
   ok = std::fclose(f) == 0 && ok;
   if (!ok) std::fprintf(stderr, "failed to write dump file %s\n", path.c_str());
   return ok;

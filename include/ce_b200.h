@@ -375,6 +375,18 @@ int ce_plan_rows(ce_plan *plan, float *normalized_dev, float *softmax_dev, const
                  ce_stream_t stream);
 int ce_plan_gemm(ce_plan *plan, float *out_dev, ce_stream_t stream);
 
+/* The plan's two GEMM operands as the tensor cores multiply them, written
+ * back as fp32: a_dev [batch][size] from the operand of the latest
+ * ce_plan_rows / ce_plan_trio / ce_plan_rmsnorm_gemm on this plan, w_dev
+ * [rows][size] from the prepared weights. Each is codes x block scale x
+ * tensor scale (MXFP6: UE8M0 per 32; NVFP4: UE4M3 per 16 and the fp32
+ * decode scale), E4M3 code x row scale, bf16 widened, or the fp32 value
+ * (TF32 plans: as stored; the tensor cores read 10 of its mantissa bits).
+ * Either pointer may be NULL. The reference's implementation check computes
+ * its CPU product on the dequantized operands the same way
+ * (decoder_lowprec.cu:947-1102). Enqueue-only. */
+int ce_plan_operands(ce_plan *plan, float *a_dev, float *w_dev, ce_stream_t stream);
+
 /* rmsnorm -> bf16 tensor-core GEMM that allocates no device memory, for
  * callers that cannot call cudaMalloc: code running while a CUDA graph is
  * captured, processes whose allocator already owns the device memory, and

@@ -444,6 +444,36 @@ def read_l2cdump1(path):
     return out
 
 
+def read_l2cdump2(path):
+    """Reader of the op-trio dump L2CDUMP2 of the llama2c_b200 harness (the
+    L2CDUMP1 layout with the GEMM output out[B][R] in place of the GEMV
+    product): "L2CDUMP2", int32 batch, size, rows, inputs, uint64 seed, int32
+    precision, int32 checked C, normalized[B*S] f32, softmax[B*S] f32,
+    out[B*R] f32, checked_rows[C] i32, out_tolerance[C*R] f32,
+    out_reference[C*R] f64."""
+    with open(path, "rb") as f:
+        raw = f.read()
+    if raw[:8] != b"L2CDUMP2":
+        raise ValueError(f"{path}: not an L2CDUMP2 dump")
+    batch, size, rows, inputs = (int(v) for v in np.frombuffer(raw, np.int32, 4, 8))
+    seed = int(np.frombuffer(raw, np.uint64, 1, 24)[0])
+    precision, checked = (int(v) for v in np.frombuffer(raw, np.int32, 2, 32))
+    out = {"batch": batch, "size": size, "rows": rows, "inputs": inputs, "seed": seed,
+           "precision": precision, "checked": checked}
+    off = 40
+    for name, dt, n, shape in (("normalized", np.float32, batch * size, (batch, size)),
+                               ("softmax", np.float32, batch * size, (batch, size)),
+                               ("out", np.float32, batch * rows, (batch, rows)),
+                               ("checked_rows", np.int32, checked, (checked,)),
+                               ("out_tolerance", np.float32, checked * rows, (checked, rows)),
+                               ("out_reference", np.float64, checked * rows, (checked, rows))):
+        out[name] = np.frombuffer(raw, dt, n, off).copy().reshape(shape)
+        off += n * np.dtype(dt).itemsize
+    if off != len(raw):
+        raise ValueError(f"{path}: {len(raw) - off} trailing bytes")
+    return out
+
+
 _TABLES = {}
 _NCODES = {0: 8, 1: 32, 2: 127, 3: 255, 4: 127}   # magnitude codes per format
 _SIGN = {0: 8, 1: 32, 4: 128}
@@ -499,3 +529,22 @@ def quantize_e4m3_rows(x):
 
 def dequantize_e4m3_rows(codes, scales):
     return decode_array(4, codes) * np.asarray(scales, np.float64)[:, None]
+
+
+def dequantize_mxfp6(codes, scales):
+    """E3M2 codes [rows][cols] (one per byte) times 2^(UE8M0 - 127) of their
+    32-value block (decoder_lowprec.cu's MXFP6 mode), in double."""
+    vals = decode_array(1, codes)
+    exps = np.repeat(np.asarray(scales, np.float64) - 127.0, 32, axis=1)[:, :vals.shape[1]]
+    return vals * np.exp2(exps)
+
+
+def dequantize_nvfp4(packed, scales, cols, decode=1.0):
+    """E2M1 codes packed two per byte (even column in the low nibble) times
+    the UE4M3 scale of their 16-value block times the fp32 decode tensor
+    scale, in double."""
+    packed = np.asarray(packed, np.uint8)
+    codes = np.empty((packed.shape[0], packed.shape[1] * 2), np.uint8)
+    codes[:, 0::2], codes[:, 1::2] = packed & 0x0F, packed >> 4
+    vals = decode_array(0, codes[:, :cols])
+    return vals * np.repeat(decode_array(2, scales), 16, axis=1)[:, :cols] * float(decode)

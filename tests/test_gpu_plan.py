@@ -76,3 +76,67 @@ def test_trio_sheet_shape_bf16(ce, O, dev):
     hn = norm.cpu().numpy()[rows]
     assert np.all(np.abs(hn - en) <= 1e-5 * np.abs(en) + 1e-30)
     plan.close()
+
+
+ALL_PRECS = ["fp32", "tf32", "bf16", "fp8", "mxfp6", "nvfp4"]
+
+
+def _reconstruct(ce, O, dev, prec, X):
+    """The GEMM operand the plan forms from fp32 rows X (device), rebuilt
+    from the standalone quantizers / conversions and dequantized in the
+    oracle, rounded to fp32 once as the device does."""
+    n, s = X.shape
+    h = X.cpu().numpy()
+    if prec in ("fp32", "tf32"):
+        return h
+    if prec == "bf16":
+        return O.bf16_value(O.bf16_bits(h)).astype(np.float32)
+    if prec == "fp8":
+        codes, scales = O.quantize_e4m3_rows(h)
+        return O.dequantize_e4m3_rows(codes, scales).astype(np.float32)
+    if prec == "mxfp6":
+        c = torch.empty((n, s), dtype=torch.uint8, device=dev)
+        sc = torch.empty((n, s // 32), dtype=torch.uint8, device=dev)
+        ce.quantize_mxfp6(c, sc, X)
+        return O.dequantize_mxfp6(c.cpu().numpy(), sc.cpu().numpy()).astype(np.float32)
+    c = torch.empty((n, s // 2), dtype=torch.uint8, device=dev)
+    sc = torch.empty((n, s // 16), dtype=torch.uint8, device=dev)
+    ts = torch.empty(2, device=dev)
+    scratch = torch.zeros(1, dtype=torch.int32, device=dev)
+    ce.quantize_nvfp4(c, sc, ts, scratch, X)
+    return O.dequantize_nvfp4(c.cpu().numpy(), sc.cpu().numpy(), s,
+                              float(ts.cpu()[1])).astype(np.float32)
+
+
+@pytest.mark.parametrize("prec", ALL_PRECS)
+@pytest.mark.parametrize("shape", [(8, 384, 300), (130, 1024, 250)])
+def test_plan_operands_are_the_quantized_operands(ce, O, dev, prec, shape):
+    """ce_plan_operands returns, bit for bit, the operands the plan's GEMM
+    multiplies (the standalone quantizers are bit-exact against the
+    reference's host quantizer), and the GEMM output is within the
+    implementation-check bound of their double product."""
+    b, s, r = shape
+    pval = {"fp32": ce.PREC_FP32, "tf32": ce.PREC_TF32, "bf16": ce.PREC_BF16,
+            "fp8": ce.PREC_FP8_E4M3, "mxfp6": ce.PREC_MXFP6_E3M2, "nvfp4": ce.PREC_NVFP4_E2M1}[prec]
+    x, w, logits, W = O.trio_inputs(2, b, s, r)
+    plan = ce.Plan(b, s, r, pval)
+    dW = torch.from_numpy(W).to(dev)
+    plan.set_weights(dW)
+    dx, dw, dl = (torch.from_numpy(a).to(dev) for a in (x, w, logits))
+    norm = torch.empty((b, s), device=dev)
+    soft = torch.empty((b, s), device=dev)
+    out = torch.empty((b, r), device=dev)
+    plan.trio(norm, soft, out, dx, dw, dl)
+    a = torch.full((b, s), float("nan"), device=dev)
+    wq = torch.full((r, s), float("nan"), device=dev)
+    plan.operands(a, wq)
+    torch.cuda.synchronize()
+    ce.device_status()
+    ha, hw = a.cpu().numpy(), wq.cpu().numpy()
+    assert np.array_equal(ha.view(np.uint32), _reconstruct(ce, O, dev, prec, norm).view(np.uint32))
+    assert np.array_equal(hw.view(np.uint32), _reconstruct(ce, O, dev, prec, dW).view(np.uint32))
+    ref, mag = O.gemm_ref(ha, hw)
+    extra = 2.0 ** -9 if prec == "tf32" else 0.0
+    bound = (O.gamma_worst(s) + extra) * mag + 2.0 ** -22 * np.abs(ref) + 1e-30
+    assert np.all(np.abs(out.cpu().numpy().astype(np.float64) - ref) <= bound)
+    plan.close()
