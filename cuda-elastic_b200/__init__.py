@@ -129,6 +129,9 @@ _SIGNATURES = {
     "ce_llama_create_shard": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _i, _i, _vp],
     "ce_llama_bind_exchange": [_vp, _vp, _vp, _vp, _vp],
     "ce_llama_exchange_open": [_vp, _vp],
+    "ce_llama_prefill_reserve": [_vp, _i],
+    "ce_llama_set_prefill_attention": [_vp, _i],
+    "ce_llama_enqueue_prefill": [_vp, _vp, _i, _vp],
     "ce_llama_set_sampling": [_vp, _f, _f, _u64],
     "ce_llama_exchange_connect": [_vp, ctypes.c_char_p],
     "ce_llama_enqueue_segment": [_vp, _i, _i, _vp],
@@ -646,6 +649,22 @@ class Llama:
 
     def step(self, stream=None):
         check(lib().ce_llama_enqueue_step(self._h, _stream(stream)))
+
+    def prefill_reserve(self, max_rows):
+        """Allocates the prefill chunk workspace (max_rows = batch x positions per chunk)."""
+        check(lib().ce_llama_prefill_reserve(self._h, max_rows))
+
+    def set_prefill_attention(self, simt):
+        """Prefill attention on the SIMT kernel (True) or the tensor cores (False, default)."""
+        check(lib().ce_llama_set_prefill_attention(self._h, int(bool(simt))))
+
+    def prefill(self, prompt, stream=None):
+        """Enqueues the prefill of prompt (device int32 [batch][prompt_len])
+        at the current position; the next token is chosen from the last
+        prompt position, as a step would."""
+        import torch
+        assert prompt.dtype == torch.int32 and prompt.is_contiguous() and prompt.shape[0] == self.batch
+        check(lib().ce_llama_enqueue_prefill(self._h, _ptr(prompt), prompt.shape[1], _stream(stream)))
 
     def set_pdl(self, enable):
         check(lib().ce_llama_set_pdl(self._h, int(bool(enable))))

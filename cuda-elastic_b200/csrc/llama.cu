@@ -35,6 +35,7 @@
 // per-rank greedy candidates). The residual stream is replicated: every rank
 // adds the same gathered outputs. Each rank generates exactly its rows of
 // the same global random model, so the sharded and unsharded models agree.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -72,6 +73,8 @@ int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uin
             int ld_bytes, int nsf, cudaStream_t s, const int *row_map = nullptr);
 int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
                    const float *x, int rows, int cols, int ld_bytes, cudaStream_t s);
+int make_bf16_rows_map(CUtensorMap *map, const void *base, unsigned long long inner, unsigned long long outer,
+                       unsigned long long ld, int box_outer);
 
 static __device__ DeviceStatus g_llama_status;
 
@@ -255,25 +258,27 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
 }
 
 // RoPE on q and k (in place in the fp32 QKV rows), then k and v to the bf16
-// cache at the current position: one thread per (sequence, pair), the q
-// pairs of a row first, then its k/v pairs; grid (pair blocks, batch). rope
-// holds (cos, sin) of pos * 10000^(-2i/hs) for every position and pair index i.
+// cache: one thread per (row, pair), the q pairs of a row first, then its
+// k/v pairs; grid (pair blocks, rows). Row r belongs to sequence r / per_seq
+// at position *pos + off + r % per_seq (a decode step: per_seq 1, off 0; a
+// prefill chunk: per_seq positions of every sequence). rope holds (cos, sin)
+// of pos * 10000^(-2i/hs) for every position and pair index i.
 __global__ void __launch_bounds__(256)
 rope_append_kernel(float *qkv, int ld_qkv, int nsplit, size_t split_stride, uint16_t *kcache,
                    uint16_t *vcache, const float2 *rope, const int *pos_ptr, int dim, int kv_dim, int hs,
-                   int kv_heads, int seq_len) {
+                   int kv_heads, int seq_len, int per_seq, int off) {
   pdl_launch_dependents();
   pdl_wait();
-  const int b = blockIdx.y;
+  const int b = blockIdx.y / per_seq;
   const int p = blockIdx.x * blockDim.x + threadIdx.x;
-  const int pos = *pos_ptr;
+  const int pos = *pos_ptr + off + (int)(blockIdx.y % per_seq);
   if (pos < 0 || pos >= seq_len) {
     if (threadIdx.x == 0) report_timeout(&g_llama_status, 900u);  // position out of the cache
     return;
   }
   const int qpairs = dim / 2;
   if (p >= qpairs + kv_dim / 2) return;
-  float *row = qkv + (size_t)b * ld_qkv;
+  float *row = qkv + (size_t)blockIdx.y * ld_qkv;
   // pair i of the QKV row: its split-K partials summed in split order
   auto pair_at = [&](int i) {
     float2 v = *reinterpret_cast<const float2 *>(row + i);
@@ -510,6 +515,477 @@ attn_decode_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const u
     att[(size_t)b * dim + (size_t)h * HS + d] = (uint16_t)(r & 0xFFFFu);
   }
 }
+
+// Prefill attention: causal attention of a chunk of per_seq query positions
+// of every sequence (chunk row r = sequence r / per_seq, position *pos + off
+// + r % per_seq) over its cache, positions 0 .. the query's own (appended by
+// rope_append_kernel before this launch). One CTA per (tile of kPfQ queries,
+// head, sequence), kPfThreads threads: thread t serves query t / 8 of the
+// tile, with the keys t % 8 + 8 j of each key tile for the scores and the
+// output dimensions 4 (t % 8) + 32 i. K and V tiles of kPfK positions are
+// staged in shared memory as fp32, rows padded by 4 floats so the 16-byte
+// reads of 8 threads fall in 8 different bank groups; an online softmax per
+// query (max and sum over its 8 threads by shuffles) rescales the output
+// after each tile, s = q . k / sqrt(hs) as in the decode attention.
+constexpr int kPfQ = 16, kPfK = 64, kPfThreads = 128;
+constexpr size_t pf_smem_bytes(int hs) {
+  return ((size_t)(kPfQ + 2 * kPfK) * (hs + 4) + (size_t)kPfQ * (kPfK + 4)) * sizeof(float);
+}
+
+template <int HS>
+__global__ void __launch_bounds__(kPfThreads)
+attn_prefill_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const uint16_t *vcache,
+                    const int *pos_ptr, int off, int per_seq, int n_heads, int kv_heads, int seq_len,
+                    uint16_t *att, int dim, int f16) {
+  extern __shared__ __align__(16) float pf_smem[];
+  constexpr int LD = HS + 4, PLD = kPfK + 4, NI = HS / 32;
+  float *qs = pf_smem;         // [kPfQ][LD]
+  float *ks = qs + kPfQ * LD;  // [kPfK][LD]
+  float *vs = ks + kPfK * LD;  // [kPfK][LD]
+  float *ps = vs + kPfK * LD;  // [kPfQ][PLD]
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.z, h = blockIdx.y, c0 = blockIdx.x * kPfQ;
+  const int kvh = h / (n_heads / kv_heads);
+  const int t = threadIdx.x, qi = t >> 3, g = t & 7;
+  const int base = *pos_ptr + off;         // position of the chunk's first row
+  const int nq = min(kPfQ, per_seq - c0);  // live queries of the tile
+  const int last = base + c0 + nq - 1;     // position of its last one
+  if (base < 0 || last >= seq_len) {
+    if (t == 0) report_timeout(&g_llama_status, 901u);  // position out of the cache
+    return;
+  }
+  const float qscale = rsqrtf((float)HS);
+  for (int i = t; i < kPfQ * HS / 4; i += kPfThreads) {
+    const int r = i / (HS / 4), d4 = i % (HS / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < nq) {
+      v = *reinterpret_cast<const float4 *>(qkv + (size_t)(b * per_seq + c0 + r) * ld_qkv + h * HS + 4 * d4);
+      v.x *= qscale, v.y *= qscale, v.z *= qscale, v.w *= qscale;
+    }
+    *reinterpret_cast<float4 *>(qs + r * LD + 4 * d4) = v;
+  }
+  const int my_pos = base + c0 + qi;
+  const size_t head_off = ((size_t)b * kv_heads + kvh) * seq_len * HS;
+  const uint16_t *kh = kcache + head_off, *vh = vcache + head_off;
+  float m = -INFINITY, l = 0.f;
+  float o[NI][4];
+#pragma unroll
+  for (int i = 0; i < NI; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int k0 = 0; k0 <= last; k0 += kPfK) {
+    const int nk = min(kPfK, last + 1 - k0);
+    __syncthreads();  // the previous tile's readers are done (first time: q staged)
+    for (int i = t; i < kPfK * HS / 8; i += kPfThreads) {
+      const int r = i / (HS / 8), d8 = i % (HS / 8);
+      uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+      if (r < nk) {
+        kv = *reinterpret_cast<const uint4 *>(kh + (size_t)(k0 + r) * HS + 8 * d8);
+        vv = *reinterpret_cast<const uint4 *>(vh + (size_t)(k0 + r) * HS + 8 * d8);
+      }
+      float4 *kd = reinterpret_cast<float4 *>(ks + r * LD + 8 * d8);
+      float4 *vd = reinterpret_cast<float4 *>(vs + r * LD + 8 * d8);
+      kd[0] = make_float4(bf16_lo(kv.x), bf16_hi(kv.x), bf16_lo(kv.y), bf16_hi(kv.y));
+      kd[1] = make_float4(bf16_lo(kv.z), bf16_hi(kv.z), bf16_lo(kv.w), bf16_hi(kv.w));
+      vd[0] = make_float4(bf16_lo(vv.x), bf16_hi(vv.x), bf16_lo(vv.y), bf16_hi(vv.y));
+      vd[1] = make_float4(bf16_lo(vv.z), bf16_hi(vv.z), bf16_lo(vv.w), bf16_hi(vv.w));
+    }
+    __syncthreads();
+    float sc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < HS; d += 4) {
+      const float4 q = *reinterpret_cast<const float4 *>(qs + qi * LD + d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float4 k = *reinterpret_cast<const float4 *>(ks + (g + 8 * j) * LD + d);
+        sc[j] = fmaf(q.x, k.x, sc[j]);
+        sc[j] = fmaf(q.y, k.y, sc[j]);
+        sc[j] = fmaf(q.z, k.z, sc[j]);
+        sc[j] = fmaf(q.w, k.w, sc[j]);
+      }
+    }
+    float tmax = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int kj = g + 8 * j;
+      if (kj >= nk || k0 + kj > my_pos) sc[j] = -INFINITY;
+      tmax = fmaxf(tmax, sc[j]);
+    }
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+    const float m_new = fmaxf(m, tmax);
+    const float rescale = m_new == -INFINITY ? 1.f : expf(m - m_new);  // 0 on the first tile
+    float psum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float e = sc[j] == -INFINITY ? 0.f : expf(sc[j] - m_new);
+      ps[qi * PLD + g + 8 * j] = e;
+      psum += e;
+    }
+    psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+    psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+    psum += __shfl_xor_sync(0xffffffffu, psum, 4);
+    l = l * rescale + psum;
+    m = m_new;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) o[i][0] *= rescale, o[i][1] *= rescale, o[i][2] *= rescale, o[i][3] *= rescale;
+    __syncwarp();  // a query's weights are written and read by the 8 lanes of one warp
+    for (int k = 0; k < nk; ++k) {
+      const float pk = ps[qi * PLD + k];
+#pragma unroll
+      for (int i = 0; i < NI; ++i) {
+        const float4 v = *reinterpret_cast<const float4 *>(vs + k * LD + 4 * g + 32 * i);
+        o[i][0] = fmaf(pk, v.x, o[i][0]);
+        o[i][1] = fmaf(pk, v.y, o[i][1]);
+        o[i][2] = fmaf(pk, v.z, o[i][2]);
+        o[i][3] = fmaf(pk, v.w, o[i][3]);
+      }
+    }
+  }
+  if (qi < nq) {
+    const float inv = 1.f / l;
+    uint16_t *dst = att + (size_t)(b * per_seq + c0 + qi) * dim + h * HS;
+#pragma unroll
+    for (int i = 0; i < NI; ++i) {
+      uint2 w;
+      w.x = pack_operand(o[i][0] * inv, o[i][1] * inv, f16);
+      w.y = pack_operand(o[i][2] * inv, o[i][3] * inv, f16);
+      *reinterpret_cast<uint2 *>(dst + 4 * g + 32 * i) = w;
+    }
+  }
+}
+
+// Prefill attention on the tensor cores (the kernel the prefill runs; the
+// SIMT kernel above states the same arithmetic plainly). One CTA per (tile of
+// kFaM = 128 query positions, head, sequence), six warps:
+//   warps 0-3  one query row per thread (= its TMEM lane): stage q / sqrt(hs)
+//              as bf16 into shared memory (128-byte swizzled, K-major); per
+//              key tile read the scores row S from TMEM, mask keys past the
+//              query, online softmax (running max m, sum l of the bf16-rounded
+//              weights), rescale the output O in TMEM when m grows, write the
+//              weights P as bf16 into TMEM; at the end O / l to att;
+//   warp 4     one thread: TMA loads of the K and V tiles (kFaN = 128
+//              positions, two stages each) from the bf16 cache;
+//   warp 5     one thread issues S = Q K^T (A, B from shared memory) and
+//              O += P V (A = P from TMEM, B = V as an MN-major operand straight
+//              from its [positions][hs] cache layout); the warp zeroes the V
+//              rows past the tile's last key (uninitialized cache rows must
+//              not meet a zero weight: 0 x NaN).
+// TMEM: S fp32 [128 x 128] at column 0, P bf16 pairs at 128, O fp32 [128 x
+// hs] at kColO. Every wait is bounded; a timeout records its site and the
+// CTA drains its copies and MMAs before freeing TMEM.
+constexpr int kFaM = 128, kFaN = 128, kFaThreads = 192;
+template <int HS>
+struct FaLayout {
+  static constexpr int q_bytes = kFaM * HS * 2;   // HS / 64 blocks of [128 rows][128 B]
+  static constexpr int kv_bytes = kFaN * HS * 2;  // one K or V tile, HS / 64 boxes of [128 rows][128 B]
+  static constexpr int k_off = q_bytes;
+  static constexpr int v_off = k_off + 2 * kv_bytes;
+  static constexpr int bar_off = v_off + 2 * kv_bytes;
+  static constexpr int total = bar_off + 256 + 1024;  // barriers + TMEM holder, 1024-byte alignment slack
+  static constexpr uint32_t tmem_cols = HS == 64 ? 256 : 512;
+  static constexpr uint32_t col_o = HS == 64 ? 192 : 256;
+};
+
+template <int HS>
+__global__ void __launch_bounds__(kFaThreads, 1)
+attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                       const float *qkv, int ld_qkv, const int *pos_ptr, int off, int per_seq, int n_heads,
+                       int kv_heads, int seq_len, long long layer_row, uint16_t *att, int dim, int f16) {
+  using Lay = FaLayout<HS>;
+  constexpr int KB = HS / 64;
+  constexpr uint32_t kColS = 0, kColP = 128, kColO = Lay::col_o;
+  extern __shared__ uint8_t fa_raw[];
+  uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t *qs = sm, *ks = sm + Lay::k_off, *vs = sm + Lay::v_off;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sm + Lay::bar_off);
+  uint64_t *kfull = bars, *vfull = bars + 2, *kempty = bars + 4, *vempty = bars + 6;
+  uint64_t *q_ready = bars + 8, *s_full = bars + 9, *s_free = bars + 10, *p_full = bars + 11,
+           *o_ready = bars + 12, *done = bars + 13;
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 16);
+  __shared__ int abort_flag;
+  pdl_launch_dependents();
+  pdl_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.z, h = blockIdx.y, c0 = blockIdx.x * kFaM;
+  const int kvh = h / (n_heads / kv_heads);
+  const int base = *pos_ptr + off;
+  const int nq = min(kFaM, per_seq - c0);
+  const int first = base + c0, last = first + nq - 1;
+  if (base < 0 || last >= seq_len) {
+    if (threadIdx.x == 0) report_timeout(&g_llama_status, 901u);  // position out of the cache
+    return;
+  }
+  const int ntiles = last / kFaN + 1;
+  const int nk_last = last + 1 - (ntiles - 1) * kFaN;  // keys of the last tile
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) mbar_init(bars + i, 1);
+    mbar_init(q_ready, 4);
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
+    mbar_init(p_full, 4);
+    mbar_init(o_ready, 1);
+    mbar_init(done, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_holder, Lay::tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  volatile int *abort_v = &abort_flag;
+  // warp-uniform: every lane of the warp takes the same branch
+  auto aborted = [&]() { return __any_sync(0xffffffffu, *abort_v != 0) != 0; };
+
+  if (warp < 4) {
+    const int r = threadIdx.x;
+    {  // Q tile
+      const float qscale = rsqrtf((float)HS);
+      const float *qrow = qkv + (size_t)(b * per_seq + c0 + r) * ld_qkv + h * HS;
+#pragma unroll
+      for (int kb = 0; kb < KB; ++kb)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+          if (r < nq) {
+            x0 = *reinterpret_cast<const float4 *>(qrow + kb * 64 + c * 8);
+            x1 = *reinterpret_cast<const float4 *>(qrow + kb * 64 + c * 8 + 4);
+          }
+          uint4 v;
+          v.x = pack_bf16x2(x0.x * qscale, x0.y * qscale);
+          v.y = pack_bf16x2(x0.z * qscale, x0.w * qscale);
+          v.z = pack_bf16x2(x1.x * qscale, x1.y * qscale);
+          v.w = pack_bf16x2(x1.z * qscale, x1.w * qscale);
+          *reinterpret_cast<uint4 *>(qs + kb * (kFaM * 128) + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+        }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    const int qpos = first + r;
+    const uint32_t lanes = (uint32_t)(warp * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      ok = warp_wait(s_full, j & 1, &g_llama_status, 910u) && !aborted();
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[kFaN];
+#pragma unroll
+      for (int q = 0; q < kFaN / 32; ++q)
+        tmem_ld_32x32b_x32(tbase + lanes + kColS + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(sv + 32 * q));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      const int k0 = j * kFaN;
+      const int kmax = min(qpos, last) - k0;  // last valid column of this row
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kFaN; ++i) {
+        const float sc = i <= kmax ? __uint_as_float(sv[i]) : -INFINITY;
+        sv[i] = __float_as_uint(sc);
+        tmax = fmaxf(tmax, sc);
+      }
+      const float m_new = fmaxf(m, tmax);
+      const float alpha = m == -INFINITY ? 0.f : expf(m - m_new);
+      float rs = 0.f;
+      uint32_t pk[kFaN / 2];
+#pragma unroll
+      for (int i = 0; i < kFaN / 2; ++i) {
+        const float s0 = __uint_as_float(sv[2 * i]), s1 = __uint_as_float(sv[2 * i + 1]);
+        const float e0 = s0 == -INFINITY ? 0.f : expf(s0 - m_new);
+        const float e1 = s1 == -INFINITY ? 0.f : expf(s1 - m_new);
+        pk[i] = pack_bf16x2(e0, e1);
+        rs += bf16_lo(pk[i]) + bf16_hi(pk[i]);
+      }
+      l = l * alpha + rs;
+      m = m_new;
+      if (j > 0) {  // O and P are free once the previous tile's O += P V is done
+        ok = warp_wait(o_ready, (j - 1) & 1, &g_llama_status, 911u) && !aborted();
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+#pragma unroll
+          for (int q = 0; q < HS / 32; ++q) {
+            uint32_t ov[32];
+            tmem_ld_32x32b_x32(tbase + lanes + kColO + 32 * q, ov);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+            tmem_st_32x32b_x32(tbase + lanes + kColO + 32 * q, ov);
+          }
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < kFaN / 64; ++q)
+        tmem_st_32x32b_x32(tbase + lanes + kColP + 32 * q, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32 * q));
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    if (!ok) *abort_v = 1;
+    if (ok && warp_wait(o_ready, (ntiles - 1) & 1, &g_llama_status, 912u)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      uint16_t *dst = att + (size_t)(b * per_seq + c0 + r) * dim + h * HS;
+#pragma unroll
+      for (int q = 0; q < HS / 32; ++q) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(tbase + lanes + kColO + 32 * q, ov);
+        tmem_ld_wait();
+        if (r < nq) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 8) {
+            uint4 w;
+            w.x = pack_operand(__uint_as_float(ov[i]) * inv, __uint_as_float(ov[i + 1]) * inv, f16);
+            w.y = pack_operand(__uint_as_float(ov[i + 2]) * inv, __uint_as_float(ov[i + 3]) * inv, f16);
+            w.z = pack_operand(__uint_as_float(ov[i + 4]) * inv, __uint_as_float(ov[i + 5]) * inv, f16);
+            w.w = pack_operand(__uint_as_float(ov[i + 6]) * inv, __uint_as_float(ov[i + 7]) * inv, f16);
+            *reinterpret_cast<uint4 *>(dst + 32 * q + i) = w;
+          }
+        }
+      }
+    } else {
+      *abort_v = 1;
+    }
+  } else if (warp == 4) {
+    if (lane == 0) {
+      const long long head_row = layer_row + ((long long)b * kv_heads + kvh) * seq_len;
+      int k_issued = 0, v_issued = 0;  // tiles whose K / V copies were started
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (j >= 2 && (!mbar_wait(kempty + st, ph ^ 1, &g_llama_status, 913u) || *abort_v)) break;
+        mbar_arrive_expect_tx(kfull + st, Lay::kv_bytes);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          tma_load_2d(ks + st * Lay::kv_bytes + kb * (kFaN * 128), &tmK, kfull + st, kb * 64,
+                      (int)(head_row + (long long)j * kFaN));
+        k_issued = j + 1;
+        if (j >= 2 && (!mbar_wait(vempty + st, ph ^ 1, &g_llama_status, 913u) || *abort_v)) break;
+        mbar_arrive_expect_tx(vfull + st, Lay::kv_bytes);
+#pragma unroll
+        for (int kb = 0; kb < KB; ++kb)
+          tma_load_2d(vs + st * Lay::kv_bytes + kb * (kFaN * 128), &tmV, vfull + st, kb * 64,
+                      (int)(head_row + (long long)j * kFaN));
+        v_issued = j + 1;
+      }
+      if (k_issued < ntiles || v_issued < ntiles) *abort_v = 1;
+      // the last copies of each stage land before the CTA may exit (they are
+      // complete already unless the loop ended early)
+      for (int j = k_issued - 2 < 0 ? 0 : k_issued - 2; j < k_issued; ++j)
+        mbar_wait(kfull + (j & 1), (j >> 1) & 1, &g_llama_status, 914u);
+      for (int j = v_issued - 2 < 0 ? 0 : v_issued - 2; j < v_issued; ++j)
+        mbar_wait(vfull + (j & 1), (j >> 1) & 1, &g_llama_status, 914u);
+    }
+  } else {
+    constexpr uint32_t idesc_qk = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kFaN >> 3) << 17) |
+                                  ((uint32_t)(kFaM >> 4) << 24);
+    constexpr uint32_t idesc_pv = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(HS >> 3) << 17) |
+                                  ((uint32_t)(kFaM >> 4) << 24);
+    bool ok = warp_wait(q_ready, 0, &g_llama_status, 915u);
+    bool issued_any = false;
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = (j >> 1) & 1;
+      ok = warp_wait(kfull + st, ph, &g_llama_status, 916u) &&
+           (j == 0 || warp_wait(s_free, (j - 1) & 1, &g_llama_status, 917u)) && !aborted();
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t kbase = smem_u32(ks + st * Lay::kv_bytes), qbase = smem_u32(qs);
+#pragma unroll
+        for (int k = 0; k < HS / 16; ++k) {
+          const uint64_t a = smem_desc_sw128(qbase + (k / 4) * (kFaM * 128) + (k % 4) * 32);
+          const uint64_t bd = smem_desc_sw128(kbase + (k / 4) * (kFaN * 128) + (k % 4) * 32);
+          tc_mma<0>(tbase + kColS, a, bd, idesc_qk, k > 0 ? 1u : 0u);
+        }
+        tc_commit(s_full);
+        tc_commit(kempty + st);
+        issued_any = true;
+      }
+      __syncwarp();
+      ok = warp_wait(vfull + st, ph, &g_llama_status, 918u) && !aborted();
+      if (!ok) break;
+      if (j == ntiles - 1 && nk_last < kFaN) {
+        // zero the V rows past the last key (both 64-wide chunks)
+        uint8_t *vt = vs + st * Lay::kv_bytes;
+        for (int i = lane; i < KB * (kFaN - nk_last) * 8; i += 32) {
+          const int kb = i / ((kFaN - nk_last) * 8), rem = i % ((kFaN - nk_last) * 8);
+          const int row = nk_last + rem / 8, piece = rem % 8;
+          *reinterpret_cast<uint4 *>(vt + kb * (kFaN * 128) + row * 128 + piece * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+      }
+      ok = warp_wait(p_full, j & 1, &g_llama_status, 919u) && !aborted();
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t vbase = smem_u32(vs + st * Lay::kv_bytes);
+#pragma unroll
+        for (int k = 0; k < kFaN / 16; ++k) {
+          const uint64_t bd = smem_desc_sw128_mn(vbase + k * 2048, kFaN * 128);
+          tc_mma_ts(tbase + kColO, tbase + kColP + k * 8, bd, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        tc_commit(o_ready);
+        tc_commit(vempty + st);
+      }
+      __syncwarp();
+    }
+    if (!ok) *abort_v = 1;
+    if (issued_any && lane == 0) {  // every MMA of this CTA complete before TMEM is freed
+      tc_commit(done);
+      mbar_wait(done, 0, &g_llama_status, 920u);
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 5) tmem_dealloc(tbase, Lay::tmem_cols);
+}
+
+// Prefill helpers: the chunk's prompt tokens in row order (row b * per_seq + c
+// takes prompt[b][off + c]); the final-norm rows of every sequence's last
+// prompt position into the decode step's operand rows; the position and step
+// advance after a prefill.
+__global__ void prefill_tokens_kernel(int *rows_tokens, const int *prompt, int prompt_len, int off, int per_seq,
+                                      int batch) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= batch * per_seq) return;
+  rows_tokens[i] = prompt[(size_t)(i / per_seq) * prompt_len + off + i % per_seq];
+}
+
+__global__ void gather_rows16_kernel(uint16_t *dst, const uint16_t *src, int per_seq, int pick, int cols,
+                                     int batch) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int v8 = cols / 8;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < batch * v8; i += gridDim.x * blockDim.x) {
+    const int b = i / v8, c = i % v8;
+    reinterpret_cast<uint4 *>(dst)[(size_t)b * v8 + c] =
+        reinterpret_cast<const uint4 *>(src)[((size_t)b * per_seq + pick) * v8 + c];
+  }
+}
+
+__global__ void advance_by_kernel(int *pos, int *step, int positions) {
+  pdl_launch_dependents();
+  pdl_wait();
+  *pos += positions;
+  *step += 1;
+}
+
 
 // hb = bf16(silu(g) * u), h = interleaved (g_i, u_i) pairs per row (the sum
 // of nsplit split-K partials split_stride floats apart), silu(g) = g / (1 + e^-g).
@@ -998,6 +1474,14 @@ int configure_attention() {
                                    (int)attn_smem_bytes(64)));
   CE_CUDA_TRY(cudaFuncSetAttribute(attn_decode_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                    (int)attn_smem_bytes(128)));
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)pf_smem_bytes(64)));
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)pf_smem_bytes(128)));
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   FaLayout<64>::total));
+  CE_CUDA_TRY(cudaFuncSetAttribute(attn_prefill_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   FaLayout<128>::total));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return CE_OK;
 }
@@ -1094,11 +1578,29 @@ struct ce_llama {
   uint8_t *q_codes = nullptr, *q_scales = nullptr;
   float *q_alpha = nullptr;
   std::vector<QMat> qm;
+  // prefill workspace (ce_llama_prefill_reserve): pf_rows chunk rows
+  int pf_rows = 0;
+  bool pf_simt = false;           // prefill attention on the SIMT kernel instead of the tensor cores
+  CUtensorMap pf_tmk{}, pf_tmv{};  // K / V cache rows for the tensor-core prefill attention
+  float *pf_x = nullptr, *pf_qkv = nullptr, *pf_delta = nullptr;
+  uint16_t *pf_xb = nullptr, *pf_att = nullptr, *pf_hb = nullptr;
+  int *pf_tokens = nullptr;
 };
 
 namespace {
 
+void free_prefill(ce_llama *m) {
+  for (void *p : {(void *)m->pf_x, (void *)m->pf_qkv, (void *)m->pf_delta, (void *)m->pf_xb, (void *)m->pf_att,
+                  (void *)m->pf_hb, (void *)m->pf_tokens})
+    if (p) cudaFree(p);
+  m->pf_x = m->pf_qkv = m->pf_delta = nullptr;
+  m->pf_xb = m->pf_att = m->pf_hb = nullptr;
+  m->pf_tokens = nullptr;
+  m->pf_rows = 0;
+}
+
 void free_llama(ce_llama *m) {
+  free_prefill(m);
   for (size_t q = 0; q < m->peer_block.size(); ++q)
     if (m->peer_block[q] != nullptr && (int)q != m->rank) cudaIpcCloseMemHandle(m->peer_block[q]);
   for (void *p : {(void *)m->x_block, (void *)m->d_blocks, (void *)m->x_counter, (void *)m->x_gen})
@@ -1553,7 +2055,7 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
     rc = launch_kernel(rope_append_kernel, rope_grid(D, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel", m->qkv,
                        m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
-                       (const int *)m->pos, D, m->kv_dim, m->hs, c.n_kv_heads, c.seq_len);
+                       (const int *)m->pos, D, m->kv_dim, m->hs, c.n_kv_heads, c.seq_len, 1, 0);
     if (rc) return rc;
     const dim3 agrid(m->attn_splits, c.n_heads, B);
     auto attention = [&](auto hs_tag) {
@@ -1598,6 +2100,162 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
                      (const int *)m->step);
   if (rc) return rc;
   return launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_kernel", m->pos, m->step);
+}
+
+int ce_llama_prefill_reserve(ce_llama *m, int max_rows) {
+  CE_REQUIRE(m != nullptr, "null model");
+  CE_REQUIRE(m->world == 1, "prefill runs on an unsharded model");
+  CE_REQUIRE(max_rows >= m->B && max_rows <= 65535, "max_rows must be in [batch (%d), 65535] (got %d)", m->B,
+             max_rows);
+  const ce_llama_config &c = m->c;
+  const size_t R = (size_t)max_rows;
+  free_prefill(m);
+  cudaError_t e = cudaSuccess;
+  for (auto [ptr, bytes] : {std::pair<void **, size_t>{(void **)&m->pf_x, R * c.dim * 4},
+                            {(void **)&m->pf_qkv, R * m->qkv_rows * 4},
+                            {(void **)&m->pf_delta, R * c.dim * 4},
+                            {(void **)&m->pf_xb, R * c.dim * 2},
+                            {(void **)&m->pf_att, R * c.dim * 2},
+                            {(void **)&m->pf_hb, R * c.hidden_dim * 2},
+                            {(void **)&m->pf_tokens, R * 4}}) {
+    e = cudaMalloc(ptr, bytes);
+    if (e != cudaSuccess) {
+      free_prefill(m);
+      return cuda_error(e, "cudaMalloc(prefill workspace)");
+    }
+  }
+  // the whole K / V cache as rows of head_size elements (one row per
+  // layer, sequence, KV head and position)
+  const unsigned long long cache_rows = (unsigned long long)c.n_layers * (m->layer_kv / m->hs);
+  int rc = make_bf16_rows_map(&m->pf_tmk, m->kcache, m->hs, cache_rows, m->hs, kFaN);
+  if (rc == CE_OK) rc = make_bf16_rows_map(&m->pf_tmv, m->vcache, m->hs, cache_rows, m->hs, kFaN);
+  if (rc != CE_OK) {
+    free_prefill(m);
+    return rc;
+  }
+  m->pf_rows = max_rows;
+  return CE_OK;
+}
+
+int ce_llama_set_prefill_attention(ce_llama *m, int simt) {
+  CE_REQUIRE(m != nullptr, "null model");
+  m->pf_simt = simt != 0;
+  return CE_OK;
+}
+
+int ce_llama_enqueue_prefill(ce_llama *m, const int32_t *prompt, int prompt_len, ce_stream_t stream) {
+  CE_REQUIRE(m != nullptr && prompt != nullptr, "null argument");
+  CE_REQUIRE(m->world == 1, "prefill runs on an unsharded model");
+  CE_REQUIRE(m->pf_rows >= m->B, "ce_llama_prefill_reserve has not been called");
+  CE_REQUIRE(prompt_len >= 1 && prompt_len <= m->c.seq_len, "prompt_len must be in [1, seq_len] (got %d)",
+             prompt_len);
+  cudaStream_t s = (cudaStream_t)stream;
+  const ce_llama_config &c = m->c;
+  const int B = m->B, D = c.dim, Hd = c.hidden_dim;
+  const float eps = 1e-5f;
+  const bool pdl = m->pdl;
+  const bool w4 = m->precision == CE_PREC_NVFP4_E2M1;
+  const int per = std::min(prompt_len, m->pf_rows / B);  // positions per chunk
+  // y = a W^T of weight kind k for M chunk rows, one split (M is large)
+  auto gemm = [&](int k, int l, int M, float *d, const uint16_t *a, int ldd, uint16_t *sw_out) -> int {
+    int N, K;
+    mat_shape(m, k, &N, &K);
+    if (w4) {
+      const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
+      return gemm_w4t(d, a, q.packed, q.alpha + 1, M, N, K, K, ldd, 1, 0, sw_out, sw_out ? N / 2 : 0, s, pdl);
+    }
+    const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
+                        : k == 2 ? m->w13 + l * w13_elems(m) : k == 3 ? m->w2 + l * w2_elems(m) : m->wcls;
+    if (sw_out) return gemm_bf16_swiglu(sw_out, N / 2, a, w, M, N, K, K, K, s, pdl);
+    return gemm_bf16_split(d, a, w, M, N, K, K, K, ldd, 1, 0, s, pdl);
+  };
+  auto norm = [&](int rows, float *x, const float *delta, size_t stride, const uint16_t *emb, const int *toks,
+                  const float *w, uint16_t *out) {
+    int lrc = CE_OK;
+    const int rc = launch_rows(m->nv, [&](auto nv) {
+      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(rows), dim3(kRowThreads), 0, s, pdl,
+                          "residual_rmsnorm_kernel", x, delta, 1, stride, emb, toks, c.vocab_size, w, out, D, eps,
+                          (int)w4, 0, ExchangeWait{});
+    });
+    return rc ? rc : lrc;
+  };
+  for (int off = 0; off < prompt_len; off += per) {
+    const int n = std::min(per, prompt_len - off), rows = B * n;
+    int rc = launch_kernel(prefill_tokens_kernel, dim3((rows + 255) / 256), dim3(256), 0, s, pdl,
+                           "prefill_tokens_kernel", m->pf_tokens, (const int *)prompt, prompt_len, off, n, B);
+    if (rc) return rc;
+    for (int l = 0; l < c.n_layers; ++l) {
+      rc = norm(rows, m->pf_x, l == 0 ? nullptr : m->pf_delta, (size_t)rows * D, l == 0 ? m->tok_emb : nullptr,
+                m->pf_tokens, m->rms_att + (size_t)l * D, m->pf_xb);
+      if (rc) return rc;
+      rc = gemm(0, l, rows, m->pf_qkv, m->pf_xb, m->qkv_rows, nullptr);
+      if (rc) return rc;
+      uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
+      rc = launch_kernel(rope_append_kernel, rope_grid(D, m->kv_dim, rows), dim3(256), 0, s, pdl,
+                         "rope_append_kernel", m->pf_qkv, m->qkv_rows, 1, (size_t)0, kc, vc,
+                         (const float2 *)m->rope, (const int *)m->pos, D, m->kv_dim, m->hs, c.n_kv_heads,
+                         c.seq_len, n, off);
+      if (rc) return rc;
+      auto attention = [&](auto hs_tag) {
+        constexpr int HS = decltype(hs_tag)::value;
+        if (m->pf_simt) {
+          const dim3 grid((unsigned)((n + kPfQ - 1) / kPfQ), (unsigned)c.n_heads, (unsigned)B);
+          return launch_kernel(attn_prefill_kernel<HS>, grid, dim3(kPfThreads), pf_smem_bytes(HS), s, pdl,
+                               "attn_prefill_kernel", (const float *)m->pf_qkv, m->qkv_rows,
+                               (const uint16_t *)kc, (const uint16_t *)vc, (const int *)m->pos, off, n, c.n_heads,
+                               c.n_kv_heads, c.seq_len, m->pf_att, D, (int)w4);
+        }
+        const dim3 grid((unsigned)((n + kFaM - 1) / kFaM), (unsigned)c.n_heads, (unsigned)B);
+        const long long layer_row = (long long)l * (long long)(m->layer_kv / m->hs);
+        return launch_kernel(attn_prefill_tc_kernel<HS>, grid, dim3(kFaThreads), (size_t)FaLayout<HS>::total, s,
+                             pdl, "attn_prefill_tc_kernel", m->pf_tmk, m->pf_tmv, (const float *)m->pf_qkv,
+                             m->qkv_rows, (const int *)m->pos, off, n, c.n_heads, c.n_kv_heads, c.seq_len,
+                             layer_row, m->pf_att, D, (int)w4);
+      };
+      rc = m->hs == 64 ? attention(std::integral_constant<int, 64>{})
+                       : attention(std::integral_constant<int, 128>{});
+      if (rc) return rc;
+      rc = gemm(1, l, rows, m->pf_delta, m->pf_att, D, nullptr);
+      if (rc) return rc;
+      rc = norm(rows, m->pf_x, m->pf_delta, (size_t)rows * D, nullptr, nullptr, m->rms_ffn + (size_t)l * D,
+                m->pf_xb);
+      if (rc) return rc;
+      rc = gemm(2, l, rows, nullptr, m->pf_xb, 2 * Hd, m->pf_hb);  // SwiGLU epilogue
+      if (rc) return rc;
+      rc = gemm(3, l, rows, m->pf_delta, m->pf_hb, D, nullptr);
+      if (rc) return rc;
+    }
+    if (off + n < prompt_len) continue;
+    // last chunk: final norm, then the decode step's tail on each
+    // sequence's last prompt position
+    rc = norm(rows, m->pf_x, m->pf_delta, (size_t)rows * D, nullptr, nullptr, m->rms_final, m->pf_xb);
+    if (rc) return rc;
+    rc = launch_kernel(gather_rows16_kernel, dim3(2 * sm_count()), dim3(256), 0, s, pdl, "gather_rows16_kernel",
+                       m->xb, (const uint16_t *)m->pf_xb, n, n - 1, D, B);
+    if (rc) return rc;
+  }
+  int rc;
+  {
+    int N, K;
+    mat_shape(m, 4, &N, &K);
+    if (w4) {
+      const QMat &q = m->qm[4 * c.n_layers];
+      rc = gemm_w4t(m->logits, m->xb, q.packed, q.alpha + 1, B, N, K, K, c.vocab_size, 1, 0, nullptr, 0, s, pdl);
+    } else {
+      rc = gemm_bf16_split(m->logits, m->xb, m->wcls, B, N, K, K, K, c.vocab_size, 1, 0, s, pdl);
+    }
+    if (rc) return rc;
+  }
+  rc = m->temperature > 0.f
+           ? launch_kernel(sample_kernel, dim3(B), dim3(kSampleThreads), 0, s, pdl, "sample_kernel",
+                           (const float *)m->logits, c.vocab_size, m->temperature, m->top_p, m->seed, m->tokens,
+                           m->generated, m->cap, (const int *)m->step)
+           : launch_kernel(argmax_kernel, dim3(B), dim3(kRowThreads), 0, s, pdl, "argmax_kernel",
+                           (const float *)m->logits, c.vocab_size, m->tokens, m->generated, m->cap,
+                           (const int *)m->step);
+  if (rc) return rc;
+  return launch_kernel(advance_by_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_by_kernel", m->pos, m->step,
+                       prompt_len);
 }
 
 int ce_llama_bind_exchange(ce_llama *m, uint16_t *att, float *delta, uint16_t *hb, float *top) {
@@ -1757,7 +2415,7 @@ int enqueue_segment_p2p(ce_llama *m, int segment, int l, cudaStream_t s) {
       uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
       rc = launch_kernel(rope_append_kernel, rope_grid(lD, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel",
                          m->qkv, m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
-                         (const int *)m->pos, lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
+                         (const int *)m->pos, lD, m->kv_dim, m->hs, m->lKH, c.seq_len, 1, 0);
       if (rc) return rc;
       const dim3 agrid(m->attn_splits, m->lH, B);
       const size_t smem = attn_smem_bytes(m->hs);
@@ -1871,7 +2529,7 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
       uint16_t *kc = m->kcache + l * m->layer_kv, *vc = m->vcache + l * m->layer_kv;
       rc = launch_kernel(rope_append_kernel, rope_grid(lD, m->kv_dim, B), dim3(256), 0, s, pdl, "rope_append_kernel",
                          m->qkv, m->qkv_rows, m->sp_qkv, qkv_stride, kc, vc, (const float2 *)m->rope,
-                         (const int *)m->pos, lD, m->kv_dim, m->hs, m->lKH, c.seq_len);
+                         (const int *)m->pos, lD, m->kv_dim, m->hs, m->lKH, c.seq_len, 1, 0);
       if (rc) return rc;
       const dim3 agrid(m->attn_splits, m->lH, B);
       const size_t smem = attn_smem_bytes(m->hs);
@@ -2006,6 +2664,7 @@ int ce_llama_status(void) {
   const DeviceStatus zero{};
   CE_CUDA_TRY(cudaMemcpyToSymbol(g_llama_status, &zero, sizeof(zero)));
   if (h.where == 900u) return set_error(CE_ERR_USAGE, "decode position reached the end of the KV cache");
+  if (h.where == 901u) return set_error(CE_ERR_USAGE, "prefill positions reached the end of the KV cache");
   return set_error(CE_ERR_TIMEOUT, format("attention staging wait gave up (site %u, block %u)", h.where, h.block));
 }
 

@@ -596,6 +596,32 @@ int ce_llama_bind_exchange(ce_llama *model, uint16_t *att_dev, float *delta_dev,
                            float *top_dev);
 int ce_llama_enqueue_segment(ce_llama *model, int segment, int layer, ce_stream_t stream);
 
+/* Prompt prefill, the step before decoding (the reference's decoder takes a
+ * one-token prompt per sequence and resets its tokens from it,
+ * decoder.cu:264-277; a longer prompt would otherwise take one decode step
+ * per token). ce_llama_enqueue_prefill runs every sequence's prompt
+ * prompt_dev int32 [batch][prompt_len] (device) at positions pos ..
+ * pos + prompt_len - 1 (pos: the device position, ce_llama_start's or after
+ * earlier steps) in chunks of max_rows / batch positions: the layer GEMMs
+ * with M = batch x chunk positions, RoPE and KV append of every row, causal
+ * attention of each position over the cache up to itself; then the final
+ * RMSNorm, classifier and token choice (greedy, or the sampler) of each
+ * sequence's last prompt position, as a decode step would make it: the
+ * chosen token goes to the tokens and to generated[step], the position
+ * advances by prompt_len and the step by 1, so decoding continues with
+ * ce_llama_enqueue_step. Capturable; allocates nothing (the chunk
+ * workspace comes from ce_llama_prefill_reserve, max_rows in
+ * [batch, 65535], a setup call that allocates). Unsharded models only.
+ * After a prefill the RESIDUAL tensor is not the last position's. A prompt
+ * running past the cache is reported by ce_llama_status, as for a step. */
+int ce_llama_prefill_reserve(ce_llama *model, int max_rows);
+/* Prefill attention kernel: 0 (default) the tensor-core kernel (tcgen05,
+ * scores and weights in tensor memory), 1 the SIMT kernel (the same
+ * arithmetic in fp32 FMAs; a cross-check). */
+int ce_llama_set_prefill_attention(ce_llama *model, int simt);
+int ce_llama_enqueue_prefill(ce_llama *model, const int32_t *prompt_dev, int prompt_len,
+                             ce_stream_t stream);
+
 /* Global rows of rank's rows of weight `which` (CE_LLAMA_WQKV, _WO, _W13,
  * _W2, _WCLS) in local order; rows_out may be NULL to get the count. No CUDA call. */
 int ce_llama_shard_rows(const ce_llama_config *cfg, int rank, int world, int which,

@@ -220,3 +220,122 @@ def test_sampling_matches_oracle_sampler(ce, vocab, temperature, top_p):
         assert agree >= 0.99 * total, (agree, total)
     finally:
         m.close()
+
+
+@pytest.mark.parametrize("cfg,batch,pos0,plen,rows,prec", [
+    # chunks of 16 positions over a cache filled to 5
+    (dict(dim=128, hidden_dim=256, n_layers=2, n_heads=2, vocab_size=512, seq_len=128), 3, 5, 37, 48, "bf16"),
+    # grouped-query, one chunk of 130 positions (three key tiles)
+    (dict(dim=256, hidden_dim=512, n_layers=2, n_heads=4, n_kv_heads=2, vocab_size=1000, seq_len=200),
+     2, 0, 130, 512, "bf16"),
+    # head size 128, chunks of 33 positions (ragged query tiles) after 70 cached positions
+    (dict(dim=256, hidden_dim=384, n_layers=2, n_heads=2, vocab_size=260, seq_len=300), 4, 70, 100, 132, "bf16"),
+    # NVFP4 weights, fp16 operands
+    (dict(dim=256, hidden_dim=512, n_layers=2, n_heads=4, vocab_size=512, seq_len=128), 3, 9, 40, 60, "nvfp4"),
+    # two full 128-position query tiles per chunk, keys over three tiles
+    (dict(dim=256, hidden_dim=512, n_layers=2, n_heads=4, vocab_size=512, seq_len=400), 2, 100, 290, 512, "bf16"),
+])
+@pytest.mark.parametrize("simt", [False, True], ids=["tensor-cores", "simt"])
+def test_prefill_matches_oracle(ce, O, cfg, batch, pos0, plen, rows, prec, simt):
+    """ce_llama_enqueue_prefill, with the tensor-core and the SIMT prefill
+    attention: the last prompt position's logits and the prompt's K/V rows
+    against the oracle's teacher-forced decode of the prompt, the first
+    token by the near-tie rule, the position advanced by the prompt length;
+    then decode steps continue from it against the oracle."""
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    steps = 3
+    m = ce.Llama(cfg, batch, 1 + steps,
+                 precision=ce.PREC_NVFP4_E2M1 if prec == "nvfp4" else ce.PREC_BF16)
+    try:
+        m.init_random(seed=4, weight_std=0.05, kv_fill=pos0)
+        m.prefill_reserve(rows)
+        m.set_prefill_attention(simt)
+        rng = np.random.default_rng(7)
+        prompt = rng.integers(0, m.cfg.vocab_size, (batch, plen)).astype(np.int32)
+        m.start(prompt[:, 0].copy(), pos0)
+        seqs = list(range(batch))
+        kc, vc = cache_from_device(m, seqs, pos0)
+        m.prefill(torch.from_numpy(prompt).to(dev))
+        torch.cuda.synchronize()
+        ce.llama_status()
+        assert m.read(ce.LLAMA_POS, dtype=np.int32)[0] == pos0 + plen
+        dev_logits = m.logits().astype(np.float64)
+        orc = LlamaOracle(m.cfg.as_dict(), m.weights(), operand="f16" if prec == "nvfp4" else "bf16")
+        forced = np.concatenate([prompt[:, 1:], prompt[:, :1]], axis=1)
+        lg, best, _ = orc.decode(prompt[:, 0], pos0, forced, kc, vc)
+        assert O.rel_l2(dev_logits, lg[-1]) <= LOGIT_REL_L2
+        gen = m.generated()
+        for i in seqs:
+            if gen[i, 0] != best[-1, i]:
+                err = np.abs(dev_logits[i] - lg[-1, i]).max()
+                assert lg[-1, i].max() - lg[-1, i, gen[i, 0]] <= max(2 * err, NEAR_TIE)
+        # the prompt's K / V rows of the device cache against the oracle's
+        dk, dv = cache_from_device(m, seqs, pos0 + plen)
+        for l in range(m.cfg.n_layers):
+            sl = slice(pos0, pos0 + plen)
+            assert O.rel_l2(dk[l][:, :, sl], kc[l][:, :, sl]) <= LOGIT_REL_L2
+            assert O.rel_l2(dv[l][:, :, sl], vc[l][:, :, sl]) <= LOGIT_REL_L2
+        # decoding continues from the prefill's token and position
+        step_logits = []
+        for _ in range(steps):
+            m.step()
+            torch.cuda.synchronize()
+            step_logits.append(m.logits().astype(np.float64))
+        ce.llama_status()
+        gen = m.generated()
+        lg2, _, _ = orc.decode(gen[:, 0], pos0 + plen, gen[:, 1:], kc, vc)
+        for s in range(steps):
+            assert O.rel_l2(step_logits[s], lg2[s]) <= LOGIT_REL_L2
+    finally:
+        m.close()
+
+
+def test_prefill_past_cache_end_reports(ce):
+    cfg = dict(dim=128, hidden_dim=256, n_layers=1, n_heads=2, vocab_size=64, seq_len=16)
+    m = ce.Llama(cfg, 2, 2)
+    try:
+        m.init_random(seed=3, kv_fill=10)
+        with pytest.raises(ce.CeError):
+            m.prefill(torch.zeros((2, 4), dtype=torch.int32, device="cuda"))  # no workspace yet
+        m.prefill_reserve(16)
+        m.start(np.array([1, 2], np.int32), 10)
+        m.prefill(torch.ones((2, 6), dtype=torch.int32, device="cuda"))  # positions 10 .. 15: fits
+        torch.cuda.synchronize()
+        ce.llama_status()
+        m.start(np.array([1, 2], np.int32), 12)
+        m.prefill(torch.ones((2, 6), dtype=torch.int32, device="cuda"))  # positions 12 .. 17: past the end
+        with pytest.raises(ce.CeError) as err:
+            ce.llama_status()
+        assert "end of the KV cache" in str(err.value)
+        ce.llama_status()
+    finally:
+        m.close()
+
+
+def test_prefill_110m_shape_sampled(ce, O):
+    """BASELINE config 4 shape, batch 16, a 300-token prompt after 20 cached
+    positions, chunks of 128 positions: two sequences checked against the
+    oracle's teacher-forced decode of their prompts."""
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    cfg = dict(dim=768, hidden_dim=2048, n_layers=12, n_heads=12, vocab_size=32000, seq_len=1024)
+    batch, pos0, plen = 16, 20, 300
+    m = ce.Llama(cfg, batch, 2)
+    try:
+        m.init_random(seed=8, weight_std=0.02, kv_fill=pos0)
+        m.prefill_reserve(batch * 128)
+        prompt = np.random.default_rng(3).integers(0, 32000, (batch, plen)).astype(np.int32)
+        m.start(prompt[:, 0].copy(), pos0)
+        seqs = [3, 14]
+        kc, vc = cache_from_device(m, seqs, pos0)
+        m.prefill(torch.from_numpy(prompt).to(dev))
+        torch.cuda.synchronize()
+        ce.llama_status()
+        dev_logits = m.logits()[seqs].astype(np.float64)
+        orc = LlamaOracle(m.cfg.as_dict(), m.weights(), operand="bf16")
+        forced = np.concatenate([prompt[seqs, 1:], prompt[seqs, :1]], axis=1)
+        lg, _, _ = orc.decode(prompt[seqs, 0], pos0, forced, kc, vc)
+        assert O.rel_l2(dev_logits, lg[-1]) <= LOGIT_REL_L2
+    finally:
+        m.close()
