@@ -131,6 +131,8 @@ _SIGNATURES = {
     "ce_llama_exchange_open": [_vp, _vp],
     "ce_llama_prefill_reserve": [_vp, _i],
     "ce_llama_set_prefill_attention": [_vp, _i],
+    "ce_llama_load": [_vp, _i, _i, _vp],
+    "ce_llama_load_nvfp4": [_vp, _i, _i, _vp, _vp, _vp],
     "ce_llama_enqueue_prefill": [_vp, _vp, _i, _vp],
     "ce_llama_set_sampling": [_vp, _f, _f, _u64],
     "ce_llama_exchange_connect": [_vp, ctypes.c_char_p],
@@ -668,6 +670,52 @@ class Llama:
 
     def set_pdl(self, enable):
         check(lib().ce_llama_set_pdl(self._h, int(bool(enable))))
+
+    def load_llama2c(self, path):
+        """Loads a llama2.c fp32 checkpoint whose config matches this model's:
+        bf16 models convert on the device, NVFP4 models quantize every GEMM
+        weight on the device at load (ce_llama_load)."""
+        from . import convert_weights as cw
+        cfg, t, _ = cw.read_llama2c(path)
+        self._check_config(cfg)
+        L = self.cfg.n_layers
+
+        def load(which, layer, a):
+            a = np.ascontiguousarray(a, dtype=np.float32)
+            check(lib().ce_llama_load(self._h, which, layer, a.ctypes.data))
+
+        load(LLAMA_TOK_EMB, 0, t["tok_emb"])
+        for l in range(L):
+            load(LLAMA_RMS_ATT, l, t["rms_att"][l])
+            load(LLAMA_RMS_FFN, l, t["rms_ffn"][l])
+            for name, which in (("wqkv", LLAMA_WQKV), ("wo", LLAMA_WO), ("w13", LLAMA_W13), ("w2", LLAMA_W2)):
+                load(which, l, cw.model_matrix(t, name, l))
+        load(LLAMA_RMS_FINAL, 0, t["rms_final"])
+        load(LLAMA_WCLS, 0, cw.model_matrix(t, "wcls", 0))
+
+    def load_nvfp4_file(self, path):
+        """Loads the output of convert_weights (weights quantized ahead of
+        time) into an NVFP4 model (ce_llama_load_nvfp4); no quantization at
+        load."""
+        from . import convert_weights as cw
+        cfg, emb, norms, mats = cw.read_nvfp4_file(path)
+        self._check_config(cfg)
+        self.write(LLAMA_TOK_EMB, np.ascontiguousarray(emb))
+        rms_att, rms_ffn, rms_final = norms
+        for l in range(self.cfg.n_layers):
+            self.write(LLAMA_RMS_ATT, np.ascontiguousarray(rms_att[l]), l)
+            self.write(LLAMA_RMS_FFN, np.ascontiguousarray(rms_ffn[l]), l)
+        self.write(LLAMA_RMS_FINAL, np.ascontiguousarray(rms_final))
+        which = {"wqkv": LLAMA_WQKV, "wo": LLAMA_WO, "w13": LLAMA_W13, "w2": LLAMA_W2, "wcls": LLAMA_WCLS}
+        for name, layer, alpha, codes, scales in mats:
+            a, c, sc = (np.ascontiguousarray(x) for x in (alpha, codes, scales))
+            check(lib().ce_llama_load_nvfp4(self._h, which[name], layer, c.ctypes.data, sc.ctypes.data,
+                                            a.ctypes.data))
+
+    def _check_config(self, cfg):
+        mine = {k: getattr(self.cfg, k) for k in cfg}
+        if mine != cfg:
+            raise ValueError(f"checkpoint config {cfg} does not match the model's {mine}")
 
     def read(self, which, layer=0, dtype=np.uint16, count=None, offset=0):
         """Host copy of `count` elements of a tensor from element `offset`."""

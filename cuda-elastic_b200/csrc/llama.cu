@@ -75,6 +75,7 @@ int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsign
                    const float *x, int rows, int cols, int ld_bytes, cudaStream_t s);
 int make_bf16_rows_map(CUtensorMap *map, const void *base, unsigned long long inner, unsigned long long outer,
                        unsigned long long ld, int box_outer);
+int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
 
 static __device__ DeviceStatus g_llama_status;
 
@@ -2651,6 +2652,150 @@ int ce_llama_write(ce_llama *m, int which, int layer, const void *host, int64_t 
              "range [%lld, %lld) outside the tensor (%zu bytes)", (long long)offset, (long long)(offset + bytes), v.bytes);
   CE_CUDA_TRY(cudaDeviceSynchronize());
   CE_CUDA_TRY(cudaMemcpy((uint8_t *)v.ptr + offset, host, (size_t)bytes, cudaMemcpyHostToDevice));
+  return CE_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+// Weight kind (0 wqkv, 1 wo, 2 w13, 3 w2, 4 classifier) of a CE_LLAMA_*
+// matrix, or -1.
+int weight_kind(int which) {
+  switch (which) {
+    case CE_LLAMA_WQKV: return 0;
+    case CE_LLAMA_WO: return 1;
+    case CE_LLAMA_W13: return 2;
+    case CE_LLAMA_W2: return 3;
+    case CE_LLAMA_WCLS: return 4;
+    default: return -1;
+  }
+}
+
+// Scratch of a load call, freed on every path.
+struct LoadScratch {
+  std::vector<void *> ptrs;
+  template <class T>
+  int alloc(T **p, size_t bytes) {
+    void *q = nullptr;
+    const cudaError_t e = cudaMalloc(&q, bytes);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(load scratch)");
+    ptrs.push_back(q);
+    *p = static_cast<T *>(q);
+    return CE_OK;
+  }
+  ~LoadScratch() {
+    for (void *q : ptrs) cudaFree(q);
+  }
+};
+
+}  // namespace
+
+extern "C" {
+
+int ce_llama_load(ce_llama *m, int which, int layer, const float *host) {
+  CE_REQUIRE(m != nullptr && host != nullptr, "null argument");
+  const ce_llama_config &c = m->c;
+  const int k = weight_kind(which);
+  cudaStream_t s = nullptr;
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  if (k < 0) {
+    switch (which) {
+      case CE_LLAMA_RMS_ATT:
+      case CE_LLAMA_RMS_FFN:
+      case CE_LLAMA_RMS_FINAL: {
+        TensorView v;
+        if (int rc = tensor_of(m, which, layer, &v)) return rc;
+        CE_CUDA_TRY(cudaMemcpy(v.ptr, host, v.bytes, cudaMemcpyHostToDevice));
+        return CE_OK;
+      }
+      case CE_LLAMA_TOK_EMB: {
+        LoadScratch sc;
+        float *tmp = nullptr;
+        const size_t n = (size_t)c.vocab_size * c.dim;
+        if (int rc = sc.alloc(&tmp, n * 4)) return rc;
+        CE_CUDA_TRY(cudaMemcpy(tmp, host, n * 4, cudaMemcpyHostToDevice));
+        if (int rc = convert_bf16(m->tok_emb, tmp, c.vocab_size, c.dim, c.dim, s)) return rc;
+        CE_CUDA_TRY(cudaStreamSynchronize(s));
+        return CE_OK;
+      }
+      default:
+        return set_error(CE_ERR_USAGE, format("tensor %d is not a loadable weight", which));
+    }
+  }
+  CE_REQUIRE(k == 4 || (layer >= 0 && layer < c.n_layers), "layer %d out of range", layer);
+  int rows, cols;
+  mat_shape(m, k, &rows, &cols);
+  std::vector<int> map;
+  shard_rows(c, m->rank, m->world, k, &map);
+  LoadScratch sc;
+  if (m->precision == CE_PREC_BF16) {
+    // this shard's rows, gathered on the host, converted on the device
+    std::vector<float> mine((size_t)rows * cols);
+    for (int r = 0; r < rows; ++r)
+      std::memcpy(mine.data() + (size_t)r * cols, host + (size_t)map[r] * cols, (size_t)cols * 4);
+    float *tmp = nullptr;
+    if (int rc = sc.alloc(&tmp, mine.size() * 4)) return rc;
+    CE_CUDA_TRY(cudaMemcpy(tmp, mine.data(), mine.size() * 4, cudaMemcpyHostToDevice));
+    TensorView v;
+    if (int rc = tensor_of(m, which, layer, &v)) return rc;
+    if (int rc = convert_bf16(static_cast<uint16_t *>(v.ptr), tmp, rows, cols, cols, s)) return rc;
+    CE_CUDA_TRY(cudaStreamSynchronize(s));
+    return CE_OK;
+  }
+  // NVFP4: the whole global matrix quantized (tensor amax over all of it),
+  // then this shard's rows packed
+  const int grows = global_rows(c, k);
+  const size_t n = (size_t)grows * cols;
+  float *tmp = nullptr;
+  uint8_t *codes = nullptr, *scales = nullptr;
+  unsigned int *amax = nullptr;
+  int *d_map = nullptr;
+  int rc = sc.alloc(&tmp, n * 4);
+  if (rc == CE_OK) rc = sc.alloc(&codes, n / 2);
+  if (rc == CE_OK) rc = sc.alloc(&scales, n / 16);
+  if (rc == CE_OK) rc = sc.alloc(&amax, 4);
+  if (rc == CE_OK) rc = sc.alloc(&d_map, map.size() * sizeof(int));
+  if (rc) return rc;
+  CE_CUDA_TRY(cudaMemcpy(tmp, host, n * 4, cudaMemcpyHostToDevice));
+  CE_CUDA_TRY(cudaMemcpy(d_map, map.data(), map.size() * sizeof(int), cudaMemcpyHostToDevice));
+  const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * layer + k];
+  rc = quantize_nvfp4(codes, scales, q.alpha, amax, tmp, grows, cols, cols / 2, s);
+  if (rc == CE_OK) rc = w4t_pack(q.packed, codes, scales, rows, cols, cols / 2, cols / 16, s, d_map);
+  if (rc) return rc;
+  CE_CUDA_TRY(cudaStreamSynchronize(s));
+  return CE_OK;
+}
+
+int ce_llama_load_nvfp4(ce_llama *m, int which, int layer, const uint8_t *codes_host, const uint8_t *scales_host,
+                        const float *alpha_host) {
+  CE_REQUIRE(m != nullptr && codes_host && scales_host && alpha_host, "null argument");
+  CE_REQUIRE(m->precision == CE_PREC_NVFP4_E2M1, "ce_llama_load_nvfp4 needs an NVFP4 model");
+  const ce_llama_config &c = m->c;
+  const int k = weight_kind(which);
+  CE_REQUIRE(k >= 0, "tensor %d is not a weight matrix", which);
+  CE_REQUIRE(k == 4 || (layer >= 0 && layer < c.n_layers), "layer %d out of range", layer);
+  int rows, cols;
+  mat_shape(m, k, &rows, &cols);
+  std::vector<int> map;
+  shard_rows(c, m->rank, m->world, k, &map);
+  const size_t n = (size_t)global_rows(c, k) * cols;
+  LoadScratch sc;
+  uint8_t *codes = nullptr, *scales = nullptr;
+  int *d_map = nullptr;
+  int rc = sc.alloc(&codes, n / 2);
+  if (rc == CE_OK) rc = sc.alloc(&scales, n / 16);
+  if (rc == CE_OK) rc = sc.alloc(&d_map, map.size() * sizeof(int));
+  if (rc) return rc;
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  CE_CUDA_TRY(cudaMemcpy(codes, codes_host, n / 2, cudaMemcpyHostToDevice));
+  CE_CUDA_TRY(cudaMemcpy(scales, scales_host, n / 16, cudaMemcpyHostToDevice));
+  CE_CUDA_TRY(cudaMemcpy(d_map, map.data(), map.size() * sizeof(int), cudaMemcpyHostToDevice));
+  const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * layer + k];
+  CE_CUDA_TRY(cudaMemcpy(q.alpha, alpha_host, 2 * sizeof(float), cudaMemcpyHostToDevice));
+  rc = w4t_pack(q.packed, codes, scales, rows, cols, cols / 2, cols / 16, nullptr, d_map);
+  if (rc) return rc;
+  CE_CUDA_TRY(cudaStreamSynchronize(nullptr));
   return CE_OK;
 }
 

@@ -653,6 +653,24 @@ int ce_llama_read(ce_llama *model, int which, int layer, void *host, int64_t off
 int ce_llama_write(ce_llama *model, int which, int layer, const void *host, int64_t offset,
                    int64_t bytes);
 
+/* Weight loading (setup calls: they allocate scratch and synchronize).
+ * ce_llama_load takes one tensor as a global fp32 host array in the model's
+ * global layout: the embedding [vocab][dim]; a norm; or a weight matrix in
+ * the row orders above (WQKV = the q, k, v rows; W13 = w1 and w3 rows
+ * interleaved; a sharded model takes its rows, ce_llama_shard_rows). The
+ * bf16 model converts to bf16 on the device; the NVFP4 model quantizes the
+ * whole global matrix on the device (tensor scale from its amax, UE4M3 per
+ * 16 values, E2M1 codes: the reference's setup-time convert_weights,
+ * decoder_lowprec.cu:573-579) and packs its rows.
+ * ce_llama_load_nvfp4 (NVFP4 model) takes one matrix quantized ahead of
+ * time, the offline conversion's output: codes_host [global rows][cols / 2]
+ * (two E2M1 codes per byte, even column in the low nibble), scales_host
+ * [global rows][cols / 16] (UE4M3) and alpha_host (encode, decode) tensor
+ * scales; the weight is e2m1(code) * ue4m3(scale) * alpha[1]. */
+int ce_llama_load(ce_llama *model, int which, int layer, const float *host);
+int ce_llama_load_nvfp4(ce_llama *model, int which, int layer, const uint8_t *codes_host,
+                        const uint8_t *scales_host, const float *alpha_host);
+
 /* NVFP4 model only: host copies of one weight matrix (CE_LLAMA_WQKV, _WO,
  * _W13, _W2 of a layer, or _WCLS; this shard's rows): packed_host receives
  * it in the ce_w4t_pack layout (ce_w4t_packed_bytes(rows, cols) bytes; codes

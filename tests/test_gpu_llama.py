@@ -339,3 +339,98 @@ def test_prefill_110m_shape_sampled(ce, O):
         assert O.rel_l2(dev_logits, lg[-1]) <= LOGIT_REL_L2
     finally:
         m.close()
+
+
+def _checkpoint(tmp_path, cfg, shared, seed=5):
+    from test_convert_weights import random_tensors
+    import cuda_elastic_b200.convert_weights as cw
+    t = random_tensors(cfg, seed)
+    for k in t:
+        if k.startswith("rms"):
+            t[k] = (0.5 + np.abs(t[k]) % 1.0).astype(np.float32)
+        else:
+            t[k] *= np.float32(0.05)
+    if shared:
+        t["wcls"] = t["tok_emb"]
+    path = str(tmp_path / "model.bin")
+    cw.write_llama2c(path, cfg, t, shared=shared)
+    return path, t, cw
+
+
+LOAD_CFG = dict(dim=256, hidden_dim=384, n_layers=2, n_heads=4, n_kv_heads=2, vocab_size=300, seq_len=64)
+
+
+@pytest.mark.parametrize("shared", [True, False])
+def test_load_llama2c_bf16(ce, O, tmp_path, shared):
+    """ce_llama_load from a llama2.c checkpoint: every weight equals the bf16
+    rounding of the checkpoint's matrix in the library's row order (q|k|v,
+    w1/w3 interleaved), norms exact; decode steps against the oracle."""
+    path, t, cw = _checkpoint(tmp_path, LOAD_CFG, shared)
+    m = ce.Llama(LOAD_CFG, 3, 3)
+    try:
+        m.init_random(seed=1, kv_fill=4)   # cache; the weights are replaced below
+        m.load_llama2c(path)
+        w = m.weights()
+        for l in range(LOAD_CFG["n_layers"]):
+            for name in ("wqkv", "wo", "w13", "w2"):
+                assert np.array_equal(w[name][l], O.bf16_bits(cw.model_matrix(t, name, l))), (name, l)
+            assert np.array_equal(w["rms_att"][l], t["rms_att"][l])
+            assert np.array_equal(w["rms_ffn"][l], t["rms_ffn"][l])
+        assert np.array_equal(w["wcls"], O.bf16_bits(t["wcls"]))
+        assert np.array_equal(w["tok_emb"], O.bf16_bits(t["tok_emb"]))
+        assert np.array_equal(w["rms_final"], t["rms_final"])
+        tokens0 = np.array([1, 77, 299], np.int32)
+        m.start(tokens0, 4)
+        kc, vc = cache_from_device(m, [0, 1, 2], 4)
+        logits = []
+        for _ in range(3):
+            m.step()
+            torch.cuda.synchronize()
+            logits.append(m.logits().astype(np.float64))
+        ce.llama_status()
+        orc = LlamaOracle(m.cfg.as_dict(), w, operand="bf16")
+        lg, _, _ = orc.decode(tokens0, 4, m.generated(), kc, vc)
+        for s in range(3):
+            assert O.rel_l2(logits[s], lg[s]) <= LOGIT_REL_L2
+    finally:
+        m.close()
+
+
+def test_offline_nvfp4_equals_quantization_at_load(ce, O, tmp_path):
+    """convert_weights (offline NVFP4 file) + ce_llama_load_nvfp4 gives bit
+    for bit the weights ce_llama_load quantizes at load, and the same decode;
+    the loaded NVFP4 weights are the quantizer's codes of the checkpoint."""
+    path, t, cw = _checkpoint(tmp_path, LOAD_CFG, False)
+    out = str(tmp_path / "model.nvfp4")
+    cw.convert(path, out)
+    models = [ce.Llama(LOAD_CFG, 3, 3, precision=ce.PREC_NVFP4_E2M1) for _ in range(2)]
+    try:
+        for m in models:
+            m.init_random(seed=1, kv_fill=4)
+        models[0].load_llama2c(path)
+        models[1].load_nvfp4_file(out)
+        w0, w1 = models[0].weights(), models[1].weights()
+        for name in ("wqkv", "wo", "w13", "w2"):
+            for l in range(LOAD_CFG["n_layers"]):
+                for a, b in zip(w0[name][l], w1[name][l]):
+                    assert np.array_equal(np.asarray(a), np.asarray(b)), (name, l)
+        for a, b in zip(w0["wcls"], w1["wcls"]):
+            assert np.array_equal(np.asarray(a), np.asarray(b))
+        assert np.array_equal(w0["tok_emb"], w1["tok_emb"])
+        # the codes dequantize to within the NVFP4 step of the checkpoint
+        codes, scales, decode = w0["w13"][1]
+        deq = O.dequantize_nvfp4(codes, scales, LOAD_CFG["dim"], decode)
+        ref = cw.model_matrix(t, "w13", 1)
+        assert O.rel_l2(deq, ref) <= 0.15
+        outs = []
+        for m in models:
+            m.start(np.array([5, 6, 7], np.int32), 4)
+            for _ in range(3):
+                m.step()
+            torch.cuda.synchronize()
+            outs.append((m.generated().copy(), m.logits().copy()))
+        ce.llama_status()
+        assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][1], outs[1][1])
+    finally:
+        for m in models:
+            m.close()
