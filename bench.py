@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--no-precisions", action="store_true", help="skip the per-precision GEMM section")
     ap.add_argument("--no-llama", action="store_true", help="skip the Llama-2 110M decode section")
     ap.add_argument("--no-llama7b", action="store_true", help="skip the row-sharded 7B decode section")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prompt prefill section")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="join of the row-sharded decoder's slices: the library's peer-memory puts "
                          "(CUDA IPC over NVLink) or NCCL all-gathers")
@@ -338,6 +339,65 @@ def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=10
                                  "layer) plus its rows of every NVFP4 weight once per step"}}
 
 
+def llama_prefill(ce, dev, stream, s, dist, world, peaks_tflops, which):
+    """Prompt prefill (ce_llama_enqueue_prefill) of a 512-token prompt per
+    sequence from position 0: the 110M shape (bf16 weights, batch 256,
+    chunks of 128 positions) or the 7B shape (NVFP4 weights, batch 64, chunks
+    of 128 positions); random weights N(0, 0.02), uniform random prompts.
+    One untimed prefill, then the best of two timed ones (CUDA events on the
+    launching stream); every rank prefills its own batch (replicas), time =
+    max over ranks. Tensor roofline: the layer GEMMs and classifier (2 x
+    tokens x weights) plus the causal attention (4 x heads x hs x sum of
+    attended positions) against the measured bf16 dense peak."""
+    import torch
+    if which == "110m":
+        cfg, batch, prec, label = LLAMA_110M, 256, ce.PREC_BF16, "bf16"
+    else:
+        cfg, batch, prec, label = LLAMA_7B, 64, ce.PREC_NVFP4_E2M1, "NVFP4 weights, fp16 activations"
+    plen, chunk = 512, 128
+    m = ce.Llama(cfg, batch, 2, precision=prec, stream=s)
+    m.init_random(seed=1, weight_std=0.02, kv_fill=0, stream=s)
+    m.prefill_reserve(batch * chunk)
+    prompt = torch.randint(0, cfg["vocab_size"], (batch, plen), dtype=torch.int32, device=dev)
+    zeros = np.zeros(batch, np.int32)
+    times = []
+    for it in range(3):
+        m.start(zeros, 0, stream=s)
+        with torch.cuda.stream(stream):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            m.prefill(prompt, stream=s)
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        if it > 0:
+            times.append(e0.elapsed_time(e1))
+    ce.llama_status()
+    m.close()
+    ms = min(times)
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    L, D, Hd, V, H = cfg["n_layers"], cfg["dim"], cfg["hidden_dim"], cfg["vocab_size"], cfg["n_heads"]
+    hs = D // H
+    kvd = hs * cfg.get("n_kv_heads", H)
+    tokens = batch * plen
+    gemm_flops = 2.0 * tokens * L * (D * (D + 2 * kvd) + D * D + 2 * Hd * D + Hd * D) + 2.0 * batch * V * D
+    attn_flops = 4.0 * batch * L * H * hs * (plen * (plen + 1) / 2)
+    achieved = (gemm_flops + attn_flops) / (ms * 1e-3) / 1e12
+    peak = peaks_tflops
+    return {"workload": f"Llama-2 {which} shape, {label}, batch {batch}, {plen}-token prompts from position 0, "
+                        f"chunks of {chunk} positions; tensor-core GEMMs (M = batch x chunk) and "
+                        f"tcgen05 causal attention",
+            "tokens_per_s": world * tokens / (ms * 1e-3), "ms_per_prefill": ms, "n_gpus": world,
+            "parallelism": f"replicas x{world} (independent batches)",
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "flops": gemm_flops + attn_flops,
+                         "note": "2 x tokens x GEMM weights + 4 x heads x hs x attended positions, "
+                                 "against the measured bf16 dense peak (sustained)"}}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import __graft_entry__
@@ -572,6 +632,15 @@ def run_ours(args, rank, world, local_rank):
         llama7b = llama7b_decode(ce, dev, stream, dist, world, peaks()[0].get("hbm_gbs", 6650.0),
                                  exchange=args.exchange)
 
+    # ---- prompt prefill (110M bf16, 7B NVFP4), 512-token prompts ----
+    prefill = {}
+    if not args.no_prefill:
+        pk0, _ = peaks()
+        sustained = pk0.get("bf16_tflops_sustained", 1400.0)
+        prefill = {"110m": llama_prefill(ce, dev, stream, s, dist, world, sustained, "110m")}
+        if not args.no_llama7b:
+            prefill["7b"] = llama_prefill(ce, dev, stream, s, dist, world, sustained, "7b")
+
     pk, pk_kind = peaks()
     long_region = total_ms > 1000.0
     peak = pk.get("bf16_tflops_sustained" if long_region else "bf16_tflops", 1590.0)
@@ -616,6 +685,7 @@ def run_ours(args, rank, world, local_rank):
                         **decoder},
             "llama_decode": llama,
             "llama7b_decode": llama7b,
+            "llama_prefill": prefill,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                     "pipeline": "2 buffer sets; host->device, compute and device->host streams"},
