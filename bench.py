@@ -47,6 +47,9 @@ def parse():
     ap.add_argument("--no-llama", action="store_true", help="skip the Llama-2 110M decode section")
     ap.add_argument("--no-llama7b", action="store_true", help="skip the row-sharded 7B decode section")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prompt prefill section")
+    ap.add_argument("--profile-prefill", choices=["110m", "7b"],
+                    help="run one prompt prefill under cudaProfilerStart/Stop (for ncu) and exit")
+    ap.add_argument("--prefill-batch", type=int, default=0, help="sequences of --profile-prefill")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="join of the row-sharded decoder's slices: the library's peer-memory puts "
                          "(CUDA IPC over NVLink) or NCCL all-gathers")
@@ -731,11 +734,50 @@ def profile_llama(args):
           f"{args.steps} steps done", flush=True)
 
 
+def profile_prefill(args):
+    """--profile-prefill: one GPU, one prompt prefill (512 tokens, chunks of
+    128 positions) of the 110M (bf16, batch 256) or 7B (NVFP4, batch 64)
+    decoder, optionally with fewer layers (--llama-layers) and sequences
+    (--prefill-batch) so that an ncu capture holds a few GB; the profiled
+    region is the prefill after one untimed one."""
+    import torch
+    import __graft_entry__
+    ce = __graft_entry__.load_package()
+    torch.cuda.set_device(0)
+    if args.profile_prefill == "110m":
+        cfg, batch, prec = dict(LLAMA_110M), 256, ce.PREC_BF16
+    else:
+        cfg, batch, prec = dict(LLAMA_7B), 64, ce.PREC_NVFP4_E2M1
+    if args.llama_layers > 0:
+        cfg["n_layers"] = args.llama_layers
+    if args.prefill_batch > 0:
+        batch = args.prefill_batch
+    m = ce.Llama(cfg, batch, 2, precision=prec)
+    m.init_random(seed=1, weight_std=0.02, kv_fill=0)
+    m.prefill_reserve(batch * 128)
+    prompt = torch.randint(0, cfg["vocab_size"], (batch, 512), dtype=torch.int32, device="cuda")
+    zeros = np.zeros(batch, np.int32)
+    m.start(zeros, 0)
+    m.prefill(prompt)
+    torch.cuda.synchronize()
+    m.start(zeros, 0)
+    torch.cuda.profiler.start()
+    m.prefill(prompt)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ce.llama_status()
+    m.close()
+    print(f"profile-prefill {args.profile_prefill}: {cfg['n_layers']} layers, batch {batch}, done", flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.profile_prefill:
+        profile_prefill(args)
+        return
     if args.profile_llama:
         profile_llama(args)
         return

@@ -57,6 +57,11 @@ struct Kind<2> {
   static constexpr int elem = 1;
   static constexpr uint32_t fmt = 0;  // E4M3
 };
+template <>
+struct Kind<3> {
+  static constexpr int elem = 2;
+  static constexpr uint32_t fmt = 0;  // F16 (kind::f16 with fp16 operands)
+};
 
 template <int BN>
 struct Smem {
@@ -83,6 +88,7 @@ struct GemmArgs {
   float *d;
   const float *row_scale;  // optional per-m scale (nullptr = 1)
   const float *col_scale;  // optional per-n scale (nullptr = 1)
+  const float *alpha;      // optional scalar scale on the device (nullptr = 1)
   int M, N, K, ldd;
   int tiles_m, tiles_n, k_blocks;
   int prefetch;  // L2 prefetch distance in k-blocks (0 = none)
@@ -295,7 +301,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
       const int m0 = (w.tile % args.tiles_m) * BM;
       const int n0 = (w.tile / args.tiles_m) * BN;
       const int row = m0 + quarter * 32 + lane;
-      const float rs = (args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f;
+      const float rs = ((args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f) *
+                       (args.alpha != nullptr ? *args.alpha : 1.0f);
       float *drow = w.d + (size_t)row * args.ldd;
       const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(w.d) & 15u) == 0);
 #pragma unroll 1
@@ -531,7 +538,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const int m0 = (w.tile % args.tiles_m) * (2 * BM) + (int)rank * BM;
       const int n0 = (w.tile / args.tiles_m) * BN;
       const int row = m0 + quarter * 32 + lane;
-      const float rs = (args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f;
+      const float rs = ((args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f) *
+                       (args.alpha != nullptr ? *args.alpha : 1.0f);
       float *drow = w.d + (size_t)row * args.ldd;
       const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(w.d) & 15u) == 0);
 #pragma unroll 1
@@ -1059,10 +1067,12 @@ template <int kKind>
 int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
                   int ldd, const float *row_scale, const float *col_scale, int force_bn,
                   int force_group, cudaStream_t s, int splits = 1, long long split_stride = 0,
-                  bool pdl = false, uint16_t *swiglu_out = nullptr, int swiglu_ld = 0) {
+                  bool pdl = false, uint16_t *swiglu_out = nullptr, int swiglu_ld = 0,
+                  const float *alpha = nullptr) {
   constexpr int elem = Kind<kKind>::elem;
   const CUtensorMapDataType dt = kKind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : kKind == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : kKind == 3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                               : CU_TENSOR_MAP_DATA_TYPE_UINT8;
   CE_REQUIRE(M >= 1 && N >= 1 && K >= 1, "GEMM dims must be >= 1 (M=%d N=%d K=%d)", M, N, K);
   CE_REQUIRE(lda >= K && ldb >= K && ldd >= N, "leading dimensions too small");
@@ -1098,6 +1108,7 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.d = d;
   args.row_scale = row_scale;
   args.col_scale = col_scale;
+  args.alpha = alpha;
   args.M = M;
   args.N = N;
   args.K = K;
@@ -1111,7 +1122,7 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.epilogue = swiglu_out != nullptr ? 1 : 0;
   args.out_bf16 = swiglu_out;
   args.ld_out = swiglu_ld;
-  args.out_f16 = 0;
+  args.out_f16 = kKind == 3 ? 1 : 0;
   const int tiles = args.tiles_m * args.tiles_n * splits;
   if (c.pair) {
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
@@ -1642,6 +1653,15 @@ int gemm_bf16_swiglu(uint16_t *out, int ld_out, const uint16_t *a, const uint16_
                           out, ld_out);
 }
 
+// fp16 GEMM (kind::f16 with fp16 operands): d = alpha x A B^T, alpha a
+// scalar on the device (nullptr = 1); with swiglu_out, B's rows interleave
+// w1 and w3 and fp16(silu(g) * u) goes to swiglu_out [M][swiglu_ld].
+int gemm_f16(float *d, const uint16_t *a, const uint16_t *b, const float *alpha, int M, int N, int K, int lda,
+             int ldb, int ldd, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl) {
+  return gemm_dispatch<3>(d, a, b, M, N, K, lda, ldb, swiglu_out != nullptr ? N : ldd, nullptr, nullptr, 0, 0, s,
+                          1, 0, pdl, swiglu_out, swiglu_ld, alpha);
+}
+
 // Time of the busiest CTA of a W4A16 launch, in units of one weight row of
 // one k-block: waves x (k-blocks per split + kW4UnitKb) x (kW4StepRows +
 // width). Each
@@ -1826,6 +1846,65 @@ int gemm_w4t_auto_splits(int M, int N, int K, int max_splits) {
 size_t w4t_packed_bytes(int N, int K) {
   const size_t kb = (size_t)(K + 127) / 128, npad = (size_t)(N + 255) / 256 * 256;
   return kb * (npad / 128) * 9216;
+}
+
+namespace {
+
+// One 32-value piece of a W4T-packed weight row to fp16: e2m1(code) x
+// ue4m3(scale), exact in fp16 (at most 6 significant bits, magnitudes in
+// [2^-10, 2688]); the tensor decode scale stays with the GEMM's alpha.
+__global__ void w4t_expand_f16_kernel(uint16_t *out, const uint8_t *packed, int N, int K, int npad) {
+  const int pieces = K / 32;
+  const size_t total = (size_t)N * pieces;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(i / pieces), p = (int)(i % pieces);
+    const int kb = p / 4, j = p % 4;
+    const int g = n / 32, r = n % 32, hg = g / 4, q = g % 4;
+    const uint8_t *blk = packed + ((size_t)kb * (npad / 128) + hg) * 9216;
+    const uint4 c = *reinterpret_cast<const uint4 *>(blk + (size_t)(q * 4 + j) * 512 + r * 16);
+    const uint8_t *sc = blk + 8192 + (size_t)(q * 32 + r) * 8 + 2 * j;
+    float scale[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t u = sc[h];
+      const int e = (u >> 3) & 15, mm = u & 7;
+      scale[h] = e == 0 ? ldexpf((float)mm, -9) : ldexpf((float)(8 + mm), e - 10);
+    }
+    const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+    uint32_t o[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) {
+      const uint32_t byte = (words[b / 4] >> (8 * (b % 4))) & 0xFFu;
+      float v[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t code = h ? byte >> 4 : byte & 15u;
+        const uint32_t mag = code & 7u;
+        const float m = mag < 4 ? 0.5f * (float)mag : (float)(mag == 4 ? 2 : mag == 5 ? 3 : mag == 6 ? 4 : 6);
+        v[h] = ((code & 8u) ? -m : m) * scale[b / 8];
+      }
+      __half2 hv = __floats2half2_rn(v[0], v[1]);
+      o[b] = *reinterpret_cast<uint32_t *>(&hv);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(out + (size_t)n * K + (size_t)p * 32);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) dst[w] = make_uint4(o[4 * w], o[4 * w + 1], o[4 * w + 2], o[4 * w + 3]);
+  }
+}
+
+}  // namespace
+
+// W4T-packed weight [N][K] (w4t_pack's layout) expanded to fp16 [N][K]
+// without the tensor decode scale (the GEMM applies it as alpha).
+int w4t_expand_f16(uint16_t *out, const uint8_t *packed, int N, int K, cudaStream_t s) {
+  CE_REQUIRE(out && packed && N >= 1 && K >= 64 && K % 64 == 0, "bad W4T expansion (N=%d K=%d)", N, K);
+  const int npad = (N + 255) / 256 * 256;
+  const size_t total = (size_t)N * (K / 32);
+  int blocks = (int)((total + 255) / 256);
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  w4t_expand_f16_kernel<<<blocks, 256, 0, s>>>(out, packed, N, K, npad);
+  CE_LAUNCH_CHECK("w4t_expand_f16_kernel");
+  return CE_OK;
 }
 
 int w4t_pack(uint8_t *packed, const uint8_t *codes, const uint8_t *scales, int N, int K, int ld_bytes, int nsf,

@@ -76,6 +76,9 @@ int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsign
 int make_bf16_rows_map(CUtensorMap *map, const void *base, unsigned long long inner, unsigned long long outer,
                        unsigned long long ld, int box_outer);
 int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
+int gemm_f16(float *d, const uint16_t *a, const uint16_t *b, const float *alpha, int M, int N, int K, int lda,
+             int ldb, int ldd, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
+int w4t_expand_f16(uint16_t *out, const uint8_t *packed, int N, int K, cudaStream_t s);
 
 static __device__ DeviceStatus g_llama_status;
 
@@ -661,12 +664,14 @@ attn_prefill_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const 
 // Prefill attention on the tensor cores (the kernel the prefill runs; the
 // SIMT kernel above states the same arithmetic plainly). One CTA per (tile of
 // kFaM = 128 query positions, head, sequence), six warps:
-//   warps 0-3  one query row per thread (= its TMEM lane): stage q / sqrt(hs)
-//              as bf16 into shared memory (128-byte swizzled, K-major); per
-//              key tile read the scores row S from TMEM, mask keys past the
-//              query, online softmax (running max m, sum l of the bf16-rounded
-//              weights), rescale the output O in TMEM when m grows, write the
-//              weights P as bf16 into TMEM; at the end O / l to att;
+//   warps 0-3  one query row per thread (= its TMEM lane): stage q log2(e) /
+//              sqrt(hs) as bf16 into shared memory (128-byte swizzled,
+//              K-major), so scores come in base-2 units; per key tile read
+//              the scores row S from TMEM, mask keys past the query, online
+//              softmax with weights 2^(s - m) (running max m, sum l of the
+//              bf16-rounded weights), rescale the output O in TMEM when m
+//              grows, write the weights P as bf16 into TMEM; at the end O / l
+//              to att;
 //   warp 4     one thread: TMA loads of the K and V tiles (kFaN = 128
 //              positions, two stages each) from the bf16 cache;
 //   warp 5     one thread issues S = Q K^T (A, B from shared memory) and
@@ -677,6 +682,13 @@ attn_prefill_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const 
 // TMEM: S fp32 [128 x 128] at column 0, P bf16 pairs at 128, O fp32 [128 x
 // hs] at kColO. Every wait is bounded; a timeout records its site and the
 // CTA drains its copies and MMAs before freeing TMEM.
+// 2^x by the ex2.approx instruction (relative error ~2^-22, far below the
+// bf16 rounding of the weights it feeds); 2^-inf = +0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 constexpr int kFaM = 128, kFaN = 128, kFaThreads = 192;
 template <int HS>
 struct FaLayout {
@@ -747,7 +759,8 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
   if (warp < 4) {
     const int r = threadIdx.x;
     {  // Q tile
-      const float qscale = rsqrtf((float)HS);
+      // scores in base-2 units: q / sqrt(hs) * log2(e), weights 2^(s - m)
+      const float qscale = rsqrtf((float)HS) * 1.4426950408889634f;
       const float *qrow = qkv + (size_t)(b * per_seq + c0 + r) * ld_qkv + h * HS;
 #pragma unroll
       for (int kb = 0; kb < KB; ++kb)
@@ -794,16 +807,15 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
         sv[i] = __float_as_uint(sc);
         tmax = fmaxf(tmax, sc);
       }
-      const float m_new = fmaxf(m, tmax);
-      const float alpha = m == -INFINITY ? 0.f : expf(m - m_new);
+      const float m_new = fmaxf(m, tmax);  // finite: key 0 is valid for every row
+      const float alpha = ex2_approx(m - m_new);  // 2^-inf = 0 on the first tile
       float rs = 0.f;
       uint32_t pk[kFaN / 2];
 #pragma unroll
       for (int i = 0; i < kFaN / 2; ++i) {
-        const float s0 = __uint_as_float(sv[2 * i]), s1 = __uint_as_float(sv[2 * i + 1]);
-        const float e0 = s0 == -INFINITY ? 0.f : expf(s0 - m_new);
-        const float e1 = s1 == -INFINITY ? 0.f : expf(s1 - m_new);
-        pk[i] = pack_bf16x2(e0, e1);
+        // masked scores are -inf: 2^-inf = 0
+        pk[i] = pack_bf16x2(ex2_approx(__uint_as_float(sv[2 * i]) - m_new),
+                            ex2_approx(__uint_as_float(sv[2 * i + 1]) - m_new));
         rs += bf16_lo(pk[i]) + bf16_hi(pk[i]);
       }
       l = l * alpha + rs;
@@ -1585,6 +1597,7 @@ struct ce_llama {
   CUtensorMap pf_tmk{}, pf_tmv{};  // K / V cache rows for the tensor-core prefill attention
   float *pf_x = nullptr, *pf_qkv = nullptr, *pf_delta = nullptr;
   uint16_t *pf_xb = nullptr, *pf_att = nullptr, *pf_hb = nullptr;
+  uint16_t *pf_w16 = nullptr;  // NVFP4 model: one layer's weights expanded to fp16 (wqkv | wo | w13 | w2)
   int *pf_tokens = nullptr;
 };
 
@@ -1592,10 +1605,10 @@ namespace {
 
 void free_prefill(ce_llama *m) {
   for (void *p : {(void *)m->pf_x, (void *)m->pf_qkv, (void *)m->pf_delta, (void *)m->pf_xb, (void *)m->pf_att,
-                  (void *)m->pf_hb, (void *)m->pf_tokens})
+                  (void *)m->pf_hb, (void *)m->pf_tokens, (void *)m->pf_w16})
     if (p) cudaFree(p);
   m->pf_x = m->pf_qkv = m->pf_delta = nullptr;
-  m->pf_xb = m->pf_att = m->pf_hb = nullptr;
+  m->pf_xb = m->pf_att = m->pf_hb = m->pf_w16 = nullptr;
   m->pf_tokens = nullptr;
   m->pf_rows = 0;
 }
@@ -2103,6 +2116,27 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
   return launch_kernel(advance_kernel, dim3(1), dim3(1), 0, s, pdl, "advance_kernel", m->pos, m->step);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Elements of one layer's four GEMM weights (wqkv, wo, w13, w2), and the
+// offset of weight kind k among them.
+size_t layer_w16_offset(const ce_llama *m, int k) {
+  size_t off = 0;
+  for (int i = 0; i < k; ++i) {
+    int r, c;
+    mat_shape(m, i, &r, &c);
+    off += (size_t)r * c;
+  }
+  return off;
+}
+size_t layer_w16_elems(const ce_llama *m) { return layer_w16_offset(m, 4); }
+
+}  // namespace
+
+extern "C" {
+
 int ce_llama_prefill_reserve(ce_llama *m, int max_rows) {
   CE_REQUIRE(m != nullptr, "null model");
   CE_REQUIRE(m->world == 1, "prefill runs on an unsharded model");
@@ -2118,7 +2152,9 @@ int ce_llama_prefill_reserve(ce_llama *m, int max_rows) {
                             {(void **)&m->pf_xb, R * c.dim * 2},
                             {(void **)&m->pf_att, R * c.dim * 2},
                             {(void **)&m->pf_hb, R * c.hidden_dim * 2},
-                            {(void **)&m->pf_tokens, R * 4}}) {
+                            {(void **)&m->pf_tokens, R * 4},
+                            {(void **)&m->pf_w16, m->precision == CE_PREC_NVFP4_E2M1 ? layer_w16_elems(m) * 2 : 0}}) {
+    if (bytes == 0) continue;
     e = cudaMalloc(ptr, bytes);
     if (e != cudaSuccess) {
       free_prefill(m);
@@ -2157,13 +2193,18 @@ int ce_llama_enqueue_prefill(ce_llama *m, const int32_t *prompt, int prompt_len,
   const bool pdl = m->pdl;
   const bool w4 = m->precision == CE_PREC_NVFP4_E2M1;
   const int per = std::min(prompt_len, m->pf_rows / B);  // positions per chunk
-  // y = a W^T of weight kind k for M chunk rows, one split (M is large)
+  // y = a W^T of weight kind k for M chunk rows, one split (M is large). The
+  // NVFP4 model multiplies the layer's weights expanded to fp16 (by the
+  // chunk, before its first GEMM) with the fp16 tensor-core GEMM and the
+  // decode scale as alpha: at M in the thousands that beats expanding the
+  // weights inside the W4T GEMM once per 256-row batch tile.
   auto gemm = [&](int k, int l, int M, float *d, const uint16_t *a, int ldd, uint16_t *sw_out) -> int {
     int N, K;
     mat_shape(m, k, &N, &K);
     if (w4) {
-      const QMat &q = m->qm[k == 4 ? 4 * c.n_layers : 4 * l + k];
-      return gemm_w4t(d, a, q.packed, q.alpha + 1, M, N, K, K, ldd, 1, 0, sw_out, sw_out ? N / 2 : 0, s, pdl);
+      const QMat &q = m->qm[4 * l + k];
+      return gemm_f16(d, a, m->pf_w16 + layer_w16_offset(m, k), q.alpha + 1, M, N, K, K, K, ldd, sw_out,
+                      sw_out ? N / 2 : 0, s, pdl);
     }
     const uint16_t *w = k == 0 ? m->wqkv + l * wqkv_elems(m) : k == 1 ? m->wo + l * wo_elems(m)
                         : k == 2 ? m->w13 + l * w13_elems(m) : k == 3 ? m->w2 + l * w2_elems(m) : m->wcls;
@@ -2186,6 +2227,13 @@ int ce_llama_enqueue_prefill(ce_llama *m, const int32_t *prompt, int prompt_len,
                            "prefill_tokens_kernel", m->pf_tokens, (const int *)prompt, prompt_len, off, n, B);
     if (rc) return rc;
     for (int l = 0; l < c.n_layers; ++l) {
+      if (w4) {
+        for (int k = 0; k < 4 && rc == CE_OK; ++k) {
+          const QMat &q = m->qm[4 * l + k];
+          rc = w4t_expand_f16(m->pf_w16 + layer_w16_offset(m, k), q.packed, q.rows, q.cols, s);
+        }
+        if (rc) return rc;
+      }
       rc = norm(rows, m->pf_x, l == 0 ? nullptr : m->pf_delta, (size_t)rows * D, l == 0 ? m->tok_emb : nullptr,
                 m->pf_tokens, m->rms_att + (size_t)l * D, m->pf_xb);
       if (rc) return rc;

@@ -37,7 +37,7 @@ def main():
         x, p = np.empty(b * s, np.float32), np.empty(b * s, np.float32)
         w, m = np.empty(s, np.float32), np.empty(r * s, np.float32)
         R.ref_fill_inputs(random, seed, b, s, r, x, p, w, m)
-        # the reference oracle needs outputs to judge; its tolerance and double
+        # the reference oracle needs outputs to check; its tolerance and double
         # reference do not depend on them
         norm = np.zeros(b * s, np.float32)
         soft = np.zeros(b * s, np.float32)
