@@ -131,6 +131,8 @@ _SIGNATURES = {
     "ce_llama_exchange_open": [_vp, _vp],
     "ce_llama_prefill_reserve": [_vp, _i],
     "ce_llama_set_prefill_attention": [_vp, _i],
+    "ce_w4t_expand_f16": [_vp, _vp, _i, _i, _vp],
+    "ce_gemm_f16": [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_llama_load": [_vp, _i, _i, _vp],
     "ce_llama_load_nvfp4": [_vp, _i, _i, _vp, _vp, _vp],
     "ce_llama_enqueue_prefill": [_vp, _vp, _i, _vp],
@@ -362,6 +364,21 @@ def gemm_w4t(d, a, packed, alpha=None, n=None, splits=1, stream=None):
     N = d.shape[-1] if n is None else n
     check(lib().ce_gemm_w4t(_ptr(d), _ptr(a), _ptr(packed), _ptr(alpha), M, N, K, K, d.shape[-1], splits,
                             M * d.shape[-1], _stream(stream)))
+    return d
+
+
+def w4t_expand_f16(out, packed, n, k, stream=None):
+    """W4T-packed weight [n][k] -> fp16 bits [n][k] (e2m1 x ue4m3, no decode scale)."""
+    check(lib().ce_w4t_expand_f16(_ptr(out), _ptr(packed), n, k, _stream(stream)))
+    return out
+
+
+def gemm_f16(d, a, b, alpha=None, stream=None):
+    """d [M][N] fp32 = alpha * A B^T, A [M][K] and B [N][K] fp16 bits (tensor cores)."""
+    M, K = a.shape
+    N = b.shape[0]
+    check(lib().ce_gemm_f16(_ptr(d), _ptr(a), _ptr(b), _ptr(alpha), M, N, K, a.shape[1], b.shape[1], d.shape[1],
+                            _stream(stream)))
     return d
 
 

@@ -24,6 +24,9 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    uint8_t *normalized_e4m3 = nullptr, int ld_e4m3 = 0, float *e4m3_scale = nullptr);
 int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
 size_t w4t_packed_bytes(int N, int K);
+int w4t_expand_f16(uint16_t *out, const uint8_t *packed, int N, int K, cudaStream_t s);
+int gemm_f16(float *d, const uint16_t *a, const uint16_t *b, const float *alpha, int M, int N, int K, int lda,
+             int ldb, int ldd, uint16_t *swiglu_out, int swiglu_ld, cudaStream_t s, bool pdl);
 int w4t_pack(uint8_t *packed, const uint8_t *codes, const uint8_t *scales, int N, int K, int ld_bytes, int nsf,
              cudaStream_t s, const int *row_map);
 int gemm_w4t(float *d, const uint16_t *a, const uint8_t *packed, const float *alpha, int M, int N, int K, int lda,
@@ -380,6 +383,15 @@ int ce_gemm_w4t(float *d, const uint16_t *a, const uint8_t *packed, const float 
                 int ldd, int splits, int64_t split_stride, ce_stream_t stream) {
   return gemm_w4t(d, a, packed, alpha, M, N, K, lda, ldd, splits, (long long)split_stride, nullptr, 0,
                   (cudaStream_t)stream, false);
+}
+
+int ce_w4t_expand_f16(uint16_t *out, const uint8_t *packed, int N, int K, ce_stream_t stream) {
+  return w4t_expand_f16(out, packed, N, K, (cudaStream_t)stream);
+}
+
+int ce_gemm_f16(float *d, const uint16_t *a, const uint16_t *b, const float *alpha, int M, int N, int K, int lda,
+                int ldb, int ldd, ce_stream_t stream) {
+  return gemm_f16(d, a, b, alpha, M, N, K, lda, ldb, ldd, nullptr, 0, (cudaStream_t)stream, false);
 }
 
 int ce_gemm_tf32(float *d, const float *a, const float *b, int M, int N, int K, int lda, int ldb,

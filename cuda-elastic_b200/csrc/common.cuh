@@ -374,10 +374,10 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster_addr) {
   asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];"
                ::"r"(bar_cluster_addr) : "memory");
 }
-template <int kKind>  // 0: kind::f16, 1: kind::tf32, 2: kind::f8f6f4
+template <int kKind>  // 0, 3: kind::f16 (bf16 / fp16 operands), 1: kind::tf32, 2: kind::f8f6f4
 __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                             uint32_t idesc, uint32_t accumulate) {
-  if constexpr (kKind == 0) {
+  if constexpr (kKind == 0 || kKind == 3) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}"
@@ -388,6 +388,7 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, ui
         "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
   } else {
+    static_assert(kKind == 2, "unknown MMA kind");
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"
@@ -396,10 +397,10 @@ __device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t a_desc, ui
 }
 
 // D(tmem) (+)= A(smem desc) x B(smem desc)^T, one instruction.
-template <int kKind>  // 0: kind::f16, 1: kind::tf32, 2: kind::f8f6f4
+template <int kKind>  // 0, 3: kind::f16 (bf16 / fp16 operands), 1: kind::tf32, 2: kind::f8f6f4
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate) {
-  if constexpr (kKind == 0) {
+  if constexpr (kKind == 0 || kKind == 3) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
@@ -410,6 +411,7 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t a_desc, uint64_
         "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
   } else {
+    static_assert(kKind == 2, "unknown MMA kind");
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}"

@@ -228,6 +228,18 @@ int ce_w4t_pack(uint8_t *packed_dev, const uint8_t *codes_dev, const uint8_t *sc
 int ce_gemm_w4t(float *d_dev, const uint16_t *a_dev, const uint8_t *packed_dev, const float *alpha_dev,
                 int M, int N, int K, int lda, int ldd, int splits, int64_t split_stride, ce_stream_t stream);
 
+/* A ce_w4t_pack-layout weight [N][K] expanded to fp16 [N][K]: e2m1(code) x
+ * ue4m3(scale), exact in fp16; the tensor decode scale is left for the GEMM
+ * (alpha below). The NVFP4 prefill multiplies its layer weights this way. */
+int ce_w4t_expand_f16(uint16_t *out_dev, const uint8_t *packed_dev, int N, int K, ce_stream_t stream);
+
+/* fp16 tensor-core GEMM (tcgen05 kind::f16 with fp16 operands):
+ * d[m][n] = alpha x sum_k A[m][k] B[n][k], A and B fp16 bit patterns,
+ * K-contiguous (lda, ldb multiples of 8, 16-byte aligned bases); alpha_dev a
+ * scalar on the device or NULL (1). */
+int ce_gemm_f16(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev, const float *alpha_dev,
+                int M, int N, int K, int lda, int ldb, int ldd, ce_stream_t stream);
+
 /* Library-wide GEMM tuning, set at setup time (not during a capture): the
  * TMA producer prefetches operand tiles this many k-blocks ahead into L2
  * (0 = off, at most 64). */

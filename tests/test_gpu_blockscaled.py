@@ -266,3 +266,40 @@ def test_w4t_pack_layout(ce, O, dev):
                 assert np.array_equal(srow, spad[rows, k * 8:k * 8 + 8])
     c2, s2 = ce.w4t_unpack(got.ravel(), N, K)
     assert np.array_equal(c2, codes) and np.array_equal(s2, sc)
+
+
+@pytest.mark.parametrize("shape", [(300, 512), (256, 256), (1000, 1216)])
+def test_w4t_expand_f16(ce, O, dev, shape):
+    """ce_w4t_expand_f16: every value e2m1(code) x ue4m3(scale) as fp16, bit
+    for bit, from the W4T-packed layout."""
+    n, k = shape
+    W = torch.randn(n, k, device=dev) * 0.05
+    codes = torch.empty((n, k // 2), dtype=torch.uint8, device=dev)
+    scales = torch.empty((n, k // 16), dtype=torch.uint8, device=dev)
+    ts = torch.empty(2, device=dev)
+    scratch = torch.zeros(1, dtype=torch.int32, device=dev)
+    ce.quantize_nvfp4(codes, scales, ts, scratch, W)
+    packed = torch.empty(ce.w4t_packed_bytes(n, k), dtype=torch.uint8, device=dev)
+    ce.w4t_pack(packed, codes, scales, n, k)
+    out = torch.full((n, k), 0x7E00, dtype=torch.int16, device=dev)
+    ce.w4t_expand_f16(out, packed, n, k)
+    torch.cuda.synchronize()
+    ref = O.dequantize_nvfp4(codes.cpu().numpy(), scales.cpu().numpy(), k).astype(np.float16)
+    assert np.array_equal(out.cpu().numpy().view(np.uint16), ref.view(np.uint16))
+
+
+@pytest.mark.parametrize("shape", [(60, 768, 256), (512, 1024, 512), (130, 200, 320)])
+def test_gemm_f16(ce, O, dev, shape):
+    """ce_gemm_f16 (kind::f16, fp16 operands, alpha from the device): within
+    the implementation-check bound of the double product."""
+    M, N, K = shape
+    a = (torch.randn(M, K, device=dev) * 0.5).half()
+    b = (torch.randn(N, K, device=dev) * 0.5).half()
+    alpha = torch.tensor([0.37], device=dev)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_f16(d, a.view(torch.int16), b.view(torch.int16), alpha)
+    torch.cuda.synchronize()
+    ref, mag = O.gemm_ref(a.float().cpu().numpy(), b.float().cpu().numpy())
+    ref *= float(np.float32(0.37))
+    bound = O.gamma_worst(K) * mag * 0.37 + 2.0 ** -22 * np.abs(ref) + 1e-30
+    assert np.all(np.abs(d.cpu().numpy().astype(np.float64) - ref) <= bound)
