@@ -664,17 +664,20 @@ attn_prefill_kernel(const float *qkv, int ld_qkv, const uint16_t *kcache, const 
 // Prefill attention on the tensor cores (the kernel the prefill runs; the
 // SIMT kernel above states the same arithmetic plainly). One CTA per (tile of
 // kFaM = 128 query positions, head, sequence), six warps:
-//   warps 0-3  one query row per thread (= its TMEM lane): stage q log2(e) /
-//              sqrt(hs) as bf16 into shared memory (128-byte swizzled,
+//   warps 0-7  one query row and one column half per thread (warps w and
+//              w + 4 share the TMEM lanes of row quarter w): stage q log2(e)
+//              / sqrt(hs) as bf16 into shared memory (128-byte swizzled,
 //              K-major), so scores come in base-2 units; per key tile read
-//              the scores row S from TMEM, mask keys past the query, online
-//              softmax with weights 2^(s - m) (running max m, sum l of the
-//              bf16-rounded weights), rescale the output O in TMEM when m
-//              grows, write the weights P as bf16 into TMEM; at the end O / l
-//              to att;
-//   warp 4     one thread: TMA loads of the K and V tiles (kFaN = 128
+//              the half's scores from TMEM, mask keys past the query, swap
+//              the half-row maxima with the partner warp (shared memory,
+//              bounded wait), online softmax with weights 2^(s - m) (running
+//              max m, the half's sum of the bf16-rounded weights), rescale
+//              the half's output columns in TMEM when m grows, write the
+//              half's weights P as bf16 into TMEM; at the end the two sums
+//              are added and O / l goes to att;
+//   warp 8     one thread: TMA loads of the K and V tiles (kFaN = 128
 //              positions, two stages each) from the bf16 cache;
-//   warp 5     one thread issues S = Q K^T (A, B from shared memory) and
+//   warp 9     one thread issues S = Q K^T (A, B from shared memory) and
 //              O += P V (A = P from TMEM, B = V as an MN-major operand straight
 //              from its [positions][hs] cache layout); the warp zeroes the V
 //              rows past the tile's last key (uninitialized cache rows must
@@ -689,7 +692,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-constexpr int kFaM = 128, kFaN = 128, kFaThreads = 192;
+constexpr int kFaM = 128, kFaN = 128, kFaThreads = 320;
 template <int HS>
 struct FaLayout {
   static constexpr int q_bytes = kFaM * HS * 2;   // HS / 64 blocks of [128 rows][128 B]
@@ -719,6 +722,9 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
            *o_ready = bars + 12, *done = bars + 13;
   uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(bars + 16);
   __shared__ int abort_flag;
+  __shared__ float pair_max[2][2][kFaM];  // [tile parity][column half][row]: the halves' row maxima
+  __shared__ float pair_l[2][kFaM];       // [column half][row]: the halves' weight sums
+  __shared__ unsigned pair_count[4];      // postings per row quarter (both halves)
   pdl_launch_dependents();
   pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -735,16 +741,17 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
   const int nk_last = last + 1 - (ntiles - 1) * kFaN;  // keys of the last tile
   if (threadIdx.x == 0) {
     for (int i = 0; i < 8; ++i) mbar_init(bars + i, 1);
-    mbar_init(q_ready, 4);
+    mbar_init(q_ready, 8);
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
-    mbar_init(p_full, 4);
+    mbar_init(s_free, 8);
+    mbar_init(p_full, 8);
     mbar_init(o_ready, 1);
     mbar_init(done, 1);
     abort_flag = 0;
+    for (int i = 0; i < 4; ++i) pair_count[i] = 0u;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_holder, Lay::tmem_cols);
     tmem_relinquish();
   }
@@ -756,69 +763,101 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
   // warp-uniform: every lane of the warp takes the same branch
   auto aborted = [&]() { return __any_sync(0xffffffffu, *abort_v != 0) != 0; };
 
-  if (warp < 4) {
-    const int r = threadIdx.x;
-    {  // Q tile
+  if (warp < 8) {
+    // thread: row r (its TMEM lane), column half hh of S, P and O; the two
+    // warps of a row quarter (w, w + 4) exchange row maxima through shared
+    // memory with a bounded wait and add their weight sums at the end
+    const int r = (warp & 3) * 32 + lane, hh = warp >> 2;
+    {  // Q tile: this half's 16-byte chunks of row r
       // scores in base-2 units: q / sqrt(hs) * log2(e), weights 2^(s - m)
       const float qscale = rsqrtf((float)HS) * 1.4426950408889634f;
       const float *qrow = qkv + (size_t)(b * per_seq + c0 + r) * ld_qkv + h * HS;
 #pragma unroll
-      for (int kb = 0; kb < KB; ++kb)
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-          if (r < nq) {
-            x0 = *reinterpret_cast<const float4 *>(qrow + kb * 64 + c * 8);
-            x1 = *reinterpret_cast<const float4 *>(qrow + kb * 64 + c * 8 + 4);
-          }
-          uint4 v;
-          v.x = pack_bf16x2(x0.x * qscale, x0.y * qscale);
-          v.y = pack_bf16x2(x0.z * qscale, x0.w * qscale);
-          v.z = pack_bf16x2(x1.x * qscale, x1.y * qscale);
-          v.w = pack_bf16x2(x1.z * qscale, x1.w * qscale);
-          *reinterpret_cast<uint4 *>(qs + kb * (kFaM * 128) + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+      for (int t = hh * KB * 4; t < (hh + 1) * KB * 4; ++t) {
+        const int kb = t / 8, c = t % 8;
+        float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+        if (r < nq) {
+          x0 = *reinterpret_cast<const float4 *>(qrow + kb * 64 + c * 8);
+          x1 = *reinterpret_cast<const float4 *>(qrow + kb * 64 + c * 8 + 4);
         }
+        uint4 v;
+        v.x = pack_bf16x2(x0.x * qscale, x0.y * qscale);
+        v.y = pack_bf16x2(x0.z * qscale, x0.w * qscale);
+        v.z = pack_bf16x2(x1.x * qscale, x1.y * qscale);
+        v.w = pack_bf16x2(x1.z * qscale, x1.w * qscale);
+        *reinterpret_cast<uint4 *>(qs + kb * (kFaM * 128) + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+      }
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(q_ready);
     }
+    constexpr int kHalfS = kFaN / 2, kHalfO = HS / 2;
     const int qpos = first + r;
-    const uint32_t lanes = (uint32_t)(warp * 32) << 16;
+    const uint32_t lanes = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t colS = kColS + hh * kHalfS, colP = kColP + hh * (kHalfS / 2), colO = kColO + hh * kHalfO;
+    unsigned *cnt = &pair_count[warp & 3];
+    // posts this warp's value for row r, then waits (bounded) until the
+    // partner warp has posted `target` times in all; returns its value
+    auto exchange = [&](float *mine, float *theirs, float v, unsigned target, unsigned where, float *out) {
+      *mine = v;
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) atomicAdd(cnt, 1u);
+      bool done_ok = true;
+      if (lane == 0) {
+        const unsigned long long t0 = globaltimer();
+        while (*reinterpret_cast<volatile unsigned *>(cnt) < target) {
+          if (globaltimer() - t0 > kWaitLimitNs) {
+            report_timeout(&g_llama_status, where);
+            done_ok = false;
+            break;
+          }
+        }
+      }
+      done_ok = __shfl_sync(0xffffffffu, done_ok ? 1 : 0, 0) != 0;
+      __syncwarp();  // orders lane 0's observation before every lane's read
+      __threadfence_block();
+      *out = *reinterpret_cast<volatile float *>(theirs);
+      return done_ok;
+    };
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < ntiles && ok; ++j) {
       ok = warp_wait(s_full, j & 1, &g_llama_status, 910u) && !aborted();
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[kFaN];
+      uint32_t sv[kHalfS];
 #pragma unroll
-      for (int q = 0; q < kFaN / 32; ++q)
-        tmem_ld_32x32b_x32(tbase + lanes + kColS + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(sv + 32 * q));
+      for (int q = 0; q < kHalfS / 32; ++q)
+        tmem_ld_32x32b_x32(tbase + lanes + colS + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(sv + 32 * q));
       tmem_ld_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
-      const int k0 = j * kFaN;
-      const int kmax = min(qpos, last) - k0;  // last valid column of this row
+      const int kmax = min(qpos, last) - j * kFaN - hh * kHalfS;  // last valid column of this half
       float tmax = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < kFaN; ++i) {
+      for (int i = 0; i < kHalfS; ++i) {
         const float sc = i <= kmax ? __uint_as_float(sv[i]) : -INFINITY;
         sv[i] = __float_as_uint(sc);
         tmax = fmaxf(tmax, sc);
       }
-      const float m_new = fmaxf(m, tmax);  // finite: key 0 is valid for every row
+      float other;
+      ok = exchange(&pair_max[j & 1][hh][r], &pair_max[j & 1][hh ^ 1][r], tmax, 2u * (j + 1), 921u, &other);
+      ok = __all_sync(0xffffffffu, ok) && !aborted();
+      if (!ok) break;
+      const float m_new = fmaxf(m, fmaxf(tmax, other));  // finite: key 0 is valid for every row
       const float alpha = ex2_approx(m - m_new);  // 2^-inf = 0 on the first tile
       float rs = 0.f;
-      uint32_t pk[kFaN / 2];
+      uint32_t pk[kHalfS / 2];
 #pragma unroll
-      for (int i = 0; i < kFaN / 2; ++i) {
+      for (int i = 0; i < kHalfS / 2; ++i) {
         // masked scores are -inf: 2^-inf = 0
         pk[i] = pack_bf16x2(ex2_approx(__uint_as_float(sv[2 * i]) - m_new),
                             ex2_approx(__uint_as_float(sv[2 * i + 1]) - m_new));
         rs += bf16_lo(pk[i]) + bf16_hi(pk[i]);
       }
-      l = l * alpha + rs;
+      l = l * alpha + rs;  // this half's sum; the halves share m and alpha
       m = m_new;
       if (j > 0) {  // O and P are free once the previous tile's O += P V is done
         ok = warp_wait(o_ready, (j - 1) & 1, &g_llama_status, 911u) && !aborted();
@@ -826,33 +865,35 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int q = 0; q < HS / 32; ++q) {
+          for (int q = 0; q < kHalfO / 32; ++q) {
             uint32_t ov[32];
-            tmem_ld_32x32b_x32(tbase + lanes + kColO + 32 * q, ov);
+            tmem_ld_32x32b_x32(tbase + lanes + colO + 32 * q, ov);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-            tmem_st_32x32b_x32(tbase + lanes + kColO + 32 * q, ov);
+            tmem_st_32x32b_x32(tbase + lanes + colO + 32 * q, ov);
           }
         }
       }
-#pragma unroll
-      for (int q = 0; q < kFaN / 64; ++q)
-        tmem_st_32x32b_x32(tbase + lanes + kColP + 32 * q, *reinterpret_cast<const uint32_t(*)[32]>(pk + 32 * q));
+      tmem_st_32x32b_x32(tbase + lanes + colP, *reinterpret_cast<const uint32_t(*)[32]>(pk));
       tmem_st_wait();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
     }
-    if (!ok) *abort_v = 1;
+    float l_other = 0.f;
+    if (ok) {
+      ok = exchange(&pair_l[hh][r], &pair_l[hh ^ 1][r], l, 2u * (ntiles + 1), 922u, &l_other);
+      ok = __all_sync(0xffffffffu, ok);
+    }
     if (ok && warp_wait(o_ready, (ntiles - 1) & 1, &g_llama_status, 912u)) {
       tc_fence_after();
-      const float inv = 1.f / l;
-      uint16_t *dst = att + (size_t)(b * per_seq + c0 + r) * dim + h * HS;
+      const float inv = 1.f / (l + l_other);
+      uint16_t *dst = att + (size_t)(b * per_seq + c0 + r) * dim + h * HS + hh * kHalfO;
 #pragma unroll
-      for (int q = 0; q < HS / 32; ++q) {
+      for (int q = 0; q < kHalfO / 32; ++q) {
         uint32_t ov[32];
-        tmem_ld_32x32b_x32(tbase + lanes + kColO + 32 * q, ov);
+        tmem_ld_32x32b_x32(tbase + lanes + colO + 32 * q, ov);
         tmem_ld_wait();
         if (r < nq) {
 #pragma unroll
@@ -869,7 +910,7 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
     } else {
       *abort_v = 1;
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     if (lane == 0) {
       const long long head_row = layer_row + ((long long)b * kv_heads + kvh) * seq_len;
       int k_issued = 0, v_issued = 0;  // tiles whose K / V copies were started
@@ -964,7 +1005,7 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 5) tmem_dealloc(tbase, Lay::tmem_cols);
+  if (warp == 9) tmem_dealloc(tbase, Lay::tmem_cols);
 }
 
 // Prefill helpers: the chunk's prompt tokens in row order (row b * per_seq + c
