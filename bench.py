@@ -9,9 +9,14 @@ Metric: TFLOP/s of the step (2*B*N*K per step) and ms per step.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-N > 1 (torchrun, one rank per GPU): every rank runs the same step on its own
-batch (batch rows are independent; no data-path collective): weak scaling,
-value = all ranks' FLOPs / max-over-ranks time.
+N > 1 (torchrun, one rank per GPU): the same step row-sharded over the ranks
+(strong scaling): rank r multiplies the whole normalized batch by its
+contiguous slice of W's rows, the slice GEMM's epilogue stores its tiles into
+every rank's output over NVLink (peer memory), and the row-independent
+normalized / softmax rows are split by batch rows; value = the step's FLOPs /
+max-over-ranks time. The NCCL all-gather join and the whole trio repeated on
+every rank (replicas) are reported beside it, and every rank's product is
+checked bit for bit against the single-GPU plan inside the run.
 --impl reference: the CPU arm (rank 0 only): the oracle's multithreaded fp32
 restatement of the same step on a bounded sample of batch rows.
 """
@@ -342,6 +347,81 @@ def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=10
                                  "layer) plus its rows of every NVFP4 weight once per step"}}
 
 
+def decoder_shard_parity(ce, dev, stream, dist, world, per_gpu=64, kv_fill=1024, steps=4, layers=2):
+    """Multi-GPU parity of the row-sharded decoder inside the run (N > 1):
+    the 7B shape cut to `layers` layers, NVFP4 weights, batch per_gpu x N,
+    `steps` greedy steps with the peer-memory exchange, against the same
+    model unsharded on every rank's own GPU (same seed). With the
+    unsharded model's splits (CE_LLAMA_REPRODUCIBLE_SPLITS) every step's
+    gathered logits, the tokens and the residual stream must be bitwise
+    equal; with the shards' own splits (the timed configuration) the logits
+    must stay within relative L2 2e-5 and the greedy tokens agree on >= 99.9%.
+    Raises if either fails."""
+    import torch
+    import importlib
+    rs = importlib.import_module("cuda_elastic_b200.rowshard")
+    cfg = dict(LLAMA_7B, n_layers=layers)
+    batch = per_gpu * world
+    tokens0 = np.random.default_rng(0).integers(0, cfg["vocab_size"], batch).astype(np.int32)
+
+    def run(model, step):
+        with torch.cuda.stream(stream):
+            model.init_random(seed=1, weight_std=0.02, kv_fill=kv_fill)
+            model.start(tokens0, kv_fill)
+            logits = []
+            for _ in range(steps):
+                step()
+                torch.cuda.synchronize(dev)
+                local = torch.from_numpy(np.ascontiguousarray(model.logits())).to(dev)
+                if model.world > 1:
+                    parts = [torch.empty_like(local) for _ in range(world)]
+                    dist.all_gather(parts, local)
+                    local = torch.cat(parts, dim=1)
+                logits.append(local.double())
+        ce.llama_status()
+        return logits, model.generated().copy(), model.read(ce.LLAMA_RESIDUAL, dtype=np.float32)
+
+    res = {}
+    for repro in (True, False):
+        with torch.cuda.stream(stream):
+            sh = rs.ShardedLlama(ce, cfg, batch, steps, ce.PREC_NVFP4_E2M1, mode="p2p", reproducible=repro)
+        res[repro] = run(sh.model, sh.step)
+        sh.close()
+    m = ce.Llama(cfg, batch, steps, precision=ce.PREC_NVFP4_E2M1, stream=stream.cuda_stream)
+    ref = run(m, m.step)
+    m.close()
+    (rl, rg, rx), (dl, dg, dx), (ul, ug, ux) = res[True], res[False], ref
+    bitwise = (all(torch.equal(a, b) for a, b in zip(rl, ul)) and np.array_equal(rg, ug)
+               and np.array_equal(rx, ux))
+    # default splits: compare each step on the sequences whose inputs agree
+    first = np.full(batch, steps)
+    for b in range(batch):
+        d = np.nonzero(dg[b] != ug[b])[0]
+        if len(d):
+            first[b] = d[0]
+    worst = 0.0
+    for s in range(steps):
+        rows = torch.from_numpy(np.nonzero(first >= s)[0]).to(dev)
+        if len(rows):
+            a, b = dl[s][rows], ul[s][rows]
+            worst = max(worst, float((a - b).norm() / b.norm().clamp_min(1e-30)))
+    agree = float((dg == ug).mean())
+    flags = torch.tensor([1.0 if bitwise else 0.0, worst, agree], device=dev, dtype=torch.float64)
+    lo = flags.clone()
+    dist.all_reduce(lo[0:1], op=dist.ReduceOp.MIN)
+    dist.all_reduce(lo[1:2], op=dist.ReduceOp.MAX)
+    dist.all_reduce(lo[2:3], op=dist.ReduceOp.MIN)
+    out = {"model": f"7B shape cut to {layers} layers, NVFP4, batch {batch}, cache to {kv_fill - 1}, "
+                    f"{steps} greedy steps, peer-memory exchange", "ranks_checked": world,
+           "reproducible_splits_bitwise_equal": bool(lo[0].item() == 1.0),
+           "default_splits": {"max_logit_rel_l2": float(lo[1].item()), "token_agreement": float(lo[2].item()),
+                              "bound_rel_l2": 2e-5}}
+    if not (out["reproducible_splits_bitwise_equal"] and out["default_splits"]["max_logit_rel_l2"] <= 2e-5
+            and out["default_splits"]["token_agreement"] >= 0.999):
+        raise RuntimeError(f"sharded decoder parity failed: {out}")
+    return out
+
+
 def llama_prefill(ce, dev, stream, s, dist, world, peaks_tflops, which):
     """Prompt prefill (ce_llama_enqueue_prefill) of a 512-token prompt per
     sequence from position 0: the 110M shape (bf16 weights, batch 256,
@@ -401,6 +481,210 @@ def llama_prefill(ce, dev, stream, s, dist, world, peaks_tflops, which):
                                  "against the measured bf16 dense peak (sustained)"}}
 
 
+def sharded_share_rows(world, rank):
+    base, extra = divmod(BATCH, world)
+    return base + (1 if rank < extra else 0)
+
+
+def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, peak_tflops, clocks_sampler):
+    """The op trio row-sharded over the ranks (strong
+    scaling: the same 1024 x 16384 batch and 8192 x 16384 matrix whatever
+    the rank count). Rank r holds W's rows [lo, hi); every rank normalizes
+    the whole batch (its slice GEMM needs every row) but writes only its
+    share of the fp32 normalized and softmax rows; the slice GEMM's epilogue
+    stores its tiles into every rank's output over NVLink (the fused
+    peer-memory join) and a bounded wait collects the peers' slices. The
+    NCCL join (ncclAllGather through the C ABI + the join kernel) is timed
+    beside it. Each rank's gathered product and its rows share are checked
+    bit for bit against the single-GPU plan on its own GPU."""
+    import torch
+    import importlib
+    rs = importlib.import_module("cuda_elastic_b200.rowshard")
+    x, w, logits = host
+    s = stream.cuda_stream
+    dx, dw, dl = (torch.from_numpy(a).to(dev) for a in (x, w, logits))
+    norm = torch.empty((BATCH, SIZE), device=dev)
+    soft = torch.empty((BATCH, SIZE), device=dev)
+
+    def barrier():
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    res = {}
+    for mode in ("p2p", "nccl"):
+        sh = rs.RowShardedPlan(ce, BATCH, SIZE, ROWS, ce.PREC_BF16, mode=mode, exchanges=2)
+        sh.set_weights(dW)
+        lo, hi = sh.lo, sh.hi
+        width = (ROWS + world - 1) // world
+
+        def step(i, ev=None):
+            sh.rows_stage(norm, soft, dx, dw, dl, stream=s)
+            if ev is not None:
+                ev[0].record(stream)
+            if mode == "p2p":
+                sh.local.gemm_rowx(sh.xs[i % 2], stream=s)
+                if ev is not None:
+                    ev[1].record(stream)
+                sh.xs[i % 2].wait(stream=s)
+            else:
+                sh.local.gemm_ld(sh.slots[i % 2], width, stream=s)
+                if ev is not None:
+                    ev[1].record(stream)
+                ce.allgather_rows(sh.comm, sh.outs[i % 2], sh.staging[i % 2], BATCH, ROWS, world, rank, stream=s)
+
+        with torch.cuda.stream(stream):
+            for i in range(max(3, args.warmup)):
+                step(i)
+        ce.device_status()
+        barrier()
+        if mode == "p2p":
+            clocks_sampler.start()
+            time.sleep(0.3)
+            barrier()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            t0.record(stream)
+            for i in range(args.steps):
+                ev[i][2].record(stream)
+                step(i, ev[i])
+                ev[i][3].record(stream)
+            t1.record(stream)
+        barrier()
+        if mode == "p2p":
+            res["clocks"] = clocks_sampler.stop()
+        ce.device_status()
+        total = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+        rows_ms = float(np.mean([e[2].elapsed_time(e[0]) for e in ev]))
+        gemm_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+        join_ms = float(np.mean([e[1].elapsed_time(e[3]) for e in ev]))
+        # the slice GEMM alone (no exchange) for the exchange's share
+        alone = torch.empty((BATCH, hi - lo), device=dev)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                sh.local.gemm(alone, stream=s)
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(10):
+                sh.local.gemm(alone, stream=s)
+            a1.record(stream)
+        torch.cuda.synchronize(dev)
+        alone_ms = a0.elapsed_time(a1) / 10
+        # in-run parity: the gathered product and the rows share against the
+        # single-GPU plan on this GPU (same operands, same k order: bitwise)
+        ref_out = torch.empty((BATCH, ROWS), device=dev)
+        ref_norm = torch.empty((BATCH, SIZE), device=dev)
+        ref_soft = torch.empty((BATCH, SIZE), device=dev)
+        with torch.cuda.stream(stream):
+            norm.fill_(float("nan"))
+            soft.fill_(float("nan"))
+            step(0)
+            ref_plan.trio(ref_norm, ref_soft, ref_out, dx, dw, dl, stream=s)
+        torch.cuda.synchronize(dev)
+        got = sh.outs[0]
+        b_lo, b_hi = sh.b_lo, sh.b_hi
+        out_equal = bool(torch.equal(got, ref_out))
+        max_rel = float(((got - ref_out).abs().max() / ref_out.abs().max().clamp_min(1e-30)).item())
+        share_equal = bool(torch.equal(norm[b_lo:b_hi], ref_norm[b_lo:b_hi]) and
+                           torch.equal(soft[b_lo:b_hi], ref_soft[b_lo:b_hi]))
+        ok = torch.tensor([1.0 if (out_equal and share_equal) else 0.0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        res[mode] = {"ms_per_step": total, "rows_ms": rows_ms,
+                     ("gemm_with_fused_exchange_ms" if mode == "p2p" else "slice_gemm_ms"): gemm_ms,
+                     ("exchange_wait_ms" if mode == "p2p" else "allgather_join_ms"): join_ms,
+                     "slice_gemm_alone_ms": alone_ms,
+                     "exchange_share": (gemm_ms + join_ms - alone_ms) / total if mode == "p2p"
+                     else join_ms / total,
+                     "parity": {"ranks_bitwise_equal_to_1gpu_plan": bool(ok.item() == 1.0),
+                                "this_rank_out_equal": out_equal, "this_rank_rows_share_equal": share_equal,
+                                "max_rel_diff": max_rel, "checked": "all 1024 x 8192 outputs and this rank's "
+                                                                    "rows share, every rank"}}
+        if not ok.item() == 1.0:
+            raise RuntimeError(f"row-sharded trio ({mode}) differs from the single-GPU plan: {res[mode]}")
+        if mode == "p2p":
+            res["slice"] = (lo, hi)
+            res["e2e"] = sharded_e2e(ce, dev, stream, dist, world, sh, host, dx, dw, dl, args)
+        sh.close()
+    return res
+
+
+def sharded_e2e(ce, dev, stream, dist, world, sh, host, dx, dw, dl, args):
+    """End to end through the row-shard API with pinned host buffers: every
+    step copies the whole batch x and this rank's share of the logits in,
+    and its share of the normalized, softmax and product rows out (the union
+    over ranks is the step's full output, nothing copied twice). Two buffer
+    sets and two exchanges pipeline neighbouring steps as at one GPU."""
+    import torch
+    x, w, logits = host
+    s = stream.cuda_stream
+    b_lo, b_hi = sh.b_lo, sh.b_hi
+    hx = torch.from_numpy(x).pin_memory()
+    hl = torch.from_numpy(logits[b_lo:b_hi]).pin_memory()
+    slots = []
+    for k in range(2):
+        din = (torch.empty_like(dx), torch.empty_like(dl))
+        dout = (torch.empty_like(dx), torch.empty_like(dx))
+        hout = (torch.empty((b_hi - b_lo, SIZE), pin_memory=True), torch.empty((b_hi - b_lo, SIZE), pin_memory=True),
+                torch.empty((b_hi - b_lo, ROWS), pin_memory=True))
+        slots.append((din, dout, hout, torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()))
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    n = max(4, min(args.steps, 12))
+
+    def e2e_step(i):
+        (dxk, dlk), (nk, sk), (hnk, hsk, hok), in_ready, comp_done, out_done = slots[i % 2]
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(comp_done)
+            dxk.copy_(hx, non_blocking=True)
+            dlk[b_lo:b_hi].copy_(hl, non_blocking=True)
+            in_ready.record(s_in)
+        stream.wait_event(in_ready)
+        stream.wait_event(out_done)
+        with torch.cuda.stream(stream):
+            sh.rows_stage(nk, sk, dxk, dw, dlk, stream=s)
+            out = sh.gemm(slot=i % 2, stream=s)
+            comp_done.record(stream)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(comp_done)
+            hnk.copy_(nk[b_lo:b_hi], non_blocking=True)
+            hsk.copy_(sk[b_lo:b_hi], non_blocking=True)
+            hok.copy_(out[b_lo:b_hi], non_blocking=True)
+            out_done.record(s_out)
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s_in)
+    for i in range(n):
+        e2e_step(i)
+    e1.record(s_out)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    ce.device_status()
+    ms = e0.elapsed_time(e1) / n
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if not all(torch.equal(a, c) for a, c in zip(slots[0][2], slots[1][2])):
+        raise RuntimeError("pipelined sharded end-to-end steps disagree between buffer sets")
+    # bytes of the whole job (every rank's copies)
+    nb = torch.tensor([hx.numel() * 4 + hl.numel() * 4, sum(t.numel() * 4 for t in slots[0][2])],
+                      device=dev, dtype=torch.float64)
+    dist.all_reduce(nb)
+    return {"value": flops_per_step() / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "h2d_bytes_per_step": int(nb[0].item()), "d2h_bytes_per_step": int(nb[1].item()), "ms_per_step": ms,
+            "pipeline": "every rank: the whole batch x and its logits share in, its share of the normalized, "
+                        "softmax and product rows out (bytes summed over ranks); 2 buffer sets and exchanges; "
+                        "host->device, compute and device->host streams"}
+
+
 def run_ours(args, rank, world, local_rank):
     import torch
     import __graft_entry__
@@ -415,12 +699,14 @@ def run_ours(args, rank, world, local_rank):
                                 device_id=dev)
 
     prec = {"bf16": ce.PREC_BF16, "tf32": ce.PREC_TF32, "fp32": ce.PREC_FP32}[args.precision]
-    # every rank: its own batch (seed = rank), the same matrix
-    x, w, logits, W = ce.trio_inputs_host(rank, BATCH, SIZE, ROWS)
+    # the same batch and matrix on every rank (the row-sharded trio splits
+    # one problem; the replica trio repeats it)
+    x, w, logits, W = ce.trio_inputs_host(0, BATCH, SIZE, ROWS)
     plan = ce.Plan(BATCH, SIZE, ROWS, prec)
     dW = torch.from_numpy(W).to(dev)
     plan.set_weights(dW)
-    del dW
+    if world == 1:
+        del dW
     dx, dw, dl = (torch.from_numpy(a).to(dev) for a in (x, w, logits))
     norm = torch.empty((BATCH, SIZE), device=dev)
     soft = torch.empty((BATCH, SIZE), device=dev)
@@ -460,8 +746,9 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- timed region: K steps, events around each GEMM launch ----
     sampler = ClockSampler(local_rank)
-    sampler.start()
-    time.sleep(0.3)
+    if world == 1:
+        sampler.start()
+        time.sleep(0.3)
     barrier()
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     mids = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
@@ -476,7 +763,7 @@ def run_ours(args, rank, world, local_rank):
             ends[i].record(stream)
         t1.record(stream)
     barrier()
-    clocks = sampler.stop()
+    clocks = sampler.stop() if world == 1 else None
     ce.device_status()
     total_ms = t0.elapsed_time(t1)
     gemm_ms = float(np.mean([mids[i].elapsed_time(ends[i]) for i in range(args.steps)]))
@@ -488,65 +775,78 @@ def run_ours(args, rank, world, local_rank):
     ms_per_step = total_ms / args.steps
     value = world * flops_per_step() / (ms_per_step * 1e-3) / 1e12
 
-    # ---- end to end through the C ABI with pinned host buffers: every step
-    # copies its inputs in and its outputs out inside the timed region. Two
-    # buffer sets and three streams overlap step i's device->host copies with
-    # step i+1's host->device copies (the two copy engines) and its compute;
-    # events keep a set's inputs until its compute has read them and its
-    # outputs until they are on the host ----
-    hx = torch.from_numpy(x).pin_memory()
-    hl = torch.from_numpy(logits).pin_memory()
-    slots = []
-    for k in range(2):
-        din = (dx, dl) if k == 0 else (torch.empty_like(dx), torch.empty_like(dl))
-        dout = (norm, soft, out) if k == 0 else (torch.empty_like(norm), torch.empty_like(soft), torch.empty_like(out))
-        hout = (torch.empty((BATCH, SIZE), pin_memory=True), torch.empty((BATCH, SIZE), pin_memory=True),
-                torch.empty((BATCH, ROWS), pin_memory=True))
-        slots.append((din, dout, hout, torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()))
-    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
-    e2e_steps = max(4, min(args.steps, 12))
+    # ---- row-sharded trio over the ranks (N > 1 headline) ----
+    sharded = None
+    if world > 1:
+        pk0, _ = peaks()
+        sharded = trio_sharded(ce, dev, stream, dist, world, rank, (x, w, logits), dW, plan, args,
+                               pk0.get("bf16_tflops", 1590.0), sampler)
+        del dW
+        clocks = sharded.pop("clocks")
+        e2e = sharded.pop("e2e")
+    else:
+        # ---- end to end through the C ABI with pinned host buffers: every step
+        # copies its inputs in and its outputs out inside the timed region. Two
+        # buffer sets and three streams overlap step i's device->host copies with
+        # step i+1's host->device copies (the two copy engines) and its compute;
+        # events keep a set's inputs until its compute has read them and its
+        # outputs until they are on the host ----
+        hx = torch.from_numpy(x).pin_memory()
+        hl = torch.from_numpy(logits).pin_memory()
+        slots = []
+        for k in range(2):
+            din = (dx, dl) if k == 0 else (torch.empty_like(dx), torch.empty_like(dl))
+            dout = (norm, soft, out) if k == 0 else (torch.empty_like(norm), torch.empty_like(soft), torch.empty_like(out))
+            hout = (torch.empty((BATCH, SIZE), pin_memory=True), torch.empty((BATCH, SIZE), pin_memory=True),
+                    torch.empty((BATCH, ROWS), pin_memory=True))
+            slots.append((din, dout, hout, torch.cuda.Event(), torch.cuda.Event(), torch.cuda.Event()))
+        s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        e2e_steps = max(4, min(args.steps, 12))
 
-    def e2e_step(i):
-        (dxk, dlk), (nk, sk, ok), (hnk, hsk, hok), in_ready, comp_done, out_done = slots[i % 2]
-        with torch.cuda.stream(s_in):
-            s_in.wait_event(comp_done)  # the set's previous compute has read its inputs
-            dxk.copy_(hx, non_blocking=True)
-            dlk.copy_(hl, non_blocking=True)
-            in_ready.record(s_in)
-        stream.wait_event(in_ready)
-        stream.wait_event(out_done)  # the set's previous outputs are on the host
-        with torch.cuda.stream(stream):
-            plan.trio(nk, sk, ok, dxk, dw, dlk, stream=s)
-            comp_done.record(stream)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(comp_done)
-            hnk.copy_(nk, non_blocking=True)
-            hsk.copy_(sk, non_blocking=True)
-            hok.copy_(ok, non_blocking=True)
-            out_done.record(s_out)
+        def e2e_step(i):
+            (dxk, dlk), (nk, sk, ok), (hnk, hsk, hok), in_ready, comp_done, out_done = slots[i % 2]
+            with torch.cuda.stream(s_in):
+                s_in.wait_event(comp_done)  # the set's previous compute has read its inputs
+                dxk.copy_(hx, non_blocking=True)
+                dlk.copy_(hl, non_blocking=True)
+                in_ready.record(s_in)
+            stream.wait_event(in_ready)
+            stream.wait_event(out_done)  # the set's previous outputs are on the host
+            with torch.cuda.stream(stream):
+                plan.trio(nk, sk, ok, dxk, dw, dlk, stream=s)
+                comp_done.record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(comp_done)
+                hnk.copy_(nk, non_blocking=True)
+                hsk.copy_(sk, non_blocking=True)
+                hok.copy_(ok, non_blocking=True)
+                out_done.record(s_out)
 
-    for i in range(2):
-        e2e_step(i)
-    barrier()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(s_in)
-    for i in range(e2e_steps):
-        e2e_step(i)
-    e1.record(s_out)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / e2e_steps
-    t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
-    if dist is not None:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t.item())
-    e2e_value = world * flops_per_step() / (e2e_ms * 1e-3) / 1e12
-    hn, hs, ho = slots[0][2]
-    # both buffer sets computed the same inputs: their host copies agree bit for bit
-    if not all(torch.equal(a, c) for a, c in zip(slots[0][2], slots[1][2])):
-        raise RuntimeError("pipelined end-to-end steps disagree between buffer sets")
-    h2d = hx.numel() * 4 + hl.numel() * 4
-    d2h = hn.numel() * 4 + hs.numel() * 4 + ho.numel() * 4
+        for i in range(2):
+            e2e_step(i)
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(s_in)
+        for i in range(e2e_steps):
+            e2e_step(i)
+        e1.record(s_out)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / e2e_steps
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        if dist is not None:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        e2e_value = world * flops_per_step() / (e2e_ms * 1e-3) / 1e12
+        hn, hs, ho = slots[0][2]
+        # both buffer sets computed the same inputs: their host copies agree bit for bit
+        if not all(torch.equal(a, c) for a, c in zip(slots[0][2], slots[1][2])):
+            raise RuntimeError("pipelined end-to-end steps disagree between buffer sets")
+        h2d = hx.numel() * 4 + hl.numel() * 4
+        d2h = hn.numel() * 4 + hs.numel() * 4 + ho.numel() * 4
+        e2e = {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+               "pipeline": "2 buffer sets; host->device, compute and device->host streams"}
 
     # ---- legacy llama2c iteration (reference semantics: GEMV on input row 0) ----
     mat = torch.empty((ROWS, SIZE), device=dev)
@@ -631,9 +931,13 @@ def run_ours(args, rank, world, local_rank):
 
     # ---- Llama-2 7B decode: row-sharded over the ranks ----
     llama7b = {}
+    if not args.no_llama7b and world > 1:
+        shard_parity = decoder_shard_parity(ce, dev, stream, dist, world)
     if not args.no_llama7b:
         llama7b = llama7b_decode(ce, dev, stream, dist, world, peaks()[0].get("hbm_gbs", 6650.0),
                                  exchange=args.exchange)
+        if world > 1:
+            llama7b["shard_parity"] = shard_parity
 
     # ---- prompt prefill (110M bf16, 7B NVFP4), 512-token prompts ----
     prefill = {}
@@ -657,29 +961,71 @@ def run_ours(args, rank, world, local_rank):
                "sample": f"{srows} of {BATCH} batch rows through rmsnorm, softmax and the "
                          f"8192x16384 GEMM (fp32, {dt:.1f} s)"}
 
+    replicas = {"ms_per_step": ms_per_step, "value": value, "unit": "TFLOP/s",
+                "rows_ms": rows_ms, "gemm_ms": gemm_ms,
+                "parallelism": f"dp{world} (the whole trio on every rank, no collective)"}
+    if sharded is not None:
+        # the headline at N > 1: one 1024 x 16384 x 8192 step split over the ranks
+        p2p = sharded["p2p"]
+        lo, hi = sharded["slice"]
+        ms_head = p2p["ms_per_step"]
+        value_head = flops_per_step() / (ms_head * 1e-3) / 1e12
+        gemm_head = p2p["gemm_with_fused_exchange_ms"]
+        achieved_head = 2.0 * BATCH * (hi - lo) * SIZE / (gemm_head * 1e-3) / 1e12
+        nvlink_bytes = BATCH * (hi - lo) * 4 * (world - 1)
+        peak_head = pk.get("bf16_tflops", 1590.0)
+        roofline = {"bound": "tensor", "achieved": achieved_head, "peak": peak_head, "unit": "TFLOP/s",
+                    "frac": achieved_head / peak_head, "traffic": None,
+                    "peak_source": f"{pk_kind} burst bf16",
+                    "kernel": "slice GEMM with the fused peer-memory exchange (rank 0's slice)",
+                    "nvlink": {"bytes_out_per_rank": nvlink_bytes, "link_gbps": 770.0,
+                               "floor_ms": nvlink_bytes / 770e9 * 1e3,
+                               "tensor_floor_ms": 2.0 * BATCH * (hi - lo) * SIZE / (peak_head * 1e12) * 1e3,
+                               "note": "the slower of the tensor floor and the NVLink floor (every other rank's "
+                                       "copy of this rank's slice at the measured 770 GB/s peer rate) bounds "
+                                       "the fused kernel"}}
+        rows_bytes = 4.0 * BATCH * SIZE + 2.0 * BATCH * SIZE + SIZE * 4 + \
+            3 * 4.0 * (sharded_share_rows(world, rank)) * SIZE
+        rows_roof = {"bound": "hbm", "achieved": rows_bytes / (p2p["rows_ms"] * 1e-3) / 1e9,
+                     "peak": pk.get("hbm_gbs", 6650.0), "unit": "GB/s",
+                     "note": "every batch row read and its bf16 operand written; fp32 normalized and softmax "
+                             "(read + write) only for this rank's batch share"}
+        head = {"value": value_head, "ms_per_step": ms_head, "scaling": "strong",
+                "parallelism": f"tp{world}: W split by output rows ({hi - lo} per rank), the slice GEMM's epilogue "
+                               f"storing its tiles into every rank's output over NVLink (peer memory, CUDA IPC); "
+                               f"NCCL all-gather join timed beside it",
+                "gpu_launches": 3 * args.steps, "kernels_ms": {"rows": p2p["rows_ms"],
+                                                               "gemm_fused_exchange": gemm_head,
+                                                               "exchange_wait": p2p["exchange_wait_ms"]}}
+    else:
+        roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": traffic,
+                    "peak_source": f"{pk_kind} {'sustained' if long_region else 'burst'} bf16"}
+        rows_roof = {"bound": "hbm", "achieved": (4.0 * BATCH * SIZE * 4 + BATCH * SIZE * 2 + SIZE * 4)
+                     / (rows_ms * 1e-3) / 1e9, "peak": pk.get("hbm_gbs", 6650.0), "unit": "GB/s"}
+        head = {"value": value, "ms_per_step": ms_per_step, "scaling": "weak",
+                "parallelism": "single GPU", "gpu_launches": 2 * args.steps,
+                "kernels_ms": {"rows": rows_ms, "gemm": gemm_ms}}
+
     if dist is not None:
         dist.barrier()
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "metric": METRIC, "value": head["value"], "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head["ms_per_step"],
+            "higher_is_better": True, "scaling": head["scaling"], "vs_baseline": None,
             "dtype": args.precision if args.precision != "fp32" else "f32",
             "data": "synthetic",
             "config": {"workload": "llama2c op trio 1024x16384x8192: fused rmsnorm+softmax rows "
                                    "launch (fp32) then the tcgen05 GEMM on the normalized batch",
                        "batch": BATCH, "size": SIZE, "rows": ROWS, "precision": args.precision,
-                       "parallelism": f"dp{world} (independent batches, no collective)",
+                       "parallelism": head["parallelism"],
                        "l2": "inputs larger than L2 (x and logits 64 MiB each, W 256 MiB bf16); "
                              "no flush between steps"},
-            "gpu_launches": 2 * args.steps,
-            "kernels_ms": {"rows": rows_ms, "gemm": gemm_ms},
-            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": traffic,
-                         "peak_source": f"{pk_kind} {'sustained' if long_region else 'burst'} bf16"},
-            "rows_roofline": {"bound": "hbm", "achieved": (4.0 * BATCH * SIZE * 4 + BATCH * SIZE * 2 + SIZE * 4)
-                              / (rows_ms * 1e-3) / 1e9, "peak": pk.get("hbm_gbs", 6650.0),
-                              "unit": "GB/s"},
+            "gpu_launches": head["gpu_launches"],
+            "kernels_ms": head["kernels_ms"],
+            "roofline": roofline,
+            "rows_roofline": rows_roof,
             "legacy_iteration": {"ms_per_iter": legacy_ms, "min_bytes_per_iter": min_bytes,
                                  "achieved_gbps": min_bytes / (legacy_ms * 1e-3) / 1e9},
             "gemm_precisions": precisions,
@@ -689,11 +1035,12 @@ def run_ours(args, rank, world, local_rank):
             "llama_decode": llama,
             "llama7b_decode": llama7b,
             "llama_prefill": prefill,
-            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                    "pipeline": "2 buffer sets; host->device, compute and device->host streams"},
+            "e2e": e2e,
             "clocks": clocks,
         }
+        if sharded is not None:
+            line["row_sharded"] = {"p2p": sharded["p2p"], "nccl": sharded["nccl"], "slice_rows": hi - lo}
+            line["replicas"] = replicas
         line["rows_roofline"]["frac"] = line["rows_roofline"]["achieved"] / line["rows_roofline"]["peak"]
         if cpu is not None:
             line["cpu_baseline"] = cpu

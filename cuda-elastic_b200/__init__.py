@@ -35,6 +35,7 @@ PREC_MXFP6_E3M2 = 4
 PREC_NVFP4_E2M1 = 5
 
 RMS_EPS = 1.0e-5  # kRmsEpsilon, llama2c/llama2c_common.h:44
+NCCL_ID_BYTES = 128  # CE_NCCL_ID_BYTES
 
 _lib = None
 
@@ -127,6 +128,7 @@ _SIGNATURES = {
     "ce_llama_read_nvfp4": [_vp, _i, _i, _vp, _vp, _vp],
     "ce_llama_validate_shard": [_vp, _i, _i, _i, _i, _i],
     "ce_llama_create_shard": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _i, _i, _vp],
+    "ce_llama_create_shard_ex": [ctypes.POINTER(_vp), _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_llama_bind_exchange": [_vp, _vp, _vp, _vp, _vp],
     "ce_llama_exchange_open": [_vp, _vp],
     "ce_llama_prefill_reserve": [_vp, _i],
@@ -143,6 +145,22 @@ _SIGNATURES = {
     "ce_llama_read": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_write": [_vp, _i, _i, _vp, _i64, _i64],
     "ce_llama_status": [],
+    "ce_plan_gemm_ld": [_vp, _vp, _i, _vp],
+    "ce_plan_rows_range": [_vp, _vp, _vp, _vp, _vp, _vp, _f, _i, _i, _vp],
+    "ce_shard_bounds": [_i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)],
+    "ce_set_wait_limit": [ctypes.c_double],
+    "ce_nccl_version": [ctypes.POINTER(_i)],
+    "ce_nccl_unique_id": [_vp],
+    "ce_nccl_comm_init": [ctypes.POINTER(_vp), _i, _i, _vp],
+    "ce_nccl_comm_destroy": [_vp],
+    "ce_allgather_staging_floats": [_i, _i, _i, ctypes.POINTER(ctypes.c_size_t)],
+    "ce_allgather_rows": [_vp, _vp, _vp, _i, _i, _i, _i, _vp],
+    "ce_rowx_open": [ctypes.POINTER(_vp), _i, _i, _i, _i, _vp],
+    "ce_rowx_connect": [_vp, ctypes.c_char_p],
+    "ce_rowx_output": [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_i), ctypes.POINTER(_i)],
+    "ce_plan_gemm_rowx": [_vp, _vp, _vp],
+    "ce_rowx_wait": [_vp, _vp],
+    "ce_rowx_close": [_vp],
 }
 _RESTYPES = {"ce_version": ctypes.c_char_p}
 
@@ -545,6 +563,119 @@ class Plan:
         check(lib().ce_plan_operands(self._h, _ptr(a), _ptr(w), _stream(stream)))
         return a, w
 
+    def rows_range(self, normalized, softmax_out, x, norm_w, logits, row_lo, row_hi, eps=RMS_EPS,
+                   stream=None):
+        """Rows stage of one row-shard rank: the GEMM operand of every batch
+        row, the fp32 normalized and softmax rows only for [row_lo, row_hi)."""
+        check(lib().ce_plan_rows_range(self._h, _ptr(normalized), _ptr(softmax_out), _ptr(x), _ptr(norm_w),
+                                       _ptr(logits), eps, row_lo, row_hi, _stream(stream)))
+
+    def gemm_ld(self, out, ldd, stream=None):
+        """The GEMM into out [batch][ldd] (ldd >= rows)."""
+        check(lib().ce_plan_gemm_ld(self._h, _ptr(out), ldd, _stream(stream)))
+        return out
+
+    def gemm_rowx(self, rowx, stream=None):
+        """This rank's slice GEMM, its tiles stored into every rank's
+        exchange output (RowExchange)."""
+        check(lib().ce_plan_gemm_rowx(self._h, rowx._h, _stream(stream)))
+
+
+def set_wait_limit(seconds):
+    """Limit of every bounded device wait launched afterwards on the
+    current device (2 s by default)."""
+    check(lib().ce_set_wait_limit(float(seconds)))
+
+
+def shard_bounds(rows, world, rank):
+    """[lo, hi) of rank's contiguous slice of `rows` (ce_shard_bounds)."""
+    lo, hi = _i(), _i()
+    check(lib().ce_shard_bounds(rows, world, rank, ctypes.byref(lo), ctypes.byref(hi)))
+    return lo.value, hi.value
+
+
+class _DeviceArray:
+    """A library-owned device buffer as a CUDA array (for torch.as_tensor)."""
+
+    def __init__(self, ptr, shape, typestr="<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class RowExchange:
+    """Peer-memory join of the row-shard GEMM (ce_rowx_*): this rank's
+    out [batch][rows] in device memory shared by CUDA IPC. open() returns the
+    IPC handle; gather every rank's handle in rank order and call connect()."""
+
+    def __init__(self, batch, rows, world, rank):
+        self.batch, self.rows, self.world, self.rank = batch, rows, world, rank
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(lib().ce_rowx_open(ctypes.byref(h), batch, rows, world, rank, buf))
+        self._h = h
+        self.handle = buf.raw
+        p, lo, hi = ctypes.c_void_p(), _i(), _i()
+        check(lib().ce_rowx_output(h, ctypes.byref(p), ctypes.byref(lo), ctypes.byref(hi)))
+        self.lo, self.hi = lo.value, hi.value
+        import torch
+        self.output = torch.as_tensor(_DeviceArray(p.value, (batch, rows)), device="cuda")
+
+    def connect(self, handles):
+        check(lib().ce_rowx_connect(self._h, b"".join(handles)))
+
+    def wait(self, stream=None):
+        check(lib().ce_rowx_wait(self._h, _stream(stream)))
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            self.output = None
+            lib().ce_rowx_close(self._h)
+            self._h = None
+
+
+class NcclComm:
+    """An NCCL communicator made through the library (ce_nccl_*); `uid` is
+    the CE_NCCL_ID_BYTES that rank 0 got from nccl_unique_id()."""
+
+    def __init__(self, world, rank, uid):
+        h = ctypes.c_void_p()
+        check(lib().ce_nccl_comm_init(ctypes.byref(h), world, rank, uid))
+        self._h, self.world, self.rank = h, world, rank
+
+    @property
+    def handle(self):
+        return self._h.value
+
+    def close(self):
+        if getattr(self, "_h", None) is not None and self._h.value:
+            lib().ce_nccl_comm_destroy(self._h)
+            self._h = None
+
+
+def nccl_unique_id():
+    buf = ctypes.create_string_buffer(NCCL_ID_BYTES)
+    check(lib().ce_nccl_unique_id(buf))
+    return buf.raw
+
+
+def nccl_version():
+    v = _i()
+    check(lib().ce_nccl_version(ctypes.byref(v)))
+    return v.value
+
+
+def allgather_staging_floats(batch, rows, world):
+    n = ctypes.c_size_t()
+    check(lib().ce_allgather_staging_floats(batch, rows, world, ctypes.byref(n)))
+    return n.value
+
+
+def allgather_rows(comm, out, staging, batch, rows, world, rank, stream=None):
+    """NCCL join of the row-shard slices (ce_allgather_rows)."""
+    check(lib().ce_allgather_rows(comm.handle if isinstance(comm, NcclComm) else comm, _ptr(out), _ptr(staging),
+                                  batch, rows, world, rank, _stream(stream)))
+    return out
+
 
 class Decoder:
     """The loom_private llama2c decoder workload (B sequences x S greedy steps
@@ -610,6 +741,7 @@ LLAMA_KCACHE, LLAMA_VCACHE, LLAMA_LOGITS, LLAMA_TOKENS = 9, 10, 11, 12
 LLAMA_GENERATED, LLAMA_POS, LLAMA_RESIDUAL = 13, 14, 15
 IPC_HANDLE_BYTES = 64  # CE_IPC_HANDLE_BYTES
 SEG_ATTN, SEG_OPROJ, SEG_FFN_IN, SEG_FFN_OUT, SEG_HEAD, SEG_PICK = 0, 1, 2, 3, 4, 5
+LLAMA_REPRODUCIBLE_SPLITS = 1  # CE_LLAMA_REPRODUCIBLE_SPLITS
 
 
 class LlamaConfig(ctypes.Structure):
@@ -636,15 +768,15 @@ class Llama:
     for every sequence (capturable; position and step counters are on the
     device, so a captured step replays for every token)."""
 
-    def __init__(self, cfg, batch, max_steps, precision=PREC_BF16, stream=None, rank=0, world=1):
+    def __init__(self, cfg, batch, max_steps, precision=PREC_BF16, stream=None, rank=0, world=1, flags=0):
         self.cfg = cfg if isinstance(cfg, LlamaConfig) else llama_config(**cfg)
         self.batch, self.max_steps, self.precision = batch, max_steps, precision
         self.rank, self.world = rank, world
         self.hs = self.cfg.dim // self.cfg.n_heads
         self.kv_dim = self.hs * self.cfg.n_kv_heads // world  # this shard's k (and v) rows
         h = ctypes.c_void_p()
-        check(lib().ce_llama_create_shard(ctypes.byref(h), ctypes.byref(self.cfg), batch, max_steps,
-                                          precision, rank, world, _stream(stream)))
+        check(lib().ce_llama_create_shard_ex(ctypes.byref(h), ctypes.byref(self.cfg), batch, max_steps,
+                                             precision, rank, world, flags, _stream(stream)))
         self._h = h
 
     def close(self):

@@ -21,7 +21,8 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    const float *weight, float *softmax, const float *logits, float *product,
                    const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
                    int cols, int gemv_rows, float eps, cudaStream_t s,
-                   uint8_t *normalized_e4m3 = nullptr, int ld_e4m3 = 0, float *e4m3_scale = nullptr);
+                   uint8_t *normalized_e4m3 = nullptr, int ld_e4m3 = 0, float *e4m3_scale = nullptr,
+                   int norm_lo = 0, int norm_hi = 0x7fffffff);
 int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
 size_t w4t_packed_bytes(int N, int K);
 int w4t_expand_f16(uint16_t *out, const uint8_t *packed, int N, int K, cudaStream_t s);
@@ -49,6 +50,15 @@ int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uin
             int ld_bytes, int nsf, cudaStream_t s, const int *row_map = nullptr);
 int gemm_status();
 int gemm_bs_status();
+int rowx_status();
+int gemm_set_wait_limit(unsigned long long ns);
+int gemm_bs_set_wait_limit(unsigned long long ns);
+int llama_set_wait_limit(unsigned long long ns);
+int rowx_set_wait_limit(unsigned long long ns);
+int rowx_sync(const ce_rowx *x, RowxSync *rx, float **out, int *lo, int *hi, int *batch, int *rows);
+int x_device_of(const ce_rowx *x);
+int gemm_rowx(int kind, float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
+              int ldd, const float *row_scale, const float *col_scale, const RowxSync &rx, cudaStream_t s);
 int pack_mxfp6(uint8_t *operand, const uint8_t *codes, int rows, int cols, int ld_codes,
                int ld_operand, cudaStream_t s);
 int sf_katoms(int fmt, int K);
@@ -201,7 +211,19 @@ int ce_device_info(int *sms, int *sm100) {
 int ce_device_status(void) {
   const int a = gemm_status();
   const int b = gemm_bs_status();
-  return a != CE_OK ? a : b;
+  const int c = rowx_status();
+  return a != CE_OK ? a : b != CE_OK ? b : c;
+}
+
+int ce_set_wait_limit(double seconds) {
+  CE_REQUIRE(seconds >= 1e-3 && seconds <= 3600.0, "wait limit must be in [0.001, 3600] s (got %g)", seconds);
+  const unsigned long long ns = (unsigned long long)(seconds * 1e9);
+  for (int (*set)(unsigned long long) :
+       {gemm_set_wait_limit, gemm_bs_set_wait_limit, llama_set_wait_limit, rowx_set_wait_limit}) {
+    const int rc = set(ns);
+    if (rc != CE_OK) return set_error(rc, "cudaMemcpyToSymbol(wait limit) failed");
+  }
+  return CE_OK;
 }
 
 int ce_fill_llama2c_host(int random, uint64_t seed, int batch, int size, int rows, float *input,
@@ -632,32 +654,33 @@ int ce_plan_set_weights(ce_plan *p, const float *w, ce_stream_t stream) {
   return CE_OK;
 }
 
-static int plan_gemm(ce_plan *p, float *out, cudaStream_t s) {
+static int plan_gemm(ce_plan *p, float *out, cudaStream_t s, int ldd = 0) {
+  if (ldd == 0) ldd = p->rows;
   switch (p->precision) {
     case CE_PREC_MXFP6_E3M2:
       return gemm_mxfp6(out, static_cast<const uint8_t *>(p->activations), p->a_atoms,
                         static_cast<const uint8_t *>(p->weights), p->w_atoms, p->batch, p->rows,
-                        p->size, p->size, p->size, p->rows, s);
+                        p->size, p->size, p->size, ldd, s);
     case CE_PREC_NVFP4_E2M1:
       return gemm_nvfp4(out, static_cast<const uint8_t *>(p->activations), p->a_atoms, p->a_ts + 1,
                         static_cast<const uint8_t *>(p->weights), p->w_atoms, p->w_ts + 1, p->batch,
-                        p->rows, p->size, p->size / 2, p->size / 2, p->rows, s);
+                        p->rows, p->size, p->size / 2, p->size / 2, ldd, s);
     case CE_PREC_BF16:
       return gemm_bf16(out, static_cast<const uint16_t *>(p->activations),
                        static_cast<const uint16_t *>(p->weights), p->batch, p->rows, p->size,
-                       p->ld, p->ld, p->rows, nullptr, nullptr, 0, s);
+                       p->ld, p->ld, ldd, nullptr, nullptr, 0, s);
     case CE_PREC_FP8_E4M3:
       return gemm_e4m3(out, static_cast<const uint8_t *>(p->activations),
                        static_cast<const uint8_t *>(p->weights), p->batch, p->rows, p->size, p->ld,
-                       p->ld, p->rows, p->a_scale, p->w_scale, 0, s);
+                       p->ld, ldd, p->a_scale, p->w_scale, 0, s);
     case CE_PREC_TF32:
       return gemm_tf32(out, static_cast<const float *>(p->activations),
                        static_cast<const float *>(p->weights), p->batch, p->rows, p->size, p->ld,
-                       p->ld, p->rows, nullptr, nullptr, 0, s);
+                       p->ld, ldd, nullptr, nullptr, 0, s);
     default:
       return gemm_simt_fp32(out, static_cast<const float *>(p->activations),
                             static_cast<const float *>(p->weights), p->batch, p->rows, p->size,
-                            p->ld, p->ld, p->rows, s);
+                            p->ld, p->ld, ldd, s);
   }
 }
 
@@ -770,10 +793,67 @@ int ce_plan_rows(ce_plan *p, float *normalized, float *softmax, const float *x,
   return plan_rows(p, normalized, softmax, x, norm_w, logits, eps, (cudaStream_t)stream);
 }
 
+int ce_plan_rows_range(ce_plan *p, float *normalized, float *softmax, const float *x, const float *norm_w,
+                       const float *logits, float eps, int row_lo, int row_hi, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && x && norm_w, "null argument");
+  CE_REQUIRE((logits == nullptr) == (softmax == nullptr), "logits and softmax go together");
+  CE_REQUIRE(0 <= row_lo && row_lo <= row_hi && row_hi <= p->batch, "row range [%d, %d) is outside the batch of %d",
+             row_lo, row_hi, p->batch);
+  CE_REQUIRE(p->precision == CE_PREC_BF16 || p->precision == CE_PREC_FP8_E4M3,
+             "a row range of the rows stage needs a bf16 or fp8 plan (precision %d)", p->precision);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int nsoft = logits ? row_hi - row_lo : 0;
+  const size_t off = (size_t)row_lo * p->size;
+  float *sm = softmax ? softmax + off : nullptr;
+  const float *lg = logits ? logits + off : nullptr;
+  if (p->precision == CE_PREC_FP8_E4M3)
+    return rows_iteration(normalized, nullptr, 0, x, norm_w, sm, lg, nullptr, nullptr, nullptr, p->batch, nsoft,
+                          p->size, 0, eps, s, static_cast<uint8_t *>(p->activations), p->ld, p->a_scale, row_lo,
+                          row_hi);
+  return rows_iteration(normalized, static_cast<uint16_t *>(p->activations), p->ld, x, norm_w, sm, lg, nullptr,
+                        nullptr, nullptr, p->batch, nsoft, p->size, 0, eps, s, nullptr, 0, nullptr, row_lo, row_hi);
+}
+
 int ce_plan_gemm(ce_plan *p, float *out, ce_stream_t stream) {
   CE_REQUIRE(p != nullptr && out != nullptr, "null argument");
   CE_REQUIRE(p->has_weights, "ce_plan_set_weights has not been called");
   return plan_gemm(p, out, (cudaStream_t)stream);
+}
+
+int ce_plan_gemm_ld(ce_plan *p, float *out, int ldd, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && out != nullptr, "null argument");
+  CE_REQUIRE(p->has_weights, "ce_plan_set_weights has not been called");
+  CE_REQUIRE(ldd >= p->rows, "output row stride %d is below the plan's %d rows", ldd, p->rows);
+  return plan_gemm(p, out, (cudaStream_t)stream, ldd);
+}
+
+int ce_plan_gemm_rowx(ce_plan *p, ce_rowx *x, ce_stream_t stream) {
+  CE_REQUIRE(p != nullptr && x != nullptr, "null argument");
+  CE_REQUIRE(p->has_weights, "ce_plan_set_weights has not been called");
+  RowxSync rx;
+  float *out = nullptr;
+  int lo = 0, hi = 0, batch = 0, rows = 0;
+  int rc = rowx_sync(x, &rx, &out, &lo, &hi, &batch, &rows);
+  if (rc) return rc;
+  CE_REQUIRE(p->batch == batch && p->rows == hi - lo,
+             "the plan (batch %d, rows %d) is not this rank's slice of the exchange (batch %d, rows %d..%d)",
+             p->batch, p->rows, batch, lo, hi);
+  CE_REQUIRE(p->device == x_device_of(x), "plan and exchange are on different devices");
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (p->precision) {
+    case CE_PREC_BF16:
+      return gemm_rowx(0, out + lo, p->activations, p->weights, p->batch, p->rows, p->size, p->ld, p->ld, rows,
+                       nullptr, nullptr, rx, s);
+    case CE_PREC_TF32:
+      return gemm_rowx(1, out + lo, p->activations, p->weights, p->batch, p->rows, p->size, p->ld, p->ld, rows,
+                       nullptr, nullptr, rx, s);
+    case CE_PREC_FP8_E4M3:
+      return gemm_rowx(2, out + lo, p->activations, p->weights, p->batch, p->rows, p->size, p->ld, p->ld, rows,
+                       p->a_scale, p->w_scale, rx, s);
+    default:
+      return set_error(CE_ERR_USAGE, format("the row-shard fan-out GEMM supports bf16, tf32 and fp8 plans "
+                                            "(precision %d)", p->precision));
+  }
 }
 
 int ce_plan_rmsnorm_gemm(ce_plan *p, float *out, float *normalized, const float *x,

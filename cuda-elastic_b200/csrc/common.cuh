@@ -1,8 +1,9 @@
 // Shared helpers of libce_b200: status reporting, launch checks and the
 // sm_100a PTX wrappers (mbarrier, TMA, tcgen05) used by the tensor-core
 // kernels. Every device-side wait here is bounded: it gives up after
-// kWaitLimitNs of wall time (read from %globaltimer), records where it gave
-// up in a device status word, and returns false so the caller can unwind.
+// wait_limit_ns() of wall time (read from %globaltimer), records where it
+// gave up in a device status word, and returns false so the caller can
+// unwind.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -54,7 +55,20 @@ struct DeviceStatus {
 // ---------------------------------------------------------------------------
 // Device-side helpers
 
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+// Wall-time limit of every bounded wait (2 s unless ce_set_wait_limit
+// changes it). Each translation unit that includes this header holds its own
+// copy on each device; set_wait_limit_here() writes the copy of the unit it
+// is compiled into, on the current device.
+static __device__ unsigned long long g_wait_limit_ns = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *reinterpret_cast<volatile unsigned long long *>(&g_wait_limit_ns);
+}
+
+[[maybe_unused]] static int set_wait_limit_here(unsigned long long ns) {
+  const cudaError_t e = cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns));
+  return e == cudaSuccess ? CE_OK : CE_ERR_CUDA;
+}
 
 __device__ __forceinline__ unsigned long long globaltimer() {
   unsigned long long t;
@@ -105,7 +119,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 }
 
 // Waits until the phase with the given parity has completed. Returns false
-// (and records the site) when kWaitLimitNs passes first, or when another
+// (and records the site) when wait_limit_ns() passes first, or when another
 // thread of the grid already reported a failure.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, DeviceStatus *st,
                                           unsigned where) {
@@ -114,7 +128,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, Device
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 255u) == 0u) {
-      if (globaltimer() - start > kWaitLimitNs) {
+      if (globaltimer() - start > wait_limit_ns()) {
         report_timeout(st, where);
         return false;
       }
@@ -211,7 +225,7 @@ __device__ __forceinline__ bool exchange_wait_warp(const ExchangeWait &w, Device
         const unsigned long long now = globaltimer();
         if (start == 0) {
           start = now;
-        } else if (now - start > kWaitLimitNs) {
+        } else if (now - start > wait_limit_ns()) {
           report_timeout(st, where);
           ok = false;
           break;
@@ -233,6 +247,84 @@ __device__ __forceinline__ void exchange_signal(const ExchangePut &p) {
     const unsigned long long epoch = exchange_epoch(p.gen, p.step, p.per_step, p.index);
     for (int q = 0; q < p.world; ++q)
       if (q != p.rank) st_release_sys(reinterpret_cast<unsigned long long *>(p.blocks[q] + p.flag_off), epoch);
+  }
+}
+
+// --- row-shard exchange of the op-trio GEMM (rowshard.cu) -------------------
+// Rank r of `world` multiplies by its contiguous slice of W's rows; the GEMM's
+// epilogue stores each output tile into every rank's [batch][rows] output
+// (peer memory mapped by CUDA IPC, plain NVLink stores). Two flags per rank
+// pair order the exchange, both in the receiver's block:
+//   ready[q]  rank q may be sent exchange e: q's GEMM for e has started, so
+//             every consumer of q's exchange e - 1 (earlier on q's stream)
+//             is done; a sender waits for it before its first peer store;
+//   done[q]   every CTA of q's GEMM for e has stored and fenced; the
+//             receiver's rowx_wait_kernel waits for it, then advances its
+//             exchange counter (e = counter + 1, in device memory, so a
+//             captured graph advances it on every replay).
+constexpr int kRowxMaxRanks = 8;
+struct RowxSync {
+  uint8_t *blocks[kRowxMaxRanks] = {};      // every rank's exchange block as mapped here (own included)
+  size_t ready_off = 0, done_off = 0;       // byte offsets of ready[] / done[] (u64 per rank) in a block
+  const unsigned long long *epoch = nullptr;  // this rank's count of completed exchanges
+  int *counter = nullptr;                   // arrival counter of the GEMM's CTAs (reset by the last)
+  int world = 0, rank = 0;                  // world <= 1: no fan-out
+};
+
+__device__ __forceinline__ unsigned long long rowx_exchange(const RowxSync &rx) {
+  return *reinterpret_cast<const volatile unsigned long long *>(rx.epoch) + 1ull;
+}
+
+// One thread per CTA of the sending GEMM, after its launch wait: tells every
+// peer that this rank accepts exchange e (idempotent; every CTA sends it, so
+// no CTA's progress depends on another being resident).
+__device__ __forceinline__ void rowx_signal_ready(const RowxSync &rx) {
+  const unsigned long long e = rowx_exchange(rx);
+  for (int q = 0; q < rx.world; ++q)
+    if (q != rx.rank)
+      st_release_sys(reinterpret_cast<unsigned long long *>(rx.blocks[q] + rx.ready_off) + rx.rank, e);
+}
+
+// One warp: lane q waits (bounded) until peer q accepts exchange e.
+__device__ __forceinline__ bool rowx_wait_ready_warp(const RowxSync &rx, DeviceStatus *st, unsigned where) {
+  const int q = threadIdx.x & 31;
+  bool ok = true;
+  if (q < rx.world && q != rx.rank) {
+    const unsigned long long e = rowx_exchange(rx);
+    const unsigned long long *flag =
+        reinterpret_cast<const unsigned long long *>(rx.blocks[rx.rank] + rx.ready_off) + q;
+    unsigned long long start = 0;
+    for (uint32_t spin = 1; ld_acquire_sys(flag) < e; ++spin) {
+      if ((spin & 1023u) == 0u) {
+        const unsigned long long now = globaltimer();
+        if (start == 0) {
+          start = now;
+        } else if (now - start > wait_limit_ns()) {
+          report_timeout(st, where);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  return __all_sync(0xffffffffu, ok) != 0;
+}
+
+// Every thread of every CTA of the sending GEMM, after its last store: the
+// last CTA to arrive tells every peer that exchange e has landed. Contains
+// __syncthreads.
+__device__ __forceinline__ void rowx_signal_done(const RowxSync &rx) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned long long e = rowx_exchange(rx);
+    if (atomicAdd(rx.counter, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
+      *rx.counter = 0;
+      __threadfence_system();
+      for (int q = 0; q < rx.world; ++q)
+        if (q != rx.rank)
+          st_release_sys(reinterpret_cast<unsigned long long *>(rx.blocks[q] + rx.done_off) + rx.rank, e);
+    }
   }
 }
 
@@ -281,7 +373,7 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait_cluster(bar, parity)) return true;
     if ((spin & 255u) == 0u) {
-      if (globaltimer() - start > kWaitLimitNs) {
+      if (globaltimer() - start > wait_limit_ns()) {
         report_timeout(st, where);
         return false;
       }

@@ -101,7 +101,36 @@ struct GemmArgs {
   uint16_t *out_bf16;  // bf16, or fp16 when out_f16
   int ld_out;
   int out_f16;
+  // Row-shard fan-out (ce_plan_gemm_rowx): d points into this rank's block
+  // of the exchange, and every output row piece is also stored at the same
+  // offset of each peer's block (rx.world <= 1: none).
+  RowxSync rx;
 };
+
+// 32 consecutive fp32 outputs of one row (n_valid of them inside the matrix).
+__device__ __forceinline__ void store_row32(float *dst, const float (&v)[32], int n_valid, bool vec) {
+  if (vec && n_valid >= 32) {
+    float4 *d4 = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) d4[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < n_valid) dst[j] = v[j];
+  }
+}
+
+// The epilogue's plain output: this rank's d, then (row-shard fan-out) the
+// same offset of every peer's block.
+__device__ __forceinline__ void store_out32(const GemmArgs &args, float *dst, const float (&v)[32], int n_valid,
+                                            bool vec, bool peers) {
+  store_row32(dst, v, n_valid, vec);
+  if (peers) {
+    const ptrdiff_t off = dst - reinterpret_cast<float *>(args.rx.blocks[args.rx.rank]);
+    for (int q = 0; q < args.rx.world; ++q)
+      if (q != args.rx.rank) store_row32(reinterpret_cast<float *>(args.rx.blocks[q]) + off, v, n_valid, vec);
+  }
+}
 
 // SwiGLU epilogue of one row's 32 accumulator columns starting at col0 (even).
 __device__ __forceinline__ void store_swiglu(const GemmArgs &args, int row, int col0, const float (&v)[32]) {
@@ -206,6 +235,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   }
   pdl_launch_dependents();
   pdl_wait();
+  if (args.rx.world > 1 && threadIdx.x == 0) rowx_signal_ready(args.rx);
 
   if (warp == 0) {
     // ---------------- TMA producer (lane 0 issues; the warp stays converged)
@@ -291,6 +321,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
   } else {
     // ---------------- Epilogue (warps 2-5)
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
+    // row-shard fan-out: every peer accepts this exchange before any store
+    const bool peers_ok = args.rx.world > 1 && rowx_wait_ready_warp(args.rx, st, 70);
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -321,15 +353,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
           }
           if (args.epilogue == 1) {
             store_swiglu(args, row, col0, v);
-          } else if (vec_ok && col0 + 32 <= args.N) {
-            float4 *dst = reinterpret_cast<float4 *>(drow + col0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.N) drow[col0 + j] = v[j];
+            store_out32(args, drow + col0, v, args.N - col0, vec_ok, peers_ok);
           }
         }
         __syncwarp();
@@ -345,6 +370,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+  if (args.rx.world > 1) rowx_signal_done(args.rx);
 }
 
 // ---------------------------------------------------------------------------
@@ -431,6 +457,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   }
   pdl_launch_dependents();
   pdl_wait();
+  if (args.rx.world > 1 && threadIdx.x == 0) rowx_signal_ready(args.rx);
   const uint32_t full0_leader = cluster_map(smem_u32(&full[0]), 0);
   const uint32_t tmem_empty0_leader = cluster_map(smem_u32(&tmem_empty[0]), 0);
 
@@ -528,6 +555,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   } else {
     // ---------------- Epilogue (warps 2-5 of both CTAs)
     const int quarter = warp & 3;
+    const bool peers_ok = args.rx.world > 1 && rowx_wait_ready_warp(args.rx, st, 71);
     int local = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++local) {
       const int acc = local & 1;
@@ -558,15 +586,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
           if (args.epilogue == 1) {
             store_swiglu(args, row, col0, v);
-          } else if (vec_ok && col0 + 32 <= args.N) {
-            float4 *dst = reinterpret_cast<float4 *>(drow + col0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.N) drow[col0 + j] = v[j];
+            store_out32(args, drow + col0, v, args.N - col0, vec_ok, peers_ok);
           }
         }
         __syncwarp();
@@ -583,6 +604,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+  if (args.rx.world > 1) rowx_signal_done(args.rx);
 }
 
 // ---------------------------------------------------------------------------
@@ -906,15 +928,8 @@ gemm_w4a16_kernel(const __grid_constant__ CUtensorMap tmA, W4Args wargs) {
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
           if (args.epilogue == 1) {
             store_swiglu(args, row, col0, v);
-          } else if (vec_ok && col0 + 32 <= args.N) {
-            float4 *dst = reinterpret_cast<float4 *>(drow + col0);
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < args.N) drow[col0 + j] = v[j];
+            store_out32(args, drow + col0, v, args.N - col0, vec_ok, false);
           }
         }
         __syncwarp();
@@ -1068,7 +1083,7 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
                   int ldd, const float *row_scale, const float *col_scale, int force_bn,
                   int force_group, cudaStream_t s, int splits = 1, long long split_stride = 0,
                   bool pdl = false, uint16_t *swiglu_out = nullptr, int swiglu_ld = 0,
-                  const float *alpha = nullptr) {
+                  const float *alpha = nullptr, const RowxSync *rx = nullptr) {
   constexpr int elem = Kind<kKind>::elem;
   const CUtensorMapDataType dt = kKind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                  : kKind == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -1123,6 +1138,12 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.out_bf16 = swiglu_out;
   args.ld_out = swiglu_ld;
   args.out_f16 = kKind == 3 ? 1 : 0;
+  if (rx != nullptr && rx->world > 1) {
+    CE_REQUIRE(splits == 1 && swiglu_out == nullptr, "the row-shard fan-out needs one split and the plain epilogue");
+    CE_REQUIRE(rx->world <= kRowxMaxRanks && rx->rank >= 0 && rx->rank < rx->world,
+               "row-shard rank %d of %d is out of range", rx->rank, rx->world);
+    args.rx = *rx;
+  }
   const int tiles = args.tiles_m * args.tiles_n * splits;
   if (c.pair) {
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
@@ -1615,6 +1636,26 @@ int gemm_e4m3(float *d, const uint8_t *a, const uint8_t *b, int M, int N, int K,
                           force_group, s);
 }
 
+// Row-shard GEMM (ce_plan_gemm_rowx): the plain GEMM of one rank's slice of
+// W's rows whose epilogue also stores every output piece into each peer's
+// exchange block, ordered by the ready / done flags of rx (common.cuh).
+// kind: 0 bf16, 1 tf32, 2 e4m3 (row_scale / col_scale as for gemm_e4m3).
+int gemm_rowx(int kind, float *d, const void *a, const void *b, int M, int N, int K, int lda, int ldb,
+              int ldd, const float *row_scale, const float *col_scale, const RowxSync &rx, cudaStream_t s) {
+  switch (kind) {
+    case 0:
+      return gemm_dispatch<0>(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, 0, s, 1, 0, false,
+                              nullptr, 0, nullptr, &rx);
+    case 1:
+      return gemm_dispatch<1>(d, a, b, M, N, K, lda, ldb, ldd, nullptr, nullptr, 0, 0, s, 1, 0, false,
+                              nullptr, 0, nullptr, &rx);
+    case 2:
+      return gemm_dispatch<2>(d, a, b, M, N, K, lda, ldb, ldd, row_scale, col_scale, 0, 0, s, 1, 0, false,
+                              nullptr, 0, nullptr, &rx);
+  }
+  return set_error(CE_ERR_USAGE, format("no row-shard GEMM for operand kind %d", kind));
+}
+
 // Split-K bf16 GEMM: split s of `splits` accumulates its balanced range of
 // k-blocks and writes its fp32 partial at d + s * split_stride; the caller
 // sums the partials (in split order, so the result is deterministic). pdl:
@@ -1990,6 +2031,8 @@ int gemm_set_prefetch(int kblocks) {
   g_prefetch_kblocks = kblocks;
   return CE_OK;
 }
+
+int gemm_set_wait_limit(unsigned long long ns) { return set_wait_limit_here(ns); }
 
 // Synchronizes the device, reads and clears the GEMM status word.
 int gemm_status() {

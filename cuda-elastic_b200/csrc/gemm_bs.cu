@@ -465,6 +465,8 @@ int gemm_nvfp4(float *d, const uint8_t *a, const uint8_t *sfa, const float *alph
   return launch_bs<1>(d, a, sfa, alpha_a, b, sfb, alpha_b, M, N, K, lda_bytes, ldb_bytes, ldd, s);
 }
 
+int gemm_bs_set_wait_limit(unsigned long long ns) { return set_wait_limit_here(ns); }
+
 int gemm_bs_status() {
   CE_CUDA_TRY(cudaDeviceSynchronize());
   DeviceStatus h{};

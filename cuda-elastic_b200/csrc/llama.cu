@@ -82,6 +82,8 @@ int w4t_expand_f16(uint16_t *out, const uint8_t *packed, int N, int K, cudaStrea
 
 static __device__ DeviceStatus g_llama_status;
 
+int llama_set_wait_limit(unsigned long long ns) { return set_wait_limit_here(ns); }
+
 namespace {
 
 using rowops::block_max;
@@ -807,7 +809,7 @@ attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_con
       if (lane == 0) {
         const unsigned long long t0 = globaltimer();
         while (*reinterpret_cast<volatile unsigned *>(cnt) < target) {
-          if (globaltimer() - t0 > kWaitLimitNs) {
+          if (globaltimer() - t0 > wait_limit_ns()) {
             report_timeout(&g_llama_status, where);
             done_ok = false;
             break;
@@ -1814,9 +1816,10 @@ int ce_llama_validate_shard(const ce_llama_config *c, int batch, int max_steps, 
   return llama_memory_check(c, batch, precision, world);
 }
 
-int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
-                          int precision, int rank, int world, ce_stream_t stream) {
+int ce_llama_create_shard_ex(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
+                             int precision, int rank, int world, int flags, ce_stream_t stream) {
   CE_REQUIRE(out != nullptr, "null model pointer");
+  CE_REQUIRE((flags & ~CE_LLAMA_REPRODUCIBLE_SPLITS) == 0, "unknown shard flags 0x%x", flags);
   *out = nullptr;
   if (int rc = ce_llama_validate_shard(cfg, batch, max_steps, precision, rank, world)) return rc;
   if (int rc = configure_attention()) return rc;
@@ -1836,7 +1839,11 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
   m->kv_dim = m->hs * m->lKH;  // this shard's k (and v) rows
   m->qkv_rows = m->lD + 2 * m->kv_dim;
   m->nv = pow2_at_least((cfg->dim / 4 + kRowThreads - 1) / kRowThreads);
-  m->attn_splits = attn_choose_splits(m->hs, (long long)batch * m->lH, cfg->seq_len);
+  // CE_LLAMA_REPRODUCIBLE_SPLITS: the attention and split-K GEMM splits of
+  // the unsharded model, so every value this rank computes is summed in the
+  // unsharded model's order (the same bits, at the cost of fewer CTAs)
+  const bool repro = (flags & CE_LLAMA_REPRODUCIBLE_SPLITS) != 0;
+  m->attn_splits = attn_choose_splits(m->hs, (long long)batch * (repro ? cfg->n_heads : m->lH), cfg->seq_len);
   m->layer_kv = (size_t)batch * m->lKH * cfg->seq_len * m->hs;
   // split-K for the GEMMs whose tiles alone leave SMs idle at decode sizes;
   // at least 4 k-blocks (256 of K) per split
@@ -1844,10 +1851,10 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
     return precision == CE_PREC_NVFP4_E2M1 ? gemm_w4t_auto_splits(batch, N, K, 8)
                                            : gemm_bf16_auto_splits(batch, N, K, 8, 4);
   };
-  m->sp_qkv = splits(m->qkv_rows, cfg->dim);
-  m->sp_o = splits(m->lD, cfg->dim);
-  m->sp_13 = splits(2 * m->lHd, cfg->dim);
-  m->sp_2 = splits(m->lD, cfg->hidden_dim);
+  m->sp_qkv = splits(repro ? cfg->dim + 2 * m->hs * cfg->n_kv_heads : m->qkv_rows, cfg->dim);
+  m->sp_o = splits(repro ? cfg->dim : m->lD, cfg->dim);
+  m->sp_13 = splits(repro ? 2 * cfg->hidden_dim : 2 * m->lHd, cfg->dim);
+  m->sp_2 = splits(repro ? cfg->dim : m->lD, cfg->hidden_dim);
   const int sp_delta = m->sp_o > m->sp_2 ? m->sp_o : m->sp_2;
   const ce_llama_config &c = *cfg;
   const size_t L = c.n_layers;
@@ -1932,9 +1939,14 @@ int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch,
   return CE_OK;
 }
 
+int ce_llama_create_shard(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
+                          int precision, int rank, int world, ce_stream_t stream) {
+  return ce_llama_create_shard_ex(out, cfg, batch, max_steps, precision, rank, world, 0, stream);
+}
+
 int ce_llama_create(ce_llama **out, const ce_llama_config *cfg, int batch, int max_steps,
                     int precision, ce_stream_t stream) {
-  return ce_llama_create_shard(out, cfg, batch, max_steps, precision, 0, 1, stream);
+  return ce_llama_create_shard_ex(out, cfg, batch, max_steps, precision, 0, 1, 0, stream);
 }
 
 int ce_llama_destroy(ce_llama *m) {
@@ -2899,6 +2911,8 @@ int ce_llama_status(void) {
   CE_CUDA_TRY(cudaMemcpyToSymbol(g_llama_status, &zero, sizeof(zero)));
   if (h.where == 900u) return set_error(CE_ERR_USAGE, "decode position reached the end of the KV cache");
   if (h.where == 901u) return set_error(CE_ERR_USAGE, "prefill positions reached the end of the KV cache");
+  if (h.where == 920u || h.where == 923u || (h.where >= 930u && h.where <= 934u))  // peer flag waits
+    return set_error(CE_ERR_TIMEOUT, format("peer exchange wait gave up (site %u, block %u)", h.where, h.block));
   return set_error(CE_ERR_TIMEOUT, format("attention staging wait gave up (site %u, block %u)", h.where, h.block));
 }
 

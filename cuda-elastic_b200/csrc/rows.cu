@@ -81,6 +81,7 @@ struct IterationWork {
   int softmax_rows;
   int gemv_rows;
   float eps;
+  int norm_lo, norm_hi;  // the fp32 normalized output covers rmsnorm rows [norm_lo, norm_hi)
 };
 
 template <int NV>
@@ -108,18 +109,19 @@ iteration_kernel(IterationWork w) {
       return;
     }
   }
+  float *const normalized = rms_row >= w.norm_lo && rms_row < w.norm_hi ? w.normalized : nullptr;
   if (rms_row >= 0 && w.normalized_e4m3 != nullptr) {
     const size_t off = (size_t)rms_row * cols4;
     rmsnorm_row_e4m3<NV>(reinterpret_cast<const float4 *>(w.input) + off,
                          reinterpret_cast<const float4 *>(w.weight),
-                         w.normalized ? reinterpret_cast<float4 *>(w.normalized) + off : nullptr,
+                         normalized ? reinterpret_cast<float4 *>(normalized) + off : nullptr,
                          w.normalized_e4m3 + (size_t)rms_row * w.ld_e4m3_4, w.e4m3_scale + rms_row,
                          cols4, w.cols, w.eps, scratch);
   } else if (rms_row >= 0) {
     const size_t off = (size_t)rms_row * cols4;
     rmsnorm_row<NV>(reinterpret_cast<const float4 *>(w.input) + off,
                     reinterpret_cast<const float4 *>(w.weight),
-                    w.normalized ? reinterpret_cast<float4 *>(w.normalized) + off : nullptr,
+                    normalized ? reinterpret_cast<float4 *>(normalized) + off : nullptr,
                     w.normalized_bf16 ? w.normalized_bf16 + (size_t)rms_row * w.ld_bf16_4 : nullptr,
                     cols4, w.cols, w.eps, scratch);
   } else {
@@ -135,10 +137,11 @@ iteration_kernel(IterationWork w) {
 // write pass. GEMV: warp per row, scalar loads.
 __global__ void __launch_bounds__(kGenericThreads)
 generic_rmsnorm_kernel(float *out, __nv_bfloat16 *out_bf16, int ld_bf16, const float *x,
-                       const float *w, int rows, int cols, float eps) {
+                       const float *w, int rows, int cols, float eps, int norm_lo, int norm_hi) {
   __shared__ float scratch[32];
   const int row = blockIdx.x;
   if (row >= rows) return;
+  if (row < norm_lo || row >= norm_hi) out = nullptr;
   const float *xr = x + (size_t)row * cols;
   float ss = 0.f;
   for (int i = threadIdx.x; i < cols; i += blockDim.x) {
@@ -282,7 +285,7 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    const float *weight, float *softmax, const float *logits, float *product,
                    const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
                    int cols, int gemv_rows, float eps, cudaStream_t s, uint8_t *normalized_e4m3,
-                   int ld_e4m3, float *e4m3_scale) {
+                   int ld_e4m3, float *e4m3_scale, int norm_lo, int norm_hi) {
   CE_REQUIRE(cols >= 1, "cols must be >= 1 (got %d)", cols);
   CE_REQUIRE(batch_rms >= 0 && batch_softmax >= 0 && gemv_rows >= 0, "negative row count");
   if (batch_rms > 0)
@@ -323,6 +326,8 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
     w.softmax_rows = batch_softmax;
     w.gemv_rows = gemv_rows;
     w.eps = eps;
+    w.norm_lo = norm_lo;
+    w.norm_hi = norm_hi;
     // At least 256 threads per block whatever the launch contains, so the
     // reduction order of a row (and so its bits) does not depend on whether
     // GEMV blocks share the launch; the GEMV blocks use the same size.
@@ -333,7 +338,7 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
     if (batch_rms > 0) {
       generic_rmsnorm_kernel<<<batch_rms, kGenericThreads, 0, s>>>(
           normalized, reinterpret_cast<__nv_bfloat16 *>(normalized_bf16), ld_bf16, input, weight,
-          batch_rms, cols, eps);
+          batch_rms, cols, eps, norm_lo, norm_hi);
       CE_LAUNCH_CHECK("generic_rmsnorm_kernel");
     }
     if (batch_softmax > 0) {

@@ -67,31 +67,121 @@ def combine_softmax_stats(maxes, sums, argmax):
 
 
 class RowShardedPlan:
-    """The op trio's rmsnorm -> GEMM with W split by output rows over the
-    ranks of a process group (see the module docstring)."""
+    """The op trio with W split by output rows over the ranks of a process
+    group (one GPU each; see the module docstring).
 
-    def __init__(self, ce, batch, size, rows, precision, group=None):
-        self.ce = ce
-        self.group = group
+    Every rank holds the full batch x and multiplies its normalized rows by
+    its slice W[lo:hi] with its own Plan; the row-independent outputs of the
+    rows stage (fp32 normalized rows and softmax rows) are split by batch
+    rows instead, rank r writing rows [b_lo, b_hi), since nothing consumes
+    them across ranks. The slices of the product are joined into every
+    rank's out [batch][rows] by one of three exchanges:
+
+    mode "p2p" (default): the library's fused peer-memory join
+      (ce_plan_gemm_rowx): the GEMM epilogue stores each output tile into
+      every rank's exchange block over NVLink as it leaves tensor memory,
+      and ce_rowx_wait waits for the peers' slices; `exchanges` independent
+      exchange blocks let callers pipeline steps (slot i % exchanges).
+    mode "nccl": the slice GEMM writes into this rank's slot of a staging
+      buffer, ce_allgather_rows joins the slots with ncclAllGather on a
+      communicator made through the library (ce_nccl_comm_init).
+    mode "torch": torch.distributed.all_gather of the padded slices (any
+      backend), the join of gather_row_shards.
+    """
+
+    MODES = ("p2p", "nccl", "torch")
+
+    def __init__(self, ce, batch, size, rows, precision, group=None, mode="p2p", exchanges=1):
+        if mode not in self.MODES:
+            raise ValueError(f"unknown exchange mode {mode!r}")
+        self.ce, self.group, self.mode = ce, group, mode
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
-        self.rows = rows
+        self.batch, self.size, self.rows, self.precision = batch, size, rows, precision
         self.lo, self.hi = shard_bounds(rows, self.world, self.rank)
+        self.b_lo, self.b_hi = shard_bounds(batch, self.world, self.rank)
         self.local = ce.Plan(batch, size, self.hi - self.lo, precision)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.outs = []
+        if mode == "p2p":
+            self.xs = [ce.RowExchange(batch, rows, self.world, self.rank) for _ in range(exchanges)]
+            for x in self.xs:
+                handles = [None] * self.world
+                dist.all_gather_object(handles, x.handle, group=group)
+                x.connect(handles)
+                self.outs.append(x.output)
+            torch.cuda.synchronize()
+            dist.barrier(group)
+        elif mode == "nccl":
+            uid = [ce.nccl_unique_id() if self.rank == 0 else None]
+            src = dist.get_global_rank(group, 0) if group is not None else 0
+            dist.broadcast_object_list(uid, src=src, group=group)
+            self.comm = ce.NcclComm(self.world, self.rank, uid[0])
+            self.width = (rows + self.world - 1) // self.world
+            n = ce.allgather_staging_floats(batch, rows, self.world)
+            self.staging, self.slots = [], []
+            for _ in range(exchanges):
+                st = torch.empty(n, device=dev)
+                self.staging.append(st)
+                self.slots.append(st[self.rank * batch * self.width:(self.rank + 1) * batch * self.width]
+                                  .view(batch, self.width))
+                self.outs.append(torch.empty((batch, rows), device=dev))
+        else:
+            self.local_out = torch.empty((batch, self.hi - self.lo), device=dev)
+            self.outs = [torch.empty((batch, rows), device=dev) for _ in range(exchanges)]
 
     def set_weights(self, W, stream=None):
         """W: the full [rows][size] matrix (device) or this rank's slice."""
         shard = W[self.lo:self.hi] if W.shape[0] == self.rows else W
         self.local.set_weights(shard.contiguous(), stream=stream)
 
-    def rmsnorm_gemm(self, out, x, norm_w, normalized=None, local_out=None, stream=None):
-        n_local = self.hi - self.lo
-        if local_out is None:
-            local_out = torch.empty((x.shape[0], n_local), device=x.device)
-        self.local.rmsnorm_gemm(local_out, x, norm_w, normalized=normalized, stream=stream)
-        return gather_row_shards(local_out, self.rows, self.group, out=out)
+    def rows_stage(self, normalized, softmax_out, x, norm_w, logits, full=False, stream=None):
+        """The GEMM operand of every batch row; the fp32 normalized and softmax
+        rows of this rank's share [b_lo, b_hi) (every row with full=True).
+        Pointers index the full batch."""
+        lo, hi = (0, self.batch) if full else (self.b_lo, self.b_hi)
+        if self.precision in (self.ce.PREC_BF16, self.ce.PREC_FP8_E4M3):
+            self.local.rows_range(normalized, softmax_out, x, norm_w, logits, lo, hi, stream=stream)
+        else:
+            self.local.rows(normalized, softmax_out, x, norm_w, logits, stream=stream)
+
+    def gemm(self, slot=0, stream=None):
+        """This rank's slice GEMM joined into the full product; returns the
+        [batch][rows] output of exchange `slot`."""
+        ce, out = self.ce, self.outs[slot]
+        if self.mode == "p2p":
+            self.local.gemm_rowx(self.xs[slot], stream=stream)
+            self.xs[slot].wait(stream=stream)
+        elif self.mode == "nccl":
+            self.local.gemm_ld(self.slots[slot], self.width, stream=stream)
+            ce.allgather_rows(self.comm, out, self.staging[slot], self.batch, self.rows, self.world, self.rank,
+                              stream=stream)
+        else:
+            self.local.gemm(self.local_out, stream=stream)
+            gather_row_shards(self.local_out, self.rows, self.group, out=out)
+        return out
+
+    def rmsnorm_gemm(self, out, x, norm_w, normalized=None, stream=None):
+        """rmsnorm -> GEMM of the whole batch, the product copied into out
+        (when given) on every rank."""
+        self.rows_stage(normalized, None, x, norm_w, None, full=True, stream=stream)
+        res = self.gemm(stream=stream)
+        if out is not None and out.data_ptr() != res.data_ptr():
+            out.copy_(res)
+            return out
+        return res
 
     def close(self):
+        if self.mode == "p2p":
+            # no rank frees its exchange block while a peer may still map it
+            torch.cuda.synchronize()
+            dist.barrier(self.group)
+            for x in self.xs:
+                x.close()
+            self.outs = []
+        elif self.mode == "nccl":
+            torch.cuda.synchronize()
+            self.comm.close()
         self.local.close()
 
 
@@ -110,9 +200,14 @@ class ShardedLlama:
       all_gather_into_tensor (NCCL) after each segment.
 
     All work is enqueued on one stream, so a whole step can be captured in a
-    CUDA graph (torch captures NCCL collectives too)."""
+    CUDA graph (torch captures NCCL collectives too).
 
-    def __init__(self, ce, cfg, batch, max_steps, precision, group=None, stream=None, mode="p2p"):
+    reproducible=True: the shards split their attention and split-K GEMMs
+    as the unsharded model does (CE_LLAMA_REPRODUCIBLE_SPLITS), so the
+    sharded step gives the unsharded model's bits."""
+
+    def __init__(self, ce, cfg, batch, max_steps, precision, group=None, stream=None, mode="p2p",
+                 reproducible=False):
         if mode not in ("p2p", "nccl"):
             raise ValueError(f"unknown exchange mode {mode!r}")
         self.ce = ce
@@ -121,7 +216,8 @@ class ShardedLlama:
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
         self.model = ce.Llama(cfg, batch, max_steps, precision=precision, stream=stream,
-                              rank=self.rank, world=self.world)
+                              rank=self.rank, world=self.world,
+                              flags=ce.LLAMA_REPRODUCIBLE_SPLITS if reproducible else 0)
         if mode == "p2p":
             handles = [None] * self.world
             dist.all_gather_object(handles, self.model.exchange_open(), group=group)

@@ -387,6 +387,16 @@ int ce_plan_rows(ce_plan *plan, float *normalized_dev, float *softmax_dev, const
                  ce_stream_t stream);
 int ce_plan_gemm(ce_plan *plan, float *out_dev, ce_stream_t stream);
 
+/* The rows stage of one rank of the row-shard layer (bf16 and fp8 plans):
+ * the GEMM operand of every batch row (the rank's slice GEMM multiplies
+ * the whole batch), but the fp32 normalized rows (normalized_dev may be
+ * NULL) and, when logits != NULL, the softmax rows only for batch rows
+ * [row_lo, row_hi) -- this rank's share of those row-independent outputs,
+ * which nothing downstream exchanges. Pointers index the full batch. */
+int ce_plan_rows_range(ce_plan *plan, float *normalized_dev, float *softmax_dev, const float *x_dev,
+                       const float *norm_w_dev, const float *logits_dev, float eps, int row_lo, int row_hi,
+                       ce_stream_t stream);
+
 /* The plan's two GEMM operands as the tensor cores multiply them, written
  * back as fp32: a_dev [batch][size] from the operand of the latest
  * ce_plan_rows / ce_plan_trio / ce_plan_rmsnorm_gemm on this plan, w_dev
@@ -425,6 +435,81 @@ int ce_rmsnorm_gemm_bf16_noalloc(float *out_dev, float *normalized_dev, const fl
 int ce_plan_trio(ce_plan *plan, float *normalized_dev, float *softmax_dev, float *out_dev,
                  const float *x_dev, const float *norm_w_dev, const float *logits_dev,
                  float eps, ce_stream_t stream);
+
+/* The plan's GEMM with the output row stride given: out_dev [batch][ldd],
+ * ldd >= the plan's rows, e.g. a column block of a wider output or one
+ * rank's slot of the row-shard staging buffer (ce_allgather_rows). */
+int ce_plan_gemm_ld(ce_plan *plan, float *out_dev, int ldd, ce_stream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* Row-shard (tensor-parallel) layer of the op-trio GEMM.               */
+/* The reference runs this GEMM (the classifier, decoder.cu:83-125 and    */
+/* decoder_lowprec.cu:85-127) on one GPU and has no multi-GPU code. Here  */
+/* W's rows are split into contiguous slices over the ranks of one node   */
+/* (rank r of n holds rows [lo_r, hi_r): the first rows % n ranks take    */
+/* one extra row), every rank multiplies the full normalized batch by its */
+/* slice with a plan of hi_r - lo_r rows, and the slices are joined into  */
+/* every rank's out [batch][rows].                                        */
+
+/* [lo, hi) of rank's slice of `rows`. */
+int ce_shard_bounds(int rows, int world, int rank, int *lo, int *hi);
+
+/* Bounded device waits (2 s by default) give up after `seconds` instead,
+ * for kernels launched afterwards on the current device; a wait that gives
+ * up is reported as CE_ERR_TIMEOUT by ce_device_status / ce_llama_status.
+ * The reference's stream-K consumer spins without a limit
+ * (applications/loom_private/decoder/decoder_optimized.cu:391-394).
+ * Setup call. */
+int ce_set_wait_limit(double seconds);
+
+/* NCCL join. The library binds at run time to the libnccl.so.2 the process
+ * has already loaded (the caller's: PyTorch's, or the one a C++ host links
+ * with -lnccl) and never loads a second copy; until one is loaded these
+ * return CE_ERR_USAGE. A caller without a communicator makes one: rank 0 calls
+ * ce_nccl_unique_id, sends the CE_NCCL_ID_BYTES to the other ranks, and
+ * every rank calls ce_nccl_comm_init (setup calls). */
+#define CE_NCCL_ID_BYTES 128
+int ce_nccl_version(int *version);
+int ce_nccl_unique_id(void *id_out);
+int ce_nccl_comm_init(void **comm_out, int world, int rank, const void *id);
+int ce_nccl_comm_destroy(void *comm);
+
+/* Floats of the staging buffer of ce_allgather_rows: world x batch x
+ * ceil(rows / world). */
+int ce_allgather_staging_floats(int batch, int rows, int world, size_t *floats);
+
+/* Joins the ranks' slices: staging_dev [world][batch][ceil(rows/world)]
+ * holds this rank's slice [batch][hi - lo] in slot `rank` (written there by
+ * ce_plan_gemm_ld with ldd = ceil(rows / world)); an in-place ncclAllGather
+ * on `comm` (the caller's ncclComm_t of these ranks, rank `rank` of `world`)
+ * fills every slot, then a kernel scatters the slots into out_dev
+ * [batch][rows]. Enqueue-only (graph capturable: NCCL collectives are). */
+int ce_allgather_rows(void *comm, float *out_dev, float *staging_dev, int batch, int rows, int world, int rank,
+                      ce_stream_t stream);
+
+/* Peer-memory join fused into the GEMM. Each rank opens an exchange that
+ * holds its out [batch][rows] (device memory shared by CUDA IPC) and writes
+ * its IPC handle (CE_IPC_HANDLE_BYTES) to handle_out; the caller gathers the
+ * handles of all ranks in rank order and passes them to ce_rowx_connect,
+ * which maps the peers' exchanges (plain NVLink loads and stores; no
+ * multicast object). ce_plan_gemm_rowx then runs this rank's slice GEMM
+ * (a plan of hi - lo rows: bf16, tf32 or fp8) whose epilogue stores every
+ * output tile into all ranks' outputs as it leaves tensor memory, and
+ * ce_rowx_wait waits (bounded) until every peer's slice of the same call
+ * has landed here; after it, ce_rowx_output's buffer holds the full
+ * product. Ordering: a rank's GEMM stores into a peer only after that
+ * peer's GEMM of the same call has started, i.e. after every consumer the
+ * peer enqueued before it has read the previous product. Every rank makes
+ * the same sequence of calls. 2 <= world <= 8. open / connect / close are
+ * setup calls; ce_plan_gemm_rowx and ce_rowx_wait are enqueue-only (the
+ * exchange count lives in device memory). */
+typedef struct ce_rowx ce_rowx;
+int ce_rowx_open(ce_rowx **x, int batch, int rows, int world, int rank, void *handle_out);
+int ce_rowx_connect(ce_rowx *x, const void *handles);
+int ce_rowx_output(ce_rowx *x, float **out_dev, int *lo, int *hi);
+int ce_plan_gemm_rowx(ce_plan *plan, ce_rowx *x, ce_stream_t stream);
+int ce_rowx_wait(ce_rowx *x, ce_stream_t stream);
+int ce_rowx_close(ce_rowx *x);
 
 /* ------------------------------------------------------------------ */
 /* loom_private llama2c decoder (applications/loom_private/decoder/).   */
@@ -576,6 +661,16 @@ int ce_llama_validate_shard(const ce_llama_config *cfg, int batch, int max_steps
                             int rank, int world);
 int ce_llama_create_shard(ce_llama **model, const ce_llama_config *cfg, int batch, int max_steps,
                           int precision, int rank, int world, ce_stream_t stream);
+
+/* ce_llama_create_shard with flags. CE_LLAMA_REPRODUCIBLE_SPLITS: the shard
+ * splits its attention and its split-K GEMMs as the unsharded model does
+ * (the counts of world 1), so every value it computes is summed in the
+ * unsharded order and the sharded step gives the unsharded model's bits
+ * (logits, tokens, residual stream). Without it each shard picks the splits
+ * that fill the GPU for its own slice, which reassociates those fp32 sums. */
+#define CE_LLAMA_REPRODUCIBLE_SPLITS 1
+int ce_llama_create_shard_ex(ce_llama **model, const ce_llama_config *cfg, int batch, int max_steps,
+                             int precision, int rank, int world, int flags, ce_stream_t stream);
 
 /* Peer-memory exchange for a sharded model, instead of caller-bound buffers
  * joined by all-gathers: ce_llama_exchange_open allocates this rank's

@@ -50,10 +50,15 @@ def to64(w):
     decode scale (the ce_quantize_nvfp4 format)."""
     if isinstance(w, tuple):
         codes, scales, alpha = w
-        nib = np.empty((codes.shape[0], codes.shape[1] * 2), np.uint8)
-        nib[:, 0::2], nib[:, 1::2] = codes & 0x0F, codes >> 4
-        vals = decode_array(0, nib).astype(np.float64)
-        return vals * np.repeat(decode_array(2, scales).astype(np.float64), 16, axis=1) * alpha
+        rows = codes.shape[0]
+        # byte -> (low-nibble value, high-nibble value), then one scale per 16
+        pair = np.stack([decode_array(0, np.arange(256) & 0x0F), decode_array(0, np.arange(256) >> 4)],
+                        axis=1).astype(np.float64)
+        sf = decode_array(2, np.arange(256)).astype(np.float64)
+        vals = pair[codes].reshape(rows, -1, 16)
+        vals *= sf[scales][:, :, None]
+        vals *= alpha
+        return vals.reshape(rows, -1)
     return bf16_value(w).astype(np.float64)
 
 
@@ -155,6 +160,61 @@ class LlamaOracle:
             gap.append(top2[:, 1] - top2[:, 0])
             tok = forced[:, s]
         return np.stack(logits), np.stack(best), np.stack(gap)
+
+
+def teacher_forced_layerwise(cfg, layer_weights, emb, rms_final, wcls, tokens_in, pos0, layer_cache,
+                             operand="bf16"):
+    """Teacher-forced logits of n sequences over S steps computed one layer
+    at a time, as a prefill of the forced tokens: the arithmetic of
+    LlamaOracle.step applied to every (sequence, step) row at once, so each
+    layer's weights and cache are needed once (a 7B-shaped model never has
+    to sit in host memory as float64).
+
+    layer_weights(l): dict of float64 wqkv, wo, w13, w2 and rms_att, rms_ffn;
+    layer_cache(l): float64 K, V [n][kv_heads][seq_len][hs] with positions
+    < pos0 filled (updated in place); emb, wcls float64 [vocab][dim];
+    tokens_in [n][S]: the token fed at step s (step 0: the start token).
+    Returns logits [S][n][vocab]."""
+    c = dict(cfg)
+    op = f16_round if operand == "f16" else bf16_round
+    D, H = c["dim"], c["n_heads"]
+    KH = c.get("n_kv_heads", H)
+    hs = D // H
+    kv_dim = hs * KH
+    group = H // KH
+    tokens_in = np.asarray(tokens_in)
+    n, S = tokens_in.shape
+    x = emb[tokens_in.reshape(-1)]          # row b * S + s
+    for l in range(c["n_layers"]):
+        W = layer_weights(l)
+        kc, vc = layer_cache(l)
+        xb = op(rmsnorm(x, W["rms_att"]))
+        qkv = xb @ W["wqkv"].T
+        q = np.empty((n * S, D))
+        for s in range(S):
+            rows = np.arange(n) * S + s
+            q[rows] = rope(qkv[rows, :D], pos0 + s, hs)
+            k = rope(qkv[rows, D:D + kv_dim], pos0 + s, hs)
+            kc[:, :, pos0 + s, :] = bf16_round(k).reshape(n, KH, hs)
+            vc[:, :, pos0 + s, :] = bf16_round(qkv[rows, D + kv_dim:]).reshape(n, KH, hs)
+        att = np.empty((n * S, H, hs))
+        for s in range(S):
+            rows = np.arange(n) * S + s
+            qh = q[rows].reshape(n, H, hs)
+            for h in range(H):
+                keys = kc[:, h // group, :pos0 + s + 1, :]
+                vals = vc[:, h // group, :pos0 + s + 1, :]
+                sc = np.einsum("nd,ntd->nt", qh[:, h, :], keys) / np.sqrt(hs)
+                p = np.exp(sc - sc.max(axis=1, keepdims=True))
+                p /= p.sum(axis=1, keepdims=True)
+                att[rows, h, :] = np.einsum("nt,ntd->nd", p, vals)
+        x = x + op(att.reshape(n * S, D)) @ W["wo"].T
+        xb = op(rmsnorm(x, W["rms_ffn"]))
+        hh = xb @ W["w13"].T
+        g, u = hh[:, 0::2], hh[:, 1::2]
+        x = x + op(g / (1.0 + np.exp(-g)) * u) @ W["w2"].T
+    lg = op(rmsnorm(x, rms_final)) @ wcls.T
+    return lg.reshape(n, S, -1).transpose(1, 0, 2)
 
 
 def cache_from_device(model, seqs, positions):

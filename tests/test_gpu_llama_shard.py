@@ -1,14 +1,21 @@
-"""The Llama-2 decoder step row-sharded over 2 GPUs (one process each, NCCL
-all-gathers between the library's segments) against the same model
-unsharded on one GPU: every step's logits (the rank slices gathered) within
-relative L2 1e-3 of the unsharded ones on the sequences whose inputs still
-agree, the residual stream after the last layer within 1e-3 on the
-sequences that never diverged, and a greedy token differing only at a near
-tie the logit error can bridge (at most 1 in 20 sequences); bf16
-and NVFP4 weights; a captured step graph (NCCL included) replays bit for bit
-like direct steps. Both exchanges: NCCL all-gathers, and the library's
-peer-memory puts and flag waits over CUDA IPC mappings. Needs at least 2
-visible GPUs; skipped otherwise."""
+"""The Llama-2 decoder step row-sharded over 2, 4 and 8 GPUs (one process
+each) against the same model unsharded on each rank's GPU.
+
+* Reproducible splits (CE_LLAMA_REPRODUCIBLE_SPLITS): every step's logits
+  (the rank slices gathered), the greedy tokens and the residual stream are
+  bitwise equal to the unsharded model's -- the shards sum every value in
+  the unsharded order and the exchanged fp32 deltas are added in a fixed
+  order, so nothing else may differ.
+* Default splits (each shard fills its GPU): every step's logits within
+  relative L2 LOGIT_BOUND of the unsharded ones on the sequences whose
+  inputs still agree, the residual stream after the last layer within the
+  same bound on the sequences that never diverged, and a greedy token
+  differing only at a near tie the logit error can bridge (at most 1 in 20
+  sequences).
+bf16 and NVFP4 weights; a captured step graph (NCCL included) replays bit
+for bit like direct steps; both exchanges (NCCL all-gathers, and the
+library's peer-memory puts and flag waits over CUDA IPC mappings). A world
+with more ranks than visible GPUs is skipped."""
 import os
 import socket
 
@@ -60,10 +67,10 @@ def _full_logits(model, dist, world):
 
 
 def _body(rank, world, case, ce, rs, dist):
-    cfg, prec_name, batch, fill, steps, graph, mode = case
+    cfg, prec_name, batch, fill, steps, graph, mode, repro = case
     prec = {"bf16": ce.PREC_BF16, "nvfp4": ce.PREC_NVFP4_E2M1}[prec_name]
     tokens0 = np.random.default_rng(5).integers(0, cfg["vocab_size"], batch).astype(np.int32)
-    sh = rs.ShardedLlama(ce, cfg, batch, steps, prec, mode=mode)
+    sh = rs.ShardedLlama(ce, cfg, batch, steps, prec, mode=mode, reproducible=repro)
     sh.model.init_random(seed=3, kv_fill=fill)
     sh.model.start(tokens0, fill)
     if graph:
@@ -132,38 +139,63 @@ def _body(rank, world, case, ce, rs, dist):
     same_rows = np.nonzero(first == steps)[0]
     xr = rel(x2[same_rows], ref_x[same_rows]) if len(same_rows) else 0.0
     diverged = int((first < steps).sum())
-    ok = worst <= 1e-3 and xr <= 1e-3 and ties_ok and diverged <= max(1, batch // 20)
     same = np.array_equal(gen, gen2) and np.array_equal(x, x2)
+    if repro:
+        # the unsharded model's splits: the same sums in the same order
+        bitwise = (all(np.array_equal(a, b) for a, b in zip(sh_logits, ref_logits)) and
+                   np.array_equal(gen2, ref_gen) and np.array_equal(x2, ref_x))
+        ok = bitwise
+    else:
+        ok = worst <= LOGIT_BOUND and xr <= LOGIT_BOUND and ties_ok and diverged <= max(1, batch // 20)
     return (rank, bool(ok and same), dict(logits=worst, x=xr, diverged=diverged, ties_ok=bool(ties_ok),
-                                          graph_equals_direct=bool(same)))
+                                          graph_equals_direct=bool(same), reproducible=bool(repro)))
 
 
-CASES = [
-    (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4, vocab_size=1024, seq_len=96),
-     "bf16", 12, 40, 5, False, "nccl"),
-    (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=4, vocab_size=1024, seq_len=96),
-     "bf16", 12, 40, 5, True, "p2p"),
-    (dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=4, vocab_size=1024, seq_len=200),
-     "nvfp4", 9, 150, 4, True, "p2p"),
-    (dict(dim=1024, hidden_dim=2816, n_layers=2, n_heads=8, vocab_size=4096, seq_len=128),
-     "nvfp4", 64, 100, 3, False, "p2p"),
-]
+# Default splits reassociate fp32 sums (split-K partials, attention split
+# merges) against the unsharded model; over these 2-layer models that moves
+# the logits by a few fp32 roundings of their magnitude, far inside this
+# relative-L2 bound (the observed values are printed by the test).
+LOGIT_BOUND = 2e-5
 
 
-@pytest.mark.parametrize("case", CASES, ids=["bf16-gqa-nccl", "bf16-gqa-p2p-graph", "nvfp4-graph-p2p",
-                                             "nvfp4-batch64-p2p"])
-def test_sharded_decoder_matches_unsharded(case):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    world = 2
+def _cases(world):
+    kv = 4 if world <= 4 else 8
+    small = dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, n_kv_heads=kv, vocab_size=1024, seq_len=96)
+    mha = dict(dim=512, hidden_dim=1024, n_layers=2, n_heads=8, vocab_size=1024, seq_len=200)
+    wide = dict(dim=1024, hidden_dim=2816 if world <= 4 else 2048, n_layers=2, n_heads=8, vocab_size=4096,
+                seq_len=128)
+    return [
+        (small, "bf16", 12, 40, 5, False, "nccl", False),
+        (small, "bf16", 12, 40, 5, True, "p2p", False),
+        (small, "bf16", 12, 40, 5, True, "p2p", True),
+        (mha, "nvfp4", 9, 150, 4, True, "p2p", False),
+        (wide, "nvfp4", 64, 100, 3, False, "p2p", True),
+    ]
+
+
+def _run_world(world):
     ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
-    for p in procs:
-        p.start()
-    results = [q.get(timeout=240) for _ in range(world)]
-    for p in procs:
-        p.join(timeout=60)
-    assert all(r[1] for r in results), results
-    assert all(p.exitcode == 0 for p in procs)
+    results = []
+    for case in _cases(world):
+        q = ctx.Queue()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, world, port, case, q)) for r in range(world)]
+        for p in procs:
+            p.start()
+        res = [q.get(timeout=240) for _ in range(world)]
+        for p in procs:
+            p.join(timeout=60)
+        results.append((case[1:], res, [p.exitcode for p in procs]))
+    return results
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_sharded_decoder_matches_unsharded(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    results = _run_world(world)
+    for case, res, codes in results:
+        print(f"world {world} {case}: {[r[2] for r in res]}")
+    for case, res, codes in results:
+        assert all(r[1] for r in res), (case, res)
+        assert all(c == 0 for c in codes), (case, codes)

@@ -131,6 +131,50 @@ def test_oracle_matches_loop_restatement():
     assert np.allclose(kc[1][0], np.array(kl[1]), rtol=0, atol=0)  # appended keys agree
 
 
+def test_layerwise_oracle_matches_step_oracle():
+    """The layer-major teacher-forced oracle (every (sequence, step) row of a
+    layer at once) gives the step-major LlamaOracle.decode logits: 3
+    sequences x 4 steps, grouped-query heads, a partly filled cache, bf16
+    and fp16 operand rounding."""
+    c = dict(dim=32, hidden_dim=48, n_layers=2, n_heads=4, n_kv_heads=2, vocab_size=40, seq_len=12)
+    hs = c["dim"] // c["n_heads"]
+    kvd = hs * c["n_kv_heads"]
+    rng = np.random.default_rng(9)
+
+    def mat(r, k):
+        return bf16_bits((rng.standard_normal((r, k)) * 0.3).astype(np.float32))
+
+    W = {"tok_emb": mat(c["vocab_size"], c["dim"]), "wcls": mat(c["vocab_size"], c["dim"]),
+         "rms_final": (1 + 0.1 * rng.standard_normal(c["dim"])).astype(np.float32),
+         "wqkv": [mat(c["dim"] + 2 * kvd, c["dim"]) for _ in range(2)],
+         "wo": [mat(c["dim"], c["dim"]) for _ in range(2)],
+         "w13": [mat(2 * c["hidden_dim"], c["dim"]) for _ in range(2)],
+         "w2": [mat(c["dim"], c["hidden_dim"]) for _ in range(2)],
+         "rms_att": [(1 + 0.1 * rng.standard_normal(c["dim"])).astype(np.float32) for _ in range(2)],
+         "rms_ffn": [(1 + 0.1 * rng.standard_normal(c["dim"])).astype(np.float32) for _ in range(2)]}
+    n, S, pos0 = 3, 4, 5
+    cache = llama_ref.bf16_round(rng.standard_normal((2, 2, n, c["n_kv_heads"], c["seq_len"], hs)))
+    cache[..., pos0:, :] = 0.0
+    tokens0 = np.array([3, 17, 39])
+    forced = rng.integers(0, c["vocab_size"], (n, S))
+    for operand in ("bf16", "f16"):
+        orc = llama_ref.LlamaOracle(c, W, operand=operand)
+        kc = [cache[0, l].copy() for l in range(2)]
+        vc = [cache[1, l].copy() for l in range(2)]
+        want, _, _ = orc.decode(tokens0, pos0, forced, kc, vc)
+        tokens_in = np.concatenate([tokens0[:, None], forced[:, :S - 1]], axis=1)
+        kc2 = [cache[0, l].copy() for l in range(2)]
+        vc2 = [cache[1, l].copy() for l in range(2)]
+        lw = lambda l: {"wqkv": orc.wqkv[l], "wo": orc.wo[l], "w13": orc.w13[l], "w2": orc.w2[l],
+                        "rms_att": orc.rms_att[l], "rms_ffn": orc.rms_ffn[l]}
+        got = llama_ref.teacher_forced_layerwise(c, lw, orc.emb, orc.rms_final, orc.wcls, tokens_in, pos0,
+                                                 lambda l: (kc2[l], vc2[l]), operand=operand)
+        assert got.shape == want.shape
+        assert np.allclose(got, want, rtol=1e-9, atol=1e-9), np.abs(got - want).max()
+        for l in range(2):  # the appended keys and values agree
+            assert np.array_equal(kc[l], kc2[l]) and np.array_equal(vc[l], vc2[l])
+
+
 @pytest.mark.parametrize("cfg,world", [
     (dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, vocab_size=32000, seq_len=2048), 8),
     (dict(dim=4096, hidden_dim=11008, n_layers=32, n_heads=32, vocab_size=32000, seq_len=2048), 2),
