@@ -34,7 +34,9 @@ namespace {
 
 // In host code g_noalloc_operand names a host-side stand-in, not device
 // memory; the device address is looked up once per device, with that device
-// current, and cached.
+// current, and cached for the life of the process (a cudaDeviceReset frees
+// the array and leaves the cached address stale: the entry point must not be
+// called on a device after it was reset).
 int operand_address(uint16_t **out) {
   static std::mutex mu;
   static uint16_t *cached[64] = {};
@@ -74,8 +76,10 @@ extern "C" int ce_rmsnorm_gemm_bf16_noalloc(float *out, float *normalized, const
   int rc = operand_address(&operand);
   if (rc) return rc;
   cudaStream_t s = (cudaStream_t)stream;
-  // The rows launch rewrites every value of [batch][ld] it uses (normalized
-  // values, zero padding columns), so nothing left by an earlier call is read.
+  // The GEMM reads only columns [0, size) of each operand row (its tensor
+  // map's inner extent is size; TMA fills the rest of the last k-block with
+  // zeros) and this rows launch rewrites all of them first, so nothing an
+  // earlier call left in the array is read.
   rc = rows_iteration(normalized, operand, ld, x, norm_w, nullptr, nullptr, nullptr, nullptr,
                       nullptr, batch, 0, size, 0, eps, s);
   if (rc) return rc;

@@ -422,10 +422,14 @@ int ce_plan_operands(ce_plan *plan, float *a_dev, float *w_dev, ce_stream_t stre
  *   values), which every GPU that loads the library holds until exit.
  *   batch x roundup(size, 64) above that limit returns CE_ERR_USAGE.
  * The first call on a device looks up that array's device address (once per
- * device, with the device current); make that first call before any stream
- * capture. All calls share the array: calls that overlap on the GPU (two
- * streams, two host threads) race on it and must be serialized by the
- * caller. Each call rewrites every value it reads, so no clearing is needed. */
+ * device, with the device current) and keeps it for the life of the
+ * process; make that first call before any stream capture. A device reset
+ * (cudaDeviceReset) frees the array, so do not call this entry point on a
+ * device after resetting it. All calls share the array: calls that overlap
+ * on the GPU (two streams, two host threads) race on it and must be
+ * serialized by the caller. The GEMM reads only the first `size` columns of
+ * each operand row, which the same call writes first, so no clearing is
+ * needed. */
 int ce_rmsnorm_gemm_bf16_noalloc(float *out_dev, float *normalized_dev, const float *x_dev,
                                  const float *norm_w_dev, const uint16_t *w_bf16_dev, int ld_w,
                                  int batch, int size, int rows, float eps, ce_stream_t stream);

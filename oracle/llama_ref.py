@@ -163,7 +163,7 @@ class LlamaOracle:
 
 
 def teacher_forced_layerwise(cfg, layer_weights, emb, rms_final, wcls, tokens_in, pos0, layer_cache,
-                             operand="bf16"):
+                             operand="bf16", x0=None, perturb=None):
     """Teacher-forced logits of n sequences over S steps computed one layer
     at a time, as a prefill of the forced tokens: the arithmetic of
     LlamaOracle.step applied to every (sequence, step) row at once, so each
@@ -173,8 +173,11 @@ def teacher_forced_layerwise(cfg, layer_weights, emb, rms_final, wcls, tokens_in
     layer_weights(l): dict of float64 wqkv, wo, w13, w2 and rms_att, rms_ffn;
     layer_cache(l): float64 K, V [n][kv_heads][seq_len][hs] with positions
     < pos0 filled (updated in place); emb, wcls float64 [vocab][dim];
-    tokens_in [n][S]: the token fed at step s (step 0: the start token).
-    Returns logits [S][n][vocab]."""
+    tokens_in [n][S]: the token fed at step s (step 0: the start token);
+    x0: optional float64 [n * S][dim] residual rows to start from instead of
+    the embedding rows (row b * S + s); perturb: optional function applied to
+    every matrix product's result rows (used to measure how far fp32-level
+    noise moves this model). Returns logits [S][n][vocab]."""
     c = dict(cfg)
     op = f16_round if operand == "f16" else bf16_round
     D, H = c["dim"], c["n_heads"]
@@ -184,12 +187,13 @@ def teacher_forced_layerwise(cfg, layer_weights, emb, rms_final, wcls, tokens_in
     group = H // KH
     tokens_in = np.asarray(tokens_in)
     n, S = tokens_in.shape
-    x = emb[tokens_in.reshape(-1)]          # row b * S + s
+    x = emb[tokens_in.reshape(-1)] if x0 is None else np.asarray(x0, np.float64)  # row b * S + s
+    mm = (lambda a, w: a @ w.T) if perturb is None else (lambda a, w: perturb(a @ w.T))
     for l in range(c["n_layers"]):
         W = layer_weights(l)
         kc, vc = layer_cache(l)
         xb = op(rmsnorm(x, W["rms_att"]))
-        qkv = xb @ W["wqkv"].T
+        qkv = mm(xb, W["wqkv"])
         q = np.empty((n * S, D))
         for s in range(S):
             rows = np.arange(n) * S + s
@@ -208,12 +212,12 @@ def teacher_forced_layerwise(cfg, layer_weights, emb, rms_final, wcls, tokens_in
                 p = np.exp(sc - sc.max(axis=1, keepdims=True))
                 p /= p.sum(axis=1, keepdims=True)
                 att[rows, h, :] = np.einsum("nt,ntd->nd", p, vals)
-        x = x + op(att.reshape(n * S, D)) @ W["wo"].T
+        x = x + mm(op(att.reshape(n * S, D)), W["wo"])
         xb = op(rmsnorm(x, W["rms_ffn"]))
-        hh = xb @ W["w13"].T
+        hh = mm(xb, W["w13"])
         g, u = hh[:, 0::2], hh[:, 1::2]
-        x = x + op(g / (1.0 + np.exp(-g)) * u) @ W["w2"].T
-    lg = op(rmsnorm(x, rms_final)) @ wcls.T
+        x = x + mm(op(g / (1.0 + np.exp(-g)) * u), W["w2"])
+    lg = mm(op(rmsnorm(x, rms_final)), wcls)
     return lg.reshape(n, S, -1).transpose(1, 0, 2)
 
 

@@ -92,6 +92,10 @@ def ref():
         L.ref_validate_all.argtypes = [ctypes.c_int, ctypes.c_uint64, _f32p, _f32p, _f32p, _f32p,
                                        _f32p, _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                        _f32p, _f64p]
+        L.ref_time_validate_all.restype = ctypes.c_double
+        L.ref_time_validate_all.argtypes = [ctypes.c_int, ctypes.c_uint64, _f32p, _f32p, _f32p, _f32p, _f32p,
+                                            _f32p, _f32p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                            ctypes.c_int, ctypes.POINTER(ctypes.c_int)]
         L.ref_gamma_probabilistic.restype = ctypes.c_double
         L.ref_gamma_probabilistic.argtypes = [ctypes.c_int]
         L.ref_decoder_compute.restype = ctypes.c_int
@@ -117,6 +121,22 @@ def ref():
         L.ref_rmsnorm_float.argtypes = [_f32p, ctypes.c_longlong, _f32p]
         _ref = L
     return _ref
+
+
+def ref_time_validate_all(x, probs, w, matrix, normalized, softmax, product, random=1, seed=0, reps=1):
+    """Mean seconds of the reference's own validate_all (its CPU path of the
+    llama2c iteration, compiled unmodified into _ref/libref.so) on the given
+    inputs and outputs, and its verdict; None when libref.so is absent."""
+    R = ref()
+    if R is None:
+        return None
+    b, s = x.shape
+    rows = matrix.shape[0]
+    valid = ctypes.c_int(0)
+    c = lambda a: np.ascontiguousarray(a, np.float32)
+    sec = R.ref_time_validate_all(random, seed, c(x), c(probs), c(w), c(matrix), c(normalized), c(softmax),
+                                  c(product), b, s, rows, reps, ctypes.byref(valid))
+    return sec, bool(valid.value)
 
 
 # ---------------------------------------------------------------------------

@@ -8,6 +8,7 @@
 //   applications/loom_private/decoder/oracle.cpp  decoder_oracle::compute/check
 //   experiments/blackwell/lowprec/reference.cpp   lowprec_ref::*
 #include <cstdint>
+#include <chrono>
 #include <cstring>
 #include <vector>
 
@@ -50,6 +51,32 @@ int ref_validate_all(int random, uint64_t seed, const float *input, const float 
   if (tolerance) std::memcpy(tolerance, tol.data(), rows * 4);
   if (reference) std::memcpy(reference, ref.data(), rows * 8);
   return ok ? 1 : 0;
+}
+
+// validate_all timed: the input and output vectors are built once, then
+// validate_all runs `reps` times; returns the mean wall seconds per call and
+// sets *valid. This is the reference's own CPU path of the llama2c iteration
+// (validate_outputs_reference: double rmsnorm, softmax and GEMV with its
+// checks, llama2c/llama2c_common.h:237-319), single-threaded as shipped.
+double ref_time_validate_all(int random, uint64_t seed, const float *input, const float *probabilities,
+                             const float *weight, const float *matrix, const float *normalized,
+                             const float *softmax, const float *product, int batch, int size, int rows,
+                             int reps, int *valid) {
+  InputOptions o;
+  o.random = random != 0;
+  o.seed = seed;
+  const size_t vec = (size_t)batch * size, mat = (size_t)rows * size;
+  const std::vector<float> in(input, input + vec), pr(probabilities, probabilities + vec),
+      w(weight, weight + size), m(matrix, matrix + mat), nz(normalized, normalized + vec),
+      sm(softmax, softmax + vec), pd(product, product + rows);
+  std::vector<float> tol;
+  std::vector<double> ref;
+  bool ok = true;
+  const auto t0 = std::chrono::steady_clock::now();
+  for (int r = 0; r < reps; ++r) ok = validate_all(o, in, pr, w, m, nz, sm, pd, batch, size, rows, &tol, &ref) && ok;
+  const auto t1 = std::chrono::steady_clock::now();
+  if (valid) *valid = ok ? 1 : 0;
+  return std::chrono::duration<double>(t1 - t0).count() / (reps > 0 ? reps : 1);
 }
 
 double ref_gamma_probabilistic(int n) { return llama2c_gamma_probabilistic(n); }

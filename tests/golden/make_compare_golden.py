@@ -28,8 +28,10 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, ROOT)
 from oracle import oracle as O  # noqa: E402
 
-# the reference tree's root, as oracle/Makefile's REF
-REF_COMPARE = os.path.join(os.environ.get("REF", "/root/reference"), "llama2c", "compare_dumps.py")
+# the reference tree's root, as oracle/Makefile's REF: $CE_REFERENCE, else a
+# checkout named `reference` beside this repository
+REF_TREE = os.environ.get("CE_REFERENCE") or os.path.join(os.path.dirname(ROOT), "reference")
+REF_COMPARE = os.path.join(REF_TREE, "llama2c", "compare_dumps.py")
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS")
 

@@ -62,12 +62,44 @@ def test_noalloc_matches_plan_two_calls(ce, O, dev):
         assert O.rel_l2(g, ref) <= 1e-2, f"call {call}"
 
 
-def test_noalloc_rejects_sizes_beyond_its_operand(ce, dev):
+def test_noalloc_without_normalized_output_fits_after_rounding(ce, O, dev):
+    """normalized_dev = NULL (only the product is wanted), at the largest
+    batch whose rounded-up operand still fits: 1024 x roundup(4033, 64) =
+    4,194,304 values, exactly the operand."""
     fn = _noalloc(ce)
-    # 1025 x 4096 bf16 values exceed the 4,194,304-value operand: rejected
-    # before any device work, so dummy non-null pointers are never touched
+    b, s, r = 1024, 4033, 96
+    stream = torch.cuda.current_stream().cuda_stream
+    ld_w = ((s + 7) // 8) * 8
+    x, w, _, W = O.trio_inputs(3, b, s, r)
+    dx, dw, dW = (torch.from_numpy(a).to(dev) for a in (x, w, W))
+    wb = torch.empty((r, ld_w), dtype=torch.int16, device=dev)
+    ce.convert_bf16(wb, dW)
+    plan = ce.Plan(b, s, r, ce.PREC_BF16)
+    plan.set_weights(dW)
+    want = torch.full((b, r), float("nan"), device=dev)
+    plan.rmsnorm_gemm(want, dx, dw)
+    got = torch.full((b, r), float("nan"), device=dev)
+    rc = fn(got.data_ptr(), None, dx.data_ptr(), dw.data_ptr(), wb.data_ptr(), ld_w, b, s, r, ce.RMS_EPS,
+            stream)
+    assert rc == ce.OK, ce.last_error()
+    ce.device_status()
+    plan.close()
+    g = got.cpu().numpy()
+    assert np.isfinite(g).all()
+    assert O.rel_l2(g, want.cpu().numpy()) <= 1e-2
+
+
+@pytest.mark.parametrize("batch,size,ld_w,words", [
+    (1025, 4096, 4096, ("exceeds", "4194304")),  # too many values
+    (1025, 4033, 4040, ("exceeds", "4198400")),  # fits unrounded (4,133,825), not rounded up to 64
+    (64, 512, 511, ("leading dimension",)),      # ld_w < size
+    (64, 512, 513, ("multiple of 8",)),          # ld_w not a multiple of 8
+])
+def test_noalloc_rejects_bad_shapes(ce, dev, batch, size, ld_w, words):
+    fn = _noalloc(ce)
+    # rejected before any device work, so dummy non-null pointers are never touched
     dummy = 256
-    rc = fn(dummy, None, dummy, dummy, dummy, 4096, 1025, 4096, 64, 1e-5, None)
+    rc = fn(dummy, None, dummy, dummy, dummy, ld_w, batch, size, 64, 1e-5, None)
     assert rc == ce.ERR_USAGE
     code, msg = ce.last_error()
-    assert "exceeds" in msg and "4194304" in msg
+    assert all(w in msg for w in words), msg
