@@ -545,7 +545,7 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
         return float(t.item())
 
     res = {}
-    for mode in ("p2p", "nccl"):
+    for mode in ("p2p", "fused", "nccl"):
         sh = rs.RowShardedPlan(ce, BATCH, SIZE, ROWS, ce.PREC_BF16, mode=mode, exchanges=2)
         sh.set_weights(dW)
         lo, hi = sh.lo, sh.hi
@@ -556,6 +556,12 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
             if ev is not None:
                 ev[0].record(stream)
             if mode == "p2p":
+                sh.local.gemm_ld(sh.outs[i % 2][:, lo:], ROWS, stream=s)
+                if ev is not None:
+                    ev[1].record(stream)
+                sh.xs[i % 2].put(stream=s)
+                sh.xs[i % 2].wait(stream=s)
+            elif mode == "fused":
                 sh.local.gemm_rowx(sh.xs[i % 2], stream=s)
                 if ev is not None:
                     ev[1].record(stream)
@@ -624,10 +630,11 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
         ok = torch.tensor([1.0 if (out_equal and share_equal) else 0.0], device=dev)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         res[mode] = {"ms_per_step": total, "rows_ms": rows_ms,
-                     ("gemm_with_fused_exchange_ms" if mode == "p2p" else "slice_gemm_ms"): gemm_ms,
-                     ("exchange_wait_ms" if mode == "p2p" else "allgather_join_ms"): join_ms,
+                     ("gemm_with_fused_exchange_ms" if mode == "fused" else "slice_gemm_ms"): gemm_ms,
+                     {"fused": "exchange_wait_ms", "p2p": "copy_engine_put_wait_ms",
+                      "nccl": "allgather_join_ms"}[mode]: join_ms,
                      "slice_gemm_alone_ms": alone_ms,
-                     "exchange_share": (gemm_ms + join_ms - alone_ms) / total if mode == "p2p"
+                     "exchange_share": (gemm_ms + join_ms - alone_ms) / total if mode == "fused"
                      else join_ms / total,
                      "parity": {"ranks_bitwise_equal_to_1gpu_plan": bool(ok.item() == 1.0),
                                 "this_rank_out_equal": out_equal, "this_rank_rows_share_equal": share_equal,
@@ -998,38 +1005,49 @@ def run_ours(args, rank, world, local_rank):
                 "rows_ms": rows_ms, "gemm_ms": gemm_ms,
                 "parallelism": f"dp{world} (the whole trio on every rank, no collective)"}
     if sharded is not None:
-        # the headline at N > 1: one 1024 x 16384 x 8192 step split over the ranks
-        p2p = sharded["p2p"]
+        # the headline at N > 1: one 1024 x 16384 x 8192 step split over the
+        # ranks, joined by the fastest of the library's three joins (all
+        # three are timed and parity-checked in this run)
+        head_mode = min(("p2p", "fused", "nccl"), key=lambda k: sharded[k]["ms_per_step"])
+        hm = sharded[head_mode]
         lo, hi = sharded["slice"]
-        ms_head = p2p["ms_per_step"]
+        ms_head = hm["ms_per_step"]
         value_head = flops_per_step() / (ms_head * 1e-3) / 1e12
-        gemm_head = p2p["gemm_with_fused_exchange_ms"]
+        gemm_head = hm["gemm_with_fused_exchange_ms" if head_mode == "fused" else "slice_gemm_ms"]
         achieved_head = 2.0 * BATCH * (hi - lo) * SIZE / (gemm_head * 1e-3) / 1e12
         nvlink_bytes = BATCH * (hi - lo) * 4 * (world - 1)
         peak_head = pk.get("bf16_tflops", 1590.0)
         roofline = {"bound": "tensor", "achieved": achieved_head, "peak": peak_head, "unit": "TFLOP/s",
                     "frac": achieved_head / peak_head, "traffic": None,
                     "peak_source": f"{pk_kind} burst bf16",
-                    "kernel": "slice GEMM with the fused peer-memory exchange (rank 0's slice)",
+                    "kernel": ("slice GEMM with the fused peer-memory exchange" if head_mode == "fused"
+                               else "slice GEMM") + " (rank 0's slice)",
                     "nvlink": {"bytes_out_per_rank": nvlink_bytes, "link_gbps": 770.0,
                                "floor_ms": nvlink_bytes / 770e9 * 1e3,
                                "tensor_floor_ms": 2.0 * BATCH * (hi - lo) * SIZE / (peak_head * 1e12) * 1e3,
-                               "note": "the slower of the tensor floor and the NVLink floor (every other rank's "
-                                       "copy of this rank's slice at the measured 770 GB/s peer rate) bounds "
-                                       "the fused kernel"}}
+                               "note": "a step is at least the slower of the tensor floor and the NVLink floor "
+                                       "(every other rank's copy of this rank's slice at the measured 770 GB/s "
+                                       "peer rate), plus the rows stage"}}
         rows_bytes = 4.0 * BATCH * SIZE + 2.0 * BATCH * SIZE + SIZE * 4 + \
             3 * 4.0 * (sharded_share_rows(world, rank)) * SIZE
-        rows_roof = {"bound": "hbm", "achieved": rows_bytes / (p2p["rows_ms"] * 1e-3) / 1e9,
+        rows_roof = {"bound": "hbm", "achieved": rows_bytes / (hm["rows_ms"] * 1e-3) / 1e9,
                      "peak": pk.get("hbm_gbs", 6650.0), "unit": "GB/s",
                      "note": "every batch row read and its bf16 operand written; fp32 normalized and softmax "
                              "(read + write) only for this rank's batch share"}
+        join_desc = {"p2p": "the slice GEMM into this rank's columns of its CUDA-IPC exchange block, copied "
+                             "into every peer's block by the copy engines over NVLink (ce_rowx_put)",
+                     "fused": "the slice GEMM's epilogue storing its tiles into every rank's exchange block "
+                              "over NVLink (ce_plan_gemm_rowx)",
+                     "nccl": "ncclAllGather of the slices through the C ABI (ce_allgather_rows) and a join "
+                             "kernel"}[head_mode]
+        launches = {"p2p": 4, "fused": 3, "nccl": 3}[head_mode]
+        join_key = {"fused": "exchange_wait_ms", "p2p": "copy_engine_put_wait_ms",
+                    "nccl": "allgather_join_ms"}[head_mode]
         head = {"value": value_head, "ms_per_step": ms_head, "scaling": "strong",
-                "parallelism": f"tp{world}: W split by output rows ({hi - lo} per rank), the slice GEMM's epilogue "
-                               f"storing its tiles into every rank's output over NVLink (peer memory, CUDA IPC); "
-                               f"NCCL all-gather join timed beside it",
-                "gpu_launches": 3 * args.steps, "kernels_ms": {"rows": p2p["rows_ms"],
-                                                               "gemm_fused_exchange": gemm_head,
-                                                               "exchange_wait": p2p["exchange_wait_ms"]}}
+                "parallelism": f"tp{world}: W split by output rows ({hi - lo} per rank), joined by {join_desc}; "
+                               f"the other two joins timed beside it",
+                "gpu_launches": launches * args.steps,
+                "kernels_ms": {"rows": hm["rows_ms"], "gemm": gemm_head, "join": hm[join_key]}}
     else:
         roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                     "frac": achieved / peak, "traffic": traffic,
@@ -1073,7 +1091,8 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks,
         }
         if sharded is not None:
-            line["row_sharded"] = {"p2p": sharded["p2p"], "nccl": sharded["nccl"], "slice_rows": hi - lo}
+            line["row_sharded"] = {"headline_join": head_mode, "p2p": sharded["p2p"], "fused": sharded["fused"],
+                                   "nccl": sharded["nccl"], "slice_rows": hi - lo}
             line["replicas"] = replicas
         line["rows_roofline"]["frac"] = line["rows_roofline"]["achieved"] / line["rows_roofline"]["peak"]
         if cpu is not None:

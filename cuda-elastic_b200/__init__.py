@@ -81,6 +81,7 @@ _SIGNATURES = {
     "ce_gemm_bf16_tile": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_tf32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_tuning": [_i],
+    "ce_gemm_wide_tiles": [_i],
     "ce_gemm_config": [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_fp32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_convert_bf16": [_vp, _vp, _i, _i, _i, _vp],
@@ -160,6 +161,7 @@ _SIGNATURES = {
     "ce_rowx_output": [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_i), ctypes.POINTER(_i)],
     "ce_plan_gemm_rowx": [_vp, _vp, _vp],
     "ce_rowx_wait": [_vp, _vp],
+    "ce_rowx_put": [_vp, _vp],
     "ce_rowx_close": [_vp],
 }
 _RESTYPES = {"ce_version": ctypes.c_char_p}
@@ -625,6 +627,10 @@ class RowExchange:
 
     def wait(self, stream=None):
         check(lib().ce_rowx_wait(self._h, _stream(stream)))
+
+    def put(self, stream=None):
+        """Copies this rank's slice of output into every peer's (copy engines)."""
+        check(lib().ce_rowx_put(self._h, _stream(stream)))
 
     def close(self):
         if getattr(self, "_h", None) is not None and self._h.value:

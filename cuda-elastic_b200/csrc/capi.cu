@@ -80,6 +80,7 @@ int quantize_mxfp6(uint8_t *codes, uint8_t *scales, const float *x, int rows, in
 int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
                    const float *x, int rows, int cols, int ld_bytes, cudaStream_t s);
 int gemm_set_prefetch(int kblocks);
+int gemm_set_wide_tiles(int on);
 
 // ---------------------------------------------------------------------------
 // Status
@@ -357,6 +358,8 @@ int ce_gemm_bf16_tile(float *d, const uint16_t *a, const uint16_t *b, int M, int
 }
 
 int ce_gemm_tuning(int l2_prefetch_kblocks) { return gemm_set_prefetch(l2_prefetch_kblocks); }
+
+int ce_gemm_wide_tiles(int on) { return gemm_set_wide_tiles(on); }
 
 int ce_gemm_config(int precision, float *d, const void *a, const void *b, int M, int N, int K,
                    int lda, int ldb, int ldd, int cta_group, int tile_n, ce_stream_t stream) {

@@ -63,16 +63,22 @@ struct Kind<3> {
   static constexpr uint32_t fmt = 0;  // F16 (kind::f16 with fp16 operands)
 };
 
-template <int BN>
+// Shared memory of the row-shard fan-out epilogue: one padded 32 x 33 fp32
+// transpose tile per epilogue warp.
+constexpr int kFanTile = 32 * 33;
+constexpr int kFanBytes = 4 * kFanTile * 4;
+
+template <int BN, int FAN = 0>
 struct Smem {
   static constexpr int a_bytes = BM * kRowBytes;
   static constexpr int b_bytes = BN * kRowBytes;
   static constexpr int stage_bytes = a_bytes + b_bytes;
-  static constexpr int max_stages = (232448 - 2048) / stage_bytes;
+  static constexpr int max_stages = (232448 - 2048 - FAN * kFanBytes) / stage_bytes;
   static constexpr int stages = max_stages > 8 ? 8 : max_stages;
   static constexpr int bar_offset = stages * stage_bytes;
   // full[kStages], empty[kStages], tmem_full[2], tmem_empty[2], drain, tmem holder
-  static constexpr int total = bar_offset + 256 + 1024;  // + alignment slack
+  static constexpr int fan_offset = bar_offset + 256;
+  static constexpr int total = fan_offset + FAN * kFanBytes + 1024;  // + alignment slack
 };
 
 // Instruction descriptor (kind::f16 / tf32 / f8f6f4): D fp32 (bits 4-5 = 1),
@@ -132,6 +138,37 @@ __device__ __forceinline__ void store_out32(const GemmArgs &args, float *dst, co
   }
 }
 
+// Row-shard fan-out through shared memory: the warp's 32 rows x 32 columns
+// (lane = row, v = its 32 columns starting at col0) are transposed through a
+// padded 32 x 33 tile, then written one row per instruction with lanes on
+// consecutive columns -- a full 128-byte segment per destination (this rank
+// and every peer), which NVLink carries far better than the lane-per-row
+// 16-byte pieces of store_out32. row0: the warp's first row.
+__device__ __forceinline__ void store_fan32(const GemmArgs &args, float *tile, float *d, int row0, int col0,
+                                            const float (&v)[32], bool peers) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) tile[lane * 33 + j] = v[j];
+  __syncwarp();
+  float *const own = reinterpret_cast<float *>(args.rx.blocks[args.rx.rank]);
+  const bool col_ok = col0 + lane < args.N;
+#pragma unroll 4
+  for (int r = 0; r < 32; ++r) {
+    const int row = row0 + r;
+    if (row < args.M && col_ok) {
+      const float x = tile[r * 33 + lane];
+      float *dst = d + (size_t)row * args.ldd + col0 + lane;
+      *dst = x;
+      if (peers) {
+        const ptrdiff_t off = dst - own;
+        for (int q = 0; q < args.rx.world; ++q)
+          if (q != args.rx.rank) reinterpret_cast<float *>(args.rx.blocks[q])[off] = x;
+      }
+    }
+  }
+  __syncwarp();
+}
+
 // SwiGLU epilogue of one row's 32 accumulator columns starting at col0 (even).
 __device__ __forceinline__ void store_swiglu(const GemmArgs &args, int row, int col0, const float (&v)[32]) {
   uint16_t *orow = args.out_bf16 + (size_t)row * args.ld_out;
@@ -178,11 +215,11 @@ __device__ __forceinline__ Unit unit_of(const GemmArgs &args, int u) {
   return w;
 }
 
-template <int kKind, int BN>
+template <int kKind, int BN, int FAN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
             GemmArgs args) {
-  using S = Smem<BN>;
+  using S = Smem<BN, FAN>;
   constexpr int kElemsPerRow = kRowBytes / Kind<kKind>::elem;  // K elements per stage
   constexpr int kUmmaK = 32 / Kind<kKind>::elem;               // K elements per MMA
   constexpr int kMmasPerStage = kElemsPerRow / kUmmaK;         // = 4
@@ -323,6 +360,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
     const int quarter = warp & 3;  // TMEM lanes 32*quarter .. +31
     // row-shard fan-out: every peer accepts this exchange before any store
     const bool peers_ok = args.rx.world > 1 && rowx_wait_ready_warp(args.rx, st, 70);
+    float *const fan_tile = reinterpret_cast<float *>(smem + S::fan_offset) + quarter * kFanTile;
+    (void)fan_tile;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -342,7 +381,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kAccStride + c, r);
         tmem_ld_wait();
-        if (row < args.M) {
+        if constexpr (FAN != 0) {
+          // every lane joins the transposed store, rows past M included
+          const int col0 = n0 + c;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(r[j]) * rs;
+            if (args.col_scale != nullptr && col0 + j < args.N) x *= args.col_scale[col0 + j];
+            v[j] = x;
+          }
+          store_fan32(args, fan_tile, w.d, m0 + quarter * 32, col0, v, peers_ok);
+        } else if (row < args.M) {
           const int col0 = n0 + c;
           float v[32];
 #pragma unroll
@@ -375,22 +425,27 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUt
 
 // ---------------------------------------------------------------------------
 // CTA-pair kernel (tcgen05 cta_group::2): a cluster of 2 CTAs on 2 SMs owns a
-// 256 x BN output tile. Each CTA stages its own 128 rows of A and its own
-// BN/2 rows of B (plain TMA loads into its own shared memory, completion
-// signalled on the even CTA's barrier); one thread of the even CTA issues
-// M=256 MMAs that read both CTAs' shared memory and write both CTAs' TMEM
-// (each holds its 128 rows x BN fp32 accumulator). Per SM this halves the B
-// bytes staged per multiply-add compared with the 1-CTA kernel.
+// 256 x (NSUB x BN) output tile. Each CTA stages its own 128 rows of A and,
+// per N piece, its own BN/2 rows of B (plain TMA loads into its own shared
+// memory, completion signalled on the even CTA's barrier); one thread of the
+// even CTA issues M=256 MMAs that read both CTAs' shared memory and write
+// both CTAs' TMEM (each holds its 128 rows x NSUB x BN fp32 accumulator). Per
+// SM this halves the B bytes staged per multiply-add compared with the 1-CTA
+// kernel; NSUB = 2 (two N=BN MMAs per k step on the same A tile, the whole
+// 512-column TMEM as one accumulator) cuts the bytes per multiply-add by
+// another ~30% for large GEMMs, at the price of an epilogue that no longer
+// overlaps the next tile's main loop (one tile per pair there anyway).
 
-template <int BN>
+template <int BN, int NSUB = 1, int FAN = 0>
 struct SmemPair {
   static constexpr int a_bytes = BM * kRowBytes;
-  static constexpr int b_bytes = (BN / 2) * kRowBytes;
+  static constexpr int b_bytes = NSUB * (BN / 2) * kRowBytes;  // NSUB pieces of BN / 2 rows
   static constexpr int stage_bytes = a_bytes + b_bytes;
-  static constexpr int max_stages = (232448 - 2048) / stage_bytes;
+  static constexpr int max_stages = (232448 - 2048 - FAN * kFanBytes) / stage_bytes;
   static constexpr int stages = max_stages > 8 ? 8 : max_stages;
   static constexpr int bar_offset = stages * stage_bytes;
-  static constexpr int total = bar_offset + 256 + 1024;
+  static constexpr int fan_offset = bar_offset + 256;
+  static constexpr int total = fan_offset + FAN * kFanBytes + 1024;
 };
 
 template <int kKind, int BN>
@@ -399,11 +454,14 @@ __host__ __device__ constexpr uint32_t instr_desc_pair() {
          ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
-template <int kKind, int BN>
+template <int kKind, int BN, int NSUB, int FAN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  GemmArgs args) {
-  using S = SmemPair<BN>;
+  using S = SmemPair<BN, NSUB, FAN>;
+  constexpr int kTileN = NSUB * BN;                  // output columns of a tile
+  constexpr int kNumAcc = kTileN <= 256 ? 2 : 1;     // TMEM accumulator buffers
+  constexpr uint32_t kPiece = (BN / 2) * kRowBytes;  // bytes of one N piece of B per CTA
   constexpr int kSt = S::stages;
   constexpr int kElemsPerRow = kRowBytes / Kind<kKind>::elem;
   constexpr int kUmmaK = 32 / Kind<kKind>::elem;
@@ -451,7 +509,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const uint32_t tmem_base = *tmem_holder;
   if (warp == 0 && lane == 0 && pair < num_tiles) {  // see gemm_kernel
     const Unit w = unit_of(args, pair);
-    const int n0 = (w.tile / args.tiles_m) * BN + (int)rank * (BN / 2);
+    const int n0 = (w.tile / args.tiles_m) * kTileN + (int)rank * (BN / 2);
     for (int kb = w.kb0; kb < w.kb1 && kb < w.kb0 + kSt; ++kb)
       tma_prefetch_2d(&tmB, kb * kElemsPerRow, n0);
   }
@@ -470,7 +528,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     for (int t = pair; t < num_tiles && okay; t += npairs) {
       const Unit w = unit_of(args, t);
       const int m0 = (w.tile % args.tiles_m) * (2 * BM) + (int)rank * BM;
-      const int n0 = (w.tile / args.tiles_m) * BN + (int)rank * (BN / 2);
+      const int n0 = (w.tile / args.tiles_m) * kTileN + (int)rank * (BN / 2);
       for (int kb = w.kb0; kb < w.kb1; ++kb) {
         if (!warp_wait_cluster(&empty[stage], phase ^ 1u, st, 11)) {
           okay = false;
@@ -486,7 +544,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * S::stage_bytes);
           const uint32_t bar = full0_leader + 8u * (uint32_t)stage;
           tma_load_2d_pair(a_dst, &tmA, bar, kb * kElemsPerRow, m0);
-          tma_load_2d_pair(b_dst, &tmB, bar, kb * kElemsPerRow, n0);
+#pragma unroll
+          for (int p = 0; p < NSUB; ++p)
+            tma_load_2d_pair(b_dst + p * kPiece, &tmB, bar, kb * kElemsPerRow, n0 + p * BN);
         }
         __syncwarp();
         issued_mask |= 1u << stage;
@@ -510,8 +570,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       bool okay = true;
       int local = 0;
       for (int t = pair; t < num_tiles && okay; t += npairs, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        const int acc = local % kNumAcc;
+        const uint32_t acc_phase = (local / kNumAcc) & 1;
         if (!warp_wait_cluster(&tmem_empty[acc], acc_phase ^ 1u, st, 13)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)acc * kAccStride;
@@ -528,8 +588,12 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
             for (int k = 0; k < kMmasPerStage; ++k) {
               const uint64_t a_desc = smem_desc_sw128(a_addr + k * 32);
-              const uint64_t b_desc = smem_desc_sw128(b_addr + k * 32);
-              tc_mma_pair<kKind>(d_tmem, a_desc, b_desc, kIdesc, ((kb - w.kb0) | k) != 0 ? 1u : 0u);
+#pragma unroll
+              for (int p = 0; p < NSUB; ++p) {
+                const uint64_t b_desc = smem_desc_sw128(b_addr + p * kPiece + k * 32);
+                tc_mma_pair<kKind>(d_tmem + (uint32_t)(p * BN), a_desc, b_desc, kIdesc,
+                                   ((kb - w.kb0) | k) != 0 ? 1u : 0u);
+              }
             }
             const uint32_t e = smem_u32(&empty[stage]);
             tc_commit_pair(cluster_map(e, 0));
@@ -556,26 +620,39 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     // ---------------- Epilogue (warps 2-5 of both CTAs)
     const int quarter = warp & 3;
     const bool peers_ok = args.rx.world > 1 && rowx_wait_ready_warp(args.rx, st, 71);
+    float *const fan_tile = reinterpret_cast<float *>(smem + S::fan_offset) + quarter * kFanTile;
+    (void)fan_tile;
     int local = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const int acc = local % kNumAcc;
+      const uint32_t acc_phase = (local / kNumAcc) & 1;
       if (!warp_wait_cluster(&tmem_full[acc], acc_phase, st, 16)) break;
       tc_fence_after();
       const Unit w = unit_of(args, t);
       const int m0 = (w.tile % args.tiles_m) * (2 * BM) + (int)rank * BM;
-      const int n0 = (w.tile / args.tiles_m) * BN;
+      const int n0 = (w.tile / args.tiles_m) * kTileN;
       const int row = m0 + quarter * 32 + lane;
       const float rs = ((args.row_scale != nullptr && row < args.M) ? args.row_scale[row] : 1.0f) *
                        (args.alpha != nullptr ? *args.alpha : 1.0f);
       float *drow = w.d + (size_t)row * args.ldd;
       const bool vec_ok = ((args.ldd & 3) == 0) && ((reinterpret_cast<uintptr_t>(w.d) & 15u) == 0);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = 0; c < kTileN; c += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kAccStride + c, r);
         tmem_ld_wait();
-        if (row < args.M) {
+        if constexpr (FAN != 0) {
+          // every lane joins the transposed store, rows past M included
+          const int col0 = n0 + c;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(r[j]) * rs;
+            if (args.col_scale != nullptr && col0 + j < args.N) x *= args.col_scale[col0 + j];
+            v[j] = x;
+          }
+          store_fan32(args, fan_tile, w.d, m0 + quarter * 32, col0, v, peers_ok);
+        } else if (row < args.M) {
           const int col0 = n0 + c;
           float v[32];
 #pragma unroll
@@ -1019,29 +1096,30 @@ int configure_smem(int bytes) {
   return CE_OK;
 }
 
-template <int kKind, int BN>
+template <int kKind, int BN, int FAN = 0>
 int launch_gemm(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args, int grid,
                 cudaStream_t s, bool pdl) {
-  using S = Smem<BN>;
-  int rc = configure_smem<gemm_kernel<kKind, BN>>(S::total);
+  using S = Smem<BN, FAN>;
+  int rc = configure_smem<gemm_kernel<kKind, BN, FAN>>(S::total);
   if (rc) return rc;
-  return launch_kernel(gemm_kernel<kKind, BN>, dim3(grid), dim3(kThreads), S::total, s, pdl,
+  return launch_kernel(gemm_kernel<kKind, BN, FAN>, dim3(grid), dim3(kThreads), S::total, s, pdl,
                        "gemm_kernel", ta, tb, args);
 }
 
-template <int kKind, int BN>
+template <int kKind, int BN, int NSUB = 1, int FAN = 0>
 int launch_gemm_pair(const CUtensorMap &ta, const CUtensorMap &tb, const GemmArgs &args,
                      int grid, cudaStream_t s, bool pdl) {
-  using S = SmemPair<BN>;
-  int rc = configure_smem<gemm_pair_kernel<kKind, BN>>(S::total);
+  using S = SmemPair<BN, NSUB, FAN>;
+  int rc = configure_smem<gemm_pair_kernel<kKind, BN, NSUB, FAN>>(S::total);
   if (rc) return rc;
-  return launch_kernel(gemm_pair_kernel<kKind, BN>, dim3(grid), dim3(kThreads), S::total, s, pdl,
+  return launch_kernel(gemm_pair_kernel<kKind, BN, NSUB, FAN>, dim3(grid), dim3(kThreads), S::total, s, pdl,
                        "gemm_pair_kernel", ta, tb, args);
 }
 
 struct GemmChoice {
   int pair;  // 1: CTA-pair kernel (256-row tiles), 0: single-CTA kernel (128-row tiles)
-  int bn;
+  int bn;    // N of one MMA
+  int nsub = 1;  // N pieces per tile (CTA pair only): tile width nsub x bn
 };
 
 // Kernel and tile width: minimise (waves x BN) / efficiency, where a wave is
@@ -1049,32 +1127,44 @@ struct GemmChoice {
 // credited with its lower staging cost per multiply-add (measured: about
 // 0.67 of peak tensor throughput for the single-CTA kernel).
 int g_prefetch_kblocks = 0;  // set by ce_gemm_tuning (setup time)
+int g_wide_tiles = 1;        // two-piece pair tiles allowed (ce_gemm_tuning)
 
-GemmChoice choose_tiles(int M, int N, int sms) {
+GemmChoice choose_tiles(int M, int N, int sms, bool allow_wide = true) {
   // 96- and 64-wide tiles only enter when 128-wide tiles cannot give every
   // SM (or SM pair) a tile: decode-sized GEMMs (few rows, narrow N), where
-  // more CTAs streaming the weights beat fewer wide tiles.
+  // more CTAs streaming the weights beat fewer wide tiles. Two-piece pair
+  // tiles (2 x bn wide) enter for GEMMs whose tiles fit one wave: their
+  // single accumulator buffer cannot overlap a next tile's main loop.
   static const int kCandidates[] = {256, 224, 192, 160, 128, 96, 64};
+  static const int kWide[] = {256, 240, 224};
   GemmChoice best{0, 256};
   double best_cost = -1;
+  auto consider = [&](int pair, int bn, int nsub, double eff) {
+    const int rows = pair ? 2 * BM : BM;
+    const int units = pair ? sms / 2 : sms;
+    const long long tiles_m = (M + rows - 1) / rows;
+    const long long tiles = tiles_m * ((N + nsub * bn - 1) / (nsub * bn));
+    const long long waves = (tiles + units - 1) / units;
+    if (nsub > 1 && waves > 1) return;
+    const double cost = (double)(waves * nsub * bn) / eff;
+    if (best_cost < 0 || cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = GemmChoice{pair, bn, nsub};
+    }
+  };
   for (int pair = 0; pair < 2; ++pair) {
     const int rows = pair ? 2 * BM : BM;
     const int units = pair ? sms / 2 : sms;
-    const double eff = pair ? 0.85 : 0.67;
     if (pair && M <= BM) continue;
     const long long tiles_m = (M + rows - 1) / rows;
     const bool narrow_ok = tiles_m * ((N + 127) / 128) < units;
     for (int bn : kCandidates) {
       if (bn < 128 && !narrow_ok) continue;
-      const long long tiles = tiles_m * ((N + bn - 1) / bn);
-      const long long waves = (tiles + units - 1) / units;
-      const double cost = (double)(waves * bn) / eff;
-      if (best_cost < 0 || cost < best_cost - 1e-9) {
-        best_cost = cost;
-        best = GemmChoice{pair, bn};
-      }
+      consider(pair, bn, 1, pair ? 0.85 : 0.67);
     }
   }
+  if (M > BM && g_wide_tiles && allow_wide)
+    for (int bn : kWide) consider(1, bn, 2, 0.95);
   return best;
 }
 
@@ -1098,11 +1188,13 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   CE_REQUIRE(d != nullptr || swiglu_out != nullptr, "null output");
   CE_REQUIRE(swiglu_out == nullptr || (splits == 1 && N % 2 == 0 && swiglu_ld >= N / 2),
              "the SwiGLU epilogue needs one split, an even N and ld_out >= N / 2");
-  CE_REQUIRE(force_group == 0 || force_group == 1 || force_group == 2,
-             "cta group must be 0 (automatic), 1 or 2 (got %d)", force_group);
+  CE_REQUIRE(force_group >= 0 && force_group <= 3,
+             "cta group must be 0 (automatic), 1, 2 or 3 (CTA pair, two N pieces per tile) (got %d)",
+             force_group);
   CE_REQUIRE(force_bn == 0 || force_bn == 64 || force_bn == 96 || force_bn == 128 || force_bn == 160 ||
-                 force_bn == 192 || force_bn == 224 || force_bn == 256,
-             "tile width must be 0, 64, 96, 128, 160, 192, 224 or 256 (got %d)", force_bn);
+                 force_bn == 192 || force_bn == 224 || force_bn == 256 || (force_bn == 240 && force_group == 3),
+             "tile width must be 0, 64, 96, 128, 160, 192, 224 or 256 (or 240 with two-piece tiles) (got %d)",
+             force_bn);
   const int k_blocks_all = (K + (kRowBytes / elem) - 1) / (kRowBytes / elem);
   CE_REQUIRE(splits >= 1 && splits <= k_blocks_all,
              "split count must be in [1, %d] for K = %d (got %d)", k_blocks_all, K, splits);
@@ -1110,9 +1202,20 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
              "split stride %lld is smaller than one output", split_stride);
   if (!is_sm100()) return set_error(CE_ERR_USAGE, "tcgen05 GEMM needs an sm_100 device");
   const int sms = sm_count();
-  GemmChoice c = choose_tiles(M, N, sms);
-  if (force_group != 0) c.pair = force_group == 2;
+  // a forced one-piece kernel takes the widths chosen among one-piece tiles
+  const bool fan = rx != nullptr && rx->world > 1;
+  GemmChoice c = choose_tiles(M, N, sms, (force_group == 0 || force_group == 3) && !fan);
+  if (force_group != 0) {
+    c.pair = force_group >= 2;
+    c.nsub = force_group == 3 ? 2 : 1;
+    if (c.nsub == 2 && force_bn == 0 && c.bn != 256 && c.bn != 240 && c.bn != 224) c.bn = 256;
+  }
   if (force_bn != 0) c.bn = force_bn;
+  if (c.nsub == 2) {
+    CE_REQUIRE(c.bn == 256 || c.bn == 240 || c.bn == 224,
+               "two-piece tiles take an MMA width of 224, 240 or 256 (got %d)", c.bn);
+    CE_REQUIRE(M > BM, "two-piece tiles need more than %d rows (M = %d)", BM, M);
+  }
   const int rows_per_tile = c.pair ? 2 * BM : BM;
   CUtensorMap ta, tb;
   int rc = make_operand_map(&ta, a, dt, elem, K, M, lda, BM);
@@ -1129,7 +1232,7 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
   args.K = K;
   args.ldd = ldd;
   args.tiles_m = (M + rows_per_tile - 1) / rows_per_tile;
-  args.tiles_n = (N + c.bn - 1) / c.bn;
+  args.tiles_n = (N + c.nsub * c.bn - 1) / (c.nsub * c.bn);
   args.k_blocks = (K + (kRowBytes / elem) - 1) / (kRowBytes / elem);
   args.prefetch = g_prefetch_kblocks;
   args.splits = splits;
@@ -1145,7 +1248,44 @@ int gemm_dispatch(float *d, const void *a, const void *b, int M, int N, int K, i
     args.rx = *rx;
   }
   const int tiles = args.tiles_m * args.tiles_n * splits;
-  if (c.pair) {
+  if constexpr (kKind == 0) {
+    // bf16 fan-out: the epilogue stages its stores through shared memory
+    if (fan && c.nsub == 1) {
+      if (c.pair) {
+        const int grid = 2 * (tiles < sms / 2 ? tiles : sms / 2);
+        switch (c.bn) {
+          case 256: return launch_gemm_pair<kKind, 256, 1, 1>(ta, tb, args, grid, s, pdl);
+          case 224: return launch_gemm_pair<kKind, 224, 1, 1>(ta, tb, args, grid, s, pdl);
+          case 192: return launch_gemm_pair<kKind, 192, 1, 1>(ta, tb, args, grid, s, pdl);
+          case 160: return launch_gemm_pair<kKind, 160, 1, 1>(ta, tb, args, grid, s, pdl);
+          case 128: return launch_gemm_pair<kKind, 128, 1, 1>(ta, tb, args, grid, s, pdl);
+          case 96: return launch_gemm_pair<kKind, 96, 1, 1>(ta, tb, args, grid, s, pdl);
+          case 64: return launch_gemm_pair<kKind, 64, 1, 1>(ta, tb, args, grid, s, pdl);
+        }
+      } else {
+        const int grid = tiles < sms ? tiles : sms;
+        switch (c.bn) {
+          case 256: return launch_gemm<kKind, 256, 1>(ta, tb, args, grid, s, pdl);
+          case 224: return launch_gemm<kKind, 224, 1>(ta, tb, args, grid, s, pdl);
+          case 192: return launch_gemm<kKind, 192, 1>(ta, tb, args, grid, s, pdl);
+          case 160: return launch_gemm<kKind, 160, 1>(ta, tb, args, grid, s, pdl);
+          case 128: return launch_gemm<kKind, 128, 1>(ta, tb, args, grid, s, pdl);
+          case 96: return launch_gemm<kKind, 96, 1>(ta, tb, args, grid, s, pdl);
+          case 64: return launch_gemm<kKind, 64, 1>(ta, tb, args, grid, s, pdl);
+        }
+      }
+      return set_error(CE_ERR_USAGE, format("unsupported tile width %d", c.bn));
+    }
+  }
+  if (c.pair && c.nsub == 2) {
+    const int pairs = tiles < sms / 2 ? tiles : sms / 2;
+    const int grid = 2 * pairs;
+    switch (c.bn) {
+      case 256: return launch_gemm_pair<kKind, 256, 2>(ta, tb, args, grid, s, pdl);
+      case 240: return launch_gemm_pair<kKind, 240, 2>(ta, tb, args, grid, s, pdl);
+      case 224: return launch_gemm_pair<kKind, 224, 2>(ta, tb, args, grid, s, pdl);
+    }
+  } else if (c.pair) {
     const int pairs = tiles < sms / 2 ? tiles : sms / 2;
     const int grid = 2 * pairs;
     switch (c.bn) {
@@ -2029,6 +2169,11 @@ int gemm_w4t(float *d, const uint16_t *a, const uint8_t *packed, const float *al
 int gemm_set_prefetch(int kblocks) {
   CE_REQUIRE(kblocks >= 0 && kblocks <= 64, "prefetch distance must be in [0, 64] (got %d)", kblocks);
   g_prefetch_kblocks = kblocks;
+  return CE_OK;
+}
+
+int gemm_set_wide_tiles(int on) {
+  g_wide_tiles = on != 0;
   return CE_OK;
 }
 

@@ -65,6 +65,24 @@ __global__ void rowx_wait_kernel(const unsigned long long *done, unsigned long l
   if (q == 0) *epoch = e;
 }
 
+// First step of ce_rowx_put, one warp: tells every peer that this rank
+// accepts the next exchange (its consumers of the previous one ran earlier
+// in the stream), then lane q waits (bounded) until peer q accepts it too.
+__global__ void rowx_ready_kernel(RowxSync rx) {
+  if (threadIdx.x == 0) rowx_signal_ready(rx);
+  rowx_wait_ready_warp(rx, &g_rowx_status, 81u);
+}
+
+// Last step of ce_rowx_put: the copies before it in the stream have landed
+// in the peers' blocks; tell every peer.
+__global__ void rowx_done_kernel(RowxSync rx) {
+  __threadfence_system();
+  const unsigned long long e = rowx_exchange(rx);
+  for (int q = 0; q < rx.world; ++q)
+    if (q != rx.rank)
+      st_release_sys(reinterpret_cast<unsigned long long *>(rx.blocks[q] + rx.done_off) + rx.rank, e);
+}
+
 // out[b][c] = staging[q][b][c - lo_q] for the rank q whose slice holds
 // column c (bounds of shard_bounds); one thread per 4 outputs when the
 // slices are 4-aligned, else per output.
@@ -270,6 +288,26 @@ int ce_rowx_wait(ce_rowx *x, ce_stream_t stream) {
   const unsigned long long *done = reinterpret_cast<const unsigned long long *>(x->block + x->done_off);
   return launch_kernel(rowx_wait_kernel, dim3(1), dim3(32), 0, (cudaStream_t)stream, false, "rowx_wait_kernel",
                        done, x->local, x->world, x->rank);
+}
+
+int ce_rowx_put(ce_rowx *x, ce_stream_t stream) {
+  RowxSync rx;
+  float *out = nullptr;
+  int lo = 0, hi = 0, batch = 0, rows = 0;
+  int rc = rowx_sync(x, &rx, &out, &lo, &hi, &batch, &rows);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  rc = launch_kernel(rowx_ready_kernel, dim3(1), dim3(32), 0, s, false, "rowx_ready_kernel", rx);
+  if (rc) return rc;
+  // this rank's columns [lo, hi) of every row, to the same place in each
+  // peer's block: strided copies over NVLink by the copy engines
+  const size_t pitch = (size_t)rows * 4, off = (size_t)lo * 4;
+  for (int q = 0; q < x->world; ++q) {
+    if (q == x->rank) continue;
+    CE_CUDA_TRY(cudaMemcpy2DAsync(x->peer[q] + off, pitch, x->block + off, pitch, (size_t)(hi - lo) * 4, batch,
+                                  cudaMemcpyDeviceToDevice, s));
+  }
+  return launch_kernel(rowx_done_kernel, dim3(1), dim3(1), 0, s, false, "rowx_done_kernel", rx);
 }
 
 int ce_rowx_close(ce_rowx *x) {

@@ -77,11 +77,16 @@ class RowShardedPlan:
     them across ranks. The slices of the product are joined into every
     rank's out [batch][rows] by one of three exchanges:
 
-    mode "p2p" (default): the library's fused peer-memory join
-      (ce_plan_gemm_rowx): the GEMM epilogue stores each output tile into
-      every rank's exchange block over NVLink as it leaves tensor memory,
-      and ce_rowx_wait waits for the peers' slices; `exchanges` independent
-      exchange blocks let callers pipeline steps (slot i % exchanges).
+    mode "p2p" (default): the library's peer-memory join: the slice GEMM
+      writes into this rank's columns of its exchange block (device memory
+      shared by CUDA IPC), ce_rowx_put copies them into every peer's block
+      with the copy engines over NVLink, and ce_rowx_wait waits for the
+      peers' slices; `exchanges` independent exchange blocks let callers
+      pipeline steps (slot i % exchanges).
+    mode "fused": the same exchange blocks, but the GEMM's epilogue stores
+      each output tile into every rank's block as it leaves tensor memory
+      (ce_plan_gemm_rowx); it overlaps the multiply where a CTA owns several
+      tiles, at the rate of the SMs' remote stores.
     mode "nccl": the slice GEMM writes into this rank's slot of a staging
       buffer, ce_allgather_rows joins the slots with ncclAllGather on a
       communicator made through the library (ce_nccl_comm_init).
@@ -89,7 +94,7 @@ class RowShardedPlan:
       backend), the join of gather_row_shards.
     """
 
-    MODES = ("p2p", "nccl", "torch")
+    MODES = ("p2p", "fused", "nccl", "torch")
 
     def __init__(self, ce, batch, size, rows, precision, group=None, mode="p2p", exchanges=1):
         if mode not in self.MODES:
@@ -103,7 +108,7 @@ class RowShardedPlan:
         self.local = ce.Plan(batch, size, self.hi - self.lo, precision)
         dev = torch.device("cuda", torch.cuda.current_device())
         self.outs = []
-        if mode == "p2p":
+        if mode in ("p2p", "fused"):
             self.xs = [ce.RowExchange(batch, rows, self.world, self.rank) for _ in range(exchanges)]
             for x in self.xs:
                 handles = [None] * self.world
@@ -150,6 +155,10 @@ class RowShardedPlan:
         [batch][rows] output of exchange `slot`."""
         ce, out = self.ce, self.outs[slot]
         if self.mode == "p2p":
+            self.local.gemm_ld(out[:, self.lo:], self.rows, stream=stream)
+            self.xs[slot].put(stream=stream)
+            self.xs[slot].wait(stream=stream)
+        elif self.mode == "fused":
             self.local.gemm_rowx(self.xs[slot], stream=stream)
             self.xs[slot].wait(stream=stream)
         elif self.mode == "nccl":
@@ -172,7 +181,7 @@ class RowShardedPlan:
         return res
 
     def close(self):
-        if self.mode == "p2p":
+        if self.mode in ("p2p", "fused"):
             # no rank frees its exchange block while a peer may still map it
             torch.cuda.synchronize()
             dist.barrier(self.group)
@@ -262,7 +271,7 @@ class ShardedLlama:
         m.segment(ce.SEG_PICK, stream=stream)
 
     def close(self):
-        if self.mode == "p2p":
+        if self.mode in ("p2p", "fused"):
             # no rank frees its exchange block while a peer may still map it
             torch.cuda.synchronize()
             dist.barrier(self.group)

@@ -165,7 +165,10 @@ int ce_gemm_bf16_tile(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev
  * bits), CE_PREC_TF32 (a, b fp32) or CE_PREC_FP8_E4M3 (a, b E4M3 codes, no
  * scales); cta_group 1 = single-CTA kernel
  * (128 x tile_n tiles), 2 = CTA-pair kernel (256 x tile_n tiles on two SMs,
- * tcgen05 cta_group::2), 0 = automatic; tile_n 64/96/128/160/192/224/256 or 0.
+ * tcgen05 cta_group::2), 3 = CTA-pair kernel with two N pieces per tile
+ * (256 x 2 tile_n tiles: two N = tile_n MMAs per k step on the same A tile,
+ * one 512-column TMEM accumulator; tile_n 224, 240 or 256, M > 128),
+ * 0 = automatic; tile_n 64/96/128/160/192/224/256 or 0.
  * Test hook in the spirit of the reference's forced tiles and schedules
  * (decoder_optimized.cu:543-557, DECODER_OPT_TILE / _SCHEDULE). */
 int ce_gemm_config(int precision, float *d_dev, const void *a_dev, const void *b_dev, int M, int N,
@@ -244,6 +247,11 @@ int ce_gemm_f16(float *d_dev, const uint16_t *a_dev, const uint16_t *b_dev, cons
  * TMA producer prefetches operand tiles this many k-blocks ahead into L2
  * (0 = off, at most 64). */
 int ce_gemm_tuning(int l2_prefetch_kblocks);
+
+/* Library-wide, set at setup time: whether the automatic tile choice may
+ * take two-piece CTA-pair tiles (cta_group 3 of ce_gemm_config) for GEMMs
+ * whose tiles then fit one wave (1, the default) or not (0). */
+int ce_gemm_wide_tiles(int on);
 
 /* Same contraction on fp32 operands with tcgen05 kind::tf32 (the tensor
  * core reads the upper 19 bits of each fp32 value). lda, ldb multiples of 4
@@ -507,12 +515,20 @@ int ce_allgather_rows(void *comm, float *out_dev, float *staging_dev, int batch,
  * the same sequence of calls. 2 <= world <= 8. open / connect / close are
  * setup calls; ce_plan_gemm_rowx and ce_rowx_wait are enqueue-only (the
  * exchange count lives in device memory). */
+/* ce_rowx_put is the same join with the copies on the copy engines instead
+ * of the GEMM's epilogue: the caller writes this rank's slice into its own
+ * output (ce_plan_gemm_ld into ce_rowx_output's buffer + lo, ldd = rows),
+ * then ce_rowx_put enqueues a readiness handshake with the peers (bounded
+ * wait), one strided cudaMemcpy2DAsync of the slice into each peer's output
+ * over NVLink, and a kernel that signals the peers; ce_rowx_wait as above.
+ * Enqueue-only. */
 typedef struct ce_rowx ce_rowx;
 int ce_rowx_open(ce_rowx **x, int batch, int rows, int world, int rank, void *handle_out);
 int ce_rowx_connect(ce_rowx *x, const void *handles);
 int ce_rowx_output(ce_rowx *x, float **out_dev, int *lo, int *hi);
 int ce_plan_gemm_rowx(ce_plan *plan, ce_rowx *x, ce_stream_t stream);
 int ce_rowx_wait(ce_rowx *x, ce_stream_t stream);
+int ce_rowx_put(ce_rowx *x, ce_stream_t stream);
 int ce_rowx_close(ce_rowx *x);
 
 /* ------------------------------------------------------------------ */

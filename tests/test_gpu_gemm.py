@@ -215,3 +215,55 @@ def test_kernels_agree_on_sheet_shape(ce, O, dev, cta_group):
     assert np.isfinite(hd).all()
     rows = np.random.default_rng(2).choice(M, 24, replace=False)
     _check_bf16(O, hd[rows], A[rows], B)
+
+
+@pytest.mark.parametrize("tile_n", [224, 240, 256])
+@pytest.mark.parametrize("shape", [(300, 1000, 520), (257, 481, 64), (1024, 2000, 1028)])
+def test_two_piece_pair_tiles_bf16(ce, O, dev, tile_n, shape):
+    """CTA-pair tiles of two N pieces (cta_group 3: 256 x 2 tile_n, one
+    512-column accumulator), ragged in M, N and K, with several tiles per
+    pair on the larger shape."""
+    M, N, K = shape
+    rng = np.random.default_rng(tile_n + M)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K)).astype(np.float32)
+    ld = (K + 7) // 8 * 8  # 16-byte row strides
+    da, db = _bf16_dev(O.bf16_bits(A), dev, ld), _bf16_dev(O.bf16_bits(B), dev, ld)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_config(ce.PREC_BF16, d, da, db, k=K, cta_group=3, tile_n=tile_n)
+    ce.device_status()
+    _check_bf16(O, d.cpu().numpy(), A, B)
+
+
+def test_two_piece_pair_tiles_tf32(ce, O, dev):
+    M, N, K = 520, 1000, 100
+    rng = np.random.default_rng(5)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K)).astype(np.float32)
+    d = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_config(ce.PREC_TF32, d, torch.from_numpy(A).to(dev), torch.from_numpy(B).to(dev), cta_group=3,
+                   tile_n=240)
+    ce.device_status()
+    ref, mag = O.gemm_ref(A, B)
+    bound = (2.0 * 2.0 ** -10 + O.gamma_worst(K)) * mag + 1e-30
+    assert np.all(np.abs(d.cpu().numpy().astype(np.float64) - ref) <= bound)
+
+
+def test_two_piece_tiles_equal_the_pair_kernel_on_sheet_shape(ce, O, dev):
+    """The BASELINE GEMM (1024 x 8192 x 16384) in two-piece pair tiles (the
+    automatic choice there) equals the one-piece pair kernel bit for bit:
+    every output element accumulates the same products in the same k order."""
+    M, N, K = 1024, 8192, 16384
+    rng = np.random.default_rng(11)
+    A = rng.standard_normal((M, K)).astype(np.float32)
+    B = (rng.standard_normal((N, K)) / 128.0).astype(np.float32)
+    da = torch.from_numpy(O.bf16_bits(A).view(np.int16)).to(dev)
+    db = torch.from_numpy(O.bf16_bits(B).view(np.int16)).to(dev)
+    d2 = torch.full((M, N), float("nan"), device=dev)
+    d3 = torch.full((M, N), float("nan"), device=dev)
+    ce.gemm_config(ce.PREC_BF16, d2, da, db, cta_group=2, tile_n=224)
+    ce.gemm_config(ce.PREC_BF16, d3, da, db, cta_group=3, tile_n=240)
+    ce.device_status()
+    assert torch.equal(d2, d3)
+    rows = np.random.default_rng(3).choice(M, 16, replace=False)
+    _check_bf16(O, d3.cpu().numpy()[rows], A[rows], B)
