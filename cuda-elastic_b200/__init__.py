@@ -82,6 +82,7 @@ _SIGNATURES = {
     "ce_gemm_tf32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_tuning": [_i],
     "ce_gemm_wide_tiles": [_i],
+    "ce_rows_tuning": [_i],
     "ce_gemm_config": [_i, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp],
     "ce_gemm_fp32": [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp],
     "ce_convert_bf16": [_vp, _vp, _i, _i, _i, _vp],

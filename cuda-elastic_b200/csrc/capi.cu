@@ -22,7 +22,7 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
                    int cols, int gemv_rows, float eps, cudaStream_t s,
                    uint8_t *normalized_e4m3 = nullptr, int ld_e4m3 = 0, float *e4m3_scale = nullptr,
-                   int norm_lo = 0, int norm_hi = 0x7fffffff);
+                   int norm_lo = 0, int norm_hi = 0x7fffffff, const RowsExtras *extras = nullptr);
 int convert_bf16(uint16_t *out, const float *in, int rows, int cols, int ld, cudaStream_t s);
 size_t w4t_packed_bytes(int N, int K);
 int w4t_expand_f16(uint16_t *out, const uint8_t *packed, int N, int K, cudaStream_t s);
@@ -51,6 +51,9 @@ int w4_pack(uint8_t *codes_t, uint8_t *scales_t, const uint8_t *codes, const uin
 int gemm_status();
 int gemm_bs_status();
 int rowx_status();
+int rows_status();
+int rows_set_wait_limit(unsigned long long ns);
+int rows_set_streaming(int on);
 int gemm_set_wait_limit(unsigned long long ns);
 int gemm_bs_set_wait_limit(unsigned long long ns);
 int llama_set_wait_limit(unsigned long long ns);
@@ -80,6 +83,8 @@ int quantize_mxfp6(uint8_t *codes, uint8_t *scales, const float *x, int rows, in
 int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsigned int *amax_bits,
                    const float *x, int rows, int cols, int ld_bytes, cudaStream_t s);
 int gemm_set_prefetch(int kblocks);
+int quantize_nvfp4_atoms(uint8_t *codes, uint8_t *atoms, float *encode_decode, const unsigned int *amax_bits,
+                         const float *x, int rows, int cols, int ld_bytes, int katoms, cudaStream_t s);
 int gemm_set_wide_tiles(int on);
 
 // ---------------------------------------------------------------------------
@@ -213,14 +218,16 @@ int ce_device_status(void) {
   const int a = gemm_status();
   const int b = gemm_bs_status();
   const int c = rowx_status();
-  return a != CE_OK ? a : b != CE_OK ? b : c;
+  const int d = rows_status();
+  return a != CE_OK ? a : b != CE_OK ? b : c != CE_OK ? c : d;
 }
 
 int ce_set_wait_limit(double seconds) {
   CE_REQUIRE(seconds >= 1e-3 && seconds <= 3600.0, "wait limit must be in [0.001, 3600] s (got %g)", seconds);
   const unsigned long long ns = (unsigned long long)(seconds * 1e9);
   for (int (*set)(unsigned long long) :
-       {gemm_set_wait_limit, gemm_bs_set_wait_limit, llama_set_wait_limit, rowx_set_wait_limit}) {
+       {gemm_set_wait_limit, gemm_bs_set_wait_limit, llama_set_wait_limit, rowx_set_wait_limit,
+        rows_set_wait_limit}) {
     const int rc = set(ns);
     if (rc != CE_OK) return set_error(rc, "cudaMemcpyToSymbol(wait limit) failed");
   }
@@ -360,6 +367,8 @@ int ce_gemm_bf16_tile(float *d, const uint16_t *a, const uint16_t *b, int M, int
 int ce_gemm_tuning(int l2_prefetch_kblocks) { return gemm_set_prefetch(l2_prefetch_kblocks); }
 
 int ce_gemm_wide_tiles(int on) { return gemm_set_wide_tiles(on); }
+
+int ce_rows_tuning(int streaming) { return rows_set_streaming(streaming); }
 
 int ce_gemm_config(int precision, float *d, const void *a, const void *b, int M, int N, int K,
                    int lda, int ldb, int ldd, int cta_group, int tile_n, ce_stream_t stream) {
@@ -517,9 +526,7 @@ struct ce_plan {
   // block-scaled (MXFP6 / NVFP4): scale atoms, tensor scales, staging
   uint8_t *w_atoms = nullptr;    // B scale atoms, grouped by CE_BS_TILE_N rows
   uint8_t *a_atoms = nullptr;    // A scale atoms, grouped by 128 rows
-  uint8_t *a_sf = nullptr;       // A scales, row-major
-  uint8_t *a_codes = nullptr;    // MXFP6: unpacked A codes before packing
-  float *a_f32 = nullptr;        // normalized rows when the caller passes none
+  float *a_f32 = nullptr;        // NVFP4: normalized rows when the caller passes none
   float *a_ts = nullptr;         // NVFP4 tensor scales of A (encode, decode)
   float *w_ts = nullptr;         // NVFP4 tensor scales of W
   uint32_t *scratch = nullptr;   // NVFP4 amax reduction word
@@ -557,11 +564,15 @@ int ce_plan_create(ce_plan **out, int batch, int size, int rows, int precision) 
     const int fmt = precision == CE_PREC_MXFP6_E3M2 ? 0 : 1;
     const int vec = fmt == 0 ? 32 : 16;
     p->ld = fmt == 0 ? size : size / 2;  // operand bytes per row
+    (void)vec;
+    // the rows launch writes the A operand and its scale atoms itself (MXFP6),
+    // or max |normalized| for a quantizer pass (NVFP4); the atoms' padding
+    // bytes are zeroed once here and never written again
+    const size_t atom_bytes = (size_t)sf_row_atoms(batch, 128) * sf_katoms(fmt, size) * 512;
     cudaError_t e2 = cudaMalloc(&p->activations, (size_t)batch * p->ld);
-    if (e2 == cudaSuccess) e2 = cudaMalloc(&p->a_atoms, (size_t)sf_row_atoms(batch, 128) * sf_katoms(fmt, size) * 512);
-    if (e2 == cudaSuccess) e2 = cudaMalloc(&p->a_sf, (size_t)batch * (size / vec));
-    if (e2 == cudaSuccess) e2 = cudaMalloc(&p->a_f32, (size_t)batch * size * 4);
-    if (e2 == cudaSuccess && fmt == 0) e2 = cudaMalloc(&p->a_codes, (size_t)batch * size);
+    if (e2 == cudaSuccess) e2 = cudaMalloc(&p->a_atoms, atom_bytes);
+    if (e2 == cudaSuccess) e2 = cudaMemset(p->a_atoms, 0, atom_bytes);
+    if (e2 == cudaSuccess && fmt == 1) e2 = cudaMalloc(&p->a_f32, (size_t)batch * size * 4);
     if (e2 == cudaSuccess && fmt == 1) e2 = cudaMalloc(&p->a_ts, 2 * sizeof(float));
     if (e2 == cudaSuccess && fmt == 1) e2 = cudaMalloc(&p->w_ts, 2 * sizeof(float));
     if (e2 == cudaSuccess && fmt == 1) e2 = cudaMalloc(&p->scratch, sizeof(uint32_t));
@@ -592,8 +603,7 @@ int ce_plan_destroy(ce_plan *p) {
   if (p->weights) cudaFree(p->weights);
   if (p->activations) cudaFree(p->activations);
   for (void *q : {(void *)p->a_scale, (void *)p->w_scale, (void *)p->w_atoms, (void *)p->a_atoms,
-                  (void *)p->a_sf, (void *)p->a_codes, (void *)p->a_f32, (void *)p->a_ts,
-                  (void *)p->w_ts, (void *)p->scratch})
+                  (void *)p->a_f32, (void *)p->a_ts, (void *)p->w_ts, (void *)p->scratch})
     if (q) cudaFree(q);
   delete p;
   return CE_OK;
@@ -693,26 +703,33 @@ static int plan_rows(ce_plan *p, float *normalized, float *softmax, const float 
                      const float *norm_w, const float *logits, float eps, cudaStream_t s) {
   const int nsoft = logits ? p->batch : 0;
   if (block_scaled(p->precision)) {
-    // rmsnorm (+ softmax) in one launch, then the activation quantizer of
-    // the format (the reference's per-step conversion,
-    // decoder_lowprec.cu:469-482), then the scale atoms
-    float *xn = normalized ? normalized : p->a_f32;
-    int rc = rows_iteration(xn, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr, nullptr,
-                            p->batch, nsoft, p->size, 0, eps, s);
-    if (rc) return rc;
+    // The activation quantizer of the format (the reference converts with
+    // separate launches per step, decoder_lowprec.cu:202-340, 469-482) fused
+    // into the rows launch: MXFP6's block scales need only each 32-value
+    // block, so the rows launch writes the packed codes and scale atoms from
+    // the normalized values in registers; NVFP4's tensor scale needs max
+    // |normalized| over the whole batch first, so the rows launch reduces it
+    // (keeping the fp32 rows L2-resident) and one pass writes codes and atoms.
     const int fmt = p->precision == CE_PREC_MXFP6_E3M2 ? 0 : 1;
-    const int vec = fmt == 0 ? 32 : 16;
+    const int katoms = sf_katoms(fmt, p->size);
+    RowsExtras ex;
+    ex.katoms = katoms;
     if (fmt == 0) {
-      rc = quantize_mxfp6(p->a_codes, p->a_sf, xn, p->batch, p->size, p->size, s);
-      if (rc == CE_OK)
-        rc = pack_mxfp6(static_cast<uint8_t *>(p->activations), p->a_codes, p->batch, p->size,
-                        p->size, p->size, s);
-    } else {
-      rc = quantize_nvfp4(static_cast<uint8_t *>(p->activations), p->a_sf, p->a_ts, p->scratch, xn,
-                          p->batch, p->size, p->size / 2, s);
+      ex.mx_operand = static_cast<uint8_t *>(p->activations);
+      ex.mx_ld = p->size;
+      ex.mx_atoms = p->a_atoms;
+      return rows_iteration(normalized, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr, nullptr,
+                            p->batch, nsoft, p->size, 0, eps, s, nullptr, 0, nullptr, 0, 0x7fffffff, &ex);
     }
+    float *xn = normalized ? normalized : p->a_f32;
+    ex.amax_bits = p->scratch;
+    ex.keep_normalized = 1;
+    CE_CUDA_TRY(cudaMemsetAsync(p->scratch, 0, sizeof(uint32_t), s));
+    int rc = rows_iteration(xn, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr, nullptr, p->batch, nsoft,
+                            p->size, 0, eps, s, nullptr, 0, nullptr, 0, 0x7fffffff, &ex);
     if (rc) return rc;
-    return sf_to_atoms(p->a_atoms, p->a_sf, p->batch, p->size / vec, sf_katoms(fmt, p->size), 128, s);
+    return quantize_nvfp4_atoms(static_cast<uint8_t *>(p->activations), p->a_atoms, p->a_ts, p->scratch, xn,
+                                p->batch, p->size, p->size / 2, katoms, s);
   }
   if (p->precision == CE_PREC_FP8_E4M3)
     return rows_iteration(normalized, nullptr, 0, x, norm_w, softmax, logits, nullptr, nullptr,
@@ -772,12 +789,12 @@ int ce_plan_operands(ce_plan *p, float *a, float *w, ce_stream_t stream) {
         d.format = fmt == 0 ? kOperandMXFP6 : kOperandNVFP4;
         d.ld = fmt == 0 ? p->size : p->size / 2;
         d.nsf = p->size / (fmt == 0 ? 32 : 16);
-        // A keeps its row-major scales; W only its atoms (grouped by the
-        // GEMM's B tile rows)
-        d.atoms = which == 1;
-        d.sf = which == 0 ? p->a_sf : p->w_atoms;
+        // both as the GEMM reads them: scale atoms, A grouped by 128 rows,
+        // W by the GEMM's B tile rows
+        d.atoms = true;
+        d.sf = which == 0 ? p->a_atoms : p->w_atoms;
         d.katoms = sf_katoms(fmt, p->size);
-        d.group_rows = CE_BS_TILE_N;
+        d.group_rows = which == 0 ? 128 : CE_BS_TILE_N;
         if (fmt == 1) d.tensor_decode = (which == 0 ? p->a_ts : p->w_ts) + 1;
         break;
       }

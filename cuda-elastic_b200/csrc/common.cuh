@@ -184,6 +184,18 @@ struct DequantOperand {
 };
 int dequant_operand(const DequantOperand &d, cudaStream_t s);
 
+// Extra outputs of the rows launch for the block-scaled GEMMs (rows.cu):
+// the MXFP6 packed operand and its scale atoms written from the normalized
+// rows, or the max |normalized| for the NVFP4 tensor scale.
+struct RowsExtras {
+  uint8_t *mx_operand = nullptr;   // [rows][mx_ld bytes]
+  int mx_ld = 0;
+  uint8_t *mx_atoms = nullptr;     // A-operand UE8M0 scale atoms (128-row groups)
+  int katoms = 0;
+  unsigned int *amax_bits = nullptr;
+  int keep_normalized = 0;         // write the fp32 normalized rows L2-resident
+};
+
 struct ExchangeWait {
   const unsigned long long *flags;  // this rank's flags of the exchange kind, one per sending rank; null = no wait
   const unsigned *gen;

@@ -20,7 +20,7 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
                    int cols, int gemv_rows, float eps, cudaStream_t s,
                    uint8_t *normalized_e4m3 = nullptr, int ld_e4m3 = 0, float *e4m3_scale = nullptr,
-                   int norm_lo = 0, int norm_hi = 0x7fffffff);
+                   int norm_lo = 0, int norm_hi = 0x7fffffff, const RowsExtras *extras = nullptr);
 int gemm_bf16(float *d, const uint16_t *a, const uint16_t *b, int M, int N, int K, int lda,
               int ldb, int ldd, const float *row_scale, const float *col_scale, int force_bn,
               cudaStream_t s, int force_group = 0);

@@ -161,6 +161,55 @@ __global__ void quantize_nvfp4_kernel(uint8_t *codes, uint8_t *scales, const flo
   if (live && i == 0) scales[(size_t)row * nblocks + blk] = (uint8_t)sc;
 }
 
+// NVFP4 activation operand after a rows launch that reduced max |x| into
+// amax_bits: the tensor scales (thread 0 of block 0 publishes them for the
+// GEMM's alpha) and the codes with quantize_nvfp4_kernel's arithmetic, four
+// consecutive values per thread (one float4 load, two code bytes), the four
+// threads of a 16-value block sharing its amax by shuffles; the UE4M3 scales
+// go straight into the A operand's 512-byte atoms. cols % 16 == 0.
+__global__ void quantize_nvfp4_atoms_kernel(uint8_t *codes, uint8_t *atoms, float *encode_decode,
+                                            const unsigned int *amax_bits, const float4 *x, int rows, int cols,
+                                            int ld_bytes, int katoms) {
+  const float a = __uint_as_float(*amax_bits);
+  const float s = a > 0.f ? 2688.0f / a : 1.0f;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    encode_decode[0] = s;
+    encode_decode[1] = 1.0f / s;
+  }
+  const int cols4 = cols / 4;
+  const long long total = (long long)rows * cols4;
+  const int lane = threadIdx.x & 31;
+  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t - lane < total;
+       t += (long long)gridDim.x * blockDim.x) {
+    const bool live = t < total;
+    const int row = live ? (int)(t / cols4) : 0, q = live ? (int)(t % cols4) : 0;  // columns 4q .. 4q + 3
+    const float4 v = live ? x[t] : make_float4(0.f, 0.f, 0.f, 0.f);
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    float target = amax / 6.0f;
+    target = target * s;
+    const uint32_t sc = e4m3x2(target, 0.f) & 0x7Fu;
+    const float f = ue4m3_value(sc);
+    float r[4] = {0.f, 0.f, 0.f, 0.f};
+    if (sc != 0) {
+      r[0] = v.x * s; r[0] = r[0] / f;
+      r[1] = v.y * s; r[1] = r[1] / f;
+      r[2] = v.z * s; r[2] = r[2] / f;
+      r[3] = v.w * s; r[3] = r[3] / f;
+    }
+    if (live) {
+      const uint32_t lo = sc != 0 ? e2m1x2(r[0], r[1]) : 0u, hi = sc != 0 ? e2m1x2(r[2], r[3]) : 0u;
+      *reinterpret_cast<uint16_t *>(codes + (size_t)row * ld_bytes + 2 * q) = (uint16_t)(lo | (hi << 8));
+      if ((q & 3) == 0) {
+        const int blk = q / 4, mm = row % 128;
+        atoms[((size_t)(row / 128) * katoms + blk / 4) * 512 + (mm % 32) * 16 + (mm / 32) * 4 + (blk % 4)] =
+            (uint8_t)sc;
+      }
+    }
+  }
+}
+
 // Row-major scales [rows][nsf] -> 512-byte atoms (see gemm_bs.cu): rows are
 // taken in groups of group_rows, each group padded to whole 128-row atom
 // rows; scale columns padded to katoms * 4. Padding bytes are 0.
@@ -344,6 +393,24 @@ int quantize_nvfp4(uint8_t *codes, uint8_t *scales, float *encode_decode, unsign
   quantize_nvfp4_kernel<<<(unsigned)((halves + 15) / 16), 256, 0, s>>>(
       codes, scales, x, encode_decode, rows, cols, ld_bytes, nblocks);
   CE_LAUNCH_CHECK("quantize_nvfp4_kernel");
+  return CE_OK;
+}
+
+// Pass 2 of the fused NVFP4 activation quantizer (pass 1: the rows launch
+// with RowsExtras::amax_bits). Padding atom bytes must already be zero.
+int quantize_nvfp4_atoms(uint8_t *codes, uint8_t *atoms, float *encode_decode, const unsigned int *amax_bits,
+                         const float *x, int rows, int cols, int ld_bytes, int katoms, cudaStream_t s) {
+  CE_REQUIRE(codes && atoms && encode_decode && amax_bits && x, "null argument");
+  CE_REQUIRE(rows >= 1 && cols >= 16 && cols % 16 == 0 && ld_bytes * 2 >= cols && ld_bytes % 2 == 0 &&
+                 katoms * 64 >= cols && (reinterpret_cast<uintptr_t>(x) & 15u) == 0,
+             "bad nvfp4 shape %dx%d (cols %% 16 == 0, 16-byte aligned rows)", rows, cols);
+  const long long total = (long long)rows * (cols / 4);
+  const long long want = (total + 255) / 256;
+  const int blocks = (int)(want < (long long)sm_count() * 16 ? want : (long long)sm_count() * 16);
+  quantize_nvfp4_atoms_kernel<<<blocks, 256, 0, s>>>(codes, atoms, encode_decode, amax_bits,
+                                                     reinterpret_cast<const float4 *>(x), rows, cols, ld_bytes,
+                                                     katoms);
+  CE_LAUNCH_CHECK("quantize_nvfp4_atoms_kernel");
   return CE_OK;
 }
 

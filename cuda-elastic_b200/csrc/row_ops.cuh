@@ -208,5 +208,65 @@ __device__ __forceinline__ void rmsnorm_row_e4m3(const float4 *x, const float4 *
   quantize_row_e4m3<NV>(v, codes, scale_out, cols4, scratch);
 }
 
+// --- block-scaled GEMM operands written from normalized rows -------------
+// (the MXFP6 and NVFP4 activation quantizers fused into the rows launch)
+
+// Two fp32 values to two E3M2 codes (round to nearest even, saturating to
+// +-28; a zero result is +0): lo in bits 0-7, hi in bits 8-15.
+__device__ __forceinline__ uint32_t e3m2x2_codes(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e3m2x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  uint32_t c = r;
+  if ((c & 0xFFu) == 0x20u) c &= ~0xFFu;  // -0 -> +0
+  if ((c & 0xFF00u) == 0x2000u) c &= ~0xFF00u;
+  return c;
+}
+
+// Byte offset of scale (row, scale column c) in the 512-byte atom layout of
+// the block-scaled GEMM's A operand (rows in groups of 128, 4 scale columns
+// per atom; the layout sf_to_atoms writes).
+__device__ __forceinline__ size_t a_atom_offset(int row, int c, int katoms) {
+  const int mm = row % 128;
+  return ((size_t)(row / 128) * katoms + c / 4) * 512 + (mm % 32) * 16 + (mm / 32) * 4 + (c % 4);
+}
+
+// MXFP6 (E3M2, UE8M0 per 32 values) operand of one normalized row held as
+// float4 slots tid + j * blockDim.x: the 8 lanes of a 32-value block share
+// its amax by shuffles, 4 lanes of a 16-value group gather their 6-bit codes
+// into the packed 16-byte group (12 bytes of fields, 4 zero bytes), and the
+// block's first lane writes the scale atom byte. The arithmetic is the
+// standalone quantizer's: shared = ilogb(amax) - 4, v * 2^-shared, E3M2.
+// blockDim.x must be a multiple of 8 (it is a multiple of 32).
+template <int NV>
+__device__ __forceinline__ void mxfp6_row(const float4 (&o)[NV], uint8_t *operand_row, uint8_t *atoms, int row,
+                                          int katoms, int cols4) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;  // float4 slot: columns 4i .. 4i + 3
+    const bool live = i < cols4;
+    float amax = live ? fmaxf(fmaxf(fabsf(o[j].x), fabsf(o[j].y)), fmaxf(fabsf(o[j].z), fabsf(o[j].w))) : 0.f;
+#pragma unroll
+    for (int m = 1; m < 8; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, m));
+    int shared = 0;
+    uint32_t scale_code = 0;
+    if (amax != 0.f) {
+      shared = ilogbf(amax) - 4;
+      shared = max(-127, min(127, shared));
+      scale_code = (uint32_t)(shared + 127);
+    }
+    const float f = amax != 0.f ? ldexpf(1.0f, -shared) : 0.f;
+    const uint32_t a = e3m2x2_codes(o[j].x * f, o[j].y * f), b = e3m2x2_codes(o[j].z * f, o[j].w * f);
+    const uint32_t c24 = (a & 63u) | (((a >> 8) & 63u) << 6) | ((b & 63u) << 12) | (((b >> 8) & 63u) << 18);
+    const uint32_t c1 = __shfl_down_sync(0xffffffffu, c24, 1);
+    const uint32_t c2 = __shfl_down_sync(0xffffffffu, c24, 2);
+    const uint32_t c3 = __shfl_down_sync(0xffffffffu, c24, 3);
+    if (live && (lane & 3) == 0)
+      *reinterpret_cast<uint4 *>(operand_row + (size_t)(i / 4) * 16) =
+          make_uint4(c24 | (c1 << 24), (c1 >> 8) | (c2 << 16), (c2 >> 16) | (c3 << 8), 0u);
+    if (live && (lane & 7) == 0) atoms[a_atom_offset(row, i / 8, katoms)] = (uint8_t)scale_code;
+  }
+}
+
 }  // namespace rowops
 }  // namespace ce

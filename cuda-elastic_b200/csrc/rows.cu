@@ -82,7 +82,65 @@ struct IterationWork {
   int gemv_rows;
   float eps;
   int norm_lo, norm_hi;  // the fp32 normalized output covers rmsnorm rows [norm_lo, norm_hi)
+  // block-scaled GEMM operands from the normalized rows (RowsExtras)
+  uint8_t *mx_operand;   // MXFP6 packed operand [rms_rows][mx_ld bytes], or nullptr
+  int mx_ld;
+  uint8_t *mx_atoms;     // its UE8M0 scale atoms
+  int katoms;
+  unsigned int *amax_bits;  // max |normalized| over the launch (NVFP4 pass 1), or nullptr
+  int keep_normalized;      // fp32 normalized with L2-resident stores (read again next)
 };
+
+// The rmsnorm row's extra outputs, from its normalized values in registers.
+template <int NV>
+__device__ __forceinline__ void rms_extras(const IterationWork &w, const float4 (&o)[NV], int row, int cols4,
+                                           float *scratch) {
+  if (w.mx_operand != nullptr)
+    mxfp6_row<NV>(o, w.mx_operand + (size_t)row * w.mx_ld, w.mx_atoms, row, w.katoms, cols4);
+  if (w.amax_bits != nullptr) {
+    float m = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * blockDim.x;
+      if (i < cols4) m = fmaxf(m, fmaxf(fmaxf(fabsf(o[j].x), fabsf(o[j].y)), fmaxf(fabsf(o[j].z), fabsf(o[j].w))));
+    }
+    m = block_max(m, scratch);
+    if (threadIdx.x == 0) atomicMax(w.amax_bits, __float_as_uint(m));  // m >= 0: bits order as values
+  }
+}
+
+// rmsnorm_row (row_ops.cuh) with the normalized values kept in registers for
+// rms_extras; the same arithmetic, so the same bits.
+template <int NV>
+__device__ __forceinline__ void rmsnorm_row_extras(const IterationWork &w, int row, float *scratch) {
+  const int cols4 = w.cols >> 2;
+  float4 v[NV];
+  load_row<NV>(v, reinterpret_cast<const float4 *>(w.input) + (size_t)row * cols4, cols4);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+  ss = block_sum(ss, scratch);
+  const float scale = 1.0f / sqrtf(ss / (float)w.cols + w.eps);
+  float4 *out = (w.normalized != nullptr && row >= w.norm_lo && row < w.norm_hi)
+                    ? reinterpret_cast<float4 *>(w.normalized) + (size_t)row * cols4 : nullptr;
+  const float4 *wt = reinterpret_cast<const float4 *>(w.weight);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    if (i < cols4) {
+      const float4 g = __ldg(wt + i);
+      v[j].x = g.x * (scale * v[j].x);
+      v[j].y = g.y * (scale * v[j].y);
+      v[j].z = g.z * (scale * v[j].z);
+      v[j].w = g.w * (scale * v[j].w);
+      if (out != nullptr) {
+        if (w.keep_normalized) out[i] = v[j];
+        else __stcs(out + i, v[j]);
+      }
+    }
+  }
+  rms_extras<NV>(w, v, row, cols4, scratch);
+}
 
 template <int NV>
 __global__ void __launch_bounds__(kRowThreads, (NV <= 8 ? 2 : 1))
@@ -117,6 +175,8 @@ iteration_kernel(IterationWork w) {
                          normalized ? reinterpret_cast<float4 *>(normalized) + off : nullptr,
                          w.normalized_e4m3 + (size_t)rms_row * w.ld_e4m3_4, w.e4m3_scale + rms_row,
                          cols4, w.cols, w.eps, scratch);
+  } else if (rms_row >= 0 && (w.mx_operand != nullptr || w.amax_bits != nullptr)) {
+    rmsnorm_row_extras<NV>(w, rms_row, scratch);
   } else if (rms_row >= 0) {
     const size_t off = (size_t)rms_row * cols4;
     rmsnorm_row<NV>(reinterpret_cast<const float4 *>(w.input) + off,
@@ -128,6 +188,178 @@ iteration_kernel(IterationWork w) {
     const size_t off = (size_t)soft_row * cols4;
     softmax_row<NV>(reinterpret_cast<const float4 *>(w.logits) + off,
                     reinterpret_cast<float4 *>(w.softmax) + off, cols4, scratch);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Streaming rows kernel for long rows (the trio's rows stage at the sheet
+// shape: 64 KiB per row). A persistent grid, one 512-thread CTA per SM, walks
+// the launch's row list (rmsnorm and softmax rows interleaved as in
+// iteration_kernel) with a stride of the grid. Rows arrive in a ring of
+// kRingRows shared-memory buffers filled by bulk copies issued two rows
+// ahead, so each SM always has loads in flight while it reduces the current
+// row from registers and streams its results out. Each thread owns the same
+// float4 slots as in iteration_kernel and does the same arithmetic in the
+// same order, so the results are the same bits. The RMSNorm weight stays in
+// registers for the whole launch.
+constexpr int kRingRows = 3;
+static __device__ DeviceStatus g_rows_status;
+
+__device__ __forceinline__ void bulk_row(void *smem_dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  mbar_arrive_expect_tx(bar, bytes);
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(smem_dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kRowThreads, 1)
+rows_stream_kernel(IterationWork w) {
+  extern __shared__ __align__(128) uint8_t ring_raw[];
+  __shared__ float scratch[32];
+  __shared__ uint64_t full[kRingRows];
+  const int cols4 = w.cols >> 2;
+  const uint32_t row_bytes = (uint32_t)w.cols * 4u;
+  const int both = min(w.rms_rows, w.softmax_rows);
+  const int items = w.rms_rows + w.softmax_rows;
+  // item k of the row list -> (is rmsnorm, row)
+  auto item_of = [&](int k, int *row) -> bool {
+    if (k < 2 * both) {
+      *row = k >> 1;
+      return (k & 1) == 0;
+    }
+    k -= 2 * both;
+    if (k < w.rms_rows - both) {
+      *row = both + k;
+      return true;
+    }
+    *row = both + (k - (w.rms_rows - both));
+    return false;
+  };
+  auto src_of = [&](int k) -> const float4 * {
+    int row = 0;
+    const bool rms = item_of(k, &row);
+    return reinterpret_cast<const float4 *>(rms ? w.input : w.logits) + (size_t)row * cols4;
+  };
+  float4 *ring = reinterpret_cast<float4 *>(ring_raw);
+  if (threadIdx.x == 0) {
+    for (int b = 0; b < kRingRows; ++b) mbar_init(&full[b], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const int first = blockIdx.x, step = gridDim.x;
+  if (threadIdx.x == 0)
+    for (int j = 0; j < kRingRows - 1; ++j) {
+      const int k = first + j * step;
+      if (k < items) bulk_row(ring + (size_t)j * cols4, src_of(k), row_bytes, &full[j]);
+    }
+  // the RMSNorm weight of this thread's slots, for every rmsnorm row
+  float4 g[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int i = threadIdx.x + j * blockDim.x;
+    g[j] = (i < cols4 && w.rms_rows > 0) ? __ldg(reinterpret_cast<const float4 *>(w.weight) + i)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  int n = 0;
+  for (int k = first; k < items; k += step, ++n) {
+    const int buf = n % kRingRows;
+    // the buffer of two rows ahead was read by every thread before the last
+    // row's block reductions, so it is free
+    if (threadIdx.x == 0) {
+      const int ahead = k + (kRingRows - 1) * step;
+      if (ahead < items)
+        bulk_row(ring + (size_t)((n + kRingRows - 1) % kRingRows) * cols4, src_of(ahead), row_bytes,
+                 &full[(n + kRingRows - 1) % kRingRows]);
+    }
+    const bool landed = mbar_wait(&full[buf], (uint32_t)((n / kRingRows) & 1), &g_rows_status, 1u);
+    if (!__syncthreads_and(landed)) break;  // a wait that gave up ends the CTA as a whole
+    const float4 *sv = ring + (size_t)buf * cols4;
+    float4 v[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int i = threadIdx.x + j * blockDim.x;
+      v[j] = i < cols4 ? sv[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    int row = 0;
+    if (item_of(k, &row)) {
+      // rmsnorm_row's arithmetic
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
+      ss = block_sum(ss, scratch);
+      const float scale = 1.0f / sqrtf(ss / (float)w.cols + w.eps);
+      float4 *out = (w.normalized != nullptr && row >= w.norm_lo && row < w.norm_hi)
+                        ? reinterpret_cast<float4 *>(w.normalized) + (size_t)row * cols4 : nullptr;
+      uint2 *ob = w.normalized_bf16 != nullptr ? w.normalized_bf16 + (size_t)row * w.ld_bf16_4 : nullptr;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols4) {
+          float4 o;
+          o.x = g[j].x * (scale * v[j].x);
+          o.y = g[j].y * (scale * v[j].y);
+          o.z = g[j].z * (scale * v[j].z);
+          o.w = g[j].w * (scale * v[j].w);
+          v[j] = o;
+          if (out != nullptr) {
+            if (w.keep_normalized) out[i] = o;
+            else __stcs(out + i, o);
+          }
+          if (ob != nullptr) {
+            __nv_bfloat162 lo = __floats2bfloat162_rn(o.x, o.y);
+            __nv_bfloat162 hi = __floats2bfloat162_rn(o.z, o.w);
+            uint2 packed;
+            packed.x = *reinterpret_cast<uint32_t *>(&lo);
+            packed.y = *reinterpret_cast<uint32_t *>(&hi);
+            ob[i] = packed;
+          }
+        }
+      }
+      if (w.mx_operand != nullptr || w.amax_bits != nullptr) rms_extras<NV>(w, v, row, cols4, scratch);
+    } else {
+      // softmax_row's arithmetic
+      float m = -FLT_MAX;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols4) m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
+      }
+      m = block_max(m, scratch);
+      float sum = 0.f;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols4) {
+          v[j].x = expf(v[j].x - m);
+          v[j].y = expf(v[j].y - m);
+          v[j].z = expf(v[j].z - m);
+          v[j].w = expf(v[j].w - m);
+          sum += (v[j].x + v[j].y) + (v[j].z + v[j].w);
+        }
+      }
+      sum = block_sum(sum, scratch);
+      float4 *out = reinterpret_cast<float4 *>(w.softmax) + (size_t)row * cols4;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < cols4) {
+          float4 o;
+          o.x = v[j].x / sum;
+          o.y = v[j].y / sum;
+          o.z = v[j].z / sum;
+          o.w = v[j].w / sum;
+          __stcs(out + i, o);
+        }
+      }
+    }
+  }
+  // every bulk copy this CTA issued has landed before it exits
+  for (int j = n; j < n + kRingRows; ++j) {
+    const int k = first + j * step;
+    if (k < items) mbar_wait(&full[j % kRingRows], (uint32_t)((j / kRingRows) & 1), &g_rows_status, 2u);
   }
 }
 
@@ -257,7 +489,45 @@ int pick_nv(int cols4, int *threads) {
   return 0;
 }
 
+// The streaming kernel for launches of long rmsnorm / softmax rows only
+// (32 to 64 KiB), with the thread count and slots iteration_kernel would use
+// (hence the same bits).
+int g_stream_rows = 1;  // ce_rows_tuning
+
+bool stream_rows_apply(const IterationWork &w, int nv, int threads) {
+  const int cols4 = w.cols >> 2;
+  return g_stream_rows && w.gemv_rows == 0 && w.normalized_e4m3 == nullptr && threads >= 256 && threads <= kRowThreads &&
+         nv <= 8 && cols4 >= 2048 && w.rms_rows + w.softmax_rows > 0;
+}
+
+template <int NV>
+int launch_stream_nv(const IterationWork &w, int threads, cudaStream_t s) {
+  const size_t smem = (size_t)kRingRows * w.cols * 4;
+  static bool configured[64] = {};
+  int dev = 0;
+  CE_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64 || !configured[dev]) {
+    CE_CUDA_TRY(cudaFuncSetAttribute(rows_stream_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)((size_t)kRingRows * 16384 * 4)));
+    if (dev >= 0 && dev < 64) configured[dev] = true;
+  }
+  const int items = w.rms_rows + w.softmax_rows;
+  const int grid = items < sm_count() ? items : sm_count();
+  rows_stream_kernel<NV><<<grid, threads, smem, s>>>(w);
+  CE_LAUNCH_CHECK("rows_stream_kernel");
+  return CE_OK;
+}
+
+int launch_stream(const IterationWork &w, int nv, int threads, cudaStream_t s) {
+  switch (nv) {
+    case 4: return launch_stream_nv<4>(w, threads, s);
+    case 8: return launch_stream_nv<8>(w, threads, s);
+  }
+  return set_error(CE_ERR_USAGE, std::string("internal: bad vector count for the streaming rows kernel"));
+}
+
 int launch_iteration(const IterationWork &w, int nv, int threads, cudaStream_t s) {
+  if (stream_rows_apply(w, nv, threads)) return launch_stream(w, nv, threads, s);
   const int both = w.rms_rows < w.softmax_rows ? w.rms_rows : w.softmax_rows;
   const int row_blocks = 2 * both + (w.rms_rows - both) + (w.softmax_rows - both);
   const int warps = threads / 32;
@@ -285,12 +555,17 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    const float *weight, float *softmax, const float *logits, float *product,
                    const float *matrix, const float *gemv_x, int batch_rms, int batch_softmax,
                    int cols, int gemv_rows, float eps, cudaStream_t s, uint8_t *normalized_e4m3,
-                   int ld_e4m3, float *e4m3_scale, int norm_lo, int norm_hi) {
+                   int ld_e4m3, float *e4m3_scale, int norm_lo, int norm_hi, const RowsExtras *extras) {
   CE_REQUIRE(cols >= 1, "cols must be >= 1 (got %d)", cols);
   CE_REQUIRE(batch_rms >= 0 && batch_softmax >= 0 && gemv_rows >= 0, "negative row count");
+  const bool ex_out = extras != nullptr && (extras->mx_operand != nullptr || extras->amax_bits != nullptr);
   if (batch_rms > 0)
-    CE_REQUIRE(input && weight && (normalized || normalized_bf16 || normalized_e4m3),
+    CE_REQUIRE(input && weight && (normalized || normalized_bf16 || normalized_e4m3 || ex_out),
                "rmsnorm needs input, weight and an output");
+  if (extras != nullptr && extras->mx_operand != nullptr)
+    CE_REQUIRE(extras->mx_atoms != nullptr && cols % 32 == 0 && extras->mx_ld >= cols && extras->mx_ld % 16 == 0 &&
+                   (reinterpret_cast<uintptr_t>(extras->mx_operand) & 15u) == 0,
+               "the fused MXFP6 operand needs its scale atoms, cols %% 32 == 0 and 16-byte rows");
   if (batch_softmax > 0) CE_REQUIRE(logits && softmax, "softmax needs logits and an output");
   if (gemv_rows > 0) CE_REQUIRE(matrix && gemv_x && product, "gemv needs matrix, x and product");
   if (normalized_bf16) CE_REQUIRE(ld_bf16 >= cols && ld_bf16 % 8 == 0, "bf16 leading dimension must be >= cols and a multiple of 8 (got %d)", ld_bf16);
@@ -306,6 +581,8 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                    aligned16(gemv_x) && aligned16(normalized_bf16) && aligned16(normalized_e4m3);
   if (normalized_e4m3 != nullptr && !vec)
     return set_error(CE_ERR_USAGE, std::string("the e4m3 operand needs 16-byte aligned rows"));
+  if (ex_out && !vec)
+    return set_error(CE_ERR_USAGE, std::string("the fused block-scaled operands need 16-byte aligned rows"));
   if (vec) {
     IterationWork w;
     w.normalized = normalized;
@@ -328,6 +605,14 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
     w.eps = eps;
     w.norm_lo = norm_lo;
     w.norm_hi = norm_hi;
+    const RowsExtras none;
+    const RowsExtras &ex = extras != nullptr ? *extras : none;
+    w.mx_operand = ex.mx_operand;
+    w.mx_ld = ex.mx_ld;
+    w.mx_atoms = ex.mx_atoms;
+    w.katoms = ex.katoms;
+    w.amax_bits = ex.amax_bits;
+    w.keep_normalized = ex.keep_normalized;
     // At least 256 threads per block whatever the launch contains, so the
     // reduction order of a row (and so its bits) does not depend on whether
     // GEMV blocks share the launch; the GEMV blocks use the same size.
@@ -362,6 +647,25 @@ int rows_iteration(float *normalized, uint16_t *normalized_bf16, int ld_bf16, co
                                         batch_rms, cols, ld_bf16);
     CE_LAUNCH_CHECK("pad_bf16_kernel");
   }
+  return CE_OK;
+}
+
+// Synchronizes the device, reads and clears the status word of the
+// streaming rows kernel (a bulk-copy wait that gave up).
+int rows_status() {
+  CE_CUDA_TRY(cudaDeviceSynchronize());
+  DeviceStatus h{};
+  CE_CUDA_TRY(cudaMemcpyFromSymbol(&h, g_rows_status, sizeof(h)));
+  if (h.code == 0) return CE_OK;
+  const DeviceStatus zero{};
+  CE_CUDA_TRY(cudaMemcpyToSymbol(g_rows_status, &zero, sizeof(zero)));
+  return set_error(CE_ERR_TIMEOUT, format("rows kernel bulk-copy wait %u gave up in block %u", h.where, h.block));
+}
+
+int rows_set_wait_limit(unsigned long long ns) { return set_wait_limit_here(ns); }
+
+int rows_set_streaming(int on) {
+  g_stream_rows = on != 0;
   return CE_OK;
 }
 

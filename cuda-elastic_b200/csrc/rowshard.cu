@@ -180,6 +180,10 @@ struct ce_rowx {
   unsigned long long *local = nullptr;  // [0] exchange counter, [1] arrival counter (int)
   uint8_t *peer[kRowxMaxRanks] = {};
   bool connected = false;
+  // ce_rowx_put: one stream per peer so the copies run on several copy
+  // engines at once, forked from and joined back to the caller's stream
+  cudaStream_t cs[kRowxMaxRanks] = {};
+  cudaEvent_t fork = nullptr, join[kRowxMaxRanks] = {};
 };
 
 namespace ce {
@@ -241,13 +245,17 @@ int ce_rowx_open(ce_rowx **out, int batch, int rows, int world, int rank, void *
   if (e == cudaSuccess) e = cudaMalloc(&x->local, 2 * sizeof(unsigned long long));
   if (e == cudaSuccess) e = cudaMemset(x->block, 0, x->block_bytes);
   if (e == cudaSuccess) e = cudaMemset(x->local, 0, 2 * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x->fork, cudaEventDisableTiming);
+  for (int q = 0; q < world && e == cudaSuccess; ++q) {
+    if (q == rank) continue;
+    e = cudaStreamCreateWithFlags(&x->cs[q], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&x->join[q], cudaEventDisableTiming);
+  }
   cudaIpcMemHandle_t h;
   if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, x->block);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
-    if (x->block) cudaFree(x->block);
-    if (x->local) cudaFree(x->local);
-    delete x;
+    ce_rowx_close(x);
     return cuda_error(e, "ce_rowx_open");
   }
   static_assert(sizeof(cudaIpcMemHandle_t) <= CE_IPC_HANDLE_BYTES, "IPC handle size");
@@ -300,20 +308,30 @@ int ce_rowx_put(ce_rowx *x, ce_stream_t stream) {
   rc = launch_kernel(rowx_ready_kernel, dim3(1), dim3(32), 0, s, false, "rowx_ready_kernel", rx);
   if (rc) return rc;
   // this rank's columns [lo, hi) of every row, to the same place in each
-  // peer's block: strided copies over NVLink by the copy engines
+  // peer's block: strided copies over NVLink, one per peer on its own
+  // stream so several copy engines work at once
   const size_t pitch = (size_t)rows * 4, off = (size_t)lo * 4;
+  CE_CUDA_TRY(cudaEventRecord(x->fork, s));
   for (int q = 0; q < x->world; ++q) {
     if (q == x->rank) continue;
+    CE_CUDA_TRY(cudaStreamWaitEvent(x->cs[q], x->fork, 0));
     CE_CUDA_TRY(cudaMemcpy2DAsync(x->peer[q] + off, pitch, x->block + off, pitch, (size_t)(hi - lo) * 4, batch,
-                                  cudaMemcpyDeviceToDevice, s));
+                                  cudaMemcpyDeviceToDevice, x->cs[q]));
+    CE_CUDA_TRY(cudaEventRecord(x->join[q], x->cs[q]));
+    CE_CUDA_TRY(cudaStreamWaitEvent(s, x->join[q], 0));
   }
   return launch_kernel(rowx_done_kernel, dim3(1), dim3(1), 0, s, false, "rowx_done_kernel", rx);
 }
 
 int ce_rowx_close(ce_rowx *x) {
   if (x == nullptr) return CE_OK;
-  for (int q = 0; q < x->world; ++q)
+  for (int q = 0; q < x->world; ++q) {
+    if (x->cs[q] != nullptr) cudaStreamSynchronize(x->cs[q]);
     if (q != x->rank && x->peer[q] != nullptr) cudaIpcCloseMemHandle(x->peer[q]);
+    if (x->cs[q] != nullptr) cudaStreamDestroy(x->cs[q]);
+    if (x->join[q] != nullptr) cudaEventDestroy(x->join[q]);
+  }
+  if (x->fork) cudaEventDestroy(x->fork);
   if (x->block) cudaFree(x->block);
   if (x->local) cudaFree(x->local);
   delete x;

@@ -253,6 +253,12 @@ int ce_gemm_tuning(int l2_prefetch_kblocks);
  * whose tiles then fit one wave (1, the default) or not (0). */
 int ce_gemm_wide_tiles(int on);
 
+/* Library-wide, set at setup time: launches of long rmsnorm / softmax rows
+ * (32 to 64 KiB, no GEMV rows) run the persistent streaming kernel (one CTA
+ * per SM, rows arriving by bulk copies two rows ahead; 1, the default) or
+ * one register-resident CTA per row (0). Both give the same bits. */
+int ce_rows_tuning(int streaming);
+
 /* Same contraction on fp32 operands with tcgen05 kind::tf32 (the tensor
  * core reads the upper 19 bits of each fp32 value). lda, ldb multiples of 4
  * elements, 16-byte aligned base pointers. */
@@ -520,8 +526,10 @@ int ce_allgather_rows(void *comm, float *out_dev, float *staging_dev, int batch,
  * output (ce_plan_gemm_ld into ce_rowx_output's buffer + lo, ldd = rows),
  * then ce_rowx_put enqueues a readiness handshake with the peers (bounded
  * wait), one strided cudaMemcpy2DAsync of the slice into each peer's output
- * over NVLink, and a kernel that signals the peers; ce_rowx_wait as above.
- * Enqueue-only. */
+ * over NVLink -- each on an internal stream of the exchange, forked from and
+ * joined back to `stream` by events, so several copy engines run at once --
+ * and a kernel that signals the peers; ce_rowx_wait as above. Enqueue-only;
+ * one host thread at a time per exchange. */
 typedef struct ce_rowx ce_rowx;
 int ce_rowx_open(ce_rowx **x, int batch, int rows, int world, int rank, void *handle_out);
 int ce_rowx_connect(ce_rowx *x, const void *handles);

@@ -121,3 +121,28 @@ def test_sheet_shape(ce, O, dev):
     assert np.all(np.abs(hn - en) <= 1e-5 * np.abs(en) + 1e-30)
     es = O.softmax_ref(p)
     assert np.all(np.abs(hs - es) <= 1e-5 * es + 1e-12)
+
+
+@pytest.mark.parametrize("batch,size", [(1024, 16384), (300, 8192), (7, 12288)])
+def test_streaming_rows_kernel_equals_register_kernel(ce, O, dev, batch, size):
+    """The trio's rows stage on long rows (32-64 KiB) runs the persistent
+    streaming kernel (bulk copies two rows ahead); the llama2c iteration with
+    its GEMV rows still runs the one-row-per-CTA register kernel. Both give
+    the same bits for the normalized and softmax rows, and the streaming
+    kernel's bf16 operand is the rounding of its fp32 output."""
+    x, w, logits, _ = O.trio_inputs(5, batch, size, 8)
+    dx, dw, dl = (torch.from_numpy(a).to(dev) for a in (x, w, logits))
+    mat = torch.zeros((8, size), device=dev)
+    n_reg, s_reg = torch.full_like(dx, float("nan")), torch.full_like(dl, float("nan"))
+    prod = torch.empty(8, device=dev)
+    ce.llama2c_iteration(n_reg, s_reg, prod, dx, dw, dl, mat)
+    plan = ce.Plan(batch, size, 8, ce.PREC_BF16)
+    n_str, s_str = torch.full_like(dx, float("nan")), torch.full_like(dl, float("nan"))
+    plan.rows(n_str, s_str, dx, dw, dl)
+    a = torch.empty((batch, size), device=dev)
+    plan.operands(a=a)
+    ce.device_status()
+    plan.close()
+    assert torch.equal(n_reg, n_str)
+    assert torch.equal(s_reg, s_str)
+    assert torch.equal(a, n_str.to(torch.bfloat16).float())
