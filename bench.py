@@ -509,9 +509,191 @@ def llama_prefill(ce, dev, stream, s, dist, world, peaks_tflops, which):
                                  "against the measured bf16 dense peak (sustained)"}}
 
 
+def trio_pipelined(ce, dev, host, plan, args):
+    """K trio steps with step i + 1's rows launch running beside step i's GEMM
+    (two plans and buffer sets, a rows stream and a GEMM stream); returns ms
+    per step over the K steps (first rows launch to last GEMM, CUDA events)
+    and the GEMM's own time while it shares the SMs."""
+    import torch
+    x, w, logits, W = host
+    dx, dw, dl = (torch.from_numpy(a).to(dev) for a in (x, w, logits))
+    plan2 = ce.Plan(BATCH, SIZE, ROWS, ce.PREC_BF16)
+    dW = torch.from_numpy(W).to(dev)
+    plan2.set_weights(dW)
+    del dW
+    plans = [plan, plan2]
+    bufs = [(torch.empty((BATCH, SIZE), device=dev), torch.empty((BATCH, SIZE), device=dev),
+             torch.empty((BATCH, ROWS), device=dev)) for _ in range(2)]
+    s_r, s_g = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    rows_done = [torch.cuda.Event() for _ in range(2)]
+    gemm_done = [torch.cuda.Event() for _ in range(2)]
+    ce.lib().ce_rows_tuning(0)
+    g_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+
+    def pstep(i, ev=None):
+        k = i % 2
+        n, so, o = bufs[k]
+        s_r.wait_event(gemm_done[k])
+        plans[k].rows(n, so, dx, dw, dl, stream=s_r.cuda_stream)
+        rows_done[k].record(s_r)
+        s_g.wait_event(rows_done[k])
+        if ev is not None:
+            ev[0].record(s_g)
+        plans[k].gemm(o, stream=s_g.cuda_stream)
+        if ev is not None:
+            ev[1].record(s_g)
+        gemm_done[k].record(s_g)
+
+    try:
+        for i in range(max(3, args.warmup)):
+            pstep(i)
+        torch.cuda.synchronize(dev)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(s_r)
+        for i in range(args.steps):
+            pstep(i, g_ev[i])
+        t1.record(s_g)
+        torch.cuda.synchronize(dev)
+        ce.device_status()
+        ms = t0.elapsed_time(t1) / args.steps
+        gemm_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in g_ev]))
+        # both buffer sets hold the same product
+        same = bool(torch.equal(bufs[0][2], bufs[1][2]))
+    finally:
+        ce.lib().ce_rows_tuning(1)
+        plan2.close()
+    if not same:
+        raise RuntimeError("pipelined trio steps disagree between buffer sets")
+    return {"ms_per_step": ms, "gemm_ms_beside_rows": gemm_ms,
+            "value": flops_per_step() / (ms * 1e-3) / 1e12}
+
+
 def sharded_share_rows(world, rank):
     base, extra = divmod(BATCH, world)
     return base + (1 if rank < extra else 0)
+
+
+def sharded_p2p_pipelined(ce, rs, dev, dist, world, rank, dx, dw, dl, dW, ref_plan, args, clocks_sampler, barrier,
+                          max_over_ranks, res, host):
+    """The row-sharded trio with the copy-engine join, steps pipelined: step
+    i + 1's rows launch runs beside step i's slice GEMM, and step i's
+    exchange (ce_rowx_put + ce_rowx_wait) on a copy stream beside both. Two
+    RowShardedPlans (operand, outputs and exchange block each) alternate; a
+    plan's rows launch waits for its previous GEMM, its GEMM for its
+    previous exchange. The timed region ends when every exchange has landed
+    on every rank. Also records the clocks, the end-to-end number (one plan,
+    serial, host buffers) and the parity check."""
+    import torch
+    # two exchanges each: the pipelined steps use slot 0 of each plan, the
+    # end-to-end run both slots of plan 0
+    shs = [rs.RowShardedPlan(ce, BATCH, SIZE, ROWS, ce.PREC_BF16, mode="p2p", exchanges=2) for _ in range(2)]
+    for sh in shs:
+        sh.set_weights(dW)
+    lo, hi = shs[0].lo, shs[0].hi
+    bufs = [(torch.empty((BATCH, SIZE), device=dev), torch.empty((BATCH, SIZE), device=dev)) for _ in range(2)]
+    s_r, s_g, s_c = (torch.cuda.Stream(device=dev) for _ in range(3))
+    rows_done, gemm_done, put_done = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+    ce.lib().ce_rows_tuning(0)  # the rows kernel that fits beside the GEMM's CTAs
+
+    def step(i, ev=None):
+        k = i % 2
+        sh, (n, so) = shs[k], bufs[k]
+        s_r.wait_event(gemm_done[k])
+        if ev is not None:
+            ev[0].record(s_r)
+        sh.rows_stage(n, so, dx, dw, dl, stream=s_r.cuda_stream)
+        if ev is not None:
+            ev[1].record(s_r)
+        rows_done[k].record(s_r)
+        s_g.wait_event(rows_done[k])
+        s_g.wait_event(put_done[k])
+        if ev is not None:
+            ev[2].record(s_g)
+        sh.local.gemm_ld(sh.outs[0][:, lo:], ROWS, stream=s_g.cuda_stream)
+        if ev is not None:
+            ev[3].record(s_g)
+        gemm_done[k].record(s_g)
+        s_c.wait_event(gemm_done[k])
+        if ev is not None:
+            ev[4].record(s_c)
+        sh.xs[0].put(stream=s_c.cuda_stream)
+        sh.xs[0].wait(stream=s_c.cuda_stream)
+        if ev is not None:
+            ev[5].record(s_c)
+        put_done[k].record(s_c)
+
+    try:
+        for i in range(max(3, args.warmup)):
+            step(i)
+        ce.device_status()
+        clocks_sampler.start()
+        time.sleep(0.3)
+        barrier()
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(s_r)
+        for i in range(args.steps):
+            step(i, ev[i])
+        s_c.wait_event(put_done[0])
+        s_c.wait_event(put_done[1])
+        t1.record(s_c)
+        barrier()
+        res["clocks"] = clocks_sampler.stop()
+        ce.device_status()
+        total = max_over_ranks(t0.elapsed_time(t1)) / args.steps
+        rows_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
+        gemm_ms = float(np.mean([e[2].elapsed_time(e[3]) for e in ev]))
+        join_ms = float(np.mean([e[4].elapsed_time(e[5]) for e in ev]))
+        # the slice GEMM alone
+        alone = torch.empty((BATCH, hi - lo), device=dev)
+        for _ in range(3):
+            shs[0].local.gemm(alone, stream=s_g.cuda_stream)
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record(s_g)
+        for _ in range(10):
+            shs[0].local.gemm(alone, stream=s_g.cuda_stream)
+        a1.record(s_g)
+        torch.cuda.synchronize(dev)
+        alone_ms = a0.elapsed_time(a1) / 10
+        # parity: a step's gathered product and rows share against the 1-GPU plan
+        ref_out = torch.empty((BATCH, ROWS), device=dev)
+        ref_norm = torch.empty((BATCH, SIZE), device=dev)
+        ref_soft = torch.empty((BATCH, SIZE), device=dev)
+        n0, so0 = bufs[0]
+        n0.fill_(float("nan"))
+        so0.fill_(float("nan"))
+        step(0)
+        torch.cuda.synchronize(dev)
+        ref_plan.trio(ref_norm, ref_soft, ref_out, dx, dw, dl)
+        torch.cuda.synchronize(dev)
+        got = shs[0].outs[0]
+        b_lo, b_hi = shs[0].b_lo, shs[0].b_hi
+        out_equal = bool(torch.equal(got, ref_out))
+        max_rel = float(((got - ref_out).abs().max() / ref_out.abs().max().clamp_min(1e-30)).item())
+        share_equal = bool(torch.equal(n0[b_lo:b_hi], ref_norm[b_lo:b_hi]) and
+                           torch.equal(so0[b_lo:b_hi], ref_soft[b_lo:b_hi]))
+        ok = torch.tensor([1.0 if (out_equal and share_equal) else 0.0], device=dev)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+        out = {"ms_per_step": total, "rows_ms": rows_ms, "slice_gemm_ms": gemm_ms,
+               "copy_engine_put_wait_ms": join_ms, "slice_gemm_alone_ms": alone_ms,
+               "exchange_share": join_ms / total,
+               "pipelining": "step i + 1's rows launch beside step i's slice GEMM, step i's exchange on a copy "
+                             "stream beside both (two plans, outputs and exchange blocks)",
+               "parity": {"ranks_bitwise_equal_to_1gpu_plan": bool(ok.item() == 1.0),
+                          "this_rank_out_equal": out_equal, "this_rank_rows_share_equal": share_equal,
+                          "max_rel_diff": max_rel, "checked": "all 1024 x 8192 outputs and this rank's "
+                                                              "rows share, every rank"}}
+        if not ok.item() == 1.0:
+            raise RuntimeError(f"row-sharded trio (p2p) differs from the single-GPU plan: {out}")
+        res["slice"] = (lo, hi)
+        ce.lib().ce_rows_tuning(1)
+        res["e2e"] = sharded_e2e(ce, dev, s_g, dist, world, shs[0], host, dx, dw, dl, args)
+    finally:
+        ce.lib().ce_rows_tuning(1)
+        torch.cuda.synchronize(dev)
+        for sh in shs:
+            sh.close()
+    return out
 
 
 def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, peak_tflops, clocks_sampler):
@@ -519,12 +701,11 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
     scaling: the same 1024 x 16384 batch and 8192 x 16384 matrix whatever
     the rank count). Rank r holds W's rows [lo, hi); every rank normalizes
     the whole batch (its slice GEMM needs every row) but writes only its
-    share of the fp32 normalized and softmax rows; the slice GEMM's epilogue
-    stores its tiles into every rank's output over NVLink (the fused
-    peer-memory join) and a bounded wait collects the peers' slices. The
-    NCCL join (ncclAllGather through the C ABI + the join kernel) is timed
-    beside it. Each rank's gathered product and its rows share are checked
-    bit for bit against the single-GPU plan on its own GPU."""
+    share of the fp32 normalized and softmax rows. Three joins are timed:
+    the copy-engine peer puts, steps pipelined (sharded_p2p_pipelined), the
+    peer stores fused into the GEMM epilogue, and ncclAllGather through the
+    C ABI + the join kernel. Each rank's gathered product and its rows share
+    are checked bit for bit against the single-GPU plan on its own GPU."""
     import torch
     import importlib
     rs = importlib.import_module("cuda_elastic_b200.rowshard")
@@ -545,40 +726,21 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
         return float(t.item())
 
     res = {}
-    # p2p: the copy-engine exchange of step i runs on its own stream while
-    # step i + 1 computes (two exchange slots; a slot's next GEMM waits for
-    # its previous exchange); the timed region ends when every exchange has
-    # landed on every rank
-    cstream = torch.cuda.Stream(device=dev)
-    gemm_done = [torch.cuda.Event() for _ in range(2)]
-    put_done = [torch.cuda.Event() for _ in range(2)]
     for mode in ("p2p", "fused", "nccl"):
+        if mode == "p2p":
+            res["p2p"] = sharded_p2p_pipelined(ce, rs, dev, dist, world, rank, dx, dw, dl, dW, ref_plan, args,
+                                               clocks_sampler, barrier, max_over_ranks, res, host)
+            continue
         sh = rs.RowShardedPlan(ce, BATCH, SIZE, ROWS, ce.PREC_BF16, mode=mode, exchanges=2)
         sh.set_weights(dW)
         lo, hi = sh.lo, sh.hi
         width = (ROWS + world - 1) // world
 
         def step(i, ev=None):
-            k = i % 2
-            if mode == "p2p":
-                stream.wait_event(put_done[k])
             sh.rows_stage(norm, soft, dx, dw, dl, stream=s)
             if ev is not None:
                 ev[0].record(stream)
-            if mode == "p2p":
-                sh.local.gemm_ld(sh.outs[k][:, lo:], ROWS, stream=s)
-                if ev is not None:
-                    ev[1].record(stream)
-                gemm_done[k].record(stream)
-                cstream.wait_event(gemm_done[k])
-                if ev is not None:
-                    ev[4].record(cstream)
-                sh.xs[k].put(stream=cstream.cuda_stream)
-                sh.xs[k].wait(stream=cstream.cuda_stream)
-                if ev is not None:
-                    ev[5].record(cstream)
-                put_done[k].record(cstream)
-            elif mode == "fused":
+            if mode == "fused":
                 sh.local.gemm_rowx(sh.xs[i % 2], stream=s)
                 if ev is not None:
                     ev[1].record(stream)
@@ -594,10 +756,6 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
                 step(i)
         ce.device_status()
         barrier()
-        if mode == "p2p":
-            clocks_sampler.start()
-            time.sleep(0.3)
-            barrier()
         ev = [[torch.cuda.Event(enable_timing=True) for _ in range(6)] for _ in range(args.steps)]
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
@@ -606,19 +764,13 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
                 ev[i][2].record(stream)
                 step(i, ev[i])
                 ev[i][3].record(stream)
-            if mode == "p2p":  # every exchange has landed
-                stream.wait_event(put_done[0])
-                stream.wait_event(put_done[1])
             t1.record(stream)
         barrier()
-        if mode == "p2p":
-            res["clocks"] = clocks_sampler.stop()
         ce.device_status()
         total = max_over_ranks(t0.elapsed_time(t1)) / args.steps
         rows_ms = float(np.mean([e[2].elapsed_time(e[0]) for e in ev]))
         gemm_ms = float(np.mean([e[0].elapsed_time(e[1]) for e in ev]))
-        join_ms = float(np.mean([(e[4].elapsed_time(e[5]) if mode == "p2p" else e[1].elapsed_time(e[3]))
-                                 for e in ev]))
+        join_ms = float(np.mean([e[1].elapsed_time(e[3]) for e in ev]))
         # the slice GEMM alone (no exchange) for the exchange's share
         alone = torch.empty((BATCH, hi - lo), device=dev)
         with torch.cuda.stream(stream):
@@ -640,8 +792,6 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
             norm.fill_(float("nan"))
             soft.fill_(float("nan"))
             step(0)
-            if mode == "p2p":
-                stream.wait_event(put_done[0])
             ref_plan.trio(ref_norm, ref_soft, ref_out, dx, dw, dl, stream=s)
         torch.cuda.synchronize(dev)
         got = sh.outs[0]
@@ -654,8 +804,7 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
         dist.all_reduce(ok, op=dist.ReduceOp.MIN)
         res[mode] = {"ms_per_step": total, "rows_ms": rows_ms,
                      ("gemm_with_fused_exchange_ms" if mode == "fused" else "slice_gemm_ms"): gemm_ms,
-                     {"fused": "exchange_wait_ms", "p2p": "copy_engine_put_wait_ms",
-                      "nccl": "allgather_join_ms"}[mode]: join_ms,
+                     ("exchange_wait_ms" if mode == "fused" else "allgather_join_ms"): join_ms,
                      "slice_gemm_alone_ms": alone_ms,
                      "exchange_share": (gemm_ms + join_ms - alone_ms) / total if mode == "fused"
                      else join_ms / total,
@@ -665,9 +814,6 @@ def trio_sharded(ce, dev, stream, dist, world, rank, host, dW, ref_plan, args, p
                                                                     "rows share, every rank"}}
         if not ok.item() == 1.0:
             raise RuntimeError(f"row-sharded trio ({mode}) differs from the single-GPU plan: {res[mode]}")
-        if mode == "p2p":
-            res["slice"] = (lo, hi)
-            res["e2e"] = sharded_e2e(ce, dev, stream, dist, world, sh, host, dx, dw, dl, args)
         sh.close()
     return res
 
@@ -832,6 +978,19 @@ def run_ours(args, rank, world, local_rank):
     total_ms = float(t.item())
     ms_per_step = total_ms / args.steps
     value = world * flops_per_step() / (ms_per_step * 1e-3) / 1e12
+    serial = {"ms_per_step": ms_per_step, "value": value, "rows_ms": rows_ms, "gemm_ms": gemm_ms}
+
+    # ---- pipelined steps (1 GPU headline): step i + 1's rows launch beside
+    # step i's GEMM on a second stream. Consecutive steps are independent
+    # batches; two plans (two operand and output buffer sets) keep them apart,
+    # and a plan's rows launch waits until its previous GEMM has read the
+    # operand. The one-CTA-per-row rows kernel (no shared memory) fits beside
+    # the GEMM's CTA on every SM. ----
+    pipe = None
+    if world == 1 and prec == ce.PREC_BF16 and not args.profile:
+        pipe = trio_pipelined(ce, dev, (x, w, logits, W), plan, args)
+        ms_per_step = pipe["ms_per_step"]
+        value = flops_per_step() / (ms_per_step * 1e-3) / 1e12
 
     # ---- row-sharded trio over the ranks (N > 1 headline) ----
     sharded = None
@@ -1086,7 +1245,9 @@ def run_ours(args, rank, world, local_rank):
         rows_roof = {"bound": "hbm", "achieved": (4.0 * BATCH * SIZE * 4 + BATCH * SIZE * 2 + SIZE * 4)
                      / (rows_ms * 1e-3) / 1e9, "peak": pk.get("hbm_gbs", 6650.0), "unit": "GB/s"}
         head = {"value": value, "ms_per_step": ms_per_step, "scaling": "weak",
-                "parallelism": "single GPU", "gpu_launches": 2 * args.steps,
+                "parallelism": "single GPU" + ("; steps pipelined: step i + 1's rows launch beside step i's GEMM "
+                                               "(two plans and buffer sets, two streams)" if pipe else ""),
+                "gpu_launches": 2 * args.steps,
                 "kernels_ms": {"rows": rows_ms, "gemm": gemm_ms}}
 
     if dist is not None:
@@ -1125,6 +1286,10 @@ def run_ours(args, rank, world, local_rank):
             line["row_sharded"] = {"headline_join": head_mode, "p2p": sharded["p2p"], "fused": sharded["fused"],
                                    "nccl": sharded["nccl"], "slice_rows": hi - lo}
             line["replicas"] = replicas
+        else:
+            line["serial_steps"] = serial
+            if pipe is not None:
+                line["pipelined_steps"] = pipe
         line["rows_roofline"]["frac"] = line["rows_roofline"]["achieved"] / line["rows_roofline"]["peak"]
         if cpu is not None:
             line["cpu_baseline"] = cpu
