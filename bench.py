@@ -63,6 +63,9 @@ def parse():
     ap.add_argument("--profile-llama", choices=["110m", "7b"],
                     help="decoder steps for ncu only (no JSON line): setup, one warm step, then --steps "
                          "direct steps between cudaProfilerStart/Stop (use ncu --profile-from-start off)")
+    ap.add_argument("--profile-trio", choices=["bf16", "fp8", "mxfp6", "nvfp4", "all"],
+                    help="trio steps for ncu only (no JSON line): per precision, setup, one warm step, then "
+                         "--steps steps at 1024x16384x8192")
     ap.add_argument("--llama-layers", type=int, default=0,
                     help="with --profile-llama: layers of the model (0 = the configuration's own)")
     return ap.parse_args()
@@ -346,6 +349,41 @@ def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=10
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
     del g  # the graph holds NCCL calls: released before the process group
+    segments = None
+    if sh is not None and exchange == "p2p":
+        # where a sharded step's time goes: one direct step with CUDA events
+        # around each segment (a consumer segment includes its bounded wait for
+        # the peers' exchange), summed per segment kind, max over ranks
+        names = {ce.SEG_ATTN: "attn", ce.SEG_OPROJ: "oproj", ce.SEG_FFN_IN: "ffn_in",
+                 ce.SEG_FFN_OUT: "ffn_out", ce.SEG_HEAD: "head", ce.SEG_PICK: "pick"}
+        with torch.cuda.stream(stream):
+            m.start(start_tokens, kv_fill)
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        evs = []
+        with torch.cuda.stream(stream):
+            def timed(seg, layer=0):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                m.segment(seg, layer)
+                b.record(stream)
+                evs.append((names[seg], a, b))
+            for layer in range(cfg["n_layers"]):
+                for seg in (ce.SEG_ATTN, ce.SEG_OPROJ, ce.SEG_FFN_IN, ce.SEG_FFN_OUT):
+                    timed(seg, layer)
+            timed(ce.SEG_HEAD)
+            timed(ce.SEG_PICK)
+        torch.cuda.synchronize(dev)
+        ce.llama_status()
+        tot = {}
+        for name, a, b in evs:
+            tot[name] = tot.get(name, 0.0) + a.elapsed_time(b)
+        keys = sorted(tot)
+        t = torch.tensor([tot[k] for k in keys], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        segments = {k: float(v) for k, v in zip(keys, t.tolist())}
+        segments["note"] = ("ms per direct step (no graph, no launch overlap), each segment's kernels including "
+                            "the peers' exchange waits inside them; max over ranks")
     if sh is not None:
         sh.close()
     else:
@@ -365,7 +403,7 @@ def llama7b_decode(ce, dev, stream, dist, world, hbm_gbs, per_gpu=64, kv_fill=10
             "n_gpus": world, "batch": batch, "setup_s": setup_s,
             "parallelism": (f"row-sharded tp{world} ({'peer-memory puts over NVLink' if exchange == 'p2p' else 'NCCL all-gathers'}, "
                             f"4 per layer + 1)") if world > 1 else "single GPU",
-            "scaling": "weak",
+            "scaling": "weak", "segment_ms_per_step": segments,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_gbs, "unit": "GB/s",
                          "frac": achieved / hbm_gbs,
                          "bytes_per_step": (kv_bytes + w_bytes) / tokens,
@@ -1332,6 +1370,34 @@ def profile_llama(args):
           f"{args.steps} steps done", flush=True)
 
 
+def profile_trio(args):
+    """--profile-trio: one GPU, the op trio (rows launch, activation
+    quantizer where the format has one, GEMM) at 1024 x 16384 x 8192 in the
+    named precision(s): setup, one warm step, then --steps steps."""
+    import torch
+    import __graft_entry__
+    ce = __graft_entry__.load_package()
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    names = {"bf16": ce.PREC_BF16, "fp8": ce.PREC_FP8_E4M3, "mxfp6": ce.PREC_MXFP6_E3M2,
+             "nvfp4": ce.PREC_NVFP4_E2M1}
+    chosen = list(names) if args.profile_trio == "all" else [args.profile_trio]
+    x, w, logits, W = ce.trio_inputs_host(0, BATCH, SIZE, ROWS)
+    dx, dw, dl, dW = (torch.from_numpy(a).to(dev) for a in (x, w, logits, W))
+    norm, soft, out = torch.empty_like(dx), torch.empty_like(dl), torch.empty(BATCH, ROWS, device=dev)
+    for name in chosen:
+        plan = ce.Plan(BATCH, SIZE, ROWS, names[name])
+        plan.set_weights(dW)
+        plan.trio(norm, soft, out, dx, dw, dl)
+        torch.cuda.synchronize()
+        for _ in range(args.steps):
+            plan.trio(norm, soft, out, dx, dw, dl)
+        torch.cuda.synchronize()
+        plan.close()
+    ce.device_status()
+    print(f"profile-trio {args.profile_trio}: {args.steps} steps done", flush=True)
+
+
 def profile_prefill(args):
     """--profile-prefill: one GPU, one prompt prefill (512 tokens, chunks of
     128 positions) of the 110M (bf16, batch 256) or 7B (NVFP4, batch 64)
@@ -1375,6 +1441,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.profile_prefill:
         profile_prefill(args)
+        return
+    if args.profile_trio:
+        profile_trio(args)
         return
     if args.profile_llama:
         profile_llama(args)
