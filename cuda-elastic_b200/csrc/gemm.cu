@@ -1390,6 +1390,54 @@ __device__ __forceinline__ W4tUnit w4t_unit(const W4tArgs &a, int u) {
   return w;
 }
 
+// Epilogue of one unit for the calling warp (TMEM lane quarter `quarter`):
+// the (128-row half, 16 batch columns) chunks ci with ci % nworkers ==
+// worker. The chunk accumulators are summed in order, times alpha; then the
+// SwiGLU product (fp16) or the fp32 outputs / split-K partials.
+template <int TR>
+__device__ __forceinline__ void w4t_store_chunks(const W4tArgs &args, const W4tUnit &w, uint32_t tmem_base,
+                                                 int quarter, int lane, float alpha, int worker, int nworkers) {
+  constexpr int kHalves = TR / 128;
+  const int NB = args.nb, per_half = args.issuers == 4 ? 2 : 1;  // accumulators per half (k chunks)
+  const int b0 = w.tile_b * NB, chunks = NB / 16;
+  const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
+  for (int ci = worker; ci < kHalves * chunks; ci += nworkers) {
+    const int h = ci / chunks, c0 = (ci % chunks) * 16;
+    const int n = w.tile_n * TR + h * 128 + quarter * 32 + lane;
+    uint32_t r[16], r2[16];
+    float v[16];
+    tmem_ld_32x32b_x16(lane_base + (uint32_t)(h * per_half * NB + c0), r);
+    if (per_half == 2)  // the second k chunk's accumulator, added in order
+      tmem_ld_32x32b_x16(lane_base + (uint32_t)((h * 2 + 1) * NB + c0), r2);
+    tmem_ld_wait();
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
+    if (per_half == 2) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(r2[j]);
+    }
+    if (args.swiglu_out != nullptr) {
+      // rows (2i, 2i+1) = (g_i, u_i) sit in adjacent lanes
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float x = v[j] * alpha;
+        const float u = __shfl_xor_sync(0xffffffffu, x, 1);
+        const int b = b0 + c0 + j;
+        if ((lane & 1) == 0 && n < args.N && b < args.M) {
+          const __half hv = __float2half_rn(x / (1.0f + expf(-x)) * u);
+          args.swiglu_out[(size_t)b * args.ld_out + n / 2] = *reinterpret_cast<const uint16_t *>(&hv);
+        }
+      }
+    } else if (n < args.N) {
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int b = b0 + c0 + j;
+        if (b < args.M) w.d[(size_t)b * args.ldd + n] = v[j] * alpha;
+      }
+    }
+  }
+}
+
 template <int TR>
 __global__ void __launch_bounds__(kW4tThreads, 1)
 gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
@@ -1410,7 +1458,8 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
   uint64_t *afull = wempty + kW4tMaxWStages, *tready = afull + kW4tMaxStages;
   uint64_t *sempty = tready + kW4tMaxStages;
   uint64_t *accfull = sempty + kW4tMaxStages, *accempty = accfull + 1, *drain = accempty + 1;
-  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *acc_last = drain + 1;  // the CTA's last unit accumulated (one phase per launch)
+  uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(acc_last + 1);
 
   DeviceStatus *st = &g_gemm_status;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1430,6 +1479,7 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
     mbar_init(accfull, args.issuers);
     mbar_init(accempty, 4);
     mbar_init(drain, args.issuers);
+    mbar_init(acc_last, args.issuers);
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
   }
@@ -1575,6 +1625,20 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
         }
       }
     }
+    // The stores of the last unit's outputs (four epilogue warps alone wrote
+    // ~25 GB/s per SM): this warp takes every fifth chunk of its lane quarter.
+    const int n_local = blockIdx.x < num_units ? (num_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    if (okay && n_local > 0) {
+      pdl_wait();  // outputs may be buffers the previous kernel reads
+      if (warp_wait(acc_last, 0, st, 75)) {
+        tc_fence_after();
+        const float alpha = args.alpha != nullptr ? *args.alpha : 1.0f;
+        const int t_last = blockIdx.x + (n_local - 1) * gridDim.x;
+        w4t_store_chunks<TR>(args, w4t_unit(args, t_last), tmem_base, quarter, lane, alpha, 1 + slot,
+                             1 + kW4tConvWarps / 4);
+        tc_fence_before();
+      }
+    }
   } else if (warp >= 1 && warp <= args.issuers) {
     // ---------------- MMA issuers (see the role list)
     const int i = warp - 1, nis = args.issuers;
@@ -1615,7 +1679,10 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
           ph ^= 1u;
         }
       }
-      if (okay && lane == 0) tc_commit(accfull);
+      if (okay && lane == 0) {
+        tc_commit(accfull);
+        if (t + (int)gridDim.x >= num_units) tc_commit(acc_last);
+      }
       __syncwarp();
     }
     if (lane == 0) tc_commit(drain);
@@ -1624,53 +1691,16 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
   } else if (warp >= kW4tFirstEpi && warp < kW4tFirstEpi + 4) {
     // ---------------- epilogue
     pdl_wait();
-    const int quarter = warp & 3, nis = args.issuers;
-    const int per_half = nis == 4 ? 2 : 1;  // accumulators per 128-row half (k chunks)
+    const int quarter = warp & 3;
     const float alpha = args.alpha != nullptr ? *args.alpha : 1.0f;
     int local = 0;
     for (int t = blockIdx.x; t < num_units; t += gridDim.x, ++local) {
       if (!warp_wait(accfull, (uint32_t)(local & 1), st, 71)) break;
       tc_fence_after();
-      const W4tUnit w = w4t_unit(args, t);
-      const int b0 = w.tile_b * NB;
-#pragma unroll
-      for (int h = 0; h < kHalves; ++h) {
-        const int n = w.tile_n * TR + h * 128 + quarter * 32 + lane;
-        for (int c0 = 0; c0 < NB; c0 += 16) {
-          const uint32_t lane_base = tmem_base + ((uint32_t)(quarter * 32) << 16);
-          uint32_t r[16], r2[16];
-          float v[16];
-          tmem_ld_32x32b_x16(lane_base + (uint32_t)(h * per_half * NB + c0), r);
-          if (per_half == 2)  // the second k chunk's accumulator, added in order
-            tmem_ld_32x32b_x16(lane_base + (uint32_t)((h * 2 + 1) * NB + c0), r2);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
-          if (per_half == 2) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] += __uint_as_float(r2[j]);
-          }
-          if (args.swiglu_out != nullptr) {
-            // rows (2i, 2i+1) = (g_i, u_i) sit in adjacent lanes
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const float x = v[j] * alpha;
-              const float u = __shfl_xor_sync(0xffffffffu, x, 1);
-              const int b = b0 + c0 + j;
-              if ((lane & 1) == 0 && n < args.N && b < args.M) {
-                const __half hv = __float2half_rn(x / (1.0f + expf(-x)) * u);
-                args.swiglu_out[(size_t)b * args.ld_out + n / 2] = *reinterpret_cast<const uint16_t *>(&hv);
-              }
-            }
-          } else if (n < args.N) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int b = b0 + c0 + j;
-              if (b < args.M) w.d[(size_t)b * args.ldd + n] = v[j] * alpha;
-            }
-          }
-        }
-      }
+      // the CTA's last unit is shared with the (then idle) converter warps
+      const bool last = t + (int)gridDim.x >= num_units;
+      w4t_store_chunks<TR>(args, w4t_unit(args, t), tmem_base, quarter, lane, alpha, 0,
+                           last ? 1 + kW4tConvWarps / 4 : 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty);

@@ -200,8 +200,12 @@ def test_w4_pack_layout(ce, O, dev):
         assert np.array_equal(st[kb], sc[:, kb * 4:(kb + 1) * 4])
 
 
+# N % 4 == 0 writes fp32 outputs through the staged bulk-copy epilogue (N =
+# 1001: direct stores); 40960 rows = 160 tiles, so some CTAs reuse the
+# staging block for a second tile.
 W4T_SHAPES = [(64, 4096, 1024, 1), (64, 4352, 4096, 4), (9, 2752, 4096, 3), (130, 452, 320, 1),
-              (1, 8, 64, 1), (300, 1000, 1024, 2), (512, 512, 4096, 8), (100, 1000, 1216, 2), (256, 768, 2048, 1)]
+              (1, 8, 64, 1), (300, 1000, 1024, 2), (512, 512, 4096, 8), (100, 1000, 1216, 2), (256, 768, 2048, 1),
+              (40, 1001, 512, 2), (64, 40960, 256, 1)]
 
 
 @pytest.mark.parametrize("shape", W4T_SHAPES)
