@@ -1353,6 +1353,9 @@ constexpr int kW4tFirstConv = 12;
 constexpr int kW4tFirstEpi = 8;
 constexpr int kW4tMaxStages = 4;   // activation slots = TMEM weight stages
 constexpr int kW4tMaxWStages = 8;  // packed weight stages in shared memory
+// Warps per TMEM lane quarter that store the CTA's last unit: the epilogue
+// warp, the four converter warps and two of warps 0-7 (done by then).
+constexpr int kW4tLastWorkers = 7;
 constexpr int kW4tSmemBudget = 232448 - 1024;
 
 struct W4tArgs {
@@ -1625,20 +1628,6 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
         }
       }
     }
-    // The stores of the last unit's outputs (four epilogue warps alone wrote
-    // ~25 GB/s per SM): this warp takes every fifth chunk of its lane quarter.
-    const int n_local = blockIdx.x < num_units ? (num_units - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-    if (okay && n_local > 0) {
-      pdl_wait();  // outputs may be buffers the previous kernel reads
-      if (warp_wait(acc_last, 0, st, 75)) {
-        tc_fence_after();
-        const float alpha = args.alpha != nullptr ? *args.alpha : 1.0f;
-        const int t_last = blockIdx.x + (n_local - 1) * gridDim.x;
-        w4t_store_chunks<TR>(args, w4t_unit(args, t_last), tmem_base, quarter, lane, alpha, 1 + slot,
-                             1 + kW4tConvWarps / 4);
-        tc_fence_before();
-      }
-    }
   } else if (warp >= 1 && warp <= args.issuers) {
     // ---------------- MMA issuers (see the role list)
     const int i = warp - 1, nis = args.issuers;
@@ -1700,10 +1689,27 @@ gemm_w4t_kernel(const __grid_constant__ CUtensorMap tmA, W4tArgs args) {
       // the CTA's last unit is shared with the (then idle) converter warps
       const bool last = t + (int)gridDim.x >= num_units;
       w4t_store_chunks<TR>(args, w4t_unit(args, t), tmem_base, quarter, lane, alpha, 0,
-                           last ? 1 + kW4tConvWarps / 4 : 1);
+                           last ? kW4tLastWorkers : 1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(accempty);
+    }
+  }
+
+  // The stores of the CTA's last unit (four epilogue warps alone wrote ~25
+  // GB/s per SM: the per-warp store rate bounds them): every warp whose role
+  // has ended takes a share of its lane quarter's chunks.
+  if (warp < kW4tFirstEpi || warp >= kW4tFirstConv) {
+    const int worker = warp >= kW4tFirstConv ? 1 + ((warp - kW4tFirstConv) >> 2) : 5 + (warp >> 2);
+    if (blockIdx.x < num_units) {
+      pdl_wait();  // outputs may be buffers the previous kernel reads
+      if (warp_wait(acc_last, 0, st, 75)) {
+        tc_fence_after();
+        const float alpha = args.alpha != nullptr ? *args.alpha : 1.0f;
+        const int t_last = blockIdx.x + (num_units - 1 - (int)blockIdx.x) / (int)gridDim.x * (int)gridDim.x;
+        w4t_store_chunks<TR>(args, w4t_unit(args, t_last), tmem_base, warp & 3, lane, alpha, worker,
+                             kW4tLastWorkers);
+      }
     }
   }
 
