@@ -178,16 +178,21 @@ __global__ void fill_f32_kernel(float *out, size_t n, float v) {
   for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += step) out[i] = v;
 }
 
-// One row of the residual stream per block: x = embedding[token] (first
-// layer), or x += delta (after a sublayer; delta is the sum of nsplit
-// split-K partials split_stride floats apart), then xb = bf16(w * (x * scale)),
-// scale = 1 / sqrtf(sum(x^2) / dim + eps). An out-of-range token makes the
-// row NaN so the failure shows in every output.
-template <int NV>
-__global__ void __launch_bounds__(kRowThreads)
+// One row of the residual stream per block of THREADS: x = embedding[token]
+// (first layer), or x += delta (after a sublayer; delta is the sum of nsplit
+// split-K partials split_stride floats apart), then xb = bf16(w * (x *
+// scale)), scale = 1 / sqrtf(sum(x^2) / dim + eps). An out-of-range token
+// makes the row NaN so the failure shows in every output. A decode step has
+// one block per sequence (64 for the 7B bench), so each thread issues all of
+// its split partials' loads before the first add (the sum stays in split
+// order): with one load in flight per thread the kernel waited on L2 latency
+// nsplit times over.
+template <int NV, int THREADS>
+__global__ void __launch_bounds__(THREADS)
 residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_stride,
                         const uint16_t *emb, const int *tokens, int vocab, const float *w,
                         uint16_t *xb, int dim, float eps, int f16, int shard_cols, ExchangeWait xw) {
+  constexpr int kMaxLoads = 8;  // split partials loaded together
   __shared__ float scratch[32];
   pdl_launch_dependents();
   pdl_wait();
@@ -204,7 +209,7 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
     const uint2 *er = reinterpret_cast<const uint2 *>(emb + (size_t)(ok ? tok : 0) * dim);
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int i = threadIdx.x + j * kRowThreads;
+      const int i = threadIdx.x + j * THREADS;
       if (i < cols4) {
         const uint2 e = er[i];
         v[j] = make_float4(__uint_as_float(e.x << 16), __uint_as_float(e.x & 0xFFFF0000u),
@@ -217,7 +222,7 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
     const float4 *dr = delta ? reinterpret_cast<const float4 *>(delta + (size_t)b * dim) : nullptr;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
-      const int i = threadIdx.x + j * kRowThreads;
+      const int i = threadIdx.x + j * THREADS;
       if (i < cols4) {
         v[j] = xr[i];
         if (dr) {
@@ -229,10 +234,17 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
                                                   (size_t)b * shard_cols + (col - sh * shard_cols));
           } else {
             // the sublayer's output: its split-K partials summed in split order
-            d = dr[i];
-            for (int sp = 1; sp < nsplit; ++sp) {
-              const float4 e = dr[i + sp * (split_stride / 4)];
-              d.x += e.x, d.y += e.y, d.z += e.z, d.w += e.w;
+            float4 e[kMaxLoads];
+#pragma unroll
+            for (int sp = 0; sp < kMaxLoads; ++sp)
+              if (sp < nsplit) e[sp] = dr[i + sp * (split_stride / 4)];
+            d = e[0];
+#pragma unroll
+            for (int sp = 1; sp < kMaxLoads; ++sp)
+              if (sp < nsplit) d.x += e[sp].x, d.y += e[sp].y, d.z += e[sp].z, d.w += e[sp].w;
+            for (int sp = kMaxLoads; sp < nsplit; ++sp) {
+              const float4 f = dr[i + sp * (split_stride / 4)];
+              d.x += f.x, d.y += f.y, d.z += f.z, d.w += f.w;
             }
           }
           v[j].x += d.x, v[j].y += d.y, v[j].z += d.z, v[j].w += d.w;
@@ -244,7 +256,7 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
   float ss = 0.f;
 #pragma unroll
   for (int j = 0; j < NV; ++j)
-    if (threadIdx.x + j * kRowThreads < cols4)
+    if (threadIdx.x + j * THREADS < cols4)
       ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
   ss = block_sum(ss, scratch);
   const float scale = 1.0f / sqrtf(ss / (float)dim + eps);
@@ -252,7 +264,7 @@ residual_rmsnorm_kernel(float *x, const float *delta, int nsplit, size_t split_s
   const float4 *wr = reinterpret_cast<const float4 *>(w);
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
-    const int i = threadIdx.x + j * kRowThreads;
+    const int i = threadIdx.x + j * THREADS;
     if (i < cols4) {
       const float4 g = wr[i];
       uint2 o;
@@ -1508,6 +1520,26 @@ int launch_rows(int nv, F &&f) {
   return CE_OK;
 }
 
+int pow2_at_least(int v);
+
+// Launches residual_rmsnorm_kernel with one block per row: 1024 threads for
+// rows of 4096 values or more, else 256; NV float4 per thread.
+template <typename... Args>
+int launch_norm(int dim, dim3 grid, cudaStream_t s, bool pdl, Args... args) {
+  const int cols4 = dim / 4, threads = cols4 >= 1024 ? 1024 : 256;
+  const int nv = pow2_at_least((cols4 + threads - 1) / threads);
+  int lrc = CE_OK;
+  const int rc = launch_rows(nv, [&](auto nvt) {
+    constexpr int NV = decltype(nvt)::value;
+    lrc = threads == 1024
+              ? launch_kernel(residual_rmsnorm_kernel<NV, 1024>, grid, dim3(1024), 0, s, pdl,
+                              "residual_rmsnorm_kernel", args...)
+              : launch_kernel(residual_rmsnorm_kernel<NV, 256>, grid, dim3(256), 0, s, pdl,
+                              "residual_rmsnorm_kernel", args...);
+  });
+  return rc ? rc : lrc;
+}
+
 // Grid of rope_append_kernel: blocks of 256 (sequence, pair) threads over the
 // dim / 2 q pairs and kv_dim / 2 k/v pairs of each of the batch rows.
 dim3 rope_grid(int dim, int kv_dim, int batch) {
@@ -2103,13 +2135,8 @@ int ce_llama_enqueue_step(ce_llama *m, ce_stream_t stream) {
     return gemm_bf16_split(d, a, w, B, N, K, K, K, ldd, splits, stride, s, pdl);
   };
   auto norm = [&](const float *delta, int nsplit, const uint16_t *emb, const float *w) {
-    int lrc = CE_OK;
-    const int rc = launch_rows(m->nv, [&](auto nv) {
-      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
-                          "residual_rmsnorm_kernel", m->x, delta, nsplit, delta_stride, emb,
-                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, 0, ExchangeWait{});
-    });
-    return rc ? rc : lrc;
+    return launch_norm(D, dim3(B), s, pdl, m->x, delta, nsplit, delta_stride, emb, (const int *)m->tokens,
+                       c.vocab_size, w, m->xb, D, eps, (int)w4, 0, ExchangeWait{});
   };
   const size_t attn_smem = attn_smem_bytes(m->hs);
   for (int l = 0; l < c.n_layers; ++l) {
@@ -2266,13 +2293,8 @@ int ce_llama_enqueue_prefill(ce_llama *m, const int32_t *prompt, int prompt_len,
   };
   auto norm = [&](int rows, float *x, const float *delta, size_t stride, const uint16_t *emb, const int *toks,
                   const float *w, uint16_t *out) {
-    int lrc = CE_OK;
-    const int rc = launch_rows(m->nv, [&](auto nv) {
-      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(rows), dim3(kRowThreads), 0, s, pdl,
-                          "residual_rmsnorm_kernel", x, delta, 1, stride, emb, toks, c.vocab_size, w, out, D, eps,
-                          (int)w4, 0, ExchangeWait{});
-    });
-    return rc ? rc : lrc;
+    return launch_norm(D, dim3(rows), s, pdl, x, delta, 1, stride, emb, toks, c.vocab_size, w, out, D, eps,
+                       (int)w4, 0, ExchangeWait{});
   };
   for (int off = 0; off < prompt_len; off += per) {
     const int n = std::min(per, prompt_len - off), rows = B * n;
@@ -2488,14 +2510,9 @@ int enqueue_segment_p2p(ce_llama *m, int segment, int l, cudaStream_t s) {
   // residual add of the exchanged delta [batch][dim] (after its wait) or the
   // embedding, then RMSNorm into xb
   auto norm = [&](bool embed, const float *w, ExchangeWait xw) {
-    int lrc = CE_OK;
-    const int rc = launch_rows(m->nv, [&](auto nv) {
-      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
-                          "residual_rmsnorm_kernel", m->x, embed ? (const float *)nullptr : (const float *)m->x_delta,
-                          1, (size_t)0, embed ? (const uint16_t *)m->tok_emb : (const uint16_t *)nullptr,
-                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, 0, xw);
-    });
-    return rc ? rc : lrc;
+    return launch_norm(D, dim3(B), s, pdl, m->x, embed ? (const float *)nullptr : (const float *)m->x_delta, 1,
+                       (size_t)0, embed ? (const uint16_t *)m->tok_emb : (const uint16_t *)nullptr,
+                       (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, 0, xw);
   };
   // the o-projection / w2 output: split-K partials summed into this rank's
   // columns of every rank's delta exchange
@@ -2598,14 +2615,9 @@ int ce_llama_enqueue_segment(ce_llama *m, int segment, int layer, ce_stream_t st
   // residual add of the gathered delta ([rank][batch][lD]) or the embedding,
   // then RMSNorm into xb
   auto norm = [&](bool embed, const float *w) {
-    int lrc = CE_OK;
-    const int rc = launch_rows(m->nv, [&](auto nv) {
-      lrc = launch_kernel(residual_rmsnorm_kernel<decltype(nv)::value>, dim3(B), dim3(kRowThreads), 0, s, pdl,
-                          "residual_rmsnorm_kernel", m->x, embed ? (const float *)nullptr : (const float *)m->x_delta,
-                          1, slot_d, embed ? (const uint16_t *)m->tok_emb : (const uint16_t *)nullptr,
-                          (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, lD, ExchangeWait{});
-    });
-    return rc ? rc : lrc;
+    return launch_norm(D, dim3(B), s, pdl, m->x, embed ? (const float *)nullptr : (const float *)m->x_delta, 1,
+                       slot_d, embed ? (const uint16_t *)m->tok_emb : (const uint16_t *)nullptr,
+                       (const int *)m->tokens, c.vocab_size, w, m->xb, D, eps, (int)w4, lD, ExchangeWait{});
   };
   // the o-projection / w2 output: GEMM into the split partials, summed into
   // this rank's slot of the delta exchange
